@@ -1,0 +1,160 @@
+"""ctypes binding of the C ABI declared in ``include/ai_attn.h``.
+
+The shared library ``_ai_attn.so`` is built in-tree by
+``autoindexer_b200.build`` (``nvcc -gencode arch=compute_100a,code=sm_100a``).
+There is no fallback: if the library is missing or cannot be loaded every
+attention call raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+__all__ = [
+    "LIB_PATH",
+    "AiTensor4",
+    "AiAttnLayout",
+    "AiAttnFwdArgs",
+    "AiAttnBwdArgs",
+    "DTYPE_BF16",
+    "DTYPE_F16",
+    "DTYPE_F32",
+    "EXPORTED_SYMBOLS",
+    "lib",
+    "check",
+]
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_ai_attn.so")
+
+DTYPE_BF16, DTYPE_F16, DTYPE_F32 = 0, 1, 2
+ABI_VERSION = 1
+
+# Every function include/ai_attn.h declares.
+EXPORTED_SYMBOLS = (
+    "ai_attn_abi_version",
+    "ai_attn_fwd_tile_rows",
+    "ai_attn_kv_tile_rows",
+    "ai_attn_fwd",
+    "ai_attn_bwd_workspace",
+    "ai_attn_bwd",
+    "ai_attn_read_status",
+    "ai_attn_strerror",
+)
+
+_i32p = ctypes.POINTER(ctypes.c_int32)
+_f32p = ctypes.POINTER(ctypes.c_float)
+
+
+class AiTensor4(ctypes.Structure):
+    _fields_ = [
+        ("ptr", ctypes.c_void_p),
+        ("stride_b", ctypes.c_int64),
+        ("stride_h", ctypes.c_int64),
+        ("stride_t", ctypes.c_int64),
+    ]
+
+
+class AiAttnLayout(ctypes.Structure):
+    _fields_ = [
+        ("n_blocks", ctypes.c_int32),
+        ("blocks", ctypes.c_void_p),
+        ("row_blocks", ctypes.c_void_p),
+        ("row_cov", ctypes.c_void_p),
+        ("key_info", ctypes.c_void_p),
+        ("n_keys", ctypes.c_int64),
+        ("q_pos", ctypes.c_void_p),
+        ("rope_cos", ctypes.c_void_p),
+        ("rope_sin", ctypes.c_void_p),
+        ("n_pos", ctypes.c_int32),
+        ("fwd_tile", ctypes.c_int32),
+        ("fwd_items", ctypes.c_void_p),
+        ("n_fwd_items", ctypes.c_int32),
+        ("kv_tile", ctypes.c_int32),
+        ("kv_items", ctypes.c_void_p),
+        ("n_kv_items", ctypes.c_int32),
+    ]
+
+
+class AiAttnFwdArgs(ctypes.Structure):
+    _fields_ = [
+        ("batch", ctypes.c_int32),
+        ("seq_len", ctypes.c_int32),
+        ("num_q_heads", ctypes.c_int32),
+        ("num_kv_heads", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
+        ("dtype", ctypes.c_int32),
+        ("scale", ctypes.c_float),
+        ("q", AiTensor4),
+        ("k", AiTensor4),
+        ("v", AiTensor4),
+        ("out", AiTensor4),
+        ("lse", ctypes.c_void_p),
+        ("layout", AiAttnLayout),
+        ("status", ctypes.c_void_p),
+    ]
+
+
+class AiAttnBwdArgs(ctypes.Structure):
+    _fields_ = [
+        ("fwd", AiAttnFwdArgs),
+        ("dout", AiTensor4),
+        ("dq", AiTensor4),
+        ("dk", AiTensor4),
+        ("dv", AiTensor4),
+        ("workspace", ctypes.c_void_p),
+        ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
+_lock = threading.Lock()
+_lib = None
+
+
+def _bind(handle):
+    P = ctypes.POINTER
+    handle.ai_attn_abi_version.restype = ctypes.c_int
+    handle.ai_attn_abi_version.argtypes = []
+    for name in ("ai_attn_fwd_tile_rows", "ai_attn_kv_tile_rows"):
+        fn = getattr(handle, name)
+        fn.restype = ctypes.c_int
+        fn.argtypes = [ctypes.c_int, ctypes.c_int]
+    handle.ai_attn_fwd.restype = ctypes.c_int
+    handle.ai_attn_fwd.argtypes = [P(AiAttnFwdArgs), ctypes.c_void_p]
+    handle.ai_attn_bwd_workspace.restype = ctypes.c_int
+    handle.ai_attn_bwd_workspace.argtypes = [P(AiAttnBwdArgs), P(ctypes.c_size_t)]
+    handle.ai_attn_bwd.restype = ctypes.c_int
+    handle.ai_attn_bwd.argtypes = [P(AiAttnBwdArgs), ctypes.c_void_p]
+    handle.ai_attn_read_status.restype = ctypes.c_int
+    handle.ai_attn_read_status.argtypes = [ctypes.c_void_p, ctypes.c_void_p, P(ctypes.c_int32)]
+    handle.ai_attn_strerror.restype = ctypes.c_char_p
+    handle.ai_attn_strerror.argtypes = [ctypes.c_int]
+    return handle
+
+
+def lib():
+    """The loaded C library (loaded once).  Raises if it is missing."""
+    global _lib
+    if _lib is None:
+        with _lock:
+            if _lib is None:
+                if not os.path.exists(LIB_PATH):
+                    raise RuntimeError(
+                        f"autoindexer_b200: CUDA library {LIB_PATH} is not built; "
+                        "run `python -m autoindexer_b200.build` (nvcc, sm_100a)")
+                handle = _bind(ctypes.CDLL(LIB_PATH))
+                ver = handle.ai_attn_abi_version()
+                if ver != ABI_VERSION:
+                    raise RuntimeError(f"autoindexer_b200: library ABI {ver} != expected {ABI_VERSION}; rebuild it")
+                _lib = handle
+    return _lib
+
+
+def strerror(code: int) -> str:
+    return lib().ai_attn_strerror(int(code)).decode()
+
+
+def check(code: int, what: str) -> None:
+    if code != 0:
+        raise RuntimeError(f"{what} failed ({code}): {strerror(code)}")

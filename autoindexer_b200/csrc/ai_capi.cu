@@ -1,0 +1,143 @@
+// C ABI of the chain-of-edits attention (declared in include/ai_attn.h):
+// host-side argument validation and kernel dispatch.  Nothing here allocates
+// device memory; the backward's scratch comes from the caller.
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstring>
+
+#include "../../include/ai_attn.h"
+#include "ai_kernels.h"
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+int g_cc_major[kMaxDevices];  // 0 = not queried yet
+
+bool device_is_sm100() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return false;
+  if (g_cc_major[dev] == 0) {
+    int major = -1;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return false;
+    g_cc_major[dev] = major;
+  }
+  return g_cc_major[dev] == 10;
+}
+
+size_t elem_bytes(int dtype) { return dtype == AI_DTYPE_F32 ? 4 : 2; }
+
+bool tensor_ok(const AiTensor4& t) {
+  return t.ptr != nullptr && t.stride_b >= 0 && t.stride_h >= 0 && t.stride_t >= 0;
+}
+
+int validate_fwd(const AiAttnFwdArgs* a) {
+  if (!a) return AI_ERR_NULL;
+  if (a->batch <= 0 || a->seq_len <= 0 || a->num_q_heads <= 0 || a->num_kv_heads <= 0) return AI_ERR_SHAPE;
+  if (a->num_q_heads % a->num_kv_heads != 0) return AI_ERR_SHAPE;
+  if (a->dtype != AI_DTYPE_BF16 && a->dtype != AI_DTYPE_F16 && a->dtype != AI_DTYPE_F32) return AI_ERR_DTYPE;
+  if (a->head_dim != 32 && a->head_dim != 64 && a->head_dim != 128) return AI_ERR_HEAD_DIM;
+  if (!tensor_ok(a->q) || !tensor_ok(a->k) || !tensor_ok(a->v) || !tensor_ok(a->out)) return AI_ERR_NULL;
+  if (!a->lse) return AI_ERR_NULL;
+  const AiAttnLayout& L = a->layout;
+  if (!L.blocks || !L.row_blocks || !L.row_cov || !L.key_info || !L.q_pos || !L.rope_cos || !L.rope_sin)
+    return AI_ERR_NULL;
+  if (L.n_blocks < 0 || L.n_keys < 0 || L.n_pos <= 0 || L.n_fwd_items < 0 || L.n_kv_items < 0) return AI_ERR_LAYOUT;
+  if (L.n_fwd_items > 0 && !L.fwd_items) return AI_ERR_NULL;
+  if (L.n_kv_items > 0 && !L.kv_items) return AI_ERR_NULL;
+  if (L.fwd_tile != ai_attn_fwd_tile_rows(a->dtype, a->head_dim)) return AI_ERR_LAYOUT;
+  if (L.kv_tile != ai_attn_kv_tile_rows(a->dtype, a->head_dim)) return AI_ERR_LAYOUT;
+  const uintptr_t mis = (uintptr_t)a->q.ptr | (uintptr_t)a->k.ptr | (uintptr_t)a->v.ptr | (uintptr_t)a->out.ptr;
+  if (mis % elem_bytes(a->dtype)) return AI_ERR_ALIGN;
+  return AI_OK;
+}
+
+size_t delta_bytes(const AiAttnFwdArgs& f) {
+  const size_t n = (size_t)f.batch * f.num_q_heads * f.seq_len * sizeof(float);
+  return (n + 255) & ~size_t(255);
+}
+
+int launch_status(cudaError_t e) { return e == cudaSuccess ? AI_OK : AI_ERR_LAUNCH; }
+
+}  // namespace
+
+extern "C" {
+
+int ai_attn_abi_version(void) { return AI_ATTN_ABI_VERSION; }
+
+int ai_attn_fwd_tile_rows(int dtype, int head_dim) {
+  return ai::sm100_fwd_supported(dtype, head_dim) ? ai::sm100_fwd_tile_rows() : ai::simt_tile_rows();
+}
+
+int ai_attn_kv_tile_rows(int dtype, int head_dim) {
+  (void)dtype;
+  (void)head_dim;
+  return ai::simt_kv_tile_rows();
+}
+
+int ai_attn_fwd(const AiAttnFwdArgs* a, void* stream) {
+  int rc = validate_fwd(a);
+  if (rc != AI_OK) return rc;
+  if (!device_is_sm100()) return AI_ERR_NO_DEVICE;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (ai::sm100_fwd_supported(a->dtype, a->head_dim)) {
+    cudaError_t ce = cudaSuccess;
+    rc = ai::sm100_fwd(*a, st, &ce);
+    if (rc != AI_OK) return rc;
+    return launch_status(ai::fwd_fill(*a, st));
+  }
+  return launch_status(ai::simt_fwd(*a, st));
+}
+
+int ai_attn_bwd_workspace(const AiAttnBwdArgs* a, size_t* bytes) {
+  if (!a || !bytes) return AI_ERR_NULL;
+  int rc = validate_fwd(&a->fwd);
+  if (rc != AI_OK) return rc;
+  *bytes = delta_bytes(a->fwd);
+  return AI_OK;
+}
+
+int ai_attn_bwd(const AiAttnBwdArgs* a, void* stream) {
+  if (!a) return AI_ERR_NULL;
+  int rc = validate_fwd(&a->fwd);
+  if (rc != AI_OK) return rc;
+  if (!tensor_ok(a->dout) || !tensor_ok(a->dq) || !tensor_ok(a->dk) || !tensor_ok(a->dv)) return AI_ERR_NULL;
+  if (!a->workspace || a->workspace_bytes < delta_bytes(a->fwd)) return AI_ERR_WORKSPACE;
+  if ((uintptr_t)a->workspace % 256) return AI_ERR_ALIGN;
+  if (!device_is_sm100()) return AI_ERR_NO_DEVICE;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return launch_status(ai::simt_bwd(*a, static_cast<float*>(a->workspace), st));
+}
+
+int ai_attn_read_status(int32_t* dev_status, void* stream, int32_t* host_out) {
+  if (!dev_status || !host_out) return AI_ERR_NULL;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (cudaMemcpyAsync(host_out, dev_status, sizeof(int32_t), cudaMemcpyDeviceToHost, st) != cudaSuccess)
+    return AI_ERR_LAUNCH;
+  if (cudaStreamSynchronize(st) != cudaSuccess) return AI_ERR_LAUNCH;
+  if (cudaMemsetAsync(dev_status, 0, sizeof(int32_t), st) != cudaSuccess) return AI_ERR_LAUNCH;
+  return AI_OK;
+}
+
+const char* ai_attn_strerror(int code) {
+  switch (code) {
+    case AI_OK: return "ok";
+    case AI_ERR_NULL: return "a required pointer is NULL";
+    case AI_ERR_SHAPE: return "inconsistent shape (sizes must be > 0 and num_q_heads % num_kv_heads == 0)";
+    case AI_ERR_HEAD_DIM: return "head_dim must be 32, 64 or 128";
+    case AI_ERR_DTYPE: return "dtype must be bf16, fp16 or fp32";
+    case AI_ERR_STRIDE: return "a stride is negative or not a multiple of 16 bytes";
+    case AI_ERR_ALIGN: return "a base pointer is misaligned";
+    case AI_ERR_LAYOUT: return "layout tables inconsistent with the call (tile sizes or counts)";
+    case AI_ERR_WORKSPACE: return "backward workspace missing or smaller than ai_attn_bwd_workspace";
+    case AI_ERR_LAUNCH: return "a CUDA launch failed";
+    case AI_ERR_NO_DEVICE: return "the current CUDA device is not an sm_100 (B200-class) GPU";
+    case AI_ERR_TMA: return "TMA tensor-map encoding rejected a tensor";
+    case AI_ERR_DEV_TIMEOUT: return "device: a bounded wait expired";
+    case AI_ERR_DEV_BOUNDS: return "device: an index fell outside its table";
+    default: return "unknown status";
+  }
+}
+
+}  // extern "C"

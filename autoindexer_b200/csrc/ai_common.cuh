@@ -1,0 +1,65 @@
+// Shared device helpers of the chain-of-edits attention kernels.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "../../include/ai_attn.h"
+
+namespace ai {
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+__device__ __forceinline__ float to_f32(float x) { return x; }
+__device__ __forceinline__ float to_f32(__nv_bfloat16 x) { return __bfloat162float(x); }
+__device__ __forceinline__ float to_f32(__half x) { return __half2float(x); }
+
+template <typename T> __device__ __forceinline__ T from_f32(float x);
+template <> __device__ __forceinline__ float from_f32<float>(float x) { return x; }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
+template <> __device__ __forceinline__ __half from_f32<__half>(float x) { return __float2half_rn(x); }
+
+// Decoded block record (see AI_BLOCK_* in ai_attn.h).
+struct Block {
+  int row, s, e, key_off, kv_lo, flags;
+};
+
+__device__ __forceinline__ Block load_block(const int32_t* blocks, int id) {
+  const int32_t* p = blocks + (int64_t)id * AI_BLOCK_FIELDS;
+  Block b;
+  b.row = p[AI_BLOCK_ROW];
+  b.s = p[AI_BLOCK_START];
+  b.e = p[AI_BLOCK_END];
+  b.key_off = p[AI_BLOCK_KEY_OFF];
+  b.kv_lo = p[AI_BLOCK_KV_LO];
+  b.flags = p[AI_BLOCK_FLAGS];
+  return b;
+}
+
+// First error wins; later errors do not overwrite it.
+__device__ __forceinline__ void report(int32_t* status, int code) {
+  if (status) atomicCAS(status, 0, code);
+}
+
+// Rotary table row of key_info, clamped into the table.  An out-of-range row
+// is reported (AI_ERR_DEV_BOUNDS) and replaced by row 0.
+__device__ __forceinline__ int key_row(uint32_t info, int n_pos, int32_t* status) {
+  int r = (int)(info & AI_KEY_ROW_MASK);
+  if (r >= n_pos) {
+    report(status, AI_ERR_DEV_BOUNDS);
+    r = 0;
+  }
+  return r;
+}
+
+__device__ __forceinline__ int clamp_row(int r, int n_pos, int32_t* status) {
+  if (r < 0 || r >= n_pos) {
+    report(status, AI_ERR_DEV_BOUNDS);
+    return 0;
+  }
+  return r;
+}
+
+}  // namespace ai

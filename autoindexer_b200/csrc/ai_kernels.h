@@ -1,0 +1,25 @@
+// Internal launch interface between the C ABI (ai_capi.cu) and the kernel
+// translation units.  Not part of the public ABI.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "../../include/ai_attn.h"
+
+namespace ai {
+
+// SIMT kernels: any supported dtype, head_dim 32, 64 or 128.
+cudaError_t simt_fwd(const AiAttnFwdArgs& a, cudaStream_t st);
+cudaError_t simt_bwd(const AiAttnBwdArgs& a, float* delta, cudaStream_t st);
+// Rows no block owns: out = v of the row, lse = 0 (any dtype / head_dim).
+cudaError_t fwd_fill(const AiAttnFwdArgs& a, cudaStream_t st);
+int simt_tile_rows();
+int simt_kv_tile_rows();
+
+// tcgen05 / TMEM / TMA kernels (sm_100a): bf16, head_dim 128.
+bool sm100_fwd_supported(int dtype, int head_dim);
+int sm100_fwd_tile_rows();
+// Returns AI_OK or an AiStatus > 0; `cuda_err` receives the CUDA error of a failed launch.
+int sm100_fwd(const AiAttnFwdArgs& a, cudaStream_t st, cudaError_t* cuda_err);
+
+}  // namespace ai

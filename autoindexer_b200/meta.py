@@ -1,0 +1,285 @@
+"""Compiles a position-block layout into the device tables the kernels read.
+
+Input: the flattened arrays of a ``PositionBlockList`` after ``concat()``
+(``perturb_labels.py:341-357`` of the reference): ``boundary_indices`` (per
+block ``(s, e, key_start, key_end)``), ``query_pos_ids``,
+``concat_key_pos_ids``, ``concat_attn_masks``, ``concat_abs_pos_masks``.  The
+reference shares one list across the batch (``cutedsl/meta.py:20-22``); a
+``RowLayouts`` list with one ``PositionBlockList`` per batch row gives every
+row its own layout (packed documents of different lengths per row).
+
+Output (``CompiledLayout``), all int32 / fp32 device tensors:
+
+* ``blocks [n, 8]``: row, s, e, key_off, kv_lo, flags (see ``AI_BLOCK_*``);
+  ``kv_lo`` is the first key the block attends to, so packed documents skip
+  the masked prefix; flags mark blocks with masked keys inside
+  ``[kv_lo, e)`` and blocks with abs keys;
+* ``key_info [sum E]``: per concatenated key, the rotary table row (bits
+  0..29), attn mask (bit 30), abs mask (bit 31);
+* ``q_pos [B, T]``: table row of every query row (rows past the covered
+  length use position 0, as ``perturb_labels.py:335`` pads);
+* ``rope_cos / rope_sin [n_pos, D/2]``: fp32 table of the rotary module;
+* ``fwd_items [m, 4]``: (block, q0, q1) query tiles, longest first;
+* ``kv_items [k, 4]``: (row, j0, j1) key tiles of the dK/dV pass, longest first.
+
+It is built once per layout object and cached on it (the reference caches
+its own per-backend metadata the same way, ``perturb_labels.py:298-331``), so
+all layers of a forward share it.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import List, Optional
+
+import numpy as np
+import torch
+
+from . import _lib
+from .rope import rope_table
+
+__all__ = ["RowLayouts", "CompiledLayout", "compile_layout", "layout_rows", "dtype_code"]
+
+_KEY_ATTN = np.uint32(1 << 30)
+_KEY_ABS = np.uint32(1 << 31)
+_ROW_MASK = (1 << 30) - 1
+BLOCKF_MASKED, BLOCKF_ABS = 1, 2
+
+
+class RowLayouts(list):
+    """One position-block list per batch row."""
+
+
+def dtype_code(dtype: torch.dtype) -> int:
+    if dtype == torch.bfloat16:
+        return _lib.DTYPE_BF16
+    if dtype == torch.float16:
+        return _lib.DTYPE_F16
+    if dtype == torch.float32:
+        return _lib.DTYPE_F32
+    raise TypeError(f"unsupported dtype {dtype}")
+
+
+def _np(x):
+    if hasattr(x, "detach"):
+        return x.detach().cpu().numpy()
+    return np.asarray(x)
+
+
+def layout_rows(parsed_positions, batch: int) -> list:
+    """Per-row layouts: a ``RowLayouts`` (or a list whose items carry
+    ``boundary_indices``) as is, anything else shared by every row."""
+    if isinstance(parsed_positions, RowLayouts) or (
+            isinstance(parsed_positions, (list, tuple)) and len(parsed_positions) > 0
+            and hasattr(parsed_positions[0], "boundary_indices")):
+        rows = list(parsed_positions)
+        if len(rows) != batch:
+            raise ValueError(f"{len(rows)} row layouts for a batch of {batch}")
+        return rows
+    return [parsed_positions] * batch
+
+
+@dataclass
+class _HostLayout:
+    bounds: np.ndarray   # [n, 4] int64
+    qpos: np.ndarray     # [T_cov]
+    kpos: np.ndarray     # [sum E]
+    attn: np.ndarray     # [sum E] bool
+    abs_: np.ndarray     # [sum E] bool
+
+
+def _host_layout(lay, seq_len: int) -> _HostLayout:
+    if getattr(lay, "concat_key_pos_ids", None) is None:
+        raise ValueError("position-block list has not been concat()-ed")
+    bounds = np.asarray([tuple(int(v) for v in b) for b in lay.boundary_indices], dtype=np.int64).reshape(-1, 4)
+    qpos = _np(lay.query_pos_ids).astype(np.int64).reshape(-1)
+    kpos = _np(lay.concat_key_pos_ids).astype(np.int64).reshape(-1)
+    attn = _np(lay.concat_attn_masks).astype(bool).reshape(-1)
+    ab = _np(lay.concat_abs_pos_masks).astype(bool).reshape(-1)
+    if bounds.shape[0] == 0:
+        raise ValueError("position-block list has no blocks")
+    expect_s = 0
+    for s, e, ks, ke in bounds:
+        if s != expect_s or e <= s or ke - ks != e or e > seq_len:
+            raise ValueError(f"blocks must partition [0, T_cov) in order with key range [0, e): got {(s, e, ks, ke)}")
+        expect_s = e
+    if qpos.shape[0] != expect_s:
+        raise ValueError(f"query_pos_ids has {qpos.shape[0]} entries, blocks cover {expect_s} rows")
+    if kpos.shape[0] != bounds[-1, 3] or attn.shape[0] != kpos.shape[0] or ab.shape[0] != kpos.shape[0]:
+        raise ValueError("concatenated key arrays do not match boundary_indices")
+    return _HostLayout(bounds, qpos, kpos, attn, ab)
+
+
+def _pairs(h: _HostLayout) -> int:
+    n = 0
+    for s, e, ks, ke in h.bounds:
+        c = np.cumsum(h.attn[ks:ke].astype(np.int64))
+        n += int(c[s:e].sum())
+    return n
+
+
+@dataclass
+class CompiledLayout:
+    batch: int
+    seq_len: int
+    head_dim: int
+    dtype: int
+    n_pos: int
+    p_min: int
+    fwd_tile: int
+    kv_tile: int
+    blocks: torch.Tensor
+    row_blocks: torch.Tensor
+    row_cov: torch.Tensor
+    key_info: torch.Tensor
+    q_pos: torch.Tensor
+    rope_cos: torch.Tensor
+    rope_sin: torch.Tensor
+    fwd_items: torch.Tensor
+    kv_items: torch.Tensor
+    pairs_per_head: int          # finite (query, key) logits of one head summed over the batch
+    host_blocks: np.ndarray = field(repr=False, default=None)
+
+    def c_struct(self) -> "_lib.AiAttnLayout":
+        L = _lib.AiAttnLayout()
+        L.n_blocks = int(self.blocks.shape[0])
+        L.blocks = self.blocks.data_ptr()
+        L.row_blocks = self.row_blocks.data_ptr()
+        L.row_cov = self.row_cov.data_ptr()
+        L.key_info = self.key_info.data_ptr()
+        L.n_keys = int(self.key_info.numel())
+        L.q_pos = self.q_pos.data_ptr()
+        L.rope_cos = self.rope_cos.data_ptr()
+        L.rope_sin = self.rope_sin.data_ptr()
+        L.n_pos = int(self.n_pos)
+        L.fwd_tile = int(self.fwd_tile)
+        L.fwd_items = self.fwd_items.data_ptr() if self.fwd_items.numel() else None
+        L.n_fwd_items = int(self.fwd_items.shape[0])
+        L.kv_tile = int(self.kv_tile)
+        L.kv_items = self.kv_items.data_ptr() if self.kv_items.numel() else None
+        L.n_kv_items = int(self.kv_items.shape[0])
+        return L
+
+
+def _tiles(fwd_tile: int, kv_tile: int, blocks: np.ndarray, row_cov: np.ndarray):
+    fwd = []
+    for bi, (row, s, e, koff, kv_lo, flags, _, _) in enumerate(blocks):
+        for q0 in range(s, e, fwd_tile):
+            q1 = min(q0 + fwd_tile, e)
+            cost = (q1 - q0) * max(0, min(e, q1) - kv_lo)
+            fwd.append((cost, bi, q0, q1))
+    fwd.sort(key=lambda t: -t[0])
+    kv = []
+    for row, cov in enumerate(row_cov):
+        for j0 in range(0, int(cov), kv_tile):
+            j1 = min(j0 + kv_tile, int(cov))
+            kv.append(((int(cov) - j0), row, j0, j1))
+    kv.sort(key=lambda t: -t[0])
+    fwd_arr = np.asarray([(bi, q0, q1, 0) for _, bi, q0, q1 in fwd], dtype=np.int32).reshape(-1, 4)
+    kv_arr = np.asarray([(row, j0, j1, 0) for _, row, j0, j1 in kv], dtype=np.int32).reshape(-1, 4)
+    return fwd_arr, kv_arr
+
+
+def compile_layout(parsed_positions, batch: int, seq_len: int, head_dim: int, dtype: torch.dtype,
+                   rotary_emb, device) -> CompiledLayout:
+    """Builds (or fetches from the layout's cache) the device tables."""
+    device = torch.device(device)
+    code = dtype_code(dtype)
+    cache_owner = parsed_positions if not isinstance(parsed_positions, tuple) else None
+    key = None
+    if cache_owner is not None:
+        rows_probe = layout_rows(parsed_positions, batch)
+        key = (batch, seq_len, head_dim, code, id(rotary_emb), str(device),
+               tuple(id(getattr(r, "concat_key_pos_ids", None)) for r in rows_probe[:1]))
+        cache = getattr(cache_owner, "_b200_layout_cache", None)
+        if cache is not None and key in cache:
+            return cache[key]
+    compiled = _compile(parsed_positions, batch, seq_len, head_dim, code, rotary_emb, device)
+    if cache_owner is not None:
+        try:
+            cache = getattr(cache_owner, "_b200_layout_cache", None)
+            if cache is None:
+                cache = {}
+                setattr(cache_owner, "_b200_layout_cache", cache)
+            cache[key] = compiled
+        except AttributeError:
+            pass  # plain list: no attribute storage, no caching
+    return compiled
+
+
+def _compile(parsed_positions, batch, seq_len, head_dim, code, rotary_emb, device) -> CompiledLayout:
+    rows = layout_rows(parsed_positions, batch)
+    uniq: List = []
+    index_of = {}
+    for r in rows:
+        if id(r) not in index_of:
+            index_of[id(r)] = len(uniq)
+            uniq.append(r)
+    hosts = [_host_layout(r, seq_len) for r in uniq]
+
+    # Table range: every owned query position, every attended key position, and 0 (padding).
+    lo, hi = 0, 0
+    for h in hosts:
+        if h.qpos.size:
+            lo, hi = min(lo, int(h.qpos.min())), max(hi, int(h.qpos.max()))
+        if h.attn.any():
+            kp = h.kpos[h.attn]
+            lo, hi = min(lo, int(kp.min())), max(hi, int(kp.max()))
+    n_pos = hi - lo + 1
+    if n_pos > _ROW_MASK:
+        raise ValueError("position range too large for the kernel tables")
+
+    key_info_parts, key_base = [], []
+    base = 0
+    for h in hosts:
+        rowidx = np.clip(h.kpos - lo, 0, n_pos - 1).astype(np.uint32)
+        info = rowidx | (h.attn.astype(np.uint32) * _KEY_ATTN) | ((h.abs_ & h.attn).astype(np.uint32) * _KEY_ABS)
+        key_info_parts.append(info)
+        key_base.append(base)
+        base += info.shape[0]
+    key_info = np.concatenate(key_info_parts).view(np.int32)
+
+    blocks, row_blocks, row_cov = [], [0], []
+    q_pos = np.zeros((batch, seq_len), dtype=np.int32)
+    pairs = 0
+    host_pairs = [_pairs(h) for h in hosts]
+    for b, r in enumerate(rows):
+        u = index_of[id(r)]
+        h = hosts[u]
+        for s, e, ks, ke in h.bounds:
+            am = h.attn[ks:ke]
+            nz = np.flatnonzero(am)
+            kv_lo = int(nz[0]) if nz.size else int(e)
+            flags = 0
+            if nz.size and not am[kv_lo:].all():
+                flags |= BLOCKF_MASKED
+            if (h.abs_[ks:ke] & am).any():
+                flags |= BLOCKF_ABS
+            blocks.append((b, int(s), int(e), key_base[u] + int(ks), kv_lo, flags, 0, 0))
+        row_blocks.append(len(blocks))
+        cov = int(h.bounds[-1, 1])
+        row_cov.append(cov)
+        qp = np.zeros(seq_len, dtype=np.int64)
+        qp[:cov] = h.qpos
+        q_pos[b] = np.clip(qp - lo, 0, n_pos - 1)
+        pairs += host_pairs[u]
+
+    blocks_np = np.asarray(blocks, dtype=np.int32).reshape(-1, 8)
+    row_cov_np = np.asarray(row_cov, dtype=np.int32)
+    lib = _lib.lib()
+    fwd_tile = lib.ai_attn_fwd_tile_rows(code, head_dim)
+    kv_tile = lib.ai_attn_kv_tile_rows(code, head_dim)
+    fwd_items, kv_items = _tiles(fwd_tile, kv_tile, blocks_np, row_cov_np)
+
+    cos, sin = rope_table(rotary_emb, lo, hi, head_dim, device)
+
+    def dev(a):
+        return torch.from_numpy(np.ascontiguousarray(a)).to(device)
+
+    return CompiledLayout(
+        batch=batch, seq_len=seq_len, head_dim=head_dim, dtype=code, n_pos=n_pos, p_min=lo,
+        fwd_tile=fwd_tile, kv_tile=kv_tile,
+        blocks=dev(blocks_np), row_blocks=dev(np.asarray(row_blocks, dtype=np.int32)), row_cov=dev(row_cov_np),
+        key_info=dev(key_info), q_pos=dev(q_pos), rope_cos=cos, rope_sin=sin,
+        fwd_items=dev(fwd_items), kv_items=dev(kv_items), pairs_per_head=pairs, host_blocks=blocks_np,
+    )

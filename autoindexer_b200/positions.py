@@ -1,0 +1,175 @@
+"""Position-block formats of the chain-of-edits attention.
+
+``PositionBlock`` / ``PositionBlockList`` carry the same fields, with the same
+meaning, as the reference's types (``type_utils.py:32-40`` and
+``perturb_labels.py:278-357`` of AutodeskAILab/autoindexer's
+``src/autoindexer/models/autoindexer``), so that a list built by the reference's
+own edit-chain code and a list built here are interchangeable inputs of
+``autoindexer_b200``'s attention function:
+
+* block ``b`` owns query rows ``[start, end)`` of the sequence; its keys are the
+  prefix ``[0, end)``;
+* ``key_pos_ids[j]`` is the rotary position id of key ``j`` *inside this block*
+  (the same physical key gets a different position in different blocks);
+* ``attn_mask[j]`` false masks key ``j`` out of the block;
+* ``abs_pos_mask[j]`` true makes the logit against key ``j`` use the unrotated
+  query (``None`` = all false);
+* ``query_pos_ids`` are the positions of the block's own query rows.
+
+``concat()`` builds the flattened view every backend reads: concatenated
+per-block key arrays and ``boundary_indices = (start, end, key_start, key_end)``.
+
+The builders below generate the synthetic layouts the benchmarks use: packed
+documents (one COMPLETE block per document, keys before the document masked)
+and cursor-style position streams for head-dim sections.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from enum import IntEnum
+from typing import List, Optional, Sequence
+
+import numpy as np
+import torch
+from torch import Tensor
+
+__all__ = [
+    "BlockType",
+    "PositionBlock",
+    "PositionBlockList",
+    "document_blocks",
+    "cursor_stream",
+]
+
+
+class BlockType(IntEnum):
+    EXTEND = 1
+    EDIT = 2
+    COMPLETE = 3
+
+
+@dataclass
+class PositionBlock:
+    key_pos_ids: Tensor
+    query_pos_ids: Optional[Tensor] = None
+    abs_pos_mask: Optional[Tensor] = None
+    attn_mask: Optional[Tensor] = None
+    start_idx: Optional[int] = None
+    end_idx: Optional[int] = None
+    block_type: Optional[BlockType] = None
+
+
+class PositionBlockList(list):
+    """List of ``PositionBlock``; ``concat()`` fills the flattened arrays."""
+
+    def __init__(self, *args):
+        super().__init__(*args)
+        self.query_pos_ids: Optional[Tensor] = None
+        self.concat_key_pos_ids: Optional[Tensor] = None
+        self.concat_abs_pos_masks: Optional[Tensor] = None
+        self.concat_attn_masks: Optional[Tensor] = None
+        self.boundary_indices = []
+
+    def concat(self) -> "PositionBlockList":
+        self.query_pos_ids = torch.cat([blk.query_pos_ids for blk in self], dim=0)
+        self.concat_key_pos_ids = torch.cat([blk.key_pos_ids for blk in self], dim=0)
+        masks = []
+        for blk in self:
+            am = blk.attn_mask
+            if am is None:
+                am = torch.ones(len(blk.key_pos_ids), dtype=torch.bool, device=blk.key_pos_ids.device)
+            masks.append(am)
+        self.concat_attn_masks = torch.cat(masks, dim=0)
+        self.concat_abs_pos_masks = torch.zeros_like(self.concat_attn_masks)
+        self.boundary_indices = []
+        offset = 0
+        for blk in self:
+            n_keys = len(blk.key_pos_ids)
+            first_row = n_keys - len(blk.query_pos_ids)
+            self.boundary_indices.append((first_row, n_keys, offset, offset + n_keys))
+            if blk.abs_pos_mask is not None:
+                self.concat_abs_pos_masks[offset:offset + n_keys] = blk.abs_pos_mask
+            offset += n_keys
+        return self
+
+    def get_rotary_pos_emb(self, rotary_emb, x: Tensor, seq_len: int):
+        """``(cos, sin)`` of the zero-padded query positions and of the
+        concatenated key positions, as the reference's eager backend expects
+        (``perturb_labels.py:333-339``); memoised per (module, dtype, device,
+        seq_len)."""
+        key = (id(rotary_emb), x.dtype, str(x.device), seq_len)
+        cache = self.__dict__.setdefault("_rotary_cache", {})
+        if key not in cache:
+            q = self.query_pos_ids
+            padded = torch.nn.functional.pad(q, (0, seq_len - len(q))).to(x.device)
+            cache[key] = (rotary_emb(x, padded.unsqueeze(0)),
+                          rotary_emb(x, self.concat_key_pos_ids.to(x.device).unsqueeze(0)))
+        return cache[key]
+
+    @property
+    def device(self):
+        return self[0].key_pos_ids.device if len(self) else None
+
+
+def document_blocks(doc_lens: Sequence[int], position_ids: Optional[Sequence[int]] = None,
+                    device=None) -> PositionBlockList:
+    """One COMPLETE block per packed document: rows ``[s, e)``, keys ``[0, e)``
+    with ``attn_mask = (j >= s)`` so attention stays inside the document.
+
+    ``position_ids`` (length ``sum(doc_lens)``) gives the rotary position id of
+    every token; by default positions restart at 0 in each document.  With a
+    ``SectionedRope`` the position ids are token indices (``arange``) and the
+    per-section positions live in the rope's streams."""
+    total = int(sum(doc_lens))
+    if position_ids is None:
+        pos = np.concatenate([np.arange(n, dtype=np.int64) for n in doc_lens]) if total else np.zeros(0, np.int64)
+    else:
+        pos = np.asarray(position_ids, dtype=np.int64)
+        assert pos.shape[0] == total
+    pos_t = torch.as_tensor(pos, device=device)
+    blocks = PositionBlockList()
+    s = 0
+    for n in doc_lens:
+        e = s + int(n)
+        am = torch.zeros(e, dtype=torch.bool, device=device)
+        am[s:e] = True
+        blocks.append(PositionBlock(
+            key_pos_ids=pos_t[:e].clone(),
+            query_pos_ids=pos_t[s:e].clone(),
+            abs_pos_mask=None,
+            attn_mask=am,
+            start_idx=s,
+            end_idx=e,
+            block_type=BlockType.COMPLETE,
+        ))
+        s = e
+    return blocks.concat()
+
+
+def cursor_stream(n: int, rng: np.random.Generator, p_step: float = 0.8) -> np.ndarray:
+    """Edit-chain cursor positions: start at 0; with probability ``p_step`` step
+    by +1, otherwise jump back to a uniform position in ``[0, current]``."""
+    out = np.zeros(n, dtype=np.int64)
+    cur = 0
+    u = rng.random(n)
+    for t in range(1, n):
+        if u[t] < p_step:
+            cur += 1
+        else:
+            cur = int(rng.integers(0, cur + 1))
+        out[t] = cur
+    return out
+
+
+def split_documents(total: int, lo: int, hi: int, rng: np.random.Generator) -> List[int]:
+    """Document lengths ~ U[lo, hi] packed into ``total`` tokens; the last
+    document is truncated to fit."""
+    lens = []
+    acc = 0
+    while acc < total:
+        n = int(rng.integers(lo, hi + 1))
+        n = min(n, total - acc)
+        lens.append(n)
+        acc += n
+    return lens

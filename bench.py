@@ -1,0 +1,347 @@
+"""Benchmark of the chain-of-edits (multi-segment RoPE) attention fwd+bwd.
+
+Workload: Qwen3-8B-shaped attention layer, bf16,
+B=4, T=4096, Hq=32, Hkv=8, head_dim=128, rope_theta=1e6, two head-dim RoPE
+sections (slots [0,32) follow arange, slots [32,64) an edit-cursor stream),
+every batch row packs documents with lengths ~ U[256, 2048] (causal inside
+each document, one position-block per document).  Synthetic seeded inputs.
+
+A step = forward + backward of the attention over the batch.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Under torchrun (N > 1) every rank runs its own batch (weak scaling, no
+collective on the data path); the step time is the max over ranks.
+``--impl reference`` times the CPU oracle (numpy restatement of the
+reference's eager path) on a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+B, T, HQ, HKV, D = 4, 4096, 32, 8, 128
+THETA = 1e6
+SECTIONS = [(0, 32), (32, 64)]
+WORKLOAD = ("cfg1: bf16 B=4 T=4096 Hq=32 Hkv=8 D=128 theta=1e6, docs U[256,2048] packed per row, "
+            "2 RoPE sections (32+32 freq slots: arange, cursor stream)")
+METRIC = "multi-seg RoPE attn fwd+bwd TFLOP/s (causal-adjusted, 14*D*pairs*Hq)"
+
+
+def make_workload(seed: int, device):
+    import torch
+
+    import autoindexer_b200 as ab
+    from autoindexer_b200.positions import split_documents
+
+    rng = np.random.default_rng(seed)
+    streams = [np.arange(T), ab.cursor_stream(T, rng)]
+    rows = ab.RowLayouts()
+    for _ in range(B):
+        lens = split_documents(T, 256, 2048, rng)
+        rows.append(ab.document_blocks(lens, position_ids=np.arange(T)))
+    rope = ab.SectionedRope(D, THETA, [torch.as_tensor(s) for s in streams], SECTIONS, device=device)
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(B, HQ, T, D, generator=g).to(torch.bfloat16)
+    k = torch.randn(B, HKV, T, D, generator=g).to(torch.bfloat16)
+    v = torch.randn(B, HKV, T, D, generator=g).to(torch.bfloat16)
+    dout = torch.randn(B, T, HQ, D, generator=g).to(torch.bfloat16)
+    return rows, rope, streams, (q, k, v, dout)
+
+
+class ClockSampler:
+    """Samples nvidia-smi SM clocks and throttle reasons while running."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = float(parts[1])
+            except ValueError:
+                continue
+            for n, p in zip(names, parts[3:7]):
+                if p.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["bf16_tflops"]), float(p["bf16_tflops_sustained"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 1590.0, 1400.0, "fallback"
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    from autoindexer_b200 import _lib
+    from autoindexer_b200.attention import attn_bwd, attn_fwd, fused_chain_of_edits_attn_b200, read_status
+    from autoindexer_b200.meta import compile_layout
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    rows, rope, _, host = make_workload(seed=rank, device=dev)
+    q, k, v, dout = (x.to(dev) for x in host)
+    scale = D ** -0.5
+    layout = compile_layout(rows, B, T, D, torch.bfloat16, rope, dev)
+    flops = 14.0 * D * HQ * layout.pairs_per_head
+    flops_fwd = 4.0 * D * HQ * layout.pairs_per_head
+    flops_bwd = 10.0 * D * HQ * layout.pairs_per_head
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        out, lse = attn_fwd(q, k, v, layout, scale)
+        return attn_bwd(q, k, v, out, lse, dout, layout, scale)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    assert read_status(dev) == 0
+
+    # Device-timed steps: events around each step, L2 flushed (untimed) between steps.
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
+           torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    with ClockSampler(local) as clocks:
+        for i in range(args.steps):
+            flush.fill_(float(i))
+            e0, e1, e2 = ev[i]
+            e0.record(stream)
+            out, lse = attn_fwd(q, k, v, layout, scale)
+            e1.record(stream)
+            attn_bwd(q, k, v, out, lse, dout, layout, scale)
+            e2.record(stream)
+        torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    t_fwd = sum(a.elapsed_time(b) for a, b, _ in ev) / 1e3
+    t_bwd = sum(b.elapsed_time(c) for _, b, c in ev) / 1e3
+    t_step = t_fwd + t_bwd
+    t_max = t_step
+    if world > 1:
+        tt = torch.tensor([t_step], device=dev, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t_max = float(tt.item())
+    value = world * flops * args.steps / t_max / 1e12
+    ms_per_step = t_max / args.steps * 1e3
+
+    # End to end through the public API: pinned host inputs -> device, forward +
+    # backward via autograd, results (out, dq, dk, dv) back to pinned host memory.
+    pinned = [x.pin_memory() for x in host]
+    outs_host = [torch.empty(B, T, HQ, D, dtype=torch.bfloat16).pin_memory(),
+                 torch.empty(B, HQ, T, D, dtype=torch.bfloat16).pin_memory(),
+                 torch.empty(B, HKV, T, D, dtype=torch.bfloat16).pin_memory(),
+                 torch.empty(B, HKV, T, D, dtype=torch.bfloat16).pin_memory()]
+    h2d = sum(x.numel() * x.element_size() for x in pinned)
+    d2h = sum(x.numel() * x.element_size() for x in outs_host)
+
+    def e2e_step():
+        xq, xk, xv = (x.to(dev, non_blocking=True).requires_grad_(True) for x in pinned[:3])
+        g = pinned[3].to(dev, non_blocking=True)
+        o, _ = fused_chain_of_edits_attn_b200(rope, xq, xk, xv, rows)
+        o.backward(g)
+        for dst, src in zip(outs_host, (o.detach(), xq.grad, xk.grad, xv.grad)):
+            dst.copy_(src, non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    torch.cuda.synchronize(dev)
+    e_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    for i in range(args.steps):
+        flush.fill_(float(i))
+        e_ev[i][0].record(stream)
+        e2e_step()
+        e_ev[i][1].record(stream)
+    torch.cuda.synchronize(dev)
+    t_e2e = sum(a.elapsed_time(b) for a, b in e_ev) / 1e3
+    if world > 1:
+        tt = torch.tensor([t_e2e], device=dev, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t_e2e = float(tt.item())
+    e2e_value = world * flops * args.steps / t_e2e / 1e12
+    assert read_status(dev) == 0
+
+    peak, peak_sus, peak_kind = peaks()
+    dom_is_bwd = t_bwd >= t_fwd
+    dom_flops = flops_bwd if dom_is_bwd else flops_fwd
+    dom_t = (t_bwd if dom_is_bwd else t_fwd) / args.steps
+    achieved = dom_flops / dom_t / 1e12
+    launches_per_step = 6  # fwd: sm100 fwd + row fill; bwd: delta, dQ, dK/dV, row fill
+    tokens = world * B * T * args.steps / t_max
+
+    line = {
+        "metric": METRIC,
+        "value": round(value, 3),
+        "unit": "TFLOP/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_per_step, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded randn q/k/v/dO; seeded document lengths and cursor streams)",
+        "config": {"workload": WORKLOAD, "global_batch": B * world, "seq_len": T, "parallelism": f"dp{world} (independent rows)",
+                   "l2": "flushed between timed steps (256 MB write, untimed)"},
+        "fwd_ms": round(t_fwd / args.steps * 1e3, 4),
+        "bwd_ms": round(t_bwd / args.steps * 1e3, 4),
+        "tokens_per_s": round(tokens, 1),
+        "pairs_per_head": layout.pairs_per_head,
+        "pct_bf16_peak": round(100 * value / world / peak, 2),
+        "pct_bf16_spec_2250": round(100 * value / world / 2250.0, 2),
+        "roofline": {"bound": "tensor", "kernel": "ai_attn_bwd (dQ + dK/dV kernels)" if dom_is_bwd else "ai_attn_fwd",
+                     "achieved": round(achieved, 3), "peak": peak, "unit": "TFLOP/s",
+                     "frac": round(achieved / peak, 4), "peak_kind": f"{peak_kind} burst bf16",
+                     "traffic": None},
+        "e2e": {"value": round(e2e_value, 3), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clocks.summary(),
+    }
+    if rank == 0 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(rows, host, seed=0)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def cpu_baseline(rows, host, seed=0, reps=1):
+    """Oracle (numpy port of the reference's eager path, fp32, all host
+    threads) on one (row, kv-group) slice: 4 query heads of batch row 0."""
+    import torch
+
+    import autoindexer_b200 as ab
+    from oracle import attn_oracle as O
+
+    q, k, v, dout = host
+    G = HQ // HKV
+    rng = np.random.default_rng(seed)
+    streams = [np.arange(T), ab.cursor_stream(T, rng)]
+    rope_mod = ab.SectionedRope(D, THETA, [torch.as_tensor(s) for s in streams], SECTIONS)
+    rope = O.make_sectioned_rope(rope_mod.inv_freq.numpy(), streams, SECTIONS)
+    lay = rows[0]
+    qs = q[:1, :G].float().numpy()
+    ks = k[:1, :1].float().numpy()
+    vs = v[:1, :1].float().numpy()
+    dos = dout[:1, :, :G].float().numpy()
+    pairs = O.count_pairs(lay, T)
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        O.attn_forward(qs, ks, vs, lay, rope, dtype=np.float32)
+        O.attn_backward(qs, ks, vs, dos, lay, rope, dtype=np.float32)
+    dt = (time.perf_counter() - t0) / reps
+    flops = 14.0 * D * G * pairs
+    return {"value": round(flops / dt / 1e12, 6), "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"batch row 0, kv group 0 ({G} query heads), T={T}: fwd+bwd, numpy fp32, {dt:.2f} s"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    import torch
+
+    rows, _, _, host = make_workload(seed=0, device="cpu")
+    for _ in range(args.warmup):
+        cpu_baseline(rows, host)
+    vals = [cpu_baseline(rows, host) for _ in range(args.steps)]
+    value = float(np.median([x["value"] for x in vals]))
+    cb = dict(vals[0])
+    cb["value"] = round(value, 6)
+    line = {
+        "metric": METRIC, "value": round(value, 6), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (same generator as the GPU arm)", "impl": "reference",
+        "config": {"workload": WORKLOAD, "global_batch": B, "seq_len": T, "parallelism": "cpu"},
+        "cpu_baseline": cb,
+        "e2e": {"value": round(value, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

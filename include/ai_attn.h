@@ -1,0 +1,170 @@
+/*
+ * ai_attn.h - C ABI of the B200 chain-of-edits (multi-segment RoPE) causal
+ * attention, forward and backward.
+ *
+ * The reference (AutodeskAILab/autoindexer, package
+ * src/autoindexer/models/autoindexer) has no native FFI: its backends are
+ * Python functions registered into transformers' ALL_ATTENTION_FUNCTIONS.  The
+ * entry points below replace the compute those backends perform:
+ *
+ *   ai_attn_fwd  <- attention/triton_wrapper.py:57-101 fused_chain_of_edits_attn_triton
+ *                   (-> kernels/triton_rope_attn.py:1710-1812 FusedMultiSegmentRoPEAttn.forward)
+ *                   and attention/cutedsl/wrapper.py:127-170 fused_chain_of_edits_attn_cutedsl;
+ *                   numerics of attention/reference.py:116-141 chain_of_edits_attn_ref.
+ *   ai_attn_bwd  <- kernels/triton_rope_attn.py:1814-1902 FusedMultiSegmentRoPEAttn.backward
+ *                   (and the CuTeDSL path's FA4 backward + PrepPackBackward +
+ *                   FastRopeKeyFunction.backward, cutedsl/prep_multi_head/autograd.py:22-69).
+ *   AiAttnLayout <- the PositionBlockList arrays the backends read
+ *                   (perturb_labels.py:341-357 concat(): boundary_indices,
+ *                   concat_key_pos_ids, concat_attn_masks, concat_abs_pos_masks,
+ *                   query_pos_ids) plus the rotary cos/sin the RotaryEmbeddingFunc
+ *                   produces (perturb_labels.py:333-339 get_rotary_pos_emb).
+ *
+ * Conventions
+ *   - Every pointer is a device pointer unless stated otherwise.  The caller
+ *     allocates every buffer (the backward's scratch through
+ *     ai_attn_bwd_workspace); the library never allocates device memory.
+ *   - A 4-D tensor (B, H, T, D) is described by AiTensor4: element strides of
+ *     the b, h and t dimensions; the d dimension is contiguous.
+ *   - All launches go on the given stream (a cudaStream_t passed as void*).
+ *   - Return value: 0 = success; > 0 = the arguments were rejected on the host
+ *     and nothing was launched; the text is available from ai_attn_strerror.
+ *     Kernels never trap: a device-side failure (bounded wait expired, an index
+ *     out of range) is written as a negative code into *status (if status is
+ *     not NULL) and can be read back with ai_attn_read_status.
+ */
+#ifndef AI_ATTN_H
+#define AI_ATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define AI_ATTN_ABI_VERSION 1
+
+typedef enum AiDtype {
+  AI_DTYPE_BF16 = 0,
+  AI_DTYPE_F16 = 1,
+  AI_DTYPE_F32 = 2
+} AiDtype;
+
+enum AiStatus {
+  AI_OK = 0,
+  AI_ERR_NULL = 1,        /* a required pointer is NULL */
+  AI_ERR_SHAPE = 2,       /* batch/seq/heads inconsistent (Hq % Hkv, sizes <= 0) */
+  AI_ERR_HEAD_DIM = 3,    /* head_dim not 32, 64 or 128 */
+  AI_ERR_DTYPE = 4,       /* dtype not supported */
+  AI_ERR_STRIDE = 5,      /* a stride is negative or not 16-byte compatible */
+  AI_ERR_ALIGN = 6,       /* a base pointer is not 16-byte aligned */
+  AI_ERR_LAYOUT = 7,      /* block table / work list inconsistent with the call */
+  AI_ERR_WORKSPACE = 8,   /* workspace missing or too small */
+  AI_ERR_LAUNCH = 9,      /* a CUDA launch failed (the CUDA error is not cleared) */
+  AI_ERR_NO_DEVICE = 10,  /* current device is not an sm_100 part */
+  AI_ERR_TMA = 11,        /* tensor map encoding refused the tensor */
+  AI_ERR_DEV_TIMEOUT = -1, /* device: a bounded wait expired */
+  AI_ERR_DEV_BOUNDS = -2   /* device: an index fell outside its table */
+};
+
+/* (B, H, T, D) view: element (b, h, t, d) is at ptr[b*stride_b + h*stride_h + t*stride_t + d]. */
+typedef struct AiTensor4 {
+  void* ptr;
+  int64_t stride_b;
+  int64_t stride_h;
+  int64_t stride_t;
+} AiTensor4;
+
+/* Block record, int32[8] per block (AI_BLOCK_* index the fields). */
+#define AI_BLOCK_ROW 0     /* batch row the block belongs to */
+#define AI_BLOCK_START 1   /* first query row s */
+#define AI_BLOCK_END 2     /* one past the last query row e; keys are [0, e) */
+#define AI_BLOCK_KEY_OFF 3 /* offset of key 0 of this block in key_info */
+#define AI_BLOCK_KV_LO 4   /* first key with attn_mask set (e if none) */
+#define AI_BLOCK_FLAGS 5   /* AI_BLOCKF_* */
+#define AI_BLOCK_FIELDS 8
+#define AI_BLOCKF_MASKED 1 /* some key in [kv_lo, e) has attn_mask false */
+#define AI_BLOCKF_ABS 2    /* some key has abs_pos_mask set */
+
+/* key_info word: bits 0..29 rotary table row, bit 30 attn_mask, bit 31 abs_pos_mask. */
+#define AI_KEY_ROW_MASK 0x3FFFFFFF
+#define AI_KEY_ATTN 0x40000000u
+#define AI_KEY_ABS 0x80000000u
+
+typedef struct AiAttnLayout {
+  int32_t n_blocks;
+  const int32_t* blocks;      /* [n_blocks][AI_BLOCK_FIELDS], grouped by batch row */
+  const int32_t* row_blocks;  /* [B + 1]: blocks of row b are [row_blocks[b], row_blocks[b+1]) */
+  const int32_t* row_cov;     /* [B]: rows >= row_cov[b] belong to no block (diagonal-only) */
+  const int32_t* key_info;    /* [n_keys] */
+  int64_t n_keys;
+  const int32_t* q_pos;       /* [B][T] rotary table row of each query row */
+  const float* rope_cos;      /* [n_pos][D/2] fp32: cos of the angle of (table row, frequency slot) */
+  const float* rope_sin;      /* [n_pos][D/2] */
+  int32_t n_pos;
+  int32_t fwd_tile;           /* query rows per forward / dQ work item (ai_attn_fwd_tile_rows) */
+  const int32_t* fwd_items;   /* [n_fwd_items][4]: block, q0, q1, 0 */
+  int32_t n_fwd_items;
+  int32_t kv_tile;            /* keys per dK/dV work item (ai_attn_kv_tile_rows) */
+  const int32_t* kv_items;    /* [n_kv_items][4]: row, j0, j1, 0 */
+  int32_t n_kv_items;
+} AiAttnLayout;
+
+typedef struct AiAttnFwdArgs {
+  int32_t batch;
+  int32_t seq_len;
+  int32_t num_q_heads;
+  int32_t num_kv_heads;   /* GQA: num_q_heads % num_kv_heads == 0; no expanded copy of K/V */
+  int32_t head_dim;
+  int32_t dtype;          /* AiDtype of q, k, v, out */
+  float scale;            /* softmax scale applied to the logits */
+  AiTensor4 q;            /* (B, Hq, T, D) */
+  AiTensor4 k;            /* (B, Hkv, T, D) */
+  AiTensor4 v;            /* (B, Hkv, T, D) */
+  AiTensor4 out;          /* (B, Hq, T, D) view of the (B, T, Hq, D) output */
+  float* lse;             /* (B, Hq, T) natural-log log-sum-exp of the scaled logits */
+  AiAttnLayout layout;
+  int32_t* status;        /* optional device status word */
+} AiAttnFwdArgs;
+
+typedef struct AiAttnBwdArgs {
+  AiAttnFwdArgs fwd;      /* the forward's arguments; out and lse as the forward wrote them */
+  AiTensor4 dout;         /* (B, Hq, T, D) view of dL/dout */
+  AiTensor4 dq;           /* (B, Hq, T, D) */
+  AiTensor4 dk;           /* (B, Hkv, T, D), summed over the query heads of each group */
+  AiTensor4 dv;           /* (B, Hkv, T, D) */
+  void* workspace;        /* device scratch of at least ai_attn_bwd_workspace bytes, 256-B aligned */
+  size_t workspace_bytes;
+} AiAttnBwdArgs;
+
+/* ABI version this library was built with (AI_ATTN_ABI_VERSION). */
+int ai_attn_abi_version(void);
+
+/* Query rows per forward/dQ work item, and keys per dK/dV work item, for a
+ * (dtype, head_dim); the caller's work lists must be tiled with these. */
+int ai_attn_fwd_tile_rows(int dtype, int head_dim);
+int ai_attn_kv_tile_rows(int dtype, int head_dim);
+
+/* Forward: out and lse for every row (rows no block owns get out = v of the
+ * row and lse = 0, the reference's diagonal-only convention). */
+int ai_attn_fwd(const AiAttnFwdArgs* args, void* stream);
+
+/* Bytes of device scratch ai_attn_bwd needs for these arguments. */
+int ai_attn_bwd_workspace(const AiAttnBwdArgs* args, size_t* bytes);
+
+/* Backward: dq, dk, dv (written, not accumulated). */
+int ai_attn_bwd(const AiAttnBwdArgs* args, void* stream);
+
+/* Synchronises the stream, copies the device status word to *host_out and
+ * resets it to AI_OK.  For tests and debugging; not needed on the hot path. */
+int ai_attn_read_status(int32_t* dev_status, void* stream, int32_t* host_out);
+
+/* Static text for a status code. */
+const char* ai_attn_strerror(int code);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* AI_ATTN_H */

@@ -1,0 +1,306 @@
+"""CPU oracle for the chain-of-edits (multi-segment RoPE) causal attention.
+
+TEST INFRASTRUCTURE ONLY.  This module is the checker that the CUDA path of
+``autoindexer_b200`` is compared against.  Only ``tests/``,
+``__graft_entry__.smoke()`` and the ``cpu_baseline`` / ``--impl reference``
+legs of ``bench.py`` may import it.  The product path never imports, calls or
+falls back to it.
+
+It is a numpy restatement of the reference's eager path (AutodeskAILab/
+autoindexer, package ``src/autoindexer/models/autoindexer``):
+
+* ``attention/utils.py:5-6``            ``apply_cos_sin``  (rotate-half RoPE)
+* ``attention/reference.py:11-64``      ``compute_attn_weights_over_segments_ref``
+* ``attention/reference.py:96-113``     ``compute_attn_weights_ref``  (causal + scale)
+* ``attention/reference.py:116-141``    ``chain_of_edits_attn_ref``   (softmax, P.V)
+* ``attention/__init__.py:36-37``       GQA expansion (``repeat_kv``) in the wrapper
+* ``perturb_labels.py:333-339``         query positions zero-padded to ``T``
+
+The reference obtains gradients through autograd; ``attn_backward`` writes the
+same gradients out by hand (softmax backward, then the per-block split of the
+logit gradient into the rotated-query part and the ``abs`` part, then the
+transpose of the rotation).
+
+Pinning: ``tests/test_oracle_golden.py`` checks this module against golden
+vectors produced by running the reference itself (``tests/golden/make_golden.py``)
+and against the reference's own known-answer position matrix
+(``src/autoindexer/models/autoindexer/tests/labels/position_matrix.json``).
+
+Layouts follow the reference: ``q`` is ``(B, Hq, T, D)``, ``k``/``v`` are
+``(B, Hkv, T, D)`` (un-expanded, ``Hq = G * Hkv``), the output is
+``(B, T, Hq, D)`` and ``lse`` is ``(B, Hq, T)``.
+
+A ``layout`` is any object with the attributes the reference's
+``PositionBlockList`` carries after ``concat()`` (``perturb_labels.py:341-357``):
+``boundary_indices`` (list of ``(start, end, key_start, key_end)``),
+``query_pos_ids``, ``concat_key_pos_ids``, ``concat_attn_masks`` and
+``concat_abs_pos_masks`` (numpy arrays or torch CPU tensors).  ``layout`` may
+also be a list with one such object per batch row.
+
+``rope`` is a callable ``rope(position_ids) -> (cos, sin)`` returning arrays
+of shape ``(L, D)``, the role ``RotaryEmbeddingFunc`` plays in the reference
+(``type_utils.py:57``).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+__all__ = [
+    "default_inv_freq",
+    "make_rope",
+    "make_sectioned_rope",
+    "apply_cos_sin",
+    "segment_logits",
+    "attn_logits",
+    "attn_forward",
+    "attn_backward",
+    "count_pairs",
+]
+
+
+def _np(x):
+    if hasattr(x, "detach"):
+        x = x.detach().cpu().numpy()
+    return np.asarray(x)
+
+
+# ---------------------------------------------------------------------------
+# Rotary tables
+# ---------------------------------------------------------------------------
+
+def default_inv_freq(head_dim: int, theta: float) -> np.ndarray:
+    """``inv_freq[k] = theta ** (-2k / D)`` in float32 (HF default RoPE init,
+    transformers ``_compute_default_rope_parameters``).  Bit equality with
+    torch's ``pow`` is not guaranteed; tests that need exact agreement take
+    ``inv_freq`` from the rotary module itself."""
+    exps = np.arange(0, head_dim, 2, dtype=np.int64).astype(np.float32) / np.float32(head_dim)
+    return (np.float32(1.0) / (np.float32(theta) ** exps)).astype(np.float32)
+
+
+def make_rope(inv_freq: np.ndarray):
+    """Standard RoPE as HF computes it: the angle is the float32 product
+    ``float32(pos) * inv_freq`` and ``cos``/``sin`` are taken of that float32
+    angle; the half-table is repeated (``cat(freqs, freqs)``)."""
+    inv_freq = np.asarray(inv_freq, dtype=np.float32)
+
+    def rope(position_ids):
+        pos = _np(position_ids).astype(np.float32).reshape(-1)
+        ang = (pos[:, None] * inv_freq[None, :]).astype(np.float32).astype(np.float64)
+        c, s = np.cos(ang), np.sin(ang)
+        return np.concatenate([c, c], axis=-1), np.concatenate([s, s], axis=-1)
+
+    return rope
+
+
+def make_sectioned_rope(inv_freq: np.ndarray, streams, slot_sections):
+    """Head-dim sections expressed through the reference's plugin type: the
+    position id handed to the rotary function is a token index ``t``; frequency
+    slot ``k`` that belongs to section ``s`` rotates by ``streams[s][t]``.
+    ``slot_sections`` lists ``(slot_begin, slot_end)`` per section (rotate-half
+    pairs dims ``k`` and ``k + D/2``, so a section owns whole slots)."""
+    inv_freq = np.asarray(inv_freq, dtype=np.float32)
+    streams = [np.asarray(_np(s), dtype=np.int64) for s in streams]
+    half = inv_freq.shape[0]
+    owner = np.empty(half, dtype=np.int64)
+    for si, (a, b) in enumerate(slot_sections):
+        owner[a:b] = si
+
+    def rope(position_ids):
+        idx = _np(position_ids).astype(np.int64).reshape(-1)
+        idx = np.clip(idx, 0, None)
+        pos = np.stack([streams[owner[k]][idx] for k in range(half)], axis=-1).astype(np.float32)
+        ang = (pos * inv_freq[None, :]).astype(np.float32).astype(np.float64)
+        c, s = np.cos(ang), np.sin(ang)
+        return np.concatenate([c, c], axis=-1), np.concatenate([s, s], axis=-1)
+
+    return rope
+
+
+def _rotate_half(x):
+    h = x.shape[-1] // 2
+    return np.concatenate([-x[..., h:], x[..., :h]], axis=-1)
+
+
+def apply_cos_sin(x, cos, sin):
+    """``x * cos + rotate_half(x) * sin`` (``attention/utils.py:5-6``); ``cos`` and
+    ``sin`` are ``(L, D)`` and broadcast over the leading dims of ``x``."""
+    return x * cos + _rotate_half(x) * sin
+
+
+def _rotate_half_T(g):
+    """Transpose of ``rotate_half``: ``rotate_half(x) = [-x2, x1]`` so the
+    adjoint maps ``[g1, g2]`` to ``[g2, -g1]``."""
+    h = g.shape[-1] // 2
+    return np.concatenate([g[..., h:], -g[..., :h]], axis=-1)
+
+
+def apply_cos_sin_T(g, cos, sin):
+    """Adjoint of ``apply_cos_sin`` with respect to ``x``."""
+    return g * cos + _rotate_half_T(g * sin)
+
+
+# ---------------------------------------------------------------------------
+# Layout helpers
+# ---------------------------------------------------------------------------
+
+def _layout_arrays(layout):
+    return (
+        [tuple(int(v) for v in b) for b in layout.boundary_indices],
+        _np(layout.query_pos_ids).astype(np.int64),
+        _np(layout.concat_key_pos_ids).astype(np.int64),
+        _np(layout.concat_attn_masks).astype(bool),
+        _np(layout.concat_abs_pos_masks).astype(bool),
+    )
+
+
+def _per_row(layout, batch):
+    if isinstance(layout, (list, tuple)) and len(layout) > 0 and hasattr(layout[0], "boundary_indices"):
+        assert len(layout) == batch, "one layout per batch row expected"
+        return list(layout)
+    return [layout] * batch
+
+
+def count_pairs(layout, seq_len: int) -> int:
+    """Number of finite logits of one head of one batch row for ``layout``
+    (owned rows only; the diagonal-only unowned rows are not counted)."""
+    bounds, _, _, am, _ = _layout_arrays(layout)
+    n = 0
+    for s, e, ks, ke in bounds:
+        m = am[ks:ke]
+        c = np.cumsum(m.astype(np.int64))
+        # row i in [s, e) sees keys j <= i with attn mask set
+        n += int(c[s:e].sum())
+    return n
+
+
+# ---------------------------------------------------------------------------
+# Forward
+# ---------------------------------------------------------------------------
+
+def segment_logits(q, q_rot, k, key_cos, key_sin, abs_mask, attn_mask, bounds):
+    """Restates ``compute_attn_weights_over_segments_ref`` (reference.py:11-64)
+    for one batch row: ``q``, ``q_rot``, ``k`` are ``(H, T, D)``; returns the
+    ``(H, T, T)`` logits with ``-inf`` outside blocks and a zero diagonal on
+    rows no block owns."""
+    H, T, D = q.shape
+    w = np.full((H, T, T), -np.inf, dtype=q.dtype)
+    idx = np.arange(T)
+    w[:, idx, idx] = 0
+    for s, e, ks, ke in bounds:
+        k_rot = apply_cos_sin(k[:, :e, :], key_cos[ks:ke], key_sin[ks:ke])  # (H, e, D)
+        kt = np.swapaxes(k_rot, -1, -2)
+        blk = q_rot[:, s:e, :] @ kt
+        blk = blk + ((q[:, s:e, :] - q_rot[:, s:e, :]) @ kt) * abs_mask[ks:ke]
+        blk = np.where(attn_mask[ks:ke], blk, -np.inf)
+        w[:, s:e, :e] = blk
+    return w
+
+
+def _row_rope(rope, qpos, kpos, T):
+    qp = np.zeros(T, dtype=np.int64)
+    qp[: qpos.shape[0]] = qpos  # perturb_labels.py:335 pads with zeros
+    qc, qs = rope(qp)
+    kc, ks = rope(kpos)
+    return qc, qs, kc, ks
+
+
+def attn_logits(q_row, k_row, layout_row, rope, scale):
+    """Restates ``compute_attn_weights_ref`` (reference.py:96-113) for one row:
+    segment logits, global causal mask, then ``* scale``."""
+    H, T, D = q_row.shape
+    bounds, qpos, kpos, am, ab = _layout_arrays(layout_row)
+    qc, qs, kc, ks = _row_rope(rope, qpos, kpos, T)
+    q_rot = apply_cos_sin(q_row, qc, qs)
+    w = segment_logits(q_row, q_rot, k_row, kc, ks, ab, am, bounds)
+    causal = np.tril(np.ones((T, T), dtype=bool))
+    w = np.where(causal, w, -np.inf)
+    return w * scale
+
+
+def _softmax(w):
+    m = np.max(w, axis=-1, keepdims=True)
+    e = np.exp(w - m)
+    ssum = e.sum(axis=-1, keepdims=True)
+    return e / ssum, (m + np.log(ssum))[..., 0]
+
+
+def _expand(x, groups):
+    return np.repeat(x, groups, axis=1) if groups > 1 else x
+
+
+def attn_forward(q, k, v, layout, rope, scale=None, dtype=np.float64):
+    """Restates ``chain_of_edits_attn_ref`` (reference.py:116-141) with the
+    wrapper's GQA expansion (``attention/__init__.py:36-37``).
+
+    Returns ``(out (B, T, Hq, D), lse (B, Hq, T))``; ``lse`` is the
+    log-sum-exp of the scaled logits of each row (the quantity the fused
+    kernels save for the backward pass)."""
+    q, k, v = (_np(t).astype(dtype) for t in (q, k, v))
+    B, Hq, T, D = q.shape
+    G = Hq // k.shape[1]
+    if scale is None:
+        scale = D ** -0.5
+    out = np.empty((B, T, Hq, D), dtype=dtype)
+    lse = np.empty((B, Hq, T), dtype=dtype)
+    for b, lay in enumerate(_per_row(layout, B)):
+        w = attn_logits(q[b], _expand(k[b:b + 1], G)[0], lay, rope, scale)
+        p, l = _softmax(w)
+        out[b] = np.swapaxes(p @ _expand(v[b:b + 1], G)[0], 0, 1)
+        lse[b] = l
+    return out, lse
+
+
+# ---------------------------------------------------------------------------
+# Backward
+# ---------------------------------------------------------------------------
+
+def attn_backward(q, k, v, dout, layout, rope, scale=None, dtype=np.float64):
+    """Gradients of ``attn_forward`` with respect to ``q``, ``k``, ``v`` for the
+    upstream gradient ``dout (B, T, Hq, D)``; the same quantities the reference
+    obtains through autograd on ``chain_of_edits_attn_ref``.
+
+    Returns ``(dq (B, Hq, T, D), dk (B, Hkv, T, D), dv (B, Hkv, T, D))``."""
+    q, k, v, dout = (_np(t).astype(dtype) for t in (q, k, v, dout))
+    B, Hq, T, D = q.shape
+    Hkv = k.shape[1]
+    G = Hq // Hkv
+    if scale is None:
+        scale = D ** -0.5
+    dq = np.zeros_like(q)
+    dk = np.zeros_like(k)
+    dv = np.zeros_like(v)
+    for b, lay in enumerate(_per_row(layout, B)):
+        bounds, qpos, kpos, am, ab = _layout_arrays(lay)
+        qc, qs, kc, ks = _row_rope(rope, qpos, kpos, T)
+        qb = q[b]
+        kb = _expand(k[b:b + 1], G)[0]
+        vb = _expand(v[b:b + 1], G)[0]
+        q_rot = apply_cos_sin(qb, qc, qs)
+        w = segment_logits(qb, q_rot, kb, kc, ks, ab, am, bounds)
+        causal = np.tril(np.ones((T, T), dtype=bool))
+        w = np.where(causal, w, -np.inf) * scale
+        p, _ = _softmax(w)
+        do = np.swapaxes(dout[b], 0, 1)  # (Hq, T, D)
+        dvb = np.swapaxes(p, -1, -2) @ do
+        dp = do @ np.swapaxes(vb, -1, -2)
+        ds = p * (dp - np.sum(dp * p, axis=-1, keepdims=True))
+        dl = np.where(np.isfinite(w), ds * scale, 0.0)  # gradient of the unscaled logits
+        dq_rot = np.zeros_like(qb)
+        dq_raw = np.zeros_like(qb)
+        dkb = np.zeros_like(kb)
+        for s, e, kst, ke in bounds:
+            cos_b, sin_b = kc[kst:ke], ks[kst:ke]
+            k_rot = apply_cos_sin(kb[:, :e, :], cos_b, sin_b)
+            g = dl[:, s:e, :e]
+            absm = ab[kst:ke].astype(dtype)
+            g_rot = g * (1.0 - absm)
+            g_abs = g * absm
+            dq_rot[:, s:e, :] += g_rot @ k_rot
+            dq_raw[:, s:e, :] += g_abs @ k_rot
+            dk_rot = np.swapaxes(g_rot, -1, -2) @ q_rot[:, s:e, :] + np.swapaxes(g_abs, -1, -2) @ qb[:, s:e, :]
+            dkb[:, :e, :] += apply_cos_sin_T(dk_rot, cos_b, sin_b)
+        dq[b] = apply_cos_sin_T(dq_rot, qc, qs) + dq_raw
+        dk[b] = dkb.reshape(Hkv, G, T, D).sum(axis=1)
+        dv[b] = dvb.reshape(Hkv, G, T, D).sum(axis=1)
+    return dq, dk, dv

@@ -1,0 +1,104 @@
+"""Layout compiler (``autoindexer_b200.meta``): the device tables the kernels
+read, built on the CPU from reference-format position-block lists."""
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import ArrayLayout, golden_names, golden_rope, load_golden
+from autoindexer_b200 import RowLayouts, document_blocks
+from autoindexer_b200.meta import compile_layout
+from oracle import attn_oracle as O
+
+KEY_ATTN, KEY_ABS = 1 << 30, 1 << 31
+
+
+def _compile(lay, B, T, D, dtype, rope_mod):
+    return compile_layout(lay, B, T, D, dtype, rope_mod, "cpu")
+
+
+@pytest.mark.parametrize("name", golden_names())
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_tables_match_layout(name, dtype):
+    g = load_golden(name)
+    lay = ArrayLayout.from_golden(g)
+    mod, rope = golden_rope(g)
+    T, D = int(g["T"]), int(g["D"])
+    c = _compile(lay, 2, T + 5, D, dtype, mod)
+    blocks = c.blocks.numpy()
+    info = c.key_info.numpy().view(np.uint32)
+    bounds = np.asarray(lay.boundary_indices)
+    assert blocks.shape[0] == 2 * bounds.shape[0]
+    am = lay.concat_attn_masks.numpy()
+    ab = lay.concat_abs_pos_masks.numpy()
+    kp = lay.concat_key_pos_ids.numpy()
+    for bi, (row, s, e, koff, kv_lo, flags, _, _) in enumerate(blocks):
+        S, E, KS, KE = bounds[bi % bounds.shape[0]]
+        assert (row, s, e, koff) == (bi // bounds.shape[0], S, E, KS)
+        m = am[KS:KE]
+        assert kv_lo == (np.flatnonzero(m)[0] if m.any() else E)
+        assert bool(flags & 2) == bool((ab[KS:KE] & m).any())
+        assert bool(flags & 1) == bool(m.any() and not m[kv_lo:].all())
+        word = info[KS:KE]
+        assert np.array_equal((word & KEY_ATTN) != 0, m)
+        assert np.array_equal((word & KEY_ABS) != 0, ab[KS:KE] & m)
+        rows = (word & ((1 << 30) - 1)).astype(np.int64)
+        assert np.array_equal(rows[m] + c.p_min, kp[KS:KE][m])
+    # the table reproduces the rotary module at every used position
+    cos_ref, sin_ref = rope(np.arange(c.p_min, c.p_min + c.n_pos))
+    np.testing.assert_allclose(c.rope_cos.numpy(), cos_ref[:, : D // 2], atol=1e-6)
+    np.testing.assert_allclose(c.rope_sin.numpy(), sin_ref[:, : D // 2], atol=1e-6)
+    # query rows: owned rows carry their position, the padding carries position 0
+    qp = c.q_pos.numpy()[0] + c.p_min
+    assert np.array_equal(qp[:T], lay.query_pos_ids.numpy())
+    assert np.all(qp[T:] == 0)
+    assert c.pairs_per_head == 2 * O.count_pairs(lay, T)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_work_items_cover_rows_and_keys_once(dtype):
+    rng = np.random.default_rng(0)
+    lens_a, lens_b = [300, 77, 190], [128, 128, 311]
+    rows = RowLayouts([document_blocks(lens_a), document_blocks(lens_b)])
+    T = 600
+    mod, _ = golden_rope(load_golden("op0_d32"))
+    D = 32
+    c = _compile(rows, 2, T, D, dtype, mod)
+    blocks = c.blocks.numpy()
+    seen = np.zeros((2, T), dtype=np.int64)
+    for bi, q0, q1, _ in c.fwd_items.numpy():
+        row, s, e = blocks[bi, :3]
+        assert s <= q0 < q1 <= e and q1 - q0 <= c.fwd_tile
+        seen[row, q0:q1] += 1
+    assert np.all(seen[0, :sum(lens_a)] == 1) and np.all(seen[0, sum(lens_a):] == 0)
+    assert np.all(seen[1, :sum(lens_b)] == 1) and np.all(seen[1, sum(lens_b):] == 0)
+    keys = np.zeros((2, T), dtype=np.int64)
+    for row, j0, j1, _ in c.kv_items.numpy():
+        assert j1 - j0 <= c.kv_tile
+        keys[row, j0:j1] += 1
+    assert np.all(keys[0, :sum(lens_a)] == 1) and np.all(keys[1, :sum(lens_b)] == 1)
+    assert list(c.row_cov.numpy()) == [sum(lens_a), sum(lens_b)]
+    # documents: each block attends from its own first row on
+    for row, s, e, koff, kv_lo, flags, _, _ in blocks:
+        assert kv_lo == s and flags == 0
+
+
+def test_layout_rejects_malformed_lists():
+    g = load_golden("op1_d32")
+    mod, _ = golden_rope(g)
+    lay = ArrayLayout.from_golden(g)
+    bad = ArrayLayout(np.asarray(lay.boundary_indices)[1:], lay.query_pos_ids, lay.concat_key_pos_ids,
+                      lay.concat_attn_masks, lay.concat_abs_pos_masks)
+    with pytest.raises(ValueError):
+        _compile(bad, 1, int(g["T"]), 32, torch.float32, mod)
+    with pytest.raises(ValueError):
+        _compile(lay, 1, int(g["T"]) - 1, 32, torch.float32, mod)
+
+
+def test_layout_cache_is_reused():
+    g = load_golden("op2_d32")
+    mod, _ = golden_rope(g)
+    lay = ArrayLayout.from_golden(g)
+    a = _compile(lay, 1, int(g["T"]), 32, torch.float32, mod)
+    b = _compile(lay, 1, int(g["T"]), 32, torch.float32, mod)
+    assert a is b
