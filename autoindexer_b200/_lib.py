@@ -39,6 +39,7 @@ EXPORTED_SYMBOLS = (
     "ai_attn_fwd",
     "ai_attn_bwd_workspace",
     "ai_attn_bwd",
+    "ai_attn_bwd_noalloc",
     "ai_attn_read_status",
     "ai_attn_strerror",
 )
@@ -126,6 +127,8 @@ def _bind(handle):
     handle.ai_attn_bwd_workspace.argtypes = [P(AiAttnBwdArgs), P(ctypes.c_size_t)]
     handle.ai_attn_bwd.restype = ctypes.c_int
     handle.ai_attn_bwd.argtypes = [P(AiAttnBwdArgs), ctypes.c_void_p]
+    handle.ai_attn_bwd_noalloc.restype = ctypes.c_int
+    handle.ai_attn_bwd_noalloc.argtypes = [P(AiAttnBwdArgs), ctypes.c_void_p]
     handle.ai_attn_read_status.restype = ctypes.c_int
     handle.ai_attn_read_status.argtypes = [ctypes.c_void_p, ctypes.c_void_p, P(ctypes.c_int32)]
     handle.ai_attn_strerror.restype = ctypes.c_char_p

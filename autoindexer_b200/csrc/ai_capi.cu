@@ -134,6 +134,8 @@ const char* ai_attn_strerror(int code) {
     case AI_ERR_LAUNCH: return "a CUDA launch failed";
     case AI_ERR_NO_DEVICE: return "the current CUDA device is not an sm_100 (B200-class) GPU";
     case AI_ERR_TMA: return "TMA tensor-map encoding rejected a tensor";
+    case AI_ERR_NOALLOC_LIMIT:
+      return "batch * num_q_heads * seq_len exceeds the fixed scratch of ai_attn_bwd_noalloc (AI_ATTN_NOALLOC_MAX_ROWS)";
     case AI_ERR_DEV_TIMEOUT: return "device: a bounded wait expired";
     case AI_ERR_DEV_BOUNDS: return "device: an index fell outside its table";
     default: return "unknown status";

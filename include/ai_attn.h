@@ -64,6 +64,7 @@ enum AiStatus {
   AI_ERR_LAUNCH = 9,      /* a CUDA launch failed (the CUDA error is not cleared) */
   AI_ERR_NO_DEVICE = 10,  /* current device is not an sm_100 part */
   AI_ERR_TMA = 11,        /* tensor map encoding refused the tensor */
+  AI_ERR_NOALLOC_LIMIT = 12, /* batch * num_q_heads * seq_len > AI_ATTN_NOALLOC_MAX_ROWS */
   AI_ERR_DEV_TIMEOUT = -1, /* device: a bounded wait expired */
   AI_ERR_DEV_BOUNDS = -2   /* device: an index fell outside its table */
 };
@@ -155,6 +156,18 @@ int ai_attn_bwd_workspace(const AiAttnBwdArgs* args, size_t* bytes);
 
 /* Backward: dq, dk, dv (written, not accumulated). */
 int ai_attn_bwd(const AiAttnBwdArgs* args, void* stream);
+
+/* Backward for callers that cannot allocate device memory (no counterpart in
+ * the reference, which allocates through PyTorch).  Same results as
+ * ai_attn_bwd; args->workspace is ignored: the scratch comes from a fixed
+ * 16 MiB array inside the library (held on every GPU that loads it until the
+ * process exits), so batch * num_q_heads * seq_len must not exceed
+ * AI_ATTN_NOALLOC_MAX_ROWS (else AI_ERR_NOALLOC_LIMIT, nothing launched).
+ * Calls no allocator.  The first call on a device looks the array up on that
+ * device; make it before any stream capture.  Calls that overlap on the GPU
+ * share the array and race. */
+#define AI_ATTN_NOALLOC_MAX_ROWS (1 << 22)
+int ai_attn_bwd_noalloc(const AiAttnBwdArgs* args, void* stream);
 
 /* Synchronises the stream, copies the device status word to *host_out and
  * resets it to AI_OK.  For tests and debugging; not needed on the hot path. */

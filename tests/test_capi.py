@@ -38,7 +38,7 @@ def test_abi_version_and_tiles():
 
 
 def test_strerror_covers_codes():
-    for code in (0, 1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11, -1, -2):
+    for code in (0, 1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12, -1, -2):
         s = _lib.strerror(code)
         assert s and s != "unknown status"
     assert _lib.strerror(12345) == "unknown status"
