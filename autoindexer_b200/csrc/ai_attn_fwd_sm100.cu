@@ -36,6 +36,7 @@
 #include "ai_common.cuh"
 #include "ai_kernels.h"
 #include "sm100_ptx.cuh"
+#include "sm100_tile.cuh"
 
 namespace ai {
 namespace sm100 {
@@ -65,51 +66,10 @@ struct Smem {
 };
 constexpr size_t kSmemBytes = Smem::TOTAL + 1024;
 
-// Byte offset of 16-byte chunk c (0..15) of row r in a 128-row K-major tile
-// stored as two 128-byte-swizzled column blocks (the TMA SWIZZLE_128B layout).
-__device__ __forceinline__ uint32_t chunk_off(int r, int c) {
-  return (uint32_t)(c >> 3) * kHalf + (uint32_t)r * 128u + ((uint32_t)((c & 7) ^ (r & 7)) << 4);
-}
+using tile::pack8;
+using tile::rotate8;
 
-__device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
-  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 t = __bfloat1622float2(h[i]);
-    f[2 * i] = t.x;
-    f[2 * i + 1] = t.y;
-  }
-}
-
-__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
-  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
-  return *reinterpret_cast<uint32_t*>(&h);
-}
-
-__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
-  return make_uint4(pack2(f[0], f[1]), pack2(f[2], f[3]), pack2(f[4], f[5]), pack2(f[6], f[7]));
-}
-
-// Rotate-half RoPE of one 8-wide chunk pair: x1 = dims [8c, 8c+8), x2 = the
-// partner dims [64 + 8c, 64 + 8c + 8); cs/sn point at table[row][8c].
-__device__ __forceinline__ void rotate8(const uint4& a, const uint4& b, const float* cs, const float* sn, uint4& ya,
-                                        uint4& yb) {
-  float x1[8], x2[8], y1[8], y2[8], c[8], s[8];
-  unpack8(a, x1);
-  unpack8(b, x2);
-  const float4* c4 = reinterpret_cast<const float4*>(cs);
-  const float4* s4 = reinterpret_cast<const float4*>(sn);
-  const float4 c0 = __ldg(c4), c1 = __ldg(c4 + 1), s0 = __ldg(s4), s1 = __ldg(s4 + 1);
-  c[0] = c0.x; c[1] = c0.y; c[2] = c0.z; c[3] = c0.w; c[4] = c1.x; c[5] = c1.y; c[6] = c1.z; c[7] = c1.w;
-  s[0] = s0.x; s[1] = s0.y; s[2] = s0.z; s[3] = s0.w; s[4] = s1.x; s[5] = s1.y; s[6] = s1.z; s[7] = s1.w;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    y1[i] = x1[i] * c[i] - x2[i] * s[i];
-    y2[i] = x2[i] * c[i] + x1[i] * s[i];
-  }
-  ya = pack8(y1);
-  yb = pack8(y2);
-}
+__device__ __forceinline__ uint32_t chunk_off(int r, int c) { return tile::chunk_off<BM>(r, c); }
 
 __global__ void __launch_bounds__(kThreads, 1)
     fwd_kernel(const AiAttnFwdArgs a, const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v) {
@@ -404,25 +364,26 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
   return fn;
 }
 
-// 4-D map over a (B, H, T, D) bf16 tensor; box = 64 dims x 128 rows, 128-byte swizzle.
-bool make_map(CUtensorMap* map, const AiTensor4& t, int B, int H, int T) {
-  auto enc = get_encode();
+bool strides_ok(const AiTensor4& t) {
+  return ((uintptr_t)t.ptr % 16 == 0) && (t.stride_b % 8 == 0) && (t.stride_h % 8 == 0) && (t.stride_t % 8 == 0);
+}
+
+}  // namespace sm100
+
+// 4-D map over a (B, H, T, 128) bf16 tensor; box = 64 dims x box_rows rows,
+// 128-byte swizzle, zero fill past T.
+bool sm100_make_map(CUtensorMap* map, const AiTensor4& t, int B, int H, int T, int box_rows) {
+  auto enc = sm100::get_encode();
   if (!enc) return false;
-  cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)T, (cuuint64_t)H, (cuuint64_t)B};
+  cuuint64_t dims[4] = {(cuuint64_t)sm100::D, (cuuint64_t)T, (cuuint64_t)H, (cuuint64_t)B};
   cuuint64_t strides[3] = {(cuuint64_t)t.stride_t * 2, (cuuint64_t)t.stride_h * 2, (cuuint64_t)t.stride_b * 2};
-  cuuint32_t box[4] = {64, (cuuint32_t)BN, 1, 1};
+  cuuint32_t box[4] = {64, (cuuint32_t)box_rows, 1, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, t.ptr, dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
-
-bool strides_ok(const AiTensor4& t) {
-  return ((uintptr_t)t.ptr % 16 == 0) && (t.stride_b % 8 == 0) && (t.stride_h % 8 == 0) && (t.stride_t % 8 == 0);
-}
-
-}  // namespace sm100
 
 bool sm100_fwd_supported(int dtype, int head_dim) { return dtype == AI_DTYPE_BF16 && head_dim == sm100::D; }
 
@@ -433,8 +394,8 @@ int sm100_fwd(const AiAttnFwdArgs& a, cudaStream_t st, cudaError_t* cuda_err) {
   if (!strides_ok(a.q) || !strides_ok(a.k) || !strides_ok(a.v) || !strides_ok(a.out)) return AI_ERR_STRIDE;
   if (a.layout.n_fwd_items == 0) return AI_OK;
   CUtensorMap tm_k, tm_v;
-  if (!make_map(&tm_k, a.k, a.batch, a.num_kv_heads, a.seq_len)) return AI_ERR_TMA;
-  if (!make_map(&tm_v, a.v, a.batch, a.num_kv_heads, a.seq_len)) return AI_ERR_TMA;
+  if (!sm100_make_map(&tm_k, a.k, a.batch, a.num_kv_heads, a.seq_len, BN)) return AI_ERR_TMA;
+  if (!sm100_make_map(&tm_v, a.v, a.batch, a.num_kv_heads, a.seq_len, BN)) return AI_ERR_TMA;
   cudaError_t e = cudaFuncSetAttribute(fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
   if (e == cudaSuccess) {
     fwd_kernel<<<dim3(a.layout.n_fwd_items, a.num_q_heads), kThreads, kSmemBytes, st>>>(a, tm_k, tm_v);

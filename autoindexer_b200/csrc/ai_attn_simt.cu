@@ -663,6 +663,20 @@ static cudaError_t bwd_impl(const AiAttnBwdArgs& a, float* delta, cudaStream_t s
   return cudaGetLastError();
 }
 
+template <typename T, int D>
+static cudaError_t delta_impl(const AiAttnBwdArgs& a, float* delta, cudaStream_t st) {
+  const AiAttnFwdArgs& f = a.fwd;
+  const int64_t rows = (int64_t)f.batch * f.num_q_heads * f.seq_len;
+  delta_kernel<T, D><<<(unsigned)((rows * 32 + 255) / 256), 256, 0, st>>>(a, delta);
+  return cudaGetLastError();
+}
+
+template <typename T, int D>
+static cudaError_t bwd_fill_impl(const AiAttnBwdArgs& a, cudaStream_t st) {
+  bwd_fill_kernel<T, D><<<dim3(a.fwd.seq_len, a.fwd.batch), 128, 0, st>>>(a);
+  return cudaGetLastError();
+}
+
 }  // namespace simt
 
 #define AI_DISPATCH_SIMT_D(FN, T, ...)                                                   \
@@ -691,6 +705,16 @@ cudaError_t fwd_fill(const AiAttnFwdArgs& a, cudaStream_t st) {
 cudaError_t simt_bwd(const AiAttnBwdArgs& a, float* delta, cudaStream_t st) {
   const int dtype = a.fwd.dtype, D = a.fwd.head_dim;
   AI_DISPATCH_SIMT(bwd_impl, a, delta, st)
+}
+
+cudaError_t bwd_delta(const AiAttnBwdArgs& a, float* delta, cudaStream_t st) {
+  const int dtype = a.fwd.dtype, D = a.fwd.head_dim;
+  AI_DISPATCH_SIMT(delta_impl, a, delta, st)
+}
+
+cudaError_t bwd_fill(const AiAttnBwdArgs& a, cudaStream_t st) {
+  const int dtype = a.fwd.dtype, D = a.fwd.head_dim;
+  AI_DISPATCH_SIMT(bwd_fill_impl, a, st)
 }
 
 int simt_tile_rows() { return simt::BM; }

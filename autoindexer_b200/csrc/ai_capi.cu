@@ -71,9 +71,7 @@ int ai_attn_fwd_tile_rows(int dtype, int head_dim) {
 }
 
 int ai_attn_kv_tile_rows(int dtype, int head_dim) {
-  (void)dtype;
-  (void)head_dim;
-  return ai::simt_kv_tile_rows();
+  return ai::sm100_bwd_supported(dtype, head_dim) ? ai::sm100_kv_tile_rows() : ai::simt_kv_tile_rows();
 }
 
 int ai_attn_fwd(const AiAttnFwdArgs* a, void* stream) {
@@ -107,7 +105,9 @@ int ai_attn_bwd(const AiAttnBwdArgs* a, void* stream) {
   if ((uintptr_t)a->workspace % 256) return AI_ERR_ALIGN;
   if (!device_is_sm100()) return AI_ERR_NO_DEVICE;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  return launch_status(ai::simt_bwd(*a, static_cast<float*>(a->workspace), st));
+  float* delta = static_cast<float*>(a->workspace);
+  if (ai::sm100_bwd_supported(a->fwd.dtype, a->fwd.head_dim)) return ai::sm100_bwd(*a, delta, st, nullptr);
+  return launch_status(ai::simt_bwd(*a, delta, st));
 }
 
 int ai_attn_read_status(int32_t* dev_status, void* stream, int32_t* host_out) {

@@ -2,6 +2,7 @@
 // translation units.  Not part of the public ABI.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include "../../include/ai_attn.h"
@@ -16,10 +17,20 @@ cudaError_t fwd_fill(const AiAttnFwdArgs& a, cudaStream_t st);
 int simt_tile_rows();
 int simt_kv_tile_rows();
 
+// Backward pieces shared by every backward path (any dtype / head_dim):
+// delta[b, h, i] = sum_d dO * O, and the rows no block owns.
+cudaError_t bwd_delta(const AiAttnBwdArgs& a, float* delta, cudaStream_t st);
+cudaError_t bwd_fill(const AiAttnBwdArgs& a, cudaStream_t st);
+
 // tcgen05 / TMEM / TMA kernels (sm_100a): bf16, head_dim 128.
 bool sm100_fwd_supported(int dtype, int head_dim);
 int sm100_fwd_tile_rows();
 // Returns AI_OK or an AiStatus > 0; `cuda_err` receives the CUDA error of a failed launch.
 int sm100_fwd(const AiAttnFwdArgs& a, cudaStream_t st, cudaError_t* cuda_err);
+bool sm100_bwd_supported(int dtype, int head_dim);
+int sm100_kv_tile_rows();
+int sm100_bwd(const AiAttnBwdArgs& a, float* delta, cudaStream_t st, cudaError_t* cuda_err);
+// TMA map over a (B, H, T, 128) bf16 tensor, box 64 x box_rows, 128-byte swizzle.
+bool sm100_make_map(CUtensorMap* map, const AiTensor4& t, int B, int H, int T, int box_rows);
 
 }  // namespace ai
