@@ -29,7 +29,7 @@ __all__ = [
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_ai_attn.so")
 
 DTYPE_BF16, DTYPE_F16, DTYPE_F32 = 0, 1, 2
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 # Every function include/ai_attn.h declares.
 EXPORTED_SYMBOLS = (
@@ -68,10 +68,12 @@ class AiAttnLayout(ctypes.Structure):
         ("q_pos", ctypes.c_void_p),
         ("rope_cos", ctypes.c_void_p),
         ("rope_sin", ctypes.c_void_p),
+        ("rope_cs16", ctypes.c_void_p),
         ("n_pos", ctypes.c_int32),
         ("fwd_tile", ctypes.c_int32),
         ("fwd_items", ctypes.c_void_p),
         ("n_fwd_items", ctypes.c_int32),
+        ("n_fwd_abs_items", ctypes.c_int32),
         ("kv_tile", ctypes.c_int32),
         ("kv_items", ctypes.c_void_p),
         ("n_kv_items", ctypes.c_int32),

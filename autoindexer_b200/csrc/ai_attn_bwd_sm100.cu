@@ -100,7 +100,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               const __grid_constant__ CUtensorMap tm_v) {
   using namespace dq;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sm = tile::align1024(smem_raw);
   const uint32_t sbase = ptx::smem_u32(sm);
   const int tid = threadIdx.x, warp = tid / 32;
   uint32_t* s_info = reinterpret_cast<uint32_t*>(sm + INFO);
@@ -383,7 +383,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const __grid_constant__ CUtensorMap tm_do) {
   using namespace kv;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sm = tile::align1024(smem_raw);
   const uint32_t sbase = ptx::smem_u32(sm);
   const int tid = threadIdx.x, warp = tid / 32;
   float* s_lse = reinterpret_cast<float*>(sm + LSE);

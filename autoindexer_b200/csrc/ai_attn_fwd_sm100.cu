@@ -74,7 +74,7 @@ __device__ __forceinline__ uint32_t chunk_off(int r, int c) { return tile::chunk
 __global__ void __launch_bounds__(kThreads, 1)
     fwd_kernel(const AiAttnFwdArgs a, const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sm = tile::align1024(smem_raw);
   const uint32_t sbase = ptx::smem_u32(sm);
   const int tid = threadIdx.x, warp = tid / 32;
   uint32_t* s_info = reinterpret_cast<uint32_t*>(sm + Smem::INFO);
@@ -349,6 +349,377 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
+// Warp-specialised forward for blocks without abs keys.
+//
+// One CTA = one work item (block, <= 128 query rows) x two query heads of the
+// same GQA group, so every rotated K tile and every V tile feeds 256 query
+// rows.  448 threads in roles:
+//   warps 0-3   softmax of head 2y     (thread = query row = TMEM lane)
+//   warps 4-7   softmax of head 2y + 1
+//   warp  8     TMA producer: K and V tiles into a 2-deep ring
+//   warp  9     MMA issuer (lane 0) and TMEM owner
+//   warps 10-13 rotate each K tile in place by its keys' block positions
+// TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512).
+// Softmax t reads S_t, writes P_t (bf16, two per column) over the first 64
+// columns of S_t, and the PV MMA takes P_t straight from TMEM.  MMA order
+// per key tile j: PV0(j), S0(j+1), PV1(j), S1(j+1): while one softmax group
+// works the tensor core runs the other group's MMAs.  S_t(j+1) is issued
+// only once PV_t(j) has completed, since it overwrites P_t.
+// ---------------------------------------------------------------------------
+namespace ws {
+constexpr int kThreads = 448;
+constexpr uint32_t Q0 = 0, Q1 = kTile, KB = 2 * kTile, VB = 4 * kTile;  // K ring at KB, V ring at VB
+constexpr uint32_t INFO = 6 * kTile;                                    // [2][128] u32
+constexpr uint32_t BARS = INFO + 2 * 4 * BN;
+enum Bar { KV_FULL = 0, K_READY = 2, KV_EMPTY = 4, S_FULL = 6, P_READY = 8, O_DONE = 10, Q_READY = 12, FINAL = 13,
+           N_BARS = 14 };
+constexpr uint32_t TMEM_SLOT = BARS + 8 * N_BARS;
+constexpr uint32_t ABORT = TMEM_SLOT + 4;
+constexpr uint32_t TOTAL = ABORT + 4;
+constexpr size_t kSmem = TOTAL + 1024;
+constexpr uint32_t C_S0 = 0, C_S1 = 128, C_O0 = 256, C_O1 = 384;
+constexpr long long kWait = 1000000000LL;
+}  // namespace ws
+
+__global__ void __launch_bounds__(ws::kThreads, 1)
+    fwd_ws_kernel(const AiAttnFwdArgs a, const __grid_constant__ CUtensorMap tm_k,
+                  const __grid_constant__ CUtensorMap tm_v) {
+  using namespace ws;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = tile::align1024(smem_raw);
+  const uint32_t sbase = ptx::smem_u32(sm);
+  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+  uint32_t* s_info = reinterpret_cast<uint32_t*>(sm + INFO);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(sm + ABORT);
+  auto bar = [&](int i) { return sbase + BARS + 8u * (uint32_t)i; };
+
+  const AiAttnLayout& L = a.layout;
+  const int32_t* item = L.fwd_items + 4 * (int64_t)(L.n_fwd_abs_items + blockIdx.x);
+  const Block blk = load_block(L.blocks, item[0]);
+  const int q0 = item[1], q1 = item[2];
+  const int G = a.num_q_heads / a.num_kv_heads, hk = (2 * blockIdx.y) / G, b = blk.row;
+  const int kv_lo = blk.kv_lo, kv_hi = min(blk.e, q1);
+  const int n = kv_hi > kv_lo ? (kv_hi - kv_lo + BN - 1) / BN : 0;
+  const bool blk_masked = (blk.flags & AI_BLOCKF_MASKED) != 0;
+
+  if (tid == 0) {
+    ptx::mbar_init(bar(KV_FULL), 1);
+    ptx::mbar_init(bar(KV_FULL + 1), 1);
+    ptx::mbar_init(bar(K_READY), 128);
+    ptx::mbar_init(bar(K_READY + 1), 128);
+    ptx::mbar_init(bar(KV_EMPTY), 1);
+    ptx::mbar_init(bar(KV_EMPTY + 1), 1);
+    ptx::mbar_init(bar(S_FULL), 1);
+    ptx::mbar_init(bar(S_FULL + 1), 1);
+    ptx::mbar_init(bar(P_READY), 128);
+    ptx::mbar_init(bar(P_READY + 1), 128);
+    ptx::mbar_init(bar(O_DONE), 1);
+    ptx::mbar_init(bar(O_DONE + 1), 1);
+    ptx::mbar_init(bar(Q_READY), 256);
+    ptx::mbar_init(bar(FINAL), 1);
+    *s_abort = 0;
+    ptx::fence_mbar_init();
+  }
+  if (warp == 9) {
+    ptx::tmem_alloc(sbase + TMEM_SLOT, kTmemCols);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sm + TMEM_SLOT);
+
+  // Bounded wait; on expiry flag the CTA (every role then leaves its loop).
+  auto wait = [&](int i, uint32_t parity) -> bool {
+    if (*s_abort) return false;
+    if (!ptx::mbar_wait(bar(i), parity, kWait)) {
+      report(a.status, AI_ERR_DEV_TIMEOUT);
+      *s_abort = 1;
+      return false;
+    }
+    return true;
+  };
+
+  if (warp < 8) {
+    // ------------------------------------------------------------ softmax
+    const int t = warp / 4, r = tid % 128, i = q0 + r, h = 2 * blockIdx.y + t;
+    const uint32_t lane_base = (uint32_t)((warp % 4) * 32) << 16;
+    const uint32_t c_s = t ? C_S1 : C_S0, c_o = t ? C_O1 : C_O0;
+    {
+      // Query row i of head h, rotated by its position: all global loads of
+      // a half row are issued before any of it is rotated and stored.
+      const __nv_bfloat16* Qrow = static_cast<const __nv_bfloat16*>(a.q.ptr) + b * a.q.stride_b +
+                                  h * a.q.stride_h + (int64_t)i * a.q.stride_t;
+      int p = 0;
+      if (i < q1) p = clamp_row(L.q_pos[(int64_t)b * a.seq_len + i], L.n_pos, a.status);
+      const uint4* tab = reinterpret_cast<const uint4*>(static_cast<const __half2*>(L.rope_cs16) + (int64_t)p * (D / 2));
+      const uint32_t qt = t ? Q1 : Q0;
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        uint4 x1[4], x2[4], cs[8];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int cc = 4 * hf + c;
+          x1[c] = i < q1 ? __ldg(reinterpret_cast<const uint4*>(Qrow + 8 * cc)) : make_uint4(0, 0, 0, 0);
+          x2[c] = i < q1 ? __ldg(reinterpret_cast<const uint4*>(Qrow + 64 + 8 * cc)) : make_uint4(0, 0, 0, 0);
+          cs[2 * c] = __ldg(tab + 2 * cc);
+          cs[2 * c + 1] = __ldg(tab + 2 * cc + 1);
+        }
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int cc = 4 * hf + c;
+          uint4 y1, y2;
+          tile::rotate8h(x1[c], x2[c], cs[2 * c], cs[2 * c + 1], y1, y2);
+          *reinterpret_cast<uint4*>(sm + qt + chunk_off(r, cc)) = y1;
+          *reinterpret_cast<uint4*>(sm + qt + chunk_off(r, cc + 8)) = y2;
+        }
+      }
+      ptx::fence_proxy_async_smem();
+      ptx::mbar_arrive(bar(Q_READY));
+    }
+    const float sl2 = a.scale * kLog2e;
+    float m_use = -CUDART_INF_F, l = 0.f;
+    int done = 0;
+    for (int j = 0; j < n; ++j) {
+      const int slot = j & 1, k0 = kv_lo + j * BN;
+      if (!wait(S_FULL + t, j & 1)) break;
+      ptx::tc_fence_after();
+      // Scores are read from TMEM twice (max pass, then exp pass), 64 columns
+      // per load round, so that at most 64 scores are live in registers.
+      // Tiles wholly below the diagonal of a block without masked keys skip
+      // the mask.
+      const bool fast = !blk_masked && (k0 + BN <= kv_hi) && (k0 + BN - 1 <= q0);
+      const uint32_t* info = s_info + slot * BN;
+      auto load64 = [&](int hf, uint32_t (&r0)[32], uint32_t (&r1)[32]) {
+        ptx::tmem_ld32(tmem + lane_base + c_s + 64 * hf, r0);
+        ptx::tmem_ld32(tmem + lane_base + c_s + 64 * hf + 32, r1);
+        ptx::tmem_wait_ld();
+        if (!fast) {
+#pragma unroll
+          for (int x = 0; x < 32; ++x) {
+            const int c0 = 64 * hf + x, c1 = c0 + 32;
+            if (!((info[c0] & AI_KEY_ATTN) && (k0 + c0 <= i))) r0[x] = 0xff800000u;  // -inf
+            if (!((info[c1] & AI_KEY_ATTN) && (k0 + c1 <= i))) r1[x] = 0xff800000u;
+          }
+        }
+      };
+      float mxa = -CUDART_INF_F, mxb = -CUDART_INF_F, mxc = -CUDART_INF_F, mxd = -CUDART_INF_F;
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        uint32_t r0[32], r1[32];
+        load64(hf, r0, r1);
+#pragma unroll
+        for (int x = 0; x < 32; x += 2) {
+          mxa = fmaxf(mxa, __uint_as_float(r0[x]));
+          mxb = fmaxf(mxb, __uint_as_float(r0[x + 1]));
+          mxc = fmaxf(mxc, __uint_as_float(r1[x]));
+          mxd = fmaxf(mxd, __uint_as_float(r1[x + 1]));
+        }
+      }
+      const float mx = fmaxf(fmaxf(mxa, mxb), fmaxf(mxc, mxd));
+      const float m_new = fmaxf(m_use, mx * sl2);
+      float alpha = 1.f;
+      bool rescale = false;
+      if (m_new > m_use + 8.f) {
+        if (j > 0 && l > 0.f) {
+          alpha = ptx::ex2(m_use - m_new);
+          rescale = true;
+        }
+        m_use = m_new;
+      }
+      if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll
+        for (int cc = 0; cc < D / 32; ++cc) {
+          uint32_t rr[32];
+          ptx::tmem_ld32(tmem + lane_base + c_o + 32 * cc, rr);
+          ptx::tmem_wait_ld();
+#pragma unroll
+          for (int x = 0; x < 32; ++x) rr[x] = __float_as_uint(__uint_as_float(rr[x]) * alpha);
+          ptx::tmem_st32(tmem + lane_base + c_o + 32 * cc, rr);
+        }
+      }
+      l *= alpha;
+      const float msub = m_use == -CUDART_INF_F ? 0.f : m_use;
+      float suma = 0.f, sumb = 0.f;
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        uint32_t r0[32], r1[32], pk[32];
+        load64(hf, r0, r1);
+#pragma unroll
+        for (int x = 0; x < 16; ++x) {
+          const float p0 = ptx::ex2(fmaf(__uint_as_float(r0[2 * x]), sl2, -msub));
+          const float p1 = ptx::ex2(fmaf(__uint_as_float(r0[2 * x + 1]), sl2, -msub));
+          const float p2 = ptx::ex2(fmaf(__uint_as_float(r1[2 * x]), sl2, -msub));
+          const float p3 = ptx::ex2(fmaf(__uint_as_float(r1[2 * x + 1]), sl2, -msub));
+          suma += p0 + p1;
+          sumb += p2 + p3;
+          pk[x] = tile::pack2(p0, p1);
+          pk[16 + x] = tile::pack2(p2, p3);
+        }
+        ptx::tmem_st32(tmem + lane_base + c_s + 32 * hf, pk);
+      }
+      l += suma + sumb;
+      ptx::tmem_wait_st();
+      ptx::tc_fence_before();
+      ptx::mbar_arrive(bar(P_READY + t));
+      done = j + 1;
+    }
+    // Epilogue: O_t / l.
+    bool have_o = false;
+    if (done == n && n > 0) have_o = wait(O_DONE + t, (n - 1) & 1);
+    if (!*s_abort) {
+      ptx::tc_fence_after();
+      __nv_bfloat16* Orow = static_cast<__nv_bfloat16*>(a.out.ptr) + b * a.out.stride_b + h * a.out.stride_h +
+                            (int64_t)i * a.out.stride_t;
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+#pragma unroll
+      for (int cc = 0; cc < D / 32; ++cc) {
+        uint32_t rr[32];
+        if (have_o) {
+          ptx::tmem_ld32(tmem + lane_base + c_o + 32 * cc, rr);
+          ptx::tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int x = 0; x < 32; ++x) rr[x] = 0u;
+        }
+        if (i < q1) {
+#pragma unroll
+          for (int c8 = 0; c8 < 4; ++c8) {
+            float f[8];
+#pragma unroll
+            for (int x = 0; x < 8; ++x) f[x] = __uint_as_float(rr[8 * c8 + x]) * inv;
+            *reinterpret_cast<uint4*>(Orow + 32 * cc + 8 * c8) = pack8(f);
+          }
+        }
+      }
+      if (i < q1)
+        a.lse[((int64_t)b * a.num_q_heads + h) * a.seq_len + i] = l > 0.f ? (m_use + log2f(l)) * kLn2 : -CUDART_INF_F;
+    }
+  } else if (warp == 8) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      ptx::prefetch_tmap(&tm_k);
+      ptx::prefetch_tmap(&tm_v);
+      for (int j = 0; j < n; ++j) {
+        const int slot = j & 1, k0 = kv_lo + j * BN;
+        if (j >= 2 && !wait(KV_EMPTY + slot, ((j >> 1) - 1) & 1)) break;
+        const uint32_t kb = sbase + KB + (uint32_t)slot * kTile, vb = sbase + VB + (uint32_t)slot * kTile;
+        ptx::mbar_arrive_expect_tx(bar(KV_FULL + slot), 2 * kTile);
+        ptx::tma_load_4d(kb, &tm_k, bar(KV_FULL + slot), 0, k0, hk, b);
+        ptx::tma_load_4d(kb + kHalf, &tm_k, bar(KV_FULL + slot), 64, k0, hk, b);
+        ptx::tma_load_4d(vb, &tm_v, bar(KV_FULL + slot), 0, k0, hk, b);
+        ptx::tma_load_4d(vb + kHalf, &tm_v, bar(KV_FULL + slot), 64, k0, hk, b);
+      }
+    }
+  } else if (warp == 9) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_qk = ptx::idesc_bf16_f32(BM, BN, false, false);
+      constexpr uint32_t idesc_pv = ptx::idesc_bf16_f32(BM, D, false, true);
+      auto issue_s = [&](int t, int slot) {
+        const uint32_t qt = sbase + (t ? Q1 : Q0), kt = sbase + KB + (uint32_t)slot * kTile;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (uint32_t)(kk >> 2) * kHalf + (uint32_t)(kk & 3) * 32u;
+          ptx::mma_ss(tmem + (t ? C_S1 : C_S0), ptx::sdesc_sw128(qt + off, 16, 1024),
+                      ptx::sdesc_sw128(kt + off, 16, 1024), idesc_qk, kk > 0);
+        }
+        ptx::mma_commit(bar(S_FULL + t));
+      };
+      auto issue_pv = [&](int t, int slot, bool first) {
+        const uint32_t vt = sbase + VB + (uint32_t)slot * kTile;
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          ptx::mma_ts(tmem + (t ? C_O1 : C_O0), tmem + (t ? C_S1 : C_S0) + 8u * (uint32_t)kk,
+                      ptx::sdesc_sw128(vt + (uint32_t)kk * 2048u, kHalf, 1024), idesc_pv,
+                      (!first || kk > 0) ? 1u : 0u);
+        }
+        ptx::mma_commit(bar(O_DONE + t));
+      };
+      bool ok = wait(Q_READY, 0);
+      if (ok && n > 0 && wait(K_READY, 0)) {
+        ptx::tc_fence_after();
+        issue_s(0, 0);
+        issue_s(1, 0);
+        for (int j = 0; j < n; ++j) {
+          const int slot = j & 1, nslot = (j + 1) & 1;
+          const bool more = j + 1 < n;
+          if (!wait(P_READY, j & 1)) break;
+          ptx::tc_fence_after();
+          issue_pv(0, slot, j == 0);
+          if (more) {
+            if (!wait(K_READY + nslot, ((j + 1) >> 1) & 1) || !wait(O_DONE, j & 1)) break;
+            ptx::tc_fence_after();
+            issue_s(0, nslot);
+          }
+          if (!wait(P_READY + 1, j & 1)) break;
+          ptx::tc_fence_after();
+          issue_pv(1, slot, j == 0);
+          ptx::mma_commit(bar(KV_EMPTY + slot));
+          if (more) {
+            if (!wait(O_DONE + 1, j & 1)) break;
+            ptx::tc_fence_after();
+            issue_s(1, nslot);
+          }
+        }
+      }
+      // Drain: every MMA issued so far has completed before TMEM is released.
+      ptx::mma_commit(bar(FINAL));
+      ptx::mbar_wait(bar(FINAL), 0, kWait);
+    }
+  } else {
+    // ------------------------------------------------------------ K rotation (warps 10-13)
+    // Thread = key row of the tile.  The key's position word and its fp16
+    // (cos, sin) row are fetched for tile j+1 while tile j is rotated, so the
+    // L2 latency hides behind the wait for the next TMA.
+    const int row = tid - 320;
+    const __half2* cs16 = static_cast<const __half2*>(L.rope_cs16);
+    uint32_t info = 0;
+    uint4 tab[16];
+    auto fetch = [&](int j) {
+      const int key = kv_lo + j * BN + row;
+      info = 0;
+      int p = 0;
+      if (key < kv_hi) {
+        info = (uint32_t)__ldg(L.key_info + blk.key_off + key);
+        p = key_row(info, L.n_pos, a.status);
+      }
+      const uint4* tp = reinterpret_cast<const uint4*>(cs16 + (int64_t)p * (D / 2));
+#pragma unroll
+      for (int c = 0; c < 16; ++c) tab[c] = __ldg(tp + c);
+    };
+    if (n > 0) fetch(0);
+    for (int j = 0; j < n; ++j) {
+      const int slot = j & 1;
+      if (!wait(KV_FULL + slot, (j >> 1) & 1)) break;
+      const uint32_t kt = KB + (uint32_t)slot * kTile;
+      if (info != 0 || kv_lo + j * BN + row < kv_hi) {
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          uint4* pa = reinterpret_cast<uint4*>(sm + kt + chunk_off(row, c));
+          uint4* pb = reinterpret_cast<uint4*>(sm + kt + chunk_off(row, c + 8));
+          uint4 y1, y2;
+          tile::rotate8h(*pa, *pb, tab[2 * c], tab[2 * c + 1], y1, y2);
+          *pa = y1;
+          *pb = y2;
+        }
+      }
+      s_info[slot * BN + row] = info;
+      ptx::fence_proxy_async_smem();
+      ptx::mbar_arrive(bar(K_READY + slot));
+      if (j + 1 < n) fetch(j + 1);
+    }
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
 
@@ -396,10 +767,26 @@ int sm100_fwd(const AiAttnFwdArgs& a, cudaStream_t st, cudaError_t* cuda_err) {
   CUtensorMap tm_k, tm_v;
   if (!sm100_make_map(&tm_k, a.k, a.batch, a.num_kv_heads, a.seq_len, BN)) return AI_ERR_TMA;
   if (!sm100_make_map(&tm_v, a.v, a.batch, a.num_kv_heads, a.seq_len, BN)) return AI_ERR_TMA;
-  cudaError_t e = cudaFuncSetAttribute(fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
-  if (e == cudaSuccess) {
-    fwd_kernel<<<dim3(a.layout.n_fwd_items, a.num_q_heads), kThreads, kSmemBytes, st>>>(a, tm_k, tm_v);
-    e = cudaGetLastError();
+  // Items of blocks with abs keys (and every item when a GQA group has an odd
+  // number of query heads) run on the one-head kernel; the rest run two heads
+  // per CTA on the warp-specialised kernel.
+  const int G = a.num_q_heads / a.num_kv_heads;
+  const int n_single = (G % 2 == 0) ? a.layout.n_fwd_abs_items : a.layout.n_fwd_items;
+  const int n_pair = a.layout.n_fwd_items - n_single;
+  cudaError_t e = cudaSuccess;
+  if (n_single > 0) {
+    e = cudaFuncSetAttribute(fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+    if (e == cudaSuccess) {
+      fwd_kernel<<<dim3(n_single, a.num_q_heads), kThreads, kSmemBytes, st>>>(a, tm_k, tm_v);
+      e = cudaGetLastError();
+    }
+  }
+  if (e == cudaSuccess && n_pair > 0) {
+    e = cudaFuncSetAttribute(fwd_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ws::kSmem);
+    if (e == cudaSuccess) {
+      fwd_ws_kernel<<<dim3(n_pair, a.num_q_heads / 2), ws::kThreads, ws::kSmem, st>>>(a, tm_k, tm_v);
+      e = cudaGetLastError();
+    }
   }
   if (cuda_err) *cuda_err = e;
   return e == cudaSuccess ? AI_OK : AI_ERR_LAUNCH;

@@ -41,7 +41,8 @@ int validate_fwd(const AiAttnFwdArgs* a) {
   if (!tensor_ok(a->q) || !tensor_ok(a->k) || !tensor_ok(a->v) || !tensor_ok(a->out)) return AI_ERR_NULL;
   if (!a->lse) return AI_ERR_NULL;
   const AiAttnLayout& L = a->layout;
-  if (!L.blocks || !L.row_blocks || !L.row_cov || !L.key_info || !L.q_pos || !L.rope_cos || !L.rope_sin)
+  if (!L.blocks || !L.row_blocks || !L.row_cov || !L.key_info || !L.q_pos || !L.rope_cos || !L.rope_sin ||
+      !L.rope_cs16)
     return AI_ERR_NULL;
   if (L.n_blocks < 0 || L.n_keys < 0 || L.n_pos <= 0 || L.n_fwd_items < 0 || L.n_kv_items < 0) return AI_ERR_LAYOUT;
   if (L.n_fwd_items > 0 && !L.fwd_items) return AI_ERR_NULL;

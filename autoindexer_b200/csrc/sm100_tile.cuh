@@ -8,10 +8,20 @@
 #pragma once
 
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <stdint.h>
 
 namespace ai {
 namespace tile {
+
+// 1024-byte-aligned start inside the dynamic shared memory.  Derived by
+// pointer arithmetic on the __shared__ array (not an integer round trip) so
+// the compiler keeps it in the shared window: shared loads/stores, and no
+// assumed aliasing with global loads.
+__device__ __forceinline__ uint8_t* align1024(uint8_t* smem_raw) {
+  const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(smem_raw));
+  return smem_raw + ((1024u - (a & 1023u)) & 1023u);
+}
 
 // Byte offset of 16-byte chunk c (0..15, 8 elements each) of row r in an
 // R-row tile (c >> 3 selects the column block).
@@ -55,6 +65,25 @@ __device__ __forceinline__ void rotate8(const uint4& a, const uint4& b, const fl
   for (int i = 0; i < 8; ++i) {
     y1[i] = x1[i] * c[i] - x2[i] * s[i];
     y2[i] = x2[i] * c[i] + x1[i] * s[i];
+  }
+  ya = pack8(y1);
+  yb = pack8(y2);
+}
+
+// Same rotation with the angles given as fp16 (cos, sin) pairs: t0 holds the
+// pairs of dims 8c .. 8c+3, t1 those of 8c+4 .. 8c+7.
+__device__ __forceinline__ void rotate8h(const uint4& a, const uint4& b, const uint4& t0, const uint4& t1, uint4& ya,
+                                         uint4& yb) {
+  float x1[8], x2[8], y1[8], y2[8];
+  unpack8(a, x1);
+  unpack8(b, x2);
+  const __half2* h0 = reinterpret_cast<const __half2*>(&t0);
+  const __half2* h1 = reinterpret_cast<const __half2*>(&t1);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float2 cs = __half22float2(i < 4 ? h0[i] : h1[i - 4]);
+    y1[i] = x1[i] * cs.x - x2[i] * cs.y;
+    y2[i] = x2[i] * cs.x + x1[i] * cs.y;
   }
   ya = pack8(y1);
   yb = pack8(y2);

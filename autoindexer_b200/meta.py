@@ -18,7 +18,9 @@ Output (``CompiledLayout``), all int32 / fp32 device tensors:
   0..29), attn mask (bit 30), abs mask (bit 31);
 * ``q_pos [B, T]``: table row of every query row (rows past the covered
   length use position 0, as ``perturb_labels.py:335`` pads);
-* ``rope_cos / rope_sin [n_pos, D/2]``: fp32 table of the rotary module;
+* ``rope_cos / rope_sin [n_pos, D/2]``: fp32 table of the rotary module, and
+  ``rope_cs16 [n_pos, D/2, 2]`` the same angles as fp16 (cos, sin) pairs for
+  the bf16 tensor-core kernels;
 * ``fwd_items [m, 4]``: (block, q0, q1) query tiles, longest first;
 * ``kv_items [k, 4]``: (row, j0, j1) key tiles of the dK/dV pass, longest first.
 
@@ -135,8 +137,10 @@ class CompiledLayout:
     q_pos: torch.Tensor
     rope_cos: torch.Tensor
     rope_sin: torch.Tensor
+    rope_cs16: torch.Tensor
     fwd_items: torch.Tensor
     kv_items: torch.Tensor
+    n_fwd_abs_items: int         # leading fwd_items whose block has abs keys
     pairs_per_head: int          # finite (query, key) logits of one head summed over the batch
     host_blocks: np.ndarray = field(repr=False, default=None)
 
@@ -151,10 +155,12 @@ class CompiledLayout:
         L.q_pos = self.q_pos.data_ptr()
         L.rope_cos = self.rope_cos.data_ptr()
         L.rope_sin = self.rope_sin.data_ptr()
+        L.rope_cs16 = self.rope_cs16.data_ptr()
         L.n_pos = int(self.n_pos)
         L.fwd_tile = int(self.fwd_tile)
         L.fwd_items = self.fwd_items.data_ptr() if self.fwd_items.numel() else None
         L.n_fwd_items = int(self.fwd_items.shape[0])
+        L.n_fwd_abs_items = int(self.n_fwd_abs_items)
         L.kv_tile = int(self.kv_tile)
         L.kv_items = self.kv_items.data_ptr() if self.kv_items.numel() else None
         L.n_kv_items = int(self.kv_items.shape[0])
@@ -168,7 +174,9 @@ def _tiles(fwd_tile: int, kv_tile: int, blocks: np.ndarray, row_cov: np.ndarray)
             q1 = min(q0 + fwd_tile, e)
             cost = (q1 - q0) * max(0, min(e, q1) - kv_lo)
             fwd.append((cost, bi, q0, q1))
-    fwd.sort(key=lambda t: -t[0])
+    # Items of blocks with abs keys first (they run on their own kernel), then longest first.
+    fwd.sort(key=lambda t: (-(int(blocks[t[1], 5]) & BLOCKF_ABS), -t[0]))
+    n_abs = sum(1 for t in fwd if int(blocks[t[1], 5]) & BLOCKF_ABS)
     kv = []
     for row, cov in enumerate(row_cov):
         for j0 in range(0, int(cov), kv_tile):
@@ -177,7 +185,7 @@ def _tiles(fwd_tile: int, kv_tile: int, blocks: np.ndarray, row_cov: np.ndarray)
     kv.sort(key=lambda t: -t[0])
     fwd_arr = np.asarray([(bi, q0, q1, 0) for _, bi, q0, q1 in fwd], dtype=np.int32).reshape(-1, 4)
     kv_arr = np.asarray([(row, j0, j1, 0) for _, row, j0, j1 in kv], dtype=np.int32).reshape(-1, 4)
-    return fwd_arr, kv_arr
+    return fwd_arr, kv_arr, n_abs
 
 
 def compile_layout(parsed_positions, batch: int, seq_len: int, head_dim: int, dtype: torch.dtype,
@@ -269,7 +277,7 @@ def _compile(parsed_positions, batch, seq_len, head_dim, code, rotary_emb, devic
     lib = _lib.lib()
     fwd_tile = lib.ai_attn_fwd_tile_rows(code, head_dim)
     kv_tile = lib.ai_attn_kv_tile_rows(code, head_dim)
-    fwd_items, kv_items = _tiles(fwd_tile, kv_tile, blocks_np, row_cov_np)
+    fwd_items, kv_items, n_abs = _tiles(fwd_tile, kv_tile, blocks_np, row_cov_np)
 
     cos, sin = rope_table(rotary_emb, lo, hi, head_dim, device)
 
@@ -281,5 +289,7 @@ def _compile(parsed_positions, batch, seq_len, head_dim, code, rotary_emb, devic
         fwd_tile=fwd_tile, kv_tile=kv_tile,
         blocks=dev(blocks_np), row_blocks=dev(np.asarray(row_blocks, dtype=np.int32)), row_cov=dev(row_cov_np),
         key_info=dev(key_info), q_pos=dev(q_pos), rope_cos=cos, rope_sin=sin,
-        fwd_items=dev(fwd_items), kv_items=dev(kv_items), pairs_per_head=pairs, host_blocks=blocks_np,
+        rope_cs16=torch.stack([cos, sin], dim=-1).to(torch.float16).contiguous(),
+        fwd_items=dev(fwd_items), kv_items=dev(kv_items), n_fwd_abs_items=n_abs, pairs_per_head=pairs,
+        host_blocks=blocks_np,
     )

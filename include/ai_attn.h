@@ -43,7 +43,7 @@
 extern "C" {
 #endif
 
-#define AI_ATTN_ABI_VERSION 1
+#define AI_ATTN_ABI_VERSION 2
 
 typedef enum AiDtype {
   AI_DTYPE_BF16 = 0,
@@ -103,10 +103,13 @@ typedef struct AiAttnLayout {
   const int32_t* q_pos;       /* [B][T] rotary table row of each query row */
   const float* rope_cos;      /* [n_pos][D/2] fp32: cos of the angle of (table row, frequency slot) */
   const float* rope_sin;      /* [n_pos][D/2] */
+  const void* rope_cs16;      /* [n_pos][D/2] fp16 pairs (cos, sin) of the same angles: the bf16 kernels'
+                                 copy (fp16 keeps 11 bits, above the bf16 operands they rotate) */
   int32_t n_pos;
   int32_t fwd_tile;           /* query rows per forward / dQ work item (ai_attn_fwd_tile_rows) */
   const int32_t* fwd_items;   /* [n_fwd_items][4]: block, q0, q1, 0 */
   int32_t n_fwd_items;
+  int32_t n_fwd_abs_items;    /* the first n_fwd_abs_items items belong to blocks with AI_BLOCKF_ABS */
   int32_t kv_tile;            /* keys per dK/dV work item (ai_attn_kv_tile_rows) */
   const int32_t* kv_items;    /* [n_kv_items][4]: row, j0, j1, 0 */
   int32_t n_kv_items;

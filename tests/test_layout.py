@@ -53,6 +53,10 @@ def test_tables_match_layout(name, dtype):
     assert np.array_equal(qp[:T], lay.query_pos_ids.numpy())
     assert np.all(qp[T:] == 0)
     assert c.pairs_per_head == 2 * O.count_pairs(lay, T)
+    # abs items lead the forward work list
+    items = c.fwd_items.numpy()
+    is_abs = (blocks[items[:, 0], 5] & 2) != 0
+    assert is_abs.sum() == c.n_fwd_abs_items and is_abs[:c.n_fwd_abs_items].all()
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
