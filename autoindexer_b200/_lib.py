@@ -77,6 +77,7 @@ class AiAttnLayout(ctypes.Structure):
         ("kv_tile", ctypes.c_int32),
         ("kv_items", ctypes.c_void_p),
         ("n_kv_items", ctypes.c_int32),
+        ("n_kv_abs_items", ctypes.c_int32),
     ]
 
 

@@ -721,6 +721,752 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ===========================================================================
+// dQ, warp-specialised (work items of blocks without abs keys)
+//
+// One CTA = one forward work item x two query heads of one GQA group.  448
+// threads: warps 0-3 / 4-7 score groups of head 2y / 2y+1 (thread = query
+// row = TMEM lane); warp 8 TMA producer (64-key K and V tiles, 2-deep ring);
+// warp 9 MMA issuer; warps 10-13 rotate each K tile by the keys' block
+// positions.  TMEM per head t: S_t [128t .. +64), dP_t [+64 .. +128), dQ_t
+// accumulator [256 + 128t .. +128).  dS_t (bf16 pairs) overwrites the first 32
+// columns of S_t and is the A operand of dQ_t += dS_t.Krot; the next S_t is
+// issued only after that MMA completed.  MMA order per key tile j:
+// dQ0(j), S0/dP0(j+1), dQ1(j), S1/dP1(j+1).
+// ===========================================================================
+namespace dqw {
+constexpr int BM = 128, BN = 64, kThreads = 448;
+constexpr uint32_t Q0 = 0, Q1 = 32768, DO0 = 65536, DO1 = 98304;  // 128 x 128 bf16 each
+constexpr uint32_t KB = 131072, VB = KB + 2 * 16384;              // rings of 64 x 128 bf16
+constexpr uint32_t INFO = VB + 2 * 16384;                         // [2][64] u32
+constexpr uint32_t BARS = INFO + 2 * 4 * BN;
+enum Bar { KV_FULL = 0, K_READY = 2, KV_EMPTY = 4, S_FULL = 6, DS_READY = 8, DQ_DONE = 10, Q_READY = 12,
+           FINAL = 13, N_BARS = 14 };
+constexpr uint32_t TMEM_SLOT = BARS + 8 * N_BARS;
+constexpr uint32_t ABORT = TMEM_SLOT + 4;
+constexpr uint32_t TOTAL = ABORT + 4;
+constexpr size_t kSmem = TOTAL + 1024;
+constexpr long long kWait = 1000000000LL;
+}  // namespace dqw
+
+__global__ void __launch_bounds__(dqw::kThreads, 1)
+    dq_ws_kernel(const AiAttnBwdArgs a, const float* __restrict__ delta, const __grid_constant__ CUtensorMap tm_k,
+                 const __grid_constant__ CUtensorMap tm_v) {
+  using namespace dqw;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = tile::align1024(smem_raw);
+  const uint32_t sbase = ptx::smem_u32(sm);
+  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+  uint32_t* s_info = reinterpret_cast<uint32_t*>(sm + INFO);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(sm + ABORT);
+  auto bar = [&](int i) { return sbase + BARS + 8u * (uint32_t)i; };
+
+  const AiAttnFwdArgs& f = a.fwd;
+  const AiAttnLayout& L = f.layout;
+  const int32_t* item = L.fwd_items + 4 * (int64_t)(L.n_fwd_abs_items + blockIdx.x);
+  const Block blk = load_block(L.blocks, item[0]);
+  const int q0 = item[1], q1 = item[2];
+  const int G = f.num_q_heads / f.num_kv_heads, hk = (2 * blockIdx.y) / G, b = blk.row;
+  const int kv_lo = blk.kv_lo, kv_hi = min(blk.e, q1);
+  const int n = kv_hi > kv_lo ? (kv_hi - kv_lo + BN - 1) / BN : 0;
+  const bool blk_masked = (blk.flags & AI_BLOCKF_MASKED) != 0;
+  const __half2* cs16 = static_cast<const __half2*>(L.rope_cs16);
+
+  if (tid == 0) {
+    for (int i = 0; i < N_BARS; ++i) {
+      uint32_t count = 1;
+      if (i == K_READY || i == K_READY + 1 || i == DS_READY || i == DS_READY + 1) count = 128;
+      if (i == Q_READY) count = 256;
+      ptx::mbar_init(bar(i), count);
+    }
+    *s_abort = 0;
+    ptx::fence_mbar_init();
+  }
+  if (warp == 9) {
+    ptx::tmem_alloc(sbase + TMEM_SLOT, kTmemCols);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sm + TMEM_SLOT);
+
+  auto wait = [&](int i, uint32_t parity) -> bool {
+    if (*s_abort) return false;
+    if (!ptx::mbar_wait(bar(i), parity, kWait)) {
+      report(f.status, AI_ERR_DEV_TIMEOUT);
+      *s_abort = 1;
+      return false;
+    }
+    return true;
+  };
+
+  if (warp < 8) {
+    // ------------------------------------------------------------ score groups
+    const int t = warp / 4, r = tid % 128, i = q0 + r, h = 2 * blockIdx.y + t;
+    const uint32_t lane_base = (uint32_t)((warp % 4) * 32) << 16;
+    const uint32_t c_s = 128u * (uint32_t)t, c_dq = 256u + 128u * (uint32_t)t;
+    int qrow = 0;
+    float lse2 = 0.f, dl = 0.f;
+    {
+      const __nv_bfloat16* Qrow = static_cast<const __nv_bfloat16*>(f.q.ptr) + b * f.q.stride_b + h * f.q.stride_h +
+                                  (int64_t)i * f.q.stride_t;
+      const __nv_bfloat16* dOrow = static_cast<const __nv_bfloat16*>(a.dout.ptr) + b * a.dout.stride_b +
+                                   h * a.dout.stride_h + (int64_t)i * a.dout.stride_t;
+      if (i < q1) {
+        qrow = clamp_row(L.q_pos[(int64_t)b * f.seq_len + i], L.n_pos, f.status);
+        const int64_t idx = ((int64_t)b * f.num_q_heads + h) * f.seq_len + i;
+        lse2 = lse_log2(f.lse[idx]);
+        dl = delta[idx];
+      }
+      const uint4* tab = reinterpret_cast<const uint4*>(cs16 + (int64_t)qrow * (D / 2));
+      const uint32_t qt = t ? Q1 : Q0, ot = t ? DO1 : DO0;
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        uint4 x1[4], x2[4], g1[4], g2[4], cs[8];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int cc = 4 * hf + c;
+          const uint4 z = make_uint4(0, 0, 0, 0);
+          x1[c] = i < q1 ? __ldg(reinterpret_cast<const uint4*>(Qrow + 8 * cc)) : z;
+          x2[c] = i < q1 ? __ldg(reinterpret_cast<const uint4*>(Qrow + 64 + 8 * cc)) : z;
+          g1[c] = i < q1 ? __ldg(reinterpret_cast<const uint4*>(dOrow + 8 * cc)) : z;
+          g2[c] = i < q1 ? __ldg(reinterpret_cast<const uint4*>(dOrow + 64 + 8 * cc)) : z;
+          cs[2 * c] = __ldg(tab + 2 * cc);
+          cs[2 * c + 1] = __ldg(tab + 2 * cc + 1);
+        }
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int cc = 4 * hf + c;
+          uint4 y1, y2;
+          tile::rotate8h(x1[c], x2[c], cs[2 * c], cs[2 * c + 1], y1, y2);
+          *reinterpret_cast<uint4*>(sm + qt + chunk_off<BM>(r, cc)) = y1;
+          *reinterpret_cast<uint4*>(sm + qt + chunk_off<BM>(r, cc + 8)) = y2;
+          *reinterpret_cast<uint4*>(sm + ot + chunk_off<BM>(r, cc)) = g1[c];
+          *reinterpret_cast<uint4*>(sm + ot + chunk_off<BM>(r, cc + 8)) = g2[c];
+        }
+      }
+      ptx::fence_proxy_async_smem();
+      ptx::mbar_arrive(bar(Q_READY));
+    }
+    const float sl2 = f.scale * kLog2e;
+    int done = 0;
+    for (int j = 0; j < n; ++j) {
+      const int slot = j & 1, k0 = kv_lo + j * BN;
+      if (!wait(S_FULL + t, j & 1)) break;
+      ptx::tc_fence_after();
+      const bool fast = !blk_masked && (k0 + BN <= kv_hi) && (k0 + BN - 1 <= q0);
+      const uint32_t* info = s_info + slot * BN;
+      uint32_t pk[32];
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        uint32_t rs[32], rp[32];
+        ptx::tmem_ld32(tmem + lane_base + c_s + 32 * hf, rs);
+        ptx::tmem_ld32(tmem + lane_base + c_s + 64 + 32 * hf, rp);
+        ptx::tmem_wait_ld();
+#pragma unroll
+        for (int x2 = 0; x2 < 16; ++x2) {
+          float ds[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int cl = 2 * x2 + u, c = 32 * hf + cl;
+            bool ok = i < q1;
+            if (!fast) ok = ok && (info[c] & AI_KEY_ATTN) && (k0 + c <= i);
+            const float p = ok ? ptx::ex2(fmaf(__uint_as_float(rs[cl]), sl2, -lse2)) : 0.f;
+            ds[u] = p * (__uint_as_float(rp[cl]) - dl) * f.scale;
+          }
+          pk[16 * hf + x2] = tile::pack2(ds[0], ds[1]);
+        }
+      }
+      ptx::tmem_st32(tmem + lane_base + c_s, pk);
+      ptx::tmem_wait_st();
+      ptx::tc_fence_before();
+      ptx::mbar_arrive(bar(DS_READY + t));
+      done = j + 1;
+    }
+    // Epilogue: dQ = R(qpos)^T dQrot.
+    bool have = false;
+    if (done == n && n > 0) have = wait(DQ_DONE + t, (n - 1) & 1);
+    if (!*s_abort) {
+      ptx::tc_fence_after();
+      __nv_bfloat16* dQrow = static_cast<__nv_bfloat16*>(a.dq.ptr) + b * a.dq.stride_b + h * a.dq.stride_h +
+                             (int64_t)i * a.dq.stride_t;
+      const uint4* tab = reinterpret_cast<const uint4*>(cs16 + (int64_t)qrow * (D / 2));
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        uint32_t g1[32], g2[32];
+        if (have) {
+          ptx::tmem_ld32(tmem + lane_base + c_dq + 32 * hf, g1);
+          ptx::tmem_ld32(tmem + lane_base + c_dq + 64 + 32 * hf, g2);
+          ptx::tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int x = 0; x < 32; ++x) g1[x] = g2[x] = 0u;
+        }
+        float o1[32], o2[32];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const uint4 tv = __ldg(tab + 8 * hf + q);
+          const __half2* h2 = reinterpret_cast<const __half2*>(&tv);
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int xx = 4 * q + u;
+            const float2 csn = __half22float2(h2[u]);
+            const float v1 = __uint_as_float(g1[xx]), v2 = __uint_as_float(g2[xx]);
+            o1[xx] = v1 * csn.x + v2 * csn.y;
+            o2[xx] = v2 * csn.x - v1 * csn.y;
+          }
+        }
+        if (i < q1) {
+          store_bf16_row32(dQrow + 32 * hf, o1);
+          store_bf16_row32(dQrow + 64 + 32 * hf, o2);
+        }
+      }
+    }
+  } else if (warp == 8) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      ptx::prefetch_tmap(&tm_k);
+      ptx::prefetch_tmap(&tm_v);
+      for (int j = 0; j < n; ++j) {
+        const int slot = j & 1, k0 = kv_lo + j * BN;
+        if (j >= 2 && !wait(KV_EMPTY + slot, ((j >> 1) - 1) & 1)) break;
+        const uint32_t kb = sbase + KB + 16384u * (uint32_t)slot, vb = sbase + VB + 16384u * (uint32_t)slot;
+        ptx::mbar_arrive_expect_tx(bar(KV_FULL + slot), 32768);
+        ptx::tma_load_4d(kb, &tm_k, bar(KV_FULL + slot), 0, k0, hk, b);
+        ptx::tma_load_4d(kb + 8192, &tm_k, bar(KV_FULL + slot), 64, k0, hk, b);
+        ptx::tma_load_4d(vb, &tm_v, bar(KV_FULL + slot), 0, k0, hk, b);
+        ptx::tma_load_4d(vb + 8192, &tm_v, bar(KV_FULL + slot), 64, k0, hk, b);
+      }
+    }
+  } else if (warp == 9) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = ptx::idesc_bf16_f32(BM, BN, false, false);
+      constexpr uint32_t idesc_dq = ptx::idesc_bf16_f32(BM, D, false, true);
+      auto issue_s = [&](int t, int slot) {
+        const uint32_t qt = sbase + (t ? Q1 : Q0), ot = sbase + (t ? DO1 : DO0);
+        const uint32_t kt = sbase + KB + 16384u * (uint32_t)slot, vt = sbase + VB + 16384u * (uint32_t)slot;
+        const uint32_t cs = tmem + 128u * (uint32_t)t;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t ao = (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u;
+          const uint32_t bo = (uint32_t)(kk >> 2) * 8192u + (uint32_t)(kk & 3) * 32u;
+          ptx::mma_ss(cs, ptx::sdesc_sw128(qt + ao, 16, 1024), ptx::sdesc_sw128(kt + bo, 16, 1024), idesc_s, kk > 0);
+          ptx::mma_ss(cs + 64, ptx::sdesc_sw128(ot + ao, 16, 1024), ptx::sdesc_sw128(vt + bo, 16, 1024), idesc_s,
+                      kk > 0);
+        }
+        ptx::mma_commit(bar(S_FULL + t));
+      };
+      auto issue_dq = [&](int t, int slot, bool first) {
+        const uint32_t kt = sbase + KB + 16384u * (uint32_t)slot;
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk)
+          ptx::mma_ts(tmem + 256u + 128u * (uint32_t)t, tmem + 128u * (uint32_t)t + 8u * (uint32_t)kk,
+                      ptx::sdesc_sw128(kt + 2048u * (uint32_t)kk, 8192, 1024), idesc_dq, (!first || kk > 0) ? 1u : 0u);
+        ptx::mma_commit(bar(DQ_DONE + t));
+      };
+      if (wait(Q_READY, 0) && n > 0 && wait(K_READY, 0)) {
+        ptx::tc_fence_after();
+        issue_s(0, 0);
+        issue_s(1, 0);
+        for (int j = 0; j < n; ++j) {
+          const int slot = j & 1, nslot = (j + 1) & 1;
+          const bool more = j + 1 < n;
+          if (!wait(DS_READY, j & 1)) break;
+          ptx::tc_fence_after();
+          issue_dq(0, slot, j == 0);
+          if (more) {
+            if (!wait(K_READY + nslot, ((j + 1) >> 1) & 1) || !wait(DQ_DONE, j & 1)) break;
+            ptx::tc_fence_after();
+            issue_s(0, nslot);
+          }
+          if (!wait(DS_READY + 1, j & 1)) break;
+          ptx::tc_fence_after();
+          issue_dq(1, slot, j == 0);
+          ptx::mma_commit(bar(KV_EMPTY + slot));
+          if (more) {
+            if (!wait(DQ_DONE + 1, j & 1)) break;
+            ptx::tc_fence_after();
+            issue_s(1, nslot);
+          }
+        }
+      }
+      ptx::mma_commit(bar(FINAL));
+      ptx::mbar_wait(bar(FINAL), 0, kWait);
+    }
+  } else {
+    // ------------------------------------------------------------ K rotation (warps 10-13)
+    const int rt = tid - 320, row = rt & 63, cg = rt >> 6;
+    uint32_t info = 0;
+    uint4 tab[8];
+    auto fetch = [&](int j) {
+      const int key = kv_lo + j * BN + row;
+      info = 0;
+      int p = 0;
+      if (key < kv_hi) {
+        info = (uint32_t)__ldg(L.key_info + blk.key_off + key);
+        p = key_row(info, L.n_pos, f.status);
+      }
+      const uint4* tp = reinterpret_cast<const uint4*>(cs16 + (int64_t)p * (D / 2)) + 8 * cg;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) tab[c] = __ldg(tp + c);
+    };
+    if (n > 0) fetch(0);
+    for (int j = 0; j < n; ++j) {
+      const int slot = j & 1;
+      if (!wait(KV_FULL + slot, (j >> 1) & 1)) break;
+      const uint32_t kt = KB + 16384u * (uint32_t)slot;
+      if (kv_lo + j * BN + row < kv_hi) {
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+          const int c = 4 * cg + cc;
+          uint4* pa = reinterpret_cast<uint4*>(sm + kt + chunk_off<BN>(row, c));
+          uint4* pb = reinterpret_cast<uint4*>(sm + kt + chunk_off<BN>(row, c + 8));
+          uint4 y1, y2;
+          tile::rotate8h(*pa, *pb, tab[2 * cc], tab[2 * cc + 1], y1, y2);
+          *pa = y1;
+          *pb = y2;
+        }
+      }
+      if (cg == 0) s_info[slot * BN + row] = info;
+      ptx::fence_proxy_async_smem();
+      ptx::mbar_arrive(bar(K_READY + slot));
+      if (j + 1 < n) fetch(j + 1);
+    }
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ===========================================================================
+// dK / dV, warp-specialised (key tiles whose blocks have no abs keys)
+//
+// One CTA = 128 keys of one batch row x one KV head.  A "step" is one
+// 64-row query tile of a block x one query head of the GQA group.  448
+// threads in roles:
+//   warps 0-3, 4-7  two score groups, taking even / odd steps (thread = key =
+//                   TMEM lane): P^T = exp(S^T - lse), dS^T = P^T (dP^T - delta)
+//                   scale, written back into TMEM as bf16 pairs;
+//   warp 8          TMA producer (V once, raw K per block, Q and dO per step)
+//   warp 9          MMA issuer and TMEM owner
+//   warps 10-13     rotate K per block and each Q tile in place; stage the
+//                   step's lse / delta rows in smem.
+// TMEM: S^T / dP^T double-buffered by step parity (4 x 64 columns), dV and
+// dKrot accumulators (128 each).  dV += P^T dO and dKrot += dS^T Qrot take
+// their A operands from TMEM.  At the end of a block score group 0 rotates
+// dKrot back by the keys' block positions into an fp32 dK accumulator in
+// smem, so keys seen by several blocks are summed without atomics.
+// ===========================================================================
+namespace kvw {
+constexpr int BN = 128, BQ = 64, kThreads = 448;
+constexpr uint32_t K = 0;                   // 128 keys x 128 d (rotated per block)
+constexpr uint32_t V = 32768;
+constexpr uint32_t Q = 65536;               // ring of 2 x (64 rows x 128 d), rotated in place
+constexpr uint32_t DO = Q + 2 * 16384;      // ring of 2 x (64 rows x 128 d)
+constexpr uint32_t DK = DO + 2 * 16384;     // fp32 [128 d][128 keys]
+constexpr uint32_t STATS = DK + 65536;      // [2 slots][lse2 64 | delta 64] fp32
+constexpr uint32_t BARS = STATS + 2 * 2 * 4 * BQ;
+enum Bar { V_FULL = 0, K_FULL, K_READY, BLK_DONE, FOLD_DONE, Q_FULL = 5, Q_READY = 7, Q_EMPTY = 9, S_FULL = 11,
+           P_READY = 13, FINAL = 15, N_BARS = 16 };
+constexpr uint32_t TMEM_SLOT = BARS + 8 * N_BARS;
+constexpr uint32_t ABORT = TMEM_SLOT + 4;
+constexpr uint32_t TOTAL = ABORT + 4;
+constexpr size_t kSmem = TOTAL + 1024;
+// TMEM columns: buffer x at 128 x: S^T [0,64) (P^T packed in [0,32)), dP^T [64,128) (dS^T packed in [64,96)).
+constexpr uint32_t C_BUF = 0, C_DV = 256, C_DKR = 384;
+constexpr long long kWait = 1000000000LL;
+}  // namespace kvw
+
+// Iterates the blocks of row b that see keys [j0, j1) (same order in every role).
+struct BlockIter {
+  const AiAttnLayout* L;
+  int b, j0, j1, bi, end;
+  __device__ BlockIter(const AiAttnLayout* L_, int b_, int j0_, int j1_) : L(L_), b(b_), j0(j0_), j1(j1_) {
+    bi = L->row_blocks[b] - 1;
+    end = L->row_blocks[b + 1];
+  }
+  __device__ bool next(Block& blk) {
+    while (++bi < end) {
+      blk = load_block(L->blocks, bi);
+      if (blk.e <= j0 || blk.kv_lo >= j1 || max(blk.s, j0) >= blk.e) continue;
+      return true;
+    }
+    return false;
+  }
+};
+
+__global__ void __launch_bounds__(kvw::kThreads, 1)
+    dkdv_ws_kernel(const AiAttnBwdArgs a, const float* __restrict__ delta, const __grid_constant__ CUtensorMap tm_k,
+                   const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_q,
+                   const __grid_constant__ CUtensorMap tm_do) {
+  using namespace kvw;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = tile::align1024(smem_raw);
+  const uint32_t sbase = ptx::smem_u32(sm);
+  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+  volatile int* s_abort = reinterpret_cast<volatile int*>(sm + ABORT);
+  float* s_dk = reinterpret_cast<float*>(sm + DK);
+  float* s_stats = reinterpret_cast<float*>(sm + STATS);
+  auto bar = [&](int i) { return sbase + BARS + 8u * (uint32_t)i; };
+
+  const AiAttnFwdArgs& f = a.fwd;
+  const AiAttnLayout& L = f.layout;
+  const int32_t* item = L.kv_items + 4 * (int64_t)(L.n_kv_abs_items + blockIdx.x);
+  const int b = item[0], j0 = item[1], j1 = item[2];
+  const int hk = blockIdx.y, G = f.num_q_heads / f.num_kv_heads;
+  const __half2* cs16 = static_cast<const __half2*>(L.rope_cs16);
+
+  if (tid == 0) {
+    for (int i = 0; i < N_BARS; ++i) {
+      uint32_t count = 1;
+      if (i == K_READY || i == Q_READY || i == Q_READY + 1 || i == FOLD_DONE) count = 128;
+      if (i == P_READY || i == P_READY + 1) count = 128;
+      ptx::mbar_init(bar(i), count);
+    }
+    *s_abort = 0;
+    ptx::fence_mbar_init();
+  }
+  if (warp == 9) {
+    ptx::tmem_alloc(sbase + TMEM_SLOT, kTmemCols);
+    ptx::tmem_relinquish();
+  }
+  if (warp < 4) {
+    for (int d = 0; d < D; ++d) s_dk[d * BN + tid] = 0.f;
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sm + TMEM_SLOT);
+
+  auto wait = [&](int i, uint32_t parity) -> bool {
+    if (*s_abort) return false;
+    if (!ptx::mbar_wait(bar(i), parity, kWait)) {
+      report(f.status, AI_ERR_DEV_TIMEOUT);
+      *s_abort = 1;
+      return false;
+    }
+    return true;
+  };
+  auto n_steps_of = [&](const Block& blk) { return ((blk.e - max(blk.s, j0) + BQ - 1) / BQ) * G; };
+
+  if (warp < 8) {
+    // ------------------------------------------------------------ score groups
+    const int t = warp / 4, lrow = tid % 128, j = j0 + lrow;
+    const uint32_t lane_base = (uint32_t)((warp % 4) * 32) << 16;
+    const float sl2 = f.scale * kLog2e;
+    BlockIter it(&L, b, j0, j1);
+    Block blk;
+    int s = 0, nb = 0;
+    bool any = false;
+    while (!*s_abort && it.next(blk)) {
+      any = true;
+      const int kmax = min(j1, blk.e), qs = max(blk.s, j0);
+      uint32_t info = 0;
+      if (j < kmax) info = (uint32_t)__ldg(L.key_info + blk.key_off + j);
+      const bool key_ok = (info & AI_KEY_ATTN) != 0;
+      const int nsteps = n_steps_of(blk);
+      for (int st = 0; st < nsteps; ++st, ++s) {
+        if ((s & 1) != t) continue;
+        const int x = s & 1, q0 = qs + (st / G) * BQ, q1 = min(q0 + BQ, blk.e);
+        if (!wait(Q_READY + x, (s >> 1) & 1) || !wait(S_FULL + x, (s >> 1) & 1)) break;
+        ptx::tc_fence_after();
+        const float* lse2 = s_stats + x * 2 * BQ;
+        const float* dlt = lse2 + BQ;
+        const uint32_t cb = tmem + lane_base + C_BUF + 128u * (uint32_t)x;
+        // Whole-step masks: causal (j <= i) holds for every pair when the tile
+        // lies wholly above the query rows, and every row is in the block when
+        // the tile is full.
+        const bool no_causal = j0 + BN - 1 <= q0, rows_full = q1 == q0 + BQ;
+        uint32_t pk[32], dk[32];
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          uint32_t rs[32], rp[32];
+          ptx::tmem_ld32(cb + 32 * hf, rs);
+          ptx::tmem_ld32(cb + 64 + 32 * hf, rp);
+          ptx::tmem_wait_ld();
+#pragma unroll
+          for (int x2 = 0; x2 < 16; ++x2) {
+            float p[2], ds[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const int cl = 2 * x2 + u, c = 32 * hf + cl;  // query row q0 + c
+              bool ok = key_ok;
+              if (!no_causal) ok = ok && (j <= q0 + c);
+              if (!rows_full) ok = ok && (q0 + c < q1);
+              p[u] = ok ? ptx::ex2(fmaf(__uint_as_float(rs[cl]), sl2, -lse2[c])) : 0.f;
+              ds[u] = p[u] * (__uint_as_float(rp[cl]) - dlt[c]) * f.scale;
+            }
+            pk[16 * hf + x2] = tile::pack2(p[0], p[1]);
+            dk[16 * hf + x2] = tile::pack2(ds[0], ds[1]);
+          }
+        }
+        ptx::tmem_st32(cb, pk);
+        ptx::tmem_st32(cb + 64, dk);
+        ptx::tmem_wait_st();
+        ptx::tc_fence_before();
+        ptx::mbar_arrive(bar(P_READY + x));
+      }
+      if (*s_abort) break;
+      if (t == 0) {
+        // Fold this block's dKrot into dK: dK += R(key position)^T dKrot.
+        if (!wait(BLK_DONE, nb & 1)) break;
+        ptx::tc_fence_after();
+        const int p = key_row(info, L.n_pos, f.status);
+        const uint4* tp = reinterpret_cast<const uint4*>(cs16 + (int64_t)p * (D / 2));
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          uint32_t g1[32], g2[32];
+          ptx::tmem_ld32(tmem + lane_base + C_DKR + 32 * hf, g1);
+          ptx::tmem_ld32(tmem + lane_base + C_DKR + 64 + 32 * hf, g2);
+          ptx::tmem_wait_ld();
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const uint4 tv = __ldg(tp + 8 * hf + q);
+            const __half2* h2 = reinterpret_cast<const __half2*>(&tv);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const int xx = 4 * q + u, d = 32 * hf + xx;
+              const float2 csn = __half22float2(h2[u]);
+              const float v1 = __uint_as_float(g1[xx]), v2 = __uint_as_float(g2[xx]);
+              s_dk[d * BN + lrow] += v1 * csn.x + v2 * csn.y;
+              s_dk[(d + 64) * BN + lrow] += v2 * csn.x - v1 * csn.y;
+            }
+          }
+        }
+        ptx::tc_fence_before();
+        ptx::mbar_arrive(bar(FOLD_DONE));
+      }
+      ++nb;
+    }
+    // Epilogue: group 0 writes dK (smem), group 1 writes dV (TMEM).
+    if (!*s_abort) {
+      if (t == 1 && any && !wait(BLK_DONE, (nb - 1) & 1)) {
+      } else if (!*s_abort) {
+        ptx::tc_fence_after();
+        __nv_bfloat16* row_ptr =
+            t == 0 ? static_cast<__nv_bfloat16*>(a.dk.ptr) + b * a.dk.stride_b + hk * a.dk.stride_h + (int64_t)j * a.dk.stride_t
+                   : static_cast<__nv_bfloat16*>(a.dv.ptr) + b * a.dv.stride_b + hk * a.dv.stride_h + (int64_t)j * a.dv.stride_t;
+#pragma unroll
+        for (int cc = 0; cc < D / 32; ++cc) {
+          float v[32];
+          if (t == 0) {
+#pragma unroll
+            for (int x = 0; x < 32; ++x) v[x] = s_dk[(32 * cc + x) * BN + lrow];
+          } else {
+            uint32_t rr[32];
+            if (any) {
+              ptx::tmem_ld32(tmem + lane_base + C_DV + 32 * cc, rr);
+              ptx::tmem_wait_ld();
+            }
+#pragma unroll
+            for (int x = 0; x < 32; ++x) v[x] = any ? __uint_as_float(rr[x]) : 0.f;
+          }
+          if (j < j1) store_bf16_row32(row_ptr + 32 * cc, v);
+        }
+      }
+    }
+  } else if (warp == 8) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      ptx::prefetch_tmap(&tm_k);
+      ptx::prefetch_tmap(&tm_v);
+      ptx::prefetch_tmap(&tm_q);
+      ptx::prefetch_tmap(&tm_do);
+      ptx::mbar_arrive_expect_tx(bar(V_FULL), 32768);
+      ptx::tma_load_4d(sbase + V, &tm_v, bar(V_FULL), 0, j0, hk, b);
+      ptx::tma_load_4d(sbase + V + 16384, &tm_v, bar(V_FULL), 64, j0, hk, b);
+      BlockIter it(&L, b, j0, j1);
+      Block blk;
+      int s = 0, nb = 0;
+      bool ok = true;
+      while (ok && it.next(blk)) {
+        if (nb > 0 && !wait(BLK_DONE, (nb - 1) & 1)) break;
+        ptx::mbar_arrive_expect_tx(bar(K_FULL), 32768);
+        ptx::tma_load_4d(sbase + K, &tm_k, bar(K_FULL), 0, j0, hk, b);
+        ptx::tma_load_4d(sbase + K + 16384, &tm_k, bar(K_FULL), 64, j0, hk, b);
+        const int qs = max(blk.s, j0), nsteps = n_steps_of(blk);
+        for (int st = 0; st < nsteps; ++st, ++s) {
+          const int x = s & 1, q0 = qs + (st / G) * BQ, h = hk * G + st % G;
+          if (s >= 2 && !wait(Q_EMPTY + x, ((s >> 1) - 1) & 1)) {
+            ok = false;
+            break;
+          }
+          const uint32_t qb = sbase + Q + 16384u * (uint32_t)x, ob = sbase + DO + 16384u * (uint32_t)x;
+          ptx::mbar_arrive_expect_tx(bar(Q_FULL + x), 32768);
+          ptx::tma_load_4d(qb, &tm_q, bar(Q_FULL + x), 0, q0, h, b);
+          ptx::tma_load_4d(qb + 8192, &tm_q, bar(Q_FULL + x), 64, q0, h, b);
+          ptx::tma_load_4d(ob, &tm_do, bar(Q_FULL + x), 0, q0, h, b);
+          ptx::tma_load_4d(ob + 8192, &tm_do, bar(Q_FULL + x), 64, q0, h, b);
+        }
+        ++nb;
+      }
+    }
+  } else if (warp == 9) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_st = ptx::idesc_bf16_f32(BN, BQ, false, false);
+      constexpr uint32_t idesc_acc = ptx::idesc_bf16_f32(BN, D, false, true);
+      auto issue_scores = [&](int s) {
+        const int x = s & 1;
+        const uint32_t qb = sbase + Q + 16384u * (uint32_t)x, ob = sbase + DO + 16384u * (uint32_t)x;
+        const uint32_t cb = tmem + C_BUF + 128u * (uint32_t)x;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t ao = (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u;
+          const uint32_t bo = (uint32_t)(kk >> 2) * 8192u + (uint32_t)(kk & 3) * 32u;
+          ptx::mma_ss(cb, ptx::sdesc_sw128(sbase + K + ao, 16, 1024), ptx::sdesc_sw128(qb + bo, 16, 1024), idesc_st,
+                      kk > 0);
+          ptx::mma_ss(cb + 64, ptx::sdesc_sw128(sbase + V + ao, 16, 1024), ptx::sdesc_sw128(ob + bo, 16, 1024),
+                      idesc_st, kk > 0);
+        }
+        ptx::mma_commit(bar(S_FULL + x));
+      };
+      bool ok = wait(V_FULL, 0);
+      BlockIter it(&L, b, j0, j1);
+      Block blk;
+      int s = 0, nb = 0;
+      bool dv_started = false;
+      while (ok && it.next(blk)) {
+        const int nsteps = n_steps_of(blk);
+        if (!wait(K_READY, nb & 1)) break;
+        ptx::tc_fence_after();
+        const int sb = s;
+        // scores of the block's first step
+        if (!wait(Q_READY + (s & 1), (s >> 1) & 1) || (s >= 2 && !wait(Q_EMPTY + (s & 1), ((s >> 1) - 1) & 1))) break;
+        ptx::tc_fence_after();
+        issue_scores(s);
+        for (; s < sb + nsteps; ++s) {
+          const int x = s & 1;
+          if (s + 1 < sb + nsteps) {
+            const int y = (s + 1) & 1;
+            if (!wait(Q_READY + y, ((s + 1) >> 1) & 1) || (s + 1 >= 2 && !wait(Q_EMPTY + y, (((s + 1) >> 1) - 1) & 1))) {
+              ok = false;
+              break;
+            }
+            ptx::tc_fence_after();
+            issue_scores(s + 1);
+          }
+          if (!wait(P_READY + x, (s >> 1) & 1)) {
+            ok = false;
+            break;
+          }
+          if (s == sb && nb > 0 && !wait(FOLD_DONE, (nb - 1) & 1)) {
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          const uint32_t qb = sbase + Q + 16384u * (uint32_t)x, ob = sbase + DO + 16384u * (uint32_t)x;
+          const uint32_t cb = tmem + C_BUF + 128u * (uint32_t)x;
+#pragma unroll
+          for (int kk = 0; kk < BQ / 16; ++kk) {
+            ptx::mma_ts(tmem + C_DV, cb + 8u * (uint32_t)kk, ptx::sdesc_sw128(ob + 2048u * (uint32_t)kk, 8192, 1024),
+                        idesc_acc, (dv_started || kk > 0) ? 1u : 0u);
+            ptx::mma_ts(tmem + C_DKR, cb + 64u + 8u * (uint32_t)kk,
+                        ptx::sdesc_sw128(qb + 2048u * (uint32_t)kk, 8192, 1024), idesc_acc,
+                        (s > sb || kk > 0) ? 1u : 0u);
+          }
+          ptx::mma_commit(bar(Q_EMPTY + x));
+          dv_started = true;
+        }
+        if (!ok) break;
+        ptx::mma_commit(bar(BLK_DONE));
+        ++nb;
+      }
+      ptx::mma_commit(bar(FINAL));
+      ptx::mbar_wait(bar(FINAL), 0, kWait);
+    }
+  } else {
+    // ------------------------------------------------------------ rotation (warps 10-13)
+    const int rt = tid - 320;  // 0..127
+    BlockIter it(&L, b, j0, j1);
+    Block blk;
+    int s = 0, nb = 0;
+    while (!*s_abort && it.next(blk)) {
+      // K row rt by this block's key position.
+      {
+        const int key = j0 + rt;
+        uint32_t info = 0;
+        int p = 0;
+        if (key < min(j1, blk.e)) {
+          info = (uint32_t)__ldg(L.key_info + blk.key_off + key);
+          p = key_row(info, L.n_pos, f.status);
+        }
+        const uint4* tp = reinterpret_cast<const uint4*>(cs16 + (int64_t)p * (D / 2));
+        uint4 tab[16];
+#pragma unroll
+        for (int c = 0; c < 16; ++c) tab[c] = __ldg(tp + c);
+        if (!wait(K_FULL, nb & 1)) break;
+        if (key < min(j1, blk.e)) {
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            uint4* pa = reinterpret_cast<uint4*>(sm + K + chunk_off<BN>(rt, c));
+            uint4* pb = reinterpret_cast<uint4*>(sm + K + chunk_off<BN>(rt, c + 8));
+            uint4 y1, y2;
+            tile::rotate8h(*pa, *pb, tab[2 * c], tab[2 * c + 1], y1, y2);
+            *pa = y1;
+            *pb = y2;
+          }
+        }
+        ptx::fence_proxy_async_smem();
+        ptx::mbar_arrive(bar(K_READY));
+      }
+      const int qs = max(blk.s, j0), nsteps = n_steps_of(blk);
+      const int r = rt & 63, cg = rt >> 6;
+      for (int st = 0; st < nsteps; ++st, ++s) {
+        const int x = s & 1, q0 = qs + (st / G) * BQ, q1 = min(q0 + BQ, blk.e), h = hk * G + st % G;
+        const int i = q0 + r;
+        // Row position, table and row statistics are fetched before the TMA wait.
+        int p = 0;
+        float l2 = CUDART_INF_F, dl = 0.f;
+        if (i < q1) {
+          p = clamp_row(__ldg(L.q_pos + (int64_t)b * f.seq_len + i), L.n_pos, f.status);
+          if (cg == 0) {
+            const int64_t idx = ((int64_t)b * f.num_q_heads + h) * f.seq_len + i;
+            l2 = lse_log2(__ldg(f.lse + idx));
+            dl = __ldg(delta + idx);
+          }
+        }
+        const uint4* tp = reinterpret_cast<const uint4*>(cs16 + (int64_t)p * (D / 2)) + 8 * cg;
+        uint4 tab[8];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) tab[c] = __ldg(tp + c);
+        if (!wait(Q_FULL + x, (s >> 1) & 1)) break;
+        const uint32_t qb = Q + 16384u * (uint32_t)x;
+#pragma unroll
+        for (int cc = 0; cc < 4; ++cc) {
+          const int c = 4 * cg + cc;
+          uint4* pa = reinterpret_cast<uint4*>(sm + qb + chunk_off<BQ>(r, c));
+          uint4* pb = reinterpret_cast<uint4*>(sm + qb + chunk_off<BQ>(r, c + 8));
+          uint4 y1, y2;
+          tile::rotate8h(*pa, *pb, tab[2 * cc], tab[2 * cc + 1], y1, y2);
+          *pa = y1;
+          *pb = y2;
+        }
+        if (cg == 0) {
+          s_stats[x * 2 * BQ + r] = l2;
+          s_stats[x * 2 * BQ + BQ + r] = dl;
+        }
+        ptx::fence_proxy_async_smem();
+        ptx::mbar_arrive(bar(Q_READY + x));
+      }
+      ++nb;
+    }
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
@@ -747,10 +1493,24 @@ int sm100_bwd(const AiAttnBwdArgs& a, float* delta, cudaStream_t st, cudaError_t
     if (!sm100_make_map(&tk, f.k, f.batch, f.num_kv_heads, f.seq_len, dq::BN) ||
         !sm100_make_map(&tv, f.v, f.batch, f.num_kv_heads, f.seq_len, dq::BN))
       return AI_ERR_TMA;
-    e = cudaFuncSetAttribute(dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dq::kSmem);
-    if (e == cudaSuccess) {
-      dq_kernel<<<dim3(f.layout.n_fwd_items, f.num_q_heads), kThreads, dq::kSmem, st>>>(a, delta, tk, tv);
-      e = cudaGetLastError();
+    // Items of blocks with abs keys (all items when a GQA group has an odd
+    // number of heads) on the one-head kernel, the rest two heads per CTA.
+    const int G = f.num_q_heads / f.num_kv_heads;
+    const int n_single = (G % 2 == 0) ? f.layout.n_fwd_abs_items : f.layout.n_fwd_items;
+    const int n_pair = f.layout.n_fwd_items - n_single;
+    if (n_single > 0) {
+      e = cudaFuncSetAttribute(dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dq::kSmem);
+      if (e == cudaSuccess) {
+        dq_kernel<<<dim3(n_single, f.num_q_heads), kThreads, dq::kSmem, st>>>(a, delta, tk, tv);
+        e = cudaGetLastError();
+      }
+    }
+    if (e == cudaSuccess && n_pair > 0) {
+      e = cudaFuncSetAttribute(dq_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dqw::kSmem);
+      if (e == cudaSuccess) {
+        dq_ws_kernel<<<dim3(n_pair, f.num_q_heads / 2), dqw::kThreads, dqw::kSmem, st>>>(a, delta, tk, tv);
+        e = cudaGetLastError();
+      }
     }
   }
   if (e == cudaSuccess && f.layout.n_kv_items > 0) {
@@ -760,10 +1520,22 @@ int sm100_bwd(const AiAttnBwdArgs& a, float* delta, cudaStream_t st, cudaError_t
         !sm100_make_map(&tq, f.q, f.batch, f.num_q_heads, f.seq_len, kv::BQ) ||
         !sm100_make_map(&tdo, a.dout, f.batch, f.num_q_heads, f.seq_len, kv::BQ))
       return AI_ERR_TMA;
-    e = cudaFuncSetAttribute(dkdv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kv::kSmem);
-    if (e == cudaSuccess) {
-      dkdv_kernel<<<dim3(f.layout.n_kv_items, f.num_kv_heads), kThreads, kv::kSmem, st>>>(a, delta, tk, tv, tq, tdo);
-      e = cudaGetLastError();
+    // Key tiles that a block with abs keys sees run on the one-warpgroup kernel,
+    // the rest on the warp-specialised one.
+    const int n_abs = f.layout.n_kv_abs_items, n_plain = f.layout.n_kv_items - n_abs;
+    if (n_abs > 0) {
+      e = cudaFuncSetAttribute(dkdv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kv::kSmem);
+      if (e == cudaSuccess) {
+        dkdv_kernel<<<dim3(n_abs, f.num_kv_heads), kThreads, kv::kSmem, st>>>(a, delta, tk, tv, tq, tdo);
+        e = cudaGetLastError();
+      }
+    }
+    if (e == cudaSuccess && n_plain > 0) {
+      e = cudaFuncSetAttribute(dkdv_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kvw::kSmem);
+      if (e == cudaSuccess) {
+        dkdv_ws_kernel<<<dim3(n_plain, f.num_kv_heads), kvw::kThreads, kvw::kSmem, st>>>(a, delta, tk, tv, tq, tdo);
+        e = cudaGetLastError();
+      }
     }
   }
   if (e == cudaSuccess) e = bwd_fill(a, st);

@@ -141,6 +141,7 @@ class CompiledLayout:
     fwd_items: torch.Tensor
     kv_items: torch.Tensor
     n_fwd_abs_items: int         # leading fwd_items whose block has abs keys
+    n_kv_abs_items: int          # leading kv_items that a block with abs keys sees
     pairs_per_head: int          # finite (query, key) logits of one head summed over the batch
     host_blocks: np.ndarray = field(repr=False, default=None)
 
@@ -164,6 +165,7 @@ class CompiledLayout:
         L.kv_tile = int(self.kv_tile)
         L.kv_items = self.kv_items.data_ptr() if self.kv_items.numel() else None
         L.n_kv_items = int(self.kv_items.shape[0])
+        L.n_kv_abs_items = int(self.n_kv_abs_items)
         return L
 
 
@@ -177,15 +179,22 @@ def _tiles(fwd_tile: int, kv_tile: int, blocks: np.ndarray, row_cov: np.ndarray)
     # Items of blocks with abs keys first (they run on their own kernel), then longest first.
     fwd.sort(key=lambda t: (-(int(blocks[t[1], 5]) & BLOCKF_ABS), -t[0]))
     n_abs = sum(1 for t in fwd if int(blocks[t[1], 5]) & BLOCKF_ABS)
+    # Key tiles: cost = query rows that see them; tiles touching a block with
+    # abs keys first (own kernel), then longest first.
     kv = []
     for row, cov in enumerate(row_cov):
+        rb = blocks[blocks[:, 0] == row]
         for j0 in range(0, int(cov), kv_tile):
             j1 = min(j0 + kv_tile, int(cov))
-            kv.append(((int(cov) - j0), row, j0, j1))
-    kv.sort(key=lambda t: -t[0])
+            seen = (rb[:, 2] > j0) & (rb[:, 4] < j1)
+            cost = int(np.maximum(rb[seen, 2] - np.maximum(rb[seen, 1], j0), 0).sum())
+            has_abs = bool((rb[seen, 5] & BLOCKF_ABS).any())
+            kv.append((has_abs, cost, row, j0, j1))
+    kv.sort(key=lambda t: (-int(t[0]), -t[1]))
+    n_kv_abs = sum(1 for t in kv if t[0])
     fwd_arr = np.asarray([(bi, q0, q1, 0) for _, bi, q0, q1 in fwd], dtype=np.int32).reshape(-1, 4)
-    kv_arr = np.asarray([(row, j0, j1, 0) for _, row, j0, j1 in kv], dtype=np.int32).reshape(-1, 4)
-    return fwd_arr, kv_arr, n_abs
+    kv_arr = np.asarray([(row, j0, j1, 0) for _, _, row, j0, j1 in kv], dtype=np.int32).reshape(-1, 4)
+    return fwd_arr, kv_arr, n_abs, n_kv_abs
 
 
 def compile_layout(parsed_positions, batch: int, seq_len: int, head_dim: int, dtype: torch.dtype,
@@ -277,7 +286,7 @@ def _compile(parsed_positions, batch, seq_len, head_dim, code, rotary_emb, devic
     lib = _lib.lib()
     fwd_tile = lib.ai_attn_fwd_tile_rows(code, head_dim)
     kv_tile = lib.ai_attn_kv_tile_rows(code, head_dim)
-    fwd_items, kv_items, n_abs = _tiles(fwd_tile, kv_tile, blocks_np, row_cov_np)
+    fwd_items, kv_items, n_abs, n_kv_abs = _tiles(fwd_tile, kv_tile, blocks_np, row_cov_np)
 
     cos, sin = rope_table(rotary_emb, lo, hi, head_dim, device)
 
@@ -290,6 +299,7 @@ def _compile(parsed_positions, batch, seq_len, head_dim, code, rotary_emb, devic
         blocks=dev(blocks_np), row_blocks=dev(np.asarray(row_blocks, dtype=np.int32)), row_cov=dev(row_cov_np),
         key_info=dev(key_info), q_pos=dev(q_pos), rope_cos=cos, rope_sin=sin,
         rope_cs16=torch.stack([cos, sin], dim=-1).to(torch.float16).contiguous(),
-        fwd_items=dev(fwd_items), kv_items=dev(kv_items), n_fwd_abs_items=n_abs, pairs_per_head=pairs,
+        fwd_items=dev(fwd_items), kv_items=dev(kv_items), n_fwd_abs_items=n_abs, n_kv_abs_items=n_kv_abs,
+        pairs_per_head=pairs,
         host_blocks=blocks_np,
     )

@@ -113,6 +113,7 @@ typedef struct AiAttnLayout {
   int32_t kv_tile;            /* keys per dK/dV work item (ai_attn_kv_tile_rows) */
   const int32_t* kv_items;    /* [n_kv_items][4]: row, j0, j1, 0 */
   int32_t n_kv_items;
+  int32_t n_kv_abs_items;     /* the first n_kv_abs_items items see a block with AI_BLOCKF_ABS */
 } AiAttnLayout;
 
 typedef struct AiAttnFwdArgs {
