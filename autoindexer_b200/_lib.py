@@ -29,7 +29,7 @@ __all__ = [
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_ai_attn.so")
 
 DTYPE_BF16, DTYPE_F16, DTYPE_F32 = 0, 1, 2
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 # Every function include/ai_attn.h declares.
 EXPORTED_SYMBOLS = (
@@ -37,6 +37,7 @@ EXPORTED_SYMBOLS = (
     "ai_attn_fwd_tile_rows",
     "ai_attn_kv_tile_rows",
     "ai_attn_fwd",
+    "ai_attn_fwd_workspace",
     "ai_attn_bwd_workspace",
     "ai_attn_bwd",
     "ai_attn_bwd_noalloc",
@@ -66,6 +67,7 @@ class AiAttnLayout(ctypes.Structure):
         ("key_info", ctypes.c_void_p),
         ("n_keys", ctypes.c_int64),
         ("q_pos", ctypes.c_void_p),
+        ("k_own", ctypes.c_void_p),
         ("rope_cos", ctypes.c_void_p),
         ("rope_sin", ctypes.c_void_p),
         ("rope_cs16", ctypes.c_void_p),
@@ -97,6 +99,8 @@ class AiAttnFwdArgs(ctypes.Structure):
         ("lse", ctypes.c_void_p),
         ("layout", AiAttnLayout),
         ("status", ctypes.c_void_p),
+        ("workspace", ctypes.c_void_p),
+        ("workspace_bytes", ctypes.c_size_t),
     ]
 
 
@@ -126,6 +130,8 @@ def _bind(handle):
         fn.argtypes = [ctypes.c_int, ctypes.c_int]
     handle.ai_attn_fwd.restype = ctypes.c_int
     handle.ai_attn_fwd.argtypes = [P(AiAttnFwdArgs), ctypes.c_void_p]
+    handle.ai_attn_fwd_workspace.restype = ctypes.c_int
+    handle.ai_attn_fwd_workspace.argtypes = [P(AiAttnFwdArgs), P(ctypes.c_size_t)]
     handle.ai_attn_bwd_workspace.restype = ctypes.c_int
     handle.ai_attn_bwd_workspace.argtypes = [P(AiAttnBwdArgs), P(ctypes.c_size_t)]
     handle.ai_attn_bwd.restype = ctypes.c_int

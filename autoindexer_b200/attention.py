@@ -94,19 +94,34 @@ def _fwd_args(q: Tensor, k: Tensor, v: Tensor, out_bhtd: Tensor, lse: Tensor, la
     return a
 
 
-def attn_fwd(q: Tensor, k: Tensor, v: Tensor, layout: CompiledLayout, scale: float) -> Tuple[Tensor, Tensor]:
-    """Launches ``ai_attn_fwd``: returns ``out (B, T, Hq, D)`` and ``lse (B, Hq, T)`` fp32."""
+def attn_fwd(q: Tensor, k: Tensor, v: Tensor, layout: CompiledLayout, scale: float,
+             rotated_copies: bool = True) -> Tuple[Tensor, Tensor]:
+    """Launches ``ai_attn_fwd``: returns ``out (B, T, Hq, D)`` and ``lse (B, Hq, T)`` fp32.
+
+    ``rotated_copies``: give the kernels scratch for once-rotated Q/K copies
+    (faster; ``ai_attn_fwd_workspace`` bytes); without it every tile is
+    rotated in shared memory."""
     B, Hq, T, D = q.shape
     out = torch.empty((B, T, Hq, D), dtype=q.dtype, device=q.device)
     lse = torch.empty((B, Hq, T), dtype=torch.float32, device=q.device)
     a = _fwd_args(q, k, v, out.permute(0, 2, 1, 3), lse, layout, scale)
+    lib = _lib.lib()
+    nbytes = ctypes.c_size_t(0)
+    _lib.check(lib.ai_attn_fwd_workspace(ctypes.byref(a), ctypes.byref(nbytes)), "ai_attn_fwd_workspace")
+    ws = None
+    if nbytes.value and rotated_copies:
+        ws = torch.empty(int(nbytes.value), dtype=torch.uint8, device=q.device)
+        a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
     stream = torch.cuda.current_stream(q.device).cuda_stream
-    _lib.check(_lib.lib().ai_attn_fwd(ctypes.byref(a), ctypes.c_void_p(stream)), "ai_attn_fwd")
+    _lib.check(lib.ai_attn_fwd(ctypes.byref(a), ctypes.c_void_p(stream)), "ai_attn_fwd")
+    del ws
     return out, lse
 
 
-def attn_bwd(q, k, v, out, lse, dout, layout: CompiledLayout, scale: float):
-    """Launches ``ai_attn_bwd``: returns ``dq, dk, dv`` shaped like ``q, k, v``."""
+def attn_bwd(q, k, v, out, lse, dout, layout: CompiledLayout, scale: float, rotated_copies: bool = True):
+    """Launches ``ai_attn_bwd``: returns ``dq, dk, dv`` shaped like ``q, k, v``
+    (``rotated_copies`` as for ``attn_fwd``; without it the workspace holds
+    only the row sums of dO.O)."""
     dq = torch.empty_like(q)
     dk = torch.empty_like(k)
     dv = torch.empty_like(v)
@@ -124,7 +139,10 @@ def attn_bwd(q, k, v, out, lse, dout, layout: CompiledLayout, scale: float):
     lib = _lib.lib()
     nbytes = ctypes.c_size_t(0)
     _lib.check(lib.ai_attn_bwd_workspace(ctypes.byref(a), ctypes.byref(nbytes)), "ai_attn_bwd_workspace")
-    ws = torch.empty(max(int(nbytes.value), 256), dtype=torch.uint8, device=q.device)
+    want = int(nbytes.value)
+    if not rotated_copies:
+        want = (q.shape[0] * q.shape[1] * q.shape[2] * 4 + 255) // 256 * 256
+    ws = torch.empty(max(want, 256), dtype=torch.uint8, device=q.device)
     a.workspace = ws.data_ptr()
     a.workspace_bytes = ws.numel()
     stream = torch.cuda.current_stream(q.device).cuda_stream

@@ -751,7 +751,9 @@ constexpr long long kWait = 1000000000LL;
 
 __global__ void __launch_bounds__(dqw::kThreads, 1)
     dq_ws_kernel(const AiAttnBwdArgs a, const float* __restrict__ delta, const __grid_constant__ CUtensorMap tm_k,
-                 const __grid_constant__ CUtensorMap tm_v) {
+                 const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_qr,
+                 const __grid_constant__ CUtensorMap tm_do, const __grid_constant__ CUtensorMap tm_kr,
+                 const int prerot) {
   using namespace dqw;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = tile::align1024(smem_raw);
@@ -771,12 +773,13 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
   const int n = kv_hi > kv_lo ? (kv_hi - kv_lo + BN - 1) / BN : 0;
   const bool blk_masked = (blk.flags & AI_BLOCKF_MASKED) != 0;
   const __half2* cs16 = static_cast<const __half2*>(L.rope_cs16);
+  const bool k_pre = prerot && (blk.flags & AI_BLOCKF_OWNPOS);
 
   if (tid == 0) {
     for (int i = 0; i < N_BARS; ++i) {
       uint32_t count = 1;
       if (i == K_READY || i == K_READY + 1 || i == DS_READY || i == DS_READY + 1) count = 128;
-      if (i == Q_READY) count = 256;
+      if (i == Q_READY) count = prerot ? 1 : 256;
       ptx::mbar_init(bar(i), count);
     }
     *s_abort = 0;
@@ -821,8 +824,9 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
       }
       const uint4* tab = reinterpret_cast<const uint4*>(cs16 + (int64_t)qrow * (D / 2));
       const uint32_t qt = t ? Q1 : Q0, ot = t ? DO1 : DO0;
+      // With the once-rotated copies the producer brings Q and dO by TMA.
 #pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
+      for (int hf = 0; hf < (prerot ? 0 : 2); ++hf) {
         uint4 x1[4], x2[4], g1[4], g2[4], cs[8];
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
@@ -846,8 +850,10 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
           *reinterpret_cast<uint4*>(sm + ot + chunk_off<BM>(r, cc + 8)) = g2[c];
         }
       }
-      ptx::fence_proxy_async_smem();
-      ptx::mbar_arrive(bar(Q_READY));
+      if (!prerot) {
+        ptx::fence_proxy_async_smem();
+        ptx::mbar_arrive(bar(Q_READY));
+      }
     }
     const float sl2 = f.scale * kLog2e;
     int done = 0;
@@ -926,15 +932,28 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
   } else if (warp == 8) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      ptx::prefetch_tmap(&tm_k);
+      const CUtensorMap* mk = k_pre ? &tm_kr : &tm_k;
+      ptx::prefetch_tmap(mk);
       ptx::prefetch_tmap(&tm_v);
+      if (prerot) {
+        const int h0 = 2 * blockIdx.y;
+        ptx::mbar_arrive_expect_tx(bar(Q_READY), 4 * 32768);
+        ptx::tma_load_4d(sbase + Q0, &tm_qr, bar(Q_READY), 0, q0, h0, b);
+        ptx::tma_load_4d(sbase + Q0 + 16384, &tm_qr, bar(Q_READY), 64, q0, h0, b);
+        ptx::tma_load_4d(sbase + Q1, &tm_qr, bar(Q_READY), 0, q0, h0 + 1, b);
+        ptx::tma_load_4d(sbase + Q1 + 16384, &tm_qr, bar(Q_READY), 64, q0, h0 + 1, b);
+        ptx::tma_load_4d(sbase + DO0, &tm_do, bar(Q_READY), 0, q0, h0, b);
+        ptx::tma_load_4d(sbase + DO0 + 16384, &tm_do, bar(Q_READY), 64, q0, h0, b);
+        ptx::tma_load_4d(sbase + DO1, &tm_do, bar(Q_READY), 0, q0, h0 + 1, b);
+        ptx::tma_load_4d(sbase + DO1 + 16384, &tm_do, bar(Q_READY), 64, q0, h0 + 1, b);
+      }
       for (int j = 0; j < n; ++j) {
         const int slot = j & 1, k0 = kv_lo + j * BN;
         if (j >= 2 && !wait(KV_EMPTY + slot, ((j >> 1) - 1) & 1)) break;
         const uint32_t kb = sbase + KB + 16384u * (uint32_t)slot, vb = sbase + VB + 16384u * (uint32_t)slot;
         ptx::mbar_arrive_expect_tx(bar(KV_FULL + slot), 32768);
-        ptx::tma_load_4d(kb, &tm_k, bar(KV_FULL + slot), 0, k0, hk, b);
-        ptx::tma_load_4d(kb + 8192, &tm_k, bar(KV_FULL + slot), 64, k0, hk, b);
+        ptx::tma_load_4d(kb, mk, bar(KV_FULL + slot), 0, k0, hk, b);
+        ptx::tma_load_4d(kb + 8192, mk, bar(KV_FULL + slot), 64, k0, hk, b);
         ptx::tma_load_4d(vb, &tm_v, bar(KV_FULL + slot), 0, k0, hk, b);
         ptx::tma_load_4d(vb + 8192, &tm_v, bar(KV_FULL + slot), 64, k0, hk, b);
       }
@@ -1008,16 +1027,18 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
         info = (uint32_t)__ldg(L.key_info + blk.key_off + key);
         p = key_row(info, L.n_pos, f.status);
       }
-      const uint4* tp = reinterpret_cast<const uint4*>(cs16 + (int64_t)p * (D / 2)) + 8 * cg;
+      if (!k_pre) {
+        const uint4* tp = reinterpret_cast<const uint4*>(cs16 + (int64_t)p * (D / 2)) + 8 * cg;
 #pragma unroll
-      for (int c = 0; c < 8; ++c) tab[c] = __ldg(tp + c);
+        for (int c = 0; c < 8; ++c) tab[c] = __ldg(tp + c);
+      }
     };
     if (n > 0) fetch(0);
     for (int j = 0; j < n; ++j) {
       const int slot = j & 1;
       if (!wait(KV_FULL + slot, (j >> 1) & 1)) break;
       const uint32_t kt = KB + 16384u * (uint32_t)slot;
-      if (kv_lo + j * BN + row < kv_hi) {
+      if (!k_pre && kv_lo + j * BN + row < kv_hi) {
 #pragma unroll
         for (int cc = 0; cc < 4; ++cc) {
           const int c = 4 * cg + cc;
@@ -1104,7 +1125,8 @@ struct BlockIter {
 __global__ void __launch_bounds__(kvw::kThreads, 1)
     dkdv_ws_kernel(const AiAttnBwdArgs a, const float* __restrict__ delta, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_q,
-                   const __grid_constant__ CUtensorMap tm_do) {
+                   const __grid_constant__ CUtensorMap tm_do, const __grid_constant__ CUtensorMap tm_kr,
+                   const int prerot) {
   using namespace kvw;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = tile::align1024(smem_raw);
@@ -1287,9 +1309,10 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
       bool ok = true;
       while (ok && it.next(blk)) {
         if (nb > 0 && !wait(BLK_DONE, (nb - 1) & 1)) break;
+        const CUtensorMap* mk = (prerot && (blk.flags & AI_BLOCKF_OWNPOS)) ? &tm_kr : &tm_k;
         ptx::mbar_arrive_expect_tx(bar(K_FULL), 32768);
-        ptx::tma_load_4d(sbase + K, &tm_k, bar(K_FULL), 0, j0, hk, b);
-        ptx::tma_load_4d(sbase + K + 16384, &tm_k, bar(K_FULL), 64, j0, hk, b);
+        ptx::tma_load_4d(sbase + K, mk, bar(K_FULL), 0, j0, hk, b);
+        ptx::tma_load_4d(sbase + K + 16384, mk, bar(K_FULL), 64, j0, hk, b);
         const int qs = max(blk.s, j0), nsteps = n_steps_of(blk);
         for (int st = 0; st < nsteps; ++st, ++s) {
           const int x = s & 1, q0 = qs + (st / G) * BQ, h = hk * G + st % G;
@@ -1388,8 +1411,10 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
     Block blk;
     int s = 0, nb = 0;
     while (!*s_abort && it.next(blk)) {
-      // K row rt by this block's key position.
+      // K row rt by this block's key position (already rotated when the block
+      // reads the once-rotated copy).
       {
+        const bool k_pre = prerot && (blk.flags & AI_BLOCKF_OWNPOS);
         const int key = j0 + rt;
         uint32_t info = 0;
         int p = 0;
@@ -1397,12 +1422,14 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
           info = (uint32_t)__ldg(L.key_info + blk.key_off + key);
           p = key_row(info, L.n_pos, f.status);
         }
-        const uint4* tp = reinterpret_cast<const uint4*>(cs16 + (int64_t)p * (D / 2));
         uint4 tab[16];
+        if (!k_pre) {
+          const uint4* tp = reinterpret_cast<const uint4*>(cs16 + (int64_t)p * (D / 2));
 #pragma unroll
-        for (int c = 0; c < 16; ++c) tab[c] = __ldg(tp + c);
+          for (int c = 0; c < 16; ++c) tab[c] = __ldg(tp + c);
+        }
         if (!wait(K_FULL, nb & 1)) break;
-        if (key < min(j1, blk.e)) {
+        if (!k_pre && key < min(j1, blk.e)) {
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
             uint4* pa = reinterpret_cast<uint4*>(sm + K + chunk_off<BN>(rt, c));
@@ -1432,14 +1459,16 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
             dl = __ldg(delta + idx);
           }
         }
-        const uint4* tp = reinterpret_cast<const uint4*>(cs16 + (int64_t)p * (D / 2)) + 8 * cg;
         uint4 tab[8];
+        if (!prerot) {
+          const uint4* tp = reinterpret_cast<const uint4*>(cs16 + (int64_t)p * (D / 2)) + 8 * cg;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) tab[c] = __ldg(tp + c);
+          for (int c = 0; c < 8; ++c) tab[c] = __ldg(tp + c);
+        }
         if (!wait(Q_FULL + x, (s >> 1) & 1)) break;
         const uint32_t qb = Q + 16384u * (uint32_t)x;
 #pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
+        for (int cc = 0; cc < (prerot ? 0 : 4); ++cc) {
           const int c = 4 * cg + cc;
           uint4* pa = reinterpret_cast<uint4*>(sm + qb + chunk_off<BQ>(r, c));
           uint4* pb = reinterpret_cast<uint4*>(sm + qb + chunk_off<BQ>(r, c + 8));
@@ -1481,17 +1510,29 @@ bool sm100_bwd_supported(int dtype, int head_dim) { return dtype == AI_DTYPE_BF1
 
 int sm100_kv_tile_rows() { return sm100bwd::kv::BN; }
 
-int sm100_bwd(const AiAttnBwdArgs& a, float* delta, cudaStream_t st, cudaError_t* cuda_err) {
+int sm100_bwd(const AiAttnBwdArgs& a, float* delta, void* rot, cudaStream_t st, cudaError_t* cuda_err) {
   using namespace sm100bwd;
   const AiAttnFwdArgs& f = a.fwd;
   if (!strides_ok(f.q) || !strides_ok(f.k) || !strides_ok(f.v) || !strides_ok(a.dout) || !strides_ok(a.dq) ||
       !strides_ok(a.dk) || !strides_ok(a.dv))
     return AI_ERR_STRIDE;
+  // With `rot` scratch, Q and K are rotated once (HBM-bound) and the
+  // warp-specialised kernels read the rotated copies.
+  AiTensor4 qr{}, kr{};
+  const bool pre = rot != nullptr;
+  if (pre && !sm100_rotated_views(f, rot, &qr, &kr)) return AI_ERR_ALIGN;
   cudaError_t e = bwd_delta(a, delta, st);
+  if (e == cudaSuccess && pre) e = prerot(f, rot, st);
   if (e == cudaSuccess && f.layout.n_fwd_items > 0) {
-    CUtensorMap tk, tv;
+    CUtensorMap tk, tv, tqr, tdo, tkr;
     if (!sm100_make_map(&tk, f.k, f.batch, f.num_kv_heads, f.seq_len, dq::BN) ||
-        !sm100_make_map(&tv, f.v, f.batch, f.num_kv_heads, f.seq_len, dq::BN))
+        !sm100_make_map(&tv, f.v, f.batch, f.num_kv_heads, f.seq_len, dq::BN) ||
+        !sm100_make_map(&tdo, a.dout, f.batch, f.num_q_heads, f.seq_len, dq::BM))
+      return AI_ERR_TMA;
+    tqr = tk;
+    tkr = tk;
+    if (pre && (!sm100_make_map(&tqr, qr, f.batch, f.num_q_heads, f.seq_len, dq::BM) ||
+                !sm100_make_map(&tkr, kr, f.batch, f.num_kv_heads, f.seq_len, dq::BN)))
       return AI_ERR_TMA;
     // Items of blocks with abs keys (all items when a GQA group has an odd
     // number of heads) on the one-head kernel, the rest two heads per CTA.
@@ -1508,17 +1549,23 @@ int sm100_bwd(const AiAttnBwdArgs& a, float* delta, cudaStream_t st, cudaError_t
     if (e == cudaSuccess && n_pair > 0) {
       e = cudaFuncSetAttribute(dq_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dqw::kSmem);
       if (e == cudaSuccess) {
-        dq_ws_kernel<<<dim3(n_pair, f.num_q_heads / 2), dqw::kThreads, dqw::kSmem, st>>>(a, delta, tk, tv);
+        dq_ws_kernel<<<dim3(n_pair, f.num_q_heads / 2), dqw::kThreads, dqw::kSmem, st>>>(a, delta, tk, tv, tqr, tdo,
+                                                                                         tkr, pre ? 1 : 0);
         e = cudaGetLastError();
       }
     }
   }
   if (e == cudaSuccess && f.layout.n_kv_items > 0) {
-    CUtensorMap tk, tv, tq, tdo;
+    CUtensorMap tk, tv, tq, tdo, tqr, tkr;
     if (!sm100_make_map(&tk, f.k, f.batch, f.num_kv_heads, f.seq_len, kv::BN) ||
         !sm100_make_map(&tv, f.v, f.batch, f.num_kv_heads, f.seq_len, kv::BN) ||
         !sm100_make_map(&tq, f.q, f.batch, f.num_q_heads, f.seq_len, kv::BQ) ||
         !sm100_make_map(&tdo, a.dout, f.batch, f.num_q_heads, f.seq_len, kv::BQ))
+      return AI_ERR_TMA;
+    tqr = tq;
+    tkr = tk;
+    if (pre && (!sm100_make_map(&tqr, qr, f.batch, f.num_q_heads, f.seq_len, kv::BQ) ||
+                !sm100_make_map(&tkr, kr, f.batch, f.num_kv_heads, f.seq_len, kv::BN)))
       return AI_ERR_TMA;
     // Key tiles that a block with abs keys sees run on the one-warpgroup kernel,
     // the rest on the warp-specialised one.
@@ -1533,7 +1580,8 @@ int sm100_bwd(const AiAttnBwdArgs& a, float* delta, cudaStream_t st, cudaError_t
     if (e == cudaSuccess && n_plain > 0) {
       e = cudaFuncSetAttribute(dkdv_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kvw::kSmem);
       if (e == cudaSuccess) {
-        dkdv_ws_kernel<<<dim3(n_plain, f.num_kv_heads), kvw::kThreads, kvw::kSmem, st>>>(a, delta, tk, tv, tq, tdo);
+        dkdv_ws_kernel<<<dim3(n_plain, f.num_kv_heads), kvw::kThreads, kvw::kSmem, st>>>(
+            a, delta, tk, tv, pre ? tqr : tq, tdo, tkr, pre ? 1 : 0);
         e = cudaGetLastError();
       }
     }

@@ -383,7 +383,8 @@ constexpr long long kWait = 1000000000LL;
 
 __global__ void __launch_bounds__(ws::kThreads, 1)
     fwd_ws_kernel(const AiAttnFwdArgs a, const __grid_constant__ CUtensorMap tm_k,
-                  const __grid_constant__ CUtensorMap tm_v) {
+                  const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_qr,
+                  const __grid_constant__ CUtensorMap tm_kr, const int prerot) {
   using namespace ws;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = tile::align1024(smem_raw);
@@ -401,6 +402,9 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
   const int kv_lo = blk.kv_lo, kv_hi = min(blk.e, q1);
   const int n = kv_hi > kv_lo ? (kv_hi - kv_lo + BN - 1) / BN : 0;
   const bool blk_masked = (blk.flags & AI_BLOCKF_MASKED) != 0;
+  // With the once-rotated copies: Q comes by TMA from q_rot, and K from k_rot
+  // when every key of this block has its own-block position.
+  const bool k_pre = prerot && (blk.flags & AI_BLOCKF_OWNPOS);
 
   if (tid == 0) {
     ptx::mbar_init(bar(KV_FULL), 1);
@@ -415,7 +419,7 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
     ptx::mbar_init(bar(P_READY + 1), 128);
     ptx::mbar_init(bar(O_DONE), 1);
     ptx::mbar_init(bar(O_DONE + 1), 1);
-    ptx::mbar_init(bar(Q_READY), 256);
+    ptx::mbar_init(bar(Q_READY), prerot ? 1 : 256);
     ptx::mbar_init(bar(FINAL), 1);
     *s_abort = 0;
     ptx::fence_mbar_init();
@@ -445,7 +449,7 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
     const int t = warp / 4, r = tid % 128, i = q0 + r, h = 2 * blockIdx.y + t;
     const uint32_t lane_base = (uint32_t)((warp % 4) * 32) << 16;
     const uint32_t c_s = t ? C_S1 : C_S0, c_o = t ? C_O1 : C_O0;
-    {
+    if (!prerot) {
       // Query row i of head h, rotated by its position: all global loads of
       // a half row are issued before any of it is rotated and stored.
       const __nv_bfloat16* Qrow = static_cast<const __nv_bfloat16*>(a.q.ptr) + b * a.q.stride_b +
@@ -598,15 +602,24 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
   } else if (warp == 8) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      ptx::prefetch_tmap(&tm_k);
+      const CUtensorMap* mk = k_pre ? &tm_kr : &tm_k;
+      ptx::prefetch_tmap(mk);
       ptx::prefetch_tmap(&tm_v);
+      if (prerot) {
+        const int h0 = 2 * blockIdx.y;
+        ptx::mbar_arrive_expect_tx(bar(Q_READY), 2 * kTile);
+        ptx::tma_load_4d(sbase + Q0, &tm_qr, bar(Q_READY), 0, q0, h0, b);
+        ptx::tma_load_4d(sbase + Q0 + kHalf, &tm_qr, bar(Q_READY), 64, q0, h0, b);
+        ptx::tma_load_4d(sbase + Q1, &tm_qr, bar(Q_READY), 0, q0, h0 + 1, b);
+        ptx::tma_load_4d(sbase + Q1 + kHalf, &tm_qr, bar(Q_READY), 64, q0, h0 + 1, b);
+      }
       for (int j = 0; j < n; ++j) {
         const int slot = j & 1, k0 = kv_lo + j * BN;
         if (j >= 2 && !wait(KV_EMPTY + slot, ((j >> 1) - 1) & 1)) break;
         const uint32_t kb = sbase + KB + (uint32_t)slot * kTile, vb = sbase + VB + (uint32_t)slot * kTile;
         ptx::mbar_arrive_expect_tx(bar(KV_FULL + slot), 2 * kTile);
-        ptx::tma_load_4d(kb, &tm_k, bar(KV_FULL + slot), 0, k0, hk, b);
-        ptx::tma_load_4d(kb + kHalf, &tm_k, bar(KV_FULL + slot), 64, k0, hk, b);
+        ptx::tma_load_4d(kb, mk, bar(KV_FULL + slot), 0, k0, hk, b);
+        ptx::tma_load_4d(kb + kHalf, mk, bar(KV_FULL + slot), 64, k0, hk, b);
         ptx::tma_load_4d(vb, &tm_v, bar(KV_FULL + slot), 0, k0, hk, b);
         ptx::tma_load_4d(vb + kHalf, &tm_v, bar(KV_FULL + slot), 64, k0, hk, b);
       }
@@ -684,16 +697,18 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
         info = (uint32_t)__ldg(L.key_info + blk.key_off + key);
         p = key_row(info, L.n_pos, a.status);
       }
-      const uint4* tp = reinterpret_cast<const uint4*>(cs16 + (int64_t)p * (D / 2));
+      if (!k_pre) {
+        const uint4* tp = reinterpret_cast<const uint4*>(cs16 + (int64_t)p * (D / 2));
 #pragma unroll
-      for (int c = 0; c < 16; ++c) tab[c] = __ldg(tp + c);
+        for (int c = 0; c < 16; ++c) tab[c] = __ldg(tp + c);
+      }
     };
     if (n > 0) fetch(0);
     for (int j = 0; j < n; ++j) {
       const int slot = j & 1;
       if (!wait(KV_FULL + slot, (j >> 1) & 1)) break;
       const uint32_t kt = KB + (uint32_t)slot * kTile;
-      if (info != 0 || kv_lo + j * BN + row < kv_hi) {
+      if (!k_pre && kv_lo + j * BN + row < kv_hi) {
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
           uint4* pa = reinterpret_cast<uint4*>(sm + kt + chunk_off(row, c));
@@ -782,14 +797,44 @@ int sm100_fwd(const AiAttnFwdArgs& a, cudaStream_t st, cudaError_t* cuda_err) {
     }
   }
   if (e == cudaSuccess && n_pair > 0) {
-    e = cudaFuncSetAttribute(fwd_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ws::kSmem);
+    // With enough workspace, rotate Q and K once (HBM-bound) and let the
+    // warp-specialised kernel read the rotated copies.
+    const bool pre = a.workspace && a.workspace_bytes >= prerot_bytes(a, nullptr);
+    CUtensorMap tm_qr = tm_k, tm_kr = tm_k;
+    if (pre) {
+      AiTensor4 qr, kr;
+      if (!sm100_rotated_views(a, a.workspace, &qr, &kr)) return AI_ERR_ALIGN;
+      if (!sm100_make_map(&tm_qr, qr, a.batch, a.num_q_heads, a.seq_len, BM) ||
+          !sm100_make_map(&tm_kr, kr, a.batch, a.num_kv_heads, a.seq_len, BN))
+        return AI_ERR_TMA;
+      e = prerot(a, a.workspace, st);
+    }
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(fwd_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ws::kSmem);
     if (e == cudaSuccess) {
-      fwd_ws_kernel<<<dim3(n_pair, a.num_q_heads / 2), ws::kThreads, ws::kSmem, st>>>(a, tm_k, tm_v);
+      fwd_ws_kernel<<<dim3(n_pair, a.num_q_heads / 2), ws::kThreads, ws::kSmem, st>>>(a, tm_k, tm_v, tm_qr, tm_kr,
+                                                                                      pre ? 1 : 0);
       e = cudaGetLastError();
     }
   }
   if (cuda_err) *cuda_err = e;
   return e == cudaSuccess ? AI_OK : AI_ERR_LAUNCH;
+}
+
+bool sm100_rotated_views(const AiAttnFwdArgs& a, void* buf, AiTensor4* qr, AiTensor4* kr) {
+  if (!buf || ((uintptr_t)buf % 256)) return false;
+  size_t qb = 0;
+  prerot_bytes(a, &qb);
+  const int64_t T = a.seq_len, Dm = sm100::D;
+  qr->ptr = buf;
+  qr->stride_t = Dm;
+  qr->stride_h = T * Dm;
+  qr->stride_b = (int64_t)a.num_q_heads * T * Dm;
+  kr->ptr = static_cast<char*>(buf) + qb;
+  kr->stride_t = Dm;
+  kr->stride_h = T * Dm;
+  kr->stride_b = (int64_t)a.num_kv_heads * T * Dm;
+  return true;
 }
 
 }  // namespace ai

@@ -41,9 +41,10 @@ int validate_fwd(const AiAttnFwdArgs* a) {
   if (!tensor_ok(a->q) || !tensor_ok(a->k) || !tensor_ok(a->v) || !tensor_ok(a->out)) return AI_ERR_NULL;
   if (!a->lse) return AI_ERR_NULL;
   const AiAttnLayout& L = a->layout;
-  if (!L.blocks || !L.row_blocks || !L.row_cov || !L.key_info || !L.q_pos || !L.rope_cos || !L.rope_sin ||
-      !L.rope_cs16)
+  if (!L.blocks || !L.row_blocks || !L.row_cov || !L.key_info || !L.q_pos || !L.k_own || !L.rope_cos ||
+      !L.rope_sin || !L.rope_cs16)
     return AI_ERR_NULL;
+  if (a->workspace && ((uintptr_t)a->workspace % 256)) return AI_ERR_ALIGN;
   if (L.n_blocks < 0 || L.n_keys < 0 || L.n_pos <= 0 || L.n_fwd_items < 0 || L.n_kv_items < 0) return AI_ERR_LAYOUT;
   if (L.n_fwd_items > 0 && !L.fwd_items) return AI_ERR_NULL;
   if (L.n_kv_items > 0 && !L.kv_items) return AI_ERR_NULL;
@@ -89,11 +90,20 @@ int ai_attn_fwd(const AiAttnFwdArgs* a, void* stream) {
   return launch_status(ai::simt_fwd(*a, st));
 }
 
+int ai_attn_fwd_workspace(const AiAttnFwdArgs* a, size_t* bytes) {
+  if (!a || !bytes) return AI_ERR_NULL;
+  int rc = validate_fwd(a);
+  if (rc != AI_OK) return rc;
+  *bytes = ai::sm100_fwd_supported(a->dtype, a->head_dim) ? ai::prerot_bytes(*a, nullptr) : 0;
+  return AI_OK;
+}
+
 int ai_attn_bwd_workspace(const AiAttnBwdArgs* a, size_t* bytes) {
   if (!a || !bytes) return AI_ERR_NULL;
   int rc = validate_fwd(&a->fwd);
   if (rc != AI_OK) return rc;
   *bytes = delta_bytes(a->fwd);
+  if (ai::sm100_bwd_supported(a->fwd.dtype, a->fwd.head_dim)) *bytes += ai::prerot_bytes(a->fwd, nullptr);
   return AI_OK;
 }
 
@@ -107,7 +117,13 @@ int ai_attn_bwd(const AiAttnBwdArgs* a, void* stream) {
   if (!device_is_sm100()) return AI_ERR_NO_DEVICE;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   float* delta = static_cast<float*>(a->workspace);
-  if (ai::sm100_bwd_supported(a->fwd.dtype, a->fwd.head_dim)) return ai::sm100_bwd(*a, delta, st, nullptr);
+  if (ai::sm100_bwd_supported(a->fwd.dtype, a->fwd.head_dim)) {
+    // Workspace = delta, then (if it fits) the once-rotated Q and K copies.
+    const size_t db = delta_bytes(a->fwd);
+    void* rot = nullptr;
+    if (a->workspace_bytes >= db + ai::prerot_bytes(a->fwd, nullptr)) rot = static_cast<char*>(a->workspace) + db;
+    return ai::sm100_bwd(*a, delta, rot, st, nullptr);
+  }
   return launch_status(ai::simt_bwd(*a, delta, st));
 }
 

@@ -29,8 +29,18 @@ int sm100_fwd_tile_rows();
 int sm100_fwd(const AiAttnFwdArgs& a, cudaStream_t st, cudaError_t* cuda_err);
 bool sm100_bwd_supported(int dtype, int head_dim);
 int sm100_kv_tile_rows();
-int sm100_bwd(const AiAttnBwdArgs& a, float* delta, cudaStream_t st, cudaError_t* cuda_err);
+// `rot`: scratch for the once-rotated Q/K copies (prerot_bytes), or nullptr to
+// rotate every tile in shared memory.
+int sm100_bwd(const AiAttnBwdArgs& a, float* delta, void* rot, cudaStream_t st, cudaError_t* cuda_err);
 // TMA map over a (B, H, T, 128) bf16 tensor, box 64 x box_rows, 128-byte swizzle.
 bool sm100_make_map(CUtensorMap* map, const AiTensor4& t, int B, int H, int T, int box_rows);
+
+// Once-rotated Q and K copies (bf16, head_dim 128) for the tensor-core kernels:
+// bytes of scratch they need (q_bytes: offset of the K copy), and the launch
+// writing q_rot = R(q_pos) q at buf and k_rot = R(k_own) k at buf + q_bytes.
+size_t prerot_bytes(const AiAttnFwdArgs& a, size_t* q_bytes);
+cudaError_t prerot(const AiAttnFwdArgs& a, void* buf, cudaStream_t st);
+// (B, H, T, 128) views of the two copies inside buf (false if buf is misaligned).
+bool sm100_rotated_views(const AiAttnFwdArgs& a, void* buf, AiTensor4* qr, AiTensor4* kr);
 
 }  // namespace ai

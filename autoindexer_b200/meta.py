@@ -17,7 +17,9 @@ Output (``CompiledLayout``), all int32 / fp32 device tensors:
 * ``key_info [sum E]``: per concatenated key, the rotary table row (bits
   0..29), attn mask (bit 30), abs mask (bit 31);
 * ``q_pos [B, T]``: table row of every query row (rows past the covered
-  length use position 0, as ``perturb_labels.py:335`` pads);
+  length use position 0, as ``perturb_labels.py:335`` pads); ``k_own [B, T]``
+  the table row of key j in the block whose query rows hold j (a block
+  flagged OWNPOS attends every key at that row, e.g. packed documents);
 * ``rope_cos / rope_sin [n_pos, D/2]``: fp32 table of the rotary module, and
   ``rope_cs16 [n_pos, D/2, 2]`` the same angles as fp16 (cos, sin) pairs for
   the bf16 tensor-core kernels;
@@ -45,7 +47,7 @@ __all__ = ["RowLayouts", "CompiledLayout", "compile_layout", "layout_rows", "dty
 _KEY_ATTN = np.uint32(1 << 30)
 _KEY_ABS = np.uint32(1 << 31)
 _ROW_MASK = (1 << 30) - 1
-BLOCKF_MASKED, BLOCKF_ABS = 1, 2
+BLOCKF_MASKED, BLOCKF_ABS, BLOCKF_OWNPOS = 1, 2, 4
 
 
 class RowLayouts(list):
@@ -135,6 +137,7 @@ class CompiledLayout:
     row_cov: torch.Tensor
     key_info: torch.Tensor
     q_pos: torch.Tensor
+    k_own: torch.Tensor
     rope_cos: torch.Tensor
     rope_sin: torch.Tensor
     rope_cs16: torch.Tensor
@@ -154,6 +157,7 @@ class CompiledLayout:
         L.key_info = self.key_info.data_ptr()
         L.n_keys = int(self.key_info.numel())
         L.q_pos = self.q_pos.data_ptr()
+        L.k_own = self.k_own.data_ptr()
         L.rope_cos = self.rope_cos.data_ptr()
         L.rope_sin = self.rope_sin.data_ptr()
         L.rope_cs16 = self.rope_cs16.data_ptr()
@@ -246,7 +250,7 @@ def _compile(parsed_positions, batch, seq_len, head_dim, code, rotary_emb, devic
     if n_pos > _ROW_MASK:
         raise ValueError("position range too large for the kernel tables")
 
-    key_info_parts, key_base = [], []
+    key_info_parts, key_base, own_rows, own_flags = [], [], [], []
     base = 0
     for h in hosts:
         rowidx = np.clip(h.kpos - lo, 0, n_pos - 1).astype(np.uint32)
@@ -254,16 +258,26 @@ def _compile(parsed_positions, batch, seq_len, head_dim, code, rotary_emb, devic
         key_info_parts.append(info)
         key_base.append(base)
         base += info.shape[0]
+        # Key j's table row in the block whose query rows hold j; a block whose
+        # attended keys all use that row can read a once-rotated copy of K.
+        own = np.zeros(seq_len, dtype=np.int64)
+        for s, e, ks, ke in h.bounds:
+            own[s:e] = rowidx[ks + s:ks + e]
+        own_rows.append(own)
+        own_flags.append([bool(np.all(rowidx[ks:ke][h.attn[ks:ke]] == own[:e][h.attn[ks:ke]]))
+                          for s, e, ks, ke in h.bounds])
     key_info = np.concatenate(key_info_parts).view(np.int32)
 
     blocks, row_blocks, row_cov = [], [0], []
     q_pos = np.zeros((batch, seq_len), dtype=np.int32)
+    k_own = np.zeros((batch, seq_len), dtype=np.int32)
     pairs = 0
     host_pairs = [_pairs(h) for h in hosts]
     for b, r in enumerate(rows):
         u = index_of[id(r)]
         h = hosts[u]
-        for s, e, ks, ke in h.bounds:
+        k_own[b] = own_rows[u]
+        for bi, (s, e, ks, ke) in enumerate(h.bounds):
             am = h.attn[ks:ke]
             nz = np.flatnonzero(am)
             kv_lo = int(nz[0]) if nz.size else int(e)
@@ -272,6 +286,8 @@ def _compile(parsed_positions, batch, seq_len, head_dim, code, rotary_emb, devic
                 flags |= BLOCKF_MASKED
             if (h.abs_[ks:ke] & am).any():
                 flags |= BLOCKF_ABS
+            if own_flags[u][bi]:
+                flags |= BLOCKF_OWNPOS
             blocks.append((b, int(s), int(e), key_base[u] + int(ks), kv_lo, flags, 0, 0))
         row_blocks.append(len(blocks))
         cov = int(h.bounds[-1, 1])
@@ -297,7 +313,7 @@ def _compile(parsed_positions, batch, seq_len, head_dim, code, rotary_emb, devic
         batch=batch, seq_len=seq_len, head_dim=head_dim, dtype=code, n_pos=n_pos, p_min=lo,
         fwd_tile=fwd_tile, kv_tile=kv_tile,
         blocks=dev(blocks_np), row_blocks=dev(np.asarray(row_blocks, dtype=np.int32)), row_cov=dev(row_cov_np),
-        key_info=dev(key_info), q_pos=dev(q_pos), rope_cos=cos, rope_sin=sin,
+        key_info=dev(key_info), q_pos=dev(q_pos), k_own=dev(k_own), rope_cos=cos, rope_sin=sin,
         rope_cs16=torch.stack([cos, sin], dim=-1).to(torch.float16).contiguous(),
         fwd_items=dev(fwd_items), kv_items=dev(kv_items), n_fwd_abs_items=n_abs, n_kv_abs_items=n_kv_abs,
         pairs_per_head=pairs,

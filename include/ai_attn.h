@@ -43,7 +43,7 @@
 extern "C" {
 #endif
 
-#define AI_ATTN_ABI_VERSION 2
+#define AI_ATTN_ABI_VERSION 3
 
 typedef enum AiDtype {
   AI_DTYPE_BF16 = 0,
@@ -87,6 +87,8 @@ typedef struct AiTensor4 {
 #define AI_BLOCK_FIELDS 8
 #define AI_BLOCKF_MASKED 1 /* some key in [kv_lo, e) has attn_mask false */
 #define AI_BLOCKF_ABS 2    /* some key has abs_pos_mask set */
+#define AI_BLOCKF_OWNPOS 4 /* every attended key has the position k_own gives it (so a K copy
+                              rotated once per key serves this block) */
 
 /* key_info word: bits 0..29 rotary table row, bit 30 attn_mask, bit 31 abs_pos_mask. */
 #define AI_KEY_ROW_MASK 0x3FFFFFFF
@@ -101,6 +103,7 @@ typedef struct AiAttnLayout {
   const int32_t* key_info;    /* [n_keys] */
   int64_t n_keys;
   const int32_t* q_pos;       /* [B][T] rotary table row of each query row */
+  const int32_t* k_own;       /* [B][T] rotary table row of key j in the block whose query rows hold j */
   const float* rope_cos;      /* [n_pos][D/2] fp32: cos of the angle of (table row, frequency slot) */
   const float* rope_sin;      /* [n_pos][D/2] */
   const void* rope_cs16;      /* [n_pos][D/2] fp16 pairs (cos, sin) of the same angles: the bf16 kernels'
@@ -131,6 +134,10 @@ typedef struct AiAttnFwdArgs {
   float* lse;             /* (B, Hq, T) natural-log log-sum-exp of the scaled logits */
   AiAttnLayout layout;
   int32_t* status;        /* optional device status word */
+  void* workspace;        /* optional scratch (256-B aligned); with ai_attn_fwd_workspace bytes the
+                             tensor-core kernels read once-rotated copies of Q and K from it, with
+                             less (or NULL) they rotate every tile in shared memory */
+  size_t workspace_bytes;
 } AiAttnFwdArgs;
 
 typedef struct AiAttnBwdArgs {
@@ -139,8 +146,9 @@ typedef struct AiAttnBwdArgs {
   AiTensor4 dq;           /* (B, Hq, T, D) */
   AiTensor4 dk;           /* (B, Hkv, T, D), summed over the query heads of each group */
   AiTensor4 dv;           /* (B, Hkv, T, D) */
-  void* workspace;        /* device scratch of at least ai_attn_bwd_workspace bytes, 256-B aligned */
-  size_t workspace_bytes;
+  void* workspace;        /* device scratch, 256-B aligned: at least B*Hq*T floats (rounded up to
+                             256 B); ai_attn_bwd_workspace bytes also hold the rotated Q/K copies */
+  size_t workspace_bytes; /* (fwd.workspace is not used by ai_attn_bwd) */
 } AiAttnBwdArgs;
 
 /* ABI version this library was built with (AI_ATTN_ABI_VERSION). */
@@ -155,7 +163,12 @@ int ai_attn_kv_tile_rows(int dtype, int head_dim);
  * row and lse = 0, the reference's diagonal-only convention). */
 int ai_attn_fwd(const AiAttnFwdArgs* args, void* stream);
 
-/* Bytes of device scratch ai_attn_bwd needs for these arguments. */
+/* Bytes of forward scratch for the fastest path (0 when the dtype / head_dim
+ * has no use for it). */
+int ai_attn_fwd_workspace(const AiAttnFwdArgs* args, size_t* bytes);
+
+/* Bytes of backward scratch for the fastest path (the minimum is
+ * B*Hq*T floats rounded up to 256 B). */
 int ai_attn_bwd_workspace(const AiAttnBwdArgs* args, size_t* bytes);
 
 /* Backward: dq, dk, dv (written, not accumulated). */

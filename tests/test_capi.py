@@ -31,7 +31,7 @@ def test_library_exports_every_declared_function():
 
 def test_abi_version_and_tiles():
     L = _lib.lib()
-    assert L.ai_attn_abi_version() == 2
+    assert L.ai_attn_abi_version() == 3
     assert L.ai_attn_fwd_tile_rows(_lib.DTYPE_BF16, 128) == 128
     assert L.ai_attn_fwd_tile_rows(_lib.DTYPE_F32, 64) == 32
     assert L.ai_attn_kv_tile_rows(_lib.DTYPE_F32, 64) > 0
@@ -53,7 +53,7 @@ def _args(**over):
         getattr(a, t).ptr = 256
     a.lse = 256
     L = a.layout
-    L.blocks = L.row_blocks = L.row_cov = L.key_info = L.q_pos = L.rope_cos = L.rope_sin = L.rope_cs16 = 256
+    L.blocks = L.row_blocks = L.row_cov = L.key_info = L.q_pos = L.k_own = L.rope_cos = L.rope_sin = L.rope_cs16 = 256
     L.n_pos = 1
     L.fwd_tile = 32
     L.kv_tile = 64

@@ -84,7 +84,11 @@ def test_work_items_cover_rows_and_keys_once(dtype):
     assert list(c.row_cov.numpy()) == [sum(lens_a), sum(lens_b)]
     # documents: each block attends from its own first row on
     for row, s, e, koff, kv_lo, flags, _, _ in blocks:
-        assert kv_lo == s and flags == 0
+        # no masked keys, no abs keys, every key at its own-block position
+        assert kv_lo == s and flags == 4
+    own = c.k_own.numpy()
+    assert np.array_equal(own[0, :sum(lens_a)] + c.p_min,
+                          np.concatenate([np.arange(n) for n in lens_a]))
 
 
 def test_layout_rejects_malformed_lists():

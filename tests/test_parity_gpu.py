@@ -186,6 +186,33 @@ def test_bf16_full_size_prefix_matches_oracle(cuda_device):
     check_bf16(sl, want, "full-size prefix")
 
 
+@pytest.mark.parametrize("layout_kind", ["documents", "edit_chain"])
+def test_bf16_rotated_copies_match_in_kernel_rotation(layout_kind, cuda_device):
+    """The fast path (Q and K rotated once into scratch, read by TMA) and the
+    small-workspace path (every tile rotated in shared memory) agree."""
+    if layout_kind == "documents":
+        B, T, Hq, Hkv, D = 2, 700, 8, 2, 128
+        rows, mod, _ = _sectioned_docs(B, T, D, 2, seed=31)
+        lay = rows
+        rng = np.random.default_rng(2)
+        q, k, v = (rng.standard_normal(s) for s in ((B, Hq, T, D), (B, Hkv, T, D), (B, Hkv, T, D)))
+        dout = rng.standard_normal((B, T, Hq, D))
+    else:
+        lay, q, k, v, dout, mod, _ = _edit_chain_case("op2_d32", 2, 4, 2, 128, 13)
+        B, Hq, T, D = q.shape
+    tq, tk, tv, tdo = (torch.as_tensor(x).to(cuda_device, torch.bfloat16) for x in (q, k, v, dout))
+    layout = compile_layout(lay, B, T, D, torch.bfloat16, mod.to(cuda_device), cuda_device)
+    res = []
+    for copies in (True, False):
+        out, lse = attn_fwd(tq, tk, tv, layout, D ** -0.5, rotated_copies=copies)
+        grads = attn_bwd(tq, tk, tv, out, lse, tdo, layout, D ** -0.5, rotated_copies=copies)
+        res.append([t.double().cpu().numpy() for t in (out, lse, *grads)])
+    torch.cuda.synchronize(cuda_device)
+    assert read_status(cuda_device) == 0
+    for name, a_, b_ in zip(("out", "lse", "dq", "dk", "dv"), *res):
+        assert rel_l2(a_, b_) <= 1e-3, (name, rel_l2(a_, b_))
+
+
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 def test_deterministic_reruns(dtype, cuda_device):
     D = 128 if dtype == torch.bfloat16 else 64
