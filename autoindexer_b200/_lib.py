@@ -29,7 +29,7 @@ __all__ = [
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_ai_attn.so")
 
 DTYPE_BF16, DTYPE_F16, DTYPE_F32 = 0, 1, 2
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 # Every function include/ai_attn.h declares.
 EXPORTED_SYMBOLS = (
@@ -113,6 +113,7 @@ class AiAttnBwdArgs(ctypes.Structure):
         ("dv", AiTensor4),
         ("workspace", ctypes.c_void_p),
         ("workspace_bytes", ctypes.c_size_t),
+        ("fwd_rotated", ctypes.c_int32),
     ]
 
 

@@ -95,12 +95,14 @@ def _fwd_args(q: Tensor, k: Tensor, v: Tensor, out_bhtd: Tensor, lse: Tensor, la
 
 
 def attn_fwd(q: Tensor, k: Tensor, v: Tensor, layout: CompiledLayout, scale: float,
-             rotated_copies: bool = True) -> Tuple[Tensor, Tensor]:
+             rotated_copies: bool = True, keep_workspace: bool = False):
     """Launches ``ai_attn_fwd``: returns ``out (B, T, Hq, D)`` and ``lse (B, Hq, T)`` fp32.
 
     ``rotated_copies``: give the kernels scratch for once-rotated Q/K copies
     (faster; ``ai_attn_fwd_workspace`` bytes); without it every tile is
-    rotated in shared memory."""
+    rotated in shared memory.  ``keep_workspace``: also return that scratch
+    (or ``None``) so that ``attn_bwd(..., fwd_workspace=...)`` reads the
+    rotated copies instead of rotating again."""
     B, Hq, T, D = q.shape
     out = torch.empty((B, T, Hq, D), dtype=q.dtype, device=q.device)
     lse = torch.empty((B, Hq, T), dtype=torch.float32, device=q.device)
@@ -114,14 +116,19 @@ def attn_fwd(q: Tensor, k: Tensor, v: Tensor, layout: CompiledLayout, scale: flo
         a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
     stream = torch.cuda.current_stream(q.device).cuda_stream
     _lib.check(lib.ai_attn_fwd(ctypes.byref(a), ctypes.c_void_p(stream)), "ai_attn_fwd")
+    if keep_workspace:
+        return out, lse, ws
     del ws
     return out, lse
 
 
-def attn_bwd(q, k, v, out, lse, dout, layout: CompiledLayout, scale: float, rotated_copies: bool = True):
+def attn_bwd(q, k, v, out, lse, dout, layout: CompiledLayout, scale: float, rotated_copies: bool = True,
+             fwd_workspace: Optional[Tensor] = None):
     """Launches ``ai_attn_bwd``: returns ``dq, dk, dv`` shaped like ``q, k, v``
     (``rotated_copies`` as for ``attn_fwd``; without it the workspace holds
-    only the row sums of dO.O)."""
+    only the row sums of dO.O).  ``fwd_workspace``: the scratch that
+    ``attn_fwd(..., keep_workspace=True)`` returned for these q, k and layout;
+    its rotated Q/K copies are reused (``fwd_rotated`` in the C ABI)."""
     dq = torch.empty_like(q)
     dk = torch.empty_like(k)
     dv = torch.empty_like(v)
@@ -136,6 +143,9 @@ def attn_bwd(q, k, v, out, lse, dout, layout: CompiledLayout, scale: float, rota
     dout_keep = _dense_d(dout)
     a.dout = _t4(dout_keep.permute(0, 2, 1, 3))
     a.dq, a.dk, a.dv = _t4(dq), _t4(dk), _t4(dv)
+    if fwd_workspace is not None and rotated_copies:
+        a.fwd.workspace, a.fwd.workspace_bytes = fwd_workspace.data_ptr(), fwd_workspace.numel()
+        a.fwd_rotated = 1
     lib = _lib.lib()
     nbytes = ctypes.c_size_t(0)
     _lib.check(lib.ai_attn_bwd_workspace(ctypes.byref(a), ctypes.byref(nbytes)), "ai_attn_bwd_workspace")
@@ -157,16 +167,18 @@ class AttentionFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, layout: CompiledLayout, scale: float):
         q, k, v = _dense_d(q), _dense_d(k), _dense_d(v)
-        out, lse = attn_fwd(q, k, v, layout, scale)
+        out, lse, ws = attn_fwd(q, k, v, layout, scale, keep_workspace=True)
         ctx.save_for_backward(q, k, v, out, lse)
         ctx.layout = layout
         ctx.scale = scale
+        ctx.fwd_ws = ws  # rotated Q/K copies, reused by the backward
         return out
 
     @staticmethod
     def backward(ctx, dout):
         q, k, v, out, lse = ctx.saved_tensors
-        dq, dk, dv = attn_bwd(q, k, v, out, lse, dout, ctx.layout, ctx.scale)
+        dq, dk, dv = attn_bwd(q, k, v, out, lse, dout, ctx.layout, ctx.scale, fwd_workspace=ctx.fwd_ws)
+        ctx.fwd_ws = None
         return dq, dk, dv, None, None
 
 

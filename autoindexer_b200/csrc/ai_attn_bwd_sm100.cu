@@ -730,9 +730,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 // warp 9 MMA issuer; warps 10-13 rotate each K tile by the keys' block
 // positions.  TMEM per head t: S_t [128t .. +64), dP_t [+64 .. +128), dQ_t
 // accumulator [256 + 128t .. +128).  dS_t (bf16 pairs) overwrites the first 32
-// columns of S_t and is the A operand of dQ_t += dS_t.Krot; the next S_t is
-// issued only after that MMA completed.  MMA order per key tile j:
-// dQ0(j), S0/dP0(j+1), dQ1(j), S1/dP1(j+1).
+// columns of S_t and is the A operand of dQ_t += dS_t.Krot; the next S_t
+// follows that MMA directly (MMAs of one thread execute in issue order).  MMA
+// order per key tile j: dQ0(j), S0/dP0(j+1), dQ1(j), S1/dP1(j+1).  The MMA
+// warp runs converged and elects one lane per MMA.
 // ===========================================================================
 namespace dqw {
 constexpr int BM = 128, BN = 64, kThreads = 448;
@@ -960,60 +961,57 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
     }
   } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc_s = ptx::idesc_bf16_f32(BM, BN, false, false);
-      constexpr uint32_t idesc_dq = ptx::idesc_bf16_f32(BM, D, false, true);
-      auto issue_s = [&](int t, int slot) {
-        const uint32_t qt = sbase + (t ? Q1 : Q0), ot = sbase + (t ? DO1 : DO0);
-        const uint32_t kt = sbase + KB + 16384u * (uint32_t)slot, vt = sbase + VB + 16384u * (uint32_t)slot;
-        const uint32_t cs = tmem + 128u * (uint32_t)t;
+    // Whole warp (warp-uniform descriptors); one elected lane issues.
+    auto wait_u = [&](int i, uint32_t parity) -> bool { return __shfl_sync(0xffffffffu, wait(i, parity), 0); };
+    constexpr uint32_t idesc_s = ptx::idesc_bf16_f32(BM, BN, false, false);
+    constexpr uint32_t idesc_dq = ptx::idesc_bf16_f32(BM, D, false, true);
+    auto issue_s = [&](int t, int slot) {
+      const uint32_t qt = sbase + (t ? Q1 : Q0), ot = sbase + (t ? DO1 : DO0);
+      const uint32_t kt = sbase + KB + 16384u * (uint32_t)slot, vt = sbase + VB + 16384u * (uint32_t)slot;
+      const uint32_t cs = tmem + 128u * (uint32_t)t;
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t ao = (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u;
-          const uint32_t bo = (uint32_t)(kk >> 2) * 8192u + (uint32_t)(kk & 3) * 32u;
-          ptx::mma_ss(cs, ptx::sdesc_sw128(qt + ao, 16, 1024), ptx::sdesc_sw128(kt + bo, 16, 1024), idesc_s, kk > 0);
-          ptx::mma_ss(cs + 64, ptx::sdesc_sw128(ot + ao, 16, 1024), ptx::sdesc_sw128(vt + bo, 16, 1024), idesc_s,
+      for (int kk = 0; kk < D / 16; ++kk) {
+        const uint32_t ao = (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u;
+        const uint32_t bo = (uint32_t)(kk >> 2) * 8192u + (uint32_t)(kk & 3) * 32u;
+        ptx::mma_ss_w(cs, ptx::sdesc_sw128(qt + ao, 16, 1024), ptx::sdesc_sw128(kt + bo, 16, 1024), idesc_s, kk > 0);
+        ptx::mma_ss_w(cs + 64, ptx::sdesc_sw128(ot + ao, 16, 1024), ptx::sdesc_sw128(vt + bo, 16, 1024), idesc_s,
                       kk > 0);
-        }
-        ptx::mma_commit(bar(S_FULL + t));
-      };
-      auto issue_dq = [&](int t, int slot, bool first) {
-        const uint32_t kt = sbase + KB + 16384u * (uint32_t)slot;
-#pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk)
-          ptx::mma_ts(tmem + 256u + 128u * (uint32_t)t, tmem + 128u * (uint32_t)t + 8u * (uint32_t)kk,
-                      ptx::sdesc_sw128(kt + 2048u * (uint32_t)kk, 8192, 1024), idesc_dq, (!first || kk > 0) ? 1u : 0u);
-        ptx::mma_commit(bar(DQ_DONE + t));
-      };
-      if (wait(Q_READY, 0) && n > 0 && wait(K_READY, 0)) {
-        ptx::tc_fence_after();
-        issue_s(0, 0);
-        issue_s(1, 0);
-        for (int j = 0; j < n; ++j) {
-          const int slot = j & 1, nslot = (j + 1) & 1;
-          const bool more = j + 1 < n;
-          if (!wait(DS_READY, j & 1)) break;
-          ptx::tc_fence_after();
-          issue_dq(0, slot, j == 0);
-          if (more) {
-            if (!wait(K_READY + nslot, ((j + 1) >> 1) & 1) || !wait(DQ_DONE, j & 1)) break;
-            ptx::tc_fence_after();
-            issue_s(0, nslot);
-          }
-          if (!wait(DS_READY + 1, j & 1)) break;
-          ptx::tc_fence_after();
-          issue_dq(1, slot, j == 0);
-          ptx::mma_commit(bar(KV_EMPTY + slot));
-          if (more) {
-            if (!wait(DQ_DONE + 1, j & 1)) break;
-            ptx::tc_fence_after();
-            issue_s(1, nslot);
-          }
-        }
       }
-      ptx::mma_commit(bar(FINAL));
-      ptx::mbar_wait(bar(FINAL), 0, kWait);
+      ptx::mma_commit_w(bar(S_FULL + t));
+    };
+    auto issue_dq = [&](int t, int slot, bool first) {
+      const uint32_t kt = sbase + KB + 16384u * (uint32_t)slot;
+#pragma unroll
+      for (int kk = 0; kk < BN / 16; ++kk)
+        ptx::mma_ts_w(tmem + 256u + 128u * (uint32_t)t, tmem + 128u * (uint32_t)t + 8u * (uint32_t)kk,
+                      ptx::sdesc_sw128(kt + 2048u * (uint32_t)kk, 8192, 1024), idesc_dq,
+                      (!first || kk > 0) ? 1u : 0u);
+      ptx::mma_commit_w(bar(DQ_DONE + t));
+    };
+    if (wait_u(Q_READY, 0) && n > 0 && wait_u(K_READY, 0)) {
+      ptx::tc_fence_after();
+      issue_s(0, 0);
+      issue_s(1, 0);
+      for (int j = 0; j < n; ++j) {
+        const int slot = j & 1, nslot = (j + 1) & 1;
+        const bool more = j + 1 < n;
+        if (!wait_u(DS_READY, j & 1)) break;
+        ptx::tc_fence_after();
+        issue_dq(0, slot, j == 0);
+        if (more) {
+          if (!wait_u(K_READY + nslot, ((j + 1) >> 1) & 1)) break;
+          ptx::tc_fence_after();
+          issue_s(0, nslot);
+        }
+        if (!wait_u(DS_READY + 1, j & 1)) break;
+        ptx::tc_fence_after();
+        issue_dq(1, slot, j == 0);
+        ptx::mma_commit_w(bar(KV_EMPTY + slot));
+        if (more) issue_s(1, nslot);
+      }
     }
+    ptx::mma_commit_w(bar(FINAL));
+    ptx::mbar_wait(bar(FINAL), 0, kWait);
   } else {
     // ------------------------------------------------------------ K rotation (warps 10-13)
     const int rt = tid - 320, row = rt & 63, cg = rt >> 6;
@@ -1080,7 +1078,10 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
 //                   step's lse / delta rows in smem.
 // TMEM: S^T / dP^T double-buffered by step parity (4 x 64 columns), dV and
 // dKrot accumulators (128 each).  dV += P^T dO and dKrot += dS^T Qrot take
-// their A operands from TMEM.  At the end of a block score group 0 rotates
+// their A operands from TMEM; the scores of step s + 2 reuse that buffer
+// right after those MMAs (one thread's MMAs execute in issue order), and the
+// producer alone waits for them before refilling the Q / dO slot.  The MMA
+// warp runs converged and elects one lane per MMA.  At the end of a block score group 0 rotates
 // dKrot back by the keys' block positions into an fp32 dK accumulator in
 // smem, so keys seen by several blocks are summed without atomics.
 // ===========================================================================
@@ -1332,78 +1333,79 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
     }
   } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc_st = ptx::idesc_bf16_f32(BN, BQ, false, false);
-      constexpr uint32_t idesc_acc = ptx::idesc_bf16_f32(BN, D, false, true);
-      auto issue_scores = [&](int s) {
-        const int x = s & 1;
-        const uint32_t qb = sbase + Q + 16384u * (uint32_t)x, ob = sbase + DO + 16384u * (uint32_t)x;
-        const uint32_t cb = tmem + C_BUF + 128u * (uint32_t)x;
+    // Whole warp (warp-uniform descriptors); one elected lane issues.
+    auto wait_u = [&](int i, uint32_t parity) -> bool { return __shfl_sync(0xffffffffu, wait(i, parity), 0); };
+    constexpr uint32_t idesc_st = ptx::idesc_bf16_f32(BN, BQ, false, false);
+    constexpr uint32_t idesc_acc = ptx::idesc_bf16_f32(BN, D, false, true);
+    auto issue_scores = [&](int s) {
+      const int x = s & 1;
+      const uint32_t qb = sbase + Q + 16384u * (uint32_t)x, ob = sbase + DO + 16384u * (uint32_t)x;
+      const uint32_t cb = tmem + C_BUF + 128u * (uint32_t)x;
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t ao = (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u;
-          const uint32_t bo = (uint32_t)(kk >> 2) * 8192u + (uint32_t)(kk & 3) * 32u;
-          ptx::mma_ss(cb, ptx::sdesc_sw128(sbase + K + ao, 16, 1024), ptx::sdesc_sw128(qb + bo, 16, 1024), idesc_st,
+      for (int kk = 0; kk < D / 16; ++kk) {
+        const uint32_t ao = (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u;
+        const uint32_t bo = (uint32_t)(kk >> 2) * 8192u + (uint32_t)(kk & 3) * 32u;
+        ptx::mma_ss_w(cb, ptx::sdesc_sw128(sbase + K + ao, 16, 1024), ptx::sdesc_sw128(qb + bo, 16, 1024), idesc_st,
                       kk > 0);
-          ptx::mma_ss(cb + 64, ptx::sdesc_sw128(sbase + V + ao, 16, 1024), ptx::sdesc_sw128(ob + bo, 16, 1024),
+        ptx::mma_ss_w(cb + 64, ptx::sdesc_sw128(sbase + V + ao, 16, 1024), ptx::sdesc_sw128(ob + bo, 16, 1024),
                       idesc_st, kk > 0);
-        }
-        ptx::mma_commit(bar(S_FULL + x));
-      };
-      bool ok = wait(V_FULL, 0);
-      BlockIter it(&L, b, j0, j1);
-      Block blk;
-      int s = 0, nb = 0;
-      bool dv_started = false;
-      while (ok && it.next(blk)) {
-        const int nsteps = n_steps_of(blk);
-        if (!wait(K_READY, nb & 1)) break;
-        ptx::tc_fence_after();
-        const int sb = s;
-        // scores of the block's first step
-        if (!wait(Q_READY + (s & 1), (s >> 1) & 1) || (s >= 2 && !wait(Q_EMPTY + (s & 1), ((s >> 1) - 1) & 1))) break;
-        ptx::tc_fence_after();
-        issue_scores(s);
-        for (; s < sb + nsteps; ++s) {
-          const int x = s & 1;
-          if (s + 1 < sb + nsteps) {
-            const int y = (s + 1) & 1;
-            if (!wait(Q_READY + y, ((s + 1) >> 1) & 1) || (s + 1 >= 2 && !wait(Q_EMPTY + y, (((s + 1) >> 1) - 1) & 1))) {
-              ok = false;
-              break;
-            }
-            ptx::tc_fence_after();
-            issue_scores(s + 1);
-          }
-          if (!wait(P_READY + x, (s >> 1) & 1)) {
-            ok = false;
-            break;
-          }
-          if (s == sb && nb > 0 && !wait(FOLD_DONE, (nb - 1) & 1)) {
+      }
+      ptx::mma_commit_w(bar(S_FULL + x));
+    };
+    bool ok = wait_u(V_FULL, 0);
+    BlockIter it(&L, b, j0, j1);
+    Block blk;
+    int s = 0, nb = 0;
+    bool dv_started = false;
+    while (ok && it.next(blk)) {
+      const int nsteps = n_steps_of(blk);
+      if (!wait_u(K_READY, nb & 1)) break;
+      ptx::tc_fence_after();
+      const int sb = s;
+      // scores of the block's first step
+      if (!wait_u(Q_READY + (s & 1), (s >> 1) & 1)) break;
+      ptx::tc_fence_after();
+      issue_scores(s);
+      for (; s < sb + nsteps; ++s) {
+        const int x = s & 1;
+        if (s + 1 < sb + nsteps) {
+          const int y = (s + 1) & 1;
+          if (!wait_u(Q_READY + y, ((s + 1) >> 1) & 1)) {
             ok = false;
             break;
           }
           ptx::tc_fence_after();
-          const uint32_t qb = sbase + Q + 16384u * (uint32_t)x, ob = sbase + DO + 16384u * (uint32_t)x;
-          const uint32_t cb = tmem + C_BUF + 128u * (uint32_t)x;
+          issue_scores(s + 1);
+        }
+        if (!wait_u(P_READY + x, (s >> 1) & 1)) {
+          ok = false;
+          break;
+        }
+        if (s == sb && nb > 0 && !wait_u(FOLD_DONE, (nb - 1) & 1)) {
+          ok = false;
+          break;
+        }
+        ptx::tc_fence_after();
+        const uint32_t qb = sbase + Q + 16384u * (uint32_t)x, ob = sbase + DO + 16384u * (uint32_t)x;
+        const uint32_t cb = tmem + C_BUF + 128u * (uint32_t)x;
 #pragma unroll
-          for (int kk = 0; kk < BQ / 16; ++kk) {
-            ptx::mma_ts(tmem + C_DV, cb + 8u * (uint32_t)kk, ptx::sdesc_sw128(ob + 2048u * (uint32_t)kk, 8192, 1024),
-                        idesc_acc, (dv_started || kk > 0) ? 1u : 0u);
-            ptx::mma_ts(tmem + C_DKR, cb + 64u + 8u * (uint32_t)kk,
+        for (int kk = 0; kk < BQ / 16; ++kk) {
+          ptx::mma_ts_w(tmem + C_DV, cb + 8u * (uint32_t)kk,
+                        ptx::sdesc_sw128(ob + 2048u * (uint32_t)kk, 8192, 1024), idesc_acc,
+                        (dv_started || kk > 0) ? 1u : 0u);
+          ptx::mma_ts_w(tmem + C_DKR, cb + 64u + 8u * (uint32_t)kk,
                         ptx::sdesc_sw128(qb + 2048u * (uint32_t)kk, 8192, 1024), idesc_acc,
                         (s > sb || kk > 0) ? 1u : 0u);
-          }
-          ptx::mma_commit(bar(Q_EMPTY + x));
-          dv_started = true;
         }
-        if (!ok) break;
-        ptx::mma_commit(bar(BLK_DONE));
-        ++nb;
+        ptx::mma_commit_w(bar(Q_EMPTY + x));
+        dv_started = true;
       }
-      ptx::mma_commit(bar(FINAL));
-      ptx::mbar_wait(bar(FINAL), 0, kWait);
+      if (!ok) break;
+      ptx::mma_commit_w(bar(BLK_DONE));
+      ++nb;
     }
+    ptx::mma_commit_w(bar(FINAL));
+    ptx::mbar_wait(bar(FINAL), 0, kWait);
   } else {
     // ------------------------------------------------------------ rotation (warps 10-13)
     const int rt = tid - 320;  // 0..127
@@ -1510,7 +1512,8 @@ bool sm100_bwd_supported(int dtype, int head_dim) { return dtype == AI_DTYPE_BF1
 
 int sm100_kv_tile_rows() { return sm100bwd::kv::BN; }
 
-int sm100_bwd(const AiAttnBwdArgs& a, float* delta, void* rot, cudaStream_t st, cudaError_t* cuda_err) {
+int sm100_bwd(const AiAttnBwdArgs& a, float* delta, void* rot, bool rot_ready, cudaStream_t st,
+              cudaError_t* cuda_err) {
   using namespace sm100bwd;
   const AiAttnFwdArgs& f = a.fwd;
   if (!strides_ok(f.q) || !strides_ok(f.k) || !strides_ok(f.v) || !strides_ok(a.dout) || !strides_ok(a.dq) ||
@@ -1522,7 +1525,7 @@ int sm100_bwd(const AiAttnBwdArgs& a, float* delta, void* rot, cudaStream_t st, 
   const bool pre = rot != nullptr;
   if (pre && !sm100_rotated_views(f, rot, &qr, &kr)) return AI_ERR_ALIGN;
   cudaError_t e = bwd_delta(a, delta, st);
-  if (e == cudaSuccess && pre) e = prerot(f, rot, st);
+  if (e == cudaSuccess && pre && !rot_ready) e = prerot(f, rot, st);
   if (e == cudaSuccess && f.layout.n_fwd_items > 0) {
     CUtensorMap tk, tv, tqr, tdo, tkr;
     if (!sm100_make_map(&tk, f.k, f.batch, f.num_kv_heads, f.seq_len, dq::BN) ||

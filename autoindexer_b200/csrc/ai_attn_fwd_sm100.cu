@@ -363,8 +363,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 // Softmax t reads S_t, writes P_t (bf16, two per column) over the first 64
 // columns of S_t, and the PV MMA takes P_t straight from TMEM.  MMA order
 // per key tile j: PV0(j), S0(j+1), PV1(j), S1(j+1): while one softmax group
-// works the tensor core runs the other group's MMAs.  S_t(j+1) is issued
-// only once PV_t(j) has completed, since it overwrites P_t.
+// works the tensor core runs the other group's MMAs.  S_t(j+1) overwrites
+// P_t right after PV_t(j) read it: tcgen05.mma ops issued by one thread
+// execute in issue order, so no wait on PV_t(j) is needed, and the S_t(j+1)
+// commit (which tracks every earlier MMA) also tells softmax t that PV_t(j)
+// is done with O_t before it may rescale O_t.
+// The MMA warp runs converged: descriptors are computed by all 32 lanes (so
+// they stay warp-uniform) and elect.sync picks the lane that issues.
 // ---------------------------------------------------------------------------
 namespace ws {
 constexpr int kThreads = 448;
@@ -626,60 +631,57 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
     }
   } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc_qk = ptx::idesc_bf16_f32(BM, BN, false, false);
-      constexpr uint32_t idesc_pv = ptx::idesc_bf16_f32(BM, D, false, true);
-      auto issue_s = [&](int t, int slot) {
-        const uint32_t qt = sbase + (t ? Q1 : Q0), kt = sbase + KB + (uint32_t)slot * kTile;
+    // The whole warp runs this loop (descriptors stay warp-uniform); one
+    // elected lane issues each MMA and commit.  Lane 0's wait result decides.
+    auto wait_u = [&](int i, uint32_t parity) -> bool { return __shfl_sync(0xffffffffu, wait(i, parity), 0); };
+    constexpr uint32_t idesc_qk = ptx::idesc_bf16_f32(BM, BN, false, false);
+    constexpr uint32_t idesc_pv = ptx::idesc_bf16_f32(BM, D, false, true);
+    auto issue_s = [&](int t, int slot) {
+      const uint32_t qt = sbase + (t ? Q1 : Q0), kt = sbase + KB + (uint32_t)slot * kTile;
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (uint32_t)(kk >> 2) * kHalf + (uint32_t)(kk & 3) * 32u;
-          ptx::mma_ss(tmem + (t ? C_S1 : C_S0), ptx::sdesc_sw128(qt + off, 16, 1024),
+      for (int kk = 0; kk < D / 16; ++kk) {
+        const uint32_t off = (uint32_t)(kk >> 2) * kHalf + (uint32_t)(kk & 3) * 32u;
+        ptx::mma_ss_w(tmem + (t ? C_S1 : C_S0), ptx::sdesc_sw128(qt + off, 16, 1024),
                       ptx::sdesc_sw128(kt + off, 16, 1024), idesc_qk, kk > 0);
-        }
-        ptx::mma_commit(bar(S_FULL + t));
-      };
-      auto issue_pv = [&](int t, int slot, bool first) {
-        const uint32_t vt = sbase + VB + (uint32_t)slot * kTile;
+      }
+      ptx::mma_commit_w(bar(S_FULL + t));
+    };
+    auto issue_pv = [&](int t, int slot, bool first) {
+      const uint32_t vt = sbase + VB + (uint32_t)slot * kTile;
 #pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk) {
-          ptx::mma_ts(tmem + (t ? C_O1 : C_O0), tmem + (t ? C_S1 : C_S0) + 8u * (uint32_t)kk,
+      for (int kk = 0; kk < BN / 16; ++kk) {
+        ptx::mma_ts_w(tmem + (t ? C_O1 : C_O0), tmem + (t ? C_S1 : C_S0) + 8u * (uint32_t)kk,
                       ptx::sdesc_sw128(vt + (uint32_t)kk * 2048u, kHalf, 1024), idesc_pv,
                       (!first || kk > 0) ? 1u : 0u);
-        }
-        ptx::mma_commit(bar(O_DONE + t));
-      };
-      bool ok = wait(Q_READY, 0);
-      if (ok && n > 0 && wait(K_READY, 0)) {
-        ptx::tc_fence_after();
-        issue_s(0, 0);
-        issue_s(1, 0);
-        for (int j = 0; j < n; ++j) {
-          const int slot = j & 1, nslot = (j + 1) & 1;
-          const bool more = j + 1 < n;
-          if (!wait(P_READY, j & 1)) break;
-          ptx::tc_fence_after();
-          issue_pv(0, slot, j == 0);
-          if (more) {
-            if (!wait(K_READY + nslot, ((j + 1) >> 1) & 1) || !wait(O_DONE, j & 1)) break;
-            ptx::tc_fence_after();
-            issue_s(0, nslot);
-          }
-          if (!wait(P_READY + 1, j & 1)) break;
-          ptx::tc_fence_after();
-          issue_pv(1, slot, j == 0);
-          ptx::mma_commit(bar(KV_EMPTY + slot));
-          if (more) {
-            if (!wait(O_DONE + 1, j & 1)) break;
-            ptx::tc_fence_after();
-            issue_s(1, nslot);
-          }
-        }
       }
-      // Drain: every MMA issued so far has completed before TMEM is released.
-      ptx::mma_commit(bar(FINAL));
-      ptx::mbar_wait(bar(FINAL), 0, kWait);
+      ptx::mma_commit_w(bar(O_DONE + t));
+    };
+    bool ok = wait_u(Q_READY, 0);
+    if (ok && n > 0 && wait_u(K_READY, 0)) {
+      ptx::tc_fence_after();
+      issue_s(0, 0);
+      issue_s(1, 0);
+      for (int j = 0; j < n; ++j) {
+        const int slot = j & 1, nslot = (j + 1) & 1;
+        const bool more = j + 1 < n;
+        if (!wait_u(P_READY, j & 1)) break;
+        ptx::tc_fence_after();
+        issue_pv(0, slot, j == 0);
+        if (more) {
+          if (!wait_u(K_READY + nslot, ((j + 1) >> 1) & 1)) break;
+          ptx::tc_fence_after();
+          issue_s(0, nslot);
+        }
+        if (!wait_u(P_READY + 1, j & 1)) break;
+        ptx::tc_fence_after();
+        issue_pv(1, slot, j == 0);
+        ptx::mma_commit_w(bar(KV_EMPTY + slot));
+        if (more) issue_s(1, nslot);
+      }
     }
+    // Drain: every MMA issued so far has completed before TMEM is released.
+    ptx::mma_commit_w(bar(FINAL));
+    ptx::mbar_wait(bar(FINAL), 0, kWait);
   } else {
     // ------------------------------------------------------------ K rotation (warps 10-13)
     // Thread = key row of the tile.  The key's position word and its fp16
@@ -778,43 +780,44 @@ int sm100_fwd_tile_rows() { return sm100::BM; }
 int sm100_fwd(const AiAttnFwdArgs& a, cudaStream_t st, cudaError_t* cuda_err) {
   using namespace sm100;
   if (!strides_ok(a.q) || !strides_ok(a.k) || !strides_ok(a.v) || !strides_ok(a.out)) return AI_ERR_STRIDE;
-  if (a.layout.n_fwd_items == 0) return AI_OK;
-  CUtensorMap tm_k, tm_v;
-  if (!sm100_make_map(&tm_k, a.k, a.batch, a.num_kv_heads, a.seq_len, BN)) return AI_ERR_TMA;
-  if (!sm100_make_map(&tm_v, a.v, a.batch, a.num_kv_heads, a.seq_len, BN)) return AI_ERR_TMA;
-  // Items of blocks with abs keys (and every item when a GQA group has an odd
-  // number of query heads) run on the one-head kernel; the rest run two heads
-  // per CTA on the warp-specialised kernel.
-  const int G = a.num_q_heads / a.num_kv_heads;
-  const int n_single = (G % 2 == 0) ? a.layout.n_fwd_abs_items : a.layout.n_fwd_items;
-  const int n_pair = a.layout.n_fwd_items - n_single;
   cudaError_t e = cudaSuccess;
-  if (n_single > 0) {
-    e = cudaFuncSetAttribute(fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
-    if (e == cudaSuccess) {
-      fwd_kernel<<<dim3(n_single, a.num_q_heads), kThreads, kSmemBytes, st>>>(a, tm_k, tm_v);
-      e = cudaGetLastError();
-    }
+  // With enough workspace, Q and K are rotated once (HBM-bound) and the
+  // warp-specialised kernel reads the rotated copies.  They are written
+  // whenever the workspace holds them, so that the backward can reuse them.
+  const bool pre = a.workspace && a.workspace_bytes >= prerot_bytes(a, nullptr);
+  AiTensor4 qr{}, kr{};
+  if (pre) {
+    if (!sm100_rotated_views(a, a.workspace, &qr, &kr)) return AI_ERR_ALIGN;
+    e = prerot(a, a.workspace, st);
   }
-  if (e == cudaSuccess && n_pair > 0) {
-    // With enough workspace, rotate Q and K once (HBM-bound) and let the
-    // warp-specialised kernel read the rotated copies.
-    const bool pre = a.workspace && a.workspace_bytes >= prerot_bytes(a, nullptr);
-    CUtensorMap tm_qr = tm_k, tm_kr = tm_k;
-    if (pre) {
-      AiTensor4 qr, kr;
-      if (!sm100_rotated_views(a, a.workspace, &qr, &kr)) return AI_ERR_ALIGN;
-      if (!sm100_make_map(&tm_qr, qr, a.batch, a.num_q_heads, a.seq_len, BM) ||
-          !sm100_make_map(&tm_kr, kr, a.batch, a.num_kv_heads, a.seq_len, BN))
-        return AI_ERR_TMA;
-      e = prerot(a, a.workspace, st);
+  if (e == cudaSuccess && a.layout.n_fwd_items > 0) {
+    CUtensorMap tm_k, tm_v;
+    if (!sm100_make_map(&tm_k, a.k, a.batch, a.num_kv_heads, a.seq_len, BN)) return AI_ERR_TMA;
+    if (!sm100_make_map(&tm_v, a.v, a.batch, a.num_kv_heads, a.seq_len, BN)) return AI_ERR_TMA;
+    // Items of blocks with abs keys (and every item when a GQA group has an
+    // odd number of query heads) run on the one-head kernel; the rest run two
+    // heads per CTA on the warp-specialised kernel.
+    const int G = a.num_q_heads / a.num_kv_heads;
+    const int n_single = (G % 2 == 0) ? a.layout.n_fwd_abs_items : a.layout.n_fwd_items;
+    const int n_pair = a.layout.n_fwd_items - n_single;
+    if (n_single > 0) {
+      e = cudaFuncSetAttribute(fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+      if (e == cudaSuccess) {
+        fwd_kernel<<<dim3(n_single, a.num_q_heads), kThreads, kSmemBytes, st>>>(a, tm_k, tm_v);
+        e = cudaGetLastError();
+      }
     }
-    if (e == cudaSuccess)
+    if (e == cudaSuccess && n_pair > 0) {
+      CUtensorMap tm_qr = tm_k, tm_kr = tm_k;
+      if (pre && (!sm100_make_map(&tm_qr, qr, a.batch, a.num_q_heads, a.seq_len, BM) ||
+                  !sm100_make_map(&tm_kr, kr, a.batch, a.num_kv_heads, a.seq_len, BN)))
+        return AI_ERR_TMA;
       e = cudaFuncSetAttribute(fwd_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ws::kSmem);
-    if (e == cudaSuccess) {
-      fwd_ws_kernel<<<dim3(n_pair, a.num_q_heads / 2), ws::kThreads, ws::kSmem, st>>>(a, tm_k, tm_v, tm_qr, tm_kr,
-                                                                                      pre ? 1 : 0);
-      e = cudaGetLastError();
+      if (e == cudaSuccess) {
+        fwd_ws_kernel<<<dim3(n_pair, a.num_q_heads / 2), ws::kThreads, ws::kSmem, st>>>(a, tm_k, tm_v, tm_qr, tm_kr,
+                                                                                        pre ? 1 : 0);
+        e = cudaGetLastError();
+      }
     }
   }
   if (cuda_err) *cuda_err = e;

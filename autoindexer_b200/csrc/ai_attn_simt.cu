@@ -348,6 +348,73 @@ __global__ void delta_kernel(const AiAttnBwdArgs a, float* delta) {
   if (lane == 0) delta[w] = s;
 }
 
+// Dot product of two 16-byte chunks (8 bf16 / 8 fp16 / 4 fp32 values).
+template <typename T>
+__device__ __forceinline__ float dot16(const uint4& x, const uint4& y);
+template <>
+__device__ __forceinline__ float dot16<__nv_bfloat16>(const uint4& x, const uint4& y) {
+  const __nv_bfloat162* a = reinterpret_cast<const __nv_bfloat162*>(&x);
+  const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&y);
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 u = __bfloat1622float2(a[i]), v = __bfloat1622float2(b[i]);
+    s = fmaf(u.x, v.x, fmaf(u.y, v.y, s));
+  }
+  return s;
+}
+template <>
+__device__ __forceinline__ float dot16<__half>(const uint4& x, const uint4& y) {
+  const __half2* a = reinterpret_cast<const __half2*>(&x);
+  const __half2* b = reinterpret_cast<const __half2*>(&y);
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 u = __half22float2(a[i]), v = __half22float2(b[i]);
+    s = fmaf(u.x, v.x, fmaf(u.y, v.y, s));
+  }
+  return s;
+}
+template <>
+__device__ __forceinline__ float dot16<float>(const uint4& x, const uint4& y) {
+  return fmaf(__uint_as_float(x.x), __uint_as_float(y.x),
+              fmaf(__uint_as_float(x.y), __uint_as_float(y.y),
+                   fmaf(__uint_as_float(x.z), __uint_as_float(y.z), __uint_as_float(x.w) * __uint_as_float(y.w))));
+}
+
+// delta as above with 16-byte loads: kTpr = D * sizeof(T) / 16 consecutive
+// lanes share a row (one chunk each) and reduce by shuffles.  Requires
+// 16-byte aligned rows (checked on the host).
+template <typename T, int D>
+__global__ void __launch_bounds__(256) delta_vec_kernel(const AiAttnBwdArgs a, float* delta) {
+  constexpr int kTpr = D * (int)sizeof(T) / 16, kPer = 16 / (int)sizeof(T);
+  static_assert(kTpr >= 1 && kTpr <= 32 && (32 % kTpr) == 0, "row chunking");
+  const AiAttnFwdArgs& f = a.fwd;
+  const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t w = g / kTpr;
+  const int c = (int)(g % kTpr);
+  const int64_t total = (int64_t)f.batch * f.num_q_heads * f.seq_len;
+  float s = 0.f;
+  if (w < total) {
+    const int i = (int)(w % f.seq_len);
+    const int h = (int)((w / f.seq_len) % f.num_q_heads);
+    const int b = (int)(w / ((int64_t)f.seq_len * f.num_q_heads));
+    const T* O = static_cast<const T*>(f.out.ptr) + b * f.out.stride_b + h * f.out.stride_h + (int64_t)i * f.out.stride_t;
+    const T* dO =
+        static_cast<const T*>(a.dout.ptr) + b * a.dout.stride_b + h * a.dout.stride_h + (int64_t)i * a.dout.stride_t;
+    s = dot16<T>(__ldg(reinterpret_cast<const uint4*>(O + kPer * c)), __ldg(reinterpret_cast<const uint4*>(dO + kPer * c)));
+  }
+#pragma unroll
+  for (int o = kTpr / 2; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (w < total && c == 0) delta[w] = s;
+}
+
+template <typename T>
+static bool rows16(const AiTensor4& t) {
+  constexpr int64_t e = 16 / (int64_t)sizeof(T);
+  return ((uintptr_t)t.ptr % 16 == 0) && t.stride_b % e == 0 && t.stride_h % e == 0 && t.stride_t % e == 0;
+}
+
 // P and dS (gradient of the unscaled logits) of the thread's 2x4 pairs.
 template <int D>
 __device__ void tile_p_ds(float (&p)[2][4], float (&ds)[2][4], const float* sQr, const float* sQ,
@@ -640,12 +707,24 @@ static cudaError_t fwd_impl(const AiAttnFwdArgs& a, cudaStream_t st) {
   return cudaGetLastError();
 }
 
+// delta for every (b, h, i) row: 16-byte loads when both row layouts allow.
+template <typename T, int D>
+static cudaError_t launch_delta(const AiAttnBwdArgs& a, float* delta, cudaStream_t st) {
+  const AiAttnFwdArgs& f = a.fwd;
+  const int64_t rows = (int64_t)f.batch * f.num_q_heads * f.seq_len;
+  if (rows16<T>(f.out) && rows16<T>(a.dout)) {
+    constexpr int kTpr = D * (int)sizeof(T) / 16;
+    delta_vec_kernel<T, D><<<(unsigned)((rows * kTpr + 255) / 256), 256, 0, st>>>(a, delta);
+  } else {
+    delta_kernel<T, D><<<(unsigned)((rows * 32 + 255) / 256), 256, 0, st>>>(a, delta);
+  }
+  return cudaGetLastError();
+}
+
 template <typename T, int D>
 static cudaError_t bwd_impl(const AiAttnBwdArgs& a, float* delta, cudaStream_t st) {
   const AiAttnFwdArgs& f = a.fwd;
-  const int64_t rows = (int64_t)f.batch * f.num_q_heads * f.seq_len;
-  delta_kernel<T, D><<<(unsigned)((rows * 32 + 255) / 256), 256, 0, st>>>(a, delta);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_delta<T, D>(a, delta, st);
   if (e != cudaSuccess) return e;
   if (f.layout.n_fwd_items > 0) {
     const size_t smem = dq_smem_bytes<D>();
@@ -665,10 +744,7 @@ static cudaError_t bwd_impl(const AiAttnBwdArgs& a, float* delta, cudaStream_t s
 
 template <typename T, int D>
 static cudaError_t delta_impl(const AiAttnBwdArgs& a, float* delta, cudaStream_t st) {
-  const AiAttnFwdArgs& f = a.fwd;
-  const int64_t rows = (int64_t)f.batch * f.num_q_heads * f.seq_len;
-  delta_kernel<T, D><<<(unsigned)((rows * 32 + 255) / 256), 256, 0, st>>>(a, delta);
-  return cudaGetLastError();
+  return launch_delta<T, D>(a, delta, st);
 }
 
 template <typename T, int D>

@@ -62,6 +62,14 @@ size_t delta_bytes(const AiAttnFwdArgs& f) {
 
 int launch_status(cudaError_t e) { return e == cudaSuccess ? AI_OK : AI_ERR_LAUNCH; }
 
+// The caller vouches (fwd_rotated) that fwd.workspace still holds the
+// forward's rotated copies; they are used when the workspace can hold them
+// and is aligned (otherwise the backward rotates into its own workspace).
+bool fwd_copies(const AiAttnBwdArgs& a) {
+  return a.fwd_rotated == 1 && a.fwd.workspace && ((uintptr_t)a.fwd.workspace % 256) == 0 &&
+         a.fwd.workspace_bytes >= ai::prerot_bytes(a.fwd, nullptr);
+}
+
 }  // namespace
 
 extern "C" {
@@ -103,7 +111,8 @@ int ai_attn_bwd_workspace(const AiAttnBwdArgs* a, size_t* bytes) {
   int rc = validate_fwd(&a->fwd);
   if (rc != AI_OK) return rc;
   *bytes = delta_bytes(a->fwd);
-  if (ai::sm100_bwd_supported(a->fwd.dtype, a->fwd.head_dim)) *bytes += ai::prerot_bytes(a->fwd, nullptr);
+  if (ai::sm100_bwd_supported(a->fwd.dtype, a->fwd.head_dim) && !fwd_copies(*a))
+    *bytes += ai::prerot_bytes(a->fwd, nullptr);
   return AI_OK;
 }
 
@@ -118,11 +127,13 @@ int ai_attn_bwd(const AiAttnBwdArgs* a, void* stream) {
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   float* delta = static_cast<float*>(a->workspace);
   if (ai::sm100_bwd_supported(a->fwd.dtype, a->fwd.head_dim)) {
-    // Workspace = delta, then (if it fits) the once-rotated Q and K copies.
+    // Rotated Q and K copies: the forward's (fwd_rotated), else rotated into
+    // the workspace after delta if it fits, else none (in-kernel rotation).
+    if (fwd_copies(*a)) return ai::sm100_bwd(*a, delta, a->fwd.workspace, true, st, nullptr);
     const size_t db = delta_bytes(a->fwd);
     void* rot = nullptr;
     if (a->workspace_bytes >= db + ai::prerot_bytes(a->fwd, nullptr)) rot = static_cast<char*>(a->workspace) + db;
-    return ai::sm100_bwd(*a, delta, rot, st, nullptr);
+    return ai::sm100_bwd(*a, delta, rot, false, st, nullptr);
   }
   return launch_status(ai::simt_bwd(*a, delta, st));
 }

@@ -30,8 +30,10 @@ int sm100_fwd(const AiAttnFwdArgs& a, cudaStream_t st, cudaError_t* cuda_err);
 bool sm100_bwd_supported(int dtype, int head_dim);
 int sm100_kv_tile_rows();
 // `rot`: scratch for the once-rotated Q/K copies (prerot_bytes), or nullptr to
-// rotate every tile in shared memory.
-int sm100_bwd(const AiAttnBwdArgs& a, float* delta, void* rot, cudaStream_t st, cudaError_t* cuda_err);
+// rotate every tile in shared memory; `rot_ready`: `rot` already holds them
+// (written by the forward), so they are not rotated again.
+int sm100_bwd(const AiAttnBwdArgs& a, float* delta, void* rot, bool rot_ready, cudaStream_t st,
+              cudaError_t* cuda_err);
 // TMA map over a (B, H, T, 128) bf16 tensor, box 64 x box_rows, 128-byte swizzle.
 bool sm100_make_map(CUtensorMap* map, const AiTensor4& t, int B, int H, int T, int box_rows);
 

@@ -125,6 +125,21 @@ def peaks():
         return 1590.0, 1400.0, "fallback"
 
 
+def our_launches_per_step(layout) -> int:
+    """Kernels of ours per step (forward, then backward reusing the forward's
+    rotated Q/K copies): Q/K rotation, the one-head kernel for abs-key items
+    (if any), the two-head kernel, the row fill; delta, the dQ kernels, the
+    dK/dV kernels, the row fill."""
+    G = HQ // HKV
+    n_fwd, n_kv = int(layout.fwd_items.shape[0]), int(layout.kv_items.shape[0])
+    n_single = layout.n_fwd_abs_items if G % 2 == 0 else n_fwd
+    n_pair = n_fwd - n_single
+    n_kv_abs, n_kv_plain = layout.n_kv_abs_items, n_kv - layout.n_kv_abs_items
+    fwd = 1 + int(n_single > 0) + int(n_pair > 0) + 1
+    bwd = 1 + int(n_single > 0) + int(n_pair > 0) + int(n_kv_abs > 0) + int(n_kv_plain > 0) + 1
+    return fwd + bwd
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -153,8 +168,8 @@ def run_ours(args):
     stream = torch.cuda.current_stream(dev)
 
     def step():
-        out, lse = attn_fwd(q, k, v, layout, scale)
-        return attn_bwd(q, k, v, out, lse, dout, layout, scale)
+        out, lse, ws = attn_fwd(q, k, v, layout, scale, keep_workspace=True)
+        return attn_bwd(q, k, v, out, lse, dout, layout, scale, fwd_workspace=ws)
 
     for _ in range(args.warmup):
         step()
@@ -172,9 +187,9 @@ def run_ours(args):
             flush.fill_(float(i))
             e0, e1, e2 = ev[i]
             e0.record(stream)
-            out, lse = attn_fwd(q, k, v, layout, scale)
+            out, lse, ws = attn_fwd(q, k, v, layout, scale, keep_workspace=True)
             e1.record(stream)
-            attn_bwd(q, k, v, out, lse, dout, layout, scale)
+            attn_bwd(q, k, v, out, lse, dout, layout, scale, fwd_workspace=ws)
             e2.record(stream)
         torch.cuda.synchronize(dev)
     if world > 1:
@@ -233,7 +248,7 @@ def run_ours(args):
     dom_flops = flops_bwd if dom_is_bwd else flops_fwd
     dom_t = (t_bwd if dom_is_bwd else t_fwd) / args.steps
     achieved = dom_flops / dom_t / 1e12
-    launches_per_step = 6  # fwd: sm100 fwd + row fill; bwd: delta, dQ, dK/dV, row fill
+    launches_per_step = our_launches_per_step(layout)
     tokens = world * B * T * args.steps / t_max
 
     line = {

@@ -43,7 +43,7 @@
 extern "C" {
 #endif
 
-#define AI_ATTN_ABI_VERSION 3
+#define AI_ATTN_ABI_VERSION 4
 
 typedef enum AiDtype {
   AI_DTYPE_BF16 = 0,
@@ -148,7 +148,12 @@ typedef struct AiAttnBwdArgs {
   AiTensor4 dv;           /* (B, Hkv, T, D) */
   void* workspace;        /* device scratch, 256-B aligned: at least B*Hq*T floats (rounded up to
                              256 B); ai_attn_bwd_workspace bytes also hold the rotated Q/K copies */
-  size_t workspace_bytes; /* (fwd.workspace is not used by ai_attn_bwd) */
+  size_t workspace_bytes;
+  int32_t fwd_rotated;    /* 1: fwd.workspace still holds the once-rotated Q/K copies that ai_attn_fwd
+                             wrote for these q, k and layout (fwd.workspace_bytes >=
+                             ai_attn_fwd_workspace); the backward reads them instead of rotating
+                             again, and its own workspace needs only the B*Hq*T floats.
+                             0: fwd.workspace is ignored. */
 } AiAttnBwdArgs;
 
 /* ABI version this library was built with (AI_ATTN_ABI_VERSION). */

@@ -85,9 +85,11 @@ def _edit_chain_case(name, B, Hq, Hkv, D, seed):
     return lay, q, k, v, dout, HFRope(inv), O.make_rope(inv)
 
 
-@pytest.mark.parametrize("name", ["op0_d32", "op5_d32", "op9_d32"])
-def test_bf16_edit_chains_match_oracle(name, cuda_device):
-    lay, q, k, v, dout, mod, rope = _edit_chain_case(name, 2, 4, 2, 128, 11)
+@pytest.mark.parametrize("name,hq,hkv", [("op0_d32", 4, 2), ("op5_d32", 4, 2), ("op9_d32", 4, 2), ("op5_d32", 8, 2),
+                                         ("op9_d32", 4, 1)])
+def test_bf16_edit_chains_match_oracle(name, hq, hkv, cuda_device):
+    """GQA groups of 2 (one CTA per head pair) and 4 (CTA pairs, 2-SM MMAs)."""
+    lay, q, k, v, dout, mod, rope = _edit_chain_case(name, 2, hq, hkv, 128, 11)
     q, k, v, dout = bf16_round(q, k, v, dout)
     got = run_kernels(lay, q, k, v, dout, mod, torch.bfloat16, cuda_device)
     out, lse = O.attn_forward(q, k, v, lay, rope)
@@ -186,7 +188,7 @@ def test_bf16_full_size_prefix_matches_oracle(cuda_device):
     check_bf16(sl, want, "full-size prefix")
 
 
-@pytest.mark.parametrize("layout_kind", ["documents", "edit_chain"])
+@pytest.mark.parametrize("layout_kind", ["documents", "edit_chain", "edit_chain_g4"])
 def test_bf16_rotated_copies_match_in_kernel_rotation(layout_kind, cuda_device):
     """The fast path (Q and K rotated once into scratch, read by TMA) and the
     small-workspace path (every tile rotated in shared memory) agree."""
@@ -198,7 +200,8 @@ def test_bf16_rotated_copies_match_in_kernel_rotation(layout_kind, cuda_device):
         q, k, v = (rng.standard_normal(s) for s in ((B, Hq, T, D), (B, Hkv, T, D), (B, Hkv, T, D)))
         dout = rng.standard_normal((B, T, Hq, D))
     else:
-        lay, q, k, v, dout, mod, _ = _edit_chain_case("op2_d32", 2, 4, 2, 128, 13)
+        hq = 8 if layout_kind == "edit_chain_g4" else 4
+        lay, q, k, v, dout, mod, _ = _edit_chain_case("op2_d32", 2, hq, 2, 128, 13)
         B, Hq, T, D = q.shape
     tq, tk, tv, tdo = (torch.as_tensor(x).to(cuda_device, torch.bfloat16) for x in (q, k, v, dout))
     layout = compile_layout(lay, B, T, D, torch.bfloat16, mod.to(cuda_device), cuda_device)
@@ -211,6 +214,33 @@ def test_bf16_rotated_copies_match_in_kernel_rotation(layout_kind, cuda_device):
     assert read_status(cuda_device) == 0
     for name, a_, b_ in zip(("out", "lse", "dq", "dk", "dv"), *res):
         assert rel_l2(a_, b_) <= 1e-3, (name, rel_l2(a_, b_))
+
+
+@pytest.mark.parametrize("layout_kind", ["documents", "edit_chain"])
+def test_bf16_backward_reuses_forward_rotation(layout_kind, cuda_device):
+    """ai_attn_bwd with fwd_rotated = 1 (reading the rotated Q/K copies the
+    forward left in its workspace) gives bit-identical gradients to a backward
+    that rotates Q and K itself."""
+    if layout_kind == "documents":
+        B, T, Hq, Hkv, D = 2, 640, 8, 2, 128
+        rows, mod, _ = _sectioned_docs(B, T, D, 2, seed=41)
+        lay = rows
+        rng = np.random.default_rng(3)
+        q, k, v = (rng.standard_normal(s) for s in ((B, Hq, T, D), (B, Hkv, T, D), (B, Hkv, T, D)))
+        dout = rng.standard_normal((B, T, Hq, D))
+    else:
+        lay, q, k, v, dout, mod, _ = _edit_chain_case("op7_d32", 2, 4, 2, 128, 17)
+        B, Hq, T, D = q.shape
+    tq, tk, tv, tdo = (torch.as_tensor(x).to(cuda_device, torch.bfloat16) for x in (q, k, v, dout))
+    layout = compile_layout(lay, B, T, D, torch.bfloat16, mod.to(cuda_device), cuda_device)
+    out, lse, ws = attn_fwd(tq, tk, tv, layout, D ** -0.5, keep_workspace=True)
+    assert ws is not None
+    reuse = attn_bwd(tq, tk, tv, out, lse, tdo, layout, D ** -0.5, fwd_workspace=ws)
+    own = attn_bwd(tq, tk, tv, out, lse, tdo, layout, D ** -0.5)
+    torch.cuda.synchronize(cuda_device)
+    assert read_status(cuda_device) == 0
+    for name, a_, b_ in zip(("dq", "dk", "dv"), reuse, own):
+        assert torch.equal(a_, b_), name
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
