@@ -856,12 +856,18 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
         ptx::mbar_arrive(bar(Q_READY));
       }
     }
-    const float sl2 = f.scale * kLog2e;
+    const float sl2 = f.scale * kLog2e, scale = f.scale;
+    // Rows past q1 (another block's rows) get lse = +inf: their P is 0 with no
+    // per-element test on the unmasked path.
+    const float lse2r = i < q1 ? lse2 : CUDART_INF_F;
     int done = 0;
     for (int j = 0; j < n; ++j) {
       const int slot = j & 1, k0 = kv_lo + j * BN;
       if (!wait(S_FULL + t, j & 1)) break;
       ptx::tc_fence_after();
+      // Tiles wholly below the diagonal of a block without masked keys take
+      // the unmasked loop; the test sits outside the unrolled element loops
+      // (a per-element branch there doubles the kernel's time).
       const bool fast = !blk_masked && (k0 + BN <= kv_hi) && (k0 + BN - 1 <= q0);
       const uint32_t* info = s_info + slot * BN;
       uint32_t pk[32];
@@ -871,18 +877,31 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
         ptx::tmem_ld32(tmem + lane_base + c_s + 32 * hf, rs);
         ptx::tmem_ld32(tmem + lane_base + c_s + 64 + 32 * hf, rp);
         ptx::tmem_wait_ld();
+        if (fast) {
 #pragma unroll
-        for (int x2 = 0; x2 < 16; ++x2) {
-          float ds[2];
+          for (int x2 = 0; x2 < 16; ++x2) {
+            float ds[2];
 #pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int cl = 2 * x2 + u, c = 32 * hf + cl;
-            bool ok = i < q1;
-            if (!fast) ok = ok && (info[c] & AI_KEY_ATTN) && (k0 + c <= i);
-            const float p = ok ? ptx::ex2(fmaf(__uint_as_float(rs[cl]), sl2, -lse2)) : 0.f;
-            ds[u] = p * (__uint_as_float(rp[cl]) - dl) * f.scale;
+            for (int u = 0; u < 2; ++u) {
+              const int cl = 2 * x2 + u;
+              const float p = ptx::ex2(fmaf(__uint_as_float(rs[cl]), sl2, -lse2r));
+              ds[u] = p * (__uint_as_float(rp[cl]) - dl) * scale;
+            }
+            pk[16 * hf + x2] = tile::pack2(ds[0], ds[1]);
           }
-          pk[16 * hf + x2] = tile::pack2(ds[0], ds[1]);
+        } else {
+#pragma unroll
+          for (int x2 = 0; x2 < 16; ++x2) {
+            float ds[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const int cl = 2 * x2 + u, c = 32 * hf + cl;
+              const bool ok = (info[c] & AI_KEY_ATTN) && (k0 + c <= i);
+              const float p = ptx::ex2(ok ? fmaf(__uint_as_float(rs[cl]), sl2, -lse2r) : -CUDART_INF_F);
+              ds[u] = p * (__uint_as_float(rp[cl]) - dl) * scale;
+            }
+            pk[16 * hf + x2] = tile::pack2(ds[0], ds[1]);
+          }
         }
       }
       ptx::tmem_st32(tmem + lane_base + c_s, pk);
@@ -1182,7 +1201,7 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
     // ------------------------------------------------------------ score groups
     const int t = warp / 4, lrow = tid % 128, j = j0 + lrow;
     const uint32_t lane_base = (uint32_t)((warp % 4) * 32) << 16;
-    const float sl2 = f.scale * kLog2e;
+    const float sl2 = f.scale * kLog2e, scale = f.scale;
     BlockIter it(&L, b, j0, j1);
     Block blk;
     int s = 0, nb = 0;
@@ -1206,6 +1225,9 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
         // lies wholly above the query rows, and every row is in the block when
         // the tile is full.
         const bool no_causal = j0 + BN - 1 <= q0, rows_full = q1 == q0 + BQ;
+        // The step-uniform test sits outside the unrolled element loops (a
+        // per-element branch there costs as much as the rest of the step).
+        const bool plain = no_causal && rows_full;
         uint32_t pk[32], dk[32];
 #pragma unroll
         for (int hf = 0; hf < 2; ++hf) {
@@ -1213,20 +1235,33 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
           ptx::tmem_ld32(cb + 32 * hf, rs);
           ptx::tmem_ld32(cb + 64 + 32 * hf, rp);
           ptx::tmem_wait_ld();
+          if (plain) {
 #pragma unroll
-          for (int x2 = 0; x2 < 16; ++x2) {
-            float p[2], ds[2];
+            for (int x2 = 0; x2 < 16; ++x2) {
+              float p[2], ds[2];
 #pragma unroll
-            for (int u = 0; u < 2; ++u) {
-              const int cl = 2 * x2 + u, c = 32 * hf + cl;  // query row q0 + c
-              bool ok = key_ok;
-              if (!no_causal) ok = ok && (j <= q0 + c);
-              if (!rows_full) ok = ok && (q0 + c < q1);
-              p[u] = ok ? ptx::ex2(fmaf(__uint_as_float(rs[cl]), sl2, -lse2[c])) : 0.f;
-              ds[u] = p[u] * (__uint_as_float(rp[cl]) - dlt[c]) * f.scale;
+              for (int u = 0; u < 2; ++u) {
+                const int cl = 2 * x2 + u, c = 32 * hf + cl;  // query row q0 + c
+                p[u] = ptx::ex2(key_ok ? fmaf(__uint_as_float(rs[cl]), sl2, -lse2[c]) : -CUDART_INF_F);
+                ds[u] = p[u] * (__uint_as_float(rp[cl]) - dlt[c]) * scale;
+              }
+              pk[16 * hf + x2] = tile::pack2(p[0], p[1]);
+              dk[16 * hf + x2] = tile::pack2(ds[0], ds[1]);
             }
-            pk[16 * hf + x2] = tile::pack2(p[0], p[1]);
-            dk[16 * hf + x2] = tile::pack2(ds[0], ds[1]);
+          } else {
+#pragma unroll
+            for (int x2 = 0; x2 < 16; ++x2) {
+              float p[2], ds[2];
+#pragma unroll
+              for (int u = 0; u < 2; ++u) {
+                const int cl = 2 * x2 + u, c = 32 * hf + cl;  // query row q0 + c
+                const bool ok = key_ok && (j <= q0 + c) && (q0 + c < q1);
+                p[u] = ptx::ex2(ok ? fmaf(__uint_as_float(rs[cl]), sl2, -lse2[c]) : -CUDART_INF_F);
+                ds[u] = p[u] * (__uint_as_float(rp[cl]) - dlt[c]) * scale;
+              }
+              pk[16 * hf + x2] = tile::pack2(p[0], p[1]);
+              dk[16 * hf + x2] = tile::pack2(ds[0], ds[1]);
+            }
           }
         }
         ptx::tmem_st32(cb, pk);
