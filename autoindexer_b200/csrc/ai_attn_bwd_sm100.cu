@@ -1106,19 +1106,23 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
 // ===========================================================================
 namespace kvw {
 constexpr int BN = 128, BQ = 64, kThreads = 448;
+// Q / dO ring depth: the load of step s + kQS starts when step s's dV / dK
+// MMAs are done, so with 3 stages it has about two steps of MMA time to land.
+constexpr int kQS = 3;
 constexpr uint32_t K = 0;                   // 128 keys x 128 d (rotated per block)
 constexpr uint32_t V = 32768;
-constexpr uint32_t Q = 65536;               // ring of 2 x (64 rows x 128 d), rotated in place
-constexpr uint32_t DO = Q + 2 * 16384;      // ring of 2 x (64 rows x 128 d)
-constexpr uint32_t DK = DO + 2 * 16384;     // fp32 [128 d][128 keys]
-constexpr uint32_t STATS = DK + 65536;      // [2 slots][lse2 64 | delta 64] fp32
-constexpr uint32_t BARS = STATS + 2 * 2 * 4 * BQ;
-enum Bar { V_FULL = 0, K_FULL, K_READY, BLK_DONE, FOLD_DONE, Q_FULL = 5, Q_READY = 7, Q_EMPTY = 9, S_FULL = 11,
-           P_READY = 13, FINAL = 15, N_BARS = 16 };
+constexpr uint32_t Q = 65536;               // ring of kQS x (64 rows x 128 d), rotated in place
+constexpr uint32_t DO = Q + kQS * 16384;    // ring of kQS x (64 rows x 128 d)
+constexpr uint32_t DK = DO + kQS * 16384;   // fp32 [128 d][128 keys]
+constexpr uint32_t STATS = DK + 65536;      // [kQS slots][lse2 64 | delta 64] fp32
+constexpr uint32_t BARS = STATS + kQS * 2 * 4 * BQ;
+enum Bar { V_FULL = 0, K_FULL, K_READY, BLK_DONE, FOLD_DONE, Q_FULL = 5, Q_READY = Q_FULL + kQS,
+           Q_EMPTY = Q_READY + kQS, S_FULL = Q_EMPTY + kQS, P_READY = S_FULL + 2, FINAL = P_READY + 2, N_BARS };
 constexpr uint32_t TMEM_SLOT = BARS + 8 * N_BARS;
 constexpr uint32_t ABORT = TMEM_SLOT + 4;
 constexpr uint32_t TOTAL = ABORT + 4;
 constexpr size_t kSmem = TOTAL + 1024;
+static_assert(kSmem <= 227 * 1024, "shared memory budget");
 // TMEM columns: buffer x at 128 x: S^T [0,64) (P^T packed in [0,32)), dP^T [64,128) (dS^T packed in [64,96)).
 constexpr uint32_t C_BUF = 0, C_DV = 256, C_DKR = 384;
 constexpr long long kWait = 1000000000LL;
@@ -1167,7 +1171,7 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
   if (tid == 0) {
     for (int i = 0; i < N_BARS; ++i) {
       uint32_t count = 1;
-      if (i == K_READY || i == Q_READY || i == Q_READY + 1 || i == FOLD_DONE) count = 128;
+      if (i == K_READY || (i >= Q_READY && i < Q_READY + kQS) || i == FOLD_DONE) count = 128;
       if (i == P_READY || i == P_READY + 1) count = 128;
       ptx::mbar_init(bar(i), count);
     }
@@ -1215,10 +1219,10 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
       const int nsteps = n_steps_of(blk);
       for (int st = 0; st < nsteps; ++st, ++s) {
         if ((s & 1) != t) continue;
-        const int x = s & 1, q0 = qs + (st / G) * BQ, q1 = min(q0 + BQ, blk.e);
-        if (!wait(Q_READY + x, (s >> 1) & 1) || !wait(S_FULL + x, (s >> 1) & 1)) break;
+        const int x = s & 1, qslot = s % kQS, q0 = qs + (st / G) * BQ, q1 = min(q0 + BQ, blk.e);
+        if (!wait(Q_READY + qslot, (s / kQS) & 1) || !wait(S_FULL + x, (s >> 1) & 1)) break;
         ptx::tc_fence_after();
-        const float* lse2 = s_stats + x * 2 * BQ;
+        const float* lse2 = s_stats + qslot * 2 * BQ;
         const float* dlt = lse2 + BQ;
         const uint32_t cb = tmem + lane_base + C_BUF + 128u * (uint32_t)x;
         // Whole-step masks: causal (j <= i) holds for every pair when the tile
@@ -1351,17 +1355,17 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
         ptx::tma_load_4d(sbase + K + 16384, mk, bar(K_FULL), 64, j0, hk, b);
         const int qs = max(blk.s, j0), nsteps = n_steps_of(blk);
         for (int st = 0; st < nsteps; ++st, ++s) {
-          const int x = s & 1, q0 = qs + (st / G) * BQ, h = hk * G + st % G;
-          if (s >= 2 && !wait(Q_EMPTY + x, ((s >> 1) - 1) & 1)) {
+          const int qslot = s % kQS, q0 = qs + (st / G) * BQ, h = hk * G + st % G;
+          if (s >= kQS && !wait(Q_EMPTY + qslot, ((s / kQS) - 1) & 1)) {
             ok = false;
             break;
           }
-          const uint32_t qb = sbase + Q + 16384u * (uint32_t)x, ob = sbase + DO + 16384u * (uint32_t)x;
-          ptx::mbar_arrive_expect_tx(bar(Q_FULL + x), 32768);
-          ptx::tma_load_4d(qb, &tm_q, bar(Q_FULL + x), 0, q0, h, b);
-          ptx::tma_load_4d(qb + 8192, &tm_q, bar(Q_FULL + x), 64, q0, h, b);
-          ptx::tma_load_4d(ob, &tm_do, bar(Q_FULL + x), 0, q0, h, b);
-          ptx::tma_load_4d(ob + 8192, &tm_do, bar(Q_FULL + x), 64, q0, h, b);
+          const uint32_t qb = sbase + Q + 16384u * (uint32_t)qslot, ob = sbase + DO + 16384u * (uint32_t)qslot;
+          ptx::mbar_arrive_expect_tx(bar(Q_FULL + qslot), 32768);
+          ptx::tma_load_4d(qb, &tm_q, bar(Q_FULL + qslot), 0, q0, h, b);
+          ptx::tma_load_4d(qb + 8192, &tm_q, bar(Q_FULL + qslot), 64, q0, h, b);
+          ptx::tma_load_4d(ob, &tm_do, bar(Q_FULL + qslot), 0, q0, h, b);
+          ptx::tma_load_4d(ob + 8192, &tm_do, bar(Q_FULL + qslot), 64, q0, h, b);
         }
         ++nb;
       }
@@ -1373,8 +1377,8 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
     constexpr uint32_t idesc_st = ptx::idesc_bf16_f32(BN, BQ, false, false);
     constexpr uint32_t idesc_acc = ptx::idesc_bf16_f32(BN, D, false, true);
     auto issue_scores = [&](int s) {
-      const int x = s & 1;
-      const uint32_t qb = sbase + Q + 16384u * (uint32_t)x, ob = sbase + DO + 16384u * (uint32_t)x;
+      const int x = s & 1, qslot = s % kQS;
+      const uint32_t qb = sbase + Q + 16384u * (uint32_t)qslot, ob = sbase + DO + 16384u * (uint32_t)qslot;
       const uint32_t cb = tmem + C_BUF + 128u * (uint32_t)x;
 #pragma unroll
       for (int kk = 0; kk < D / 16; ++kk) {
@@ -1398,14 +1402,13 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
       ptx::tc_fence_after();
       const int sb = s;
       // scores of the block's first step
-      if (!wait_u(Q_READY + (s & 1), (s >> 1) & 1)) break;
+      if (!wait_u(Q_READY + s % kQS, (s / kQS) & 1)) break;
       ptx::tc_fence_after();
       issue_scores(s);
       for (; s < sb + nsteps; ++s) {
         const int x = s & 1;
         if (s + 1 < sb + nsteps) {
-          const int y = (s + 1) & 1;
-          if (!wait_u(Q_READY + y, ((s + 1) >> 1) & 1)) {
+          if (!wait_u(Q_READY + (s + 1) % kQS, ((s + 1) / kQS) & 1)) {
             ok = false;
             break;
           }
@@ -1421,7 +1424,8 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
           break;
         }
         ptx::tc_fence_after();
-        const uint32_t qb = sbase + Q + 16384u * (uint32_t)x, ob = sbase + DO + 16384u * (uint32_t)x;
+        const int qslot = s % kQS;
+        const uint32_t qb = sbase + Q + 16384u * (uint32_t)qslot, ob = sbase + DO + 16384u * (uint32_t)qslot;
         const uint32_t cb = tmem + C_BUF + 128u * (uint32_t)x;
 #pragma unroll
         for (int kk = 0; kk < BQ / 16; ++kk) {
@@ -1432,7 +1436,7 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
                         ptx::sdesc_sw128(qb + 2048u * (uint32_t)kk, 8192, 1024), idesc_acc,
                         (s > sb || kk > 0) ? 1u : 0u);
         }
-        ptx::mma_commit_w(bar(Q_EMPTY + x));
+        ptx::mma_commit_w(bar(Q_EMPTY + qslot));
         dv_started = true;
       }
       if (!ok) break;
@@ -1483,7 +1487,7 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
       const int qs = max(blk.s, j0), nsteps = n_steps_of(blk);
       const int r = rt & 63, cg = rt >> 6;
       for (int st = 0; st < nsteps; ++st, ++s) {
-        const int x = s & 1, q0 = qs + (st / G) * BQ, q1 = min(q0 + BQ, blk.e), h = hk * G + st % G;
+        const int qslot = s % kQS, q0 = qs + (st / G) * BQ, q1 = min(q0 + BQ, blk.e), h = hk * G + st % G;
         const int i = q0 + r;
         // Row position, table and row statistics are fetched before the TMA wait.
         int p = 0;
@@ -1502,8 +1506,8 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
 #pragma unroll
           for (int c = 0; c < 8; ++c) tab[c] = __ldg(tp + c);
         }
-        if (!wait(Q_FULL + x, (s >> 1) & 1)) break;
-        const uint32_t qb = Q + 16384u * (uint32_t)x;
+        if (!wait(Q_FULL + qslot, (s / kQS) & 1)) break;
+        const uint32_t qb = Q + 16384u * (uint32_t)qslot;
 #pragma unroll
         for (int cc = 0; cc < (prerot ? 0 : 4); ++cc) {
           const int c = 4 * cg + cc;
@@ -1515,11 +1519,11 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
           *pb = y2;
         }
         if (cg == 0) {
-          s_stats[x * 2 * BQ + r] = l2;
-          s_stats[x * 2 * BQ + BQ + r] = dl;
+          s_stats[qslot * 2 * BQ + r] = l2;
+          s_stats[qslot * 2 * BQ + BQ + r] = dl;
         }
         ptx::fence_proxy_async_smem();
-        ptx::mbar_arrive(bar(Q_READY + x));
+        ptx::mbar_arrive(bar(Q_READY + qslot));
       }
       ++nb;
     }
