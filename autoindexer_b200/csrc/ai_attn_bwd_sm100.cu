@@ -737,16 +737,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ===========================================================================
 namespace dqw {
 constexpr int BM = 128, BN = 64, kThreads = 448;
+constexpr int kKS = 3;  // K / V ring depth (the refill of tile j + kKS starts when tile j is done)
 constexpr uint32_t Q0 = 0, Q1 = 32768, DO0 = 65536, DO1 = 98304;  // 128 x 128 bf16 each
-constexpr uint32_t KB = 131072, VB = KB + 2 * 16384;              // rings of 64 x 128 bf16
-constexpr uint32_t INFO = VB + 2 * 16384;                         // [2][64] u32
-constexpr uint32_t BARS = INFO + 2 * 4 * BN;
-enum Bar { KV_FULL = 0, K_READY = 2, KV_EMPTY = 4, S_FULL = 6, DS_READY = 8, DQ_DONE = 10, Q_READY = 12,
-           FINAL = 13, N_BARS = 14 };
+constexpr uint32_t KB = 131072, VB = KB + kKS * 16384;            // rings of 64 x 128 bf16
+constexpr uint32_t INFO = VB + kKS * 16384;                       // [kKS][64] u32
+constexpr uint32_t BARS = INFO + kKS * 4 * BN;
+enum Bar { KV_FULL = 0, K_READY = kKS, KV_EMPTY = 2 * kKS, S_FULL = 3 * kKS, DS_READY = S_FULL + 2,
+           DQ_DONE = DS_READY + 2, Q_READY = DQ_DONE + 2, FINAL, N_BARS };
 constexpr uint32_t TMEM_SLOT = BARS + 8 * N_BARS;
 constexpr uint32_t ABORT = TMEM_SLOT + 4;
 constexpr uint32_t TOTAL = ABORT + 4;
 constexpr size_t kSmem = TOTAL + 1024;
+static_assert(kSmem <= 227 * 1024, "shared memory budget");
 constexpr long long kWait = 1000000000LL;
 }  // namespace dqw
 
@@ -779,7 +781,7 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
   if (tid == 0) {
     for (int i = 0; i < N_BARS; ++i) {
       uint32_t count = 1;
-      if (i == K_READY || i == K_READY + 1 || i == DS_READY || i == DS_READY + 1) count = 128;
+      if ((i >= K_READY && i < K_READY + kKS) || i == DS_READY || i == DS_READY + 1) count = 128;
       if (i == Q_READY) count = prerot ? 1 : 256;
       ptx::mbar_init(bar(i), count);
     }
@@ -862,13 +864,14 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
     const float lse2r = i < q1 ? lse2 : CUDART_INF_F;
     int done = 0;
     for (int j = 0; j < n; ++j) {
-      const int slot = j & 1, k0 = kv_lo + j * BN;
+      const int slot = j % kKS, k0 = kv_lo + j * BN;
       if (!wait(S_FULL + t, j & 1)) break;
       ptx::tc_fence_after();
       // Tiles wholly below the diagonal of a block without masked keys take
       // the unmasked loop; the test sits outside the unrolled element loops
       // (a per-element branch there doubles the kernel's time).
       const bool fast = !blk_masked && (k0 + BN <= kv_hi) && (k0 + BN - 1 <= q0);
+      const int lim = min(i - k0, kv_hi - 1 - k0);
       const uint32_t* info = s_info + slot * BN;
       uint32_t pk[32];
 #pragma unroll
@@ -889,6 +892,19 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
             }
             pk[16 * hf + x2] = tile::pack2(ds[0], ds[1]);
           }
+        } else if (!blk_masked) {
+          // causal / key-range limit only: column c valid iff c <= lim
+#pragma unroll
+          for (int x2 = 0; x2 < 16; ++x2) {
+            float ds[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const int cl = 2 * x2 + u, c = 32 * hf + cl;
+              const float p = ptx::ex2(c <= lim ? fmaf(__uint_as_float(rs[cl]), sl2, -lse2r) : -CUDART_INF_F);
+              ds[u] = p * (__uint_as_float(rp[cl]) - dl) * scale;
+            }
+            pk[16 * hf + x2] = tile::pack2(ds[0], ds[1]);
+          }
         } else {
 #pragma unroll
           for (int x2 = 0; x2 < 16; ++x2) {
@@ -896,7 +912,7 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
 #pragma unroll
             for (int u = 0; u < 2; ++u) {
               const int cl = 2 * x2 + u, c = 32 * hf + cl;
-              const bool ok = (info[c] & AI_KEY_ATTN) && (k0 + c <= i);
+              const bool ok = (info[c] & AI_KEY_ATTN) && c <= lim;
               const float p = ptx::ex2(ok ? fmaf(__uint_as_float(rs[cl]), sl2, -lse2r) : -CUDART_INF_F);
               ds[u] = p * (__uint_as_float(rp[cl]) - dl) * scale;
             }
@@ -968,8 +984,8 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
         ptx::tma_load_4d(sbase + DO1 + 16384, &tm_do, bar(Q_READY), 64, q0, h0 + 1, b);
       }
       for (int j = 0; j < n; ++j) {
-        const int slot = j & 1, k0 = kv_lo + j * BN;
-        if (j >= 2 && !wait(KV_EMPTY + slot, ((j >> 1) - 1) & 1)) break;
+        const int slot = j % kKS, k0 = kv_lo + j * BN;
+        if (j >= kKS && !wait(KV_EMPTY + slot, ((j / kKS) - 1) & 1)) break;
         const uint32_t kb = sbase + KB + 16384u * (uint32_t)slot, vb = sbase + VB + 16384u * (uint32_t)slot;
         ptx::mbar_arrive_expect_tx(bar(KV_FULL + slot), 32768);
         ptx::tma_load_4d(kb, mk, bar(KV_FULL + slot), 0, k0, hk, b);
@@ -1012,13 +1028,13 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
       issue_s(0, 0);
       issue_s(1, 0);
       for (int j = 0; j < n; ++j) {
-        const int slot = j & 1, nslot = (j + 1) & 1;
+        const int slot = j % kKS, nslot = (j + 1) % kKS;
         const bool more = j + 1 < n;
         if (!wait_u(DS_READY, j & 1)) break;
         ptx::tc_fence_after();
         issue_dq(0, slot, j == 0);
         if (more) {
-          if (!wait_u(K_READY + nslot, ((j + 1) >> 1) & 1)) break;
+          if (!wait_u(K_READY + nslot, ((j + 1) / kKS) & 1)) break;
           ptx::tc_fence_after();
           issue_s(0, nslot);
         }
@@ -1052,8 +1068,8 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
     };
     if (n > 0) fetch(0);
     for (int j = 0; j < n; ++j) {
-      const int slot = j & 1;
-      if (!wait(KV_FULL + slot, (j >> 1) & 1)) break;
+      const int slot = j % kKS;
+      if (!wait(KV_FULL + slot, (j / kKS) & 1)) break;
       const uint32_t kt = KB + 16384u * (uint32_t)slot;
       if (!k_pre && kv_lo + j * BN + row < kv_hi) {
 #pragma unroll

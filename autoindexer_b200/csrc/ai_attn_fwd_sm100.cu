@@ -496,19 +496,29 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
       // Scores are read from TMEM twice (max pass, then exp pass), 64 columns
       // per load round, so that at most 64 scores are live in registers.
       // Tiles wholly below the diagonal of a block without masked keys skip
-      // the mask.
+      // the mask; other tiles of such a block only need the causal / key-range
+      // limit (column c valid iff c <= lim); blocks with masked keys also test
+      // each key's info word.
       const bool fast = !blk_masked && (k0 + BN <= kv_hi) && (k0 + BN - 1 <= q0);
+      const int lim = min(i - k0, kv_hi - 1 - k0);
       const uint32_t* info = s_info + slot * BN;
       auto load64 = [&](int hf, uint32_t (&r0)[32], uint32_t (&r1)[32]) {
         ptx::tmem_ld32(tmem + lane_base + c_s + 64 * hf, r0);
         ptx::tmem_ld32(tmem + lane_base + c_s + 64 * hf + 32, r1);
         ptx::tmem_wait_ld();
-        if (!fast) {
+        if (!fast && !blk_masked) {
 #pragma unroll
           for (int x = 0; x < 32; ++x) {
             const int c0 = 64 * hf + x, c1 = c0 + 32;
-            if (!((info[c0] & AI_KEY_ATTN) && (k0 + c0 <= i))) r0[x] = 0xff800000u;  // -inf
-            if (!((info[c1] & AI_KEY_ATTN) && (k0 + c1 <= i))) r1[x] = 0xff800000u;
+            if (c0 > lim) r0[x] = 0xff800000u;  // -inf
+            if (c1 > lim) r1[x] = 0xff800000u;
+          }
+        } else if (blk_masked) {
+#pragma unroll
+          for (int x = 0; x < 32; ++x) {
+            const int c0 = 64 * hf + x, c1 = c0 + 32;
+            if (!((info[c0] & AI_KEY_ATTN) && c0 <= lim)) r0[x] = 0xff800000u;
+            if (!((info[c1] & AI_KEY_ATTN) && c1 <= lim)) r1[x] = 0xff800000u;
           }
         }
       };
