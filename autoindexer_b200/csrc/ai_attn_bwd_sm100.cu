@@ -861,7 +861,7 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
     const float sl2 = f.scale * kLog2e, scale = f.scale;
     // Rows past q1 (another block's rows) get lse = +inf: their P is 0 with no
     // per-element test on the unmasked path.
-    const float lse2r = i < q1 ? lse2 : CUDART_INF_F;
+    const float lse2r = i < q1 ? lse2 : CUDART_INF_F, dls = dl * scale;
     int done = 0;
     for (int j = 0; j < n; ++j) {
       const int slot = j % kKS, k0 = kv_lo + j * BN;
@@ -888,7 +888,7 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
             for (int u = 0; u < 2; ++u) {
               const int cl = 2 * x2 + u;
               const float p = ptx::ex2(fmaf(__uint_as_float(rs[cl]), sl2, -lse2r));
-              ds[u] = p * (__uint_as_float(rp[cl]) - dl) * scale;
+              ds[u] = p * fmaf(__uint_as_float(rp[cl]), scale, -dls);
             }
             pk[16 * hf + x2] = tile::pack2(ds[0], ds[1]);
           }
@@ -901,7 +901,7 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
             for (int u = 0; u < 2; ++u) {
               const int cl = 2 * x2 + u, c = 32 * hf + cl;
               const float p = ptx::ex2(c <= lim ? fmaf(__uint_as_float(rs[cl]), sl2, -lse2r) : -CUDART_INF_F);
-              ds[u] = p * (__uint_as_float(rp[cl]) - dl) * scale;
+              ds[u] = p * fmaf(__uint_as_float(rp[cl]), scale, -dls);
             }
             pk[16 * hf + x2] = tile::pack2(ds[0], ds[1]);
           }
@@ -914,7 +914,7 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
               const int cl = 2 * x2 + u, c = 32 * hf + cl;
               const bool ok = (info[c] & AI_KEY_ATTN) && c <= lim;
               const float p = ptx::ex2(ok ? fmaf(__uint_as_float(rs[cl]), sl2, -lse2r) : -CUDART_INF_F);
-              ds[u] = p * (__uint_as_float(rp[cl]) - dl) * scale;
+              ds[u] = p * fmaf(__uint_as_float(rp[cl]), scale, -dls);
             }
             pk[16 * hf + x2] = tile::pack2(ds[0], ds[1]);
           }
@@ -1263,7 +1263,7 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
               for (int u = 0; u < 2; ++u) {
                 const int cl = 2 * x2 + u, c = 32 * hf + cl;  // query row q0 + c
                 p[u] = ptx::ex2(key_ok ? fmaf(__uint_as_float(rs[cl]), sl2, -lse2[c]) : -CUDART_INF_F);
-                ds[u] = p[u] * (__uint_as_float(rp[cl]) - dlt[c]) * scale;
+                ds[u] = p[u] * fmaf(__uint_as_float(rp[cl]), scale, -dlt[c]);
               }
               pk[16 * hf + x2] = tile::pack2(p[0], p[1]);
               dk[16 * hf + x2] = tile::pack2(ds[0], ds[1]);
@@ -1277,7 +1277,7 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
                 const int cl = 2 * x2 + u, c = 32 * hf + cl;  // query row q0 + c
                 const bool ok = key_ok && (j <= q0 + c) && (q0 + c < q1);
                 p[u] = ptx::ex2(ok ? fmaf(__uint_as_float(rs[cl]), sl2, -lse2[c]) : -CUDART_INF_F);
-                ds[u] = p[u] * (__uint_as_float(rp[cl]) - dlt[c]) * scale;
+                ds[u] = p[u] * fmaf(__uint_as_float(rp[cl]), scale, -dlt[c]);
               }
               pk[16 * hf + x2] = tile::pack2(p[0], p[1]);
               dk[16 * hf + x2] = tile::pack2(ds[0], ds[1]);
@@ -1536,7 +1536,7 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
         }
         if (cg == 0) {
           s_stats[qslot * 2 * BQ + r] = l2;
-          s_stats[qslot * 2 * BQ + BQ + r] = dl;
+          s_stats[qslot * 2 * BQ + BQ + r] = dl * f.scale;
         }
         ptx::fence_proxy_async_smem();
         ptx::mbar_arrive(bar(Q_READY + qslot));
