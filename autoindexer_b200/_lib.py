@@ -29,6 +29,8 @@ __all__ = [
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_ai_attn.so")
 
 DTYPE_BF16, DTYPE_F16, DTYPE_F32 = 0, 1, 2
+# AiProfKind, in order.
+PROF_KINDS = ("prerot", "fwd", "fwd_fill", "delta", "dq", "dkdv", "bwd_fill", "simt")
 ABI_VERSION = 4
 
 # Every function include/ai_attn.h declares.
@@ -41,6 +43,8 @@ EXPORTED_SYMBOLS = (
     "ai_attn_bwd_workspace",
     "ai_attn_bwd",
     "ai_attn_bwd_noalloc",
+    "ai_attn_profile_enable",
+    "ai_attn_profile_read",
     "ai_attn_read_status",
     "ai_attn_strerror",
 )
@@ -143,6 +147,10 @@ def _bind(handle):
     handle.ai_attn_read_status.argtypes = [ctypes.c_void_p, ctypes.c_void_p, P(ctypes.c_int32)]
     handle.ai_attn_strerror.restype = ctypes.c_char_p
     handle.ai_attn_strerror.argtypes = [ctypes.c_int]
+    handle.ai_attn_profile_enable.restype = ctypes.c_int
+    handle.ai_attn_profile_enable.argtypes = [ctypes.c_int]
+    handle.ai_attn_profile_read.restype = ctypes.c_int
+    handle.ai_attn_profile_read.argtypes = [P(ctypes.c_float), P(ctypes.c_int32)]
     return handle
 
 

@@ -161,6 +161,32 @@ def attn_bwd(q, k, v, out, lse, dout, layout: CompiledLayout, scale: float, rota
     return dq, dk, dv
 
 
+class KernelTimes:
+    """Per-kernel device times of this library's launches (CUDA events on the
+    launch streams; ``ai_attn_profile_enable`` / ``ai_attn_profile_read``)::
+
+        with KernelTimes() as kt:
+            ...  # calls into the library
+        kt.ms["dkdv"], kt.launches["dkdv"]
+    """
+
+    def __enter__(self):
+        _lib.check(_lib.lib().ai_attn_profile_enable(1), "ai_attn_profile_enable")
+        return self
+
+    def __exit__(self, *exc):
+        lib = _lib.lib()
+        n = len(_lib.PROF_KINDS)
+        ms = (ctypes.c_float * n)()
+        cnt = (ctypes.c_int32 * n)()
+        rc = lib.ai_attn_profile_read(ms, cnt)
+        lib.ai_attn_profile_enable(0)
+        _lib.check(rc, "ai_attn_profile_read")
+        self.ms = {k: float(ms[i]) for i, k in enumerate(_lib.PROF_KINDS)}
+        self.launches = {k: int(cnt[i]) for i, k in enumerate(_lib.PROF_KINDS)}
+        return False
+
+
 class AttentionFn(torch.autograd.Function):
     """Autograd wrapper: saves q, k, v, out and lse; backward is ``ai_attn_bwd``."""
 

@@ -1579,7 +1579,11 @@ int sm100_bwd(const AiAttnBwdArgs& a, float* delta, void* rot, bool rot_ready, c
   AiTensor4 qr{}, kr{};
   const bool pre = rot != nullptr;
   if (pre && !sm100_rotated_views(f, rot, &qr, &kr)) return AI_ERR_ALIGN;
-  cudaError_t e = bwd_delta(a, delta, st);
+  cudaError_t e;
+  {
+    ProfScope ps(AI_PROF_DELTA, st);
+    e = bwd_delta(a, delta, st);
+  }
   if (e == cudaSuccess && pre && !rot_ready) e = prerot(f, rot, st);
   if (e == cudaSuccess && f.layout.n_fwd_items > 0) {
     CUtensorMap tk, tv, tqr, tdo, tkr;
@@ -1600,6 +1604,7 @@ int sm100_bwd(const AiAttnBwdArgs& a, float* delta, void* rot, bool rot_ready, c
     if (n_single > 0) {
       e = cudaFuncSetAttribute(dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dq::kSmem);
       if (e == cudaSuccess) {
+        ProfScope ps(AI_PROF_DQ, st);
         dq_kernel<<<dim3(n_single, f.num_q_heads), kThreads, dq::kSmem, st>>>(a, delta, tk, tv);
         e = cudaGetLastError();
       }
@@ -1607,6 +1612,7 @@ int sm100_bwd(const AiAttnBwdArgs& a, float* delta, void* rot, bool rot_ready, c
     if (e == cudaSuccess && n_pair > 0) {
       e = cudaFuncSetAttribute(dq_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dqw::kSmem);
       if (e == cudaSuccess) {
+        ProfScope ps(AI_PROF_DQ, st);
         dq_ws_kernel<<<dim3(n_pair, f.num_q_heads / 2), dqw::kThreads, dqw::kSmem, st>>>(a, delta, tk, tv, tqr, tdo,
                                                                                          tkr, pre ? 1 : 0);
         e = cudaGetLastError();
@@ -1631,6 +1637,7 @@ int sm100_bwd(const AiAttnBwdArgs& a, float* delta, void* rot, bool rot_ready, c
     if (n_abs > 0) {
       e = cudaFuncSetAttribute(dkdv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kv::kSmem);
       if (e == cudaSuccess) {
+        ProfScope ps(AI_PROF_DKDV, st);
         dkdv_kernel<<<dim3(n_abs, f.num_kv_heads), kThreads, kv::kSmem, st>>>(a, delta, tk, tv, tq, tdo);
         e = cudaGetLastError();
       }
@@ -1638,13 +1645,17 @@ int sm100_bwd(const AiAttnBwdArgs& a, float* delta, void* rot, bool rot_ready, c
     if (e == cudaSuccess && n_plain > 0) {
       e = cudaFuncSetAttribute(dkdv_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kvw::kSmem);
       if (e == cudaSuccess) {
+        ProfScope ps(AI_PROF_DKDV, st);
         dkdv_ws_kernel<<<dim3(n_plain, f.num_kv_heads), kvw::kThreads, kvw::kSmem, st>>>(
             a, delta, tk, tv, pre ? tqr : tq, tdo, tkr, pre ? 1 : 0);
         e = cudaGetLastError();
       }
     }
   }
-  if (e == cudaSuccess) e = bwd_fill(a, st);
+  if (e == cudaSuccess) {
+    ProfScope ps(AI_PROF_BWD_FILL, st);
+    e = bwd_fill(a, st);
+  }
   if (cuda_err) *cuda_err = e;
   return e == cudaSuccess ? AI_OK : AI_ERR_LAUNCH;
 }

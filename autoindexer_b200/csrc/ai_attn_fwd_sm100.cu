@@ -813,6 +813,7 @@ int sm100_fwd(const AiAttnFwdArgs& a, cudaStream_t st, cudaError_t* cuda_err) {
     if (n_single > 0) {
       e = cudaFuncSetAttribute(fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
       if (e == cudaSuccess) {
+        ProfScope ps(AI_PROF_FWD, st);
         fwd_kernel<<<dim3(n_single, a.num_q_heads), kThreads, kSmemBytes, st>>>(a, tm_k, tm_v);
         e = cudaGetLastError();
       }
@@ -824,6 +825,7 @@ int sm100_fwd(const AiAttnFwdArgs& a, cudaStream_t st, cudaError_t* cuda_err) {
         return AI_ERR_TMA;
       e = cudaFuncSetAttribute(fwd_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ws::kSmem);
       if (e == cudaSuccess) {
+        ProfScope ps(AI_PROF_FWD, st);
         fwd_ws_kernel<<<dim3(n_pair, a.num_q_heads / 2), ws::kThreads, ws::kSmem, st>>>(a, tm_k, tm_v, tm_qr, tm_kr,
                                                                                         pre ? 1 : 0);
         e = cudaGetLastError();

@@ -93,8 +93,10 @@ int ai_attn_fwd(const AiAttnFwdArgs* a, void* stream) {
     cudaError_t ce = cudaSuccess;
     rc = ai::sm100_fwd(*a, st, &ce);
     if (rc != AI_OK) return rc;
+    ai::ProfScope ps(AI_PROF_FWD_FILL, st);
     return launch_status(ai::fwd_fill(*a, st));
   }
+  ai::ProfScope ps(AI_PROF_SIMT, st);
   return launch_status(ai::simt_fwd(*a, st));
 }
 
@@ -135,6 +137,7 @@ int ai_attn_bwd(const AiAttnBwdArgs* a, void* stream) {
     if (a->workspace_bytes >= db + ai::prerot_bytes(a->fwd, nullptr)) rot = static_cast<char*>(a->workspace) + db;
     return ai::sm100_bwd(*a, delta, rot, false, st, nullptr);
   }
+  ai::ProfScope ps(AI_PROF_SIMT, st);
   return launch_status(ai::simt_bwd(*a, delta, st));
 }
 

@@ -25,6 +25,17 @@ cudaError_t bwd_fill(const AiAttnBwdArgs& a, cudaStream_t st);
 // tcgen05 / TMEM / TMA kernels (sm_100a): bf16, head_dim 128.
 bool sm100_fwd_supported(int dtype, int head_dim);
 int sm100_fwd_tile_rows();
+// Optional launch timing (ai_profile.cu): a scope around one kernel launch
+// records CUDA events on the launch stream while profiling is enabled.
+int prof_begin(int kind, cudaStream_t st);
+void prof_end(int slot, cudaStream_t st);
+struct ProfScope {
+  int slot;
+  cudaStream_t st;
+  ProfScope(int kind, cudaStream_t s) : slot(prof_begin(kind, s)), st(s) {}
+  ~ProfScope() { prof_end(slot, st); }
+};
+
 // Returns AI_OK or an AiStatus > 0; `cuda_err` receives the CUDA error of a failed launch.
 int sm100_fwd(const AiAttnFwdArgs& a, cudaStream_t st, cudaError_t* cuda_err);
 bool sm100_bwd_supported(int dtype, int head_dim);

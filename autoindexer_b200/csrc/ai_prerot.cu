@@ -72,6 +72,7 @@ cudaError_t prerot(const AiAttnFwdArgs& a, void* buf, cudaStream_t st) {
   const int64_t work = (int64_t)a.batch * (a.num_q_heads + a.num_kv_heads) * a.seq_len * 8;
   int blocks = (int)((work + 255) / 256);
   if (blocks > 148 * 16) blocks = 148 * 16;
+  ProfScope ps(AI_PROF_PREROT, st);
   prerot_kernel<<<blocks, 256, 0, st>>>(a, q_rot, k_rot);
   return cudaGetLastError();
 }

@@ -37,6 +37,10 @@ SECTIONS = [(0, 32), (32, 64)]
 WORKLOAD = ("cfg1: bf16 B=4 T=4096 Hq=32 Hkv=8 D=128 theta=1e6, docs U[256,2048] packed per row, "
             "2 RoPE sections (32+32 freq slots: arange, cursor stream)")
 METRIC = "multi-seg RoPE attn fwd+bwd TFLOP/s (causal-adjusted, 14*D*pairs*Hq)"
+DOM_KERNEL_NAMES = {"fwd": "fwd_ws_kernel (forward)", "dq": "dq_ws_kernel (dQ)", "dkdv": "dkdv_ws_kernel (dK/dV)"}
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch on this
+# workload, from one ncu capture of the three kernels (profiles/).
+TRAFFIC_BYTES = {"fwd": 304252928, "dq": 447438080, "dkdv": 403690752}
 
 
 def make_workload(seed: int, device):
@@ -125,27 +129,12 @@ def peaks():
         return 1590.0, 1400.0, "fallback"
 
 
-def our_launches_per_step(layout) -> int:
-    """Kernels of ours per step (forward, then backward reusing the forward's
-    rotated Q/K copies): Q/K rotation, the one-head kernel for abs-key items
-    (if any), the two-head kernel, the row fill; delta, the dQ kernels, the
-    dK/dV kernels, the row fill."""
-    G = HQ // HKV
-    n_fwd, n_kv = int(layout.fwd_items.shape[0]), int(layout.kv_items.shape[0])
-    n_single = layout.n_fwd_abs_items if G % 2 == 0 else n_fwd
-    n_pair = n_fwd - n_single
-    n_kv_abs, n_kv_plain = layout.n_kv_abs_items, n_kv - layout.n_kv_abs_items
-    fwd = 1 + int(n_single > 0) + int(n_pair > 0) + 1
-    bwd = 1 + int(n_single > 0) + int(n_pair > 0) + int(n_kv_abs > 0) + int(n_kv_plain > 0) + 1
-    return fwd + bwd
-
-
 def run_ours(args):
     import torch
     import torch.distributed as dist
 
     from autoindexer_b200 import _lib
-    from autoindexer_b200.attention import attn_bwd, attn_fwd, fused_chain_of_edits_attn_b200, read_status
+    from autoindexer_b200.attention import KernelTimes, attn_bwd, attn_fwd, fused_chain_of_edits_attn_b200, read_status
     from autoindexer_b200.meta import compile_layout
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -189,8 +178,11 @@ def run_ours(args):
             e0.record(stream)
             out, lse, ws = attn_fwd(q, k, v, layout, scale, keep_workspace=True)
             e1.record(stream)
-            attn_bwd(q, k, v, out, lse, dout, layout, scale, fwd_workspace=ws)
+            grads = attn_bwd(q, k, v, out, lse, dout, layout, scale, fwd_workspace=ws)
             e2.record(stream)
+            # Release this step's tensors as the warm-up does, so that every
+            # step reuses the same allocator blocks.
+            del out, lse, ws, grads
         torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
@@ -204,6 +196,16 @@ def run_ours(args):
         t_max = float(tt.item())
     value = world * flops * args.steps / t_max / 1e12
     ms_per_step = t_max / args.steps * 1e3
+
+    # Per-kernel device times: the same steps again with the library's launch
+    # events on (ai_attn_profile_*); they give the dominant kernel's duration
+    # for the roofline and the count of our launches.
+    torch.cuda.synchronize(dev)
+    with KernelTimes() as kt:
+        for i in range(args.steps):
+            flush.fill_(float(i))
+            step()
+        torch.cuda.synchronize(dev)
 
     # End to end through the public API: pinned host inputs -> device, forward +
     # backward via autograd, results (out, dq, dk, dv) back to pinned host memory.
@@ -244,11 +246,15 @@ def run_ours(args):
     assert read_status(dev) == 0
 
     peak, peak_sus, peak_kind = peaks()
-    dom_is_bwd = t_bwd >= t_fwd
-    dom_flops = flops_bwd if dom_is_bwd else flops_fwd
-    dom_t = (t_bwd if dom_is_bwd else t_fwd) / args.steps
-    achieved = dom_flops / dom_t / 1e12
-    launches_per_step = our_launches_per_step(layout)
+    # Dominant kernel: algorithmic FLOPs per launch (per query head and finite
+    # (query, key) pair: forward 4·D, dQ 6·D — S, dP, dQ — and dK/dV 8·D — S,
+    # dP, dV, dK) over its event-timed duration.
+    kflops = {"fwd": 4.0 * D * HQ * layout.pairs_per_head, "dq": 6.0 * D * HQ * layout.pairs_per_head,
+              "dkdv": 8.0 * D * HQ * layout.pairs_per_head}
+    dom = max(kflops, key=lambda kk: kt.ms[kk])
+    dom_ms = kt.ms[dom] / max(1, kt.launches[dom])  # per launch
+    achieved = kflops[dom] * args.steps / (kt.ms[dom] * 1e-3) / 1e12
+    launches_per_step = sum(kt.launches.values()) / args.steps
     tokens = world * B * T * args.steps / t_max
 
     line = {
@@ -272,13 +278,14 @@ def run_ours(args):
         "pairs_per_head": layout.pairs_per_head,
         "pct_bf16_peak": round(100 * value / world / peak, 2),
         "pct_bf16_spec_2250": round(100 * value / world / 2250.0, 2),
-        "roofline": {"bound": "tensor", "kernel": "ai_attn_bwd (dQ + dK/dV kernels)" if dom_is_bwd else "ai_attn_fwd",
+        "roofline": {"bound": "tensor", "kernel": DOM_KERNEL_NAMES[dom],
                      "achieved": round(achieved, 3), "peak": peak, "unit": "TFLOP/s",
                      "frac": round(achieved / peak, 4), "peak_kind": f"{peak_kind} burst bf16",
-                     "traffic": None},
+                     "launch_ms": round(dom_ms, 4), "traffic": TRAFFIC_BYTES.get(dom)},
+        "kernel_ms_per_step": {kk: round(v / args.steps, 4) for kk, v in kt.ms.items() if v > 0},
         "e2e": {"value": round(e2e_value, 3), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
-        "gpu_launches": launches_per_step * args.steps,
+        "gpu_launches": int(round(launches_per_step * args.steps)),
         "clocks": clocks.summary(),
     }
     if rank == 0 and not args.no_cpu_baseline:

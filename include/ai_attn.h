@@ -198,6 +198,29 @@ int ai_attn_read_status(int32_t* dev_status, void* stream, int32_t* host_out);
 /* Static text for a status code. */
 const char* ai_attn_strerror(int code);
 
+/* Optional per-kernel timing (no reference counterpart; for benchmarks and
+ * profiling).  While enabled, each kernel launch of this library is
+ * bracketed by two CUDA events recorded on the launch's own stream (nothing
+ * is skipped or reordered).  ai_attn_profile_enable(1) starts a fresh
+ * collection, (0) stops it.  ai_attn_profile_read synchronises the recorded
+ * events and writes, per kind, the summed elapsed milliseconds and the launch
+ * count (arrays of AI_PROF_KINDS entries), then clears the collection.  At
+ * most 4096 launches are recorded per collection.  Not for concurrent use
+ * from several host threads. */
+typedef enum AiProfKind {
+  AI_PROF_PREROT = 0,   /* once-rotated Q/K copies */
+  AI_PROF_FWD = 1,      /* tensor-core forward kernels */
+  AI_PROF_FWD_FILL = 2, /* forward rows no block owns */
+  AI_PROF_DELTA = 3,    /* row sums of dO.O */
+  AI_PROF_DQ = 4,       /* tensor-core dQ kernels */
+  AI_PROF_DKDV = 5,     /* tensor-core dK/dV kernels */
+  AI_PROF_BWD_FILL = 6, /* backward rows no block owns */
+  AI_PROF_SIMT = 7,     /* fp32 / fp16 / other head_dim path */
+  AI_PROF_KINDS = 8
+} AiProfKind;
+int ai_attn_profile_enable(int on);
+int ai_attn_profile_read(float* ms_by_kind, int32_t* launches_by_kind);
+
 #ifdef __cplusplus
 }
 #endif

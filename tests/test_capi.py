@@ -88,3 +88,19 @@ def test_host_validation_null_and_layout():
     assert nbytes.value >= 1 * 4 * 16 * 4
     b.workspace = None
     assert L.ai_attn_bwd(ctypes.byref(b), None) == 8
+
+
+def test_profile_entry_points_without_gpu():
+    """Profiling: NULL outputs are rejected; enabling, reading with nothing
+    recorded (no GPU here) and disabling succeed and report zeros."""
+    L = _lib.lib()
+    n = len(_lib.PROF_KINDS)
+    ms = (ctypes.c_float * n)()
+    cnt = (ctypes.c_int32 * n)()
+    assert L.ai_attn_profile_read(None, cnt) == 1  # AI_ERR_NULL
+    assert L.ai_attn_profile_enable(1) == 0
+    assert L.ai_attn_profile_read(ms, cnt) == 0
+    assert L.ai_attn_profile_enable(0) == 0
+    assert list(cnt) == [0] * n and list(ms) == [0.0] * n
+    header = open(HEADER).read()
+    assert f"AI_PROF_KINDS = {n}" in header

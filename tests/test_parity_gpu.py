@@ -88,7 +88,7 @@ def _edit_chain_case(name, B, Hq, Hkv, D, seed):
 @pytest.mark.parametrize("name,hq,hkv", [("op0_d32", 4, 2), ("op5_d32", 4, 2), ("op9_d32", 4, 2), ("op5_d32", 8, 2),
                                          ("op9_d32", 4, 1)])
 def test_bf16_edit_chains_match_oracle(name, hq, hkv, cuda_device):
-    """GQA groups of 2 (one CTA per head pair) and 4 (CTA pairs, 2-SM MMAs)."""
+    """GQA groups of 1 query-head pair and of 2 pairs (one CTA per pair)."""
     lay, q, k, v, dout, mod, rope = _edit_chain_case(name, 2, hq, hkv, 128, 11)
     q, k, v, dout = bf16_round(q, k, v, dout)
     got = run_kernels(lay, q, k, v, dout, mod, torch.bfloat16, cuda_device)
@@ -241,6 +241,27 @@ def test_bf16_backward_reuses_forward_rotation(layout_kind, cuda_device):
     assert read_status(cuda_device) == 0
     for name, a_, b_ in zip(("dq", "dk", "dv"), reuse, own):
         assert torch.equal(a_, b_), name
+
+
+def test_kernel_times_count_launches(cuda_device):
+    """ai_attn_profile_*: one forward + backward on a documents layout records
+    the rotation, forward, delta, dQ and dK/dV launches with positive times."""
+    from autoindexer_b200.attention import KernelTimes
+
+    B, T, Hq, Hkv, D = 2, 640, 8, 2, 128
+    rows, mod, _ = _sectioned_docs(B, T, D, 2, seed=43)
+    rng = np.random.default_rng(4)
+    tq, tk, tv = (torch.as_tensor(rng.standard_normal(s)).to(cuda_device, torch.bfloat16)
+                  for s in ((B, Hq, T, D), (B, Hkv, T, D), (B, Hkv, T, D)))
+    tdo = torch.as_tensor(rng.standard_normal((B, T, Hq, D))).to(cuda_device, torch.bfloat16)
+    layout = compile_layout(rows, B, T, D, torch.bfloat16, mod.to(cuda_device), cuda_device)
+    with KernelTimes() as kt:
+        out, lse, ws = attn_fwd(tq, tk, tv, layout, D ** -0.5, keep_workspace=True)
+        attn_bwd(tq, tk, tv, out, lse, tdo, layout, D ** -0.5, fwd_workspace=ws)
+    assert kt.launches["prerot"] == 1  # the backward reuses the forward's copies
+    for kind in ("fwd", "fwd_fill", "delta", "dq", "dkdv", "bwd_fill"):
+        assert kt.launches[kind] >= 1 and kt.ms[kind] > 0.0, kind
+    assert kt.launches["simt"] == 0
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
