@@ -862,6 +862,8 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
     // Rows past q1 (another block's rows) get lse = +inf: their P is 0 with no
     // per-element test on the unmasked path.
     const float lse2r = i < q1 ? lse2 : CUDART_INF_F, dls = dl * scale;
+    const float2 sl2x2 = make_float2(sl2, sl2), scalex2 = make_float2(scale, scale);
+    const float2 nlse2 = make_float2(-lse2r, -lse2r), ndls = make_float2(-dls, -dls);
     int done = 0;
     for (int j = 0; j < n; ++j) {
       const int slot = j % kKS, k0 = kv_lo + j * BN;
@@ -880,43 +882,32 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
         ptx::tmem_ld32(tmem + lane_base + c_s + 32 * hf, rs);
         ptx::tmem_ld32(tmem + lane_base + c_s + 64 + 32 * hf, rp);
         ptx::tmem_wait_ld();
+        // Pairs of keys on the packed f32x2 pipe (FFMA2 for the exp argument
+        // and for dP * scale - scale * delta, FMUL2 for dS).
+        auto pair = [&](int x2, bool ok0, bool ok1) {
+          float2 arg = __ffma2_rn(make_float2(__uint_as_float(rs[2 * x2]), __uint_as_float(rs[2 * x2 + 1])), sl2x2, nlse2);
+          arg.x = ok0 ? arg.x : -CUDART_INF_F;
+          arg.y = ok1 ? arg.y : -CUDART_INF_F;
+          const float2 pp = make_float2(ptx::ex2(arg.x), ptx::ex2(arg.y));
+          const float2 ds = __fmul2_rn(
+              pp, __ffma2_rn(make_float2(__uint_as_float(rp[2 * x2]), __uint_as_float(rp[2 * x2 + 1])), scalex2, ndls));
+          pk[16 * hf + x2] = tile::pack2(ds.x, ds.y);
+        };
         if (fast) {
 #pragma unroll
-          for (int x2 = 0; x2 < 16; ++x2) {
-            float ds[2];
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-              const int cl = 2 * x2 + u;
-              const float p = ptx::ex2(fmaf(__uint_as_float(rs[cl]), sl2, -lse2r));
-              ds[u] = p * fmaf(__uint_as_float(rp[cl]), scale, -dls);
-            }
-            pk[16 * hf + x2] = tile::pack2(ds[0], ds[1]);
-          }
+          for (int x2 = 0; x2 < 16; ++x2) pair(x2, true, true);
         } else if (!blk_masked) {
           // causal / key-range limit only: column c valid iff c <= lim
 #pragma unroll
           for (int x2 = 0; x2 < 16; ++x2) {
-            float ds[2];
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-              const int cl = 2 * x2 + u, c = 32 * hf + cl;
-              const float p = ptx::ex2(c <= lim ? fmaf(__uint_as_float(rs[cl]), sl2, -lse2r) : -CUDART_INF_F);
-              ds[u] = p * fmaf(__uint_as_float(rp[cl]), scale, -dls);
-            }
-            pk[16 * hf + x2] = tile::pack2(ds[0], ds[1]);
+            const int c = 32 * hf + 2 * x2;
+            pair(x2, c <= lim, c + 1 <= lim);
           }
         } else {
 #pragma unroll
           for (int x2 = 0; x2 < 16; ++x2) {
-            float ds[2];
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-              const int cl = 2 * x2 + u, c = 32 * hf + cl;
-              const bool ok = (info[c] & AI_KEY_ATTN) && c <= lim;
-              const float p = ptx::ex2(ok ? fmaf(__uint_as_float(rs[cl]), sl2, -lse2r) : -CUDART_INF_F);
-              ds[u] = p * fmaf(__uint_as_float(rp[cl]), scale, -dls);
-            }
-            pk[16 * hf + x2] = tile::pack2(ds[0], ds[1]);
+            const int c = 32 * hf + 2 * x2;
+            pair(x2, (info[c] & AI_KEY_ATTN) && c <= lim, (info[c + 1] & AI_KEY_ATTN) && c + 1 <= lim);
           }
         }
       }
@@ -1222,6 +1213,7 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
     const int t = warp / 4, lrow = tid % 128, j = j0 + lrow;
     const uint32_t lane_base = (uint32_t)((warp % 4) * 32) << 16;
     const float sl2 = f.scale * kLog2e, scale = f.scale;
+    const float2 sl2x2 = make_float2(sl2, sl2), scalex2 = make_float2(scale, scale);
     BlockIter it(&L, b, j0, j1);
     Block blk;
     int s = 0, nb = 0;
@@ -1238,8 +1230,8 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
         const int x = s & 1, qslot = s % kQS, q0 = qs + (st / G) * BQ, q1 = min(q0 + BQ, blk.e);
         if (!wait(Q_READY + qslot, (s / kQS) & 1) || !wait(S_FULL + x, (s >> 1) & 1)) break;
         ptx::tc_fence_after();
-        const float* lse2 = s_stats + qslot * 2 * BQ;
-        const float* dlt = lse2 + BQ;
+        const float* nlse2 = s_stats + qslot * 2 * BQ;  // -lse2 per query row
+        const float* ndlt = nlse2 + BQ;                  // -scale * delta per query row
         const uint32_t cb = tmem + lane_base + C_BUF + 128u * (uint32_t)x;
         // Whole-step masks: causal (j <= i) holds for every pair when the tile
         // lies wholly above the query rows, and every row is in the block when
@@ -1248,6 +1240,7 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
         // The step-uniform test sits outside the unrolled element loops (a
         // per-element branch there costs as much as the rest of the step).
         const bool plain = no_causal && rows_full;
+        const int clo = j - q0, chi = q1 - q0;  // general path: query columns clo <= c < chi
         uint32_t pk[32], dk[32];
 #pragma unroll
         for (int hf = 0; hf < 2; ++hf) {
@@ -1255,32 +1248,32 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
           ptx::tmem_ld32(cb + 32 * hf, rs);
           ptx::tmem_ld32(cb + 64 + 32 * hf, rp);
           ptx::tmem_wait_ld();
+          // Pairs of query columns on the packed f32x2 pipe: the exp argument
+          // s * sl2 - lse2 and dP * scale - scale * delta are one FFMA2 each
+          // (row statistics are staged negated), dS one FMUL2.  The plain /
+          // general choice sits outside the unrolled loops.
+          auto pair = [&](int x2, bool ok0, bool ok1) {
+            const int c = 32 * hf + 2 * x2;  // query rows q0 + c, q0 + c + 1
+            const float2 nl = *reinterpret_cast<const float2*>(nlse2 + c);
+            const float2 nd = *reinterpret_cast<const float2*>(ndlt + c);
+            float2 arg =
+                __ffma2_rn(make_float2(__uint_as_float(rs[2 * x2]), __uint_as_float(rs[2 * x2 + 1])), sl2x2, nl);
+            arg.x = ok0 ? arg.x : -CUDART_INF_F;
+            arg.y = ok1 ? arg.y : -CUDART_INF_F;
+            const float2 pp = make_float2(ptx::ex2(arg.x), ptx::ex2(arg.y));
+            const float2 ds = __fmul2_rn(
+                pp, __ffma2_rn(make_float2(__uint_as_float(rp[2 * x2]), __uint_as_float(rp[2 * x2 + 1])), scalex2, nd));
+            pk[16 * hf + x2] = tile::pack2(pp.x, pp.y);
+            dk[16 * hf + x2] = tile::pack2(ds.x, ds.y);
+          };
           if (plain) {
 #pragma unroll
-            for (int x2 = 0; x2 < 16; ++x2) {
-              float p[2], ds[2];
-#pragma unroll
-              for (int u = 0; u < 2; ++u) {
-                const int cl = 2 * x2 + u, c = 32 * hf + cl;  // query row q0 + c
-                p[u] = ptx::ex2(key_ok ? fmaf(__uint_as_float(rs[cl]), sl2, -lse2[c]) : -CUDART_INF_F);
-                ds[u] = p[u] * fmaf(__uint_as_float(rp[cl]), scale, -dlt[c]);
-              }
-              pk[16 * hf + x2] = tile::pack2(p[0], p[1]);
-              dk[16 * hf + x2] = tile::pack2(ds[0], ds[1]);
-            }
+            for (int x2 = 0; x2 < 16; ++x2) pair(x2, key_ok, key_ok);
           } else {
 #pragma unroll
             for (int x2 = 0; x2 < 16; ++x2) {
-              float p[2], ds[2];
-#pragma unroll
-              for (int u = 0; u < 2; ++u) {
-                const int cl = 2 * x2 + u, c = 32 * hf + cl;  // query row q0 + c
-                const bool ok = key_ok && (j <= q0 + c) && (q0 + c < q1);
-                p[u] = ptx::ex2(ok ? fmaf(__uint_as_float(rs[cl]), sl2, -lse2[c]) : -CUDART_INF_F);
-                ds[u] = p[u] * fmaf(__uint_as_float(rp[cl]), scale, -dlt[c]);
-              }
-              pk[16 * hf + x2] = tile::pack2(p[0], p[1]);
-              dk[16 * hf + x2] = tile::pack2(ds[0], ds[1]);
+              const int c = 32 * hf + 2 * x2;
+              pair(x2, key_ok && c >= clo && c < chi, key_ok && c + 1 >= clo && c + 1 < chi);
             }
           }
         }
@@ -1535,8 +1528,8 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
           *pb = y2;
         }
         if (cg == 0) {
-          s_stats[qslot * 2 * BQ + r] = l2;
-          s_stats[qslot * 2 * BQ + BQ + r] = dl * f.scale;
+          s_stats[qslot * 2 * BQ + r] = -l2;
+          s_stats[qslot * 2 * BQ + BQ + r] = -(dl * f.scale);
         }
         ptx::fence_proxy_async_smem();
         ptx::mbar_arrive(bar(Q_READY + qslot));

@@ -559,25 +559,29 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
       }
       l *= alpha;
       const float msub = m_use == -CUDART_INF_F ? 0.f : m_use;
-      float suma = 0.f, sumb = 0.f;
+      // Exponent arguments and row sums on the packed f32x2 pipe.
+      const float2 sl2x2 = make_float2(sl2, sl2), nm2 = make_float2(-msub, -msub);
+      float2 suma = make_float2(0.f, 0.f), sumb = make_float2(0.f, 0.f);
 #pragma unroll
       for (int hf = 0; hf < 2; ++hf) {
         uint32_t r0[32], r1[32], pk[32];
         load64(hf, r0, r1);
 #pragma unroll
         for (int x = 0; x < 16; ++x) {
-          const float p0 = ptx::ex2(fmaf(__uint_as_float(r0[2 * x]), sl2, -msub));
-          const float p1 = ptx::ex2(fmaf(__uint_as_float(r0[2 * x + 1]), sl2, -msub));
-          const float p2 = ptx::ex2(fmaf(__uint_as_float(r1[2 * x]), sl2, -msub));
-          const float p3 = ptx::ex2(fmaf(__uint_as_float(r1[2 * x + 1]), sl2, -msub));
-          suma += p0 + p1;
-          sumb += p2 + p3;
-          pk[x] = tile::pack2(p0, p1);
-          pk[16 + x] = tile::pack2(p2, p3);
+          const float2 a01 =
+              __ffma2_rn(make_float2(__uint_as_float(r0[2 * x]), __uint_as_float(r0[2 * x + 1])), sl2x2, nm2);
+          const float2 a23 =
+              __ffma2_rn(make_float2(__uint_as_float(r1[2 * x]), __uint_as_float(r1[2 * x + 1])), sl2x2, nm2);
+          const float2 p01 = make_float2(ptx::ex2(a01.x), ptx::ex2(a01.y));
+          const float2 p23 = make_float2(ptx::ex2(a23.x), ptx::ex2(a23.y));
+          suma = __fadd2_rn(suma, p01);
+          sumb = __fadd2_rn(sumb, p23);
+          pk[x] = tile::pack2(p01.x, p01.y);
+          pk[16 + x] = tile::pack2(p23.x, p23.y);
         }
         ptx::tmem_st32(tmem + lane_base + c_s + 32 * hf, pk);
       }
-      l += suma + sumb;
+      l += (suma.x + suma.y) + (sumb.x + sumb.y);
       ptx::tmem_wait_st();
       ptx::tc_fence_before();
       ptx::mbar_arrive(bar(P_READY + t));
