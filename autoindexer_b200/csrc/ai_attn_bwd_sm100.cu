@@ -1243,36 +1243,30 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
         const int clo = j - q0, chi = q1 - q0;  // general path: query columns clo <= c < chi
         uint32_t pk[32], dk[32];
 #pragma unroll
-        for (int hf = 0; hf < 2; ++hf) {
-          uint32_t rs[32], rp[32];
-          ptx::tmem_ld32(cb + 32 * hf, rs);
-          ptx::tmem_ld32(cb + 64 + 32 * hf, rp);
+        for (int qq = 0; qq < 4; ++qq) {
+          uint32_t rs[16], rp[16];
+          ptx::tmem_ld16(cb + 16 * qq, rs);
+          ptx::tmem_ld16(cb + 64 + 16 * qq, rp);
           ptx::tmem_wait_ld();
-          // Pairs of query columns on the packed f32x2 pipe: the exp argument
-          // s * sl2 - lse2 and dP * scale - scale * delta are one FFMA2 each
-          // (row statistics are staged negated), dS one FMUL2.  The plain /
-          // general choice sits outside the unrolled loops.
           auto pair = [&](int x2, bool ok0, bool ok1) {
-            const int c = 32 * hf + 2 * x2;  // query rows q0 + c, q0 + c + 1
+            const int c = 16 * qq + 2 * x2;
             const float2 nl = *reinterpret_cast<const float2*>(nlse2 + c);
             const float2 nd = *reinterpret_cast<const float2*>(ndlt + c);
-            float2 arg =
-                __ffma2_rn(make_float2(__uint_as_float(rs[2 * x2]), __uint_as_float(rs[2 * x2 + 1])), sl2x2, nl);
+            float2 arg = __ffma2_rn(make_float2(__uint_as_float(rs[2 * x2]), __uint_as_float(rs[2 * x2 + 1])), sl2x2, nl);
             arg.x = ok0 ? arg.x : -CUDART_INF_F;
             arg.y = ok1 ? arg.y : -CUDART_INF_F;
             const float2 pp = make_float2(ptx::ex2(arg.x), ptx::ex2(arg.y));
-            const float2 ds = __fmul2_rn(
-                pp, __ffma2_rn(make_float2(__uint_as_float(rp[2 * x2]), __uint_as_float(rp[2 * x2 + 1])), scalex2, nd));
-            pk[16 * hf + x2] = tile::pack2(pp.x, pp.y);
-            dk[16 * hf + x2] = tile::pack2(ds.x, ds.y);
+            const float2 ds = __fmul2_rn(pp, __ffma2_rn(make_float2(__uint_as_float(rp[2 * x2]), __uint_as_float(rp[2 * x2 + 1])), scalex2, nd));
+            pk[8 * qq + x2] = tile::pack2(pp.x, pp.y);
+            dk[8 * qq + x2] = tile::pack2(ds.x, ds.y);
           };
           if (plain) {
 #pragma unroll
-            for (int x2 = 0; x2 < 16; ++x2) pair(x2, key_ok, key_ok);
+            for (int x2 = 0; x2 < 8; ++x2) pair(x2, key_ok, key_ok);
           } else {
 #pragma unroll
-            for (int x2 = 0; x2 < 16; ++x2) {
-              const int c = 32 * hf + 2 * x2;
+            for (int x2 = 0; x2 < 8; ++x2) {
+              const int c = 16 * qq + 2 * x2;
               pair(x2, key_ok && c >= clo && c < chi, key_ok && c + 1 >= clo && c + 1 < chi);
             }
           }

@@ -43,9 +43,9 @@ DOM_KERNEL_NAMES = {"fwd": "fwd_ws_kernel (forward)", "dq": "dq_ws_kernel (dQ)",
 TRAFFIC_BYTES = {"fwd": 304252928, "dq": 447438080, "dkdv": 403690752}
 
 
-def make_workload(seed: int, device):
-    import torch
-
+def make_rows(seed: int):
+    """The seeded document layout of one rank: per batch row, documents of
+    U[256, 2048] tokens packed to T; the second RoPE section's cursor stream."""
     import autoindexer_b200 as ab
     from autoindexer_b200.positions import split_documents
 
@@ -55,6 +55,17 @@ def make_workload(seed: int, device):
     for _ in range(B):
         lens = split_documents(T, 256, 2048, rng)
         rows.append(ab.document_blocks(lens, position_ids=np.arange(T)))
+    return rows, streams
+
+
+def make_workload(seed: int, device):
+    """Config-1 inputs: the document layout is the same on every rank (seed 0:
+    fixed per-GPU work for weak scaling), q/k/v/dO values are seeded by `seed`."""
+    import torch
+
+    import autoindexer_b200 as ab
+
+    rows, streams = make_rows(0)
     rope = ab.SectionedRope(D, THETA, [torch.as_tensor(s) for s in streams], SECTIONS, device=device)
     g = torch.Generator().manual_seed(seed)
     q = torch.randn(B, HQ, T, D, generator=g).to(torch.bfloat16)
@@ -129,6 +140,37 @@ def peaks():
         return 1590.0, 1400.0, "fallback"
 
 
+def max_over_ranks(t: float, world: int, device) -> float:
+    """The largest of the ranks' values (every rank calls it; world 1: t)."""
+    if world <= 1:
+        return t
+    import torch
+    import torch.distributed as dist
+
+    tt = torch.tensor([t], device=device, dtype=torch.float64)
+    dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    return float(tt.item())
+
+
+def sum_over_ranks(x: float, world: int, device) -> float:
+    """Sum of the ranks' values (every rank calls it; world 1: x)."""
+    if world <= 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    tt = torch.tensor([x], device=device, dtype=torch.float64)
+    dist.all_reduce(tt, op=dist.ReduceOp.SUM)
+    return float(tt.item())
+
+
+def job_tflops(job_flops_per_step: float, steps: int, t_max: float) -> float:
+    """Whole-job throughput: every rank processes its own seeded batch (weak
+    scaling), so the job's FLOPs per step are the sum over ranks; the job
+    takes as long as its slowest rank."""
+    return job_flops_per_step * steps / t_max / 1e12
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -144,6 +186,7 @@ def run_ours(args):
     dev = torch.device("cuda", local)
     if world > 1:
         from datetime import timedelta
+        os.environ.setdefault("NCCL_DEBUG", "WARN")  # keep stdout to the one JSON line
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
 
     rows, rope, _, host = make_workload(seed=rank, device=dev)
@@ -189,12 +232,9 @@ def run_ours(args):
     t_fwd = sum(a.elapsed_time(b) for a, b, _ in ev) / 1e3
     t_bwd = sum(b.elapsed_time(c) for _, b, c in ev) / 1e3
     t_step = t_fwd + t_bwd
-    t_max = t_step
-    if world > 1:
-        tt = torch.tensor([t_step], device=dev, dtype=torch.float64)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        t_max = float(tt.item())
-    value = world * flops * args.steps / t_max / 1e12
+    t_max = max_over_ranks(t_step, world, dev)
+    job_flops = sum_over_ranks(flops, world, dev)
+    value = job_tflops(job_flops, args.steps, t_max)
     ms_per_step = t_max / args.steps * 1e3
 
     # Per-kernel device times: the same steps again with the library's launch
@@ -237,12 +277,8 @@ def run_ours(args):
         e2e_step()
         e_ev[i][1].record(stream)
     torch.cuda.synchronize(dev)
-    t_e2e = sum(a.elapsed_time(b) for a, b in e_ev) / 1e3
-    if world > 1:
-        tt = torch.tensor([t_e2e], device=dev, dtype=torch.float64)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        t_e2e = float(tt.item())
-    e2e_value = world * flops * args.steps / t_e2e / 1e12
+    t_e2e = max_over_ranks(sum(a.elapsed_time(b) for a, b in e_ev) / 1e3, world, dev)
+    e2e_value = job_tflops(job_flops, args.steps, t_e2e)
     assert read_status(dev) == 0
 
     peak, peak_sus, peak_kind = peaks()
@@ -316,11 +352,16 @@ def cpu_baseline(rows, host, seed=0, reps=1):
     vs = v[:1, :1].float().numpy()
     dos = dout[:1, :, :G].float().numpy()
     pairs = O.count_pairs(lay, T)
-    t0 = time.perf_counter()
-    for _ in range(reps):
-        O.attn_forward(qs, ks, vs, lay, rope, dtype=np.float32)
-        O.attn_backward(qs, ks, vs, dos, lay, rope, dtype=np.float32)
-    dt = (time.perf_counter() - t0) / reps
+    # All host threads for the BLAS calls, also under torchrun (which sets
+    # OMP_NUM_THREADS=1 for its workers).
+    from threadpoolctl import threadpool_limits
+
+    with threadpool_limits(limits=os.cpu_count()):
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            O.attn_forward(qs, ks, vs, lay, rope, dtype=np.float32)
+            O.attn_backward(qs, ks, vs, dos, lay, rope, dtype=np.float32)
+        dt = (time.perf_counter() - t0) / reps
     flops = 14.0 * D * G * pairs
     return {"value": round(flops / dt / 1e12, 6), "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "port",
             "sample": f"batch row 0, kv group 0 ({G} query heads), T={T}: fwd+bwd, numpy fp32, {dt:.2f} s"}
