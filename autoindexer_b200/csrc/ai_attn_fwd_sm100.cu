@@ -349,15 +349,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
-// Warp-specialised forward for blocks without abs keys.
+// Warp-specialised forward for blocks without abs keys (fwd_pers_kernel).
 //
-// One CTA = one work item (block, <= 128 query rows) x two query heads of the
-// same GQA group, so every rotated K tile and every V tile feeds 256 query
+// Work unit = one work item (block, <= 128 query rows) x two query heads of
+// the same GQA group, so every rotated K tile and every V tile feeds 256 query
 // rows.  448 threads in roles:
 //   warps 0-3   softmax of head 2y     (thread = query row = TMEM lane)
 //   warps 4-7   softmax of head 2y + 1
 //   warp  8     TMA producer: K and V tiles into a 2-deep ring
-//   warp  9     MMA issuer (lane 0) and TMEM owner
+//   warp  9     MMA issuer and TMEM owner
 //   warps 10-13 rotate each K tile in place by its keys' block positions
 // TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512).
 // Softmax t reads S_t, writes P_t (bf16, two per column) over the first 64
@@ -375,22 +375,81 @@ namespace ws {
 constexpr int kThreads = 448;
 constexpr uint32_t Q0 = 0, Q1 = kTile, KB = 2 * kTile, VB = 4 * kTile;  // K ring at KB, V ring at VB
 constexpr uint32_t INFO = 6 * kTile;                                    // [2][128] u32
-constexpr uint32_t BARS = INFO + 2 * 4 * BN;
-enum Bar { KV_FULL = 0, K_READY = 2, KV_EMPTY = 4, S_FULL = 6, P_READY = 8, O_DONE = 10, Q_READY = 12, FINAL = 13,
-           N_BARS = 14 };
+constexpr uint32_t C_S0 = 0, C_S1 = 128, C_O0 = 256, C_O1 = 384;
+}  // namespace ws
+
+// ---------------------------------------------------------------------------
+// Persistent form of the warp-specialised forward: one CTA per SM walks the
+// work units u = blockIdx.x, blockIdx.x + gridDim.x, ... (unit = work item x
+// pair of query heads; items are longest first, so every CTA sees a
+// decreasing sequence).  Roles, tiles and shared-memory layout as in
+// fwd_ws_kernel; what carries across units:
+//   * tile barriers (K/V ring, S, P, O commits) count phases by the CTA's
+//     running tile index g, unit barriers by its running unit index k;
+//   * the next unit's Q tiles are loaded as soon as the current unit's last
+//     S MMAs are done (Q_EMPTY), and its K/V tiles stream into the ring
+//     behind the current unit's — the load latency of a unit start hides
+//     behind the end of the previous unit;
+//   * the first PV of a unit (accumulate = 0) overwrites O_t, so it waits
+//     until softmax group t has read the previous unit's O_t (O_FREE);
+//   * barriers, TMEM allocation and tensor-map prefetch happen once per CTA.
+// ---------------------------------------------------------------------------
+namespace pf {
+using ws::Q0;
+using ws::Q1;
+using ws::KB;
+using ws::VB;
+using ws::INFO;
+using ws::C_S0;
+using ws::C_S1;
+using ws::C_O0;
+using ws::C_O1;
+using ws::kThreads;
+// Output staging tile (128 rows x 128 bf16, 128-byte swizzle) for the TMA
+// store of a full unit; the two softmax groups take it in turn (OST0, OST1).
+constexpr uint32_t OSTAGE = INFO + 2 * 4 * BN;
+constexpr uint32_t BARS = OSTAGE + kTile;
+enum Bar { KV_FULL = 0, K_READY = 2, KV_EMPTY = 4, S_FULL = 6, P_READY = 8, O_DONE = 10, O_FREE = 12, Q_READY = 14,
+           Q_EMPTY = 15, OST0 = 16, OST1 = 17, FINAL = 18, N_BARS = 19 };
 constexpr uint32_t TMEM_SLOT = BARS + 8 * N_BARS;
 constexpr uint32_t ABORT = TMEM_SLOT + 4;
 constexpr uint32_t TOTAL = ABORT + 4;
 constexpr size_t kSmem = TOTAL + 1024;
-constexpr uint32_t C_S0 = 0, C_S1 = 128, C_O0 = 256, C_O1 = 384;
 constexpr long long kWait = 1000000000LL;
-}  // namespace ws
+static_assert(kSmem <= 227 * 1024, "shared memory budget");
 
-__global__ void __launch_bounds__(ws::kThreads, 1)
-    fwd_ws_kernel(const AiAttnFwdArgs a, const __grid_constant__ CUtensorMap tm_k,
-                  const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_qr,
-                  const __grid_constant__ CUtensorMap tm_kr, const int prerot) {
-  using namespace ws;
+// One work unit: rows [q0, q1) of a block x query heads 2 hp, 2 hp + 1.
+struct Unit {
+  Block blk;
+  int q0, q1, hp, hk, kv_lo, kv_hi, n;
+  bool masked, k_pre;
+};
+
+__device__ __forceinline__ Unit load_unit(const AiAttnFwdArgs& a, int u, int prerot) {
+  const AiAttnLayout& L = a.layout;
+  const int hpairs = a.num_q_heads / 2, G = a.num_q_heads / a.num_kv_heads;
+  const int32_t* item = L.fwd_items + 4 * (int64_t)(L.n_fwd_abs_items + u / hpairs);
+  Unit w;
+  w.blk = load_block(L.blocks, item[0]);
+  w.q0 = item[1];
+  w.q1 = item[2];
+  w.hp = u % hpairs;
+  w.hk = (2 * w.hp) / G;
+  w.kv_lo = w.blk.kv_lo;
+  w.kv_hi = min(w.blk.e, w.q1);
+  w.n = w.kv_hi > w.kv_lo ? (w.kv_hi - w.kv_lo + BN - 1) / BN : 0;
+  w.masked = (w.blk.flags & AI_BLOCKF_MASKED) != 0;
+  w.k_pre = prerot && (w.blk.flags & AI_BLOCKF_OWNPOS);
+  return w;
+}
+}  // namespace pf
+
+__global__ void __launch_bounds__(pf::kThreads, 1)
+    fwd_pers_kernel(const AiAttnFwdArgs a, const __grid_constant__ CUtensorMap tm_k,
+                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_qr,
+                    const __grid_constant__ CUtensorMap tm_kr, const __grid_constant__ CUtensorMap tm_o,
+                    const int prerot, const int n_units) {
+  using namespace pf;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = tile::align1024(smem_raw);
   const uint32_t sbase = ptx::smem_u32(sm);
@@ -398,34 +457,17 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
   uint32_t* s_info = reinterpret_cast<uint32_t*>(sm + INFO);
   volatile int* s_abort = reinterpret_cast<volatile int*>(sm + ABORT);
   auto bar = [&](int i) { return sbase + BARS + 8u * (uint32_t)i; };
-
   const AiAttnLayout& L = a.layout;
-  const int32_t* item = L.fwd_items + 4 * (int64_t)(L.n_fwd_abs_items + blockIdx.x);
-  const Block blk = load_block(L.blocks, item[0]);
-  const int q0 = item[1], q1 = item[2];
-  const int G = a.num_q_heads / a.num_kv_heads, hk = (2 * blockIdx.y) / G, b = blk.row;
-  const int kv_lo = blk.kv_lo, kv_hi = min(blk.e, q1);
-  const int n = kv_hi > kv_lo ? (kv_hi - kv_lo + BN - 1) / BN : 0;
-  const bool blk_masked = (blk.flags & AI_BLOCKF_MASKED) != 0;
-  // With the once-rotated copies: Q comes by TMA from q_rot, and K from k_rot
-  // when every key of this block has its own-block position.
-  const bool k_pre = prerot && (blk.flags & AI_BLOCKF_OWNPOS);
 
   if (tid == 0) {
-    ptx::mbar_init(bar(KV_FULL), 1);
-    ptx::mbar_init(bar(KV_FULL + 1), 1);
-    ptx::mbar_init(bar(K_READY), 128);
-    ptx::mbar_init(bar(K_READY + 1), 128);
-    ptx::mbar_init(bar(KV_EMPTY), 1);
-    ptx::mbar_init(bar(KV_EMPTY + 1), 1);
-    ptx::mbar_init(bar(S_FULL), 1);
-    ptx::mbar_init(bar(S_FULL + 1), 1);
-    ptx::mbar_init(bar(P_READY), 128);
-    ptx::mbar_init(bar(P_READY + 1), 128);
-    ptx::mbar_init(bar(O_DONE), 1);
-    ptx::mbar_init(bar(O_DONE + 1), 1);
-    ptx::mbar_init(bar(Q_READY), prerot ? 1 : 256);
-    ptx::mbar_init(bar(FINAL), 1);
+    for (int i = 0; i < N_BARS; ++i) {
+      uint32_t count = 1;
+      if (i == K_READY || i == K_READY + 1 || i == P_READY || i == P_READY + 1 || i == O_FREE || i == O_FREE + 1 ||
+          i == OST0 || i == OST1)
+        count = 128;
+      if (i == Q_READY) count = prerot ? 1 : 256;
+      ptx::mbar_init(bar(i), count);
+    }
     *s_abort = 0;
     ptx::fence_mbar_init();
   }
@@ -438,7 +480,6 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
   ptx::tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sm + TMEM_SLOT);
 
-  // Bounded wait; on expiry flag the CTA (every role then leaves its loop).
   auto wait = [&](int i, uint32_t parity) -> bool {
     if (*s_abort) return false;
     if (!ptx::mbar_wait(bar(i), parity, kWait)) {
@@ -451,150 +492,155 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
 
   if (warp < 8) {
     // ------------------------------------------------------------ softmax
-    const int t = warp / 4, r = tid % 128, i = q0 + r, h = 2 * blockIdx.y + t;
+    const int t = warp / 4, r = tid % 128;
     const uint32_t lane_base = (uint32_t)((warp % 4) * 32) << 16;
     const uint32_t c_s = t ? C_S1 : C_S0, c_o = t ? C_O1 : C_O0;
-    if (!prerot) {
-      // Query row i of head h, rotated by its position: all global loads of
-      // a half row are issued before any of it is rotated and stored.
-      const __nv_bfloat16* Qrow = static_cast<const __nv_bfloat16*>(a.q.ptr) + b * a.q.stride_b +
-                                  h * a.q.stride_h + (int64_t)i * a.q.stride_t;
-      int p = 0;
-      if (i < q1) p = clamp_row(L.q_pos[(int64_t)b * a.seq_len + i], L.n_pos, a.status);
-      const uint4* tab = reinterpret_cast<const uint4*>(static_cast<const __half2*>(L.rope_cs16) + (int64_t)p * (D / 2));
-      const uint32_t qt = t ? Q1 : Q0;
-#pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        uint4 x1[4], x2[4], cs[8];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const int cc = 4 * hf + c;
-          x1[c] = i < q1 ? __ldg(reinterpret_cast<const uint4*>(Qrow + 8 * cc)) : make_uint4(0, 0, 0, 0);
-          x2[c] = i < q1 ? __ldg(reinterpret_cast<const uint4*>(Qrow + 64 + 8 * cc)) : make_uint4(0, 0, 0, 0);
-          cs[2 * c] = __ldg(tab + 2 * cc);
-          cs[2 * c + 1] = __ldg(tab + 2 * cc + 1);
-        }
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const int cc = 4 * hf + c;
-          uint4 y1, y2;
-          tile::rotate8h(x1[c], x2[c], cs[2 * c], cs[2 * c + 1], y1, y2);
-          *reinterpret_cast<uint4*>(sm + qt + chunk_off(r, cc)) = y1;
-          *reinterpret_cast<uint4*>(sm + qt + chunk_off(r, cc + 8)) = y2;
-        }
-      }
-      ptx::fence_proxy_async_smem();
-      ptx::mbar_arrive(bar(Q_READY));
-    }
     const float sl2 = a.scale * kLog2e;
-    float m_use = -CUDART_INF_F, l = 0.f;
-    int done = 0;
-    for (int j = 0; j < n; ++j) {
-      const int slot = j & 1, k0 = kv_lo + j * BN;
-      if (!wait(S_FULL + t, j & 1)) break;
-      ptx::tc_fence_after();
-      // Scores are read from TMEM twice (max pass, then exp pass), 64 columns
-      // per load round, so that at most 64 scores are live in registers.
-      // Tiles wholly below the diagonal of a block without masked keys skip
-      // the mask; other tiles of such a block only need the causal / key-range
-      // limit (column c valid iff c <= lim); blocks with masked keys also test
-      // each key's info word.
-      const bool fast = !blk_masked && (k0 + BN <= kv_hi) && (k0 + BN - 1 <= q0);
-      const int lim = min(i - k0, kv_hi - 1 - k0);
-      const uint32_t* info = s_info + slot * BN;
-      auto load64 = [&](int hf, uint32_t (&r0)[32], uint32_t (&r1)[32]) {
-        ptx::tmem_ld32(tmem + lane_base + c_s + 64 * hf, r0);
-        ptx::tmem_ld32(tmem + lane_base + c_s + 64 * hf + 32, r1);
-        ptx::tmem_wait_ld();
-        if (!fast && !blk_masked) {
+    const float2 sl2x2 = make_float2(sl2, sl2);
+    int g = 0, k = 0;
+    for (int u = blockIdx.x; u < n_units && !*s_abort; u += gridDim.x, ++k) {
+      const Unit w = load_unit(a, u, prerot);
+      const int i = w.q0 + r, h = 2 * w.hp + t, b = w.blk.row;
+      if (!prerot) {
+        // Q rows of this unit (rotated): the previous unit's S MMAs must be
+        // done reading Q_t.
+        if (k > 0 && !wait(Q_EMPTY, (k - 1) & 1)) break;
+        const __nv_bfloat16* Qrow = static_cast<const __nv_bfloat16*>(a.q.ptr) + b * a.q.stride_b +
+                                    h * a.q.stride_h + (int64_t)i * a.q.stride_t;
+        int p = 0;
+        if (i < w.q1) p = clamp_row(L.q_pos[(int64_t)b * a.seq_len + i], L.n_pos, a.status);
+        const uint4* tab =
+            reinterpret_cast<const uint4*>(static_cast<const __half2*>(L.rope_cs16) + (int64_t)p * (D / 2));
+        const uint32_t qt = t ? Q1 : Q0;
 #pragma unroll
-          for (int x = 0; x < 32; ++x) {
-            const int c0 = 64 * hf + x, c1 = c0 + 32;
-            if (c0 > lim) r0[x] = 0xff800000u;  // -inf
-            if (c1 > lim) r1[x] = 0xff800000u;
+        for (int hf = 0; hf < 2; ++hf) {
+          uint4 x1[4], x2[4], cs[8];
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const int cc = 4 * hf + c;
+            x1[c] = i < w.q1 ? __ldg(reinterpret_cast<const uint4*>(Qrow + 8 * cc)) : make_uint4(0, 0, 0, 0);
+            x2[c] = i < w.q1 ? __ldg(reinterpret_cast<const uint4*>(Qrow + 64 + 8 * cc)) : make_uint4(0, 0, 0, 0);
+            cs[2 * c] = __ldg(tab + 2 * cc);
+            cs[2 * c + 1] = __ldg(tab + 2 * cc + 1);
           }
-        } else if (blk_masked) {
 #pragma unroll
-          for (int x = 0; x < 32; ++x) {
-            const int c0 = 64 * hf + x, c1 = c0 + 32;
-            if (!((info[c0] & AI_KEY_ATTN) && c0 <= lim)) r0[x] = 0xff800000u;
-            if (!((info[c1] & AI_KEY_ATTN) && c1 <= lim)) r1[x] = 0xff800000u;
+          for (int c = 0; c < 4; ++c) {
+            const int cc = 4 * hf + c;
+            uint4 y1, y2;
+            tile::rotate8h(x1[c], x2[c], cs[2 * c], cs[2 * c + 1], y1, y2);
+            *reinterpret_cast<uint4*>(sm + qt + chunk_off(r, cc)) = y1;
+            *reinterpret_cast<uint4*>(sm + qt + chunk_off(r, cc + 8)) = y2;
           }
         }
-      };
-      float mxa = -CUDART_INF_F, mxb = -CUDART_INF_F, mxc = -CUDART_INF_F, mxd = -CUDART_INF_F;
-#pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        uint32_t r0[32], r1[32];
-        load64(hf, r0, r1);
-#pragma unroll
-        for (int x = 0; x < 32; x += 2) {
-          mxa = fmaxf(mxa, __uint_as_float(r0[x]));
-          mxb = fmaxf(mxb, __uint_as_float(r0[x + 1]));
-          mxc = fmaxf(mxc, __uint_as_float(r1[x]));
-          mxd = fmaxf(mxd, __uint_as_float(r1[x + 1]));
-        }
+        ptx::fence_proxy_async_smem();
+        ptx::mbar_arrive(bar(Q_READY));
       }
-      const float mx = fmaxf(fmaxf(mxa, mxb), fmaxf(mxc, mxd));
-      const float m_new = fmaxf(m_use, mx * sl2);
-      float alpha = 1.f;
-      bool rescale = false;
-      if (m_new > m_use + 8.f) {
-        if (j > 0 && l > 0.f) {
-          alpha = ptx::ex2(m_use - m_new);
-          rescale = true;
-        }
-        m_use = m_new;
-      }
-      if (__any_sync(0xffffffffu, rescale)) {
-#pragma unroll
-        for (int cc = 0; cc < D / 32; ++cc) {
-          uint32_t rr[32];
-          ptx::tmem_ld32(tmem + lane_base + c_o + 32 * cc, rr);
+      float m_use = -CUDART_INF_F, l = 0.f;
+      int done = 0;
+      for (int j = 0; j < w.n; ++j) {
+        const int gj = g + j, slot = gj & 1, k0 = w.kv_lo + j * BN;
+        if (!wait(S_FULL + t, gj & 1)) break;
+        ptx::tc_fence_after();
+        const bool fast = !w.masked && (k0 + BN <= w.kv_hi) && (k0 + BN - 1 <= w.q0);
+        const int lim = min(i - k0, w.kv_hi - 1 - k0);
+        const uint32_t* info = s_info + slot * BN;
+        auto load64 = [&](int hf, uint32_t (&r0)[32], uint32_t (&r1)[32]) {
+          ptx::tmem_ld32(tmem + lane_base + c_s + 64 * hf, r0);
+          ptx::tmem_ld32(tmem + lane_base + c_s + 64 * hf + 32, r1);
           ptx::tmem_wait_ld();
+          if (!fast && !w.masked) {
 #pragma unroll
-          for (int x = 0; x < 32; ++x) rr[x] = __float_as_uint(__uint_as_float(rr[x]) * alpha);
-          ptx::tmem_st32(tmem + lane_base + c_o + 32 * cc, rr);
+            for (int x = 0; x < 32; ++x) {
+              const int c0 = 64 * hf + x, c1 = c0 + 32;
+              if (c0 > lim) r0[x] = 0xff800000u;  // -inf
+              if (c1 > lim) r1[x] = 0xff800000u;
+            }
+          } else if (w.masked) {
+#pragma unroll
+            for (int x = 0; x < 32; ++x) {
+              const int c0 = 64 * hf + x, c1 = c0 + 32;
+              if (!((info[c0] & AI_KEY_ATTN) && c0 <= lim)) r0[x] = 0xff800000u;
+              if (!((info[c1] & AI_KEY_ATTN) && c1 <= lim)) r1[x] = 0xff800000u;
+            }
+          }
+        };
+        float mxa = -CUDART_INF_F, mxb = -CUDART_INF_F, mxc = -CUDART_INF_F, mxd = -CUDART_INF_F;
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          uint32_t r0[32], r1[32];
+          load64(hf, r0, r1);
+#pragma unroll
+          for (int x = 0; x < 32; x += 2) {
+            mxa = fmaxf(mxa, __uint_as_float(r0[x]));
+            mxb = fmaxf(mxb, __uint_as_float(r0[x + 1]));
+            mxc = fmaxf(mxc, __uint_as_float(r1[x]));
+            mxd = fmaxf(mxd, __uint_as_float(r1[x + 1]));
+          }
         }
-      }
-      l *= alpha;
-      const float msub = m_use == -CUDART_INF_F ? 0.f : m_use;
-      // Exponent arguments and row sums on the packed f32x2 pipe.
-      const float2 sl2x2 = make_float2(sl2, sl2), nm2 = make_float2(-msub, -msub);
-      float2 suma = make_float2(0.f, 0.f), sumb = make_float2(0.f, 0.f);
-#pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        uint32_t r0[32], r1[32], pk[32];
-        load64(hf, r0, r1);
-#pragma unroll
-        for (int x = 0; x < 16; ++x) {
-          const float2 a01 =
-              __ffma2_rn(make_float2(__uint_as_float(r0[2 * x]), __uint_as_float(r0[2 * x + 1])), sl2x2, nm2);
-          const float2 a23 =
-              __ffma2_rn(make_float2(__uint_as_float(r1[2 * x]), __uint_as_float(r1[2 * x + 1])), sl2x2, nm2);
-          const float2 p01 = make_float2(ptx::ex2(a01.x), ptx::ex2(a01.y));
-          const float2 p23 = make_float2(ptx::ex2(a23.x), ptx::ex2(a23.y));
-          suma = __fadd2_rn(suma, p01);
-          sumb = __fadd2_rn(sumb, p23);
-          pk[x] = tile::pack2(p01.x, p01.y);
-          pk[16 + x] = tile::pack2(p23.x, p23.y);
+        const float mx = fmaxf(fmaxf(mxa, mxb), fmaxf(mxc, mxd));
+        const float m_new = fmaxf(m_use, mx * sl2);
+        float alpha = 1.f;
+        bool rescale = false;
+        if (m_new > m_use + 8.f) {
+          if (j > 0 && l > 0.f) {
+            alpha = ptx::ex2(m_use - m_new);
+            rescale = true;
+          }
+          m_use = m_new;
         }
-        ptx::tmem_st32(tmem + lane_base + c_s + 32 * hf, pk);
+        if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll
+          for (int cc = 0; cc < D / 32; ++cc) {
+            uint32_t rr[32];
+            ptx::tmem_ld32(tmem + lane_base + c_o + 32 * cc, rr);
+            ptx::tmem_wait_ld();
+#pragma unroll
+            for (int x = 0; x < 32; ++x) rr[x] = __float_as_uint(__uint_as_float(rr[x]) * alpha);
+            ptx::tmem_st32(tmem + lane_base + c_o + 32 * cc, rr);
+          }
+        }
+        l *= alpha;
+        const float msub = m_use == -CUDART_INF_F ? 0.f : m_use;
+        const float2 nm2 = make_float2(-msub, -msub);
+        float2 suma = make_float2(0.f, 0.f), sumb = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          uint32_t r0[32], r1[32], pk[32];
+          load64(hf, r0, r1);
+#pragma unroll
+          for (int x = 0; x < 16; ++x) {
+            const float2 a01 =
+                __ffma2_rn(make_float2(__uint_as_float(r0[2 * x]), __uint_as_float(r0[2 * x + 1])), sl2x2, nm2);
+            const float2 a23 =
+                __ffma2_rn(make_float2(__uint_as_float(r1[2 * x]), __uint_as_float(r1[2 * x + 1])), sl2x2, nm2);
+            const float2 p01 = make_float2(ptx::ex2(a01.x), ptx::ex2(a01.y));
+            const float2 p23 = make_float2(ptx::ex2(a23.x), ptx::ex2(a23.y));
+            suma = __fadd2_rn(suma, p01);
+            sumb = __fadd2_rn(sumb, p23);
+            pk[x] = tile::pack2(p01.x, p01.y);
+            pk[16 + x] = tile::pack2(p23.x, p23.y);
+          }
+          ptx::tmem_st32(tmem + lane_base + c_s + 32 * hf, pk);
+        }
+        l += (suma.x + suma.y) + (sumb.x + sumb.y);
+        ptx::tmem_wait_st();
+        ptx::tc_fence_before();
+        ptx::mbar_arrive(bar(P_READY + t));
+        done = j + 1;
       }
-      l += (suma.x + suma.y) + (sumb.x + sumb.y);
-      ptx::tmem_wait_st();
-      ptx::tc_fence_before();
-      ptx::mbar_arrive(bar(P_READY + t));
-      done = j + 1;
-    }
-    // Epilogue: O_t / l.
-    bool have_o = false;
-    if (done == n && n > 0) have_o = wait(O_DONE + t, (n - 1) & 1);
-    if (!*s_abort) {
+      if (done != w.n) break;
+      // Epilogue: O_t / l.  O_t is read into registers, then released to the
+      // next unit's first PV before the global stores.
+      bool have_o = false;
+      if (w.n > 0) {
+        have_o = wait(O_DONE + t, (g + w.n - 1) & 1);
+        if (!have_o) break;
+      }
       ptx::tc_fence_after();
       __nv_bfloat16* Orow = static_cast<__nv_bfloat16*>(a.out.ptr) + b * a.out.stride_b + h * a.out.stride_h +
                             (int64_t)i * a.out.stride_t;
       const float inv = l > 0.f ? 1.f / l : 0.f;
+      uint4 packed[D / 8];
 #pragma unroll
       for (int cc = 0; cc < D / 32; ++cc) {
         uint32_t rr[32];
@@ -605,48 +651,90 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
 #pragma unroll
           for (int x = 0; x < 32; ++x) rr[x] = 0u;
         }
-        if (i < q1) {
 #pragma unroll
-          for (int c8 = 0; c8 < 4; ++c8) {
-            float f[8];
+        for (int c8 = 0; c8 < 4; ++c8) {
+          float fo[8];
 #pragma unroll
-            for (int x = 0; x < 8; ++x) f[x] = __uint_as_float(rr[8 * c8 + x]) * inv;
-            *reinterpret_cast<uint4*>(Orow + 32 * cc + 8 * c8) = pack8(f);
-          }
+          for (int x = 0; x < 8; ++x) fo[x] = __uint_as_float(rr[8 * c8 + x]) * inv;
+          packed[4 * cc + c8] = pack8(fo);
         }
       }
-      if (i < q1)
+      ptx::tc_fence_before();
+      ptx::mbar_arrive(bar(O_FREE + t));
+      // Output rows: a full unit goes through the staging tile and one TMA
+      // store per 64-column block (coalesced, asynchronous); a unit whose
+      // item ends early is stored row by row (the TMA box would spill into
+      // the next block's rows).  Group 0 then group 1 use the tile; every
+      // thread of both groups takes part in the hand-off of every unit (all
+      // 128 arrive, thread 0 once its TMA store has read the tile), so that
+      // no thread can still be waiting on a phase the other group has
+      // already moved past.
+      const bool full = w.q1 == w.q0 + BM;
+      bool ok_st = t == 0 ? (k == 0 || wait(OST1, (k - 1) & 1)) : wait(OST0, k & 1);
+      if (!ok_st) break;
+      if (full) {
+#pragma unroll
+        for (int c = 0; c < D / 8; ++c) *reinterpret_cast<uint4*>(sm + OSTAGE + chunk_off(r, c)) = packed[c];
+        ptx::fence_proxy_async_smem();
+        ptx::named_bar_sync(1 + t, 128);
+        if (r == 0) {
+          ptx::tma_store_4d(&tm_o, sbase + OSTAGE, 0, w.q0, h, b);
+          ptx::tma_store_4d(&tm_o, sbase + OSTAGE + kHalf, 64, w.q0, h, b);
+          ptx::bulk_commit_group();
+          ptx::bulk_wait_read_all();
+        }
+      } else if (i < w.q1) {
+#pragma unroll
+        for (int c = 0; c < D / 8; ++c) *reinterpret_cast<uint4*>(Orow + 8 * c) = packed[c];
+      }
+      ptx::mbar_arrive(bar(OST0 + t));
+      if (i < w.q1)
         a.lse[((int64_t)b * a.num_q_heads + h) * a.seq_len + i] = l > 0.f ? (m_use + log2f(l)) * kLn2 : -CUDART_INF_F;
+      g += w.n;
     }
+    if (r == 0) ptx::bulk_wait_all();  // this thread's output stores have landed
   } else if (warp == 8) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      const CUtensorMap* mk = k_pre ? &tm_kr : &tm_k;
-      ptx::prefetch_tmap(mk);
+      ptx::prefetch_tmap(&tm_k);
       ptx::prefetch_tmap(&tm_v);
       if (prerot) {
-        const int h0 = 2 * blockIdx.y;
-        ptx::mbar_arrive_expect_tx(bar(Q_READY), 2 * kTile);
-        ptx::tma_load_4d(sbase + Q0, &tm_qr, bar(Q_READY), 0, q0, h0, b);
-        ptx::tma_load_4d(sbase + Q0 + kHalf, &tm_qr, bar(Q_READY), 64, q0, h0, b);
-        ptx::tma_load_4d(sbase + Q1, &tm_qr, bar(Q_READY), 0, q0, h0 + 1, b);
-        ptx::tma_load_4d(sbase + Q1 + kHalf, &tm_qr, bar(Q_READY), 64, q0, h0 + 1, b);
+        ptx::prefetch_tmap(&tm_qr);
+        ptx::prefetch_tmap(&tm_kr);
       }
-      for (int j = 0; j < n; ++j) {
-        const int slot = j & 1, k0 = kv_lo + j * BN;
-        if (j >= 2 && !wait(KV_EMPTY + slot, ((j >> 1) - 1) & 1)) break;
-        const uint32_t kb = sbase + KB + (uint32_t)slot * kTile, vb = sbase + VB + (uint32_t)slot * kTile;
-        ptx::mbar_arrive_expect_tx(bar(KV_FULL + slot), 2 * kTile);
-        ptx::tma_load_4d(kb, mk, bar(KV_FULL + slot), 0, k0, hk, b);
-        ptx::tma_load_4d(kb + kHalf, mk, bar(KV_FULL + slot), 64, k0, hk, b);
-        ptx::tma_load_4d(vb, &tm_v, bar(KV_FULL + slot), 0, k0, hk, b);
-        ptx::tma_load_4d(vb + kHalf, &tm_v, bar(KV_FULL + slot), 64, k0, hk, b);
+      int g = 0, k = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x, ++k) {
+        const Unit w = load_unit(a, u, prerot);
+        const int b = w.blk.row;
+        if (prerot) {
+          if (k > 0 && !wait(Q_EMPTY, (k - 1) & 1)) break;
+          const int h0 = 2 * w.hp;
+          ptx::mbar_arrive_expect_tx(bar(Q_READY), 2 * kTile);
+          ptx::tma_load_4d(sbase + Q0, &tm_qr, bar(Q_READY), 0, w.q0, h0, b);
+          ptx::tma_load_4d(sbase + Q0 + kHalf, &tm_qr, bar(Q_READY), 64, w.q0, h0, b);
+          ptx::tma_load_4d(sbase + Q1, &tm_qr, bar(Q_READY), 0, w.q0, h0 + 1, b);
+          ptx::tma_load_4d(sbase + Q1 + kHalf, &tm_qr, bar(Q_READY), 64, w.q0, h0 + 1, b);
+        }
+        const CUtensorMap* mk = w.k_pre ? &tm_kr : &tm_k;
+        for (int j = 0; j < w.n; ++j, ++g) {
+          const int slot = g & 1, k0 = w.kv_lo + j * BN;
+          if (g >= 2 && !wait(KV_EMPTY + slot, ((g >> 1) - 1) & 1)) {
+            ok = false;
+            break;
+          }
+          const uint32_t kb = sbase + KB + (uint32_t)slot * kTile, vb = sbase + VB + (uint32_t)slot * kTile;
+          ptx::mbar_arrive_expect_tx(bar(KV_FULL + slot), 2 * kTile);
+          ptx::tma_load_4d(kb, mk, bar(KV_FULL + slot), 0, k0, w.hk, b);
+          ptx::tma_load_4d(kb + kHalf, mk, bar(KV_FULL + slot), 64, k0, w.hk, b);
+          ptx::tma_load_4d(vb, &tm_v, bar(KV_FULL + slot), 0, k0, w.hk, b);
+          ptx::tma_load_4d(vb + kHalf, &tm_v, bar(KV_FULL + slot), 64, k0, w.hk, b);
+        }
       }
     }
   } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
-    // The whole warp runs this loop (descriptors stay warp-uniform); one
-    // elected lane issues each MMA and commit.  Lane 0's wait result decides.
+    // Whole warp (warp-uniform descriptors); one elected lane issues.
     auto wait_u = [&](int i, uint32_t parity) -> bool { return __shfl_sync(0xffffffffu, wait(i, parity), 0); };
     constexpr uint32_t idesc_qk = ptx::idesc_bf16_f32(BM, BN, false, false);
     constexpr uint32_t idesc_pv = ptx::idesc_bf16_f32(BM, D, false, true);
@@ -670,75 +758,92 @@ __global__ void __launch_bounds__(ws::kThreads, 1)
       }
       ptx::mma_commit_w(bar(O_DONE + t));
     };
-    bool ok = wait_u(Q_READY, 0);
-    if (ok && n > 0 && wait_u(K_READY, 0)) {
+    int g = 0, k = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x, ++k) {
+      const Unit w = load_unit(a, u, prerot);
+      if (!wait_u(Q_READY, k & 1)) break;
+      if (w.n == 0) {
+        ptx::mma_commit_w(bar(Q_EMPTY));
+        continue;
+      }
+      if (!wait_u(K_READY + (g & 1), (g >> 1) & 1)) break;
       ptx::tc_fence_after();
-      issue_s(0, 0);
-      issue_s(1, 0);
-      for (int j = 0; j < n; ++j) {
-        const int slot = j & 1, nslot = (j + 1) & 1;
-        const bool more = j + 1 < n;
-        if (!wait_u(P_READY, j & 1)) break;
+      issue_s(0, g & 1);
+      issue_s(1, g & 1);
+      if (w.n == 1) ptx::mma_commit_w(bar(Q_EMPTY));  // the unit's last reads of Q
+      for (int j = 0; j < w.n; ++j) {
+        const int gj = g + j, slot = gj & 1, nslot = (gj + 1) & 1;
+        const bool more = j + 1 < w.n;
+        if (!wait_u(P_READY, gj & 1) || (j == 0 && k > 0 && !wait_u(O_FREE, (k - 1) & 1))) {
+          ok = false;
+          break;
+        }
         ptx::tc_fence_after();
         issue_pv(0, slot, j == 0);
         if (more) {
-          if (!wait_u(K_READY + nslot, ((j + 1) >> 1) & 1)) break;
+          if (!wait_u(K_READY + nslot, ((gj + 1) >> 1) & 1)) {
+            ok = false;
+            break;
+          }
           ptx::tc_fence_after();
           issue_s(0, nslot);
         }
-        if (!wait_u(P_READY + 1, j & 1)) break;
+        if (!wait_u(P_READY + 1, gj & 1) || (j == 0 && k > 0 && !wait_u(O_FREE + 1, (k - 1) & 1))) {
+          ok = false;
+          break;
+        }
         ptx::tc_fence_after();
         issue_pv(1, slot, j == 0);
         ptx::mma_commit_w(bar(KV_EMPTY + slot));
-        if (more) issue_s(1, nslot);
+        if (more) {
+          issue_s(1, nslot);
+          if (j + 2 == w.n) ptx::mma_commit_w(bar(Q_EMPTY));
+        }
       }
+      g += w.n;
     }
     // Drain: every MMA issued so far has completed before TMEM is released.
     ptx::mma_commit_w(bar(FINAL));
     ptx::mbar_wait(bar(FINAL), 0, kWait);
   } else {
     // ------------------------------------------------------------ K rotation (warps 10-13)
-    // Thread = key row of the tile.  The key's position word and its fp16
-    // (cos, sin) row are fetched for tile j+1 while tile j is rotated, so the
-    // L2 latency hides behind the wait for the next TMA.
     const int row = tid - 320;
     const __half2* cs16 = static_cast<const __half2*>(L.rope_cs16);
-    uint32_t info = 0;
-    uint4 tab[16];
-    auto fetch = [&](int j) {
-      const int key = kv_lo + j * BN + row;
-      info = 0;
-      int p = 0;
-      if (key < kv_hi) {
-        info = (uint32_t)__ldg(L.key_info + blk.key_off + key);
-        p = key_row(info, L.n_pos, a.status);
-      }
-      if (!k_pre) {
-        const uint4* tp = reinterpret_cast<const uint4*>(cs16 + (int64_t)p * (D / 2));
-#pragma unroll
-        for (int c = 0; c < 16; ++c) tab[c] = __ldg(tp + c);
-      }
-    };
-    if (n > 0) fetch(0);
-    for (int j = 0; j < n; ++j) {
-      const int slot = j & 1;
-      if (!wait(KV_FULL + slot, (j >> 1) & 1)) break;
-      const uint32_t kt = KB + (uint32_t)slot * kTile;
-      if (!k_pre && kv_lo + j * BN + row < kv_hi) {
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          uint4* pa = reinterpret_cast<uint4*>(sm + kt + chunk_off(row, c));
-          uint4* pb = reinterpret_cast<uint4*>(sm + kt + chunk_off(row, c + 8));
-          uint4 y1, y2;
-          tile::rotate8h(*pa, *pb, tab[2 * c], tab[2 * c + 1], y1, y2);
-          *pa = y1;
-          *pb = y2;
+    int g = 0;
+    for (int u = blockIdx.x; u < n_units && !*s_abort; u += gridDim.x) {
+      const Unit w = load_unit(a, u, prerot);
+      for (int j = 0; j < w.n; ++j, ++g) {
+        const int slot = g & 1, key = w.kv_lo + j * BN + row;
+        uint32_t info = 0;
+        int p = 0;
+        if (key < w.kv_hi) {
+          info = (uint32_t)__ldg(L.key_info + w.blk.key_off + key);
+          p = key_row(info, L.n_pos, a.status);
         }
+        uint4 tab[16];
+        if (!w.k_pre) {
+          const uint4* tp = reinterpret_cast<const uint4*>(cs16 + (int64_t)p * (D / 2));
+#pragma unroll
+          for (int c = 0; c < 16; ++c) tab[c] = __ldg(tp + c);
+        }
+        if (!wait(KV_FULL + slot, (g >> 1) & 1)) break;
+        const uint32_t kt = KB + (uint32_t)slot * kTile;
+        if (!w.k_pre && key < w.kv_hi) {
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            uint4* pa = reinterpret_cast<uint4*>(sm + kt + chunk_off(row, c));
+            uint4* pb = reinterpret_cast<uint4*>(sm + kt + chunk_off(row, c + 8));
+            uint4 y1, y2;
+            tile::rotate8h(*pa, *pb, tab[2 * c], tab[2 * c + 1], y1, y2);
+            *pa = y1;
+            *pb = y2;
+          }
+        }
+        s_info[slot * BN + row] = info;
+        ptx::fence_proxy_async_smem();
+        ptx::mbar_arrive(bar(K_READY + slot));
       }
-      s_info[slot * BN + row] = info;
-      ptx::fence_proxy_async_smem();
-      ptx::mbar_arrive(bar(K_READY + slot));
-      if (j + 1 < n) fetch(j + 1);
     }
   }
 
@@ -827,11 +932,18 @@ int sm100_fwd(const AiAttnFwdArgs& a, cudaStream_t st, cudaError_t* cuda_err) {
       if (pre && (!sm100_make_map(&tm_qr, qr, a.batch, a.num_q_heads, a.seq_len, BM) ||
                   !sm100_make_map(&tm_kr, kr, a.batch, a.num_kv_heads, a.seq_len, BN)))
         return AI_ERR_TMA;
-      e = cudaFuncSetAttribute(fwd_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ws::kSmem);
+      // Persistent: one CTA per SM walks the (item, head pair) units.
+      const int n_units = n_pair * (a.num_q_heads / 2);
+      int dev = 0, sms = 148;
+      if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+      const int grid = n_units < sms ? n_units : sms;
+      CUtensorMap tm_o;
+      if (!sm100_make_map(&tm_o, a.out, a.batch, a.num_q_heads, a.seq_len, BM)) return AI_ERR_TMA;
+      e = cudaFuncSetAttribute(fwd_pers_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pf::kSmem);
       if (e == cudaSuccess) {
         ProfScope ps(AI_PROF_FWD, st);
-        fwd_ws_kernel<<<dim3(n_pair, a.num_q_heads / 2), ws::kThreads, ws::kSmem, st>>>(a, tm_k, tm_v, tm_qr, tm_kr,
-                                                                                        pre ? 1 : 0);
+        fwd_pers_kernel<<<grid, pf::kThreads, pf::kSmem, st>>>(a, tm_k, tm_v, tm_qr, tm_kr, tm_o, pre ? 1 : 0,
+                                                                n_units);
         e = cudaGetLastError();
       }
     }
