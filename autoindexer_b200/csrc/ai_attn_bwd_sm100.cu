@@ -737,26 +737,71 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ===========================================================================
 namespace dqw {
 constexpr int BM = 128, BN = 64, kThreads = 448;
-constexpr int kKS = 3;  // K / V ring depth (the refill of tile j + kKS starts when tile j is done)
+constexpr int kKS = 3;  // K / V ring depth (the refill of tile g + kKS starts when tile g is done)
 constexpr uint32_t Q0 = 0, Q1 = 32768, DO0 = 65536, DO1 = 98304;  // 128 x 128 bf16 each
-constexpr uint32_t KB = 131072, VB = KB + kKS * 16384;            // rings of 64 x 128 bf16
+constexpr uint32_t KB = 131072, VB = KB + kKS * 16384;            // rings of kKS x (64 x 128 bf16)
 constexpr uint32_t INFO = VB + kKS * 16384;                       // [kKS][64] u32
 constexpr uint32_t BARS = INFO + kKS * 4 * BN;
 enum Bar { KV_FULL = 0, K_READY = kKS, KV_EMPTY = 2 * kKS, S_FULL = 3 * kKS, DS_READY = S_FULL + 2,
-           DQ_DONE = DS_READY + 2, Q_READY = DQ_DONE + 2, FINAL, N_BARS };
+           DQ_DONE = DS_READY + 2, DQ_FREE = DQ_DONE + 2, Q_READY = DQ_FREE + 2, Q_EMPTY, FINAL, N_BARS };
 constexpr uint32_t TMEM_SLOT = BARS + 8 * N_BARS;
 constexpr uint32_t ABORT = TMEM_SLOT + 4;
 constexpr uint32_t TOTAL = ABORT + 4;
 constexpr size_t kSmem = TOTAL + 1024;
 static_assert(kSmem <= 227 * 1024, "shared memory budget");
 constexpr long long kWait = 1000000000LL;
+
+// One work unit: rows [q0, q1) of a block x query heads 2 hp, 2 hp + 1.
+struct Unit {
+  Block blk;
+  int q0, q1, hp, hk, kv_lo, kv_hi, n;
+  bool masked, k_pre;
+};
+
+__device__ __forceinline__ Unit load_unit(const AiAttnFwdArgs& f, int u, int prerot) {
+  const AiAttnLayout& L = f.layout;
+  const int hpairs = f.num_q_heads / 2, G = f.num_q_heads / f.num_kv_heads;
+  const int32_t* item = L.fwd_items + 4 * (int64_t)(L.n_fwd_abs_items + u / hpairs);
+  Unit w;
+  w.blk = load_block(L.blocks, item[0]);
+  w.q0 = item[1];
+  w.q1 = item[2];
+  w.hp = u % hpairs;
+  w.hk = (2 * w.hp) / G;
+  w.kv_lo = w.blk.kv_lo;
+  w.kv_hi = min(w.blk.e, w.q1);
+  w.n = w.kv_hi > w.kv_lo ? (w.kv_hi - w.kv_lo + BN - 1) / BN : 0;
+  w.masked = (w.blk.flags & AI_BLOCKF_MASKED) != 0;
+  w.k_pre = prerot && (w.blk.flags & AI_BLOCKF_OWNPOS);
+  return w;
+}
 }  // namespace dqw
 
+// ===========================================================================
+// dQ, warp-specialised and persistent (work items of blocks without abs keys)
+//
+// One CTA per SM walks the work units u = blockIdx.x, blockIdx.x + gridDim.x,
+// ... (unit = forward work item x two query heads of one GQA group; items
+// longest first).  448 threads: warps 0-3 / 4-7 score groups of heads 2 hp /
+// 2 hp + 1 (thread = query row = TMEM lane); warp 8 TMA producer (64-key K and
+// V tiles, 3-deep ring); warp 9 MMA issuer; warps 10-13 rotate each K tile by
+// the keys' block positions.  TMEM per head t: S_t [128t .. +64), dP_t
+// [+64 .. +128), dQ_t accumulator [256 + 128t .. +128).  dS_t (bf16 pairs)
+// overwrites the first 32 columns of S_t and is the A operand of dQ_t +=
+// dS_t.Krot; the next S_t follows that MMA directly (MMAs of one thread
+// execute in issue order).  MMA order per key tile j: dQ0(j), S0/dP0(j+1),
+// dQ1(j), S1/dP1(j+1).  The MMA warp runs converged and elects one lane per
+// MMA.  Across units (as in the persistent forward): tile barriers count by
+// the running tile index, unit barriers by the running unit index; the next
+// unit's Q / dO load starts once the current unit's last S / dP MMAs are done
+// (Q_EMPTY); a unit's first dQ MMA waits until the previous unit's dQ_t has
+// been read (DQ_FREE).
+// ===========================================================================
 __global__ void __launch_bounds__(dqw::kThreads, 1)
-    dq_ws_kernel(const AiAttnBwdArgs a, const float* __restrict__ delta, const __grid_constant__ CUtensorMap tm_k,
-                 const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_qr,
-                 const __grid_constant__ CUtensorMap tm_do, const __grid_constant__ CUtensorMap tm_kr,
-                 const int prerot) {
+    dq_pers_kernel(const AiAttnBwdArgs a, const float* __restrict__ delta, const __grid_constant__ CUtensorMap tm_k,
+                   const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_qr,
+                   const __grid_constant__ CUtensorMap tm_do, const __grid_constant__ CUtensorMap tm_kr,
+                   const int prerot, const int n_units) {
   using namespace dqw;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = tile::align1024(smem_raw);
@@ -768,20 +813,14 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
 
   const AiAttnFwdArgs& f = a.fwd;
   const AiAttnLayout& L = f.layout;
-  const int32_t* item = L.fwd_items + 4 * (int64_t)(L.n_fwd_abs_items + blockIdx.x);
-  const Block blk = load_block(L.blocks, item[0]);
-  const int q0 = item[1], q1 = item[2];
-  const int G = f.num_q_heads / f.num_kv_heads, hk = (2 * blockIdx.y) / G, b = blk.row;
-  const int kv_lo = blk.kv_lo, kv_hi = min(blk.e, q1);
-  const int n = kv_hi > kv_lo ? (kv_hi - kv_lo + BN - 1) / BN : 0;
-  const bool blk_masked = (blk.flags & AI_BLOCKF_MASKED) != 0;
   const __half2* cs16 = static_cast<const __half2*>(L.rope_cs16);
-  const bool k_pre = prerot && (blk.flags & AI_BLOCKF_OWNPOS);
 
   if (tid == 0) {
     for (int i = 0; i < N_BARS; ++i) {
       uint32_t count = 1;
-      if ((i >= K_READY && i < K_READY + kKS) || i == DS_READY || i == DS_READY + 1) count = 128;
+      if ((i >= K_READY && i < K_READY + kKS) || i == DS_READY || i == DS_READY + 1 || i == DQ_FREE ||
+          i == DQ_FREE + 1)
+        count = 128;
       if (i == Q_READY) count = prerot ? 1 : 256;
       ptx::mbar_init(bar(i), count);
     }
@@ -809,118 +848,126 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
 
   if (warp < 8) {
     // ------------------------------------------------------------ score groups
-    const int t = warp / 4, r = tid % 128, i = q0 + r, h = 2 * blockIdx.y + t;
+    const int t = warp / 4, r = tid % 128;
     const uint32_t lane_base = (uint32_t)((warp % 4) * 32) << 16;
     const uint32_t c_s = 128u * (uint32_t)t, c_dq = 256u + 128u * (uint32_t)t;
-    int qrow = 0;
-    float lse2 = 0.f, dl = 0.f;
-    {
-      const __nv_bfloat16* Qrow = static_cast<const __nv_bfloat16*>(f.q.ptr) + b * f.q.stride_b + h * f.q.stride_h +
-                                  (int64_t)i * f.q.stride_t;
-      const __nv_bfloat16* dOrow = static_cast<const __nv_bfloat16*>(a.dout.ptr) + b * a.dout.stride_b +
-                                   h * a.dout.stride_h + (int64_t)i * a.dout.stride_t;
+    const float sl2 = f.scale * kLog2e, scale = f.scale;
+    const float2 sl2x2 = make_float2(sl2, sl2), scalex2 = make_float2(scale, scale);
+    int g = 0, k = 0;
+    for (int u = snake_unit(k); u < n_units && !*s_abort; u = snake_unit(++k)) {
+      const Unit w = load_unit(f, u, prerot);
+      const int i = w.q0 + r, h = 2 * w.hp + t, b = w.blk.row, q1 = w.q1;
+      int qrow = 0;
+      float lse2 = 0.f, dl = 0.f;
       if (i < q1) {
         qrow = clamp_row(L.q_pos[(int64_t)b * f.seq_len + i], L.n_pos, f.status);
         const int64_t idx = ((int64_t)b * f.num_q_heads + h) * f.seq_len + i;
         lse2 = lse_log2(f.lse[idx]);
         dl = delta[idx];
       }
-      const uint4* tab = reinterpret_cast<const uint4*>(cs16 + (int64_t)qrow * (D / 2));
-      const uint32_t qt = t ? Q1 : Q0, ot = t ? DO1 : DO0;
-      // With the once-rotated copies the producer brings Q and dO by TMA.
-#pragma unroll
-      for (int hf = 0; hf < (prerot ? 0 : 2); ++hf) {
-        uint4 x1[4], x2[4], g1[4], g2[4], cs[8];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const int cc = 4 * hf + c;
-          const uint4 z = make_uint4(0, 0, 0, 0);
-          x1[c] = i < q1 ? __ldg(reinterpret_cast<const uint4*>(Qrow + 8 * cc)) : z;
-          x2[c] = i < q1 ? __ldg(reinterpret_cast<const uint4*>(Qrow + 64 + 8 * cc)) : z;
-          g1[c] = i < q1 ? __ldg(reinterpret_cast<const uint4*>(dOrow + 8 * cc)) : z;
-          g2[c] = i < q1 ? __ldg(reinterpret_cast<const uint4*>(dOrow + 64 + 8 * cc)) : z;
-          cs[2 * c] = __ldg(tab + 2 * cc);
-          cs[2 * c + 1] = __ldg(tab + 2 * cc + 1);
-        }
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const int cc = 4 * hf + c;
-          uint4 y1, y2;
-          tile::rotate8h(x1[c], x2[c], cs[2 * c], cs[2 * c + 1], y1, y2);
-          *reinterpret_cast<uint4*>(sm + qt + chunk_off<BM>(r, cc)) = y1;
-          *reinterpret_cast<uint4*>(sm + qt + chunk_off<BM>(r, cc + 8)) = y2;
-          *reinterpret_cast<uint4*>(sm + ot + chunk_off<BM>(r, cc)) = g1[c];
-          *reinterpret_cast<uint4*>(sm + ot + chunk_off<BM>(r, cc + 8)) = g2[c];
-        }
-      }
       if (!prerot) {
+        // Q rows (rotated) and dO rows of this unit into shared memory, once
+        // the previous unit's S / dP MMAs are done reading them.
+        if (k > 0 && !wait(Q_EMPTY, (k - 1) & 1)) break;
+        const __nv_bfloat16* Qrow = static_cast<const __nv_bfloat16*>(f.q.ptr) + b * f.q.stride_b +
+                                    h * f.q.stride_h + (int64_t)i * f.q.stride_t;
+        const __nv_bfloat16* dOrow = static_cast<const __nv_bfloat16*>(a.dout.ptr) + b * a.dout.stride_b +
+                                     h * a.dout.stride_h + (int64_t)i * a.dout.stride_t;
+        const uint4* tab = reinterpret_cast<const uint4*>(cs16 + (int64_t)qrow * (D / 2));
+        const uint32_t qt = t ? Q1 : Q0, ot = t ? DO1 : DO0;
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          uint4 x1[4], x2[4], g1[4], g2[4], cs[8];
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const int cc = 4 * hf + c;
+            const uint4 z = make_uint4(0, 0, 0, 0);
+            x1[c] = i < q1 ? __ldg(reinterpret_cast<const uint4*>(Qrow + 8 * cc)) : z;
+            x2[c] = i < q1 ? __ldg(reinterpret_cast<const uint4*>(Qrow + 64 + 8 * cc)) : z;
+            g1[c] = i < q1 ? __ldg(reinterpret_cast<const uint4*>(dOrow + 8 * cc)) : z;
+            g2[c] = i < q1 ? __ldg(reinterpret_cast<const uint4*>(dOrow + 64 + 8 * cc)) : z;
+            cs[2 * c] = __ldg(tab + 2 * cc);
+            cs[2 * c + 1] = __ldg(tab + 2 * cc + 1);
+          }
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const int cc = 4 * hf + c;
+            uint4 y1, y2;
+            tile::rotate8h(x1[c], x2[c], cs[2 * c], cs[2 * c + 1], y1, y2);
+            *reinterpret_cast<uint4*>(sm + qt + chunk_off<BM>(r, cc)) = y1;
+            *reinterpret_cast<uint4*>(sm + qt + chunk_off<BM>(r, cc + 8)) = y2;
+            *reinterpret_cast<uint4*>(sm + ot + chunk_off<BM>(r, cc)) = g1[c];
+            *reinterpret_cast<uint4*>(sm + ot + chunk_off<BM>(r, cc + 8)) = g2[c];
+          }
+        }
         ptx::fence_proxy_async_smem();
         ptx::mbar_arrive(bar(Q_READY));
       }
-    }
-    const float sl2 = f.scale * kLog2e, scale = f.scale;
-    // Rows past q1 (another block's rows) get lse = +inf: their P is 0 with no
-    // per-element test on the unmasked path.
-    const float lse2r = i < q1 ? lse2 : CUDART_INF_F, dls = dl * scale;
-    const float2 sl2x2 = make_float2(sl2, sl2), scalex2 = make_float2(scale, scale);
-    const float2 nlse2 = make_float2(-lse2r, -lse2r), ndls = make_float2(-dls, -dls);
-    int done = 0;
-    for (int j = 0; j < n; ++j) {
-      const int slot = j % kKS, k0 = kv_lo + j * BN;
-      if (!wait(S_FULL + t, j & 1)) break;
-      ptx::tc_fence_after();
-      // Tiles wholly below the diagonal of a block without masked keys take
-      // the unmasked loop; the test sits outside the unrolled element loops
-      // (a per-element branch there doubles the kernel's time).
-      const bool fast = !blk_masked && (k0 + BN <= kv_hi) && (k0 + BN - 1 <= q0);
-      const int lim = min(i - k0, kv_hi - 1 - k0);
-      const uint32_t* info = s_info + slot * BN;
-      uint32_t pk[32];
+      // Rows past q1 (another block's rows) get lse = +inf: their P is 0 with
+      // no per-element test on the unmasked path.
+      const float lse2r = i < q1 ? lse2 : CUDART_INF_F, dls = dl * scale;
+      const float2 nlse2 = make_float2(-lse2r, -lse2r), ndls = make_float2(-dls, -dls);
+      int done = 0;
+      for (int j = 0; j < w.n; ++j) {
+        const int gj = g + j, slot = gj % kKS, k0 = w.kv_lo + j * BN;
+        if (!wait(S_FULL + t, gj & 1)) break;
+        ptx::tc_fence_after();
+        // Tiles wholly below the diagonal of a block without masked keys take
+        // the unmasked loop; the test sits outside the unrolled element loops.
+        const bool fast = !w.masked && (k0 + BN <= w.kv_hi) && (k0 + BN - 1 <= w.q0);
+        const int lim = min(i - k0, w.kv_hi - 1 - k0);
+        const uint32_t* info = s_info + slot * BN;
+        uint32_t pk[32];
 #pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        uint32_t rs[32], rp[32];
-        ptx::tmem_ld32(tmem + lane_base + c_s + 32 * hf, rs);
-        ptx::tmem_ld32(tmem + lane_base + c_s + 64 + 32 * hf, rp);
-        ptx::tmem_wait_ld();
-        // Pairs of keys on the packed f32x2 pipe (FFMA2 for the exp argument
-        // and for dP * scale - scale * delta, FMUL2 for dS).
-        auto pair = [&](int x2, bool ok0, bool ok1) {
-          float2 arg = __ffma2_rn(make_float2(__uint_as_float(rs[2 * x2]), __uint_as_float(rs[2 * x2 + 1])), sl2x2, nlse2);
-          arg.x = ok0 ? arg.x : -CUDART_INF_F;
-          arg.y = ok1 ? arg.y : -CUDART_INF_F;
-          const float2 pp = make_float2(ptx::ex2(arg.x), ptx::ex2(arg.y));
-          const float2 ds = __fmul2_rn(
-              pp, __ffma2_rn(make_float2(__uint_as_float(rp[2 * x2]), __uint_as_float(rp[2 * x2 + 1])), scalex2, ndls));
-          pk[16 * hf + x2] = tile::pack2(ds.x, ds.y);
-        };
-        if (fast) {
+        for (int hf = 0; hf < 2; ++hf) {
+          uint32_t rs[32], rp[32];
+          ptx::tmem_ld32(tmem + lane_base + c_s + 32 * hf, rs);
+          ptx::tmem_ld32(tmem + lane_base + c_s + 64 + 32 * hf, rp);
+          ptx::tmem_wait_ld();
+          // Pairs of keys on the packed f32x2 pipe.
+          auto pair = [&](int x2, bool ok0, bool ok1) {
+            float2 arg = __ffma2_rn(make_float2(__uint_as_float(rs[2 * x2]), __uint_as_float(rs[2 * x2 + 1])), sl2x2,
+                                    nlse2);
+            arg.x = ok0 ? arg.x : -CUDART_INF_F;
+            arg.y = ok1 ? arg.y : -CUDART_INF_F;
+            const float2 pp = make_float2(ptx::ex2(arg.x), ptx::ex2(arg.y));
+            const float2 ds = __fmul2_rn(
+                pp, __ffma2_rn(make_float2(__uint_as_float(rp[2 * x2]), __uint_as_float(rp[2 * x2 + 1])), scalex2,
+                               ndls));
+            pk[16 * hf + x2] = tile::pack2(ds.x, ds.y);
+          };
+          if (fast) {
 #pragma unroll
-          for (int x2 = 0; x2 < 16; ++x2) pair(x2, true, true);
-        } else if (!blk_masked) {
-          // causal / key-range limit only: column c valid iff c <= lim
+            for (int x2 = 0; x2 < 16; ++x2) pair(x2, true, true);
+          } else if (!w.masked) {
+            // causal / key-range limit only: column c valid iff c <= lim
 #pragma unroll
-          for (int x2 = 0; x2 < 16; ++x2) {
-            const int c = 32 * hf + 2 * x2;
-            pair(x2, c <= lim, c + 1 <= lim);
-          }
-        } else {
+            for (int x2 = 0; x2 < 16; ++x2) {
+              const int c = 32 * hf + 2 * x2;
+              pair(x2, c <= lim, c + 1 <= lim);
+            }
+          } else {
 #pragma unroll
-          for (int x2 = 0; x2 < 16; ++x2) {
-            const int c = 32 * hf + 2 * x2;
-            pair(x2, (info[c] & AI_KEY_ATTN) && c <= lim, (info[c + 1] & AI_KEY_ATTN) && c + 1 <= lim);
+            for (int x2 = 0; x2 < 16; ++x2) {
+              const int c = 32 * hf + 2 * x2;
+              pair(x2, (info[c] & AI_KEY_ATTN) && c <= lim, (info[c + 1] & AI_KEY_ATTN) && c + 1 <= lim);
+            }
           }
         }
+        ptx::tmem_st32(tmem + lane_base + c_s, pk);
+        ptx::tmem_wait_st();
+        ptx::tc_fence_before();
+        ptx::mbar_arrive(bar(DS_READY + t));
+        done = j + 1;
       }
-      ptx::tmem_st32(tmem + lane_base + c_s, pk);
-      ptx::tmem_wait_st();
-      ptx::tc_fence_before();
-      ptx::mbar_arrive(bar(DS_READY + t));
-      done = j + 1;
-    }
-    // Epilogue: dQ = R(qpos)^T dQrot.
-    bool have = false;
-    if (done == n && n > 0) have = wait(DQ_DONE + t, (n - 1) & 1);
-    if (!*s_abort) {
+      if (done != w.n) break;
+      // Epilogue: dQ = R(qpos)^T dQrot; dQ_t is released to the next unit's
+      // first dQ MMA once it has been read.
+      bool have = false;
+      if (w.n > 0) {
+        have = wait(DQ_DONE + t, (g + w.n - 1) & 1);
+        if (!have) break;
+      }
       ptx::tc_fence_after();
       __nv_bfloat16* dQrow = static_cast<__nv_bfloat16*>(a.dq.ptr) + b * a.dq.stride_b + h * a.dq.stride_h +
                              (int64_t)i * a.dq.stride_t;
@@ -936,15 +983,19 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
 #pragma unroll
           for (int x = 0; x < 32; ++x) g1[x] = g2[x] = 0u;
         }
+        if (hf == 1) {  // dQ_t has been read
+          ptx::tc_fence_before();
+          ptx::mbar_arrive(bar(DQ_FREE + t));
+        }
         float o1[32], o2[32];
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
           const uint4 tv = __ldg(tab + 8 * hf + q);
           const __half2* h2 = reinterpret_cast<const __half2*>(&tv);
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int xx = 4 * q + u;
-            const float2 csn = __half22float2(h2[u]);
+          for (int uu = 0; uu < 4; ++uu) {
+            const int xx = 4 * q + uu;
+            const float2 csn = __half22float2(h2[uu]);
             const float v1 = __uint_as_float(g1[xx]), v2 = __uint_as_float(g2[xx]);
             o1[xx] = v1 * csn.x + v2 * csn.y;
             o2[xx] = v2 * csn.x - v1 * csn.y;
@@ -955,34 +1006,50 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
           store_bf16_row32(dQrow + 64 + 32 * hf, o2);
         }
       }
+      g += w.n;
     }
   } else if (warp == 8) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      const CUtensorMap* mk = k_pre ? &tm_kr : &tm_k;
-      ptx::prefetch_tmap(mk);
+      ptx::prefetch_tmap(&tm_k);
       ptx::prefetch_tmap(&tm_v);
       if (prerot) {
-        const int h0 = 2 * blockIdx.y;
-        ptx::mbar_arrive_expect_tx(bar(Q_READY), 4 * 32768);
-        ptx::tma_load_4d(sbase + Q0, &tm_qr, bar(Q_READY), 0, q0, h0, b);
-        ptx::tma_load_4d(sbase + Q0 + 16384, &tm_qr, bar(Q_READY), 64, q0, h0, b);
-        ptx::tma_load_4d(sbase + Q1, &tm_qr, bar(Q_READY), 0, q0, h0 + 1, b);
-        ptx::tma_load_4d(sbase + Q1 + 16384, &tm_qr, bar(Q_READY), 64, q0, h0 + 1, b);
-        ptx::tma_load_4d(sbase + DO0, &tm_do, bar(Q_READY), 0, q0, h0, b);
-        ptx::tma_load_4d(sbase + DO0 + 16384, &tm_do, bar(Q_READY), 64, q0, h0, b);
-        ptx::tma_load_4d(sbase + DO1, &tm_do, bar(Q_READY), 0, q0, h0 + 1, b);
-        ptx::tma_load_4d(sbase + DO1 + 16384, &tm_do, bar(Q_READY), 64, q0, h0 + 1, b);
+        ptx::prefetch_tmap(&tm_kr);
+        ptx::prefetch_tmap(&tm_qr);
+        ptx::prefetch_tmap(&tm_do);
       }
-      for (int j = 0; j < n; ++j) {
-        const int slot = j % kKS, k0 = kv_lo + j * BN;
-        if (j >= kKS && !wait(KV_EMPTY + slot, ((j / kKS) - 1) & 1)) break;
-        const uint32_t kb = sbase + KB + 16384u * (uint32_t)slot, vb = sbase + VB + 16384u * (uint32_t)slot;
-        ptx::mbar_arrive_expect_tx(bar(KV_FULL + slot), 32768);
-        ptx::tma_load_4d(kb, mk, bar(KV_FULL + slot), 0, k0, hk, b);
-        ptx::tma_load_4d(kb + 8192, mk, bar(KV_FULL + slot), 64, k0, hk, b);
-        ptx::tma_load_4d(vb, &tm_v, bar(KV_FULL + slot), 0, k0, hk, b);
-        ptx::tma_load_4d(vb + 8192, &tm_v, bar(KV_FULL + slot), 64, k0, hk, b);
+      int g = 0, k = 0;
+      bool ok = true;
+      for (int u = snake_unit(k); ok && u < n_units; u = snake_unit(++k)) {
+        const Unit w = load_unit(f, u, prerot);
+        const int b = w.blk.row;
+        if (prerot) {
+          if (k > 0 && !wait(Q_EMPTY, (k - 1) & 1)) break;
+          const int h0 = 2 * w.hp;
+          ptx::mbar_arrive_expect_tx(bar(Q_READY), 4 * 32768);
+          ptx::tma_load_4d(sbase + Q0, &tm_qr, bar(Q_READY), 0, w.q0, h0, b);
+          ptx::tma_load_4d(sbase + Q0 + 16384, &tm_qr, bar(Q_READY), 64, w.q0, h0, b);
+          ptx::tma_load_4d(sbase + Q1, &tm_qr, bar(Q_READY), 0, w.q0, h0 + 1, b);
+          ptx::tma_load_4d(sbase + Q1 + 16384, &tm_qr, bar(Q_READY), 64, w.q0, h0 + 1, b);
+          ptx::tma_load_4d(sbase + DO0, &tm_do, bar(Q_READY), 0, w.q0, h0, b);
+          ptx::tma_load_4d(sbase + DO0 + 16384, &tm_do, bar(Q_READY), 64, w.q0, h0, b);
+          ptx::tma_load_4d(sbase + DO1, &tm_do, bar(Q_READY), 0, w.q0, h0 + 1, b);
+          ptx::tma_load_4d(sbase + DO1 + 16384, &tm_do, bar(Q_READY), 64, w.q0, h0 + 1, b);
+        }
+        const CUtensorMap* mk = w.k_pre ? &tm_kr : &tm_k;
+        for (int j = 0; j < w.n; ++j, ++g) {
+          const int slot = g % kKS, k0 = w.kv_lo + j * BN;
+          if (g >= kKS && !wait(KV_EMPTY + slot, ((g / kKS) - 1) & 1)) {
+            ok = false;
+            break;
+          }
+          const uint32_t kb = sbase + KB + 16384u * (uint32_t)slot, vb = sbase + VB + 16384u * (uint32_t)slot;
+          ptx::mbar_arrive_expect_tx(bar(KV_FULL + slot), 32768);
+          ptx::tma_load_4d(kb, mk, bar(KV_FULL + slot), 0, k0, w.hk, b);
+          ptx::tma_load_4d(kb + 8192, mk, bar(KV_FULL + slot), 64, k0, w.hk, b);
+          ptx::tma_load_4d(vb, &tm_v, bar(KV_FULL + slot), 0, k0, w.hk, b);
+          ptx::tma_load_4d(vb + 8192, &tm_v, bar(KV_FULL + slot), 64, k0, w.hk, b);
+        }
       }
     }
   } else if (warp == 9) {
@@ -1014,70 +1081,91 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
                       (!first || kk > 0) ? 1u : 0u);
       ptx::mma_commit_w(bar(DQ_DONE + t));
     };
-    if (wait_u(Q_READY, 0) && n > 0 && wait_u(K_READY, 0)) {
+    int g = 0, k = 0;
+    bool ok = true;
+    for (int u = snake_unit(k); ok && u < n_units; u = snake_unit(++k)) {
+      const Unit w = load_unit(f, u, prerot);
+      if (!wait_u(Q_READY, k & 1)) break;
+      if (w.n == 0) {
+        ptx::mma_commit_w(bar(Q_EMPTY));
+        continue;
+      }
+      if (!wait_u(K_READY + g % kKS, (g / kKS) & 1)) break;
       ptx::tc_fence_after();
-      issue_s(0, 0);
-      issue_s(1, 0);
-      for (int j = 0; j < n; ++j) {
-        const int slot = j % kKS, nslot = (j + 1) % kKS;
-        const bool more = j + 1 < n;
-        if (!wait_u(DS_READY, j & 1)) break;
+      issue_s(0, g % kKS);
+      issue_s(1, g % kKS);
+      if (w.n == 1) ptx::mma_commit_w(bar(Q_EMPTY));  // the unit's last reads of Q and dO
+      for (int j = 0; j < w.n; ++j) {
+        const int gj = g + j, slot = gj % kKS, nslot = (gj + 1) % kKS;
+        const bool more = j + 1 < w.n;
+        if (!wait_u(DS_READY, gj & 1) || (j == 0 && k > 0 && !wait_u(DQ_FREE, (k - 1) & 1))) {
+          ok = false;
+          break;
+        }
         ptx::tc_fence_after();
         issue_dq(0, slot, j == 0);
         if (more) {
-          if (!wait_u(K_READY + nslot, ((j + 1) / kKS) & 1)) break;
+          if (!wait_u(K_READY + nslot, ((gj + 1) / kKS) & 1)) {
+            ok = false;
+            break;
+          }
           ptx::tc_fence_after();
           issue_s(0, nslot);
         }
-        if (!wait_u(DS_READY + 1, j & 1)) break;
+        if (!wait_u(DS_READY + 1, gj & 1) || (j == 0 && k > 0 && !wait_u(DQ_FREE + 1, (k - 1) & 1))) {
+          ok = false;
+          break;
+        }
         ptx::tc_fence_after();
         issue_dq(1, slot, j == 0);
         ptx::mma_commit_w(bar(KV_EMPTY + slot));
-        if (more) issue_s(1, nslot);
+        if (more) {
+          issue_s(1, nslot);
+          if (j + 2 == w.n) ptx::mma_commit_w(bar(Q_EMPTY));
+        }
       }
+      g += w.n;
     }
     ptx::mma_commit_w(bar(FINAL));
     ptx::mbar_wait(bar(FINAL), 0, kWait);
   } else {
     // ------------------------------------------------------------ K rotation (warps 10-13)
     const int rt = tid - 320, row = rt & 63, cg = rt >> 6;
-    uint32_t info = 0;
-    uint4 tab[8];
-    auto fetch = [&](int j) {
-      const int key = kv_lo + j * BN + row;
-      info = 0;
-      int p = 0;
-      if (key < kv_hi) {
-        info = (uint32_t)__ldg(L.key_info + blk.key_off + key);
-        p = key_row(info, L.n_pos, f.status);
-      }
-      if (!k_pre) {
-        const uint4* tp = reinterpret_cast<const uint4*>(cs16 + (int64_t)p * (D / 2)) + 8 * cg;
-#pragma unroll
-        for (int c = 0; c < 8; ++c) tab[c] = __ldg(tp + c);
-      }
-    };
-    if (n > 0) fetch(0);
-    for (int j = 0; j < n; ++j) {
-      const int slot = j % kKS;
-      if (!wait(KV_FULL + slot, (j / kKS) & 1)) break;
-      const uint32_t kt = KB + 16384u * (uint32_t)slot;
-      if (!k_pre && kv_lo + j * BN + row < kv_hi) {
-#pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
-          const int c = 4 * cg + cc;
-          uint4* pa = reinterpret_cast<uint4*>(sm + kt + chunk_off<BN>(row, c));
-          uint4* pb = reinterpret_cast<uint4*>(sm + kt + chunk_off<BN>(row, c + 8));
-          uint4 y1, y2;
-          tile::rotate8h(*pa, *pb, tab[2 * cc], tab[2 * cc + 1], y1, y2);
-          *pa = y1;
-          *pb = y2;
+    int g = 0;
+    for (int kr = 0, u = snake_unit(0); u < n_units && !*s_abort; u = snake_unit(++kr)) {
+      const Unit w = load_unit(f, u, prerot);
+      for (int j = 0; j < w.n; ++j, ++g) {
+        const int slot = g % kKS, key = w.kv_lo + j * BN + row;
+        uint32_t info = 0;
+        int p = 0;
+        if (key < w.kv_hi) {
+          info = (uint32_t)__ldg(L.key_info + w.blk.key_off + key);
+          p = key_row(info, L.n_pos, f.status);
         }
+        uint4 tab[8];
+        if (!w.k_pre) {
+          const uint4* tp = reinterpret_cast<const uint4*>(cs16 + (int64_t)p * (D / 2)) + 8 * cg;
+#pragma unroll
+          for (int c = 0; c < 8; ++c) tab[c] = __ldg(tp + c);
+        }
+        if (!wait(KV_FULL + slot, (g / kKS) & 1)) break;
+        const uint32_t kt = KB + 16384u * (uint32_t)slot;
+        if (!w.k_pre && key < w.kv_hi) {
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) {
+            const int c = 4 * cg + cc;
+            uint4* pa = reinterpret_cast<uint4*>(sm + kt + chunk_off<BN>(row, c));
+            uint4* pb = reinterpret_cast<uint4*>(sm + kt + chunk_off<BN>(row, c + 8));
+            uint4 y1, y2;
+            tile::rotate8h(*pa, *pb, tab[2 * cc], tab[2 * cc + 1], y1, y2);
+            *pa = y1;
+            *pb = y2;
+          }
+        }
+        if (cg == 0) s_info[slot * BN + row] = info;
+        ptx::fence_proxy_async_smem();
+        ptx::mbar_arrive(bar(K_READY + slot));
       }
-      if (cg == 0) s_info[slot * BN + row] = info;
-      ptx::fence_proxy_async_smem();
-      ptx::mbar_arrive(bar(K_READY + slot));
-      if (j + 1 < n) fetch(j + 1);
     }
   }
 
@@ -1597,11 +1685,16 @@ int sm100_bwd(const AiAttnBwdArgs& a, float* delta, void* rot, bool rot_ready, c
       }
     }
     if (e == cudaSuccess && n_pair > 0) {
-      e = cudaFuncSetAttribute(dq_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dqw::kSmem);
+      // Persistent: one CTA per SM walks the (item, head pair) units.
+      const int n_units = n_pair * (f.num_q_heads / 2);
+      int dev = 0, sms = 148;
+      if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+      const int grid = n_units < sms ? n_units : sms;
+      e = cudaFuncSetAttribute(dq_pers_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dqw::kSmem);
       if (e == cudaSuccess) {
         ProfScope ps(AI_PROF_DQ, st);
-        dq_ws_kernel<<<dim3(n_pair, f.num_q_heads / 2), dqw::kThreads, dqw::kSmem, st>>>(a, delta, tk, tv, tqr, tdo,
-                                                                                         tkr, pre ? 1 : 0);
+        dq_pers_kernel<<<grid, dqw::kThreads, dqw::kSmem, st>>>(a, delta, tk, tv, tqr, tdo, tkr, pre ? 1 : 0,
+                                                                n_units);
         e = cudaGetLastError();
       }
     }

@@ -379,11 +379,10 @@ constexpr uint32_t C_S0 = 0, C_S1 = 128, C_O0 = 256, C_O1 = 384;
 }  // namespace ws
 
 // ---------------------------------------------------------------------------
-// Persistent form of the warp-specialised forward: one CTA per SM walks the
-// work units u = blockIdx.x, blockIdx.x + gridDim.x, ... (unit = work item x
-// pair of query heads; items are longest first, so every CTA sees a
-// decreasing sequence).  Roles, tiles and shared-memory layout as in
-// fwd_ws_kernel; what carries across units:
+// Persistence: one CTA per SM walks the work units in a snake order (unit =
+// work item x pair of query heads; items are longest first, and the snake
+// evens out the sum of unit lengths per CTA).  Roles and tiles as above;
+// what carries across units:
 //   * tile barriers (K/V ring, S, P, O commits) count phases by the CTA's
 //     running tile index g, unit barriers by its running unit index k;
 //   * the next unit's Q tiles are loaded as soon as the current unit's last
@@ -498,7 +497,7 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
     const float sl2 = a.scale * kLog2e;
     const float2 sl2x2 = make_float2(sl2, sl2);
     int g = 0, k = 0;
-    for (int u = blockIdx.x; u < n_units && !*s_abort; u += gridDim.x, ++k) {
+    for (int u = snake_unit(k); u < n_units && !*s_abort; u = snake_unit(++k)) {
       const Unit w = load_unit(a, u, prerot);
       const int i = w.q0 + r, h = 2 * w.hp + t, b = w.blk.row;
       if (!prerot) {
@@ -704,7 +703,7 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
       }
       int g = 0, k = 0;
       bool ok = true;
-      for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x, ++k) {
+      for (int u = snake_unit(k); ok && u < n_units; u = snake_unit(++k)) {
         const Unit w = load_unit(a, u, prerot);
         const int b = w.blk.row;
         if (prerot) {
@@ -760,7 +759,7 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
     };
     int g = 0, k = 0;
     bool ok = true;
-    for (int u = blockIdx.x; ok && u < n_units; u += gridDim.x, ++k) {
+    for (int u = snake_unit(k); ok && u < n_units; u = snake_unit(++k)) {
       const Unit w = load_unit(a, u, prerot);
       if (!wait_u(Q_READY, k & 1)) break;
       if (w.n == 0) {
@@ -811,7 +810,7 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
     const int row = tid - 320;
     const __half2* cs16 = static_cast<const __half2*>(L.rope_cs16);
     int g = 0;
-    for (int u = blockIdx.x; u < n_units && !*s_abort; u += gridDim.x) {
+    for (int kr = 0, u = snake_unit(0); u < n_units && !*s_abort; u = snake_unit(++kr)) {
       const Unit w = load_unit(a, u, prerot);
       for (int j = 0; j < w.n; ++j, ++g) {
         const int slot = g & 1, key = w.kv_lo + j * BN + row;

@@ -54,6 +54,15 @@ __device__ __forceinline__ int key_row(uint32_t info, int n_pos, int32_t* status
   return r;
 }
 
+// Work unit of the k-th round of a persistent CTA: rounds of gridDim.x units
+// alternate direction (snake order), so that with units sorted longest first
+// every CTA's total stays close to the mean.  A value >= the unit count ends
+// the CTA's walk (only the last round can be partial).
+__device__ __forceinline__ int snake_unit(int k) {
+  const int G = (int)gridDim.x, c = (int)blockIdx.x;
+  return k * G + ((k & 1) ? G - 1 - c : c);
+}
+
 __device__ __forceinline__ int clamp_row(int r, int n_pos, int32_t* status) {
   if (r < 0 || r >= n_pos) {
     report(status, AI_ERR_DEV_BOUNDS);

@@ -37,7 +37,7 @@ SECTIONS = [(0, 32), (32, 64)]
 WORKLOAD = ("cfg1: bf16 B=4 T=4096 Hq=32 Hkv=8 D=128 theta=1e6, docs U[256,2048] packed per row, "
             "2 RoPE sections (32+32 freq slots: arange, cursor stream)")
 METRIC = "multi-seg RoPE attn fwd+bwd TFLOP/s (causal-adjusted, 14*D*pairs*Hq)"
-DOM_KERNEL_NAMES = {"fwd": "fwd_pers_kernel (forward)", "dq": "dq_ws_kernel (dQ)", "dkdv": "dkdv_ws_kernel (dK/dV)"}
+DOM_KERNEL_NAMES = {"fwd": "fwd_pers_kernel (forward)", "dq": "dq_pers_kernel (dQ)", "dkdv": "dkdv_ws_kernel (dK/dV)"}
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch on this
 # workload, from one ncu capture of the three kernels (profiles/).
 TRAFFIC_BYTES = {"fwd": 304252928, "dq": 447438080, "dkdv": 403690752}
