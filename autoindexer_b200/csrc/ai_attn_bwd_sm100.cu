@@ -1266,8 +1266,8 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
   if (tid == 0) {
     for (int i = 0; i < N_BARS; ++i) {
       uint32_t count = 1;
-      if (i == K_READY || (i >= Q_READY && i < Q_READY + kQS) || i == FOLD_DONE) count = 128;
-      if (i == P_READY || i == P_READY + 1) count = 128;
+      if (i == K_READY || (i >= Q_READY && i < Q_READY + kQS)) count = 128;
+      if (i == P_READY || i == P_READY + 1 || i == FOLD_DONE) count = 256;
       ptx::mbar_init(bar(i), count);
     }
     *s_abort = 0;
@@ -1314,13 +1314,17 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
       const bool key_ok = (info & AI_KEY_ATTN) != 0;
       const int nsteps = n_steps_of(blk);
       for (int st = 0; st < nsteps; ++st, ++s) {
-        if ((s & 1) != t) continue;
         const int x = s & 1, qslot = s % kQS, q0 = qs + (st / G) * BQ, q1 = min(q0 + BQ, blk.e);
         if (!wait(Q_READY + qslot, (s / kQS) & 1) || !wait(S_FULL + x, (s >> 1) & 1)) break;
         ptx::tc_fence_after();
-        const float* nlse2 = s_stats + qslot * 2 * BQ;  // -lse2 per query row
-        const float* ndlt = nlse2 + BQ;                  // -scale * delta per query row
-        const uint32_t cb = tmem + lane_base + C_BUF + 128u * (uint32_t)x;
+        // This group's 32 query columns of the step: c0 + [0, 32).
+        const int c0 = 32 * t;
+        const float* nlse2 = s_stats + qslot * 2 * BQ + c0;  // -lse2 per query row
+        const float* ndlt = nlse2 + BQ;                       // -scale * delta per query row
+        const uint32_t cb = tmem + lane_base + C_BUF + 128u * (uint32_t)x + (uint32_t)c0;
+        uint32_t rs[32], rp[32];
+        ptx::tmem_ld32(cb, rs);
+        ptx::tmem_ld32(cb + 64, rp);
         // Whole-step masks: causal (j <= i) holds for every pair when the tile
         // lies wholly above the query rows, and every row is in the block when
         // the tile is full.
@@ -1328,52 +1332,50 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
         // The step-uniform test sits outside the unrolled element loops (a
         // per-element branch there costs as much as the rest of the step).
         const bool plain = no_causal && rows_full;
-        const int clo = j - q0, chi = q1 - q0;  // general path: query columns clo <= c < chi
-        uint32_t pk[32], dk[32];
+        const int clo = j - q0 - c0, chi = q1 - q0 - c0;  // general path: clo <= c < chi
+        uint32_t pk[16], dk[16];
+        ptx::tmem_wait_ld();
+        auto pair = [&](int x2, bool ok0, bool ok1) {
+          const int c = 2 * x2;
+          const float2 nl = *reinterpret_cast<const float2*>(nlse2 + c);
+          const float2 nd = *reinterpret_cast<const float2*>(ndlt + c);
+          float2 arg = __ffma2_rn(make_float2(__uint_as_float(rs[c]), __uint_as_float(rs[c + 1])), sl2x2, nl);
+          arg.x = ok0 ? arg.x : -CUDART_INF_F;
+          arg.y = ok1 ? arg.y : -CUDART_INF_F;
+          const float2 pp = make_float2(ptx::ex2(arg.x), ptx::ex2(arg.y));
+          const float2 ds =
+              __fmul2_rn(pp, __ffma2_rn(make_float2(__uint_as_float(rp[c]), __uint_as_float(rp[c + 1])), scalex2, nd));
+          pk[x2] = tile::pack2(pp.x, pp.y);
+          dk[x2] = tile::pack2(ds.x, ds.y);
+        };
+        if (plain) {
 #pragma unroll
-        for (int qq = 0; qq < 4; ++qq) {
-          uint32_t rs[16], rp[16];
-          ptx::tmem_ld16(cb + 16 * qq, rs);
-          ptx::tmem_ld16(cb + 64 + 16 * qq, rp);
-          ptx::tmem_wait_ld();
-          auto pair = [&](int x2, bool ok0, bool ok1) {
-            const int c = 16 * qq + 2 * x2;
-            const float2 nl = *reinterpret_cast<const float2*>(nlse2 + c);
-            const float2 nd = *reinterpret_cast<const float2*>(ndlt + c);
-            float2 arg = __ffma2_rn(make_float2(__uint_as_float(rs[2 * x2]), __uint_as_float(rs[2 * x2 + 1])), sl2x2, nl);
-            arg.x = ok0 ? arg.x : -CUDART_INF_F;
-            arg.y = ok1 ? arg.y : -CUDART_INF_F;
-            const float2 pp = make_float2(ptx::ex2(arg.x), ptx::ex2(arg.y));
-            const float2 ds = __fmul2_rn(pp, __ffma2_rn(make_float2(__uint_as_float(rp[2 * x2]), __uint_as_float(rp[2 * x2 + 1])), scalex2, nd));
-            pk[8 * qq + x2] = tile::pack2(pp.x, pp.y);
-            dk[8 * qq + x2] = tile::pack2(ds.x, ds.y);
-          };
-          if (plain) {
+          for (int x2 = 0; x2 < 16; ++x2) pair(x2, key_ok, key_ok);
+        } else {
 #pragma unroll
-            for (int x2 = 0; x2 < 8; ++x2) pair(x2, key_ok, key_ok);
-          } else {
-#pragma unroll
-            for (int x2 = 0; x2 < 8; ++x2) {
-              const int c = 16 * qq + 2 * x2;
-              pair(x2, key_ok && c >= clo && c < chi, key_ok && c + 1 >= clo && c + 1 < chi);
-            }
+          for (int x2 = 0; x2 < 16; ++x2) {
+            const int c = 2 * x2;
+            pair(x2, key_ok && c >= clo && c < chi, key_ok && c + 1 >= clo && c + 1 < chi);
           }
         }
-        ptx::tmem_st32(cb, pk);
-        ptx::tmem_st32(cb + 64, dk);
+        // P^T / dS^T of these columns go over the first 16 of the group's own
+        // 32 score columns (bf16 pairs), where the dV / dK MMAs read them.
+        ptx::tmem_st16(cb, pk);
+        ptx::tmem_st16(cb + 64, dk);
         ptx::tmem_wait_st();
         ptx::tc_fence_before();
         ptx::mbar_arrive(bar(P_READY + x));
       }
       if (*s_abort) break;
-      if (t == 0) {
-        // Fold this block's dKrot into dK: dK += R(key position)^T dKrot.
+      {
+        // Fold this block's dKrot into dK: dK += R(key position)^T dKrot;
+        // group t takes the rotation pairs (d, d + 64) with d in [32t, 32t + 32).
         if (!wait(BLK_DONE, nb & 1)) break;
         ptx::tc_fence_after();
         const int p = key_row(info, L.n_pos, f.status);
         const uint4* tp = reinterpret_cast<const uint4*>(cs16 + (int64_t)p * (D / 2));
-#pragma unroll
-        for (int hf = 0; hf < 2; ++hf) {
+        {
+          const int hf = t;
           uint32_t g1[32], g2[32];
           ptx::tmem_ld32(tmem + lane_base + C_DKR + 32 * hf, g1);
           ptx::tmem_ld32(tmem + lane_base + C_DKR + 64 + 32 * hf, g2);
@@ -1397,31 +1399,30 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
       }
       ++nb;
     }
-    // Epilogue: group 0 writes dK (smem), group 1 writes dV (TMEM).
+    // Epilogue: group t writes the columns it folded, d in [32t, 32t + 32)
+    // and [64 + 32t, 96 + 32t), of dK (smem) and dV (TMEM; the last block's
+    // MMAs are done, its fold waited for them).
     if (!*s_abort) {
-      if (t == 1 && any && !wait(BLK_DONE, (nb - 1) & 1)) {
-      } else if (!*s_abort) {
-        ptx::tc_fence_after();
-        __nv_bfloat16* row_ptr =
-            t == 0 ? static_cast<__nv_bfloat16*>(a.dk.ptr) + b * a.dk.stride_b + hk * a.dk.stride_h + (int64_t)j * a.dk.stride_t
-                   : static_cast<__nv_bfloat16*>(a.dv.ptr) + b * a.dv.stride_b + hk * a.dv.stride_h + (int64_t)j * a.dv.stride_t;
+      ptx::tc_fence_after();
+      __nv_bfloat16* dk_row =
+          static_cast<__nv_bfloat16*>(a.dk.ptr) + b * a.dk.stride_b + hk * a.dk.stride_h + (int64_t)j * a.dk.stride_t;
+      __nv_bfloat16* dv_row =
+          static_cast<__nv_bfloat16*>(a.dv.ptr) + b * a.dv.stride_b + hk * a.dv.stride_h + (int64_t)j * a.dv.stride_t;
 #pragma unroll
-        for (int cc = 0; cc < D / 32; ++cc) {
-          float v[32];
-          if (t == 0) {
+      for (int h2 = 0; h2 < 2; ++h2) {
+        const int cc = t + 2 * h2;
+        float v[32];
 #pragma unroll
-            for (int x = 0; x < 32; ++x) v[x] = s_dk[(32 * cc + x) * BN + lrow];
-          } else {
-            uint32_t rr[32];
-            if (any) {
-              ptx::tmem_ld32(tmem + lane_base + C_DV + 32 * cc, rr);
-              ptx::tmem_wait_ld();
-            }
-#pragma unroll
-            for (int x = 0; x < 32; ++x) v[x] = any ? __uint_as_float(rr[x]) : 0.f;
-          }
-          if (j < j1) store_bf16_row32(row_ptr + 32 * cc, v);
+        for (int x = 0; x < 32; ++x) v[x] = s_dk[(32 * cc + x) * BN + lrow];
+        if (j < j1) store_bf16_row32(dk_row + 32 * cc, v);
+        uint32_t rr[32];
+        if (any) {
+          ptx::tmem_ld32(tmem + lane_base + C_DV + 32 * cc, rr);
+          ptx::tmem_wait_ld();
         }
+#pragma unroll
+        for (int x = 0; x < 32; ++x) v[x] = any ? __uint_as_float(rr[x]) : 0.f;
+        if (j < j1) store_bf16_row32(dv_row + 32 * cc, v);
       }
     }
   } else if (warp == 8) {
@@ -1520,10 +1521,11 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
         const uint32_t cb = tmem + C_BUF + 128u * (uint32_t)x;
 #pragma unroll
         for (int kk = 0; kk < BQ / 16; ++kk) {
-          ptx::mma_ts_w(tmem + C_DV, cb + 8u * (uint32_t)kk,
-                        ptx::sdesc_sw128(ob + 2048u * (uint32_t)kk, 8192, 1024), idesc_acc,
+          // query rows 16 kk .. 16 kk + 15: packed by score group kk / 2
+          const uint32_t ca = cb + 32u * (uint32_t)(kk >> 1) + 8u * (uint32_t)(kk & 1);
+          ptx::mma_ts_w(tmem + C_DV, ca, ptx::sdesc_sw128(ob + 2048u * (uint32_t)kk, 8192, 1024), idesc_acc,
                         (dv_started || kk > 0) ? 1u : 0u);
-          ptx::mma_ts_w(tmem + C_DKR, cb + 64u + 8u * (uint32_t)kk,
+          ptx::mma_ts_w(tmem + C_DKR, ca + 64u,
                         ptx::sdesc_sw128(qb + 2048u * (uint32_t)kk, 8192, 1024), idesc_acc,
                         (s > sb || kk > 0) ? 1u : 0u);
         }
