@@ -734,7 +734,14 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
   } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
     // Whole warp (warp-uniform descriptors); one elected lane issues.
-    auto wait_u = [&](int i, uint32_t parity) -> bool { return __shfl_sync(0xffffffffu, wait(i, parity), 0); };
+    // The tensor core's instruction queue holds only a couple of MMAs, so the
+    // warp's time between two MMA groups idles the tensor core almost one for
+    // one: a barrier that has already completed is recognised by one try_wait
+    // of the whole warp, before the bounded polling path.
+    auto wait_u = [&](int i, uint32_t parity) -> bool {
+      if (__all_sync(0xffffffffu, ptx::mbar_try_wait(bar(i), parity))) return true;
+      return __shfl_sync(0xffffffffu, wait(i, parity), 0);
+    };
     constexpr uint32_t idesc_qk = ptx::idesc_bf16_f32(BM, BN, false, false);
     constexpr uint32_t idesc_pv = ptx::idesc_bf16_f32(BM, D, false, true);
     auto issue_s = [&](int t, int slot) {
