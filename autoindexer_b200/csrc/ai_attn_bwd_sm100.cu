@@ -853,7 +853,7 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
     const uint32_t c_s = 128u * (uint32_t)t, c_dq = 256u + 128u * (uint32_t)t;
     const float sl2 = f.scale * kLog2e, scale = f.scale;
     const float2 sl2x2 = make_float2(sl2, sl2), scalex2 = make_float2(scale, scale);
-    int g = 0, k = 0;
+    int g = 0, k = 0, ko = 0;  // ko: units with key tiles so far (DQ_DONE phases)
     for (int u = snake_unit(k); u < n_units && !*s_abort; u = snake_unit(++k)) {
       const Unit w = load_unit(f, u, prerot);
       const int i = w.q0 + r, h = 2 * w.hp + t, b = w.blk.row, q1 = w.q1;
@@ -965,7 +965,8 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
       // first dQ MMA once it has been read.
       bool have = false;
       if (w.n > 0) {
-        have = wait(DQ_DONE + t, (g + w.n - 1) & 1);
+        have = wait(DQ_DONE + t, (uint32_t)ko & 1u);
+        ++ko;
         if (!have) break;
       }
       ptx::tc_fence_after();
@@ -1065,28 +1066,36 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
     };
     constexpr uint32_t idesc_s = ptx::idesc_bf16_f32(BM, BN, false, false);
     constexpr uint32_t idesc_dq = ptx::idesc_bf16_f32(BM, D, false, true);
+    // Every operand tile sits at a constant offset from a base descriptor, and
+    // a descriptor's low 14 bits are the shared address / 16 (addresses stay
+    // below 256 KB, so no carry leaves that field): each MMA's descriptor is
+    // one add.
+    static_assert(Q1 == Q0 + 32768 && DO0 == Q0 + 65536 && DO1 == Q0 + 98304, "Q / dO tile layout");
+    const uint64_t d_q = ptx::sdesc_sw128(sbase + Q0, 16, 1024);
+    const uint64_t d_k = ptx::sdesc_sw128(sbase + KB, 16, 1024);
+    const uint64_t d_ka = ptx::sdesc_sw128(sbase + KB, 8192, 1024);  // K as the MN-major B of dQ += dS.K
+    constexpr uint64_t kSlot = 16384u >> 4, kHead = 32768u >> 4, kDo = 65536u >> 4, kV = (uint64_t)(VB - KB) >> 4;
     auto issue_s = [&](int t, int slot) {
-      const uint32_t qt = sbase + (t ? Q1 : Q0), ot = sbase + (t ? DO1 : DO0);
-      const uint32_t kt = sbase + KB + 16384u * (uint32_t)slot, vt = sbase + VB + 16384u * (uint32_t)slot;
+      const uint64_t dq = d_q + kHead * (uint64_t)t, dk = d_k + kSlot * (uint64_t)slot;
       const uint32_t cs = tmem + 128u * (uint32_t)t;
 #pragma unroll
       for (int kk = 0; kk < D / 16; ++kk) {
-        const uint32_t ao = (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u;
-        const uint32_t bo = (uint32_t)(kk >> 2) * 8192u + (uint32_t)(kk & 3) * 32u;
-        ptx::mma_ss_w(cs, ptx::sdesc_sw128(qt + ao, 16, 1024), ptx::sdesc_sw128(kt + bo, 16, 1024), idesc_s, kk > 0);
-        ptx::mma_ss_w(cs + 64, ptx::sdesc_sw128(ot + ao, 16, 1024), ptx::sdesc_sw128(vt + bo, 16, 1024), idesc_s,
-                      kk > 0);
+        const uint64_t ao = (uint64_t)(((kk >> 2) * 16384 + (kk & 3) * 32) >> 4);
+        const uint64_t bo = (uint64_t)(((kk >> 2) * 8192 + (kk & 3) * 32) >> 4);
+        ptx::mma_ss_w(cs, dq + ao, dk + bo, idesc_s, kk > 0);
+        ptx::mma_ss_w(cs + 64, dq + kDo + ao, dk + kV + bo, idesc_s, kk > 0);
       }
       ptx::mma_commit_w(bar(S_FULL + t));
     };
-    auto issue_dq = [&](int t, int slot, bool first) {
-      const uint32_t kt = sbase + KB + 16384u * (uint32_t)slot;
+    // DQ_DONE is committed after a unit's last dQ MMAs only (the epilogue's
+    // wait).
+    auto issue_dq = [&](int t, int slot, bool first, bool last) {
+      const uint64_t dk = d_ka + kSlot * (uint64_t)slot;
 #pragma unroll
       for (int kk = 0; kk < BN / 16; ++kk)
         ptx::mma_ts_w(tmem + 256u + 128u * (uint32_t)t, tmem + 128u * (uint32_t)t + 8u * (uint32_t)kk,
-                      ptx::sdesc_sw128(kt + 2048u * (uint32_t)kk, 8192, 1024), idesc_dq,
-                      (!first || kk > 0) ? 1u : 0u);
-      ptx::mma_commit_w(bar(DQ_DONE + t));
+                      dk + (uint64_t)((2048 * kk) >> 4), idesc_dq, (!first || kk > 0) ? 1u : 0u);
+      if (last) ptx::mma_commit_w(bar(DQ_DONE + t));
     };
     int g = 0, k = 0;
     bool ok = true;
@@ -1110,7 +1119,7 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
           break;
         }
         ptx::tc_fence_after();
-        issue_dq(0, slot, j == 0);
+        issue_dq(0, slot, j == 0, !more);
         if (more) {
           if (!wait_u(K_READY + nslot, ((gj + 1) / kKS) & 1)) {
             ok = false;
@@ -1124,7 +1133,7 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
           break;
         }
         ptx::tc_fence_after();
-        issue_dq(1, slot, j == 0);
+        issue_dq(1, slot, j == 0, !more);
         ptx::mma_commit_w(bar(KV_EMPTY + slot));
         if (more) {
           issue_s(1, nslot);
@@ -1482,25 +1491,39 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
     };
     constexpr uint32_t idesc_st = ptx::idesc_bf16_f32(BN, BQ, false, false);
     constexpr uint32_t idesc_acc = ptx::idesc_bf16_f32(BN, D, false, true);
-    auto issue_scores = [&](int s) {
-      const int x = s & 1, qslot = s % kQS;
-      const uint32_t qb = sbase + Q + 16384u * (uint32_t)qslot, ob = sbase + DO + 16384u * (uint32_t)qslot;
+    // Every operand tile sits at a constant offset from one of four base
+    // descriptors, and a descriptor's low 14 bits are the shared address / 16
+    // (addresses stay below 256 KB, so no carry leaves that field): each MMA's
+    // descriptor is one add, and a step's slot one more.
+    const uint64_t d_k = ptx::sdesc_sw128(sbase + K, 16, 1024);
+    const uint64_t d_v = ptx::sdesc_sw128(sbase + V, 16, 1024);
+    const uint64_t d_q = ptx::sdesc_sw128(sbase + Q, 16, 1024);     // Q / dO K-major (scores)
+    const uint64_t d_qa = ptx::sdesc_sw128(sbase + Q, 8192, 1024);  // Q / dO MN-major (dV / dK)
+    constexpr uint64_t kSlot = 16384u >> 4, kDo = (uint64_t)(DO - Q) >> 4;
+    auto issue_scores = [&](int x, int slot) {
+      const uint64_t dq = d_q + kSlot * (uint64_t)slot;
       const uint32_t cb = tmem + C_BUF + 128u * (uint32_t)x;
 #pragma unroll
       for (int kk = 0; kk < D / 16; ++kk) {
-        const uint32_t ao = (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u;
-        const uint32_t bo = (uint32_t)(kk >> 2) * 8192u + (uint32_t)(kk & 3) * 32u;
-        ptx::mma_ss_w(cb, ptx::sdesc_sw128(sbase + K + ao, 16, 1024), ptx::sdesc_sw128(qb + bo, 16, 1024), idesc_st,
-                      kk > 0);
-        ptx::mma_ss_w(cb + 64, ptx::sdesc_sw128(sbase + V + ao, 16, 1024), ptx::sdesc_sw128(ob + bo, 16, 1024),
-                      idesc_st, kk > 0);
+        const uint64_t ao = (uint64_t)(((kk >> 2) * 16384 + (kk & 3) * 32) >> 4);
+        const uint64_t bo = (uint64_t)(((kk >> 2) * 8192 + (kk & 3) * 32) >> 4);
+        ptx::mma_ss_w(cb, d_k + ao, dq + bo, idesc_st, kk > 0);
+        ptx::mma_ss_w(cb + 64, d_v + ao, dq + kDo + bo, idesc_st, kk > 0);
       }
       ptx::mma_commit_w(bar(S_FULL + x));
+    };
+    // Q / dO slot and Q_READY parity of a step, advanced one step at a time.
+    auto advance = [](int& slot, uint32_t& phase) {
+      if (++slot == kQS) {
+        slot = 0;
+        phase ^= 1u;
+      }
     };
     bool ok = wait_u(V_FULL, 0);
     BlockIter it(&L, b, j0, j1);
     Block blk;
-    int s = 0, nb = 0;
+    int s = 0, nb = 0, sl = 0;
+    uint32_t ph = 0;
     bool dv_started = false;
     while (ok && it.next(blk)) {
       const int nsteps = n_steps_of(blk);
@@ -1508,18 +1531,21 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
       ptx::tc_fence_after();
       const int sb = s;
       // scores of the block's first step
-      if (!wait_u(Q_READY + s % kQS, (s / kQS) & 1)) break;
+      if (!wait_u(Q_READY + sl, ph)) break;
       ptx::tc_fence_after();
-      issue_scores(s);
+      issue_scores(s & 1, sl);
+      int sl1 = sl;  // step s + 1
+      uint32_t ph1 = ph;
+      advance(sl1, ph1);
       for (; s < sb + nsteps; ++s) {
         const int x = s & 1;
         if (s + 1 < sb + nsteps) {
-          if (!wait_u(Q_READY + (s + 1) % kQS, ((s + 1) / kQS) & 1)) {
+          if (!wait_u(Q_READY + sl1, ph1)) {
             ok = false;
             break;
           }
           ptx::tc_fence_after();
-          issue_scores(s + 1);
+          issue_scores(x ^ 1, sl1);
         }
         if (!wait_u(P_READY + x, (s >> 1) & 1)) {
           ok = false;
@@ -1530,21 +1556,21 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
           break;
         }
         ptx::tc_fence_after();
-        const int qslot = s % kQS;
-        const uint32_t qb = sbase + Q + 16384u * (uint32_t)qslot, ob = sbase + DO + 16384u * (uint32_t)qslot;
+        const uint64_t dqa = d_qa + kSlot * (uint64_t)sl;
         const uint32_t cb = tmem + C_BUF + 128u * (uint32_t)x;
 #pragma unroll
         for (int kk = 0; kk < BQ / 16; ++kk) {
           // query rows 16 kk .. 16 kk + 15: packed by score group kk / 2
           const uint32_t ca = cb + 32u * (uint32_t)(kk >> 1) + 8u * (uint32_t)(kk & 1);
-          ptx::mma_ts_w(tmem + C_DV, ca, ptx::sdesc_sw128(ob + 2048u * (uint32_t)kk, 8192, 1024), idesc_acc,
-                        (dv_started || kk > 0) ? 1u : 0u);
-          ptx::mma_ts_w(tmem + C_DKR, ca + 64u,
-                        ptx::sdesc_sw128(qb + 2048u * (uint32_t)kk, 8192, 1024), idesc_acc,
-                        (s > sb || kk > 0) ? 1u : 0u);
+          const uint64_t ko = (uint64_t)(2048 * kk) >> 4;
+          ptx::mma_ts_w(tmem + C_DV, ca, dqa + kDo + ko, idesc_acc, (dv_started || kk > 0) ? 1u : 0u);
+          ptx::mma_ts_w(tmem + C_DKR, ca + 64u, dqa + ko, idesc_acc, (s > sb || kk > 0) ? 1u : 0u);
         }
-        ptx::mma_commit_w(bar(Q_EMPTY + qslot));
+        ptx::mma_commit_w(bar(Q_EMPTY + sl));
         dv_started = true;
+        sl = sl1;
+        ph = ph1;
+        advance(sl1, ph1);
       }
       if (!ok) break;
       ptx::mma_commit_w(bar(BLK_DONE));

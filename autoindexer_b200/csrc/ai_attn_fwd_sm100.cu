@@ -496,7 +496,7 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
     const uint32_t c_s = t ? C_S1 : C_S0, c_o = t ? C_O1 : C_O0;
     const float sl2 = a.scale * kLog2e;
     const float2 sl2x2 = make_float2(sl2, sl2);
-    int g = 0, k = 0;
+    int g = 0, k = 0, ko = 0;  // ko: units with key tiles so far (O_DONE phases)
     for (int u = snake_unit(k); u < n_units && !*s_abort; u = snake_unit(++k)) {
       const Unit w = load_unit(a, u, prerot);
       const int i = w.q0 + r, h = 2 * w.hp + t, b = w.blk.row;
@@ -632,7 +632,8 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
       // next unit's first PV before the global stores.
       bool have_o = false;
       if (w.n > 0) {
-        have_o = wait(O_DONE + t, (g + w.n - 1) & 1);
+        have_o = wait(O_DONE + t, (uint32_t)ko & 1u);
+        ++ko;
         if (!have_o) break;
       }
       ptx::tc_fence_after();
@@ -744,25 +745,35 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
     };
     constexpr uint32_t idesc_qk = ptx::idesc_bf16_f32(BM, BN, false, false);
     constexpr uint32_t idesc_pv = ptx::idesc_bf16_f32(BM, D, false, true);
+    // Every operand tile sits at a constant offset from a base descriptor, and
+    // a descriptor's low 14 bits are the shared address / 16 (addresses stay
+    // below 256 KB, so no carry leaves that field): each MMA's descriptor is
+    // one add.
+    const uint64_t d_q = ptx::sdesc_sw128(sbase + Q0, 16, 1024);
+    const uint64_t d_k = ptx::sdesc_sw128(sbase + KB, 16, 1024);
+    const uint64_t d_v = ptx::sdesc_sw128(sbase + VB, kHalf, 1024);
+    constexpr uint64_t kT = kTile >> 4;
+    static_assert(Q1 == Q0 + kTile, "Q tiles adjacent");
     auto issue_s = [&](int t, int slot) {
-      const uint32_t qt = sbase + (t ? Q1 : Q0), kt = sbase + KB + (uint32_t)slot * kTile;
+      const uint64_t dq = d_q + kT * (uint64_t)t, dk = d_k + kT * (uint64_t)slot;
 #pragma unroll
       for (int kk = 0; kk < D / 16; ++kk) {
-        const uint32_t off = (uint32_t)(kk >> 2) * kHalf + (uint32_t)(kk & 3) * 32u;
-        ptx::mma_ss_w(tmem + (t ? C_S1 : C_S0), ptx::sdesc_sw128(qt + off, 16, 1024),
-                      ptx::sdesc_sw128(kt + off, 16, 1024), idesc_qk, kk > 0);
+        const uint64_t off = (uint64_t)(((kk >> 2) * kHalf + (kk & 3) * 32) >> 4);
+        ptx::mma_ss_w(tmem + (t ? C_S1 : C_S0), dq + off, dk + off, idesc_qk, kk > 0);
       }
       ptx::mma_commit_w(bar(S_FULL + t));
     };
-    auto issue_pv = [&](int t, int slot, bool first) {
-      const uint32_t vt = sbase + VB + (uint32_t)slot * kTile;
+    // O_DONE is committed after a unit's last PV only (the epilogue's wait);
+    // the softmax's rescale of O_t is ordered by the S_t commit that follows
+    // each PV_t.
+    auto issue_pv = [&](int t, int slot, bool first, bool last) {
+      const uint64_t dv = d_v + kT * (uint64_t)slot;
 #pragma unroll
       for (int kk = 0; kk < BN / 16; ++kk) {
         ptx::mma_ts_w(tmem + (t ? C_O1 : C_O0), tmem + (t ? C_S1 : C_S0) + 8u * (uint32_t)kk,
-                      ptx::sdesc_sw128(vt + (uint32_t)kk * 2048u, kHalf, 1024), idesc_pv,
-                      (!first || kk > 0) ? 1u : 0u);
+                      dv + (uint64_t)((kk * 2048) >> 4), idesc_pv, (!first || kk > 0) ? 1u : 0u);
       }
-      ptx::mma_commit_w(bar(O_DONE + t));
+      if (last) ptx::mma_commit_w(bar(O_DONE + t));
     };
     int g = 0, k = 0;
     bool ok = true;
@@ -786,7 +797,7 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
           break;
         }
         ptx::tc_fence_after();
-        issue_pv(0, slot, j == 0);
+        issue_pv(0, slot, j == 0, !more);
         if (more) {
           if (!wait_u(K_READY + nslot, ((gj + 1) >> 1) & 1)) {
             ok = false;
@@ -800,7 +811,7 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
           break;
         }
         ptx::tc_fence_after();
-        issue_pv(1, slot, j == 0);
+        issue_pv(1, slot, j == 0, !more);
         ptx::mma_commit_w(bar(KV_EMPTY + slot));
         if (more) {
           issue_s(1, nslot);
