@@ -72,6 +72,22 @@ __device__ __forceinline__ void store_bf16_row32(__nv_bfloat16* dst, const float
   }
 }
 
+// The same with two 32-byte stores (each a full sector); dst 32-byte aligned.
+__device__ __forceinline__ void store_bf16_row32_v8(__nv_bfloat16* dst, const float* f) {
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    uint32_t w[8];
+#pragma unroll
+    for (int x = 0; x < 8; ++x) w[x] = tile::pack2(f[16 * h + 2 * x], f[16 * h + 2 * x + 1]);
+    ptx::st_global_v8(dst + 16 * h, w);
+  }
+}
+
+// Whether every row of t starts on a 32-byte boundary.
+__device__ __forceinline__ bool rows_32b(const AiTensor4& t) {
+  return ((uintptr_t)t.ptr % 32 == 0) && (t.stride_b % 16 == 0) && (t.stride_h % 16 == 0) && (t.stride_t % 16 == 0);
+}
+
 // ===========================================================================
 // dQ
 // ===========================================================================
@@ -851,6 +867,7 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
     const int t = warp / 4, r = tid % 128;
     const uint32_t lane_base = (uint32_t)((warp % 4) * 32) << 16;
     const uint32_t c_s = 128u * (uint32_t)t, c_dq = 256u + 128u * (uint32_t)t;
+    const bool v8 = rows_32b(a.dq);
     const float sl2 = f.scale * kLog2e, scale = f.scale;
     const float2 sl2x2 = make_float2(sl2, sl2), scalex2 = make_float2(scale, scale);
     int g = 0, k = 0, ko = 0;  // ko: units with key tiles so far (DQ_DONE phases)
@@ -1003,8 +1020,15 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
           }
         }
         if (i < q1) {
-          store_bf16_row32(dQrow + 32 * hf, o1);
-          store_bf16_row32(dQrow + 64 + 32 * hf, o2);
+          // Rows 8 KB apart: each store instruction touches 32 rows, so full
+          // 32-byte sectors halve the L1 / L2 write requests.
+          if (v8) {
+            store_bf16_row32_v8(dQrow + 32 * hf, o1);
+            store_bf16_row32_v8(dQrow + 64 + 32 * hf, o2);
+          } else {
+            store_bf16_row32(dQrow + 32 * hf, o1);
+            store_bf16_row32(dQrow + 64 + 32 * hf, o2);
+          }
         }
       }
       g += w.n;

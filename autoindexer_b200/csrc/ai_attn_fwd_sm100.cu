@@ -409,7 +409,7 @@ using ws::kThreads;
 constexpr uint32_t OSTAGE = INFO + 2 * 4 * BN;
 constexpr uint32_t BARS = OSTAGE + kTile;
 enum Bar { KV_FULL = 0, K_READY = 2, KV_EMPTY = 4, S_FULL = 6, P_READY = 8, O_DONE = 10, O_FREE = 12, Q_READY = 14,
-           Q_EMPTY = 15, OST0 = 16, OST1 = 17, FINAL = 18, N_BARS = 19 };
+           Q_EMPTY = 15, OST0 = 16, OST1 = 17, STG0 = 18, STG1 = 19, FINAL = 20, N_BARS = 21 };
 constexpr uint32_t TMEM_SLOT = BARS + 8 * N_BARS;
 constexpr uint32_t ABORT = TMEM_SLOT + 4;
 constexpr uint32_t TOTAL = ABORT + 4;
@@ -462,7 +462,7 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
     for (int i = 0; i < N_BARS; ++i) {
       uint32_t count = 1;
       if (i == K_READY || i == K_READY + 1 || i == P_READY || i == P_READY + 1 || i == O_FREE || i == O_FREE + 1 ||
-          i == OST0 || i == OST1)
+          i == OST0 || i == OST1 || i == STG0 || i == STG1)
         count = 128;
       if (i == Q_READY) count = prerot ? 1 : 256;
       ptx::mbar_init(bar(i), count);
@@ -669,23 +669,28 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
       // 128 arrive, thread 0 once its TMA store has read the tile), so that
       // no thread can still be waiting on a phase the other group has
       // already moved past.
-      const bool full = w.q1 == w.q0 + BM;
+      // (a unit without key tiles stores its zero rows directly: its thread 0
+      // has not waited for the group's other threads in O_DONE)
+      const bool full = w.q1 == w.q0 + BM && w.n > 0;
       bool ok_st = t == 0 ? (k == 0 || wait(OST1, (k - 1) & 1)) : wait(OST0, k & 1);
       if (!ok_st) break;
       if (full) {
 #pragma unroll
         for (int c = 0; c < D / 8; ++c) *reinterpret_cast<uint4*>(sm + OSTAGE + chunk_off(r, c)) = packed[c];
         ptx::fence_proxy_async_smem();
-        ptx::named_bar_sync(1 + t, 128);
-        if (r == 0) {
-          ptx::tma_store_4d(&tm_o, sbase + OSTAGE, 0, w.q0, h, b);
-          ptx::tma_store_4d(&tm_o, sbase + OSTAGE + kHalf, 64, w.q0, h, b);
-          ptx::bulk_commit_group();
-          ptx::bulk_wait_read_all();
-        }
       } else if (i < w.q1) {
 #pragma unroll
         for (int c = 0; c < D / 8; ++c) *reinterpret_cast<uint4*>(Orow + 8 * c) = packed[c];
+      }
+      // The group's rows are in the tile once all 128 threads arrived (a
+      // bounded wait, unlike a named barrier, if another warp gave up).
+      ptx::mbar_arrive(bar(STG0 + t));
+      if (full && r == 0) {
+        if (!wait(STG0 + t, (uint32_t)k & 1u)) break;
+        ptx::tma_store_4d(&tm_o, sbase + OSTAGE, 0, w.q0, h, b);
+        ptx::tma_store_4d(&tm_o, sbase + OSTAGE + kHalf, 64, w.q0, h, b);
+        ptx::bulk_commit_group();
+        ptx::bulk_wait_read_all();
       }
       ptx::mbar_arrive(bar(OST0 + t));
       if (i < w.q1)

@@ -220,6 +220,14 @@ __device__ __forceinline__ void mma_commit_w(uint32_t bar) {
       : "memory");
 }
 
+// 32-byte global store (one full sector per thread); the address must be
+// 32-byte aligned.
+__device__ __forceinline__ void st_global_v8(void* p, const uint32_t (&r)[8]) {
+  asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(r[0]), "r"(r[1]),
+               "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
+}
+
 // 2^x on the SFU (PTX ex2.approx.ftz.f32; ex2(-inf) = +0).
 __device__ __forceinline__ float ex2(float x) {
   float y;
