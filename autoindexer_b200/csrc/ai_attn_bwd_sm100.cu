@@ -1798,7 +1798,7 @@ int sm100_bwd(const AiAttnBwdArgs& a, float* delta, void* rot, bool rot_ready, c
       }
     }
   }
-  if (e == cudaSuccess) {
+  if (e == cudaSuccess && !f.layout.all_rows_owned) {
     ProfScope ps(AI_PROF_BWD_FILL, st);
     e = bwd_fill(a, st);
   }

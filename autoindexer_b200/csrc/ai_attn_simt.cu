@@ -385,20 +385,17 @@ __device__ __forceinline__ float dot16<float>(const uint4& x, const uint4& y) {
 // delta as above with 16-byte loads: kTpr = D * sizeof(T) / 16 consecutive
 // lanes share a row (one chunk each) and reduce by shuffles.  Requires
 // 16-byte aligned rows (checked on the host).
+// Grid (query-row blocks, batch x head): kTpr lanes per row, no 64-bit
+// index arithmetic.
 template <typename T, int D>
 __global__ void __launch_bounds__(256) delta_vec_kernel(const AiAttnBwdArgs a, float* delta) {
   constexpr int kTpr = D * (int)sizeof(T) / 16, kPer = 16 / (int)sizeof(T);
   static_assert(kTpr >= 1 && kTpr <= 32 && (32 % kTpr) == 0, "row chunking");
   const AiAttnFwdArgs& f = a.fwd;
-  const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const int64_t w = g / kTpr;
-  const int c = (int)(g % kTpr);
-  const int64_t total = (int64_t)f.batch * f.num_q_heads * f.seq_len;
+  const int i = blockIdx.x * (256 / kTpr) + (int)threadIdx.x / kTpr, c = (int)threadIdx.x % kTpr;
+  const int bh = blockIdx.y, b = bh / f.num_q_heads, h = bh - b * f.num_q_heads;
   float s = 0.f;
-  if (w < total) {
-    const int i = (int)(w % f.seq_len);
-    const int h = (int)((w / f.seq_len) % f.num_q_heads);
-    const int b = (int)(w / ((int64_t)f.seq_len * f.num_q_heads));
+  if (i < f.seq_len) {
     const T* O = static_cast<const T*>(f.out.ptr) + b * f.out.stride_b + h * f.out.stride_h + (int64_t)i * f.out.stride_t;
     const T* dO =
         static_cast<const T*>(a.dout.ptr) + b * a.dout.stride_b + h * a.dout.stride_h + (int64_t)i * a.dout.stride_t;
@@ -406,7 +403,7 @@ __global__ void __launch_bounds__(256) delta_vec_kernel(const AiAttnBwdArgs a, f
   }
 #pragma unroll
   for (int o = kTpr / 2; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-  if (w < total && c == 0) delta[w] = s;
+  if (i < f.seq_len && c == 0) delta[(int64_t)bh * f.seq_len + i] = s;
 }
 
 template <typename T>
@@ -690,6 +687,7 @@ static cudaError_t set_smem(K kernel, size_t bytes) {
 
 template <typename T, int D>
 static cudaError_t fwd_fill_impl(const AiAttnFwdArgs& a, cudaStream_t st) {
+  if (a.layout.all_rows_owned) return cudaSuccess;
   fwd_fill_kernel<T, D><<<dim3(a.seq_len, a.batch), 128, 0, st>>>(a);
   return cudaGetLastError();
 }
@@ -703,6 +701,7 @@ static cudaError_t fwd_impl(const AiAttnFwdArgs& a, cudaStream_t st) {
     fwd_kernel<T, D><<<dim3(a.layout.n_fwd_items, a.num_q_heads), kThreads, smem, st>>>(a);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
+  if (a.layout.all_rows_owned) return cudaSuccess;
   fwd_fill_kernel<T, D><<<dim3(a.seq_len, a.batch), 128, 0, st>>>(a);
   return cudaGetLastError();
 }
@@ -713,8 +712,9 @@ static cudaError_t launch_delta(const AiAttnBwdArgs& a, float* delta, cudaStream
   const AiAttnFwdArgs& f = a.fwd;
   const int64_t rows = (int64_t)f.batch * f.num_q_heads * f.seq_len;
   if (rows16<T>(f.out) && rows16<T>(a.dout)) {
-    constexpr int kTpr = D * (int)sizeof(T) / 16;
-    delta_vec_kernel<T, D><<<(unsigned)((rows * kTpr + 255) / 256), 256, 0, st>>>(a, delta);
+    constexpr int kTpr = D * (int)sizeof(T) / 16, kRpb = 256 / kTpr;
+    const dim3 grid((unsigned)((f.seq_len + kRpb - 1) / kRpb), (unsigned)(f.batch * f.num_q_heads));
+    delta_vec_kernel<T, D><<<grid, 256, 0, st>>>(a, delta);
   } else {
     delta_kernel<T, D><<<(unsigned)((rows * 32 + 255) / 256), 256, 0, st>>>(a, delta);
   }
@@ -738,6 +738,7 @@ static cudaError_t bwd_impl(const AiAttnBwdArgs& a, float* delta, cudaStream_t s
     dkdv_kernel<T, D><<<dim3(f.layout.n_kv_items, f.num_kv_heads), kThreads, smem, st>>>(a, delta);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
   }
+  if (f.layout.all_rows_owned) return cudaSuccess;
   bwd_fill_kernel<T, D><<<dim3(f.seq_len, f.batch), 128, 0, st>>>(a);
   return cudaGetLastError();
 }
@@ -749,6 +750,7 @@ static cudaError_t delta_impl(const AiAttnBwdArgs& a, float* delta, cudaStream_t
 
 template <typename T, int D>
 static cudaError_t bwd_fill_impl(const AiAttnBwdArgs& a, cudaStream_t st) {
+  if (a.fwd.layout.all_rows_owned) return cudaSuccess;
   bwd_fill_kernel<T, D><<<dim3(a.fwd.seq_len, a.fwd.batch), 128, 0, st>>>(a);
   return cudaGetLastError();
 }

@@ -93,6 +93,7 @@ int ai_attn_fwd(const AiAttnFwdArgs* a, void* stream) {
     cudaError_t ce = cudaSuccess;
     rc = ai::sm100_fwd(*a, st, &ce);
     if (rc != AI_OK) return rc;
+    if (a->layout.all_rows_owned) return AI_OK;
     ai::ProfScope ps(AI_PROF_FWD_FILL, st);
     return launch_status(ai::fwd_fill(*a, st));
   }

@@ -146,6 +146,7 @@ class CompiledLayout:
     n_fwd_abs_items: int         # leading fwd_items whose block has abs keys
     n_kv_abs_items: int          # leading kv_items that a block with abs keys sees
     pairs_per_head: int          # finite (query, key) logits of one head summed over the batch
+    all_rows_owned: bool = False  # every row of every batch row belongs to a block (no fill launches)
     host_blocks: np.ndarray = field(repr=False, default=None)
 
     def c_struct(self) -> "_lib.AiAttnLayout":
@@ -170,6 +171,7 @@ class CompiledLayout:
         L.kv_items = self.kv_items.data_ptr() if self.kv_items.numel() else None
         L.n_kv_items = int(self.kv_items.shape[0])
         L.n_kv_abs_items = int(self.n_kv_abs_items)
+        L.all_rows_owned = int(self.all_rows_owned)
         return L
 
 
@@ -317,5 +319,6 @@ def _compile(parsed_positions, batch, seq_len, head_dim, code, rotary_emb, devic
         rope_cs16=torch.stack([cos, sin], dim=-1).to(torch.float16).contiguous(),
         fwd_items=dev(fwd_items), kv_items=dev(kv_items), n_fwd_abs_items=n_abs, n_kv_abs_items=n_kv_abs,
         pairs_per_head=pairs,
+        all_rows_owned=bool(np.all(row_cov_np >= seq_len)),
         host_blocks=blocks_np,
     )

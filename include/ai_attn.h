@@ -43,7 +43,7 @@
 extern "C" {
 #endif
 
-#define AI_ATTN_ABI_VERSION 4
+#define AI_ATTN_ABI_VERSION 5
 
 typedef enum AiDtype {
   AI_DTYPE_BF16 = 0,
@@ -117,6 +117,8 @@ typedef struct AiAttnLayout {
   const int32_t* kv_items;    /* [n_kv_items][4]: row, j0, j1, 0 */
   int32_t n_kv_items;
   int32_t n_kv_abs_items;     /* the first n_kv_abs_items items see a block with AI_BLOCKF_ABS */
+  int32_t all_rows_owned;     /* 1: row_cov[b] == seq_len for every b (no diagonal-only rows), so the
+                                 fill launches are skipped; 0: not known (they run) */
 } AiAttnLayout;
 
 typedef struct AiAttnFwdArgs {

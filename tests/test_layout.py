@@ -110,3 +110,17 @@ def test_layout_cache_is_reused():
     a = _compile(lay, 1, int(g["T"]), 32, torch.float32, mod)
     b = _compile(lay, 1, int(g["T"]), 32, torch.float32, mod)
     assert a is b
+
+
+def test_all_rows_owned_flag():
+    """The layout tells the library when no row is diagonal-only, so the fill
+    launches are skipped; rows past the blocks' coverage keep them."""
+    g = load_golden("op2_d32")
+    mod, _ = golden_rope(g)
+    T = int(g["T"])
+    padded = _compile(ArrayLayout.from_golden(g), 1, T + 5, 32, torch.float32, mod)
+    assert not padded.all_rows_owned and padded.c_struct().all_rows_owned == 0
+    rows = RowLayouts()
+    rows.append(document_blocks([T // 2, T - T // 2], position_ids=np.arange(T)))
+    docs = _compile(rows, 1, T, 32, torch.float32, mod)
+    assert docs.all_rows_owned and docs.c_struct().all_rows_owned == 1
