@@ -403,7 +403,14 @@ using ws::C_S0;
 using ws::C_S1;
 using ws::C_O0;
 using ws::C_O1;
-using ws::kThreads;
+// 384 threads = three whole warpgroups (the register split below is per
+// warpgroup): warps 0-7 softmax, 8 TMA producer, 9 MMA, 10-11 K rotation (two
+// key rows per thread).  Launched at 168 registers a thread (64,512 for the
+// block), the softmax warpgroups raise theirs to 200 (a row's 128 scores stay
+// in registers) and warpgroup 2 lowers its to 104: 256 x 200 + 128 x 104.
+constexpr int kThreads = 384;
+constexpr uint32_t kRegLaunch = 168, kRegSoftmax = 200, kRegOther = 104;
+static_assert(256 * kRegSoftmax + 128 * kRegOther <= kThreads * kRegLaunch, "register split");
 // Output staging tile (128 rows x 128 bf16, 128-byte swizzle) for the TMA
 // store of a full unit; the two softmax groups take it in turn (OST0, OST1).
 constexpr uint32_t OSTAGE = INFO + 2 * 4 * BN;
@@ -461,7 +468,8 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
   if (tid == 0) {
     for (int i = 0; i < N_BARS; ++i) {
       uint32_t count = 1;
-      if (i == K_READY || i == K_READY + 1 || i == P_READY || i == P_READY + 1 || i == O_FREE || i == O_FREE + 1 ||
+      if (i == K_READY || i == K_READY + 1) count = 64;
+      if (i == P_READY || i == P_READY + 1 || i == O_FREE || i == O_FREE + 1 ||
           i == OST0 || i == OST1 || i == STG0 || i == STG1)
         count = 128;
       if (i == Q_READY) count = prerot ? 1 : 256;
@@ -478,6 +486,10 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sm + TMEM_SLOT);
+  if (warp < 8)
+    ptx::setmaxnreg_inc<kRegSoftmax>();
+  else
+    ptx::setmaxnreg_dec<kRegOther>();
 
   auto wait = [&](int i, uint32_t parity) -> bool {
     if (*s_abort) return false;
@@ -543,38 +555,37 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
         const bool fast = !w.masked && (k0 + BN <= w.kv_hi) && (k0 + BN - 1 <= w.q0);
         const int lim = min(i - k0, w.kv_hi - 1 - k0);
         const uint32_t* info = s_info + slot * BN;
-        auto load64 = [&](int hf, uint32_t (&r0)[32], uint32_t (&r1)[32]) {
-          ptx::tmem_ld32(tmem + lane_base + c_s + 64 * hf, r0);
-          ptx::tmem_ld32(tmem + lane_base + c_s + 64 * hf + 32, r1);
-          ptx::tmem_wait_ld();
-          if (!fast && !w.masked) {
+        // The row's 128 scores, read from TMEM once (cols 32 q + x in sq[x]).
+        uint32_t s0[32], s1[32], s2[32], s3[32];
+        ptx::tmem_ld32(tmem + lane_base + c_s, s0);
+        ptx::tmem_ld32(tmem + lane_base + c_s + 32, s1);
+        ptx::tmem_ld32(tmem + lane_base + c_s + 64, s2);
+        ptx::tmem_ld32(tmem + lane_base + c_s + 96, s3);
+        ptx::tmem_wait_ld();
+        if (!fast && !w.masked) {
 #pragma unroll
-            for (int x = 0; x < 32; ++x) {
-              const int c0 = 64 * hf + x, c1 = c0 + 32;
-              if (c0 > lim) r0[x] = 0xff800000u;  // -inf
-              if (c1 > lim) r1[x] = 0xff800000u;
-            }
-          } else if (w.masked) {
-#pragma unroll
-            for (int x = 0; x < 32; ++x) {
-              const int c0 = 64 * hf + x, c1 = c0 + 32;
-              if (!((info[c0] & AI_KEY_ATTN) && c0 <= lim)) r0[x] = 0xff800000u;
-              if (!((info[c1] & AI_KEY_ATTN) && c1 <= lim)) r1[x] = 0xff800000u;
-            }
+          for (int x = 0; x < 32; ++x) {
+            if (x > lim) s0[x] = 0xff800000u;  // -inf
+            if (x + 32 > lim) s1[x] = 0xff800000u;
+            if (x + 64 > lim) s2[x] = 0xff800000u;
+            if (x + 96 > lim) s3[x] = 0xff800000u;
           }
-        };
+        } else if (w.masked) {
+#pragma unroll
+          for (int x = 0; x < 32; ++x) {
+            if (!((info[x] & AI_KEY_ATTN) && x <= lim)) s0[x] = 0xff800000u;
+            if (!((info[x + 32] & AI_KEY_ATTN) && x + 32 <= lim)) s1[x] = 0xff800000u;
+            if (!((info[x + 64] & AI_KEY_ATTN) && x + 64 <= lim)) s2[x] = 0xff800000u;
+            if (!((info[x + 96] & AI_KEY_ATTN) && x + 96 <= lim)) s3[x] = 0xff800000u;
+          }
+        }
         float mxa = -CUDART_INF_F, mxb = -CUDART_INF_F, mxc = -CUDART_INF_F, mxd = -CUDART_INF_F;
 #pragma unroll
-        for (int hf = 0; hf < 2; ++hf) {
-          uint32_t r0[32], r1[32];
-          load64(hf, r0, r1);
-#pragma unroll
-          for (int x = 0; x < 32; x += 2) {
-            mxa = fmaxf(mxa, __uint_as_float(r0[x]));
-            mxb = fmaxf(mxb, __uint_as_float(r0[x + 1]));
-            mxc = fmaxf(mxc, __uint_as_float(r1[x]));
-            mxd = fmaxf(mxd, __uint_as_float(r1[x + 1]));
-          }
+        for (int x = 0; x < 32; x += 2) {
+          mxa = ptx::fmax3(mxa, __uint_as_float(s0[x]), __uint_as_float(s0[x + 1]));
+          mxb = ptx::fmax3(mxb, __uint_as_float(s1[x]), __uint_as_float(s1[x + 1]));
+          mxc = ptx::fmax3(mxc, __uint_as_float(s2[x]), __uint_as_float(s2[x + 1]));
+          mxd = ptx::fmax3(mxd, __uint_as_float(s3[x]), __uint_as_float(s3[x + 1]));
         }
         const float mx = fmaxf(fmaxf(mxa, mxb), fmaxf(mxc, mxd));
         const float m_new = fmaxf(m_use, mx * sl2);
@@ -589,38 +600,38 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
         }
         if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll
-          for (int cc = 0; cc < D / 32; ++cc) {
-            uint32_t rr[32];
-            ptx::tmem_ld32(tmem + lane_base + c_o + 32 * cc, rr);
+          for (int cc = 0; cc < D / 16; ++cc) {
+            uint32_t rr[16];
+            ptx::tmem_ld16(tmem + lane_base + c_o + 16 * cc, rr);
             ptx::tmem_wait_ld();
 #pragma unroll
-            for (int x = 0; x < 32; ++x) rr[x] = __float_as_uint(__uint_as_float(rr[x]) * alpha);
-            ptx::tmem_st32(tmem + lane_base + c_o + 32 * cc, rr);
+            for (int x = 0; x < 16; ++x) rr[x] = __float_as_uint(__uint_as_float(rr[x]) * alpha);
+            ptx::tmem_st16(tmem + lane_base + c_o + 16 * cc, rr);
           }
         }
         l *= alpha;
         const float msub = m_use == -CUDART_INF_F ? 0.f : m_use;
         const float2 nm2 = make_float2(-msub, -msub);
         float2 suma = make_float2(0.f, 0.f), sumb = make_float2(0.f, 0.f);
-#pragma unroll
-        for (int hf = 0; hf < 2; ++hf) {
-          uint32_t r0[32], r1[32], pk[32];
-          load64(hf, r0, r1);
+        // P (bf16 pairs) over S columns [0, 64): column 16 q + x holds keys
+        // 32 q + 2 x and 32 q + 2 x + 1 (the PV MMA's A operand); each score
+        // array is done with once its 16 columns are stored.
+        auto emit = [&](const uint32_t (&ra)[32], uint32_t col, float2& sum) {
+          uint32_t pk[16];
 #pragma unroll
           for (int x = 0; x < 16; ++x) {
             const float2 a01 =
-                __ffma2_rn(make_float2(__uint_as_float(r0[2 * x]), __uint_as_float(r0[2 * x + 1])), sl2x2, nm2);
-            const float2 a23 =
-                __ffma2_rn(make_float2(__uint_as_float(r1[2 * x]), __uint_as_float(r1[2 * x + 1])), sl2x2, nm2);
+                __ffma2_rn(make_float2(__uint_as_float(ra[2 * x]), __uint_as_float(ra[2 * x + 1])), sl2x2, nm2);
             const float2 p01 = make_float2(ptx::ex2(a01.x), ptx::ex2(a01.y));
-            const float2 p23 = make_float2(ptx::ex2(a23.x), ptx::ex2(a23.y));
-            suma = __fadd2_rn(suma, p01);
-            sumb = __fadd2_rn(sumb, p23);
+            sum = __fadd2_rn(sum, p01);
             pk[x] = tile::pack2(p01.x, p01.y);
-            pk[16 + x] = tile::pack2(p23.x, p23.y);
           }
-          ptx::tmem_st32(tmem + lane_base + c_s + 32 * hf, pk);
-        }
+          ptx::tmem_st16(tmem + lane_base + c_s + col, pk);
+        };
+        emit(s0, 0, suma);
+        emit(s1, 16, sumb);
+        emit(s2, 32, suma);
+        emit(s3, 48, sumb);
         l += (suma.x + suma.y) + (sumb.x + sumb.y);
         ptx::tmem_wait_st();
         ptx::tc_fence_before();
@@ -829,40 +840,47 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
     ptx::mma_commit_w(bar(FINAL));
     ptx::mbar_wait(bar(FINAL), 0, kWait);
   } else {
-    // ------------------------------------------------------------ K rotation (warps 10-13)
-    const int row = tid - 320;
+    // ------------------------------------------------------------ K rotation (warps 10-11)
+    // Thread rt rotates key rows rt and rt + 64 of each K tile in place by
+    // the keys' block positions (nothing to do for a pre-rotated copy) and
+    // records their key_info words.
+    const int rt = tid - 320;
     const __half2* cs16 = static_cast<const __half2*>(L.rope_cs16);
     int g = 0;
     for (int kr = 0, u = snake_unit(0); u < n_units && !*s_abort; u = snake_unit(++kr)) {
       const Unit w = load_unit(a, u, prerot);
       for (int j = 0; j < w.n; ++j, ++g) {
-        const int slot = g & 1, key = w.kv_lo + j * BN + row;
-        uint32_t info = 0;
-        int p = 0;
-        if (key < w.kv_hi) {
-          info = (uint32_t)__ldg(L.key_info + w.blk.key_off + key);
-          p = key_row(info, L.n_pos, a.status);
-        }
-        uint4 tab[16];
-        if (!w.k_pre) {
-          const uint4* tp = reinterpret_cast<const uint4*>(cs16 + (int64_t)p * (D / 2));
-#pragma unroll
-          for (int c = 0; c < 16; ++c) tab[c] = __ldg(tp + c);
-        }
+        const int slot = g & 1;
         if (!wait(KV_FULL + slot, (g >> 1) & 1)) break;
         const uint32_t kt = KB + (uint32_t)slot * kTile;
-        if (!w.k_pre && key < w.kv_hi) {
 #pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            uint4* pa = reinterpret_cast<uint4*>(sm + kt + chunk_off(row, c));
-            uint4* pb = reinterpret_cast<uint4*>(sm + kt + chunk_off(row, c + 8));
-            uint4 y1, y2;
-            tile::rotate8h(*pa, *pb, tab[2 * c], tab[2 * c + 1], y1, y2);
-            *pa = y1;
-            *pb = y2;
+        for (int hr = 0; hr < 2; ++hr) {
+          const int row = rt + 64 * hr, key = w.kv_lo + j * BN + row;
+          uint32_t info = 0;
+          if (key < w.kv_hi) {
+            info = (uint32_t)__ldg(L.key_info + w.blk.key_off + key);
+            if (!w.k_pre) {
+              const int p = key_row(info, L.n_pos, a.status);
+              const uint4* tp = reinterpret_cast<const uint4*>(cs16 + (int64_t)p * (D / 2));
+#pragma unroll
+              for (int qt = 0; qt < 4; ++qt) {
+                uint4 tab[4];
+#pragma unroll
+                for (int c = 0; c < 4; ++c) tab[c] = __ldg(tp + 4 * qt + c);
+#pragma unroll
+                for (int c = 0; c < 2; ++c) {
+                  uint4* pa = reinterpret_cast<uint4*>(sm + kt + chunk_off(row, 2 * qt + c));
+                  uint4* pb = reinterpret_cast<uint4*>(sm + kt + chunk_off(row, 2 * qt + c + 8));
+                  uint4 y1, y2;
+                  tile::rotate8h(*pa, *pb, tab[2 * c], tab[2 * c + 1], y1, y2);
+                  *pa = y1;
+                  *pb = y2;
+                }
+              }
+            }
           }
+          s_info[slot * BN + row] = info;
         }
-        s_info[slot * BN + row] = info;
         ptx::fence_proxy_async_smem();
         ptx::mbar_arrive(bar(K_READY + slot));
       }

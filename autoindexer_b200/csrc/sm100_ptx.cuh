@@ -228,6 +228,24 @@ __device__ __forceinline__ void st_global_v8(void* p, const uint32_t (&r)[8]) {
                : "memory");
 }
 
+// Per-warpgroup register budget (every warp of the warpgroup executes the
+// same one; the raises must fit in what the block was launched with).
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
+// max of three floats in one instruction.
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 // 2^x on the SFU (PTX ex2.approx.ftz.f32; ex2(-inf) = +0).
 __device__ __forceinline__ float ex2(float x) {
   float y;
