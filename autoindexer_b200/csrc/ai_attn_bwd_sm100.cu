@@ -740,10 +740,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ===========================================================================
 // dQ, warp-specialised (work items of blocks without abs keys)
 //
-// One CTA = one forward work item x two query heads of one GQA group.  448
+// Work unit = one forward work item x two query heads of one GQA group.  384
 // threads: warps 0-3 / 4-7 score groups of head 2y / 2y+1 (thread = query
-// row = TMEM lane); warp 8 TMA producer (64-key K and V tiles, 2-deep ring);
-// warp 9 MMA issuer; warps 10-13 rotate each K tile by the keys' block
+// row = TMEM lane); warp 8 TMA producer (64-key K and V tiles, 3-deep ring);
+// warp 9 MMA issuer; warps 10-11 rotate each K tile by the keys' block
 // positions.  TMEM per head t: S_t [128t .. +64), dP_t [+64 .. +128), dQ_t
 // accumulator [256 + 128t .. +128).  dS_t (bf16 pairs) overwrites the first 32
 // columns of S_t and is the A operand of dQ_t += dS_t.Krot; the next S_t
@@ -752,7 +752,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 // warp runs converged and elects one lane per MMA.
 // ===========================================================================
 namespace dqw {
-constexpr int BM = 128, BN = 64, kThreads = 448;
+// 384 threads = three whole warpgroups (the register split is per
+// warpgroup): warps 0-7 score groups, 8 TMA producer, 9 MMA, 10-11 K rotation
+// (one key row per thread).  Launched at 168 registers a thread, the score
+// warpgroups raise theirs to 184 (a tile's S and dP columns are read from
+// TMEM at once) and warpgroup 2 lowers its to 136: 256 x 184 + 128 x 136.
+constexpr int BM = 128, BN = 64, kThreads = 384;
+constexpr uint32_t kRegScore = 184, kRegOther = 136;
+static_assert(256 * kRegScore + 128 * kRegOther <= kThreads * 168, "register split");
 constexpr int kKS = 3;  // K / V ring depth (the refill of tile g + kKS starts when tile g is done)
 constexpr uint32_t Q0 = 0, Q1 = 32768, DO0 = 65536, DO1 = 98304;  // 128 x 128 bf16 each
 constexpr uint32_t KB = 131072, VB = KB + kKS * 16384;            // rings of kKS x (64 x 128 bf16)
@@ -798,9 +805,9 @@ __device__ __forceinline__ Unit load_unit(const AiAttnFwdArgs& f, int u, int pre
 //
 // One CTA per SM walks the work units u = blockIdx.x, blockIdx.x + gridDim.x,
 // ... (unit = forward work item x two query heads of one GQA group; items
-// longest first).  448 threads: warps 0-3 / 4-7 score groups of heads 2 hp /
+// longest first).  384 threads: warps 0-3 / 4-7 score groups of heads 2 hp /
 // 2 hp + 1 (thread = query row = TMEM lane); warp 8 TMA producer (64-key K and
-// V tiles, 3-deep ring); warp 9 MMA issuer; warps 10-13 rotate each K tile by
+// V tiles, 3-deep ring); warp 9 MMA issuer; warps 10-11 rotate each K tile by
 // the keys' block positions.  TMEM per head t: S_t [128t .. +64), dP_t
 // [+64 .. +128), dQ_t accumulator [256 + 128t .. +128).  dS_t (bf16 pairs)
 // overwrites the first 32 columns of S_t and is the A operand of dQ_t +=
@@ -834,9 +841,8 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
   if (tid == 0) {
     for (int i = 0; i < N_BARS; ++i) {
       uint32_t count = 1;
-      if ((i >= K_READY && i < K_READY + kKS) || i == DS_READY || i == DS_READY + 1 || i == DQ_FREE ||
-          i == DQ_FREE + 1)
-        count = 128;
+      if (i == DS_READY || i == DS_READY + 1 || i == DQ_FREE || i == DQ_FREE + 1) count = 128;
+      if (i >= K_READY && i < K_READY + kKS) count = 64;
       if (i == Q_READY) count = prerot ? 1 : 256;
       ptx::mbar_init(bar(i), count);
     }
@@ -851,6 +857,10 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(sm + TMEM_SLOT);
+  if (warp < 8)
+    ptx::setmaxnreg_inc<kRegScore>();
+  else
+    ptx::setmaxnreg_dec<kRegOther>();
 
   auto wait = [&](int i, uint32_t parity) -> bool {
     if (*s_abort) return false;
@@ -935,12 +945,18 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
         const int lim = min(i - k0, w.kv_hi - 1 - k0);
         const uint32_t* info = s_info + slot * BN;
         uint32_t pk[32];
+        // The tile's 64 S and 64 dP columns, read from TMEM at once.
+        uint32_t rs2[2][32], rp2[2][32];
 #pragma unroll
         for (int hf = 0; hf < 2; ++hf) {
-          uint32_t rs[32], rp[32];
-          ptx::tmem_ld32(tmem + lane_base + c_s + 32 * hf, rs);
-          ptx::tmem_ld32(tmem + lane_base + c_s + 64 + 32 * hf, rp);
-          ptx::tmem_wait_ld();
+          ptx::tmem_ld32(tmem + lane_base + c_s + 32 * hf, rs2[hf]);
+          ptx::tmem_ld32(tmem + lane_base + c_s + 64 + 32 * hf, rp2[hf]);
+        }
+        ptx::tmem_wait_ld();
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          const uint32_t(&rs)[32] = rs2[hf];
+          const uint32_t(&rp)[32] = rp2[hf];
           // Pairs of keys on the packed f32x2 pipe.
           auto pair = [&](int x2, bool ok0, bool ok1) {
             float2 arg = __ffma2_rn(make_float2(__uint_as_float(rs[2 * x2]), __uint_as_float(rs[2 * x2 + 1])), sl2x2,
@@ -1169,8 +1185,8 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
     ptx::mma_commit_w(bar(FINAL));
     ptx::mbar_wait(bar(FINAL), 0, kWait);
   } else {
-    // ------------------------------------------------------------ K rotation (warps 10-13)
-    const int rt = tid - 320, row = rt & 63, cg = rt >> 6;
+    // ------------------------------------------------------------ K rotation (warps 10-11)
+    const int row = tid - 320;  // 0..63: key row of the tile
     int g = 0;
     for (int kr = 0, u = snake_unit(0); u < n_units && !*s_abort; u = snake_unit(++kr)) {
       const Unit w = load_unit(f, u, prerot);
@@ -1182,27 +1198,28 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
           info = (uint32_t)__ldg(L.key_info + w.blk.key_off + key);
           p = key_row(info, L.n_pos, f.status);
         }
-        uint4 tab[8];
-        if (!w.k_pre) {
-          const uint4* tp = reinterpret_cast<const uint4*>(cs16 + (int64_t)p * (D / 2)) + 8 * cg;
-#pragma unroll
-          for (int c = 0; c < 8; ++c) tab[c] = __ldg(tp + c);
-        }
         if (!wait(KV_FULL + slot, (g / kKS) & 1)) break;
         const uint32_t kt = KB + 16384u * (uint32_t)slot;
         if (!w.k_pre && key < w.kv_hi) {
+          const uint4* tp = reinterpret_cast<const uint4*>(cs16 + (int64_t)p * (D / 2));
 #pragma unroll
-          for (int cc = 0; cc < 4; ++cc) {
-            const int c = 4 * cg + cc;
-            uint4* pa = reinterpret_cast<uint4*>(sm + kt + chunk_off<BN>(row, c));
-            uint4* pb = reinterpret_cast<uint4*>(sm + kt + chunk_off<BN>(row, c + 8));
-            uint4 y1, y2;
-            tile::rotate8h(*pa, *pb, tab[2 * cc], tab[2 * cc + 1], y1, y2);
-            *pa = y1;
-            *pb = y2;
+          for (int cg = 0; cg < 2; ++cg) {
+            uint4 tab[8];
+#pragma unroll
+            for (int c = 0; c < 8; ++c) tab[c] = __ldg(tp + 8 * cg + c);
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) {
+              const int c = 4 * cg + cc;
+              uint4* pa = reinterpret_cast<uint4*>(sm + kt + chunk_off<BN>(row, c));
+              uint4* pb = reinterpret_cast<uint4*>(sm + kt + chunk_off<BN>(row, c + 8));
+              uint4 y1, y2;
+              tile::rotate8h(*pa, *pb, tab[2 * cc], tab[2 * cc + 1], y1, y2);
+              *pa = y1;
+              *pb = y2;
+            }
           }
         }
-        if (cg == 0) s_info[slot * BN + row] = info;
+        s_info[slot * BN + row] = info;
         ptx::fence_proxy_async_smem();
         ptx::mbar_arrive(bar(K_READY + slot));
       }

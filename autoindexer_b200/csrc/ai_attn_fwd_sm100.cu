@@ -353,12 +353,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 //
 // Work unit = one work item (block, <= 128 query rows) x two query heads of
 // the same GQA group, so every rotated K tile and every V tile feeds 256 query
-// rows.  448 threads in roles:
+// rows.  384 threads in roles:
 //   warps 0-3   softmax of head 2y     (thread = query row = TMEM lane)
 //   warps 4-7   softmax of head 2y + 1
 //   warp  8     TMA producer: K and V tiles into a 2-deep ring
 //   warp  9     MMA issuer and TMEM owner
-//   warps 10-13 rotate each K tile in place by its keys' block positions
+//   warps 10-11 rotate each K tile in place by its keys' block positions
 // TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512).
 // Softmax t reads S_t, writes P_t (bf16, two per column) over the first 64
 // columns of S_t, and the PV MMA takes P_t straight from TMEM.  MMA order
@@ -372,7 +372,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 // they stay warp-uniform) and elect.sync picks the lane that issues.
 // ---------------------------------------------------------------------------
 namespace ws {
-constexpr int kThreads = 448;
 constexpr uint32_t Q0 = 0, Q1 = kTile, KB = 2 * kTile, VB = 4 * kTile;  // K ring at KB, V ring at VB
 constexpr uint32_t INFO = 6 * kTile;                                    // [2][128] u32
 constexpr uint32_t C_S0 = 0, C_S1 = 128, C_O0 = 256, C_O1 = 384;
