@@ -188,6 +188,79 @@ def test_bf16_full_size_prefix_matches_oracle(cuda_device):
     check_bf16(sl, want, "full-size prefix")
 
 
+def _full_size_run(rows, mod, B, T, Hq, Hkv, D, device, seed):
+    """Seeded bf16 inputs on the device, forward + backward through the C ABI;
+    returns the inputs and the outputs, all on the device."""
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(B, Hq, T, D, generator=g).to(torch.bfloat16).to(device)
+    k = torch.randn(B, Hkv, T, D, generator=g).to(torch.bfloat16).to(device)
+    v = torch.randn(B, Hkv, T, D, generator=g).to(torch.bfloat16).to(device)
+    dout = torch.randn(B, T, Hq, D, generator=g).to(torch.bfloat16).to(device)
+    layout = compile_layout(rows, B, T, D, torch.bfloat16, mod.to(device), device)
+    out, lse = attn_fwd(q, k, v, layout, D ** -0.5)
+    dq, dk, dv = attn_bwd(q, k, v, out, lse, dout, layout, D ** -0.5)
+    torch.cuda.synchronize(device)
+    assert read_status(device) == 0
+    return (q, k, v, dout), (out, lse, dq, dk, dv)
+
+
+def test_bf16_config4_varlen_prefix_matches_oracle(cuda_device):
+    """Config-4 shape: 64 sequences of U[64, 2048] tokens rescaled to sum to
+    65,536, packed in one row (Hq=32, Hkv=8, D=128, 2 RoPE sections).  A
+    sequence depends on nothing outside itself, so the first two (made 500
+    and 400 tokens long) are checked in full — out, lse, dQ, dK, dV — against
+    the oracle."""
+    T, Hq, Hkv, D, P = 65536, 32, 8, 128, 900
+    rng = np.random.default_rng(4)
+    raw = rng.integers(64, 2049, 62).astype(np.float64)
+    lens = np.maximum(np.round(raw / raw.sum() * (T - P)).astype(int), 1)
+    lens[-1] += (T - P) - lens.sum()
+    lens = [500, 400] + [int(x) for x in lens]
+    assert len(lens) == 64 and sum(lens) == T
+    sections = [(0, 32), (32, 64)]
+    streams = [np.arange(T), cursor_stream(T, rng)]
+    mod = SectionedRope(D, 1e6, [torch.as_tensor(x) for x in streams], sections)
+    rope = O.make_sectioned_rope(mod.inv_freq.numpy(), streams, sections)
+    rows = RowLayouts()
+    rows.append(document_blocks(lens, position_ids=np.arange(T)))
+    (q, k, v, dout), got = _full_size_run(rows, mod, 1, T, Hq, Hkv, D, cuda_device, seed=4)
+    qs, ks, vs = (x[:, :h, :P].double().cpu().numpy() for x, h in ((q, 8), (k, 2), (v, 2)))
+    dos = dout[:, :P, :8].double().cpu().numpy()
+    prefix = document_blocks([500, 400], position_ids=np.arange(P))
+    out, lse = O.attn_forward(qs, ks, vs, prefix, rope)
+    want = [out, lse, *O.attn_backward(qs, ks, vs, dos, prefix, rope)]
+    o, l, dq, dk, dv = got
+    sl = [t.double().cpu().numpy() for t in (o[:, :P, :8], l[:, :8, :P], dq[:, :8, :P], dk[:, :2, :P], dv[:, :2, :P])]
+    check_bf16(sl, want, "config-4 prefix")
+
+
+def test_bf16_config3_long_causal_prefix_matches_oracle(cuda_device):
+    """Config-3 shape: one causal sequence of 32,768 tokens (Hq=32, Hkv=8,
+    D=128) with three RoPE sections of 24 / 24 / 16 frequency slots (arange
+    and two cursor streams).  Rows below 1,024 depend only on keys below
+    1,024, so their output, lse and dQ are checked against the oracle on that
+    prefix (dK / dV of those keys also take every later row)."""
+    T, Hq, Hkv, D, P = 32768, 32, 8, 128, 1024
+    rng = np.random.default_rng(3)
+    sections = [(0, 24), (24, 48), (48, 64)]
+    streams = [np.arange(T), cursor_stream(T, rng), cursor_stream(T, rng)]
+    mod = SectionedRope(D, 1e6, [torch.as_tensor(x) for x in streams], sections)
+    rope = O.make_sectioned_rope(mod.inv_freq.numpy(), streams, sections)
+    rows = RowLayouts()
+    rows.append(document_blocks([T], position_ids=np.arange(T)))
+    (q, k, v, dout), got = _full_size_run(rows, mod, 1, T, Hq, Hkv, D, cuda_device, seed=3)
+    qs, ks, vs = (x[:, :h, :P].double().cpu().numpy() for x, h in ((q, 8), (k, 2), (v, 2)))
+    dos = dout[:, :P, :8].double().cpu().numpy()
+    prefix = document_blocks([P], position_ids=np.arange(P))
+    wo, wl = O.attn_forward(qs, ks, vs, prefix, rope)
+    wdq, _, _ = O.attn_backward(qs, ks, vs, dos, prefix, rope)
+    o, l, dq = (t.double().cpu().numpy() for t in (got[0][:, :P, :8], got[1][:, :8, :P], got[2][:, :8, :P]))
+    assert np.max(np.abs(o - wo)) <= BF16_OUT_ABS, f"config-3 out max-abs {np.max(np.abs(o - wo))}"
+    assert rel_l2(o, wo) <= BF16_REL
+    assert np.max(np.abs(l - wl)) <= BF16_OUT_ABS, f"config-3 lse max-abs {np.max(np.abs(l - wl))}"
+    assert rel_l2(dq, wdq) <= BF16_REL, f"config-3 dq rel-L2 {rel_l2(dq, wdq)}"
+
+
 @pytest.mark.parametrize("layout_kind", ["documents", "edit_chain", "edit_chain_g4"])
 def test_bf16_rotated_copies_match_in_kernel_rotation(layout_kind, cuda_device):
     """The fast path (Q and K rotated once into scratch, read by TMA) and the
