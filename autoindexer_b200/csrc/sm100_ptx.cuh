@@ -127,7 +127,7 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
 }
 
 // Tiled TMA store of a shared-memory box to global memory (bulk-group
-// completion; no multicast).  The writing threads must have made their smem
+// completion, this CTA's box only).  The writing threads must have made their smem
 // stores visible to the async proxy (fence_proxy_async_smem + a barrier).
 __device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, uint32_t src, int c0, int c1, int c2, int c3) {
   asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
