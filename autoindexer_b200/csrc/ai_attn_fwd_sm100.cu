@@ -410,12 +410,13 @@ using ws::C_O1;
 constexpr int kThreads = 384;
 constexpr uint32_t kRegLaunch = 168, kRegSoftmax = 200, kRegOther = 104;
 static_assert(256 * kRegSoftmax + 128 * kRegOther <= kThreads * kRegLaunch, "register split");
-// Output staging tile (128 rows x 128 bf16, 128-byte swizzle) for the TMA
-// store of a full unit; the two softmax groups take it in turn (OST0, OST1).
+// Output staging (128 rows x 64 bf16, 128-byte swizzle, 16 KB) per softmax
+// group: a full unit's O_t leaves as two 64-column TMA stores through its
+// group's own buffer, so neither group waits for the other's stores.
 constexpr uint32_t OSTAGE = INFO + 2 * 4 * BN;
 constexpr uint32_t BARS = OSTAGE + kTile;
 enum Bar { KV_FULL = 0, K_READY = 2, KV_EMPTY = 4, S_FULL = 6, P_READY = 8, O_DONE = 10, O_FREE = 12, Q_READY = 14,
-           Q_EMPTY = 15, OST0 = 16, OST1 = 17, STG0 = 18, STG1 = 19, FINAL = 20, N_BARS = 21 };
+           Q_EMPTY = 15, SFREE0 = 16, SFREE1 = 17, STG0 = 18, STG1 = 19, FINAL = 20, N_BARS = 21 };
 constexpr uint32_t TMEM_SLOT = BARS + 8 * N_BARS;
 constexpr uint32_t ABORT = TMEM_SLOT + 4;
 constexpr uint32_t TOTAL = ABORT + 4;
@@ -469,7 +470,7 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
       uint32_t count = 1;
       if (i == K_READY || i == K_READY + 1) count = 64;
       if (i == P_READY || i == P_READY + 1 || i == O_FREE || i == O_FREE + 1 ||
-          i == OST0 || i == OST1 || i == STG0 || i == STG1)
+          i == STG0 || i == STG1)
         count = 128;
       if (i == Q_READY) count = prerot ? 1 : 256;
       ptx::mbar_init(bar(i), count);
@@ -508,6 +509,7 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
     const float sl2 = a.scale * kLog2e;
     const float2 sl2x2 = make_float2(sl2, sl2);
     int g = 0, k = 0, ko = 0;  // ko: units with key tiles so far (O_DONE phases)
+    int nst = 0;               // this group's staging-buffer uses
     for (int u = snake_unit(k); u < n_units && !*s_abort; u = snake_unit(++k)) {
       const Unit w = load_unit(a, u, prerot);
       const int i = w.q0 + r, h = 2 * w.hp + t, b = w.blk.row;
@@ -671,38 +673,44 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
       }
       ptx::tc_fence_before();
       ptx::mbar_arrive(bar(O_FREE + t));
-      // Output rows: a full unit goes through the staging tile and one TMA
-      // store per 64-column block (coalesced, asynchronous); a unit whose
-      // item ends early is stored row by row (the TMA box would spill into
-      // the next block's rows).  Group 0 then group 1 use the tile; every
-      // thread of both groups takes part in the hand-off of every unit (all
-      // 128 arrive, thread 0 once its TMA store has read the tile), so that
-      // no thread can still be waiting on a phase the other group has
-      // already moved past.
-      // (a unit without key tiles stores its zero rows directly: its thread 0
-      // has not waited for the group's other threads in O_DONE)
+      // Output rows: a full unit goes through the group's staging buffer, one
+      // 64-column half at a time (its threads hand their rows to thread 0
+      // through STG_t; thread 0 frees the buffer through SFREE_t once the TMA
+      // store has read it); a unit whose item ends early is stored row by row
+      // (the TMA box would spill into the next block's rows).  A unit without
+      // key tiles stores its zero rows directly: its thread 0 has not waited
+      // for the group's other threads in O_DONE.
       const bool full = w.q1 == w.q0 + BM && w.n > 0;
-      bool ok_st = t == 0 ? (k == 0 || wait(OST1, (k - 1) & 1)) : wait(OST0, k & 1);
-      if (!ok_st) break;
+      const uint32_t buf = OSTAGE + (uint32_t)t * kHalf;
+      bool ok_st = true;
       if (full) {
 #pragma unroll
-        for (int c = 0; c < D / 8; ++c) *reinterpret_cast<uint4*>(sm + OSTAGE + chunk_off(r, c)) = packed[c];
-        ptx::fence_proxy_async_smem();
+        for (int hf = 0; hf < 2; ++hf) {
+          if (nst > 0 && !wait(SFREE0 + t, (uint32_t)(nst - 1) & 1u)) {
+            ok_st = false;
+            break;
+          }
+#pragma unroll
+          for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(sm + buf + chunk_off(r, c)) = packed[8 * hf + c];
+          ptx::fence_proxy_async_smem();
+          ptx::mbar_arrive(bar(STG0 + t));
+          if (r == 0) {
+            if (!wait(STG0 + t, (uint32_t)nst & 1u)) {
+              ok_st = false;
+              break;
+            }
+            ptx::tma_store_4d(&tm_o, sbase + buf, 64 * hf, w.q0, h, b);
+            ptx::bulk_commit_group();
+            ptx::bulk_wait_read_all();
+            ptx::mbar_arrive(bar(SFREE0 + t));
+          }
+          ++nst;
+        }
       } else if (i < w.q1) {
 #pragma unroll
         for (int c = 0; c < D / 8; ++c) *reinterpret_cast<uint4*>(Orow + 8 * c) = packed[c];
       }
-      // The group's rows are in the tile once all 128 threads arrived (a
-      // bounded wait, unlike a named barrier, if another warp gave up).
-      ptx::mbar_arrive(bar(STG0 + t));
-      if (full && r == 0) {
-        if (!wait(STG0 + t, (uint32_t)k & 1u)) break;
-        ptx::tma_store_4d(&tm_o, sbase + OSTAGE, 0, w.q0, h, b);
-        ptx::tma_store_4d(&tm_o, sbase + OSTAGE + kHalf, 64, w.q0, h, b);
-        ptx::bulk_commit_group();
-        ptx::bulk_wait_read_all();
-      }
-      ptx::mbar_arrive(bar(OST0 + t));
+      if (!ok_st) break;
       if (i < w.q1)
         a.lse[((int64_t)b * a.num_q_heads + h) * a.seq_len + i] = l > 0.f ? (m_use + log2f(l)) * kLn2 : -CUDART_INF_F;
       g += w.n;

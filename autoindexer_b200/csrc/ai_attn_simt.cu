@@ -389,21 +389,33 @@ __device__ __forceinline__ float dot16<float>(const uint4& x, const uint4& y) {
 // index arithmetic.
 template <typename T, int D>
 __global__ void __launch_bounds__(256) delta_vec_kernel(const AiAttnBwdArgs a, float* delta) {
-  constexpr int kTpr = D * (int)sizeof(T) / 16, kPer = 16 / (int)sizeof(T);
+  // kR rows per lane group (kRpb rows apart), their loads issued before any
+  // use: more bytes in flight per thread for this HBM-bound pass.
+  constexpr int kTpr = D * (int)sizeof(T) / 16, kPer = 16 / (int)sizeof(T), kRpb = 256 / kTpr, kR = 2;
   static_assert(kTpr >= 1 && kTpr <= 32 && (32 % kTpr) == 0, "row chunking");
   const AiAttnFwdArgs& f = a.fwd;
-  const int i = blockIdx.x * (256 / kTpr) + (int)threadIdx.x / kTpr, c = (int)threadIdx.x % kTpr;
+  const int i0 = blockIdx.x * (kRpb * kR) + (int)threadIdx.x / kTpr, c = (int)threadIdx.x % kTpr;
   const int bh = blockIdx.y, b = bh / f.num_q_heads, h = bh - b * f.num_q_heads;
-  float s = 0.f;
-  if (i < f.seq_len) {
-    const T* O = static_cast<const T*>(f.out.ptr) + b * f.out.stride_b + h * f.out.stride_h + (int64_t)i * f.out.stride_t;
-    const T* dO =
-        static_cast<const T*>(a.dout.ptr) + b * a.dout.stride_b + h * a.dout.stride_h + (int64_t)i * a.dout.stride_t;
-    s = dot16<T>(__ldg(reinterpret_cast<const uint4*>(O + kPer * c)), __ldg(reinterpret_cast<const uint4*>(dO + kPer * c)));
+  const T* O0 = static_cast<const T*>(f.out.ptr) + b * f.out.stride_b + h * f.out.stride_h + kPer * c;
+  const T* dO0 = static_cast<const T*>(a.dout.ptr) + b * a.dout.stride_b + h * a.dout.stride_h + kPer * c;
+  uint4 xo[kR], xd[kR];
+#pragma unroll
+  for (int r = 0; r < kR; ++r) {
+    const int i = i0 + r * kRpb;
+    xo[r] = xd[r] = make_uint4(0, 0, 0, 0);
+    if (i < f.seq_len) {
+      xo[r] = __ldg(reinterpret_cast<const uint4*>(O0 + (int64_t)i * f.out.stride_t));
+      xd[r] = __ldg(reinterpret_cast<const uint4*>(dO0 + (int64_t)i * a.dout.stride_t));
+    }
   }
 #pragma unroll
-  for (int o = kTpr / 2; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-  if (i < f.seq_len && c == 0) delta[(int64_t)bh * f.seq_len + i] = s;
+  for (int r = 0; r < kR; ++r) {
+    const int i = i0 + r * kRpb;
+    float s = dot16<T>(xo[r], xd[r]);
+#pragma unroll
+    for (int o = kTpr / 2; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (i < f.seq_len && c == 0) delta[(int64_t)bh * f.seq_len + i] = s;
+  }
 }
 
 template <typename T>
@@ -712,7 +724,7 @@ static cudaError_t launch_delta(const AiAttnBwdArgs& a, float* delta, cudaStream
   const AiAttnFwdArgs& f = a.fwd;
   const int64_t rows = (int64_t)f.batch * f.num_q_heads * f.seq_len;
   if (rows16<T>(f.out) && rows16<T>(a.dout)) {
-    constexpr int kTpr = D * (int)sizeof(T) / 16, kRpb = 256 / kTpr;
+    constexpr int kTpr = D * (int)sizeof(T) / 16, kRpb = 256 / kTpr * 2;
     const dim3 grid((unsigned)((f.seq_len + kRpb - 1) / kRpb), (unsigned)(f.batch * f.num_q_heads));
     delta_vec_kernel<T, D><<<grid, 256, 0, st>>>(a, delta);
   } else {
