@@ -826,6 +826,10 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
                    const __grid_constant__ CUtensorMap tm_do, const __grid_constant__ CUtensorMap tm_kr,
                    const int prerot, const int n_units) {
   using namespace dqw;
+  // The dK/dV kernel launched after this one reads nothing it writes: let it
+  // start as soon as every CTA here has started, so its CTAs take each SM as
+  // this kernel's CTA there finishes.
+  if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = tile::align1024(smem_raw);
   const uint32_t sbase = ptx::smem_u32(sm);
@@ -1809,9 +1813,23 @@ int sm100_bwd(const AiAttnBwdArgs& a, float* delta, void* rot, bool rot_ready, c
       e = cudaFuncSetAttribute(dkdv_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kvw::kSmem);
       if (e == cudaSuccess) {
         ProfScope ps(AI_PROF_DKDV, st);
-        dkdv_ws_kernel<<<dim3(n_plain, f.num_kv_heads), kvw::kThreads, kvw::kSmem, st>>>(
-            a, delta, tk, tv, pre ? tqr : tq, tdo, tkr, pre ? 1 : 0);
-        e = cudaGetLastError();
+        // Programmatic dependent launch: the kernel before this one (the
+        // persistent dQ, which reads nothing this one writes and writes
+        // nothing it reads) signals at the start of each CTA, so these CTAs
+        // fill the SMs its CTAs leave; everything before that kernel is done.
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(n_plain, f.num_kv_heads);
+        cfg.blockDim = dim3(kvw::kThreads);
+        cfg.dynamicSmemBytes = kvw::kSmem;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        e = cudaLaunchKernelEx(&cfg, dkdv_ws_kernel, a, (const float*)delta, tk, tv, pre ? tqr : tq, tdo, tkr,
+                               pre ? 1 : 0);
+        if (e == cudaSuccess) e = cudaGetLastError();
       }
     }
   }
