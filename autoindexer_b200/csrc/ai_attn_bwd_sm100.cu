@@ -1242,26 +1242,34 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
 // dK / dV, warp-specialised (key tiles whose blocks have no abs keys)
 //
 // One CTA = 128 keys of one batch row x one KV head.  A "step" is one
-// 64-row query tile of a block x one query head of the GQA group.  448
+// 64-row query tile of a block x one query head of the GQA group.  640
 // threads in roles:
-//   warps 0-3, 4-7  two score groups, taking even / odd steps (thread = key =
+//   warps 0-15      four score groups of four warps, group t taking query
+//                   columns [16t, 16t + 16) of every step (thread = key =
 //                   TMEM lane): P^T = exp(S^T - lse), dS^T = P^T (dP^T - delta)
 //                   scale, written back into TMEM as bf16 pairs;
-//   warp 8          TMA producer (V once, raw K per block, Q and dO per step)
-//   warp 9          MMA issuer and TMEM owner
-//   warps 10-13     rotate K per block and each Q tile in place; stage the
-//                   step's lse / delta rows in smem.
+//   warp 16         TMA producer (V once, raw K per block, Q and dO per step)
+//   warp 17         MMA issuer and TMEM owner
+//   warps 18-19     rotate K per block (two keys a thread) and each Q tile in
+//                   place (one row a thread); stage the step's lse / delta
+//                   rows in smem.
 // TMEM: S^T / dP^T double-buffered by step parity (4 x 64 columns), dV and
 // dKrot accumulators (128 each).  dV += P^T dO and dKrot += dS^T Qrot take
 // their A operands from TMEM; the scores of step s + 2 reuse that buffer
 // right after those MMAs (one thread's MMAs execute in issue order), and the
 // producer alone waits for them before refilling the Q / dO slot.  The MMA
-// warp runs converged and elects one lane per MMA.  At the end of a block score group 0 rotates
-// dKrot back by the keys' block positions into an fp32 dK accumulator in
-// smem, so keys seen by several blocks are summed without atomics.
+// warp runs converged and elects one lane per MMA.  At the end of a block the
+// score groups rotate dKrot back by the keys' block positions (group t the
+// rotation pairs (d, d + 64), d in [16t, 16t + 16)) into an fp32 dK
+// accumulator in smem, so keys seen by several blocks are summed without
+// atomics.
 // ===========================================================================
 namespace kvw {
-constexpr int BN = 128, BQ = 64, kThreads = 448;
+// 640 threads (five whole warpgroups): warps 0-15 four score groups of 16
+// query columns each, 16 TMA producer, 17 MMA issuer, 18-19 rotation.
+constexpr int BN = 128, BQ = 64, kThreads = 640, kGroups = 4, kCols = BQ / kGroups;
+constexpr int kRot = kThreads - 32 * (4 * kGroups + 2);  // rotation threads
+static_assert(kRot == 64 && BQ == kRot && BN == 2 * kRot, "rotation: one Q row, two K rows per thread");
 // Q / dO ring depth: the load of step s + kQS starts when step s's dV / dK
 // MMAs are done, so with 3 stages it has about two steps of MMA time to land.
 constexpr int kQS = 3;
@@ -1327,14 +1335,14 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
   if (tid == 0) {
     for (int i = 0; i < N_BARS; ++i) {
       uint32_t count = 1;
-      if (i == K_READY || (i >= Q_READY && i < Q_READY + kQS)) count = 128;
-      if (i == P_READY || i == P_READY + 1 || i == FOLD_DONE) count = 256;
+      if (i == K_READY || (i >= Q_READY && i < Q_READY + kQS)) count = kRot;
+      if (i == P_READY || i == P_READY + 1 || i == FOLD_DONE) count = 32 * 4 * kGroups;
       ptx::mbar_init(bar(i), count);
     }
     *s_abort = 0;
     ptx::fence_mbar_init();
   }
-  if (warp == 9) {
+  if (warp == 4 * kGroups + 1) {
     ptx::tmem_alloc(sbase + TMEM_SLOT, kTmemCols);
     ptx::tmem_relinquish();
   }
@@ -1357,7 +1365,7 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
   };
   auto n_steps_of = [&](const Block& blk) { return ((blk.e - max(blk.s, j0) + BQ - 1) / BQ) * G; };
 
-  if (warp < 8) {
+  if (warp < 4 * kGroups) {
     // ------------------------------------------------------------ score groups
     const int t = warp / 4, lrow = tid % 128, j = j0 + lrow;
     const uint32_t lane_base = (uint32_t)((warp % 4) * 32) << 16;
@@ -1378,14 +1386,14 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
         const int x = s & 1, qslot = s % kQS, q0 = qs + (st / G) * BQ, q1 = min(q0 + BQ, blk.e);
         if (!wait(Q_READY + qslot, (s / kQS) & 1) || !wait(S_FULL + x, (s >> 1) & 1)) break;
         ptx::tc_fence_after();
-        // This group's 32 query columns of the step: c0 + [0, 32).
-        const int c0 = 32 * t;
+        // This group's 16 query columns of the step: c0 + [0, 16).
+        const int c0 = kCols * t;
         const float* nlse2 = s_stats + qslot * 2 * BQ + c0;  // -lse2 per query row
         const float* ndlt = nlse2 + BQ;                       // -scale * delta per query row
         const uint32_t cb = tmem + lane_base + C_BUF + 128u * (uint32_t)x + (uint32_t)c0;
-        uint32_t rs[32], rp[32];
-        ptx::tmem_ld32(cb, rs);
-        ptx::tmem_ld32(cb + 64, rp);
+        uint32_t rs[kCols], rp[kCols];
+        ptx::tmem_ld16(cb, rs);
+        ptx::tmem_ld16(cb + 64, rp);
         // Whole-step masks: causal (j <= i) holds for every pair when the tile
         // lies wholly above the query rows, and every row is in the block when
         // the tile is full.
@@ -1394,7 +1402,7 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
         // per-element branch there costs as much as the rest of the step).
         const bool plain = no_causal && rows_full;
         const int clo = j - q0 - c0, chi = q1 - q0 - c0;  // general path: clo <= c < chi
-        uint32_t pk[16], dk[16];
+        uint32_t pk[kCols / 2], dk[kCols / 2];
         ptx::tmem_wait_ld();
         auto pair = [&](int x2, bool ok0, bool ok1) {
           const int c = 2 * x2;
@@ -1411,18 +1419,18 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
         };
         if (plain) {
 #pragma unroll
-          for (int x2 = 0; x2 < 16; ++x2) pair(x2, key_ok, key_ok);
+          for (int x2 = 0; x2 < kCols / 2; ++x2) pair(x2, key_ok, key_ok);
         } else {
 #pragma unroll
-          for (int x2 = 0; x2 < 16; ++x2) {
+          for (int x2 = 0; x2 < kCols / 2; ++x2) {
             const int c = 2 * x2;
             pair(x2, key_ok && c >= clo && c < chi, key_ok && c + 1 >= clo && c + 1 < chi);
           }
         }
-        // P^T / dS^T of these columns go over the first 16 of the group's own
-        // 32 score columns (bf16 pairs), where the dV / dK MMAs read them.
-        ptx::tmem_st16(cb, pk);
-        ptx::tmem_st16(cb + 64, dk);
+        // P^T / dS^T of these columns go over the first 8 of the group's own
+        // 16 score columns (bf16 pairs), where the dV / dK MMAs read them.
+        ptx::tmem_st8(cb, pk);
+        ptx::tmem_st8(cb + 64, dk);
         ptx::tmem_wait_st();
         ptx::tc_fence_before();
         ptx::mbar_arrive(bar(P_READY + x));
@@ -1430,24 +1438,23 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
       if (*s_abort) break;
       {
         // Fold this block's dKrot into dK: dK += R(key position)^T dKrot;
-        // group t takes the rotation pairs (d, d + 64) with d in [32t, 32t + 32).
+        // group t takes the rotation pairs (d, d + 64) with d in [16t, 16t + 16).
         if (!wait(BLK_DONE, nb & 1)) break;
         ptx::tc_fence_after();
         const int p = key_row(info, L.n_pos, f.status);
         const uint4* tp = reinterpret_cast<const uint4*>(cs16 + (int64_t)p * (D / 2));
         {
-          const int hf = t;
-          uint32_t g1[32], g2[32];
-          ptx::tmem_ld32(tmem + lane_base + C_DKR + 32 * hf, g1);
-          ptx::tmem_ld32(tmem + lane_base + C_DKR + 64 + 32 * hf, g2);
+          uint32_t g1[kCols], g2[kCols];
+          ptx::tmem_ld16(tmem + lane_base + C_DKR + kCols * t, g1);
+          ptx::tmem_ld16(tmem + lane_base + C_DKR + 64 + kCols * t, g2);
           ptx::tmem_wait_ld();
 #pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            const uint4 tv = __ldg(tp + 8 * hf + q);
+          for (int q = 0; q < kCols / 4; ++q) {
+            const uint4 tv = __ldg(tp + (kCols / 4) * t + q);
             const __half2* h2 = reinterpret_cast<const __half2*>(&tv);
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
-              const int xx = 4 * q + u, d = 32 * hf + xx;
+              const int xx = 4 * q + u, d = kCols * t + xx;
               const float2 csn = __half22float2(h2[u]);
               const float v1 = __uint_as_float(g1[xx]), v2 = __uint_as_float(g2[xx]);
               s_dk[d * BN + lrow] += v1 * csn.x + v2 * csn.y;
@@ -1460,8 +1467,8 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
       }
       ++nb;
     }
-    // Epilogue: group t writes the columns it folded, d in [32t, 32t + 32)
-    // and [64 + 32t, 96 + 32t), of dK (smem) and dV (TMEM; the last block's
+    // Epilogue: group t writes the columns it folded, d in [16t, 16t + 16)
+    // and [64 + 16t, 80 + 16t), of dK (smem) and dV (TMEM; the last block's
     // MMAs are done, its fold waited for them).
     if (!*s_abort) {
       ptx::tc_fence_after();
@@ -1471,22 +1478,28 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
           static_cast<__nv_bfloat16*>(a.dv.ptr) + b * a.dv.stride_b + hk * a.dv.stride_h + (int64_t)j * a.dv.stride_t;
 #pragma unroll
       for (int h2 = 0; h2 < 2; ++h2) {
-        const int cc = t + 2 * h2;
-        float v[32];
+        const int d0 = kCols * t + 64 * h2;
+        float v[kCols];
 #pragma unroll
-        for (int x = 0; x < 32; ++x) v[x] = s_dk[(32 * cc + x) * BN + lrow];
-        if (j < j1) store_bf16_row32(dk_row + 32 * cc, v);
-        uint32_t rr[32];
+        for (int x = 0; x < kCols; ++x) v[x] = s_dk[(d0 + x) * BN + lrow];
+        if (j < j1) {
+          *reinterpret_cast<uint4*>(dk_row + d0) = tile::pack8(*reinterpret_cast<const float(*)[8]>(v));
+          *reinterpret_cast<uint4*>(dk_row + d0 + 8) = tile::pack8(*reinterpret_cast<const float(*)[8]>(v + 8));
+        }
+        uint32_t rr[kCols];
         if (any) {
-          ptx::tmem_ld32(tmem + lane_base + C_DV + 32 * cc, rr);
+          ptx::tmem_ld16(tmem + lane_base + C_DV + d0, rr);
           ptx::tmem_wait_ld();
         }
 #pragma unroll
-        for (int x = 0; x < 32; ++x) v[x] = any ? __uint_as_float(rr[x]) : 0.f;
-        if (j < j1) store_bf16_row32(dv_row + 32 * cc, v);
+        for (int x = 0; x < kCols; ++x) v[x] = any ? __uint_as_float(rr[x]) : 0.f;
+        if (j < j1) {
+          *reinterpret_cast<uint4*>(dv_row + d0) = tile::pack8(*reinterpret_cast<const float(*)[8]>(v));
+          *reinterpret_cast<uint4*>(dv_row + d0 + 8) = tile::pack8(*reinterpret_cast<const float(*)[8]>(v + 8));
+        }
       }
     }
-  } else if (warp == 8) {
+  } else if (warp == 4 * kGroups) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
       ptx::prefetch_tmap(&tm_k);
@@ -1523,7 +1536,7 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
         ++nb;
       }
     }
-  } else if (warp == 9) {
+  } else if (warp == 4 * kGroups + 1) {
     // ------------------------------------------------------------ MMA issuer
     // Whole warp (warp-uniform descriptors); one elected lane issues.
     // The tensor core's instruction queue holds only a couple of MMAs, so the
@@ -1605,8 +1618,8 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
         const uint32_t cb = tmem + C_BUF + 128u * (uint32_t)x;
 #pragma unroll
         for (int kk = 0; kk < BQ / 16; ++kk) {
-          // query rows 16 kk .. 16 kk + 15: packed by score group kk / 2
-          const uint32_t ca = cb + 32u * (uint32_t)(kk >> 1) + 8u * (uint32_t)(kk & 1);
+          // query rows 16 kk .. 16 kk + 15: packed by score group kk
+          const uint32_t ca = cb + (uint32_t)(kCols * kk);
           const uint64_t ko = (uint64_t)(2048 * kk) >> 4;
           ptx::mma_ts_w(tmem + C_DV, ca, dqa + kDo + ko, idesc_acc, (dv_started || kk > 0) ? 1u : 0u);
           ptx::mma_ts_w(tmem + C_DKR, ca + 64u, dqa + ko, idesc_acc, (s > sb || kk > 0) ? 1u : 0u);
@@ -1624,82 +1637,85 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
     ptx::mma_commit_w(bar(FINAL));
     ptx::mbar_wait(bar(FINAL), 0, kWait);
   } else {
-    // ------------------------------------------------------------ rotation (warps 10-13)
-    const int rt = tid - 320;  // 0..127
+    // ------------------------------------------------------------ rotation (warps 18-19)
+    const int rt = tid - 32 * (4 * kGroups + 2);  // 0..63: Q row rt, K rows rt and rt + 64
     BlockIter it(&L, b, j0, j1);
     Block blk;
     int s = 0, nb = 0;
     while (!*s_abort && it.next(blk)) {
-      // K row rt by this block's key position (already rotated when the block
+      // K rows by this block's key position (already rotated when the block
       // reads the once-rotated copy).
       {
         const bool k_pre = prerot && (blk.flags & AI_BLOCKF_OWNPOS);
-        const int key = j0 + rt;
-        uint32_t info = 0;
-        int p = 0;
-        if (key < min(j1, blk.e)) {
-          info = (uint32_t)__ldg(L.key_info + blk.key_off + key);
-          p = key_row(info, L.n_pos, f.status);
-        }
-        uint4 tab[16];
-        if (!k_pre) {
-          const uint4* tp = reinterpret_cast<const uint4*>(cs16 + (int64_t)p * (D / 2));
+        const int kend = min(j1, blk.e);
+        int p[2] = {0, 0};
 #pragma unroll
-          for (int c = 0; c < 16; ++c) tab[c] = __ldg(tp + c);
+        for (int u = 0; u < 2; ++u) {
+          const int key = j0 + rt + kRot * u;
+          if (key < kend) p[u] = key_row((uint32_t)__ldg(L.key_info + blk.key_off + key), L.n_pos, f.status);
         }
         if (!wait(K_FULL, nb & 1)) break;
-        if (!k_pre && key < min(j1, blk.e)) {
+#pragma unroll 1
+        for (int u = 0; u < 2; ++u) {
+          const int kr = rt + kRot * u;
+          if (k_pre || j0 + kr >= kend) continue;
+          // (a quarter of the row at a time: these warps have 96 registers)
+          const uint4* tp = reinterpret_cast<const uint4*>(cs16 + (int64_t)(u ? p[1] : p[0]) * (D / 2));
 #pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            uint4* pa = reinterpret_cast<uint4*>(sm + K + chunk_off<BN>(rt, c));
-            uint4* pb = reinterpret_cast<uint4*>(sm + K + chunk_off<BN>(rt, c + 8));
-            uint4 y1, y2;
-            tile::rotate8h(*pa, *pb, tab[2 * c], tab[2 * c + 1], y1, y2);
-            *pa = y1;
-            *pb = y2;
+          for (int qt = 0; qt < 4; ++qt) {
+            uint4 tab[4];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) tab[c] = __ldg(tp + 4 * qt + c);
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+              uint4* pa = reinterpret_cast<uint4*>(sm + K + chunk_off<BN>(kr, 2 * qt + c));
+              uint4* pb = reinterpret_cast<uint4*>(sm + K + chunk_off<BN>(kr, 2 * qt + c + 8));
+              uint4 y1, y2;
+              tile::rotate8h(*pa, *pb, tab[2 * c], tab[2 * c + 1], y1, y2);
+              *pa = y1;
+              *pb = y2;
+            }
           }
         }
         ptx::fence_proxy_async_smem();
         ptx::mbar_arrive(bar(K_READY));
       }
       const int qs = max(blk.s, j0), nsteps = n_steps_of(blk);
-      const int r = rt & 63, cg = rt >> 6;
+      const int r = rt;
       for (int st = 0; st < nsteps; ++st, ++s) {
         const int qslot = s % kQS, q0 = qs + (st / G) * BQ, q1 = min(q0 + BQ, blk.e), h = hk * G + st % G;
         const int i = q0 + r;
-        // Row position, table and row statistics are fetched before the TMA wait.
+        // Row position and row statistics are fetched before the TMA wait.
         int p = 0;
         float l2 = CUDART_INF_F, dl = 0.f;
         if (i < q1) {
           p = clamp_row(__ldg(L.q_pos + (int64_t)b * f.seq_len + i), L.n_pos, f.status);
-          if (cg == 0) {
-            const int64_t idx = ((int64_t)b * f.num_q_heads + h) * f.seq_len + i;
-            l2 = lse_log2(__ldg(f.lse + idx));
-            dl = __ldg(delta + idx);
-          }
-        }
-        uint4 tab[8];
-        if (!prerot) {
-          const uint4* tp = reinterpret_cast<const uint4*>(cs16 + (int64_t)p * (D / 2)) + 8 * cg;
-#pragma unroll
-          for (int c = 0; c < 8; ++c) tab[c] = __ldg(tp + c);
+          const int64_t idx = ((int64_t)b * f.num_q_heads + h) * f.seq_len + i;
+          l2 = lse_log2(__ldg(f.lse + idx));
+          dl = __ldg(delta + idx);
         }
         if (!wait(Q_FULL + qslot, (s / kQS) & 1)) break;
         const uint32_t qb = Q + 16384u * (uint32_t)qslot;
+        if (!prerot) {
+          const uint4* tp = reinterpret_cast<const uint4*>(cs16 + (int64_t)p * (D / 2));
 #pragma unroll
-        for (int cc = 0; cc < (prerot ? 0 : 4); ++cc) {
-          const int c = 4 * cg + cc;
-          uint4* pa = reinterpret_cast<uint4*>(sm + qb + chunk_off<BQ>(r, c));
-          uint4* pb = reinterpret_cast<uint4*>(sm + qb + chunk_off<BQ>(r, c + 8));
-          uint4 y1, y2;
-          tile::rotate8h(*pa, *pb, tab[2 * cc], tab[2 * cc + 1], y1, y2);
-          *pa = y1;
-          *pb = y2;
+          for (int qt = 0; qt < 4; ++qt) {
+            uint4 tab[4];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) tab[c] = __ldg(tp + 4 * qt + c);
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+              uint4* pa = reinterpret_cast<uint4*>(sm + qb + chunk_off<BQ>(r, 2 * qt + c));
+              uint4* pb = reinterpret_cast<uint4*>(sm + qb + chunk_off<BQ>(r, 2 * qt + c + 8));
+              uint4 y1, y2;
+              tile::rotate8h(*pa, *pb, tab[2 * c], tab[2 * c + 1], y1, y2);
+              *pa = y1;
+              *pb = y2;
+            }
+          }
         }
-        if (cg == 0) {
-          s_stats[qslot * 2 * BQ + r] = -l2;
-          s_stats[qslot * 2 * BQ + BQ + r] = -(dl * f.scale);
-        }
+        s_stats[qslot * 2 * BQ + r] = -l2;
+        s_stats[qslot * 2 * BQ + BQ + r] = -(dl * f.scale);
         ptx::fence_proxy_async_smem();
         ptx::mbar_arrive(bar(Q_READY + qslot));
       }
@@ -1709,7 +1725,7 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
 
   ptx::tc_fence_before();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == 4 * kGroups + 1) {
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tmem, kTmemCols);
   }
