@@ -349,7 +349,7 @@ def run_ours(args):
         "gpu_launches": int(round(launches_per_step * args.steps)),
         "clocks": clocks.summary(),
     }
-    if rank == 0 and not args.no_cpu_baseline:
+    if world == 1 and not args.no_cpu_baseline:  # the CPU baseline is an N=1 figure
         line["cpu_baseline"] = cpu_baseline(rows, host, seed=0)
     if rank == 0:
         print(json.dumps(line), flush=True)
