@@ -415,8 +415,18 @@ static_assert(256 * kRegSoftmax + 128 * kRegOther <= kThreads * kRegLaunch, "reg
 // group's own buffer, so neither group waits for the other's stores.
 constexpr uint32_t OSTAGE = INFO + 2 * 4 * BN;
 constexpr uint32_t BARS = OSTAGE + kTile;
-enum Bar { KV_FULL = 0, K_READY = 2, KV_EMPTY = 4, S_FULL = 6, P_READY = 8, O_DONE = 10, O_FREE = 12, Q_READY = 14,
-           Q_EMPTY = 15, SFREE0 = 16, SFREE1 = 17, STG0 = 18, STG1 = 19, FINAL = 20, N_BARS = 21 };
+// K and V tiles have their own full / empty barriers: a K slot is released
+// when the second head's S MMAs of its tile are done and a V slot when the
+// second head's PV MMAs are, so the K load of tile j + 2 starts about a
+// thousand cycles before the V load and has as long to land as the V load.
+enum Bar { K_FULL = 0, K_READY = 2, K_EMPTY = 4, S_FULL = 6, P_READY = 8, O_DONE = 10, O_FREE = 12, Q_READY = 14,
+           Q_EMPTY = 15, SFREE0 = 16, SFREE1 = 17, STG0 = 18, STG1 = 19, FINAL = 20, V_FULL = 21, V_EMPTY = 23,
+           N_BARS = 25 };
+// Key flags (1 = the key may be attended) of the last four K tiles, slot
+// g % 4 for tile g: the rotation warps fill tile g + 2's while the softmax
+// may still read tile g's and g + 1's.
+constexpr int kInfoSlots = 4;
+static_assert(kInfoSlots * BN <= 2 * 4 * BN, "key flags fit the INFO area");
 constexpr uint32_t TMEM_SLOT = BARS + 8 * N_BARS;
 constexpr uint32_t ABORT = TMEM_SLOT + 4;
 constexpr uint32_t TOTAL = ABORT + 4;
@@ -460,7 +470,7 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
   uint8_t* sm = tile::align1024(smem_raw);
   const uint32_t sbase = ptx::smem_u32(sm);
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
-  uint32_t* s_info = reinterpret_cast<uint32_t*>(sm + INFO);
+  uint8_t* s_flag = sm + INFO;
   volatile int* s_abort = reinterpret_cast<volatile int*>(sm + ABORT);
   auto bar = [&](int i) { return sbase + BARS + 8u * (uint32_t)i; };
   const AiAttnLayout& L = a.layout;
@@ -550,12 +560,12 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
       float m_use = -CUDART_INF_F, l = 0.f;
       int done = 0;
       for (int j = 0; j < w.n; ++j) {
-        const int gj = g + j, slot = gj & 1, k0 = w.kv_lo + j * BN;
+        const int gj = g + j, k0 = w.kv_lo + j * BN;
         if (!wait(S_FULL + t, gj & 1)) break;
         ptx::tc_fence_after();
         const bool fast = !w.masked && (k0 + BN <= w.kv_hi) && (k0 + BN - 1 <= w.q0);
         const int lim = min(i - k0, w.kv_hi - 1 - k0);
-        const uint32_t* info = s_info + slot * BN;
+        const uint8_t* info = s_flag + (gj & (kInfoSlots - 1)) * BN;
         // The row's 128 scores, read from TMEM once (cols 32 q + x in sq[x]).
         uint32_t s0[32], s1[32], s2[32], s3[32];
         ptx::tmem_ld32(tmem + lane_base + c_s, s0);
@@ -574,10 +584,10 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
         } else if (w.masked) {
 #pragma unroll
           for (int x = 0; x < 32; ++x) {
-            if (!((info[x] & AI_KEY_ATTN) && x <= lim)) s0[x] = 0xff800000u;
-            if (!((info[x + 32] & AI_KEY_ATTN) && x + 32 <= lim)) s1[x] = 0xff800000u;
-            if (!((info[x + 64] & AI_KEY_ATTN) && x + 64 <= lim)) s2[x] = 0xff800000u;
-            if (!((info[x + 96] & AI_KEY_ATTN) && x + 96 <= lim)) s3[x] = 0xff800000u;
+            if (!(info[x] && x <= lim)) s0[x] = 0xff800000u;
+            if (!(info[x + 32] && x + 32 <= lim)) s1[x] = 0xff800000u;
+            if (!(info[x + 64] && x + 64 <= lim)) s2[x] = 0xff800000u;
+            if (!(info[x + 96] && x + 96 <= lim)) s3[x] = 0xff800000u;
           }
         }
         float mxa = -CUDART_INF_F, mxb = -CUDART_INF_F, mxc = -CUDART_INF_F, mxd = -CUDART_INF_F;
@@ -725,33 +735,46 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
         ptx::prefetch_tmap(&tm_qr);
         ptx::prefetch_tmap(&tm_kr);
       }
+      // Loads in the order their slots are released: K(g), V(g), ... with a
+      // unit's Q after its first K and V tiles (Q is released by the previous
+      // unit's last S MMAs, after that unit's second-to-last K and V).
       int g = 0, k = 0;
       bool ok = true;
       for (int u = snake_unit(k); ok && u < n_units; u = snake_unit(++k)) {
         const Unit w = load_unit(a, u, prerot);
         const int b = w.blk.row;
-        if (prerot) {
-          if (k > 0 && !wait(Q_EMPTY, (k - 1) & 1)) break;
-          const int h0 = 2 * w.hp;
-          ptx::mbar_arrive_expect_tx(bar(Q_READY), 2 * kTile);
-          ptx::tma_load_4d(sbase + Q0, &tm_qr, bar(Q_READY), 0, w.q0, h0, b);
-          ptx::tma_load_4d(sbase + Q0 + kHalf, &tm_qr, bar(Q_READY), 64, w.q0, h0, b);
-          ptx::tma_load_4d(sbase + Q1, &tm_qr, bar(Q_READY), 0, w.q0, h0 + 1, b);
-          ptx::tma_load_4d(sbase + Q1 + kHalf, &tm_qr, bar(Q_READY), 64, w.q0, h0 + 1, b);
-        }
         const CUtensorMap* mk = w.k_pre ? &tm_kr : &tm_k;
-        for (int j = 0; j < w.n; ++j, ++g) {
+        for (int j = 0; j <= w.n && ok; ++j) {
+          if (j == min(1, w.n) && prerot) {
+            if (k > 0 && !wait(Q_EMPTY, (k - 1) & 1)) {
+              ok = false;
+              break;
+            }
+            const int h0 = 2 * w.hp;
+            ptx::mbar_arrive_expect_tx(bar(Q_READY), 2 * kTile);
+            ptx::tma_load_4d(sbase + Q0, &tm_qr, bar(Q_READY), 0, w.q0, h0, b);
+            ptx::tma_load_4d(sbase + Q0 + kHalf, &tm_qr, bar(Q_READY), 64, w.q0, h0, b);
+            ptx::tma_load_4d(sbase + Q1, &tm_qr, bar(Q_READY), 0, w.q0, h0 + 1, b);
+            ptx::tma_load_4d(sbase + Q1 + kHalf, &tm_qr, bar(Q_READY), 64, w.q0, h0 + 1, b);
+          }
+          if (j == w.n) break;
           const int slot = g & 1, k0 = w.kv_lo + j * BN;
-          if (g >= 2 && !wait(KV_EMPTY + slot, ((g >> 1) - 1) & 1)) {
+          const uint32_t kb = sbase + KB + (uint32_t)slot * kTile, vb = sbase + VB + (uint32_t)slot * kTile;
+          if (g >= 2 && !wait(K_EMPTY + slot, ((g >> 1) - 1) & 1)) {
             ok = false;
             break;
           }
-          const uint32_t kb = sbase + KB + (uint32_t)slot * kTile, vb = sbase + VB + (uint32_t)slot * kTile;
-          ptx::mbar_arrive_expect_tx(bar(KV_FULL + slot), 2 * kTile);
-          ptx::tma_load_4d(kb, mk, bar(KV_FULL + slot), 0, k0, w.hk, b);
-          ptx::tma_load_4d(kb + kHalf, mk, bar(KV_FULL + slot), 64, k0, w.hk, b);
-          ptx::tma_load_4d(vb, &tm_v, bar(KV_FULL + slot), 0, k0, w.hk, b);
-          ptx::tma_load_4d(vb + kHalf, &tm_v, bar(KV_FULL + slot), 64, k0, w.hk, b);
+          ptx::mbar_arrive_expect_tx(bar(K_FULL + slot), kTile);
+          ptx::tma_load_4d(kb, mk, bar(K_FULL + slot), 0, k0, w.hk, b);
+          ptx::tma_load_4d(kb + kHalf, mk, bar(K_FULL + slot), 64, k0, w.hk, b);
+          if (g >= 2 && !wait(V_EMPTY + slot, ((g >> 1) - 1) & 1)) {
+            ok = false;
+            break;
+          }
+          ptx::mbar_arrive_expect_tx(bar(V_FULL + slot), kTile);
+          ptx::tma_load_4d(vb, &tm_v, bar(V_FULL + slot), 0, k0, w.hk, b);
+          ptx::tma_load_4d(vb + kHalf, &tm_v, bar(V_FULL + slot), 64, k0, w.hk, b);
+          ++g;
         }
       }
     }
@@ -811,11 +834,13 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
       ptx::tc_fence_after();
       issue_s(0, g & 1);
       issue_s(1, g & 1);
+      ptx::mma_commit_w(bar(K_EMPTY + (g & 1)));
       if (w.n == 1) ptx::mma_commit_w(bar(Q_EMPTY));  // the unit's last reads of Q
       for (int j = 0; j < w.n; ++j) {
         const int gj = g + j, slot = gj & 1, nslot = (gj + 1) & 1;
         const bool more = j + 1 < w.n;
-        if (!wait_u(P_READY, gj & 1) || (j == 0 && k > 0 && !wait_u(O_FREE, (k - 1) & 1))) {
+        if (!wait_u(P_READY, gj & 1) || (j == 0 && k > 0 && !wait_u(O_FREE, (k - 1) & 1)) ||
+            !wait_u(V_FULL + slot, (gj >> 1) & 1)) {
           ok = false;
           break;
         }
@@ -835,9 +860,10 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
         }
         ptx::tc_fence_after();
         issue_pv(1, slot, j == 0, !more);
-        ptx::mma_commit_w(bar(KV_EMPTY + slot));
+        ptx::mma_commit_w(bar(V_EMPTY + slot));
         if (more) {
           issue_s(1, nslot);
+          ptx::mma_commit_w(bar(K_EMPTY + nslot));
           if (j + 2 == w.n) ptx::mma_commit_w(bar(Q_EMPTY));
         }
       }
@@ -858,7 +884,7 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
       const Unit w = load_unit(a, u, prerot);
       for (int j = 0; j < w.n; ++j, ++g) {
         const int slot = g & 1;
-        if (!wait(KV_FULL + slot, (g >> 1) & 1)) break;
+        if (!wait(K_FULL + slot, (g >> 1) & 1)) break;
         const uint32_t kt = KB + (uint32_t)slot * kTile;
 #pragma unroll
         for (int hr = 0; hr < 2; ++hr) {
@@ -886,7 +912,7 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
               }
             }
           }
-          s_info[slot * BN + row] = info;
+          s_flag[(g & (kInfoSlots - 1)) * BN + row] = (info & AI_KEY_ATTN) ? 1 : 0;
         }
         ptx::fence_proxy_async_smem();
         ptx::mbar_arrive(bar(K_READY + slot));
