@@ -520,8 +520,13 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
     const float2 sl2x2 = make_float2(sl2, sl2);
     int g = 0, k = 0, ko = 0;  // ko: units with key tiles so far (O_DONE phases)
     int nst = 0;               // this group's staging-buffer uses
+    // The next unit's description is read from global memory while this
+    // unit's last PV MMAs run (before the epilogue's O_DONE wait).
+    Unit w_next{};
+    if (snake_unit(0) < n_units) w_next = load_unit(a, snake_unit(0), prerot);
+    bool store_pending = false;  // thread 0: the last TMA store's smem read not yet waited for
     for (int u = snake_unit(k); u < n_units && !*s_abort; u = snake_unit(++k)) {
-      const Unit w = load_unit(a, u, prerot);
+      const Unit w = w_next;
       const int i = w.q0 + r, h = 2 * w.hp + t, b = w.blk.row;
       if (!prerot) {
         // Q rows of this unit (rotated): the previous unit's S MMAs must be
@@ -650,6 +655,7 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
         done = j + 1;
       }
       if (done != w.n) break;
+      if (snake_unit(k + 1) < n_units) w_next = load_unit(a, snake_unit(k + 1), prerot);
       // Epilogue: O_t / l.  O_t is read into registers, then released to the
       // next unit's first PV before the global stores.
       bool have_o = false;
@@ -686,7 +692,9 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
       // Output rows: a full unit goes through the group's staging buffer, one
       // 64-column half at a time (its threads hand their rows to thread 0
       // through STG_t; thread 0 frees the buffer through SFREE_t once the TMA
-      // store has read it); a unit whose item ends early is stored row by row
+      // store has read it, for the second half only at the group's next staged
+      // epilogue, so no thread waits for that read before the next unit's
+      // scores); a unit whose item ends early is stored row by row
       // (the TMA box would spill into the next block's rows).  A unit without
       // key tiles stores its zero rows directly: its thread 0 has not waited
       // for the group's other threads in O_DONE.
@@ -694,6 +702,13 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
       const uint32_t buf = OSTAGE + (uint32_t)t * kHalf;
       bool ok_st = true;
       if (full) {
+        if (r == 0 && store_pending) {
+          // The previous unit's second half: its store has long read the
+          // buffer by now.
+          ptx::bulk_wait_read_all();
+          ptx::mbar_arrive(bar(SFREE0 + t));
+          store_pending = false;
+        }
 #pragma unroll
         for (int hf = 0; hf < 2; ++hf) {
           if (nst > 0 && !wait(SFREE0 + t, (uint32_t)(nst - 1) & 1u)) {
@@ -711,8 +726,12 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
             }
             ptx::tma_store_4d(&tm_o, sbase + buf, 64 * hf, w.q0, h, b);
             ptx::bulk_commit_group();
-            ptx::bulk_wait_read_all();
-            ptx::mbar_arrive(bar(SFREE0 + t));
+            if (hf == 0) {
+              ptx::bulk_wait_read_all();
+              ptx::mbar_arrive(bar(SFREE0 + t));
+            } else {
+              store_pending = true;  // released at the group's next staged epilogue
+            }
           }
           ++nst;
         }
