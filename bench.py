@@ -40,7 +40,7 @@ METRIC = "multi-seg RoPE attn fwd+bwd TFLOP/s (causal-adjusted, 14*D*pairs*Hq)"
 DOM_KERNEL_NAMES = {"fwd": "fwd_pers_kernel (forward)", "dq": "dq_pers_kernel (dQ)", "dkdv": "dkdv_ws_kernel (dK/dV)"}
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch on this
 # workload, from one ncu capture of the three kernels (profiles/).
-TRAFFIC_BYTES = {"fwd": 362506752, "dq": 537964544, "dkdv": 400634112}
+TRAFFIC_BYTES = {"fwd": 368016640, "dq": 549332224, "dkdv": 401622016}
 
 
 def make_rows(seed: int):
