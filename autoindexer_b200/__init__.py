@@ -17,6 +17,7 @@ from .attention import (
 )
 from .meta import CompiledLayout, RowLayouts, compile_layout
 from .positions import BlockType, PositionBlock, PositionBlockList, cursor_stream, document_blocks
+from .prefill import plain_causal_attn_b200, prefill_attention_interface, prefill_layout
 from .rope import SectionedRope, default_inv_freq
 
 __all__ = [
@@ -35,6 +36,9 @@ __all__ = [
     "PositionBlockList",
     "cursor_stream",
     "document_blocks",
+    "plain_causal_attn_b200",
+    "prefill_attention_interface",
+    "prefill_layout",
     "SectionedRope",
     "default_inv_freq",
 ]

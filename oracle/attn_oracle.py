@@ -15,6 +15,7 @@ autoindexer, package ``src/autoindexer/models/autoindexer``):
 * ``attention/reference.py:116-141``    ``chain_of_edits_attn_ref``   (softmax, P.V)
 * ``attention/__init__.py:36-37``       GQA expansion (``repeat_kv``) in the wrapper
 * ``perturb_labels.py:333-339``         query positions zero-padded to ``T``
+* ``attention/prefill_sdpa.py:11-71``   ``plain_causal_attn_sdpa`` (prefill)
 
 The reference obtains gradients through autograd; ``attn_backward`` writes the
 same gradients out by hand (softmax backward, then the per-block split of the
@@ -304,3 +305,39 @@ def attn_backward(q, k, v, dout, layout, rope, scale=None, dtype=np.float64):
         dk[b] = dkb.reshape(Hkv, G, T, D).sum(axis=1)
         dv[b] = dvb.reshape(Hkv, G, T, D).sum(axis=1)
     return dq, dk, dv
+
+
+# ---------------------------------------------------------------------------
+# Prefill (plain causal attention of left-padded prompts)
+# ---------------------------------------------------------------------------
+
+def plain_causal_forward(q, k, v, keep, rope, scale=None, dtype=np.float64):
+    """Restates ``plain_causal_attn_sdpa`` (``attention/prefill_sdpa.py:11-71``)
+    after the registry wrapper's GQA expansion (``attention/__init__.py:36-37``):
+    ``q`` and ``k`` rotated by ``rope(arange(T))`` (one position table for
+    every row, ``prefill_sdpa.py:55-58``), then softmax attention under
+    ``tril(T, T) & keep[b]`` (``prefill_sdpa.py:60-68``; ``keep`` ``(B, T)``
+    bool or ``None`` for plain causal).  A query row that attends no key has
+    no defined result in the reference (SDPA); here it is zero, with lse
+    ``-inf``.  Returns ``(out (B, T, Hq, D), lse (B, Hq, T))``."""
+    q, k, v = (_np(t).astype(dtype) for t in (q, k, v))
+    B, Hq, T, D = q.shape
+    G = Hq // k.shape[1]
+    if scale is None:
+        scale = D ** -0.5
+    cos, sin = rope(np.arange(T))
+    qr = apply_cos_sin(q, cos, sin)
+    kr = apply_cos_sin(_expand(k, G), cos, sin)
+    ve = _expand(v, G)
+    causal = np.tril(np.ones((T, T), dtype=bool))
+    out = np.zeros((B, T, Hq, D), dtype=dtype)
+    lse = np.full((B, Hq, T), -np.inf, dtype=dtype)
+    for b in range(B):
+        allowed = causal if keep is None else causal & np.asarray(keep[b], dtype=bool)[None, :]
+        rows = allowed.any(axis=1)
+        w = np.einsum("htd,hsd->hts", qr[b], kr[b]) * scale
+        w = np.where(allowed[None], w, -np.inf)
+        p, l = _softmax(w[:, rows])
+        out[b][rows] = np.swapaxes(p @ ve[b], 0, 1)
+        lse[b][:, rows] = l
+    return out, lse
