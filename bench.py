@@ -417,6 +417,88 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+PREFILL_B = 8
+PREFILL_WORKLOAD = ("prefill: bf16 B=8 T=4096 Hq=32 Hkv=8 D=128 theta=1e6, left padding U[0, T/2) per row "
+                    "(seed 0), RoPE positions arange(T)")
+
+
+def run_prefill(args):
+    """Prefill attention (``plain_causal_attn_b200``) against the reference's
+    own prefill path on the same GPU: RoPE by ``apply_cos_sin``, K/V expanded
+    for GQA (``repeat_kv``), ``scaled_dot_product_attention`` under the causal
+    & key-padding mask (``prefill_sdpa.py:55-70``, ``attention/__init__.py:
+    36-37``).  Forward only (prefill is inference), L2 flushed between steps;
+    one JSON line, not the headline metric."""
+    import torch
+    import torch.nn.functional as F
+
+    import autoindexer_b200 as ab
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    Bp = PREFILL_B
+    rng = np.random.default_rng(0)
+    pads = rng.integers(0, T // 2, size=Bp)
+    keep = np.arange(T)[None, :] >= pads[:, None]
+    mask = torch.as_tensor(keep)[:, None, None, :].to(dev)
+    g = torch.Generator().manual_seed(0)
+    q, k, v = (torch.randn(Bp, h, T, D, generator=g).to(torch.bfloat16).to(dev) for h in (HQ, HKV, HKV))
+    rope = ab.SectionedRope(D, THETA, [torch.arange(T)], [(0, D // 2)], device=dev)
+    # valid (query, key) pairs: row b, query i >= pad_b sees keys [pad_b, i]
+    pairs_all = int(sum(((T - p) * (T - p + 1)) // 2 for p in pads))
+    flops = 4.0 * D * HQ * pairs_all
+    flush = torch.empty(64 * 1024 * 1024, device=dev)
+
+    def ours():
+        return ab.plain_causal_attn_b200(rope, q, k, v, attention_mask=mask)[0]
+
+    pos = torch.arange(T, device=dev).unsqueeze(0)
+    causal = torch.tril(torch.ones((T, T), dtype=torch.bool, device=dev))
+
+    def reference():
+        cos, sin = rope(q, pos)
+        cos, sin = cos.unsqueeze(1), sin.unsqueeze(1)
+
+        def rot(x):
+            h = x.shape[-1] // 2
+            return x * cos + torch.cat((-x[..., h:], x[..., :h]), dim=-1) * sin
+
+        ke = k.repeat_interleave(HQ // HKV, dim=1)
+        ve = v.repeat_interleave(HQ // HKV, dim=1)
+        o = F.scaled_dot_product_attention(rot(q), rot(ke), ve, attn_mask=causal & mask, is_causal=False)
+        return o.transpose(1, 2).contiguous()
+
+    def timed(fn):
+        for _ in range(max(3, args.warmup)):
+            fn()
+        torch.cuda.synchronize(dev)
+        tot = 0.0
+        for i in range(args.steps):
+            flush.fill_(float(i))
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize(dev)
+            tot += e0.elapsed_time(e1) / 1e3
+        return tot / args.steps
+
+    t_ours = timed(ours)
+    t_ref = timed(reference)
+    a, b = ours(), reference()
+    valid = torch.as_tensor(keep).to(dev)[:, :, None, None]  # rows that attend a key
+    diff = float(((a.float() - b.float()).abs() * valid).max())
+    print(json.dumps({
+        "metric": "prefill attention fwd TFLOP/s (4*D*valid pairs*Hq)", "value": round(flops / t_ours / 1e12, 3),
+        "unit": "TFLOP/s", "ms_per_step": round(t_ours * 1e3, 4), "steps": args.steps, "warmup": args.warmup,
+        "higher_is_better": True, "dtype": "bf16", "data": "synthetic (seeded randn q/k/v, seeded pads)",
+        "config": {"workload": PREFILL_WORKLOAD, "l2": "flushed between timed steps"},
+        "reference_sdpa": {"value": round(flops / t_ref / 1e12, 3), "ms_per_step": round(t_ref * 1e3, 4),
+                           "what": "rotate + repeat_kv + torch scaled_dot_product_attention, same GPU"},
+        "max_abs_diff_valid_rows": round(diff, 5),
+    }), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -424,8 +506,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--prefill", action="store_true", help="time the prefill path instead (one extra JSON line)")
     args = ap.parse_args()
-    if args.impl == "reference":
+    if args.prefill:
+        run_prefill(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)
