@@ -17,6 +17,7 @@ from .attention import (
 )
 from .meta import CompiledLayout, RowLayouts, compile_layout
 from .positions import BlockType, PositionBlock, PositionBlockList, cursor_stream, document_blocks
+from .decode import decode_attention
 from .prefill import plain_causal_attn_b200, prefill_attention_interface, prefill_layout
 from .rope import SectionedRope, default_inv_freq
 
@@ -36,6 +37,7 @@ __all__ = [
     "PositionBlockList",
     "cursor_stream",
     "document_blocks",
+    "decode_attention",
     "plain_causal_attn_b200",
     "prefill_attention_interface",
     "prefill_layout",

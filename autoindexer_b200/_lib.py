@@ -18,6 +18,7 @@ __all__ = [
     "AiAttnLayout",
     "AiAttnFwdArgs",
     "AiAttnBwdArgs",
+    "AiAttnDecodeArgs",
     "DTYPE_BF16",
     "DTYPE_F16",
     "DTYPE_F32",
@@ -30,8 +31,8 @@ LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_ai_attn.so
 
 DTYPE_BF16, DTYPE_F16, DTYPE_F32 = 0, 1, 2
 # AiProfKind, in order.
-PROF_KINDS = ("prerot", "fwd", "fwd_fill", "delta", "dq", "dkdv", "bwd_fill", "simt")
-ABI_VERSION = 5
+PROF_KINDS = ("prerot", "fwd", "fwd_fill", "delta", "dq", "dkdv", "bwd_fill", "simt", "decode")
+ABI_VERSION = 6
 
 # Every function include/ai_attn.h declares.
 EXPORTED_SYMBOLS = (
@@ -43,6 +44,8 @@ EXPORTED_SYMBOLS = (
     "ai_attn_bwd_workspace",
     "ai_attn_bwd",
     "ai_attn_bwd_noalloc",
+    "ai_attn_decode_workspace",
+    "ai_attn_decode",
     "ai_attn_profile_enable",
     "ai_attn_profile_read",
     "ai_attn_read_status",
@@ -122,6 +125,31 @@ class AiAttnBwdArgs(ctypes.Structure):
     ]
 
 
+class AiAttnDecodeArgs(ctypes.Structure):
+    _fields_ = [
+        ("batch", ctypes.c_int32),
+        ("kv_len", ctypes.c_int32),
+        ("num_q_heads", ctypes.c_int32),
+        ("num_kv_heads", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
+        ("dtype", ctypes.c_int32),
+        ("scale", ctypes.c_float),
+        ("q", AiTensor4),
+        ("k", AiTensor4),
+        ("v", AiTensor4),
+        ("out", AiTensor4),
+        ("key_rows", ctypes.c_void_p),
+        ("key_rows_stride_b", ctypes.c_int64),
+        ("key_ok", ctypes.c_void_p),
+        ("key_ok_stride_b", ctypes.c_int64),
+        ("rope_cs16", ctypes.c_void_p),
+        ("n_pos", ctypes.c_int32),
+        ("status", ctypes.c_void_p),
+        ("workspace", ctypes.c_void_p),
+        ("workspace_bytes", ctypes.c_size_t),
+    ]
+
+
 _lock = threading.Lock()
 _lib = None
 
@@ -144,6 +172,10 @@ def _bind(handle):
     handle.ai_attn_bwd.argtypes = [P(AiAttnBwdArgs), ctypes.c_void_p]
     handle.ai_attn_bwd_noalloc.restype = ctypes.c_int
     handle.ai_attn_bwd_noalloc.argtypes = [P(AiAttnBwdArgs), ctypes.c_void_p]
+    handle.ai_attn_decode_workspace.restype = ctypes.c_int
+    handle.ai_attn_decode_workspace.argtypes = [P(AiAttnDecodeArgs), P(ctypes.c_size_t)]
+    handle.ai_attn_decode.restype = ctypes.c_int
+    handle.ai_attn_decode.argtypes = [P(AiAttnDecodeArgs), ctypes.c_void_p]
     handle.ai_attn_read_status.restype = ctypes.c_int
     handle.ai_attn_read_status.argtypes = [ctypes.c_void_p, ctypes.c_void_p, P(ctypes.c_int32)]
     handle.ai_attn_strerror.restype = ctypes.c_char_p

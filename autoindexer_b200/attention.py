@@ -260,8 +260,16 @@ def fused_chain_of_edits_attn_b200(
 
 def _iter_positions_attention(module, query, key, value, attention_mask, dropout, scaling, rotary_emb,
                               parsed_positions):
-    """Decode step (one query token): the reference's eager math
-    (``attn_layers.py:15-27`` then ``__init__.py:41-51``)."""
+    """Decode step (one query token).  On the kernel's domain (CUDA bf16,
+    head_dim 128, <= 8 query heads per KV head, boolean or 0/-inf mask) the
+    ``ai_attn_decode`` kernels (``autoindexer_b200.decode``), returning no
+    attention weights, as the SDPA and flash backends of transformers do;
+    otherwise the reference's eager math (``attn_layers.py:15-27`` then
+    ``__init__.py:41-51``), weights included."""
+    from .decode import decode_attention, decode_supported
+
+    if decode_supported(query, key, attention_mask):
+        return decode_attention(query, key, value, parsed_positions, rotary_emb, scaling, attention_mask), None
     groups = query.shape[1] // key.shape[1]
     if groups > 1:
         key = key.repeat_interleave(groups, dim=1)

@@ -1,0 +1,309 @@
+// Decode step (one query token per batch row) against an unrotated K/V cache:
+// the IterPositions branch of the reference's attention interface
+// (attention/__init__.py:36-51 with attn_layers.py:15-27
+// compute_attn_weights_iter).  Each key is rotated by its own position id as
+// it is read (the reference rotates the whole cache every token), one CTA
+// reads a key chunk of one KV head once for the whole query-head group (the
+// reference expands K/V per query head), and a second launch combines the
+// chunks' partial softmax results.
+//
+// HBM-bound: per key 2 x 256 B of K and V (bf16, D = 128) plus a 256 B rotary
+// row that stays in L2.  Split CTA (256 threads), per 256-key sub-tile:
+//   phase 1  thread t = key: rotated K row . q_g for each query head g
+//            (q in shared memory, broadcast reads), logits to shared memory;
+//   softmax  warp g = query head g: sub-tile max, running max / sum, the
+//            probabilities back to shared memory, the rescale factor of O;
+//   phase 2  warp w = keys 32 w .. 32 w + 31, lane = dims 4 l .. 4 l + 3 (V
+//            rows read coalesced): o_g += p_g,j v_j in registers.
+// At the end the eight warps' O partials are summed through shared memory and
+// (m, l, o[128]) per query head go to the workspace; the combine kernel
+// merges the chunks and writes bf16 out.
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <math_constants.h>
+
+#include "../../include/ai_attn.h"
+#include "ai_common.cuh"
+#include "ai_kernels.h"
+
+namespace ai {
+namespace dec {
+
+constexpr int D = 128;
+constexpr int kThreads = 256;  // one key per thread in phase 1
+constexpr int kSub = kThreads;  // keys per sub-tile
+constexpr int kMaxG = 8;       // query heads per KV head
+constexpr float kLog2e = 1.4426950408889634f;
+
+struct Smem {
+  float q[kMaxG][D];           // the group's queries, fp32
+  float p[kMaxG][kSub];        // logits, then probabilities, of the sub-tile
+  float alpha[kMaxG];          // O rescale factor of the sub-tile
+  float o[kThreads / 32][D];   // per-warp O partial of one head at the end
+};
+
+__device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 t = __bfloat1622float2(h[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+
+__global__ void __launch_bounds__(kThreads)
+    decode_split_kernel(const AiAttnDecodeArgs a, float* __restrict__ part, int n_split, int chunk) {
+  __shared__ Smem sm;
+  const int split = blockIdx.x, bh = blockIdx.y;
+  const int b = bh / a.num_kv_heads, hk = bh % a.num_kv_heads;
+  const int G = a.num_q_heads / a.num_kv_heads;
+  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+  const int c0 = split * chunk, c1 = min(a.kv_len, c0 + chunk);
+
+  for (int i = tid; i < G * D; i += kThreads) {
+    const int g = i / D, d = i % D;
+    const __nv_bfloat16* qr = static_cast<const __nv_bfloat16*>(a.q.ptr) + b * a.q.stride_b +
+                              (int64_t)(hk * G + g) * a.q.stride_h;
+    sm.q[g][d] = __bfloat162float(qr[d]);
+  }
+  const __nv_bfloat16* kbase = static_cast<const __nv_bfloat16*>(a.k.ptr) + b * a.k.stride_b + hk * a.k.stride_h;
+  const __nv_bfloat16* vbase = static_cast<const __nv_bfloat16*>(a.v.ptr) + b * a.v.stride_b + hk * a.v.stride_h;
+  const int32_t* krow = a.key_rows + b * a.key_rows_stride_b;
+  const uint8_t* kok = a.key_ok ? a.key_ok + b * a.key_ok_stride_b : nullptr;
+  const uint4* cs = static_cast<const uint4*>(a.rope_cs16);  // 16 uint4 per table row
+  const float sl2 = a.scale * kLog2e;
+
+  float m_run = -CUDART_INF_F, l_run = 0.f;  // warp g < G: head g's running max (log2 units) and sum
+  float o[kMaxG][4];
+#pragma unroll
+  for (int g = 0; g < kMaxG; ++g) o[g][0] = o[g][1] = o[g][2] = o[g][3] = 0.f;
+  __syncthreads();
+
+  for (int s0 = c0; s0 < c1; s0 += kSub) {
+    // ---- phase 1: logits of key s0 + tid for every head of the group
+    {
+      const int j = s0 + tid;
+      float acc[kMaxG];
+#pragma unroll
+      for (int g = 0; g < kMaxG; ++g) acc[g] = 0.f;
+      bool ok = j < c1 && (kok == nullptr || kok[j] != 0);
+      if (ok) {
+        int r = krow[j];
+        if (r < 0 || r >= a.n_pos) {
+          report(a.status, AI_ERR_DEV_BOUNDS);
+          r = 0;
+        }
+        const uint4* kr = reinterpret_cast<const uint4*>(kbase + (int64_t)j * a.k.stride_t);
+        const uint4* tr = cs + (int64_t)r * (D / 8);
+#pragma unroll 2
+        for (int c = 0; c < 8; ++c) {
+          // dims 8c .. 8c+7 and their rotate-half partners 64 + 8c .. 64 + 8c + 7
+          float x1[8], x2[8];
+          unpack8(__ldg(kr + c), x1);
+          unpack8(__ldg(kr + 8 + c), x2);
+          const uint4 t0 = __ldg(tr + 2 * c), t1 = __ldg(tr + 2 * c + 1);
+          const __half2* h = reinterpret_cast<const __half2*>(&t0);
+          const __half2* h1 = reinterpret_cast<const __half2*>(&t1);
+          float y1[8], y2[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float2 csn = __half22float2(i < 4 ? h[i] : h1[i - 4]);
+            y1[i] = x1[i] * csn.x - x2[i] * csn.y;
+            y2[i] = x2[i] * csn.x + x1[i] * csn.y;
+          }
+#pragma unroll
+          for (int g = 0; g < kMaxG; ++g) {
+            if (g < G) {
+#pragma unroll
+              for (int i = 0; i < 8; ++i) acc[g] = fmaf(y1[i], sm.q[g][8 * c + i], fmaf(y2[i], sm.q[g][64 + 8 * c + i], acc[g]));
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int g = 0; g < kMaxG; ++g)
+        if (g < G) sm.p[g][tid] = ok ? acc[g] * sl2 : -CUDART_INF_F;
+    }
+    __syncthreads();
+    // ---- softmax bookkeeping: warp g handles head g
+    if (warp < G) {
+      float v[kSub / 32];
+      float mx = -CUDART_INF_F;
+#pragma unroll
+      for (int i = 0; i < kSub / 32; ++i) {
+        v[i] = sm.p[warp][lane + 32 * i];
+        mx = fmaxf(mx, v[i]);
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      const float m_new = fmaxf(m_run, mx);
+      const float msub = m_new == -CUDART_INF_F ? 0.f : m_new;
+      float sum = 0.f;
+#pragma unroll
+      for (int i = 0; i < kSub / 32; ++i) {
+        const float pv = exp2f(v[i] - msub);
+        sm.p[warp][lane + 32 * i] = pv;
+        sum += pv;
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+      const float alpha = exp2f(m_run - msub);  // 0 while m_run is -inf
+      l_run = l_run * alpha + sum;
+      m_run = m_new;
+      if (lane == 0) sm.alpha[warp] = alpha;
+    }
+    __syncthreads();
+    // ---- phase 2: o_g += p_g,j v_j over this warp's 32 keys
+    {
+#pragma unroll
+      for (int g = 0; g < kMaxG; ++g) {
+        if (g < G) {
+          const float al = sm.alpha[g];
+          o[g][0] *= al;
+          o[g][1] *= al;
+          o[g][2] *= al;
+          o[g][3] *= al;
+        }
+      }
+      const int jb = 32 * warp;
+#pragma unroll 4
+      for (int jj = 0; jj < 32; ++jj) {
+        const int j = s0 + jb + jj;
+        if (j >= c1) break;
+        const uint2 raw = __ldg(reinterpret_cast<const uint2*>(vbase + (int64_t)j * a.v.stride_t) + lane);
+        const float2 v01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
+        const float2 v23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
+#pragma unroll
+        for (int g = 0; g < kMaxG; ++g) {
+          if (g < G) {
+            const float pv = sm.p[g][jb + jj];
+            o[g][0] = fmaf(pv, v01.x, o[g][0]);
+            o[g][1] = fmaf(pv, v01.y, o[g][1]);
+            o[g][2] = fmaf(pv, v23.x, o[g][2]);
+            o[g][3] = fmaf(pv, v23.y, o[g][3]);
+          }
+        }
+      }
+    }
+    __syncthreads();
+  }
+
+  // ---- partials: per head, (m, l, o[128]) with o summed over the warps
+  float* base = part + ((int64_t)(b * a.num_q_heads + hk * G) * n_split + split) * (2 + D);
+#pragma unroll
+  for (int g = 0; g < kMaxG; ++g) {
+    if (g >= G) break;  // (G is uniform: every thread leaves together)
+    sm.o[warp][4 * lane] = o[g][0];
+    sm.o[warp][4 * lane + 1] = o[g][1];
+    sm.o[warp][4 * lane + 2] = o[g][2];
+    sm.o[warp][4 * lane + 3] = o[g][3];
+    __syncthreads();
+    float* dst = base + (int64_t)g * n_split * (2 + D);
+    if (tid < D) {
+      float acc = 0.f;
+#pragma unroll
+      for (int w = 0; w < kThreads / 32; ++w) acc += sm.o[w][tid];
+      dst[2 + tid] = acc;
+    }
+    if (warp == g && lane == 0) {
+      dst[0] = m_run;
+      dst[1] = l_run;
+    }
+    __syncthreads();
+  }
+}
+
+// One CTA per (row, query head), thread = dim: merges the chunks' partials.
+__global__ void __launch_bounds__(D) decode_combine_kernel(const AiAttnDecodeArgs a, const float* __restrict__ part,
+                                                           int n_split) {
+  const int bh = blockIdx.x, b = bh / a.num_q_heads, h = bh % a.num_q_heads, d = threadIdx.x;
+  const float* p = part + (int64_t)bh * n_split * (2 + D);
+  float M = -CUDART_INF_F;
+  for (int s = 0; s < n_split; ++s) M = fmaxf(M, p[s * (2 + D)]);
+  float L = 0.f, acc = 0.f;
+  if (M != -CUDART_INF_F) {
+    for (int s = 0; s < n_split; ++s) {
+      const float w = exp2f(p[s * (2 + D)] - M);
+      L += w * p[s * (2 + D) + 1];
+      acc += w * p[s * (2 + D) + 2 + d];
+    }
+  }
+  __nv_bfloat16* o = static_cast<__nv_bfloat16*>(a.out.ptr) + b * a.out.stride_b + h * a.out.stride_h;
+  o[d] = __float2bfloat16(L > 0.f ? acc / L : 0.f);
+}
+
+}  // namespace dec
+
+// Splits: enough CTAs for two per SM, chunks of whole 256-key sub-tiles.
+static void decode_plan(const AiAttnDecodeArgs& a, int* n_split, int* chunk) {
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int pairs = a.batch * a.num_kv_heads;
+  const int subtiles = (a.kv_len + dec::kSub - 1) / dec::kSub;
+  int want = (2 * sms + pairs - 1) / pairs;
+  if (want > subtiles) want = subtiles;
+  if (want < 1) want = 1;
+  const int per = (subtiles + want - 1) / want;  // sub-tiles per chunk
+  *chunk = per * dec::kSub;
+  *n_split = (a.kv_len + *chunk - 1) / *chunk;
+  if (*n_split < 1) *n_split = 1;
+}
+
+int decode_check(const AiAttnDecodeArgs* a) {
+  if (!a) return AI_ERR_NULL;
+  if (a->batch <= 0 || a->kv_len <= 0 || a->num_q_heads <= 0 || a->num_kv_heads <= 0 ||
+      a->num_q_heads % a->num_kv_heads != 0 || a->num_q_heads / a->num_kv_heads > dec::kMaxG)
+    return AI_ERR_SHAPE;
+  if (a->head_dim != dec::D) return AI_ERR_HEAD_DIM;
+  if (a->dtype != AI_DTYPE_BF16) return AI_ERR_DTYPE;
+  if (!a->q.ptr || !a->k.ptr || !a->v.ptr || !a->out.ptr || !a->key_rows || !a->rope_cs16) return AI_ERR_NULL;
+  if (a->n_pos <= 0) return AI_ERR_SHAPE;
+  // 16-byte K rows (uint4 loads), 8-byte V slices, 16-byte rotary rows
+  if ((reinterpret_cast<uintptr_t>(a->k.ptr) & 15) || (a->k.stride_t & 7) || (a->k.stride_h & 7) ||
+      (a->k.stride_b & 7))
+    return AI_ERR_ALIGN;
+  if ((reinterpret_cast<uintptr_t>(a->v.ptr) & 7) || (a->v.stride_t & 3) || (a->v.stride_h & 3) ||
+      (a->v.stride_b & 3))
+    return AI_ERR_ALIGN;
+  if (reinterpret_cast<uintptr_t>(a->rope_cs16) & 15) return AI_ERR_ALIGN;
+  if (a->key_rows_stride_b < 0 || a->key_ok_stride_b < 0) return AI_ERR_STRIDE;
+  return AI_OK;
+}
+
+size_t decode_workspace_bytes(const AiAttnDecodeArgs& a) {
+  int n_split = 1, chunk = dec::kSub;
+  decode_plan(a, &n_split, &chunk);
+  const size_t b = (size_t)a.batch * a.num_q_heads * n_split * (2 + dec::D) * sizeof(float);
+  return (b + 255) / 256 * 256;
+}
+
+int decode_launch(const AiAttnDecodeArgs& a, cudaStream_t st) {
+  int n_split = 1, chunk = dec::kSub;
+  decode_plan(a, &n_split, &chunk);
+  if (!a.workspace || a.workspace_bytes < decode_workspace_bytes(a)) return AI_ERR_WORKSPACE;
+  float* part = static_cast<float*>(a.workspace);
+  ProfScope ps(AI_PROF_DECODE, st);
+  dec::decode_split_kernel<<<dim3(n_split, a.batch * a.num_kv_heads), dec::kThreads, 0, st>>>(a, part, n_split,
+                                                                                            chunk);
+  dec::decode_combine_kernel<<<a.batch * a.num_q_heads, dec::D, 0, st>>>(a, part, n_split);
+  return cudaGetLastError() == cudaSuccess ? AI_OK : AI_ERR_LAUNCH;
+}
+
+}  // namespace ai
+
+extern "C" int ai_attn_decode_workspace(const AiAttnDecodeArgs* args, size_t* bytes) {
+  const int rc = ai::decode_check(args);
+  if (rc != AI_OK) return rc;
+  if (!bytes) return AI_ERR_NULL;
+  *bytes = ai::decode_workspace_bytes(*args);
+  return AI_OK;
+}
+
+extern "C" int ai_attn_decode(const AiAttnDecodeArgs* args, void* stream) {
+  const int rc = ai::decode_check(args);
+  if (rc != AI_OK) return rc;
+  return ai::decode_launch(*args, static_cast<cudaStream_t>(stream));
+}

@@ -499,6 +499,101 @@ def run_prefill(args):
     }), flush=True)
 
 
+DECODE_WORKLOAD = ("decode: bf16 B=8 Hq=32 Hkv=8 D=128 theta=1e6, one query token against an unrotated "
+                   "cache of L=32768 keys, relative key positions, every key attended")
+
+
+def run_decode(args):
+    """One decode step (``decode_attention``) against the reference's eager
+    decode branch on the same GPU (``repeat_kv``, the whole cache rotated,
+    ``q . k_rot``, mask, scale, fp32 softmax, ``P . V``:
+    ``attention/__init__.py:36-51``, ``attn_layers.py:15-27``).  HBM-bound:
+    the metric is the cache bytes one step must read (K and V once) over its
+    time, against the measured copy bandwidth.  One JSON line, not the
+    headline metric."""
+    import torch
+
+    import autoindexer_b200 as ab
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    Bd, L = 8, 32768
+    g = torch.Generator().manual_seed(0)
+    q = torch.randn(Bd, HQ, 1, D, generator=g).to(torch.bfloat16).to(dev)
+    k, v = (torch.randn(Bd, HKV, L, D, generator=g).to(torch.bfloat16).to(dev) for _ in range(2))
+    rope = ab.SectionedRope(D, THETA, [torch.arange(L)], [(0, D // 2)], device=dev)
+
+    class Pos:  # the IterPositions fields attention reads (type_utils.py:48-67)
+        key_pos_ids = torch.arange(L, device=dev) - (L - 1)
+        attn_mask = torch.ones(L, dtype=torch.bool, device=dev)
+
+        def get_rotary_pos_emb(self, rotary_emb, x):
+            return rotary_emb(x, (self.key_pos_ids + (L - 1)).unsqueeze(0))
+
+    pp = Pos()
+    flush = torch.empty(64 * 1024 * 1024, device=dev)
+
+    def ours():
+        return ab.decode_attention(q, k, v, pp, rope)
+
+    def reference():
+        G = HQ // HKV
+        ke, ve = k.repeat_interleave(G, dim=1), v.repeat_interleave(G, dim=1)
+        cos, sin = pp.get_rotary_pos_emb(rope, ke)
+        cos, sin = cos.unsqueeze(1), sin.unsqueeze(1)
+        h = D // 2
+        kr = ke * cos + torch.cat((-ke[..., h:], ke[..., :h]), dim=-1) * sin
+        w = q @ kr.transpose(-1, -2)
+        w.masked_fill_(~pp.attn_mask.view(-1, 1, 1, L), float("-inf"))
+        w = torch.softmax(w * D ** -0.5, dim=-1, dtype=torch.float32).to(q.dtype)
+        return w @ ve
+
+    def timed(fn):
+        for _ in range(max(3, args.warmup)):
+            fn()
+        torch.cuda.synchronize(dev)
+        tot = 0.0
+        for i in range(args.steps):
+            flush.fill_(float(i))
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize(dev)
+            tot += e0.elapsed_time(e1) / 1e3
+        return tot / args.steps
+
+    t_ours, t_ref = timed(ours), timed(reference)
+    from autoindexer_b200.attention import KernelTimes
+
+    with KernelTimes() as kt:  # the two decode launches alone, CUDA events on their stream
+        for i in range(args.steps):
+            flush.fill_(float(i))
+            ours()
+        torch.cuda.synchronize(dev)
+    t_kern = kt.ms["decode"] / max(1, kt.launches["decode"]) / 1e3
+    diff = float((ours().float() - reference().float()).abs().max())
+    nbytes = 2 * Bd * HKV * L * D * 2  # K and V read once
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            hbm = float(json.load(f).get("hbm_gbs"))
+    except (OSError, ValueError, TypeError):
+        hbm = 6650.0
+    gbs = nbytes / t_ours / 1e9
+    print(json.dumps({
+        "metric": "decode step cache read GB/s (K and V bytes / step time)", "value": round(gbs, 1), "unit": "GB/s",
+        "ms_per_step": round(t_ours * 1e3, 4), "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+        "dtype": "bf16", "data": "synthetic (seeded randn q/k/v)",
+        "config": {"workload": DECODE_WORKLOAD, "l2": "flushed between timed steps (cache 1.07 GB > L2)"},
+        "kernel_ms": round(t_kern * 1e3, 4),
+        "roofline": {"bound": "hbm", "achieved": round(nbytes / t_kern / 1e9, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(nbytes / t_kern / 1e9 / hbm, 4), "traffic": None},
+        "reference_eager": {"value": round(nbytes / t_ref / 1e9, 1), "ms_per_step": round(t_ref * 1e3, 4),
+                            "what": "repeat_kv + rotate the cache + matmul + fp32 softmax + matmul, same GPU"},
+        "max_abs_diff": round(diff, 5),
+    }), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -507,9 +602,12 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--prefill", action="store_true", help="time the prefill path instead (one extra JSON line)")
+    ap.add_argument("--decode", action="store_true", help="time one decode step instead (one extra JSON line)")
     args = ap.parse_args()
     if args.prefill:
         run_prefill(args)
+    elif args.decode:
+        run_decode(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

@@ -43,7 +43,7 @@
 extern "C" {
 #endif
 
-#define AI_ATTN_ABI_VERSION 5
+#define AI_ATTN_ABI_VERSION 6
 
 typedef enum AiDtype {
   AI_DTYPE_BF16 = 0,
@@ -193,6 +193,48 @@ int ai_attn_bwd(const AiAttnBwdArgs* args, void* stream);
 #define AI_ATTN_NOALLOC_MAX_ROWS (1 << 22)
 int ai_attn_bwd_noalloc(const AiAttnBwdArgs* args, void* stream);
 
+/* Decode step: one query token per batch row against an unrotated K/V cache.
+ *
+ *   ai_attn_decode <- attention/__init__.py:39-51, the IterPositions branch of the registered
+ *                     attention interface (keys expanded by repeat_kv, :36-37), with
+ *                     attn_layers.py:15-27 compute_attn_weights_iter: each key rotated by its own
+ *                     position id (IterPositions.key_pos_ids, type_utils.py:48-67), the query
+ *                     unrotated, attn_mask, scale, softmax, P.V.
+ *
+ * The reference rotates the whole cache and expands K/V for GQA every token;
+ * here every key is rotated as it is read, each KV head's cache is read once
+ * for its whole query-head group, and the keys are split over CTAs whose
+ * partial results a second launch combines.  bf16, head_dim 128, at most 8
+ * query heads per KV head.  A row whose keys are all masked returns zeros. */
+typedef struct AiAttnDecodeArgs {
+  int32_t batch;
+  int32_t kv_len;             /* L: keys in the cache */
+  int32_t num_q_heads;
+  int32_t num_kv_heads;       /* num_q_heads / num_kv_heads <= 8 */
+  int32_t head_dim;           /* 128 */
+  int32_t dtype;              /* AI_DTYPE_BF16 */
+  float scale;                /* softmax scale applied to the logits */
+  AiTensor4 q;                /* (B, Hq, 1, D) */
+  AiTensor4 k;                /* (B, Hkv, L, D) unrotated cache */
+  AiTensor4 v;                /* (B, Hkv, L, D) */
+  AiTensor4 out;              /* (B, Hq, 1, D) */
+  const int32_t* key_rows;    /* [B or 1][L]: rotary table row of each key's position id */
+  int64_t key_rows_stride_b;  /* elements between rows; 0: one position row shared by the batch */
+  const uint8_t* key_ok;      /* [B or 1][L]: 1 = the key is attended; NULL: every key */
+  int64_t key_ok_stride_b;    /* 0: one mask row shared by the batch */
+  const void* rope_cs16;      /* [n_pos][D/2] fp16 pairs (cos, sin), as AiAttnLayout.rope_cs16 */
+  int32_t n_pos;
+  int32_t* status;            /* optional device status word */
+  void* workspace;            /* device scratch, 256-B aligned, ai_attn_decode_workspace bytes */
+  size_t workspace_bytes;
+} AiAttnDecodeArgs;
+
+/* Scratch the decode step needs (the split-K partial results). */
+int ai_attn_decode_workspace(const AiAttnDecodeArgs* args, size_t* bytes);
+
+/* out = softmax(scale * q . R(pos_j) k_j masked) . v, per (row, query head). */
+int ai_attn_decode(const AiAttnDecodeArgs* args, void* stream);
+
 /* Synchronises the stream, copies the device status word to *host_out and
  * resets it to AI_OK.  For tests and debugging; not needed on the hot path. */
 int ai_attn_read_status(int32_t* dev_status, void* stream, int32_t* host_out);
@@ -218,7 +260,8 @@ typedef enum AiProfKind {
   AI_PROF_DKDV = 5,     /* tensor-core dK/dV kernels */
   AI_PROF_BWD_FILL = 6, /* backward rows no block owns */
   AI_PROF_SIMT = 7,     /* fp32 / fp16 / other head_dim path */
-  AI_PROF_KINDS = 8
+  AI_PROF_DECODE = 8,   /* decode step (split-K + combine) */
+  AI_PROF_KINDS = 9
 } AiProfKind;
 int ai_attn_profile_enable(int on);
 int ai_attn_profile_read(float* ms_by_kind, int32_t* launches_by_kind);

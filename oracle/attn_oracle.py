@@ -16,6 +16,7 @@ autoindexer, package ``src/autoindexer/models/autoindexer``):
 * ``attention/__init__.py:36-37``       GQA expansion (``repeat_kv``) in the wrapper
 * ``perturb_labels.py:333-339``         query positions zero-padded to ``T``
 * ``attention/prefill_sdpa.py:11-71``   ``plain_causal_attn_sdpa`` (prefill)
+* ``attention/__init__.py:36-51``, ``attn_layers.py:15-27``  decode step (``IterPositions``)
 
 The reference obtains gradients through autograd; ``attn_backward`` writes the
 same gradients out by hand (softmax backward, then the per-block split of the
@@ -341,3 +342,40 @@ def plain_causal_forward(q, k, v, keep, rope, scale=None, dtype=np.float64):
         out[b][rows] = np.swapaxes(p @ ve[b], 0, 1)
         lse[b][:, rows] = l
     return out, lse
+
+
+# ---------------------------------------------------------------------------
+# Decode step (IterPositions)
+# ---------------------------------------------------------------------------
+
+def decode_forward(q, k, v, key_pos, attn_mask, rope, scale=None, attention_mask=None, dtype=np.float64):
+    """Restates the IterPositions branch of the registered interface
+    (``attention/__init__.py:36-51``): K/V expanded for GQA (``repeat_kv``),
+    ``compute_attn_weights_iter`` (``attn_layers.py:15-27``: keys rotated by
+    ``rope(key_pos)``, the query unrotated, ``q . k_rot``, ``attn_mask``
+    positions set to -inf, times ``scale``), a boolean ``attention_mask``
+    applied as a fill and a float one added, softmax, ``P . V``.
+
+    ``q`` ``(B, Hq, 1, D)``; ``k``, ``v`` ``(B, Hkv, L, D)``; ``key_pos``
+    ``(L,)`` or ``(B, L)``; ``attn_mask`` the same shape (bool) or ``None``.
+    Returns ``(B, Hq, 1, D)``."""
+    q, k, v = (_np(t).astype(dtype) for t in (q, k, v))
+    B, Hq, _, D = q.shape
+    L = k.shape[2]
+    G = Hq // k.shape[1]
+    if scale is None:
+        scale = D ** -0.5
+    kp = np.asarray(_np(key_pos)).reshape(-1, L)
+    cos, sin = rope(kp.reshape(-1))
+    cos, sin = cos.reshape(kp.shape[0], 1, L, D), sin.reshape(kp.shape[0], 1, L, D)
+    kr = apply_cos_sin(_expand(k, G), cos, sin)
+    w = np.einsum("bhqd,bhkd->bhqk", q, kr)
+    if attn_mask is not None:
+        am = np.asarray(_np(attn_mask), dtype=bool).reshape(-1, 1, 1, L)
+        w = np.where(am, w, -np.inf)
+    w = w * scale
+    if attention_mask is not None:
+        m = _np(attention_mask)
+        w = np.where(m, w, -np.inf) if m.dtype == bool else w + m.astype(dtype)
+    p, _ = _softmax(w)
+    return p @ _expand(v, G)

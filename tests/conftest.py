@@ -25,7 +25,10 @@ def pytest_configure(config):
 
 
 def golden_names():
-    return sorted(f[:-4] for f in os.listdir(GOLDEN) if f.endswith(".npz") and not f.startswith("kat_"))
+    """The chain-of-edits golden cases (not the known-answer tables or the
+    decode-step vectors)."""
+    return sorted(f[:-4] for f in os.listdir(GOLDEN)
+                  if f.endswith(".npz") and not f.startswith(("kat_", "decode_")))
 
 
 def load_golden(name):
