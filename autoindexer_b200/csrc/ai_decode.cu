@@ -54,7 +54,7 @@ __device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
   }
 }
 
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, 3)
     decode_split_kernel(const AiAttnDecodeArgs a, float* __restrict__ part, int n_split, int chunk) {
   __shared__ Smem sm;
   const int split = blockIdx.x, bh = blockIdx.y;
@@ -89,9 +89,12 @@ __global__ void __launch_bounds__(kThreads)
       float acc[kMaxG];
 #pragma unroll
       for (int g = 0; g < kMaxG; ++g) acc[g] = 0.f;
-      bool ok = j < c1 && (kok == nullptr || kok[j] != 0);
+      // The key's table row and flag are requested together (neither waits
+      // for the other).
+      const bool inb = j < c1;
+      int r = inb ? __ldg(krow + j) : 0;
+      const bool ok = inb && (kok == nullptr || __ldg(kok + j) != 0);
       if (ok) {
-        int r = krow[j];
         if (r < 0 || r >= a.n_pos) {
           report(a.status, AI_ERR_DEV_BOUNDS);
           r = 0;
@@ -237,13 +240,14 @@ __global__ void __launch_bounds__(D) decode_combine_kernel(const AiAttnDecodeArg
 
 }  // namespace dec
 
-// Splits: enough CTAs for two per SM, chunks of whole 256-key sub-tiles.
+// Splits: enough CTAs for three per SM (the split kernel's register bound),
+// chunks of whole 256-key sub-tiles.
 static void decode_plan(const AiAttnDecodeArgs& a, int* n_split, int* chunk) {
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int pairs = a.batch * a.num_kv_heads;
   const int subtiles = (a.kv_len + dec::kSub - 1) / dec::kSub;
-  int want = (2 * sms + pairs - 1) / pairs;
+  int want = (3 * sms + pairs - 1) / pairs;
   if (want > subtiles) want = subtiles;
   if (want < 1) want = 1;
   const int per = (subtiles + want - 1) / want;  // sub-tiles per chunk
