@@ -54,7 +54,10 @@ __device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
   }
 }
 
-__global__ void __launch_bounds__(kThreads, 3)
+// kG: query heads per KV head rounded up to 1, 2, 4 or 8 (the register
+// arrays are sized by it; G, the actual count, guards the loops).
+template <int kG>
+__global__ void __launch_bounds__(kThreads, kG <= 4 ? 4 : 3)
     decode_split_kernel(const AiAttnDecodeArgs a, float* __restrict__ part, int n_split, int chunk) {
   __shared__ Smem sm;
   const int split = blockIdx.x, bh = blockIdx.y;
@@ -77,18 +80,18 @@ __global__ void __launch_bounds__(kThreads, 3)
   const float sl2 = a.scale * kLog2e;
 
   float m_run = -CUDART_INF_F, l_run = 0.f;  // warp g < G: head g's running max (log2 units) and sum
-  float o[kMaxG][4];
+  float o[kG][4];
 #pragma unroll
-  for (int g = 0; g < kMaxG; ++g) o[g][0] = o[g][1] = o[g][2] = o[g][3] = 0.f;
+  for (int g = 0; g < kG; ++g) o[g][0] = o[g][1] = o[g][2] = o[g][3] = 0.f;
   __syncthreads();
 
   for (int s0 = c0; s0 < c1; s0 += kSub) {
     // ---- phase 1: logits of key s0 + tid for every head of the group
     {
       const int j = s0 + tid;
-      float acc[kMaxG];
+      float acc[kG];
 #pragma unroll
-      for (int g = 0; g < kMaxG; ++g) acc[g] = 0.f;
+      for (int g = 0; g < kG; ++g) acc[g] = 0.f;
       // The key's table row and flag are requested together (neither waits
       // for the other).
       const bool inb = j < c1;
@@ -118,7 +121,7 @@ __global__ void __launch_bounds__(kThreads, 3)
             y2[i] = x2[i] * csn.x + x1[i] * csn.y;
           }
 #pragma unroll
-          for (int g = 0; g < kMaxG; ++g) {
+          for (int g = 0; g < kG; ++g) {
             if (g < G) {
 #pragma unroll
               for (int i = 0; i < 8; ++i) acc[g] = fmaf(y1[i], sm.q[g][8 * c + i], fmaf(y2[i], sm.q[g][64 + 8 * c + i], acc[g]));
@@ -127,7 +130,7 @@ __global__ void __launch_bounds__(kThreads, 3)
         }
       }
 #pragma unroll
-      for (int g = 0; g < kMaxG; ++g)
+      for (int g = 0; g < kG; ++g)
         if (g < G) sm.p[g][tid] = ok ? acc[g] * sl2 : -CUDART_INF_F;
     }
     __syncthreads();
@@ -162,7 +165,7 @@ __global__ void __launch_bounds__(kThreads, 3)
     // ---- phase 2: o_g += p_g,j v_j over this warp's 32 keys
     {
 #pragma unroll
-      for (int g = 0; g < kMaxG; ++g) {
+      for (int g = 0; g < kG; ++g) {
         if (g < G) {
           const float al = sm.alpha[g];
           o[g][0] *= al;
@@ -180,7 +183,7 @@ __global__ void __launch_bounds__(kThreads, 3)
         const float2 v01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
         const float2 v23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
 #pragma unroll
-        for (int g = 0; g < kMaxG; ++g) {
+        for (int g = 0; g < kG; ++g) {
           if (g < G) {
             const float pv = sm.p[g][jb + jj];
             o[g][0] = fmaf(pv, v01.x, o[g][0]);
@@ -197,7 +200,7 @@ __global__ void __launch_bounds__(kThreads, 3)
   // ---- partials: per head, (m, l, o[128]) with o summed over the warps
   float* base = part + ((int64_t)(b * a.num_q_heads + hk * G) * n_split + split) * (2 + D);
 #pragma unroll
-  for (int g = 0; g < kMaxG; ++g) {
+  for (int g = 0; g < kG; ++g) {
     if (g >= G) break;  // (G is uniform: every thread leaves together)
     sm.o[warp][4 * lane] = o[g][0];
     sm.o[warp][4 * lane + 1] = o[g][1];
@@ -240,14 +243,15 @@ __global__ void __launch_bounds__(D) decode_combine_kernel(const AiAttnDecodeArg
 
 }  // namespace dec
 
-// Splits: enough CTAs for three per SM (the split kernel's register bound),
+// Splits: enough CTAs to fill every SM at the split kernel's register bound,
 // chunks of whole 256-key sub-tiles.
 static void decode_plan(const AiAttnDecodeArgs& a, int* n_split, int* chunk) {
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int pairs = a.batch * a.num_kv_heads;
   const int subtiles = (a.kv_len + dec::kSub - 1) / dec::kSub;
-  int want = (3 * sms + pairs - 1) / pairs;
+  const int per_sm = a.num_q_heads / a.num_kv_heads <= 4 ? 4 : 3;  // the split kernel's CTAs per SM
+  int want = (per_sm * sms + pairs - 1) / pairs;
   if (want > subtiles) want = subtiles;
   if (want < 1) want = 1;
   const int per = (subtiles + want - 1) / want;  // sub-tiles per chunk
@@ -290,8 +294,16 @@ int decode_launch(const AiAttnDecodeArgs& a, cudaStream_t st) {
   if (!a.workspace || a.workspace_bytes < decode_workspace_bytes(a)) return AI_ERR_WORKSPACE;
   float* part = static_cast<float*>(a.workspace);
   ProfScope ps(AI_PROF_DECODE, st);
-  dec::decode_split_kernel<<<dim3(n_split, a.batch * a.num_kv_heads), dec::kThreads, 0, st>>>(a, part, n_split,
-                                                                                            chunk);
+  const dim3 grid(n_split, a.batch * a.num_kv_heads);
+  const int G = a.num_q_heads / a.num_kv_heads;
+  if (G <= 1)
+    dec::decode_split_kernel<1><<<grid, dec::kThreads, 0, st>>>(a, part, n_split, chunk);
+  else if (G <= 2)
+    dec::decode_split_kernel<2><<<grid, dec::kThreads, 0, st>>>(a, part, n_split, chunk);
+  else if (G <= 4)
+    dec::decode_split_kernel<4><<<grid, dec::kThreads, 0, st>>>(a, part, n_split, chunk);
+  else
+    dec::decode_split_kernel<8><<<grid, dec::kThreads, 0, st>>>(a, part, n_split, chunk);
   dec::decode_combine_kernel<<<a.batch * a.num_q_heads, dec::D, 0, st>>>(a, part, n_split);
   return cudaGetLastError() == cudaSuccess ? AI_OK : AI_ERR_LAUNCH;
 }
