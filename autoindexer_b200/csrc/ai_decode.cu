@@ -251,7 +251,7 @@ static void decode_plan(const AiAttnDecodeArgs& a, int* n_split, int* chunk) {
   const int pairs = a.batch * a.num_kv_heads;
   const int subtiles = (a.kv_len + dec::kSub - 1) / dec::kSub;
   const int per_sm = a.num_q_heads / a.num_kv_heads <= 4 ? 4 : 3;  // the split kernel's CTAs per SM
-  int want = (per_sm * sms + pairs - 1) / pairs;
+  int want = (per_sm * sms) / pairs;  // at most one wave: a partial second wave doubles the tail
   if (want > subtiles) want = subtiles;
   if (want < 1) want = 1;
   const int per = (subtiles + want - 1) / want;  // sub-tiles per chunk
