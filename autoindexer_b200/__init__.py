@@ -16,7 +16,8 @@ from .attention import (
     resolve_available_attn_implementation,
 )
 from .meta import CompiledLayout, RowLayouts, compile_layout
-from .positions import BlockType, PositionBlock, PositionBlockList, cursor_stream, document_blocks
+from .positions import (BlockType, PositionBlock, PositionBlockList, blocks_from_concat, cursor_stream,
+                        document_blocks)
 from .decode import decode_attention
 from .prefill import plain_causal_attn_b200, prefill_attention_interface, prefill_layout
 from .rope import SectionedRope, default_inv_freq
@@ -37,6 +38,7 @@ __all__ = [
     "PositionBlockList",
     "cursor_stream",
     "document_blocks",
+    "blocks_from_concat",
     "decode_attention",
     "plain_causal_attn_b200",
     "prefill_attention_interface",

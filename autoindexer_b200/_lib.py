@@ -49,6 +49,7 @@ EXPORTED_SYMBOLS = (
     "ai_attn_profile_enable",
     "ai_attn_profile_read",
     "ai_attn_read_status",
+    "ai_attn_selftest_wait",
     "ai_attn_strerror",
 )
 
@@ -184,6 +185,8 @@ def _bind(handle):
     handle.ai_attn_profile_enable.argtypes = [ctypes.c_int]
     handle.ai_attn_profile_read.restype = ctypes.c_int
     handle.ai_attn_profile_read.argtypes = [P(ctypes.c_float), P(ctypes.c_int32)]
+    handle.ai_attn_selftest_wait.restype = ctypes.c_int
+    handle.ai_attn_selftest_wait.argtypes = [ctypes.c_void_p, ctypes.c_longlong, ctypes.c_void_p]
     return handle
 
 

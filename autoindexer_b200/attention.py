@@ -95,18 +95,26 @@ def _fwd_args(q: Tensor, k: Tensor, v: Tensor, out_bhtd: Tensor, lse: Tensor, la
 
 
 def attn_fwd(q: Tensor, k: Tensor, v: Tensor, layout: CompiledLayout, scale: float,
-             rotated_copies: bool = True, keep_workspace: bool = False):
+             rotated_copies: bool = True, keep_workspace: bool = False, out_bhtd: Optional[Tensor] = None):
     """Launches ``ai_attn_fwd``: returns ``out (B, T, Hq, D)`` and ``lse (B, Hq, T)`` fp32.
 
     ``rotated_copies``: give the kernels scratch for once-rotated Q/K copies
     (faster; ``ai_attn_fwd_workspace`` bytes); without it every tile is
     rotated in shared memory.  ``keep_workspace``: also return that scratch
     (or ``None``) so that ``attn_bwd(..., fwd_workspace=...)`` reads the
-    rotated copies instead of rotating again."""
+    rotated copies instead of rotating again.  ``out_bhtd``: a ``(B, Hq, T,
+    D)`` view (d contiguous, any other strides) the kernels write the output
+    into; the returned ``out`` is then its ``(B, T, Hq, D)`` permutation."""
     B, Hq, T, D = q.shape
-    out = torch.empty((B, T, Hq, D), dtype=q.dtype, device=q.device)
+    if out_bhtd is None:
+        out = torch.empty((B, T, Hq, D), dtype=q.dtype, device=q.device)
+        out_bhtd = out.permute(0, 2, 1, 3)
+    else:
+        if tuple(out_bhtd.shape) != (B, Hq, T, D) or out_bhtd.stride(-1) != 1 or out_bhtd.dtype != q.dtype:
+            raise ValueError("out_bhtd must be a (B, Hq, T, D) view of q's dtype with d contiguous")
+        out = out_bhtd.permute(0, 2, 1, 3)
     lse = torch.empty((B, Hq, T), dtype=torch.float32, device=q.device)
-    a = _fwd_args(q, k, v, out.permute(0, 2, 1, 3), lse, layout, scale)
+    a = _fwd_args(q, k, v, out_bhtd, lse, layout, scale)
     lib = _lib.lib()
     nbytes = ctypes.c_size_t(0)
     _lib.check(lib.ai_attn_fwd_workspace(ctypes.byref(a), ctypes.byref(nbytes)), "ai_attn_fwd_workspace")
@@ -123,21 +131,29 @@ def attn_fwd(q: Tensor, k: Tensor, v: Tensor, layout: CompiledLayout, scale: flo
 
 
 def attn_bwd(q, k, v, out, lse, dout, layout: CompiledLayout, scale: float, rotated_copies: bool = True,
-             fwd_workspace: Optional[Tensor] = None):
+             fwd_workspace: Optional[Tensor] = None, grads: Optional[Tuple[Tensor, Tensor, Tensor]] = None):
     """Launches ``ai_attn_bwd``: returns ``dq, dk, dv`` shaped like ``q, k, v``
     (``rotated_copies`` as for ``attn_fwd``; without it the workspace holds
     only the row sums of dO.O).  ``fwd_workspace``: the scratch that
     ``attn_fwd(..., keep_workspace=True)`` returned for these q, k and layout;
-    its rotated Q/K copies are reused (``fwd_rotated`` in the C ABI)."""
-    dq = torch.empty_like(q)
-    dk = torch.empty_like(k)
-    dv = torch.empty_like(v)
-    if dq.stride(-1) != 1:
-        dq = torch.empty(q.shape, dtype=q.dtype, device=q.device)
-    if dk.stride(-1) != 1:
-        dk = torch.empty(k.shape, dtype=k.dtype, device=k.device)
-    if dv.stride(-1) != 1:
-        dv = torch.empty(v.shape, dtype=v.dtype, device=v.device)
+    its rotated Q/K copies are reused (``fwd_rotated`` in the C ABI).
+    ``grads``: ``(dq, dk, dv)`` views (shaped like q, k, v, d contiguous) the
+    kernels write into instead of new tensors."""
+    if grads is not None:
+        dq, dk, dv = grads
+        for g, x in ((dq, q), (dk, k), (dv, v)):
+            if g.shape != x.shape or g.stride(-1) != 1 or g.dtype != x.dtype:
+                raise ValueError("grads must be shaped like q, k, v with d contiguous")
+    else:
+        dq = torch.empty_like(q)
+        dk = torch.empty_like(k)
+        dv = torch.empty_like(v)
+        if dq.stride(-1) != 1:
+            dq = torch.empty(q.shape, dtype=q.dtype, device=q.device)
+        if dk.stride(-1) != 1:
+            dk = torch.empty(k.shape, dtype=k.dtype, device=k.device)
+        if dv.stride(-1) != 1:
+            dv = torch.empty(v.shape, dtype=v.dtype, device=v.device)
     a = _lib.AiAttnBwdArgs()
     a.fwd = _fwd_args(q, k, v, out.permute(0, 2, 1, 3), lse, layout, scale)
     dout_keep = _dense_d(dout)
@@ -208,20 +224,39 @@ class AttentionFn(torch.autograd.Function):
         return dq, dk, dv, None, None
 
 
+_MASK_CHECK_ELEMS = 1 << 26  # mask entries examined per chunk of rows
+
+
 def _check_mask_is_causal(attention_mask: Tensor, T: int) -> None:
     """The kernels apply the block masks plus the global causal mask.  An
     external mask is accepted only when it removes nothing inside the causal
-    triangle (HF injects a plain causal mask); anything else raises."""
+    triangle (HF injects a plain causal mask); anything else raises.
+
+    The check runs once per mask tensor and version (every layer of a
+    forward gets the same mask object), over chunks of rows so that no T x T
+    temporary is built, with a single device-to-host read at the end."""
     m = attention_mask
     if m.dim() != 4 or m.shape[-1] != T or m.shape[-2] != T:
         raise NotImplementedError(f"attention_mask of shape {tuple(m.shape)} is not supported")
-    tril = torch.ones((T, T), dtype=torch.bool, device=m.device).tril()
-    if m.dtype == torch.bool:
-        ok = bool(m[..., tril].all())
-    else:
-        ok = bool((m[..., tril] == 0).all())
-    if not ok:
+    stamp = (m._version, m.data_ptr(), tuple(m.shape), m.dtype)
+    if getattr(m, "_b200_causal_ok", None) == stamp:
+        return
+    lead = max(1, m.shape[0] * m.shape[1])
+    rows = max(1, _MASK_CHECK_ELEMS // (lead * T))
+    cols = torch.arange(T, device=m.device)
+    bad = torch.zeros((), dtype=torch.bool, device=m.device)
+    for r0 in range(0, T, rows):
+        r1 = min(T, r0 + rows)
+        lower = cols[None, :] <= torch.arange(r0, r1, device=m.device)[:, None]  # causal triangle of these rows
+        sub = m[..., r0:r1, :]
+        removed = ~sub if m.dtype == torch.bool else sub != 0
+        bad |= (removed & lower).any()
+    if bool(bad):
         raise NotImplementedError("attention_mask masks entries inside the causal triangle; not supported")
+    try:
+        m._b200_causal_ok = stamp
+    except (AttributeError, RuntimeError):
+        pass
 
 
 def fused_chain_of_edits_attn_b200(

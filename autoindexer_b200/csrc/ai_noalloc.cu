@@ -17,6 +17,15 @@
 // last call's contents; the kernels overwrite every entry they read, so
 // nothing needs clearing.  Calls that overlap on the GPU (different streams,
 // or different host threads on one device) race on the array.
+//
+// What the array holds: the B * Hq * T row sums first; when the caller did
+// not pass the forward's rotated Q/K copies (fwd_rotated = 0) and they fit in
+// the rest of the array (B * Hq * T up to about 50,000 at head_dim 128 with
+// four query heads per KV head), the once-rotated Q/K copies as well, exactly
+// as ai_attn_bwd places them in a workspace of that size.  Above that the kernels rotate each tile in shared
+// memory instead (same results to rounding, slower), so the speed of this
+// entry point drops at a shape-dependent size and the race between
+// overlapping calls covers the copies too when they are there.
 
 #include <cuda_runtime.h>
 
@@ -39,10 +48,20 @@ std::mutex g_scratch_mu;
 int scratch_for_current_device(float** out) {
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return AI_ERR_NO_DEVICE;
+  // The library holds sm_100a code only: on any other part the symbol does
+  // not exist there, so say so before looking it up.
+  int major = -1;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess || major != 10) {
+    cudaGetLastError();
+    return AI_ERR_NO_DEVICE;
+  }
   std::lock_guard<std::mutex> lock(g_scratch_mu);
   if (!g_scratch_ptr[dev]) {
     void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) return AI_ERR_LAUNCH;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) {
+      cudaGetLastError();  // leave no pending error for the next launch check of this thread
+      return AI_ERR_NO_DEVICE;
+    }
     g_scratch_ptr[dev] = static_cast<float*>(p);
   }
   *out = g_scratch_ptr[dev];

@@ -61,56 +61,6 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, long lo
   return true;
 }
 
-// ---------------------------------------------------------------- clusters
-// A CTA pair (cluster of two) shares one 2-SM tcgen05.mma: rank 0 issues it,
-// both CTAs supply operands from the same shared-memory offsets and receive
-// their own 128 accumulator rows in TMEM.
-__device__ __forceinline__ uint32_t cluster_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-
-// Every thread of both CTAs; orders all earlier shared-memory accesses.
-__device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
-// Address of the same shared-memory location in the CTA of cluster rank `rank`.
-__device__ __forceinline__ uint32_t mapa(uint32_t addr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
-  return r;
-}
-
-// Arrive (release at cluster scope) on an mbarrier given by a shared::cluster
-// address, which may lie in the peer CTA.
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cl_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cl_addr) : "memory");
-}
-
-// Wait that acquires at cluster scope (the barrier collects arrivals of both CTAs).
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, long long max_cycles) {
-  if (mbar_try_wait_cluster(bar, parity)) return true;
-  const long long t0 = clock64();
-  while (!mbar_try_wait_cluster(bar, parity)) {
-    if (clock64() - t0 > max_cycles) return false;
-  }
-  return true;
-}
-
 // ---------------------------------------------------------------- proxies
 // Generic-proxy shared-memory writes -> visible to the async proxy (TMA, tcgen05.mma).
 __device__ __forceinline__ void fence_proxy_async_smem() {
@@ -141,11 +91,6 @@ __device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bu
 // Every committed bulk store has completed.
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
-// Named barrier over `count` threads (ids 1..15; 0 is __syncthreads).
-__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t count) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
-}
-
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -173,18 +118,6 @@ __device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-// D[tmem] (+)= A[tmem] * B[smem]^T, kind::f16; A (M x 16 per instruction,
-// 16-bit elements packed two per 32-bit column, row = lane) sits in TMEM.
-__device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
-                                       uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 
@@ -253,65 +186,9 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// 2^x for x <= 2^22 on the FMA pipe (no SFU): x = n + f with n = round(x)
-// (the 1.5 * 2^23 shift leaves n in the low mantissa bits), 2^f for
-// f in [-1/2, 1/2] from a degree-3 least-squares polynomial fitted at 4000
-// Chebyshev nodes (max relative error 7.7e-5), and n added to the exponent
-// field.  Inputs below -125 (masked scores are -inf) return 2^-125.
-__device__ __forceinline__ float exp2_fma(float x) {
-  x = fmaxf(x, -125.f);
-  const float t = x + 12582912.f;
-  const float f = x - (t - 12582912.f);
-  const float p = fmaf(fmaf(fmaf(0.05508868396f, f, 0.2426040471f), f, 0.6932762265f), f, 0.9999289513f);
-  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
-}
-
 // Arrive on `bar` once every tcgen05 operation this thread issued so far has completed.
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
-}
-
-// ---------------------------------------------------------------- tcgen05, CTA pairs
-// The same warp (same warp index) of both CTAs of the pair calls alloc,
-// relinquish and dealloc; the column address lands at the same smem offset.
-__device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
-  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols) : "memory");
-}
-__device__ __forceinline__ void tmem_relinquish_pair() {
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
-}
-
-// 2-SM MMA (M = 256: rows 0-127 from rank 0, rows 128-255 from rank 1; each
-// CTA supplies N/2 rows (K-major) or columns (MN-major) of B from its own
-// shared memory at the descriptor's offset).  Issued by one thread of rank 0.
-__device__ __forceinline__ void mma_ss_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                            uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-__device__ __forceinline__ void mma_ts_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
-                                            uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-// Arrive on the mbarrier at offset `bar` in BOTH CTAs of the pair once every
-// pair MMA this thread issued so far has completed: one commit to the local
-// barrier, one to the peer's (shared::cluster address from mapa).
-__device__ __forceinline__ void mma_commit_pair(uint32_t bar, uint32_t peer_bar) {
-  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
-  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(peer_bar) : "memory");
 }
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }

@@ -39,6 +39,7 @@ __all__ = [
     "PositionBlock",
     "PositionBlockList",
     "document_blocks",
+    "blocks_from_concat",
     "cursor_stream",
 ]
 
@@ -145,6 +146,36 @@ def document_blocks(doc_lens: Sequence[int], position_ids: Optional[Sequence[int
         ))
         s = e
     return blocks.concat()
+
+
+def blocks_from_concat(boundary_indices, query_pos_ids, concat_key_pos_ids, concat_attn_masks,
+                       concat_abs_pos_masks, block_cls=None, list_cls=None, device=None):
+    """The position-block list whose ``concat()`` gives these flattened arrays
+    (the inverse of ``concat()``, ``perturb_labels.py:341-357``): block ``b``
+    with ``boundary_indices[b] = (s, e, ks, ke)`` gets query positions
+    ``query_pos_ids[s:e]`` and the key arrays ``[ks, ke)``.  ``block_cls`` /
+    ``list_cls`` choose the block and list types (default: this module's; the
+    reference's own types have the same fields)."""
+    block_cls = block_cls or PositionBlock
+    list_cls = list_cls or PositionBlockList
+
+    def t(x, dtype):
+        return torch.as_tensor(np.asarray(x.detach().cpu() if hasattr(x, "detach") else x), dtype=dtype,
+                               device=device)
+
+    qp = t(query_pos_ids, torch.long)
+    kp = t(concat_key_pos_ids, torch.long)
+    am = t(concat_attn_masks, torch.bool)
+    ab = t(concat_abs_pos_masks, torch.bool)
+    out = list_cls()
+    for s, e, ks, ke in np.asarray(boundary_indices, dtype=np.int64).reshape(-1, 4):
+        s, e, ks, ke = int(s), int(e), int(ks), int(ke)
+        a = ab[ks:ke]
+        out.append(block_cls(key_pos_ids=kp[ks:ke].clone(), query_pos_ids=qp[s:e].clone(),
+                             abs_pos_mask=a.clone() if bool(a.any()) else None, attn_mask=am[ks:ke].clone(),
+                             start_idx=s, end_idx=e, block_type=None))
+    out.concat()
+    return out
 
 
 def cursor_stream(n: int, rng: np.random.Generator, p_step: float = 0.8) -> np.ndarray:

@@ -1,19 +1,35 @@
 """Benchmark of the chain-of-edits (multi-segment RoPE) attention fwd+bwd.
 
-Workload: Qwen3-8B-shaped attention layer, bf16,
-B=4, T=4096, Hq=32, Hkv=8, head_dim=128, rope_theta=1e6, two head-dim RoPE
-sections (slots [0,32) follow arange, slots [32,64) an edit-cursor stream),
-every batch row packs documents with lengths ~ U[256, 2048] (causal inside
-each document, one position-block per document).  Synthetic seeded inputs.
-
-A step = forward + backward of the attention over the batch.
+Headline workload (the default): Qwen3-8B-shaped attention
+layer, bf16, B=4, T=4096, Hq=32, Hkv=8, head_dim=128, rope_theta=1e6, two
+head-dim RoPE sections (slots [0,32) follow arange, slots [32,64) an
+edit-cursor stream), every batch row packs documents with lengths
+~ U[256, 2048] (causal inside each document, one position block per
+document).  Synthetic seeded inputs.  A step = forward + backward of the
+attention over the batch.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config 1|E|4|2a|3] [--compare-triton]
 
-Under torchrun (N > 1) every rank runs its own batch (weak scaling, no
-collective on the data path); the step time is the max over ranks.
-``--impl reference`` times the CPU oracle (numpy restatement of the
-reference's eager path) on a bounded sample of the same workload.
+Other workloads (``--config``), one JSON line each:
+
+* ``E``: the reference's own workload, a CPT edit chain built by its sampler
+  (``tests/golden/chain_e.npz``: T=3072, 71 blocks, abs keys, keys at
+  block-dependent positions), B=1, Hq=32, Hkv=8, one RoPE section;
+* ``4``: 64 sequences of U[64, 2048] tokens packed into one 65,536-token row,
+  two sections;
+* ``2a``: the attention layer of config 2 (one causal sequence of 8,192
+  tokens, micro-batch 1), two sections;
+* ``3``: one causal sequence of 32,768 tokens, three sections (24/24/16
+  frequency slots).  Under torchrun its heads are split by KV head over the
+  ranks and O, dQ, dK, dV are all-gathered (NCCL), strong scaling.
+
+Under torchrun (N > 1) configs 1, E, 4 and 2a run one batch per rank (weak
+scaling, no collective on the data path); the step time is the max over
+ranks.  ``--impl reference`` times the reference's own eager attention (fp32,
+all host cores) on a bounded sample of the workload.  ``--compare-triton``
+times the reference's Triton backend against this library on the same GPU
+and inputs (configs 1 and E).
 """
 
 from __future__ import annotations
@@ -25,6 +41,8 @@ import subprocess
 import sys
 import threading
 import time
+from dataclasses import dataclass
+from typing import Any, List
 
 import numpy as np
 
@@ -34,13 +52,15 @@ sys.path.insert(0, ROOT)
 B, T, HQ, HKV, D = 4, 4096, 32, 8, 128
 THETA = 1e6
 SECTIONS = [(0, 32), (32, 64)]
+SECTIONS3 = [(0, 24), (24, 48), (48, 64)]
 WORKLOAD = ("cfg1: bf16 B=4 T=4096 Hq=32 Hkv=8 D=128 theta=1e6, docs U[256,2048] packed per row, "
             "2 RoPE sections (32+32 freq slots: arange, cursor stream)")
 METRIC = "multi-seg RoPE attn fwd+bwd TFLOP/s (causal-adjusted, 14*D*pairs*Hq)"
 DOM_KERNEL_NAMES = {"fwd": "fwd_pers_kernel (forward)", "dq": "dq_pers_kernel (dQ)", "dkdv": "dkdv_ws_kernel (dK/dV)"}
-# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch on this
-# workload, from one ncu capture of the three kernels (profiles/).
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch on the
+# config-1 workload, from one ncu capture of the three kernels (profiles/).
 TRAFFIC_BYTES = {"fwd": 368016640, "dq": 549332224, "dkdv": 401622016}
+REF_PATH = os.path.join(ROOT, "baseline", "_ref")
 
 
 def make_rows(seed: int):
@@ -58,6 +78,17 @@ def make_rows(seed: int):
     return rows, streams
 
 
+def _inputs(seed, b, hq, hkv, t):
+    import torch
+
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(b, hq, t, D, generator=g).to(torch.bfloat16)
+    k = torch.randn(b, hkv, t, D, generator=g).to(torch.bfloat16)
+    v = torch.randn(b, hkv, t, D, generator=g).to(torch.bfloat16)
+    dout = torch.randn(b, t, hq, D, generator=g).to(torch.bfloat16)
+    return q, k, v, dout
+
+
 def make_workload(seed: int, device):
     """Config-1 inputs: the document layout is the same on every rank (seed 0:
     fixed per-GPU work for weak scaling), q/k/v/dO values are seeded by `seed`."""
@@ -67,12 +98,86 @@ def make_workload(seed: int, device):
 
     rows, streams = make_rows(0)
     rope = ab.SectionedRope(D, THETA, [torch.as_tensor(s) for s in streams], SECTIONS, device=device)
-    g = torch.Generator().manual_seed(seed)
-    q = torch.randn(B, HQ, T, D, generator=g).to(torch.bfloat16)
-    k = torch.randn(B, HKV, T, D, generator=g).to(torch.bfloat16)
-    v = torch.randn(B, HKV, T, D, generator=g).to(torch.bfloat16)
-    dout = torch.randn(B, T, HQ, D, generator=g).to(torch.bfloat16)
-    return rows, rope, streams, (q, k, v, dout)
+    return rows, rope, streams, _inputs(seed, B, HQ, HKV, T)
+
+
+@dataclass
+class Workload:
+    cfg: str
+    desc: str
+    batch: int
+    seq_len: int
+    rows: Any          # the layout handed to the attention (RowLayouts or a shared list)
+    rope: Any          # RotaryEmbeddingFunc (torch module)
+    streams: List[np.ndarray]
+    sections: List[tuple]
+    host: tuple        # q, k, v, dout (CPU bf16)
+
+    def row_lists(self):
+        """One position-block list per batch row."""
+        from autoindexer_b200.meta import layout_rows
+
+        return layout_rows(self.rows, self.batch)
+
+
+CONFIG_DESC = {
+    "1": WORKLOAD,
+    "E": ("cfgE: bf16 B=1 T=3072 Hq=32 Hkv=8 D=128 theta=1e6, CPT edit chain from the reference's sampler "
+          "(autoindexer_8B.yaml perturbation: 71 blocks, sum E=145958, 12798 abs keys), 1 RoPE section"),
+    "4": ("cfg4: bf16 B=1 T=65536 Hq=32 Hkv=8 D=128 theta=1e6, 64 sequences U[64,2048] rescaled to 65536 tokens, "
+          "2 RoPE sections"),
+    "2a": ("cfg2 attention layer: bf16 B=1 T=8192 Hq=32 Hkv=8 D=128 theta=1e6, one causal sequence, "
+           "2 RoPE sections"),
+    "3": ("cfg3: bf16 B=1 T=32768 Hq=32 Hkv=8 D=128 theta=1e6, one causal sequence, 3 RoPE sections "
+          "(24/24/16 freq slots: arange, two cursor streams)"),
+}
+
+
+def build_workload(cfg: str, seed: int, device) -> Workload:
+    """The seeded workload of a configuration: the layout is fixed per
+    configuration; q/k/v/dO are seeded by ``seed``."""
+    import torch
+
+    import autoindexer_b200 as ab
+
+    if cfg == "1":
+        rows, rope, streams, host = make_workload(seed, device)
+        return Workload(cfg, CONFIG_DESC[cfg], B, T, rows, rope, streams, SECTIONS, host)
+    if cfg == "E":
+        with np.load(os.path.join(ROOT, "tests", "golden", "chain_e.npz")) as z:
+            g = {k: z[k] for k in z.files}
+        lay = ab.blocks_from_concat(g["boundary_indices"], g["query_pos_ids"], g["concat_key_pos_ids"],
+                                    g["concat_attn_masks"], g["concat_abs_pos_masks"])
+        t = int(g["T_model"])
+        pmax = int(max(g["query_pos_ids"].max(), g["concat_key_pos_ids"].max())) + 1
+        streams = [np.arange(pmax)]
+        rope = ab.SectionedRope(D, THETA, [torch.as_tensor(streams[0])], [(0, D // 2)], device=device)
+        return Workload(cfg, CONFIG_DESC[cfg], 1, t, lay, rope, streams, [(0, D // 2)], _inputs(seed, 1, HQ, HKV, t))
+    if cfg == "4":
+        t = 65536
+        rng = np.random.default_rng(4)
+        raw = rng.integers(64, 2049, 64).astype(np.float64)
+        lens = np.maximum(np.round(raw / raw.sum() * t).astype(int), 1)
+        lens[-1] += t - lens.sum()
+        streams = [np.arange(t), ab.cursor_stream(t, rng)]
+        rows = ab.RowLayouts([ab.document_blocks([int(x) for x in lens], position_ids=np.arange(t))])
+        sections = SECTIONS
+    elif cfg == "2a":
+        t = 8192
+        rng = np.random.default_rng(2)
+        streams = [np.arange(t), ab.cursor_stream(t, rng)]
+        rows = ab.RowLayouts([ab.document_blocks([t], position_ids=np.arange(t))])
+        sections = SECTIONS
+    elif cfg == "3":
+        t = 32768
+        rng = np.random.default_rng(3)
+        streams = [np.arange(t), ab.cursor_stream(t, rng), ab.cursor_stream(t, rng)]
+        rows = ab.RowLayouts([ab.document_blocks([t], position_ids=np.arange(t))])
+        sections = SECTIONS3
+    else:
+        raise ValueError(f"unknown config {cfg}")
+    rope = ab.SectionedRope(D, THETA, [torch.as_tensor(s) for s in streams], sections, device=device)
+    return Workload(cfg, CONFIG_DESC[cfg], 1, t, rows, rope, streams, sections, _inputs(seed, 1, HQ, HKV, t))
 
 
 class ClockSampler:
@@ -165,107 +270,31 @@ def sum_over_ranks(x: float, world: int, device) -> float:
 
 
 def job_tflops(job_flops_per_step: float, steps: int, t_max: float) -> float:
-    """Whole-job throughput: every rank processes its own seeded batch (weak
-    scaling), so the job's FLOPs per step are the sum over ranks; the job
-    takes as long as its slowest rank."""
+    """Whole-job throughput: job FLOPs per step (summed over ranks for weak
+    scaling, the one problem's FLOPs for strong scaling) over the slowest
+    rank's time."""
     return job_flops_per_step * steps / t_max / 1e12
 
 
-def run_ours(args):
+def _e2e(args, dev, host, apply, out_shapes, world):
+    """End to end through a public function: every step copies its inputs in
+    from pinned host memory (copy-in stream, two device buffer sets), runs
+    ``apply(q, k, v) -> out`` and its autograd backward (compute stream), and
+    copies (out, dq, dk, dv) back to pinned host memory (copy-out stream);
+    the three streams overlap consecutive steps the way a training loop
+    feeding host data runs them.  Returns (seconds for ``args.steps`` steps,
+    max over ranks; bytes in; bytes out) per step."""
     import torch
     import torch.distributed as dist
 
-    from autoindexer_b200 import _lib
-    from autoindexer_b200.attention import KernelTimes, attn_bwd, attn_fwd, fused_chain_of_edits_attn_b200, read_status
-    from autoindexer_b200.meta import compile_layout
-
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        from datetime import timedelta
-        os.environ.setdefault("NCCL_DEBUG", "WARN")  # keep stdout to the one JSON line
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
-
-    rows, rope, _, host = make_workload(seed=rank, device=dev)
-    q, k, v, dout = (x.to(dev) for x in host)
-    scale = D ** -0.5
-    layout = compile_layout(rows, B, T, D, torch.bfloat16, rope, dev)
-    flops = 14.0 * D * HQ * layout.pairs_per_head
-    flops_fwd = 4.0 * D * HQ * layout.pairs_per_head
-    flops_bwd = 10.0 * D * HQ * layout.pairs_per_head
-    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
-    stream = torch.cuda.current_stream(dev)
-
-    def step():
-        out, lse, ws = attn_fwd(q, k, v, layout, scale, keep_workspace=True)
-        return attn_bwd(q, k, v, out, lse, dout, layout, scale, fwd_workspace=ws)
-
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize(dev)
-    assert read_status(dev) == 0
-
-    # Device-timed steps: events around each step, L2 flushed (untimed) between steps.
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
-           torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize(dev)
-    with ClockSampler(local) as clocks:
-        for i in range(args.steps):
-            flush.fill_(float(i))
-            e0, e1, e2 = ev[i]
-            e0.record(stream)
-            out, lse, ws = attn_fwd(q, k, v, layout, scale, keep_workspace=True)
-            e1.record(stream)
-            grads = attn_bwd(q, k, v, out, lse, dout, layout, scale, fwd_workspace=ws)
-            e2.record(stream)
-            # Release this step's tensors as the warm-up does, so that every
-            # step reuses the same allocator blocks.
-            del out, lse, ws, grads
-        torch.cuda.synchronize(dev)
-    if world > 1:
-        dist.barrier()
-    t_fwd = sum(a.elapsed_time(b) for a, b, _ in ev) / 1e3
-    t_bwd = sum(b.elapsed_time(c) for _, b, c in ev) / 1e3
-    t_step = t_fwd + t_bwd
-    t_max = max_over_ranks(t_step, world, dev)
-    job_flops = sum_over_ranks(flops, world, dev)
-    value = job_tflops(job_flops, args.steps, t_max)
-    ms_per_step = t_max / args.steps * 1e3
-
-    # Per-kernel device times: the same steps again with the library's launch
-    # events on (ai_attn_profile_*); they give the dominant kernel's duration
-    # for the roofline and the count of our launches.
-    torch.cuda.synchronize(dev)
-    with KernelTimes() as kt:
-        for i in range(args.steps):
-            flush.fill_(float(i))
-            step()
-        torch.cuda.synchronize(dev)
-
-    # End to end through the public API: pinned host inputs -> device, forward +
-    # backward via autograd, results (out, dq, dk, dv) back to pinned host memory.
     pinned = [x.pin_memory() for x in host]
-    outs_host = [torch.empty(B, T, HQ, D, dtype=torch.bfloat16).pin_memory(),
-                 torch.empty(B, HQ, T, D, dtype=torch.bfloat16).pin_memory(),
-                 torch.empty(B, HKV, T, D, dtype=torch.bfloat16).pin_memory(),
-                 torch.empty(B, HKV, T, D, dtype=torch.bfloat16).pin_memory()]
+    outs_host = [torch.empty(s, dtype=torch.bfloat16).pin_memory() for s in out_shapes]
     h2d = sum(x.numel() * x.element_size() for x in pinned)
     d2h = sum(x.numel() * x.element_size() for x in outs_host)
-
-    # The steps are pipelined over three streams: step i's inputs are copied in
-    # (copy-in stream, two device buffer sets) while step i - 1 computes and
-    # step i - 2's results are copied out (copy-out stream), the way a training
-    # loop feeding host data would run them; every step copies its own inputs
-    # in and its own results out inside the timed span.
     s_in, s_comp, s_out = (torch.cuda.Stream(dev) for _ in range(3))
     dev_in = [[torch.empty(x.shape, dtype=x.dtype, device=dev) for x in pinned] for _ in range(2)]
 
-    def e2e_run(nsteps, ev_start=None, ev_end=None):
+    def run(nsteps, ev_start=None, ev_end=None):
         comp_done = []
         if ev_start is not None:
             ev_start.record(s_in)
@@ -281,7 +310,7 @@ def run_ours(args):
             s_comp.wait_event(in_done)
             with torch.cuda.stream(s_comp):
                 xq, xk, xv = (b.detach().requires_grad_(True) for b in buf[:3])
-                o, _ = fused_chain_of_edits_attn_b200(rope, xq, xk, xv, rows)
+                o = apply(xq, xk, xv)
                 o.backward(buf[3])
                 res = (o.detach(), xq.grad, xk.grad, xv.grad)
                 ev = torch.cuda.Event()
@@ -295,14 +324,121 @@ def run_ours(args):
         if ev_end is not None:
             ev_end.record(s_out)
 
-    e2e_run(max(1, args.warmup))
+    run(max(1, args.warmup))
     torch.cuda.synchronize(dev)
     e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if world > 1:
         dist.barrier()
-    e2e_run(args.steps, e_start, e_end)
+    run(args.steps, e_start, e_end)
     torch.cuda.synchronize(dev)
     t_e2e = max_over_ranks(e_start.elapsed_time(e_end) / 1e3, world, dev)
+    return t_e2e, h2d, d2h
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    from autoindexer_b200.attention import KernelTimes, attn_bwd, attn_fwd, fused_chain_of_edits_attn_b200, read_status
+    from autoindexer_b200.meta import compile_layout
+    from autoindexer_b200 import sharding
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        os.environ.setdefault("NCCL_DEBUG", "WARN")  # keep stdout to the one JSON line
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    sharded = args.config == "3" and world > 1
+    # Weak scaling: every rank its own seeded values on the same layout.
+    # Strong scaling (sharded config 3): one problem, the same inputs everywhere.
+    wl = build_workload(args.config, seed=0 if sharded else rank, device=dev)
+    Bw, Tw = wl.batch, wl.seq_len
+    q, k, v, dout = (x.to(dev) for x in wl.host)
+    scale = D ** -0.5
+    layout = compile_layout(wl.rows, Bw, Tw, D, torch.bfloat16, wl.rope, dev)
+    flops = 14.0 * D * HQ * layout.pairs_per_head
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    G = HQ // HKV
+    if sharded:
+        k0, k1 = sharding.head_range(HKV, rank, world)
+        ql, kl, vl = q[:, k0 * G:k1 * G], k[:, k0:k1], v[:, k0:k1]
+        dol = dout[:, :, k0 * G:k1 * G].contiguous()
+        bufs = sharding.GatherBuffers(q, k)
+    gather_ev = []
+
+    def step(timed=None):
+        """One forward + backward; ``timed``: (e0, e1, e2) events recorded
+        around the forward and the backward."""
+        if timed:
+            timed[0].record(stream)
+        if not sharded:
+            out, lse, ws = attn_fwd(q, k, v, layout, scale, keep_workspace=True)
+            if timed:
+                timed[1].record(stream)
+            grads = attn_bwd(q, k, v, out, lse, dout, layout, scale, fwd_workspace=ws)
+            if timed:
+                timed[2].record(stream)
+            return
+        out = sharding.sharded_forward(ql, kl, vl, layout, scale, bufs)
+        if timed:
+            timed[1].record(stream)
+        sharding.sharded_backward(dol, bufs)
+        if timed:
+            timed[2].record(stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    assert read_status(dev) == 0
+
+    # Device-timed steps: events around each step, L2 flushed (untimed) between steps.
+    ev = [tuple(torch.cuda.Event(enable_timing=True) for _ in range(3)) for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    with ClockSampler(local) as clocks:
+        for i in range(args.steps):
+            flush.fill_(float(i))
+            step(ev[i])
+        torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    t_fwd = sum(a.elapsed_time(b) for a, b, _ in ev) / 1e3
+    t_bwd = sum(b.elapsed_time(c) for _, b, c in ev) / 1e3
+    t_step = t_fwd + t_bwd
+    t_max = max_over_ranks(t_step, world, dev)
+    job_flops = flops if sharded else sum_over_ranks(flops, world, dev)
+    value = job_tflops(job_flops, args.steps, t_max)
+    ms_per_step = t_max / args.steps * 1e3
+
+    # Per-kernel device times: the same steps again with the library's launch
+    # events on (ai_attn_profile_*); they give the dominant kernel's duration
+    # for the roofline and the count of our launches.
+    torch.cuda.synchronize(dev)
+    with KernelTimes() as kt:
+        for i in range(args.steps):
+            flush.fill_(float(i))
+            step()
+        torch.cuda.synchronize(dev)
+    gather_ms = None
+    if sharded:
+        gather_ms = bufs.gather_ms()
+
+    # End to end through the public API.
+    if sharded:
+        def apply(xq, xk, xv):
+            return sharding.kv_sharded_attention(xq, xk, xv, layout, scale)
+    else:
+        def apply(xq, xk, xv):
+            return fused_chain_of_edits_attn_b200(wl.rope, xq, xk, xv, wl.rows)[0]
+    out_shapes = [(Bw, Tw, HQ, D), (Bw, HQ, Tw, D), (Bw, HKV, Tw, D), (Bw, HKV, Tw, D)]
+    t_e2e, h2d, d2h = _e2e(args, dev, wl.host, apply, out_shapes, world)
     e2e_value = job_tflops(job_flops, args.steps, t_e2e)
     assert read_status(dev) == 0
 
@@ -310,14 +446,14 @@ def run_ours(args):
     # Dominant kernel: algorithmic FLOPs per launch (per query head and finite
     # (query, key) pair: forward 4·D, dQ 6·D — S, dP, dQ — and dK/dV 8·D — S,
     # dP, dV, dK) over its event-timed duration.
-    kflops = {"fwd": 4.0 * D * HQ * layout.pairs_per_head, "dq": 6.0 * D * HQ * layout.pairs_per_head,
-              "dkdv": 8.0 * D * HQ * layout.pairs_per_head}
+    hq_local = (HQ // world) if sharded else HQ
+    kflops = {kk: c * D * hq_local * layout.pairs_per_head for kk, c in (("fwd", 4.0), ("dq", 6.0), ("dkdv", 8.0))}
     dom = max(kflops, key=lambda kk: kt.ms[kk])
     dom_ms = kt.ms[dom] / max(1, kt.launches[dom])  # per launch
     achieved = kflops[dom] * args.steps / (kt.ms[dom] * 1e-3) / 1e12
     launches_per_step = sum(kt.launches.values()) / args.steps
-    tokens = world * B * T * args.steps / t_max
-
+    tokens = (1 if sharded else world) * Bw * Tw * args.steps / t_max
+    n_ranks_work = 1 if sharded else world
     line = {
         "metric": METRIC,
         "value": round(value, 3),
@@ -327,69 +463,117 @@ def run_ours(args):
         "warmup": args.warmup,
         "ms_per_step": round(ms_per_step, 4),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if sharded else "weak",
         "vs_baseline": None,
         "dtype": "bf16",
-        "data": "synthetic (seeded randn q/k/v/dO; seeded document lengths and cursor streams)",
-        "config": {"workload": WORKLOAD, "global_batch": B * world, "seq_len": T, "parallelism": f"dp{world} (independent rows)",
+        "data": "synthetic (seeded randn q/k/v/dO; seeded layouts and cursor streams)",
+        "config": {"workload": wl.desc, "global_batch": Bw * n_ranks_work, "seq_len": Tw,
+                   "parallelism": (f"kv-head shards over {world} ranks + NCCL all-gather" if sharded
+                                   else f"dp{world} (independent rows)"),
                    "l2": "flushed between timed steps (256 MB write, untimed)"},
-        "fwd_ms": round(t_fwd / args.steps * 1e3, 4),
-        "bwd_ms": round(t_bwd / args.steps * 1e3, 4),
+        "fwd_ms": round(max_over_ranks(t_fwd, world, dev) / args.steps * 1e3, 4),
+        "bwd_ms": round(max_over_ranks(t_bwd, world, dev) / args.steps * 1e3, 4),
         "tokens_per_s": round(tokens, 1),
         "pairs_per_head": layout.pairs_per_head,
-        "pct_bf16_peak": round(100 * value / world / peak, 2),
-        "pct_bf16_spec_2250": round(100 * value / world / 2250.0, 2),
+        "pct_bf16_peak": round(100 * value / n_ranks_work / peak, 2) if not sharded else
+        round(100 * value / world / peak, 2),
+        "pct_bf16_spec_2250": round(100 * value / (world if sharded else n_ranks_work) / 2250.0, 2),
         "roofline": {"bound": "tensor", "kernel": DOM_KERNEL_NAMES[dom],
                      "achieved": round(achieved, 3), "peak": peak, "unit": "TFLOP/s",
                      "frac": round(achieved / peak, 4), "peak_kind": f"{peak_kind} burst bf16",
-                     "launch_ms": round(dom_ms, 4), "traffic": TRAFFIC_BYTES.get(dom)},
-        "kernel_ms_per_step": {kk: round(v / args.steps, 4) for kk, v in kt.ms.items() if v > 0},
+                     "launch_ms": round(dom_ms, 4),
+                     "traffic": TRAFFIC_BYTES.get(dom) if args.config == "1" else None},
+        "kernel_ms_per_step": {kk: round(v_ / args.steps, 4) for kk, v_ in kt.ms.items() if v_ > 0},
         "e2e": {"value": round(e2e_value, 3), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
         "gpu_launches": int(round(launches_per_step * args.steps)),
         "clocks": clocks.summary(),
     }
-    if world == 1 and not args.no_cpu_baseline:  # the CPU baseline is an N=1 figure
-        line["cpu_baseline"] = cpu_baseline(rows, host, seed=0)
+    if gather_ms is not None:
+        line["allgather_ms_per_step"] = round(max_over_ranks(gather_ms / args.steps, world, dev), 4)
+    if world == 1 and args.config == "1" and not args.no_cpu_baseline:  # the CPU baseline is an N=1 figure
+        line["cpu_baseline"] = cpu_baseline(wl, seed=0)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
 
 
-def cpu_baseline(rows, host, seed=0, reps=1):
-    """Oracle (numpy port of the reference's eager path, fp32, all host
-    threads) on one (row, kv-group) slice: 4 query heads of batch row 0."""
+def _reference_modules():
+    """The reference's own attention code from its offline install under
+    ``baseline/_ref`` (``pip install --no-deps --target baseline/_ref``), or
+    None when it is not there."""
+    if not os.path.isdir(REF_PATH):
+        return None
+    if REF_PATH not in sys.path:
+        sys.path.insert(0, REF_PATH)
+    try:
+        from autoindexer.models.autoindexer.attention import reference as ref
+        from autoindexer.models.autoindexer import perturb_labels as pl
+        from autoindexer.models.autoindexer import type_utils as tu
+    except Exception:  # noqa: BLE001 - any import failure means "not available"
+        return None
+    return ref, pl, tu
+
+
+def cpu_baseline(wl: Workload, seed=0, reps=1):
+    """The reference's eager attention (``chain_of_edits_attn_ref``,
+    ``attention/reference.py:116-141``, from ``baseline/_ref``) forward +
+    autograd backward in fp32 on all host cores, on one (batch row, KV group)
+    slice of the workload: 4 query heads of batch row 0, K/V expanded as the
+    reference's interface does.  Without the install, the oracle (numpy
+    restatement of the same code) on the same slice."""
     import torch
 
-    import autoindexer_b200 as ab
-    from oracle import attn_oracle as O
-
-    q, k, v, dout = host
+    q, k, v, dout = wl.host
     G = HQ // HKV
-    rng = np.random.default_rng(seed)
-    streams = [np.arange(T), ab.cursor_stream(T, rng)]
-    rope_mod = ab.SectionedRope(D, THETA, [torch.as_tensor(s) for s in streams], SECTIONS)
-    rope = O.make_sectioned_rope(rope_mod.inv_freq.numpy(), streams, SECTIONS)
-    lay = rows[0]
-    qs = q[:1, :G].float().numpy()
-    ks = k[:1, :1].float().numpy()
-    vs = v[:1, :1].float().numpy()
-    dos = dout[:1, :, :G].float().numpy()
-    pairs = O.count_pairs(lay, T)
-    # All host threads for the BLAS calls, also under torchrun (which sets
-    # OMP_NUM_THREADS=1 for its workers).
+    lay = wl.row_lists()[0]
+    Tw = wl.seq_len
+    pairs = sum(int(np.cumsum(np.asarray(lay.concat_attn_masks[ks:ke], dtype=np.int64))[s:e].sum())
+                for s, e, ks, ke in lay.boundary_indices)
+    flops = 14.0 * D * G * pairs
+    mods = _reference_modules()
     from threadpoolctl import threadpool_limits
 
-    with threadpool_limits(limits=os.cpu_count()):
-        t0 = time.perf_counter()
-        for _ in range(reps):
-            O.attn_forward(qs, ks, vs, lay, rope, dtype=np.float32)
-            O.attn_backward(qs, ks, vs, dos, lay, rope, dtype=np.float32)
-        dt = (time.perf_counter() - t0) / reps
-    flops = 14.0 * D * G * pairs
-    return {"value": round(flops / dt / 1e12, 6), "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "port",
-            "sample": f"batch row 0, kv group 0 ({G} query heads), T={T}: fwd+bwd, numpy fp32, {dt:.2f} s"}
+    cores = os.cpu_count()
+    if mods is not None:
+        ref, pl, tu = mods
+        import autoindexer_b200 as ab
+
+        rlay = ab.blocks_from_concat(lay.boundary_indices, lay.query_pos_ids, lay.concat_key_pos_ids,
+                                     lay.concat_attn_masks, lay.concat_abs_pos_masks,
+                                     block_cls=tu.PositionBlock, list_cls=pl.PositionBlockList)
+        rope = ab.SectionedRope(D, THETA, [torch.as_tensor(s) for s in wl.streams], wl.sections)
+        prev = torch.get_num_threads()
+        torch.set_num_threads(cores)
+        try:
+            t0 = time.perf_counter()
+            for _ in range(reps):
+                rlay._query_rotary_pos_emb = rlay._keys_rotary_pos_emb = None
+                qs = q[:1, :G].float().requires_grad_(True)
+                ks = k[:1, :1].float().requires_grad_(True)
+                vs = v[:1, :1].float().requires_grad_(True)
+                out, _ = ref.chain_of_edits_attn_ref(rope, qs, ks.expand(1, G, Tw, D), vs.expand(1, G, Tw, D), rlay)
+                out.backward(dout[:1, :, :G].float())
+            dt = (time.perf_counter() - t0) / reps
+        finally:
+            torch.set_num_threads(prev)
+        kind, what = "reference", "reference eager chain_of_edits_attn_ref + autograd, torch fp32"
+    else:
+        from oracle import attn_oracle as O
+
+        rope = O.make_sectioned_rope(wl.rope.inv_freq.cpu().numpy(), wl.streams, wl.sections)
+        qs, ks, vs = (x[:1, :n].float().numpy() for x, n in ((q, G), (k, 1), (v, 1)))
+        dos = dout[:1, :, :G].float().numpy()
+        with threadpool_limits(limits=cores):
+            t0 = time.perf_counter()
+            for _ in range(reps):
+                O.attn_forward(qs, ks, vs, lay, rope, dtype=np.float32)
+                O.attn_backward(qs, ks, vs, dos, lay, rope, dtype=np.float32)
+            dt = (time.perf_counter() - t0) / reps
+        kind, what = "port", "oracle (numpy restatement of the reference's eager path), fp32"
+    return {"value": round(flops / dt / 1e12, 6), "unit": "TFLOP/s", "cores": cores, "kind": kind,
+            "sample": f"batch row 0, kv group 0 ({G} query heads), T={Tw}: fwd+bwd, {what}, {dt:.2f} s"}
 
 
 def run_reference(args):
@@ -397,12 +581,10 @@ def run_reference(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
-    import torch
-
-    rows, _, _, host = make_workload(seed=0, device="cpu")
+    wl = build_workload(args.config, seed=0, device="cpu")
     for _ in range(args.warmup):
-        cpu_baseline(rows, host)
-    vals = [cpu_baseline(rows, host) for _ in range(args.steps)]
+        cpu_baseline(wl)
+    vals = [cpu_baseline(wl) for _ in range(args.steps)]
     value = float(np.median([x["value"] for x in vals]))
     cb = dict(vals[0])
     cb["value"] = round(value, 6)
@@ -410,10 +592,109 @@ def run_reference(args):
         "metric": METRIC, "value": round(value, 6), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (same generator as the GPU arm)", "impl": "reference",
-        "config": {"workload": WORKLOAD, "global_batch": B, "seq_len": T, "parallelism": "cpu"},
+        "config": {"workload": wl.desc, "global_batch": wl.batch, "seq_len": wl.seq_len, "parallelism": "cpu"},
         "cpu_baseline": cb,
         "e2e": {"value": round(value, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    print(json.dumps(line), flush=True)
+
+
+def run_compare_triton(args):
+    """This library against the reference's Triton backend
+    (``fused_chain_of_edits_attn_triton``, ``attention/triton_wrapper.py:57-101``,
+    from ``baseline/_ref``) on the same GPU and the same inputs: forward +
+    autograd backward through each public function, L2 flushed between
+    steps.  The reference's kernel takes one position-block list shared by
+    the batch and expanded K/V (its interface calls ``repeat_kv``,
+    ``attention/__init__.py:36-37``), so it runs one call per batch row with
+    K/V expanded; the expansion is part of its step, as in the reference."""
+    import torch
+
+    import autoindexer_b200 as ab
+    from autoindexer_b200.attention import fused_chain_of_edits_attn_b200
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    wl = build_workload(args.config, seed=0, device=dev)
+    q, k, v, dout = (x.to(dev) for x in wl.host)
+    Bw, Tw = wl.batch, wl.seq_len
+    G = HQ // HKV
+    flush = torch.empty(64 * 1024 * 1024, device=dev)
+    line = {"metric": "fwd+bwd ms per step, this library vs the reference's Triton backend (same GPU, inputs)",
+            "config": {"workload": wl.desc, "l2": "flushed between timed steps"}, "steps": args.steps,
+            "warmup": args.warmup, "dtype": "bf16", "higher_is_better": False}
+
+    def timed(fn):
+        for _ in range(max(3, args.warmup)):
+            fn()
+        torch.cuda.synchronize(dev)
+        tot = 0.0
+        for i in range(args.steps):
+            flush.fill_(float(i))
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize(dev)
+            tot += e0.elapsed_time(e1)
+        return tot / args.steps
+
+    def ours():
+        xq, xk, xv = (x.detach().requires_grad_(True) for x in (q, k, v))
+        o, _ = fused_chain_of_edits_attn_b200(wl.rope, xq, xk, xv, wl.rows)
+        o.backward(dout)
+        return o.detach(), xq.grad, xk.grad, xv.grad
+
+    from autoindexer_b200.meta import compile_layout
+
+    pairs = compile_layout(wl.rows, Bw, Tw, D, torch.bfloat16, wl.rope, dev).pairs_per_head
+    flops = 14.0 * D * HQ * pairs
+    with ClockSampler(0) as clocks:
+        t_ours = timed(ours)
+    line["ours_ms"] = round(t_ours, 4)
+    line["ours_tflops"] = round(flops / t_ours / 1e9, 3)
+    mods = _reference_modules()
+    try:
+        if mods is None:
+            raise RuntimeError("baseline/_ref (the reference's offline install) is missing")
+        ref, pl, tu = mods
+        from autoindexer.models.autoindexer.attention.triton_wrapper import _HAS_TRITON, fused_chain_of_edits_attn_triton
+
+        if not _HAS_TRITON:
+            raise RuntimeError("the reference's Triton kernels did not import")
+        rls = [ab.blocks_from_concat(r.boundary_indices, r.query_pos_ids, r.concat_key_pos_ids, r.concat_attn_masks,
+                                     r.concat_abs_pos_masks, block_cls=tu.PositionBlock,
+                                     list_cls=pl.PositionBlockList, device=dev) for r in wl.row_lists()]
+
+        def triton_step():
+            res = []
+            for b in range(Bw):
+                xq = q[b:b + 1].detach().requires_grad_(True)
+                xk = k[b:b + 1].detach().requires_grad_(True)
+                xv = v[b:b + 1].detach().requires_grad_(True)
+                ke = xk.repeat_interleave(G, dim=1)
+                ve = xv.repeat_interleave(G, dim=1)
+                o, _ = fused_chain_of_edits_attn_triton(wl.rope, xq, ke, ve, rls[b])
+                o.backward(dout[b:b + 1])
+                res.append((o.detach(), xq.grad, xk.grad, xv.grad))
+            return [torch.cat(x, dim=0) for x in zip(*res)]
+
+        with ClockSampler(0) as clocks_t:
+            t_tri = timed(triton_step)
+        a, b_ = ours(), triton_step()
+        par = {}
+        for name, x, y in zip(("out", "dq", "dk", "dv"), a, b_):
+            x, y = x.float(), y.float()
+            par[name] = {"max_abs": round(float((x - y).abs().max()), 5),
+                         "rel_l2": round(float((x - y).norm() / y.norm().clamp_min(1e-30)), 6)}
+        line.update({"triton_ms": round(t_tri, 4), "triton_tflops": round(flops / t_tri / 1e9, 3),
+                     "speedup_vs_triton": round(t_tri / t_ours, 2), "parity_ours_vs_triton": par,
+                     "clocks_triton": clocks_t.summary()})
+    except Exception as e:  # noqa: BLE001 - report why the comparison arm could not run
+        line["triton"] = f"unavailable: {type(e).__name__}: {e}"
+    line["clocks"] = clocks.summary()
+    line["cutedsl"] = ("unavailable: the reference's CuTeDSL backend needs flash-attn-4==4.0.0b29 "
+                       "(flash_attn.cute), which is not installed in this image and cannot be installed offline")
     print(json.dumps(line), flush=True)
 
 
@@ -594,13 +875,18 @@ def run_decode(args):
     }), flush=True)
 
 
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="1", choices=sorted(CONFIG_DESC), help="workload (default: config 1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--compare-triton", action="store_true",
+                    help="time the reference's Triton backend against this library (one extra JSON line)")
     ap.add_argument("--prefill", action="store_true", help="time the prefill path instead (one extra JSON line)")
     ap.add_argument("--decode", action="store_true", help="time one decode step instead (one extra JSON line)")
     args = ap.parse_args()
@@ -608,6 +894,8 @@ def main():
         run_prefill(args)
     elif args.decode:
         run_decode(args)
+    elif args.compare_triton:
+        run_compare_triton(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

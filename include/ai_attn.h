@@ -183,13 +183,18 @@ int ai_attn_bwd(const AiAttnBwdArgs* args, void* stream);
 
 /* Backward for callers that cannot allocate device memory (no counterpart in
  * the reference, which allocates through PyTorch).  Same results as
- * ai_attn_bwd; args->workspace is ignored: the scratch comes from a fixed
- * 16 MiB array inside the library (held on every GPU that loads it until the
- * process exits), so batch * num_q_heads * seq_len must not exceed
- * AI_ATTN_NOALLOC_MAX_ROWS (else AI_ERR_NOALLOC_LIMIT, nothing launched).
- * Calls no allocator.  The first call on a device looks the array up on that
- * device; make it before any stream capture.  Calls that overlap on the GPU
- * share the array and race. */
+ * ai_attn_bwd given a workspace of the same 16 MiB; args->workspace is
+ * ignored: the scratch comes from a fixed 16 MiB array inside the library
+ * (held on every GPU that loads it until the process exits), so
+ * batch * num_q_heads * seq_len must not exceed AI_ATTN_NOALLOC_MAX_ROWS
+ * (else AI_ERR_NOALLOC_LIMIT, nothing launched).  The array holds the row
+ * sums of dO.O and, when fwd_rotated is 0 and they fit (B * Hq * T up to
+ * about 50,000 at head_dim 128 with four query heads per KV head), the
+ * rotated Q/K copies; larger calls rotate every tile in shared memory
+ * instead (slower).  Calls no allocator.  The
+ * first call on a device looks the array up on that device; make it before
+ * any stream capture.  Calls that overlap on the GPU share the array and
+ * race. */
 #define AI_ATTN_NOALLOC_MAX_ROWS (1 << 22)
 int ai_attn_bwd_noalloc(const AiAttnBwdArgs* args, void* stream);
 
@@ -238,6 +243,15 @@ int ai_attn_decode(const AiAttnDecodeArgs* args, void* stream);
 /* Synchronises the stream, copies the device status word to *host_out and
  * resets it to AI_OK.  For tests and debugging; not needed on the hot path. */
 int ai_attn_read_status(int32_t* dev_status, void* stream, int32_t* host_out);
+
+/* Self-test of the device-side failure path (no reference counterpart): one
+ * CTA waits, with the bounded mbarrier wait every kernel here uses, on a
+ * barrier that nothing completes; after max_cycles SM clocks (1 ..
+ * 2,000,000,000) the wait gives up and AI_ERR_DEV_TIMEOUT is recorded in
+ * *status (a device pointer), as a kernel whose wait expired records it.
+ * Nothing asynchronous is in flight, so no fault or hang can follow; read the
+ * code back with ai_attn_read_status. */
+int ai_attn_selftest_wait(int32_t* status, long long max_cycles, void* stream);
 
 /* Static text for a status code. */
 const char* ai_attn_strerror(int code);

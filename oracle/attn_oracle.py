@@ -58,6 +58,7 @@ __all__ = [
     "attn_forward",
     "attn_backward",
     "count_pairs",
+    "attn_chunked",
 ]
 
 
@@ -306,6 +307,111 @@ def attn_backward(q, k, v, dout, layout, rope, scale=None, dtype=np.float64):
         dk[b] = dkb.reshape(Hkv, G, T, D).sum(axis=1)
         dv[b] = dvb.reshape(Hkv, G, T, D).sum(axis=1)
     return dq, dk, dv
+
+
+# ---------------------------------------------------------------------------
+# Query-chunked forward + backward (long sequences)
+# ---------------------------------------------------------------------------
+
+def attn_chunked(q, k, v, dout, layout, rope, scale=None, dtype=np.float64, chunk=512, backward=True):
+    """The same function as ``attn_forward`` / ``attn_backward``, evaluated one
+    block and one chunk of its query rows at a time, so that no ``(H, T, T)``
+    array is ever held (the reference's eager path needs one; at T = 8192 and
+    beyond it does not fit).  Per block ``[s, e)`` (``reference.py:46-62``) a
+    chunk of rows ``[r0, r1)`` sees keys ``[kv_lo, r1)``: the causal limit of
+    its last row, from the block's first attended key on (every key before
+    it is masked, so its logit is ``-inf`` and its weight 0).  Softmax is
+    per row, so chunking rows changes nothing; dK / dV are summed over the
+    chunks and blocks that see a key.  Rows no block owns follow
+    ``reference.py:42-43`` (only their own key, logit 0).
+
+    Returns ``(out, lse, dq, dk, dv)`` (the gradients are ``None`` when
+    ``backward`` is false); shapes as in ``attn_forward`` / ``attn_backward``."""
+    q, k, v = (_np(t).astype(dtype) for t in (q, k, v))
+    B, Hq, T, D = q.shape
+    Hkv = k.shape[1]
+    G = Hq // Hkv
+    if scale is None:
+        scale = D ** -0.5
+    out = np.empty((B, T, Hq, D), dtype=dtype)
+    lse = np.empty((B, Hq, T), dtype=dtype)
+    if backward:
+        dout = _np(dout).astype(dtype)
+        dq = np.zeros_like(q)
+        dk = np.zeros_like(k)
+        dv = np.zeros_like(v)
+    for b, lay in enumerate(_per_row(layout, B)):
+        bounds, qpos, kpos, am, ab = _layout_arrays(lay)
+        qc, qs, kc, ks = _row_rope(rope, qpos, kpos, T)
+        qb = q[b]
+        kb = _expand(k[b:b + 1], G)[0]
+        vb = _expand(v[b:b + 1], G)[0]
+        q_rot = apply_cos_sin(qb, qc, qs)
+        if backward:
+            do_b = np.swapaxes(dout[b], 0, 1)  # (Hq, T, D)
+            dq_rot = np.zeros_like(qb)
+            dq_raw = np.zeros_like(qb)
+            dkb = np.zeros_like(kb)
+            dvb = np.zeros_like(vb)
+        cov = bounds[-1][1] if bounds else 0
+        # rows no block owns: p = 1 on the own key, so out = v, lse = 0, dV += dO
+        out[b, cov:] = np.swapaxes(vb[:, cov:], 0, 1)
+        lse[b, :, cov:] = 0
+        if backward:
+            dvb[:, cov:] += do_b[:, cov:]
+        for s, e, kst, ke in bounds:
+            attm = am[kst:ke]
+            absm = ab[kst:ke]
+            nz = np.flatnonzero(attm)
+            lo = int(nz[0]) if nz.size else e
+            if lo >= e:
+                out[b, s:e] = np.nan  # softmax over no key (the reference gives NaN as well)
+                lse[b, :, s:e] = -np.inf
+                continue
+            k_rot = apply_cos_sin(kb[:, lo:e, :], kc[kst + lo:ke], ks[kst + lo:ke])  # keys [lo, e)
+            has_abs = bool(absm[lo:e].any())
+            if backward:
+                dk_rot = np.zeros_like(k_rot)
+            for r0 in range(s, e, chunk):
+                r1 = min(r0 + chunk, e)
+                n = r1 - lo
+                kr = k_rot[:, :n]
+                krt = np.swapaxes(kr, -1, -2)
+                w = q_rot[:, r0:r1] @ krt
+                if has_abs:
+                    w = w + ((qb[:, r0:r1] - q_rot[:, r0:r1]) @ krt) * absm[lo:r1]
+                rows = np.arange(r0, r1)[:, None]
+                cols = np.arange(lo, r1)[None, :]
+                ok = attm[lo:r1][None, :] & (cols <= rows)
+                w = np.where(ok, w, -np.inf) * scale
+                p, l = _softmax(w)
+                out[b, r0:r1] = np.swapaxes(p @ vb[:, lo:r1], 0, 1)
+                lse[b, :, r0:r1] = l
+                if not backward:
+                    continue
+                do = do_b[:, r0:r1]
+                dvb[:, lo:r1] += np.swapaxes(p, -1, -2) @ do
+                dp = do @ np.swapaxes(vb[:, lo:r1], -1, -2)
+                ds = p * (dp - np.sum(dp * p, axis=-1, keepdims=True))
+                dl = np.where(ok, ds * scale, 0.0)
+                if has_abs:
+                    a_ = absm[lo:r1].astype(dtype)
+                    g_rot, g_abs = dl * (1.0 - a_), dl * a_
+                    dq_raw[:, r0:r1] += g_abs @ kr
+                    dk_rot[:, :n] += np.swapaxes(g_abs, -1, -2) @ qb[:, r0:r1]
+                else:
+                    g_rot = dl
+                dq_rot[:, r0:r1] += g_rot @ kr
+                dk_rot[:, :n] += np.swapaxes(g_rot, -1, -2) @ q_rot[:, r0:r1]
+            if backward:
+                dkb[:, lo:e] += apply_cos_sin_T(dk_rot, kc[kst + lo:ke], ks[kst + lo:ke])
+        if backward:
+            dq[b] = apply_cos_sin_T(dq_rot, qc, qs) + dq_raw
+            dk[b] = dkb.reshape(Hkv, G, T, D).sum(axis=1)
+            dv[b] = dvb.reshape(Hkv, G, T, D).sum(axis=1)
+    if not backward:
+        return out, lse, None, None, None
+    return out, lse, dq, dk, dv
 
 
 # ---------------------------------------------------------------------------

@@ -104,3 +104,30 @@ def test_profile_entry_points_without_gpu():
     assert list(cnt) == [0] * n and list(ms) == [0.0] * n
     header = open(HEADER).read()
     assert f"AI_PROF_KINDS = {n}" in header
+
+
+def test_selftest_wait_rejects_bad_arguments():
+    L = _lib.lib()
+    assert L.ai_attn_selftest_wait(None, 1000, None) == 1
+    assert L.ai_attn_selftest_wait(ctypes.c_void_p(256), 0, None) == 2
+    assert L.ai_attn_selftest_wait(ctypes.c_void_p(256), 3_000_000_000, None) == 2
+
+
+@pytest.mark.gpu
+def test_bounded_wait_expiry_reports_timeout(cuda_device):
+    """A bounded mbarrier wait that nothing completes gives up after its
+    limit and records AI_ERR_DEV_TIMEOUT (-1) in the status word; reading the
+    word back clears it, and the context stays usable."""
+    import torch
+
+    from autoindexer_b200.attention import read_status, status_word
+
+    L = _lib.lib()
+    w = status_word(cuda_device)
+    assert read_status(cuda_device) == 0
+    stream = ctypes.c_void_p(torch.cuda.current_stream(cuda_device).cuda_stream)
+    assert L.ai_attn_selftest_wait(ctypes.c_void_p(w.data_ptr()), 2_000_000, stream) == 0
+    assert read_status(cuda_device) == -1
+    assert read_status(cuda_device) == 0
+    x = torch.ones(1024, device=cuda_device)
+    assert float(x.sum()) == 1024.0

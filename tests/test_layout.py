@@ -124,3 +124,42 @@ def test_all_rows_owned_flag():
     rows.append(document_blocks([T // 2, T - T // 2], position_ids=np.arange(T)))
     docs = _compile(rows, 1, T, 32, torch.float32, mod)
     assert docs.all_rows_owned and docs.c_struct().all_rows_owned == 1
+
+
+def test_external_mask_check():
+    """An external 4-D mask is accepted when it removes nothing inside the
+    causal triangle (bool or additive), rejected otherwise, and rechecked
+    after an in-place change."""
+    from autoindexer_b200.attention import _check_mask_is_causal
+
+    T = 260
+    tri = torch.tril(torch.ones(T, T, dtype=torch.bool))
+    m = tri[None, None].expand(2, 1, T, T)
+    _check_mask_is_causal(m, T)
+    _check_mask_is_causal(m, T)  # cached for this tensor and version
+    f = torch.zeros(2, 1, T, T).masked_fill_(~tri, float("-inf"))
+    _check_mask_is_causal(f, T)
+    f[1, 0, 200, 150] = float("-inf")  # in place: a new version, checked again
+    with pytest.raises(NotImplementedError):
+        _check_mask_is_causal(f, T)
+    b = tri[None, None].repeat(1, 1, 1, 1)
+    b[0, 0, 7, 3] = False
+    with pytest.raises(NotImplementedError):
+        _check_mask_is_causal(b, T)
+    with pytest.raises(NotImplementedError):
+        _check_mask_is_causal(torch.ones(1, 1, T, T + 1, dtype=torch.bool), T)
+
+
+def test_blocks_from_concat_inverts_concat():
+    """Rebuilding a list from the concat()-ed arrays of the +E chain (built by
+    the reference's own sampler) gives the same arrays back."""
+    from autoindexer_b200 import blocks_from_concat
+
+    g = load_golden("chain_e")
+    lay = blocks_from_concat(g["boundary_indices"], g["query_pos_ids"], g["concat_key_pos_ids"],
+                             g["concat_attn_masks"], g["concat_abs_pos_masks"])
+    assert np.array_equal(np.asarray(lay.boundary_indices), g["boundary_indices"])
+    assert np.array_equal(lay.query_pos_ids.numpy(), g["query_pos_ids"])
+    assert np.array_equal(lay.concat_key_pos_ids.numpy(), g["concat_key_pos_ids"])
+    assert np.array_equal(lay.concat_attn_masks.numpy(), g["concat_attn_masks"])
+    assert np.array_equal(lay.concat_abs_pos_masks.numpy(), g["concat_abs_pos_masks"])

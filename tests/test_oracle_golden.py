@@ -79,3 +79,19 @@ def test_count_pairs_matches_logits():
     q, k, _, _ = golden_inputs(g)
     w = O.attn_logits(q[0], np.repeat(k[0], 2, axis=0), lay, rope, 1.0)
     assert int(np.isfinite(w[0]).sum()) == O.count_pairs(lay, q.shape[2])
+
+
+@pytest.mark.parametrize("name", ["op0_d32", "op5_d32", "op9_d32", "sec3", "chain_e"])
+def test_chunked_oracle_matches_dense_oracle(name):
+    """The query-chunked restatement (used at sizes where the dense one's
+    (H, T, T) arrays do not fit) gives the dense oracle's results; chunks of
+    a few rows put chunk edges inside every block."""
+    g = load_golden(name)
+    lay = ArrayLayout.from_golden(g)
+    _, rope = golden_rope(g)
+    q, k, v, dout = golden_inputs(g)
+    want = O.attn_forward(q, k, v, lay, rope) + O.attn_backward(q, k, v, dout, lay, rope)
+    got = O.attn_chunked(q, k, v, dout, lay, rope, chunk=37 if name == "chain_e" else 5)
+    for label, a, b in zip(("out", "lse", "dq", "dk", "dv"), got, want):
+        np.testing.assert_allclose(a, b, rtol=1e-10, atol=1e-10, err_msg=f"{name}:{label}")
+    np.testing.assert_allclose(got[0], g["out"], rtol=2e-5, atol=2e-5)

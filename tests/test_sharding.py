@@ -46,17 +46,26 @@ def _case(T=96, Hq=8, Hkv=2, D=32, seed=7):
 
 
 def _oracle_local(rope):
+    """Local forward / backward of one rank's heads by the oracle, writing
+    into the buffer views the sharded path hands over."""
     from oracle import attn_oracle as O
 
-    def fwd(q, k, v, rows, scale):
+    def fwd(q, k, v, rows, scale, out_bhtd=None):
         out, _ = O.attn_forward(q.detach().numpy(), k.detach().numpy(), v.detach().numpy(), rows, rope, scale)
-        return torch.from_numpy(out), (q, k, v, rows, scale)
+        out = torch.from_numpy(out)
+        if out_bhtd is not None:
+            out_bhtd.copy_(out.permute(0, 2, 1, 3))
+        return out, (q, k, v, rows, scale)
 
-    def bwd(state, dout):
+    def bwd(state, dout, grads=None):
         q, k, v, rows, scale = state
-        grads = O.attn_backward(q.detach().numpy(), k.detach().numpy(), v.detach().numpy(), dout.numpy(), rows,
-                                rope, scale)
-        return tuple(torch.from_numpy(x) for x in grads)
+        res = O.attn_backward(q.detach().numpy(), k.detach().numpy(), v.detach().numpy(), dout.numpy(), rows,
+                              rope, scale)
+        res = tuple(torch.from_numpy(x) for x in res)
+        if grads is not None:
+            for g, x in zip(grads, res):
+                g.copy_(x)
+        return res
 
     return fwd, bwd
 
