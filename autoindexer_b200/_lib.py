@@ -32,7 +32,7 @@ LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_ai_attn.so
 DTYPE_BF16, DTYPE_F16, DTYPE_F32 = 0, 1, 2
 # AiProfKind, in order.
 PROF_KINDS = ("prerot", "fwd", "fwd_fill", "delta", "dq", "dkdv", "bwd_fill", "simt", "decode")
-ABI_VERSION = 6
+ABI_VERSION = 7
 
 # Every function include/ai_attn.h declares.
 EXPORTED_SYMBOLS = (
@@ -89,6 +89,7 @@ class AiAttnLayout(ctypes.Structure):
         ("n_kv_items", ctypes.c_int32),
         ("n_kv_abs_items", ctypes.c_int32),
         ("all_rows_owned", ctypes.c_int32),
+        ("n_fwd_short_items", ctypes.c_int32),
     ]
 
 

@@ -3,7 +3,8 @@
 // head_dim 128.  Two kernels, no atomics (deterministic):
 //
 // dq_kernel  (Q-stationary; one CTA = one forward work item x one query head,
-//             thread = query row = TMEM lane):
+//             or two / four heads of a GQA group for items of at most 64 / 32
+//             rows, thread = query row = TMEM lane):
 //   for each 64-key tile of the block's key range: S = Qrot.Krot^T (and
 //   S_abs = Q.Krot^T on abs blocks) and dP = dO.V^T into TMEM; P =
 //   exp(S*scale - lse); dS = P (dP - delta) scale; dS goes to smem split by key
@@ -16,7 +17,8 @@
 //   V is loaded once; for every block that sees these keys the raw K tile is
 //   re-loaded and rotated by the keys' positions *in that block*; then for
 //   every 64-row query tile of the block and every query head of the GQA
-//   group: S^T = Krot.Qrot^T (abs keys take Krot.Q^T: a per-thread choice,
+//   group (or once for all G heads when the block has at most 64 / G rows,
+//   their rows packed side by side): S^T = Krot.Qrot^T (abs keys take Krot.Q^T: a per-thread choice,
 //   since abs is a property of the key), dP^T = V.dO^T, P^T, dS^T; dV += P^T.dO
 //   and dKrot += dS^T.Qrot (+ dS^T_abs.Q) in TMEM.  When a block is done its
 //   dKrot is rotated back by the block's key positions and added to the dK
@@ -128,10 +130,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int32_t* item = L.fwd_items + 4 * (int64_t)blockIdx.x;
   const Block blk = load_block(L.blocks, item[0]);
   const int q0 = item[1], q1 = item[2];
-  const int h = blockIdx.y, G = f.num_q_heads / f.num_kv_heads, hk = h / G, b = blk.row;
+  // A short item packs P heads of the group into the tile (as the forward).
+  const int G = f.num_q_heads / f.num_kv_heads, P = pack_heads(q1 - q0, G), slot = BM / P;
+  if ((int)blockIdx.y * P >= f.num_q_heads) return;
+  const int h = (int)blockIdx.y * P + tid / slot, hk = ((int)blockIdx.y * P) / G, b = blk.row;
   const bool has_abs = (blk.flags & AI_BLOCKF_ABS) != 0;
   const int kv_hi = min(blk.e, q1);
-  const int i = q0 + tid;
+  const int i = q0 + tid % slot;
 
   if (tid == 0) {
     ptx::mbar_init(bar_tma, 1);
@@ -195,9 +200,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const float sl2 = f.scale * kLog2e;
   uint32_t ph_tma = 0, ph_mma = 0;
   int n_tiles = 0;
-  bool aborted = false;
+  bool aborted = false, dqa_started = false;
 
   for (int k0 = blk.kv_lo; k0 < kv_hi; k0 += BN) {
+    // Only a tile that holds one of the block's abs keys needs S_abs and dQabs.
+    const bool tabs = blk.abs_in(k0, min(k0 + BN, kv_hi));
     if (tid == 0) {
       ptx::fence_proxy_async_smem();
       ptx::mbar_arrive_expect_tx(bar_tma, 2 * 16384);
@@ -245,7 +252,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     idesc_s, kk > 0);
         ptx::mma_ss(tmem + C_DP, ptx::sdesc_sw128(sbase + DO + ao, 16, 1024),
                     ptx::sdesc_sw128(sbase + VV + bo, 16, 1024), idesc_s, kk > 0);
-        if (has_abs)
+        if (tabs)
           ptx::mma_ss(tmem + C_SA, ptx::sdesc_sw128(sbase + QA + ao, 16, 1024),
                       ptx::sdesc_sw128(sbase + KR + bo, 16, 1024), idesc_s, kk > 0);
       }
@@ -262,14 +269,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t rs[32], rp[32], ra[32];
       ptx::tmem_ld32(tmem + lane_base + C_S + 32 * cc, rs);
       ptx::tmem_ld32(tmem + lane_base + C_DP + 32 * cc, rp);
-      if (has_abs) ptx::tmem_ld32(tmem + lane_base + C_SA + 32 * cc, ra);
+      if (tabs) ptx::tmem_ld32(tmem + lane_base + C_SA + 32 * cc, ra);
       ptx::tmem_wait_ld();
       float dsr[32], dsa[32];
 #pragma unroll
       for (int x = 0; x < 32; ++x) {
         const int c = 32 * cc + x;
         const uint32_t info = s_info[c];
-        const bool is_abs = has_abs && (info & AI_KEY_ABS);
+        const bool is_abs = tabs && (info & AI_KEY_ABS);
         const float s = is_abs ? __uint_as_float(ra[x]) : __uint_as_float(rs[x]);
         const bool valid = (info & AI_KEY_ATTN) && (k0 + c <= i) && (i < q1);
         const float p = valid ? exp2f(s * sl2 - lse2) : 0.f;
@@ -283,7 +290,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int x = 0; x < 8; ++x) v[x] = dsr[8 * c8 + x];
         *reinterpret_cast<uint4*>(sm + DS + chunk_off<BM>(tid, 4 * cc + c8)) = pack8(v);
-        if (has_abs) {
+        if (tabs) {
 #pragma unroll
           for (int x = 0; x < 8; ++x) v[x] = dsa[8 * c8 + x];
           *reinterpret_cast<uint4*>(sm + DSA + chunk_off<BM>(tid, 4 * cc + c8)) = pack8(v);
@@ -303,9 +310,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t acc = (n_tiles > 0 || kk > 0) ? 1u : 0u;
         ptx::mma_ss(tmem + C_DQR, ptx::sdesc_sw128(sbase + DS + ao, 16, 1024),
                     ptx::sdesc_sw128(sbase + KR + bo, 8192, 1024), idesc_dq, acc);
-        if (has_abs)
+        if (tabs)
           ptx::mma_ss(tmem + C_DQA, ptx::sdesc_sw128(sbase + DSA + ao, 16, 1024),
-                      ptx::sdesc_sw128(sbase + KR + bo, 8192, 1024), idesc_dq, acc);
+                      ptx::sdesc_sw128(sbase + KR + bo, 8192, 1024), idesc_dq, (dqa_started || kk > 0) ? 1u : 0u);
       }
       ptx::mma_commit(bar_mma);
     }
@@ -314,6 +321,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (*s_abort) { aborted = true; break; }
     ptx::tc_fence_after();
     ++n_tiles;
+    dqa_started = dqa_started || tabs;
   }
 
   // dQ = R(qpos)^T dQrot + dQabs.
@@ -328,7 +336,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (n_tiles > 0) {
         ptx::tmem_ld32(tmem + lane_base + C_DQR + 32 * half, g1);
         ptx::tmem_ld32(tmem + lane_base + C_DQR + 64 + 32 * half, g2);
-        if (has_abs) {
+        if (dqa_started) {
           ptx::tmem_ld32(tmem + lane_base + C_DQA + 32 * half, a1);
           ptx::tmem_ld32(tmem + lane_base + C_DQA + 64 + 32 * half, a2);
         }
@@ -344,7 +352,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const float v1 = __uint_as_float(g1[x]), v2 = __uint_as_float(g2[x]);
           y1 = v1 * c + v2 * s;
           y2 = v2 * c - v1 * s;
-          if (has_abs) {
+          if (dqa_started) {
             y1 += __uint_as_float(a1[x]);
             y2 += __uint_as_float(a2[x]);
           }
@@ -396,7 +404,8 @@ constexpr uint32_t C_ST = 0, C_DPT = 64, C_DV = 128, C_DKR = 256, C_DK = 384;
 __global__ void __launch_bounds__(kThreads, 1)
     dkdv_kernel(const AiAttnBwdArgs a, const float* __restrict__ delta, const __grid_constant__ CUtensorMap tm_k,
                 const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_q,
-                const __grid_constant__ CUtensorMap tm_do) {
+                const __grid_constant__ CUtensorMap tm_do, const __grid_constant__ CUtensorMap tm_qp,
+                const __grid_constant__ CUtensorMap tm_dop, const int abs_only) {
   using namespace kv;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = tile::align1024(smem_raw);
@@ -458,6 +467,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int qs = max(blk.s, j0);
     if (qs >= blk.e) continue;
     const bool has_abs = (blk.flags & AI_BLOCKF_ABS) != 0;
+    if (abs_only && !blk.abs_in(j0, j1)) continue;
     const int kmax = min(j1, blk.e);
 
     // Raw K tile, rotated in place by this block's key positions.
@@ -493,25 +503,39 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
 
     bool dkr_started = false;
+    // A block of at most 64 / G rows packs the rows of all G heads of the
+    // group into one step: column c is row q0 + c % (64 / G) of head
+    // hk * G + c / (64 / G) (tm_qp / tm_dop have boxes of 64 / G rows).
+    const int P = ((G == 2 || G == 4 || G == 8) && blk.e - qs <= BQ / G) ? G : 1, sr = BQ / P;
     for (int q0 = qs; q0 < blk.e && !aborted; q0 += BQ) {
       const int q1 = min(q0 + BQ, blk.e);
-      for (int g = 0; g < G; ++g) {
+      for (int g = 0; g < G; g += P) {
         const int h = hk * G + g;
         const uint32_t qdst = has_abs ? QA : QR;
         if (tid == 0) {
           ptx::fence_proxy_async_smem();
           ptx::mbar_arrive_expect_tx(bar_q, 4 * 8192);
-          ptx::tma_load_4d(sbase + qdst, &tm_q, bar_q, 0, q0, h, b);
-          ptx::tma_load_4d(sbase + qdst + 8192, &tm_q, bar_q, 64, q0, h, b);
-          ptx::tma_load_4d(sbase + DO, &tm_do, bar_q, 0, q0, h, b);
-          ptx::tma_load_4d(sbase + DO + 8192, &tm_do, bar_q, 64, q0, h, b);
+          if (P == 1) {
+            ptx::tma_load_4d(sbase + qdst, &tm_q, bar_q, 0, q0, h, b);
+            ptx::tma_load_4d(sbase + qdst + 8192, &tm_q, bar_q, 64, q0, h, b);
+            ptx::tma_load_4d(sbase + DO, &tm_do, bar_q, 0, q0, h, b);
+            ptx::tma_load_4d(sbase + DO + 8192, &tm_do, bar_q, 64, q0, h, b);
+          } else {
+            for (int x = 0; x < P; ++x) {
+              const uint32_t ro = (uint32_t)(x * sr) * 128u;
+              ptx::tma_load_4d(sbase + qdst + ro, &tm_qp, bar_q, 0, q0, hk * G + x, b);
+              ptx::tma_load_4d(sbase + qdst + 8192 + ro, &tm_qp, bar_q, 64, q0, hk * G + x, b);
+              ptx::tma_load_4d(sbase + DO + ro, &tm_dop, bar_q, 0, q0, hk * G + x, b);
+              ptx::tma_load_4d(sbase + DO + 8192 + ro, &tm_dop, bar_q, 64, q0, hk * G + x, b);
+            }
+          }
         }
         if (tid < BQ) {
-          const int r = q0 + tid;
+          const int r = q0 + tid % sr, hc = P == 1 ? h : hk * G + tid / sr;
           float l2 = CUDART_INF_F, dlt = 0.f;
           int qp = 0;
           if (r < q1) {
-            const int64_t idx = ((int64_t)b * f.num_q_heads + h) * f.seq_len + r;
+            const int64_t idx = ((int64_t)b * f.num_q_heads + hc) * f.seq_len + r;
             l2 = lse_log2(f.lse[idx]);
             dlt = delta[idx];
             qp = clamp_row(L.q_pos[(int64_t)b * f.seq_len + r], L.n_pos, f.status);
@@ -607,7 +631,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           float pv[32], dsv[32];
 #pragma unroll
           for (int x = 0; x < 32; ++x) {
-            const int c = 32 * cc + x, r = q0 + c;
+            const int c = 32 * cc + x, r = q0 + c % sr;
             const bool valid = key_ok && (j <= r) && (r < q1) && (j < kmax);
             const float p = valid ? exp2f(s[c] * sl2 - s_lse[c]) : 0.f;
             pv[x] = p;
@@ -724,6 +748,25 @@ __global__ void __launch_bounds__(kThreads, 1)
         fv[x] = dv_started ? __uint_as_float(rv[x]) : 0.f;
       }
       if (j < j1) {
+        if (abs_only) {
+          // The warp-specialised pass already wrote the other blocks' part
+          // of these rows (stream order): add to it.
+#pragma unroll
+          for (int c8 = 0; c8 < 4; ++c8) {
+            const uint4 ok_ = *reinterpret_cast<const uint4*>(dKrow + 32 * cc + 8 * c8);
+            const uint4 ov_ = *reinterpret_cast<const uint4*>(dVrow + 32 * cc + 8 * c8);
+            const __nv_bfloat162* pk2 = reinterpret_cast<const __nv_bfloat162*>(&ok_);
+            const __nv_bfloat162* pv2 = reinterpret_cast<const __nv_bfloat162*>(&ov_);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const float2 k2 = __bfloat1622float2(pk2[u]), v2 = __bfloat1622float2(pv2[u]);
+              fk[8 * c8 + 2 * u] += k2.x;
+              fk[8 * c8 + 2 * u + 1] += k2.y;
+              fv[8 * c8 + 2 * u] += v2.x;
+              fv[8 * c8 + 2 * u + 1] += v2.y;
+            }
+          }
+        }
         store_bf16_row32(dKrow + 32 * cc, fk);
         store_bf16_row32(dVrow + 32 * cc, fv);
       }
@@ -774,23 +817,41 @@ constexpr size_t kSmem = TOTAL + 1024;
 static_assert(kSmem <= 227 * 1024, "shared memory budget");
 constexpr long long kWait = 1000000000LL;
 
-// One work unit: rows [q0, q1) of a block x query heads 2 hp, 2 hp + 1.
+// One work unit: rows [q0, q1) of a block x four query heads h0 .. h0 + 3 of
+// one GQA group (pk = 2: an item of at most 64 rows, tile t holds heads
+// h0 + 2t in lanes 0-63 and h0 + 2t + 1 in lanes 64-127) or x two query heads
+// h0, h0 + 1 (pk = 1: tile t holds head h0 + t), as in the persistent forward.
 struct Unit {
   Block blk;
-  int q0, q1, hp, hk, kv_lo, kv_hi, n;
+  int q0, q1, h0, pk, hk, kv_lo, kv_hi, n;
   bool masked, k_pre;
 };
 
-__device__ __forceinline__ Unit load_unit(const AiAttnFwdArgs& f, int u, int prerot) {
+__device__ __forceinline__ int unit_head(const Unit& w, int t, int r) {
+  return w.pk == 2 ? w.h0 + 2 * t + (r >> 6) : w.h0 + t;
+}
+__device__ __forceinline__ int unit_row(const Unit& w, int r) { return w.q0 + (w.pk == 2 ? (r & 63) : r); }
+
+__device__ __forceinline__ Unit load_unit(const AiAttnFwdArgs& f, int u, int prerot, int n_pack_units) {
   const AiAttnLayout& L = f.layout;
-  const int hpairs = f.num_q_heads / 2, G = f.num_q_heads / f.num_kv_heads;
-  const int32_t* item = L.fwd_items + 4 * (int64_t)(L.n_fwd_abs_items + u / hpairs);
+  const int hpairs = f.num_q_heads / 2, hquads = f.num_q_heads / 4, G = f.num_q_heads / f.num_kv_heads;
+  int it;
   Unit w;
+  if (u < n_pack_units) {
+    it = L.n_fwd_abs_items + u / hquads;
+    w.h0 = 4 * (u % hquads);
+    w.pk = 2;
+  } else {
+    const int v = u - n_pack_units;
+    it = L.n_fwd_abs_items + (n_pack_units > 0 ? L.n_fwd_short_items : 0) + v / hpairs;
+    w.h0 = 2 * (v % hpairs);
+    w.pk = 1;
+  }
+  const int32_t* item = L.fwd_items + 4 * (int64_t)it;
   w.blk = load_block(L.blocks, item[0]);
   w.q0 = item[1];
   w.q1 = item[2];
-  w.hp = u % hpairs;
-  w.hk = (2 * w.hp) / G;
+  w.hk = w.h0 / G;
   w.kv_lo = w.blk.kv_lo;
   w.kv_hi = min(w.blk.e, w.q1);
   w.n = w.kv_hi > w.kv_lo ? (w.kv_hi - w.kv_lo + BN - 1) / BN : 0;
@@ -824,7 +885,8 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
     dq_pers_kernel(const AiAttnBwdArgs a, const float* __restrict__ delta, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_qr,
                    const __grid_constant__ CUtensorMap tm_do, const __grid_constant__ CUtensorMap tm_kr,
-                   const int prerot, const int n_units) {
+                   const __grid_constant__ CUtensorMap tm_qr64, const __grid_constant__ CUtensorMap tm_do64,
+                   const int prerot, const int n_units, const int n_pack_units) {
   using namespace dqw;
   // The dK/dV kernel launched after this one reads nothing it writes: let it
   // start as soon as every CTA here has started, so its CTAs take each SM as
@@ -886,8 +948,8 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
     const float2 sl2x2 = make_float2(sl2, sl2), scalex2 = make_float2(scale, scale);
     int g = 0, k = 0, ko = 0;  // ko: units with key tiles so far (DQ_DONE phases)
     for (int u = snake_unit(k); u < n_units && !*s_abort; u = snake_unit(++k)) {
-      const Unit w = load_unit(f, u, prerot);
-      const int i = w.q0 + r, h = 2 * w.hp + t, b = w.blk.row, q1 = w.q1;
+      const Unit w = load_unit(f, u, prerot, n_pack_units);
+      const int i = unit_row(w, r), h = unit_head(w, t, r), b = w.blk.row, q1 = w.q1;
       int qrow = 0;
       float lse2 = 0.f, dl = 0.f;
       if (i < q1) {
@@ -1062,24 +1124,38 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
         ptx::prefetch_tmap(&tm_kr);
         ptx::prefetch_tmap(&tm_qr);
         ptx::prefetch_tmap(&tm_do);
+        ptx::prefetch_tmap(&tm_qr64);
+        ptx::prefetch_tmap(&tm_do64);
       }
       int g = 0, k = 0;
       bool ok = true;
       for (int u = snake_unit(k); ok && u < n_units; u = snake_unit(++k)) {
-        const Unit w = load_unit(f, u, prerot);
+        const Unit w = load_unit(f, u, prerot, n_pack_units);
         const int b = w.blk.row;
         if (prerot) {
           if (k > 0 && !wait(Q_EMPTY, (k - 1) & 1)) break;
-          const int h0 = 2 * w.hp;
+          const int h0 = w.h0;
           ptx::mbar_arrive_expect_tx(bar(Q_READY), 4 * 32768);
-          ptx::tma_load_4d(sbase + Q0, &tm_qr, bar(Q_READY), 0, w.q0, h0, b);
-          ptx::tma_load_4d(sbase + Q0 + 16384, &tm_qr, bar(Q_READY), 64, w.q0, h0, b);
-          ptx::tma_load_4d(sbase + Q1, &tm_qr, bar(Q_READY), 0, w.q0, h0 + 1, b);
-          ptx::tma_load_4d(sbase + Q1 + 16384, &tm_qr, bar(Q_READY), 64, w.q0, h0 + 1, b);
-          ptx::tma_load_4d(sbase + DO0, &tm_do, bar(Q_READY), 0, w.q0, h0, b);
-          ptx::tma_load_4d(sbase + DO0 + 16384, &tm_do, bar(Q_READY), 64, w.q0, h0, b);
-          ptx::tma_load_4d(sbase + DO1, &tm_do, bar(Q_READY), 0, w.q0, h0 + 1, b);
-          ptx::tma_load_4d(sbase + DO1 + 16384, &tm_do, bar(Q_READY), 64, w.q0, h0 + 1, b);
+          if (w.pk == 1) {
+            ptx::tma_load_4d(sbase + Q0, &tm_qr, bar(Q_READY), 0, w.q0, h0, b);
+            ptx::tma_load_4d(sbase + Q0 + 16384, &tm_qr, bar(Q_READY), 64, w.q0, h0, b);
+            ptx::tma_load_4d(sbase + Q1, &tm_qr, bar(Q_READY), 0, w.q0, h0 + 1, b);
+            ptx::tma_load_4d(sbase + Q1 + 16384, &tm_qr, bar(Q_READY), 64, w.q0, h0 + 1, b);
+            ptx::tma_load_4d(sbase + DO0, &tm_do, bar(Q_READY), 0, w.q0, h0, b);
+            ptx::tma_load_4d(sbase + DO0 + 16384, &tm_do, bar(Q_READY), 64, w.q0, h0, b);
+            ptx::tma_load_4d(sbase + DO1, &tm_do, bar(Q_READY), 0, w.q0, h0 + 1, b);
+            ptx::tma_load_4d(sbase + DO1 + 16384, &tm_do, bar(Q_READY), 64, w.q0, h0 + 1, b);
+          } else {
+            // Four heads, 64 rows each: head h0 + 2t + x into rows [64x, 64x + 64) of tile t.
+#pragma unroll
+            for (int hh = 0; hh < 4; ++hh) {
+              const uint32_t off = (uint32_t)(hh >> 1) * 32768u + (uint32_t)(hh & 1) * 8192u;
+              ptx::tma_load_4d(sbase + Q0 + off, &tm_qr64, bar(Q_READY), 0, w.q0, h0 + hh, b);
+              ptx::tma_load_4d(sbase + Q0 + off + 16384, &tm_qr64, bar(Q_READY), 64, w.q0, h0 + hh, b);
+              ptx::tma_load_4d(sbase + DO0 + off, &tm_do64, bar(Q_READY), 0, w.q0, h0 + hh, b);
+              ptx::tma_load_4d(sbase + DO0 + off + 16384, &tm_do64, bar(Q_READY), 64, w.q0, h0 + hh, b);
+            }
+          }
         }
         const CUtensorMap* mk = w.k_pre ? &tm_kr : &tm_k;
         for (int j = 0; j < w.n; ++j, ++g) {
@@ -1144,7 +1220,7 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
     int g = 0, k = 0;
     bool ok = true;
     for (int u = snake_unit(k); ok && u < n_units; u = snake_unit(++k)) {
-      const Unit w = load_unit(f, u, prerot);
+      const Unit w = load_unit(f, u, prerot, n_pack_units);
       if (!wait_u(Q_READY, k & 1)) break;
       if (w.n == 0) {
         ptx::mma_commit_w(bar(Q_EMPTY));
@@ -1193,7 +1269,7 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
     const int row = tid - 320;  // 0..63: key row of the tile
     int g = 0;
     for (int kr = 0, u = snake_unit(0); u < n_units && !*s_abort; u = snake_unit(++kr)) {
-      const Unit w = load_unit(f, u, prerot);
+      const Unit w = load_unit(f, u, prerot, n_pack_units);
       for (int j = 0; j < w.n; ++j, ++g) {
         const int slot = g % kKS, key = w.kv_lo + j * BN + row;
         uint32_t info = 0;
@@ -1292,11 +1368,16 @@ constexpr uint32_t C_BUF = 0, C_DV = 256, C_DKR = 384;
 constexpr long long kWait = 1000000000LL;
 }  // namespace kvw
 
-// Iterates the blocks of row b that see keys [j0, j1) (same order in every role).
+// Iterates the blocks of row b that see keys [j0, j1) (same order in every
+// role); with skip_abs, only the blocks with no abs key among [j0, j1)
+// (the others go to the abs pass, dkdv_kernel with abs_only, which adds its
+// part afterwards).
 struct BlockIter {
   const AiAttnLayout* L;
   int b, j0, j1, bi, end;
-  __device__ BlockIter(const AiAttnLayout* L_, int b_, int j0_, int j1_) : L(L_), b(b_), j0(j0_), j1(j1_) {
+  bool skip_abs;
+  __device__ BlockIter(const AiAttnLayout* L_, int b_, int j0_, int j1_, bool skip_abs_)
+      : L(L_), b(b_), j0(j0_), j1(j1_), skip_abs(skip_abs_) {
     bi = L->row_blocks[b] - 1;
     end = L->row_blocks[b + 1];
   }
@@ -1304,6 +1385,7 @@ struct BlockIter {
     while (++bi < end) {
       blk = load_block(L->blocks, bi);
       if (blk.e <= j0 || blk.kv_lo >= j1 || max(blk.s, j0) >= blk.e) continue;
+      if (skip_abs && blk.abs_in(j0, j1)) continue;
       return true;
     }
     return false;
@@ -1314,7 +1396,7 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
     dkdv_ws_kernel(const AiAttnBwdArgs a, const float* __restrict__ delta, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_q,
                    const __grid_constant__ CUtensorMap tm_do, const __grid_constant__ CUtensorMap tm_kr,
-                   const int prerot) {
+                   const int prerot, const int item_base, const int skip_abs) {
   using namespace kvw;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = tile::align1024(smem_raw);
@@ -1327,7 +1409,7 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
 
   const AiAttnFwdArgs& f = a.fwd;
   const AiAttnLayout& L = f.layout;
-  const int32_t* item = L.kv_items + 4 * (int64_t)(L.n_kv_abs_items + blockIdx.x);
+  const int32_t* item = L.kv_items + 4 * (int64_t)(item_base + blockIdx.x);
   const int b = item[0], j0 = item[1], j1 = item[2];
   const int hk = blockIdx.y, G = f.num_q_heads / f.num_kv_heads;
   const __half2* cs16 = static_cast<const __half2*>(L.rope_cs16);
@@ -1371,7 +1453,7 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
     const uint32_t lane_base = (uint32_t)((warp % 4) * 32) << 16;
     const float sl2 = f.scale * kLog2e, scale = f.scale;
     const float2 sl2x2 = make_float2(sl2, sl2), scalex2 = make_float2(scale, scale);
-    BlockIter it(&L, b, j0, j1);
+    BlockIter it(&L, b, j0, j1, skip_abs != 0);
     Block blk;
     int s = 0, nb = 0;
     bool any = false;
@@ -1509,7 +1591,7 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
       ptx::mbar_arrive_expect_tx(bar(V_FULL), 32768);
       ptx::tma_load_4d(sbase + V, &tm_v, bar(V_FULL), 0, j0, hk, b);
       ptx::tma_load_4d(sbase + V + 16384, &tm_v, bar(V_FULL), 64, j0, hk, b);
-      BlockIter it(&L, b, j0, j1);
+      BlockIter it(&L, b, j0, j1, skip_abs != 0);
       Block blk;
       int s = 0, nb = 0;
       bool ok = true;
@@ -1578,7 +1660,7 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
       }
     };
     bool ok = wait_u(V_FULL, 0);
-    BlockIter it(&L, b, j0, j1);
+    BlockIter it(&L, b, j0, j1, skip_abs != 0);
     Block blk;
     int s = 0, nb = 0, sl = 0;
     uint32_t ph = 0;
@@ -1639,7 +1721,7 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
   } else {
     // ------------------------------------------------------------ rotation (warps 18-19)
     const int rt = tid - 32 * (4 * kGroups + 2);  // 0..63: Q row rt, K rows rt and rt + 64
-    BlockIter it(&L, b, j0, j1);
+    BlockIter it(&L, b, j0, j1, skip_abs != 0);
     Block blk;
     int s = 0, nb = 0;
     while (!*s_abort && it.next(blk)) {
@@ -1787,17 +1869,24 @@ int sm100_bwd(const AiAttnBwdArgs& a, float* delta, void* rot, bool rot_ready, c
         e = cudaGetLastError();
       }
     }
+    CUtensorMap tqr64 = tk, tdo64 = tk;
+    if (!sm100_make_map(&tdo64, a.dout, f.batch, f.num_q_heads, f.seq_len, dq::BM / 2)) return AI_ERR_TMA;
+    if (pre && !sm100_make_map(&tqr64, qr, f.batch, f.num_q_heads, f.seq_len, dq::BM / 2)) return AI_ERR_TMA;
     if (e == cudaSuccess && n_pair > 0) {
-      // Persistent: one CTA per SM walks the (item, head pair) units.
-      const int n_units = n_pair * (f.num_q_heads / 2);
+      // Persistent: one CTA per SM walks the units: four-head units of the
+      // short items when a GQA group has a multiple of four query heads, then
+      // two-head units of the other items (the forward's order).
+      const int n_short = (G % 4 == 0) ? f.layout.n_fwd_short_items : 0;
+      const int n_pack_units = n_short * (f.num_q_heads / 4);
+      const int n_units = n_pack_units + (n_pair - n_short) * (f.num_q_heads / 2);
       int dev = 0, sms = 148;
       if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
       const int grid = n_units < sms ? n_units : sms;
       e = cudaFuncSetAttribute(dq_pers_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dqw::kSmem);
       if (e == cudaSuccess) {
         ProfScope ps(AI_PROF_DQ, st);
-        dq_pers_kernel<<<grid, dqw::kThreads, dqw::kSmem, st>>>(a, delta, tk, tv, tqr, tdo, tkr, pre ? 1 : 0,
-                                                                n_units);
+        dq_pers_kernel<<<grid, dqw::kThreads, dqw::kSmem, st>>>(a, delta, tk, tv, tqr, tdo, tkr, tqr64, tdo64,
+                                                                pre ? 1 : 0, n_units, n_pack_units);
         e = cudaGetLastError();
       }
     }
@@ -1814,18 +1903,12 @@ int sm100_bwd(const AiAttnBwdArgs& a, float* delta, void* rot, bool rot_ready, c
     if (pre && (!sm100_make_map(&tqr, qr, f.batch, f.num_q_heads, f.seq_len, kv::BQ) ||
                 !sm100_make_map(&tkr, kr, f.batch, f.num_kv_heads, f.seq_len, kv::BN)))
       return AI_ERR_TMA;
-    // Key tiles that a block with abs keys sees run on the one-warpgroup kernel,
-    // the rest on the warp-specialised one.
-    const int n_abs = f.layout.n_kv_abs_items, n_plain = f.layout.n_kv_items - n_abs;
-    if (n_abs > 0) {
-      e = cudaFuncSetAttribute(dkdv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kv::kSmem);
-      if (e == cudaSuccess) {
-        ProfScope ps(AI_PROF_DKDV, st);
-        dkdv_kernel<<<dim3(n_abs, f.num_kv_heads), kThreads, kv::kSmem, st>>>(a, delta, tk, tv, tq, tdo);
-        e = cudaGetLastError();
-      }
-    }
-    if (e == cudaSuccess && n_plain > 0) {
+    // Every key tile runs on the warp-specialised kernel for the blocks
+    // without abs keys; then the key tiles that blocks with abs keys see
+    // run on the one-warpgroup kernel for those blocks only, adding their
+    // part to the rows the first pass wrote (stream order, no atomics).
+    const int n_abs = f.layout.n_kv_abs_items, n_plain = f.layout.n_kv_items;
+    if (n_plain > 0) {
       e = cudaFuncSetAttribute(dkdv_ws_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kvw::kSmem);
       if (e == cudaSuccess) {
         ProfScope ps(AI_PROF_DKDV, st);
@@ -1844,8 +1927,24 @@ int sm100_bwd(const AiAttnBwdArgs& a, float* delta, void* rot, bool rot_ready, c
         cfg.attrs = attr;
         cfg.numAttrs = 1;
         e = cudaLaunchKernelEx(&cfg, dkdv_ws_kernel, a, (const float*)delta, tk, tv, pre ? tqr : tq, tdo, tkr,
-                               pre ? 1 : 0);
+                               pre ? 1 : 0, 0, n_abs > 0 ? 1 : 0);
         if (e == cudaSuccess) e = cudaGetLastError();
+      }
+    }
+    if (e == cudaSuccess && n_abs > 0) {
+      // Boxes of 64 / G rows for the steps that pack a group's heads.
+      const int Gk = f.num_q_heads / f.num_kv_heads;
+      CUtensorMap tqp = tq, tdop = tdo;
+      if ((Gk == 2 || Gk == 4 || Gk == 8) &&
+          (!sm100_make_map(&tqp, f.q, f.batch, f.num_q_heads, f.seq_len, kv::BQ / Gk) ||
+           !sm100_make_map(&tdop, a.dout, f.batch, f.num_q_heads, f.seq_len, kv::BQ / Gk)))
+        return AI_ERR_TMA;
+      e = cudaFuncSetAttribute(dkdv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kv::kSmem);
+      if (e == cudaSuccess) {
+        ProfScope ps(AI_PROF_DKDV, st);
+        dkdv_kernel<<<dim3(n_abs, f.num_kv_heads), kThreads, kv::kSmem, st>>>(a, delta, tk, tv, tq, tdo, tqp, tdop,
+                                                                               1);
+        e = cudaGetLastError();
       }
     }
   }

@@ -3,7 +3,9 @@
 // accumulate, head_dim 128.
 //
 // One CTA computes one work item (block b, query rows [q0, q1) with
-// q1 - q0 <= 128) for one query head:
+// q1 - q0 <= 128) for one query head, or for two or four heads of the same
+// GQA group when the item has at most 64 or 32 rows (their rows share the
+// 128 TMEM lanes and every K / V tile):
 //   * Q rows are loaded by their owning thread, rotated by the row's query
 //     position (fp32 cos/sin table) and written as bf16 into a 128-byte
 //     swizzled K-major tile; the unrotated rows go to a second tile when the
@@ -85,7 +87,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int32_t* item = L.fwd_items + 4 * (int64_t)blockIdx.x;
   const Block blk = load_block(L.blocks, item[0]);
   const int q0 = item[1], q1 = item[2];
-  const int h = blockIdx.y, G = a.num_q_heads / a.num_kv_heads, hk = h / G, b = blk.row;
+  // A short item packs P heads of the group into the tile: thread tid is row
+  // tid % (128 / P) of head blockIdx.y * P + tid / (128 / P); the CTAs of
+  // the heads that others took return at once.
+  const int G = a.num_q_heads / a.num_kv_heads, P = pack_heads(q1 - q0, G), slot = BM / P;
+  if ((int)blockIdx.y * P >= a.num_q_heads) return;
+  const int h = (int)blockIdx.y * P + tid / slot, hk = ((int)blockIdx.y * P) / G, b = blk.row;
   const bool has_abs = (blk.flags & AI_BLOCKF_ABS) != 0;
   const int kv_hi = min(blk.e, q1);
 
@@ -104,7 +111,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // Query row `tid`: rotated into Q, raw into QA (abs blocks only).
   {
-    const int i = q0 + tid;
+    const int i = q0 + tid % slot;
     const __nv_bfloat16* Qrow =
         static_cast<const __nv_bfloat16*>(a.q.ptr) + b * a.q.stride_b + h * a.q.stride_h + (int64_t)i * a.q.stride_t;
     int p = 0;
@@ -137,13 +144,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   const float sl2 = a.scale * kLog2e;
   constexpr uint32_t idesc_qk = ptx::idesc_bf16_f32(BM, BN, false, false);
   constexpr uint32_t idesc_pv = ptx::idesc_bf16_f32(BM, D, false, true);
-  const int i = q0 + tid;
+  const int i = q0 + tid % slot;
   float m_use = -CUDART_INF_F, l = 0.f;
   uint32_t ph_tma = 0, ph_mma = 0;
   int n_tiles = 0;
   bool aborted = false;
 
   for (int k0 = blk.kv_lo; k0 < kv_hi; k0 += BN) {
+    // Only a tile that holds one of the block's abs keys needs S_abs.
+    const bool tabs = blk.abs_in(k0, min(k0 + BN, kv_hi));
     // 1. K and V tiles by TMA.
     if (tid == 0) {
       ptx::fence_proxy_async_smem();
@@ -197,7 +206,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ptx::mma_ss(tmem + kColS, ptx::sdesc_sw128(sbase + Smem::Q + off, 16, 1024),
                     ptx::sdesc_sw128(sbase + Smem::K + off, 16, 1024), idesc_qk, kk > 0);
       }
-      if (has_abs) {
+      if (tabs) {
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (uint32_t)(kk >> 2) * kHalf + (uint32_t)(kk & 3) * 32u;
@@ -228,7 +237,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::tmem_wait_ld();
 #pragma unroll
       for (int x = 0; x < 32; ++x) s[32 * cc + x] = __uint_as_float(r[x]);
-      if (has_abs) {
+      if (tabs) {
         ptx::tmem_ld32(tmem + lane_base + kColSabs + 32 * cc, r);
         ptx::tmem_wait_ld();
 #pragma unroll
@@ -434,23 +443,44 @@ constexpr size_t kSmem = TOTAL + 1024;
 constexpr long long kWait = 1000000000LL;
 static_assert(kSmem <= 227 * 1024, "shared memory budget");
 
-// One work unit: rows [q0, q1) of a block x query heads 2 hp, 2 hp + 1.
+// One work unit: rows [q0, q1) of a block x four query heads h0 .. h0 + 3 of
+// one GQA group (pk = 2: an item of at most 64 rows, tile t holds heads
+// h0 + 2t in lanes 0-63 and h0 + 2t + 1 in lanes 64-127) or x two query heads
+// h0, h0 + 1 (pk = 1: tile t holds head h0 + t in all 128 lanes).  The
+// n_pack_units packed units come first (the short items follow the abs items
+// in the work list), then the two-head units of the remaining items.
 struct Unit {
   Block blk;
-  int q0, q1, hp, hk, kv_lo, kv_hi, n;
+  int q0, q1, h0, pk, hk, kv_lo, kv_hi, n;
   bool masked, k_pre;
 };
 
-__device__ __forceinline__ Unit load_unit(const AiAttnFwdArgs& a, int u, int prerot) {
+// Head and query row of TMEM lane r of tile t.
+__device__ __forceinline__ int unit_head(const Unit& w, int t, int r) {
+  return w.pk == 2 ? w.h0 + 2 * t + (r >> 6) : w.h0 + t;
+}
+__device__ __forceinline__ int unit_row(const Unit& w, int r) { return w.q0 + (w.pk == 2 ? (r & 63) : r); }
+
+__device__ __forceinline__ Unit load_unit(const AiAttnFwdArgs& a, int u, int prerot, int n_pack_units) {
   const AiAttnLayout& L = a.layout;
-  const int hpairs = a.num_q_heads / 2, G = a.num_q_heads / a.num_kv_heads;
-  const int32_t* item = L.fwd_items + 4 * (int64_t)(L.n_fwd_abs_items + u / hpairs);
+  const int hpairs = a.num_q_heads / 2, hquads = a.num_q_heads / 4, G = a.num_q_heads / a.num_kv_heads;
+  int it;
   Unit w;
+  if (u < n_pack_units) {
+    it = L.n_fwd_abs_items + u / hquads;
+    w.h0 = 4 * (u % hquads);
+    w.pk = 2;
+  } else {
+    const int v = u - n_pack_units;
+    it = L.n_fwd_abs_items + (n_pack_units > 0 ? L.n_fwd_short_items : 0) + v / hpairs;
+    w.h0 = 2 * (v % hpairs);
+    w.pk = 1;
+  }
+  const int32_t* item = L.fwd_items + 4 * (int64_t)it;
   w.blk = load_block(L.blocks, item[0]);
   w.q0 = item[1];
   w.q1 = item[2];
-  w.hp = u % hpairs;
-  w.hk = (2 * w.hp) / G;
+  w.hk = w.h0 / G;
   w.kv_lo = w.blk.kv_lo;
   w.kv_hi = min(w.blk.e, w.q1);
   w.n = w.kv_hi > w.kv_lo ? (w.kv_hi - w.kv_lo + BN - 1) / BN : 0;
@@ -464,7 +494,8 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
     fwd_pers_kernel(const AiAttnFwdArgs a, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_qr,
                     const __grid_constant__ CUtensorMap tm_kr, const __grid_constant__ CUtensorMap tm_o,
-                    const int prerot, const int n_units) {
+                    const __grid_constant__ CUtensorMap tm_qr64, const int prerot, const int n_units,
+                    const int n_pack_units) {
   using namespace pf;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = tile::align1024(smem_raw);
@@ -523,11 +554,11 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
     // The next unit's description is read from global memory while this
     // unit's last PV MMAs run (before the epilogue's O_DONE wait).
     Unit w_next{};
-    if (snake_unit(0) < n_units) w_next = load_unit(a, snake_unit(0), prerot);
+    if (snake_unit(0) < n_units) w_next = load_unit(a, snake_unit(0), prerot, n_pack_units);
     bool store_pending = false;  // thread 0: the last TMA store's smem read not yet waited for
     for (int u = snake_unit(k); u < n_units && !*s_abort; u = snake_unit(++k)) {
       const Unit w = w_next;
-      const int i = w.q0 + r, h = 2 * w.hp + t, b = w.blk.row;
+      const int i = unit_row(w, r), h = unit_head(w, t, r), b = w.blk.row;
       if (!prerot) {
         // Q rows of this unit (rotated): the previous unit's S MMAs must be
         // done reading Q_t.
@@ -655,7 +686,7 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
         done = j + 1;
       }
       if (done != w.n) break;
-      if (snake_unit(k + 1) < n_units) w_next = load_unit(a, snake_unit(k + 1), prerot);
+      if (snake_unit(k + 1) < n_units) w_next = load_unit(a, snake_unit(k + 1), prerot, n_pack_units);
       // Epilogue: O_t / l.  O_t is read into registers, then released to the
       // next unit's first PV before the global stores.
       bool have_o = false;
@@ -698,7 +729,7 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
       // (the TMA box would spill into the next block's rows).  A unit without
       // key tiles stores its zero rows directly: its thread 0 has not waited
       // for the group's other threads in O_DONE.
-      const bool full = w.q1 == w.q0 + BM && w.n > 0;
+      const bool full = w.pk == 1 && w.q1 == w.q0 + BM && w.n > 0;
       const uint32_t buf = OSTAGE + (uint32_t)t * kHalf;
       bool ok_st = true;
       if (full) {
@@ -752,6 +783,7 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
       ptx::prefetch_tmap(&tm_v);
       if (prerot) {
         ptx::prefetch_tmap(&tm_qr);
+        ptx::prefetch_tmap(&tm_qr64);
         ptx::prefetch_tmap(&tm_kr);
       }
       // Loads in the order their slots are released: K(g), V(g), ... with a
@@ -760,7 +792,7 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
       int g = 0, k = 0;
       bool ok = true;
       for (int u = snake_unit(k); ok && u < n_units; u = snake_unit(++k)) {
-        const Unit w = load_unit(a, u, prerot);
+        const Unit w = load_unit(a, u, prerot, n_pack_units);
         const int b = w.blk.row;
         const CUtensorMap* mk = w.k_pre ? &tm_kr : &tm_k;
         for (int j = 0; j <= w.n && ok; ++j) {
@@ -769,12 +801,22 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
               ok = false;
               break;
             }
-            const int h0 = 2 * w.hp;
+            const int h0 = w.h0;
             ptx::mbar_arrive_expect_tx(bar(Q_READY), 2 * kTile);
-            ptx::tma_load_4d(sbase + Q0, &tm_qr, bar(Q_READY), 0, w.q0, h0, b);
-            ptx::tma_load_4d(sbase + Q0 + kHalf, &tm_qr, bar(Q_READY), 64, w.q0, h0, b);
-            ptx::tma_load_4d(sbase + Q1, &tm_qr, bar(Q_READY), 0, w.q0, h0 + 1, b);
-            ptx::tma_load_4d(sbase + Q1 + kHalf, &tm_qr, bar(Q_READY), 64, w.q0, h0 + 1, b);
+            if (w.pk == 1) {
+              ptx::tma_load_4d(sbase + Q0, &tm_qr, bar(Q_READY), 0, w.q0, h0, b);
+              ptx::tma_load_4d(sbase + Q0 + kHalf, &tm_qr, bar(Q_READY), 64, w.q0, h0, b);
+              ptx::tma_load_4d(sbase + Q1, &tm_qr, bar(Q_READY), 0, w.q0, h0 + 1, b);
+              ptx::tma_load_4d(sbase + Q1 + kHalf, &tm_qr, bar(Q_READY), 64, w.q0, h0 + 1, b);
+            } else {
+              // Four heads, 64 rows each: head h0 + 2t + x into rows [64x, 64x + 64) of tile t.
+#pragma unroll
+              for (int hh = 0; hh < 4; ++hh) {
+                const uint32_t dst = sbase + Q0 + (uint32_t)(hh >> 1) * kTile + (uint32_t)(hh & 1) * (kHalf / 2);
+                ptx::tma_load_4d(dst, &tm_qr64, bar(Q_READY), 0, w.q0, h0 + hh, b);
+                ptx::tma_load_4d(dst + kHalf, &tm_qr64, bar(Q_READY), 64, w.q0, h0 + hh, b);
+              }
+            }
           }
           if (j == w.n) break;
           const int slot = g & 1, k0 = w.kv_lo + j * BN;
@@ -843,7 +885,7 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
     int g = 0, k = 0;
     bool ok = true;
     for (int u = snake_unit(k); ok && u < n_units; u = snake_unit(++k)) {
-      const Unit w = load_unit(a, u, prerot);
+      const Unit w = load_unit(a, u, prerot, n_pack_units);
       if (!wait_u(Q_READY, k & 1)) break;
       if (w.n == 0) {
         ptx::mma_commit_w(bar(Q_EMPTY));
@@ -900,7 +942,7 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
     const __half2* cs16 = static_cast<const __half2*>(L.rope_cs16);
     int g = 0;
     for (int kr = 0, u = snake_unit(0); u < n_units && !*s_abort; u = snake_unit(++kr)) {
-      const Unit w = load_unit(a, u, prerot);
+      const Unit w = load_unit(a, u, prerot, n_pack_units);
       for (int j = 0; j < w.n; ++j, ++g) {
         const int slot = g & 1;
         if (!wait(K_FULL + slot, (g >> 1) & 1)) break;
@@ -1020,12 +1062,17 @@ int sm100_fwd(const AiAttnFwdArgs& a, cudaStream_t st, cudaError_t* cuda_err) {
       }
     }
     if (e == cudaSuccess && n_pair > 0) {
-      CUtensorMap tm_qr = tm_k, tm_kr = tm_k;
+      CUtensorMap tm_qr = tm_k, tm_kr = tm_k, tm_qr64 = tm_k;
       if (pre && (!sm100_make_map(&tm_qr, qr, a.batch, a.num_q_heads, a.seq_len, BM) ||
+                  !sm100_make_map(&tm_qr64, qr, a.batch, a.num_q_heads, a.seq_len, BM / 2) ||
                   !sm100_make_map(&tm_kr, kr, a.batch, a.num_kv_heads, a.seq_len, BN)))
         return AI_ERR_TMA;
-      // Persistent: one CTA per SM walks the (item, head pair) units.
-      const int n_units = n_pair * (a.num_q_heads / 2);
+      // Persistent: one CTA per SM walks the units: four-head units of the
+      // short items when a GQA group has a multiple of four query heads, then
+      // two-head units of the other items.
+      const int n_short = (G % 4 == 0) ? a.layout.n_fwd_short_items : 0;
+      const int n_pack_units = n_short * (a.num_q_heads / 4);
+      const int n_units = n_pack_units + (n_pair - n_short) * (a.num_q_heads / 2);
       int dev = 0, sms = 148;
       if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
       const int grid = n_units < sms ? n_units : sms;
@@ -1034,8 +1081,8 @@ int sm100_fwd(const AiAttnFwdArgs& a, cudaStream_t st, cudaError_t* cuda_err) {
       e = cudaFuncSetAttribute(fwd_pers_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pf::kSmem);
       if (e == cudaSuccess) {
         ProfScope ps(AI_PROF_FWD, st);
-        fwd_pers_kernel<<<grid, pf::kThreads, pf::kSmem, st>>>(a, tm_k, tm_v, tm_qr, tm_kr, tm_o, pre ? 1 : 0,
-                                                                n_units);
+        fwd_pers_kernel<<<grid, pf::kThreads, pf::kSmem, st>>>(a, tm_k, tm_v, tm_qr, tm_kr, tm_o, tm_qr64,
+                                                                pre ? 1 : 0, n_units, n_pack_units);
         e = cudaGetLastError();
       }
     }

@@ -46,6 +46,10 @@ int validate_fwd(const AiAttnFwdArgs* a) {
     return AI_ERR_NULL;
   if (a->workspace && ((uintptr_t)a->workspace % 256)) return AI_ERR_ALIGN;
   if (L.n_blocks < 0 || L.n_keys < 0 || L.n_pos <= 0 || L.n_fwd_items < 0 || L.n_kv_items < 0) return AI_ERR_LAYOUT;
+  if (L.n_fwd_abs_items < 0 || L.n_fwd_short_items < 0 ||
+      (int64_t)L.n_fwd_abs_items + L.n_fwd_short_items > L.n_fwd_items || L.n_kv_abs_items < 0 ||
+      L.n_kv_abs_items > L.n_kv_items)
+    return AI_ERR_LAYOUT;
   if (L.n_fwd_items > 0 && !L.fwd_items) return AI_ERR_NULL;
   if (L.n_kv_items > 0 && !L.kv_items) return AI_ERR_NULL;
   if (L.fwd_tile != ai_attn_fwd_tile_rows(a->dtype, a->head_dim)) return AI_ERR_LAYOUT;

@@ -23,7 +23,13 @@ template <> __device__ __forceinline__ __half from_f32<__half>(float x) { return
 
 // Decoded block record (see AI_BLOCK_* in ai_attn.h).
 struct Block {
-  int row, s, e, key_off, kv_lo, flags;
+  int row, s, e, key_off, kv_lo, flags, abs_lo, abs_hi;
+  // Whether keys [j0, j1) include one of the block's abs keys.
+  __device__ __forceinline__ bool abs_in(int j0, int j1) const {
+    if (!(flags & AI_BLOCKF_ABS)) return false;
+    if (abs_hi <= abs_lo) return true;
+    return j0 < abs_hi && abs_lo < j1;
+  }
 };
 
 __device__ __forceinline__ Block load_block(const int32_t* blocks, int id) {
@@ -35,6 +41,8 @@ __device__ __forceinline__ Block load_block(const int32_t* blocks, int id) {
   b.key_off = p[AI_BLOCK_KEY_OFF];
   b.kv_lo = p[AI_BLOCK_KV_LO];
   b.flags = p[AI_BLOCK_FLAGS];
+  b.abs_lo = p[AI_BLOCK_ABS_LO];
+  b.abs_hi = p[AI_BLOCK_ABS_HI];
   return b;
 }
 
@@ -61,6 +69,14 @@ __device__ __forceinline__ int key_row(uint32_t info, int n_pos, int32_t* status
 __device__ __forceinline__ int snake_unit(int k) {
   const int G = (int)gridDim.x, c = (int)blockIdx.x;
   return k * G + ((k & 1) ? G - 1 - c : c);
+}
+
+// Query heads of one GQA group (G heads) packed into one 128-row tile for a
+// work item of `rows` query rows: four heads of 32 rows, two of 64, or one.
+__device__ __forceinline__ int pack_heads(int rows, int G) {
+  if (G % 4 == 0 && rows <= 32) return 4;
+  if (G % 2 == 0 && rows <= 64) return 2;
+  return 1;
 }
 
 __device__ __forceinline__ int clamp_row(int r, int n_pos, int32_t* status) {

@@ -10,10 +10,11 @@ row its own layout (packed documents of different lengths per row).
 
 Output (``CompiledLayout``), all int32 / fp32 device tensors:
 
-* ``blocks [n, 8]``: row, s, e, key_off, kv_lo, flags (see ``AI_BLOCK_*``);
-  ``kv_lo`` is the first key the block attends to, so packed documents skip
-  the masked prefix; flags mark blocks with masked keys inside
-  ``[kv_lo, e)`` and blocks with abs keys;
+* ``blocks [n, 8]``: row, s, e, key_off, kv_lo, flags, abs_lo, abs_hi (see
+  ``AI_BLOCK_*``); ``kv_lo`` is the first key the block attends to, so packed
+  documents skip the masked prefix; flags mark blocks with masked keys inside
+  ``[kv_lo, e)`` and blocks with abs keys, whose abs keys lie in
+  ``[abs_lo, abs_hi)``;
 * ``key_info [sum E]``: per concatenated key, the rotary table row (bits
   0..29), attn mask (bit 30), abs mask (bit 31);
 * ``q_pos [B, T]``: table row of every query row (rows past the covered
@@ -23,8 +24,11 @@ Output (``CompiledLayout``), all int32 / fp32 device tensors:
 * ``rope_cos / rope_sin [n_pos, D/2]``: fp32 table of the rotary module, and
   ``rope_cs16 [n_pos, D/2, 2]`` the same angles as fp16 (cos, sin) pairs for
   the bf16 tensor-core kernels;
-* ``fwd_items [m, 4]``: (block, q0, q1) query tiles, longest first;
-* ``kv_items [k, 4]``: (row, j0, j1) key tiles of the dK/dV pass, longest first.
+* ``fwd_items [m, 4]``: (block, q0, q1) query tiles: those of blocks with
+  abs keys, then those with at most half a tile of rows, then the rest, each
+  group longest first;
+* ``kv_items [k, 4]``: (row, j0, j1) key tiles of the dK/dV pass: those that
+  hold an abs key of some block first, then the rest, longest first.
 
 It is built once per layout object and cached on it (the reference caches
 its own per-backend metadata the same way, ``perturb_labels.py:298-331``), so
@@ -145,6 +149,7 @@ class CompiledLayout:
     kv_items: torch.Tensor
     n_fwd_abs_items: int         # leading fwd_items whose block has abs keys
     n_kv_abs_items: int          # leading kv_items that a block with abs keys sees
+    n_fwd_short_items: int       # fwd_items after the abs ones with at most fwd_tile / 2 rows
     pairs_per_head: int          # finite (query, key) logits of one head summed over the batch
     all_rows_owned: bool = False  # every row of every batch row belongs to a block (no fill launches)
     host_blocks: np.ndarray = field(repr=False, default=None)
@@ -172,6 +177,7 @@ class CompiledLayout:
         L.n_kv_items = int(self.kv_items.shape[0])
         L.n_kv_abs_items = int(self.n_kv_abs_items)
         L.all_rows_owned = int(self.all_rows_owned)
+        L.n_fwd_short_items = int(self.n_fwd_short_items)
         return L
 
 
@@ -182,11 +188,20 @@ def _tiles(fwd_tile: int, kv_tile: int, blocks: np.ndarray, row_cov: np.ndarray)
             q1 = min(q0 + fwd_tile, e)
             cost = (q1 - q0) * max(0, min(e, q1) - kv_lo)
             fwd.append((cost, bi, q0, q1))
-    # Items of blocks with abs keys first (they run on their own kernel), then longest first.
-    fwd.sort(key=lambda t: (-(int(blocks[t[1], 5]) & BLOCKF_ABS), -t[0]))
-    n_abs = sum(1 for t in fwd if int(blocks[t[1], 5]) & BLOCKF_ABS)
-    # Key tiles: cost = query rows that see them; tiles touching a block with
-    # abs keys first (own kernel), then longest first.
+    # Items of blocks with abs keys first (they run on their own kernel), then
+    # the short items (at most half a tile of rows: the tensor-core kernels
+    # pack two heads of such an item into one tile), then the rest; longest
+    # first within each group.
+    def group(t):
+        if int(blocks[t[1], 5]) & BLOCKF_ABS:
+            return 0
+        return 1 if t[3] - t[2] <= fwd_tile // 2 else 2
+    fwd.sort(key=lambda t: (group(t), -t[0]))
+    n_abs = sum(1 for t in fwd if group(t) == 0)
+    n_short = sum(1 for t in fwd if group(t) == 1)
+    # Key tiles: cost = query rows that see them; tiles that hold an abs key
+    # of some block first (the abs pass adds those blocks' part), then
+    # longest first.
     kv = []
     for row, cov in enumerate(row_cov):
         rb = blocks[blocks[:, 0] == row]
@@ -194,13 +209,14 @@ def _tiles(fwd_tile: int, kv_tile: int, blocks: np.ndarray, row_cov: np.ndarray)
             j1 = min(j0 + kv_tile, int(cov))
             seen = (rb[:, 2] > j0) & (rb[:, 4] < j1)
             cost = int(np.maximum(rb[seen, 2] - np.maximum(rb[seen, 1], j0), 0).sum())
-            has_abs = bool((rb[seen, 5] & BLOCKF_ABS).any())
+            # an abs key of a block among these keys (its range [abs_lo, abs_hi) meets [j0, j1))
+            has_abs = bool(((rb[seen, 5] & BLOCKF_ABS) != 0)[(rb[seen, 6] < j1) & (rb[seen, 7] > j0)].any())
             kv.append((has_abs, cost, row, j0, j1))
     kv.sort(key=lambda t: (-int(t[0]), -t[1]))
     n_kv_abs = sum(1 for t in kv if t[0])
     fwd_arr = np.asarray([(bi, q0, q1, 0) for _, bi, q0, q1 in fwd], dtype=np.int32).reshape(-1, 4)
     kv_arr = np.asarray([(row, j0, j1, 0) for _, _, row, j0, j1 in kv], dtype=np.int32).reshape(-1, 4)
-    return fwd_arr, kv_arr, n_abs, n_kv_abs
+    return fwd_arr, kv_arr, n_abs, n_kv_abs, n_short
 
 
 def compile_layout(parsed_positions, batch: int, seq_len: int, head_dim: int, dtype: torch.dtype,
@@ -290,7 +306,11 @@ def _compile(parsed_positions, batch, seq_len, head_dim, code, rotary_emb, devic
                 flags |= BLOCKF_ABS
             if own_flags[u][bi]:
                 flags |= BLOCKF_OWNPOS
-            blocks.append((b, int(s), int(e), key_base[u] + int(ks), kv_lo, flags, 0, 0))
+            abs_lo = abs_hi = 0
+            if flags & BLOCKF_ABS:
+                na = np.flatnonzero(h.abs_[ks:ke] & am)
+                abs_lo, abs_hi = int(na[0]), int(na[-1]) + 1
+            blocks.append((b, int(s), int(e), key_base[u] + int(ks), kv_lo, flags, abs_lo, abs_hi))
         row_blocks.append(len(blocks))
         cov = int(h.bounds[-1, 1])
         row_cov.append(cov)
@@ -304,7 +324,7 @@ def _compile(parsed_positions, batch, seq_len, head_dim, code, rotary_emb, devic
     lib = _lib.lib()
     fwd_tile = lib.ai_attn_fwd_tile_rows(code, head_dim)
     kv_tile = lib.ai_attn_kv_tile_rows(code, head_dim)
-    fwd_items, kv_items, n_abs, n_kv_abs = _tiles(fwd_tile, kv_tile, blocks_np, row_cov_np)
+    fwd_items, kv_items, n_abs, n_kv_abs, n_short = _tiles(fwd_tile, kv_tile, blocks_np, row_cov_np)
 
     cos, sin = rope_table(rotary_emb, lo, hi, head_dim, device)
 
@@ -318,6 +338,7 @@ def _compile(parsed_positions, batch, seq_len, head_dim, code, rotary_emb, devic
         key_info=dev(key_info), q_pos=dev(q_pos), k_own=dev(k_own), rope_cos=cos, rope_sin=sin,
         rope_cs16=torch.stack([cos, sin], dim=-1).to(torch.float16).contiguous(),
         fwd_items=dev(fwd_items), kv_items=dev(kv_items), n_fwd_abs_items=n_abs, n_kv_abs_items=n_kv_abs,
+        n_fwd_short_items=n_short,
         pairs_per_head=pairs,
         all_rows_owned=bool(np.all(row_cov_np >= seq_len)),
         host_blocks=blocks_np,

@@ -43,7 +43,7 @@
 extern "C" {
 #endif
 
-#define AI_ATTN_ABI_VERSION 6
+#define AI_ATTN_ABI_VERSION 7
 
 typedef enum AiDtype {
   AI_DTYPE_BF16 = 0,
@@ -84,6 +84,9 @@ typedef struct AiTensor4 {
 #define AI_BLOCK_KEY_OFF 3 /* offset of key 0 of this block in key_info */
 #define AI_BLOCK_KV_LO 4   /* first key with attn_mask set (e if none) */
 #define AI_BLOCK_FLAGS 5   /* AI_BLOCKF_* */
+#define AI_BLOCK_ABS_LO 6  /* blocks with AI_BLOCKF_ABS: first key with abs_pos_mask (and attn_mask) set */
+#define AI_BLOCK_ABS_HI 7  /* ... one past the last such key; ABS_HI <= ABS_LO means "any key of the block"
+                              (ABI 7: key tiles outside [ABS_LO, ABS_HI) take the fast kernels) */
 #define AI_BLOCK_FIELDS 8
 #define AI_BLOCKF_MASKED 1 /* some key in [kv_lo, e) has attn_mask false */
 #define AI_BLOCKF_ABS 2    /* some key has abs_pos_mask set */
@@ -119,6 +122,10 @@ typedef struct AiAttnLayout {
   int32_t n_kv_abs_items;     /* the first n_kv_abs_items items see a block with AI_BLOCKF_ABS */
   int32_t all_rows_owned;     /* 1: row_cov[b] == seq_len for every b (no diagonal-only rows), so the
                                  fill launches are skipped; 0: not known (they run) */
+  int32_t n_fwd_short_items;  /* the n_fwd_short_items items right after the abs items have at most
+                                 fwd_tile / 2 query rows (ABI 7): with four or more query heads per KV
+                                 head the tensor-core kernels pack two heads' rows of such an item into
+                                 one 128-row tile; 0: no item is treated as short */
 } AiAttnLayout;
 
 typedef struct AiAttnFwdArgs {

@@ -53,10 +53,26 @@ def test_tables_match_layout(name, dtype):
     assert np.array_equal(qp[:T], lay.query_pos_ids.numpy())
     assert np.all(qp[T:] == 0)
     assert c.pairs_per_head == 2 * O.count_pairs(lay, T)
-    # abs items lead the forward work list
+    # abs items lead the forward work list, then the short items (at most
+    # half a tile of rows), then the rest
     items = c.fwd_items.numpy()
     is_abs = (blocks[items[:, 0], 5] & 2) != 0
     assert is_abs.sum() == c.n_fwd_abs_items and is_abs[:c.n_fwd_abs_items].all()
+    rest = items[c.n_fwd_abs_items:]
+    short = (rest[:, 2] - rest[:, 1]) <= c.fwd_tile // 2
+    assert short.sum() == c.n_fwd_short_items and short[:c.n_fwd_short_items].all()
+    # abs-key ranges: [abs_lo, abs_hi) is the span of the block's abs keys
+    for (s_, e_, KS, KE), blk in zip(lay.boundary_indices, blocks):
+        a_ = ab[KS:KE] & am[KS:KE]
+        if a_.any():
+            nz = np.flatnonzero(a_)
+            assert (blk[6], blk[7]) == (nz[0], nz[-1] + 1)
+        else:
+            assert (blk[6], blk[7]) == (0, 0)
+    # key tiles holding an abs key of some block lead the dK/dV work list
+    kv = c.kv_items.numpy()
+    hold = [any(b_[5] & 2 and b_[6] < j1 and b_[7] > j0 and b_[2] > j0 for b_ in blocks) for _, j0, j1, _ in kv]
+    assert sum(hold) == c.n_kv_abs_items and all(hold[:c.n_kv_abs_items])
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])

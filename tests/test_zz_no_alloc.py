@@ -131,7 +131,7 @@ def test_noalloc_backward_at_the_row_limit(cuda_device):
     layout = compile_layout(lay, B, T, D, torch.bfloat16, mod.to(cuda_device), cuda_device)
     out, lse = attn_fwd(tq, tk, tv, layout, D ** -0.5)
     dq, dk, dv = _compare_two_noalloc_calls(tq, tk, tv, out, lse, tdo, layout, 4 * MAX_ROWS, None, cuda_device)
-    rope = O.make_sectioned_rope(mod.inv_freq.numpy(), [np.arange(T)], [(0, D // 2)])
+    rope = O.make_sectioned_rope(mod.inv_freq.cpu().numpy(), [np.arange(T)], [(0, D // 2)])
     bounds = lay.boundary_indices
     G = Hq // Hkv
     for di in (0, 1, len(bounds) // 2, len(bounds) - 1):
