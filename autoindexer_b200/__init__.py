@@ -17,7 +17,7 @@ from .attention import (
 )
 from .meta import CompiledLayout, RowLayouts, compile_layout
 from .positions import (BlockType, PositionBlock, PositionBlockList, blocks_from_concat, cursor_stream,
-                        document_blocks)
+                        document_blocks, positions_from_operations)
 from .decode import decode_attention
 from .prefill import plain_causal_attn_b200, prefill_attention_interface, prefill_layout
 from .rope import SectionedRope, default_inv_freq
@@ -39,6 +39,7 @@ __all__ = [
     "cursor_stream",
     "document_blocks",
     "blocks_from_concat",
+    "positions_from_operations",
     "decode_attention",
     "plain_causal_attn_b200",
     "prefill_attention_interface",

@@ -51,6 +51,10 @@ EXPORTED_SYMBOLS = (
     "ai_attn_read_status",
     "ai_attn_selftest_wait",
     "ai_attn_strerror",
+    "ai_attn_positions_from_ops_sizes",
+    "ai_attn_positions_from_ops",
+    "ai_attn_prep_sizes",
+    "ai_attn_prep",
 )
 
 _i32p = ctypes.POINTER(ctypes.c_int32)
@@ -152,6 +156,48 @@ class AiAttnDecodeArgs(ctypes.Structure):
     ]
 
 
+class AiPrepList(ctypes.Structure):
+    _fields_ = [
+        ("n_blocks", ctypes.c_int32),
+        ("boundary", ctypes.c_void_p),
+        ("n_query", ctypes.c_int64),
+        ("query_pos", ctypes.c_void_p),
+        ("n_keys", ctypes.c_int64),
+        ("key_pos", ctypes.c_void_p),
+        ("attn_mask", ctypes.c_void_p),
+        ("abs_mask", ctypes.c_void_p),
+    ]
+
+
+class AiPrepSizes(ctypes.Structure):
+    _fields_ = [
+        ("n_blocks", ctypes.c_int32),
+        ("n_fwd_items", ctypes.c_int32),
+        ("n_kv_items", ctypes.c_int32),
+        ("n_keys", ctypes.c_int64),
+        ("p_min", ctypes.c_int64),
+        ("p_max", ctypes.c_int64),
+    ]
+
+
+class AiPrepTables(ctypes.Structure):
+    _fields_ = [
+        ("blocks", ctypes.c_void_p),
+        ("row_blocks", ctypes.c_void_p),
+        ("row_cov", ctypes.c_void_p),
+        ("key_info", ctypes.c_void_p),
+        ("q_pos", ctypes.c_void_p),
+        ("k_own", ctypes.c_void_p),
+        ("fwd_items", ctypes.c_void_p),
+        ("kv_items", ctypes.c_void_p),
+        ("n_fwd_abs_items", ctypes.c_int32),
+        ("n_fwd_short_items", ctypes.c_int32),
+        ("n_kv_abs_items", ctypes.c_int32),
+        ("all_rows_owned", ctypes.c_int32),
+        ("pairs_per_head", ctypes.c_int64),
+    ]
+
+
 _lock = threading.Lock()
 _lib = None
 
@@ -188,6 +234,15 @@ def _bind(handle):
     handle.ai_attn_profile_read.argtypes = [P(ctypes.c_float), P(ctypes.c_int32)]
     handle.ai_attn_selftest_wait.restype = ctypes.c_int
     handle.ai_attn_selftest_wait.argtypes = [ctypes.c_void_p, ctypes.c_longlong, ctypes.c_void_p]
+    vp, i32, i64 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64
+    handle.ai_attn_positions_from_ops_sizes.restype = ctypes.c_int
+    handle.ai_attn_positions_from_ops_sizes.argtypes = [vp, i32, P(i32), P(i64), P(i64)]
+    handle.ai_attn_positions_from_ops.restype = ctypes.c_int
+    handle.ai_attn_positions_from_ops.argtypes = [vp, i32, vp, vp, vp, vp, vp, vp]
+    handle.ai_attn_prep_sizes.restype = ctypes.c_int
+    handle.ai_attn_prep_sizes.argtypes = [P(AiPrepList), i32, vp, i32, i32, i32, i32, P(AiPrepSizes)]
+    handle.ai_attn_prep.restype = ctypes.c_int
+    handle.ai_attn_prep.argtypes = [P(AiPrepList), i32, vp, i32, i32, i32, i32, P(AiPrepTables)]
     return handle
 
 

@@ -1,0 +1,453 @@
+// Host-side layout builders of the chain-of-edits attention (C ABI in
+// include/ai_attn.h; no GPU involved).
+//
+// ai_attn_positions_from_ops: an edit chain -> the concat()-ed arrays of its
+//   position-block list.  Restates, in one pass over plain arrays, the
+//   reference's perturb_labels_per_sequence (perturb_labels.py:236-275: the
+//   token index bookkeeping of each operation) and
+//   get_parsed_positions_from_perturbations (perturb_labels.py:395-467: the
+//   running position ids, abs mask and attention mask, and the EXTEND / EDIT /
+//   COMPLETE blocks pushed from them), followed by PositionBlockList.concat()
+//   (perturb_labels.py:341-357).  The reference runs these as per-operation
+//   torch ops on the training device with a host sync per operation.
+//
+// ai_attn_prep: concat()-ed lists (one per batch row, or shared) -> the
+//   device tables of AiAttnLayout (block records, key words, query / own-key
+//   table rows, forward and dK/dV work lists, counts), written into host
+//   buffers the caller copies to the device in one transfer.
+
+#include <algorithm>
+#include <cstdint>
+#include <cstring>
+#include <vector>
+
+#include "../../include/ai_attn.h"
+
+namespace {
+
+struct Op {
+  int64_t num_insert, num_delete, start_rel_pos, end_rel_pos, num_extend;
+};
+
+// One pushed block: [start, end) query rows; key arrays are the snapshots of
+// the running arrays over [0, end) at push time.
+struct PushedBlock {
+  int64_t start, end;
+  int32_t type;  // AI_BLOCK_TYPE_*
+  std::vector<int64_t> key_pos;
+  std::vector<uint8_t> attn, abs;
+  std::vector<int64_t> query_pos;
+};
+
+// Replays the operations; fills `blocks` (when not null) and returns
+// AI_OK, or AI_ERR_LAYOUT for an operation list the reference rejects.
+int replay_ops(const Op* ops, int n_ops, std::vector<PushedBlock>* blocks, int64_t* token_count_out,
+               int32_t* n_blocks_out, int64_t* n_keys_out) {
+  if (n_ops <= 0) return AI_ERR_LAYOUT;
+  // perturb_labels_per_sequence: lengths and marker indices per operation.
+  struct Pert {
+    int64_t edit_idx, return_idx, post_len;
+    bool edit;
+  };
+  std::vector<Pert> perts((size_t)n_ops);
+  int64_t len = 0, cur = 0;  // len(token_indices), curr_seq_idx
+  for (int i = 0; i < n_ops; ++i) {
+    const Op& op = ops[i];
+    if (op.num_insert < 0 || op.num_delete < 0 || op.num_extend < 0) return AI_ERR_LAYOUT;
+    Pert p{-1, -1, 0, false};
+    if (op.num_insert > 0 || op.num_delete > 0) {
+      // an edit needs a token before it and a valid cursor range
+      if (cur <= 0 || op.start_rel_pos < 0 || op.start_rel_pos > op.end_rel_pos || op.start_rel_pos >= len ||
+          op.end_rel_pos > len)
+        return AI_ERR_LAYOUT;
+      p.edit = true;
+      p.edit_idx = cur;
+      p.return_idx = cur + op.num_insert + 1;
+      len = len - (op.end_rel_pos - op.start_rel_pos) + op.num_insert;
+      cur += op.num_insert + 2;
+    }
+    p.post_len = len;
+    len += op.num_extend;
+    cur += op.num_extend;
+    perts[(size_t)i] = p;
+  }
+  const int64_t T = cur;  // token_count
+  if (T <= 0 || T > (int64_t)1 << 30) return AI_ERR_LAYOUT;
+  std::vector<int64_t> pos((size_t)T, 0);
+  std::vector<uint8_t> absm((size_t)T, 0), attn((size_t)T, 1);
+  int64_t start = 0, n_keys = 0;
+  int32_t n_blocks = 0;
+  auto push = [&](int64_t end, int32_t type) -> int {
+    if (end <= start || end > T) return AI_ERR_LAYOUT;
+    if (type == AI_BLOCK_TYPE_EXTEND) {
+      int64_t attended = 0;
+      for (int64_t j = 0; j < end; ++j) attended += attn[(size_t)j];
+      if (attended <= 1 || end < 2) return AI_ERR_LAYOUT;  // an edit marker cannot open the sequence
+    }
+    if (blocks) {
+      PushedBlock b;
+      b.start = start;
+      b.end = end;
+      b.type = type;
+      b.key_pos.assign(pos.begin(), pos.begin() + end);
+      if (type == AI_BLOCK_TYPE_EXTEND) b.key_pos[(size_t)end - 1] = b.key_pos[(size_t)end - 2] + 1;
+      b.attn.assign(attn.begin(), attn.begin() + end);
+      for (int64_t j = 0; j < end; ++j)
+        if (!b.attn[(size_t)j]) b.key_pos[(size_t)j] = -1;
+      if (type == AI_BLOCK_TYPE_EDIT)
+        b.abs.assign(absm.begin(), absm.begin() + end);
+      else
+        b.abs.assign((size_t)end, 0);
+      b.query_pos.assign(pos.begin() + start, pos.begin() + end);
+      blocks->push_back(std::move(b));
+    }
+    n_keys += end;
+    ++n_blocks;
+    start = end;
+    return AI_OK;
+  };
+  for (int i = 0; i < n_ops; ++i) {
+    const Op& op = ops[i];
+    const Pert& pt = perts[(size_t)i];
+    if (pt.edit) {
+      const int64_t ed = pt.edit_idx, rt = pt.return_idx;
+      if (rt >= T) return AI_ERR_LAYOUT;
+      pos[(size_t)ed] = op.start_rel_pos - 1;
+      for (int64_t j = 0; j < ed; ++j) absm[(size_t)j] = pos[(size_t)j] >= op.start_rel_pos;
+      absm[(size_t)ed] = 1;
+      for (int64_t j = 0; j < T; ++j) absm[(size_t)j] &= attn[(size_t)j];
+      int rc = push(ed + 1, AI_BLOCK_TYPE_EXTEND);
+      if (rc != AI_OK) return rc;
+      for (int64_t j = 0; j < T; ++j)
+        if (absm[(size_t)j]) pos[(size_t)j] += 1 - op.start_rel_pos;
+      for (int64_t j = 0; j < T; ++j)
+        if (absm[(size_t)j] && pos[(size_t)j] > op.num_delete) pos[(size_t)j] += 1;
+      pos[(size_t)ed] = op.num_delete + 1;
+      if (op.num_insert > 0) {
+        for (int64_t j = start; j < rt; ++j) pos[(size_t)j] = op.start_rel_pos + (j - start);
+        rc = push(rt, AI_BLOCK_TYPE_EDIT);
+        if (rc != AI_OK) return rc;
+      }
+      for (int64_t j = 0; j < T; ++j)
+        if (absm[(size_t)j]) pos[(size_t)j] += op.start_rel_pos + op.num_insert - op.num_delete - 2;
+      pos[(size_t)rt] = pt.post_len - 1;
+      const int64_t pe = pos[(size_t)ed];
+      for (int64_t j = 0; j < T; ++j)
+        if (absm[(size_t)j] && pos[(size_t)j] <= pe) attn[(size_t)j] = 0;
+      attn[(size_t)rt] = 0;
+      std::fill(absm.begin(), absm.end(), 0);
+    }
+    const int64_t ext_pos = start > 0 ? pos[(size_t)start] + 1 : 0;
+    const int64_t ext_idx = start > 0 ? start + 1 : 0;
+    for (int64_t x = 0; x < op.num_extend && ext_idx + x < T; ++x) pos[(size_t)(ext_idx + x)] = ext_pos + x;
+  }
+  int rc = push(T, AI_BLOCK_TYPE_COMPLETE);
+  if (rc != AI_OK) return rc;
+  *token_count_out = T;
+  *n_blocks_out = n_blocks;
+  *n_keys_out = n_keys;
+  return AI_OK;
+}
+
+// ------------------------------------------------------------------ ai_attn_prep
+
+struct ListView {
+  const AiPrepList* l;
+  std::vector<uint32_t> info;   // key words (table row | attn | abs)
+  std::vector<int32_t> own;     // [seq_len] own-block table row of each key
+  std::vector<uint8_t> own_ok;  // per block: every attended key at its own-block row
+  int64_t pairs = 0;
+  int64_t key_base = 0;
+};
+
+int check_list(const AiPrepList& l, int32_t seq_len) {
+  if (l.n_blocks <= 0 || !l.boundary || !l.query_pos || !l.key_pos || !l.attn_mask) return AI_ERR_NULL;
+  int64_t expect = 0;
+  for (int32_t i = 0; i < l.n_blocks; ++i) {
+    const int64_t* b = l.boundary + 4 * (int64_t)i;
+    if (b[0] != expect || b[1] <= b[0] || b[3] - b[2] != b[1] || b[1] > seq_len) return AI_ERR_LAYOUT;
+    if (i > 0 && b[2] != l.boundary[4 * (int64_t)(i - 1) + 3]) return AI_ERR_LAYOUT;
+    if (i == 0 && b[2] != 0) return AI_ERR_LAYOUT;
+    expect = b[1];
+  }
+  if (l.n_query != expect) return AI_ERR_LAYOUT;
+  if (l.n_keys != l.boundary[4 * (int64_t)(l.n_blocks - 1) + 3]) return AI_ERR_LAYOUT;
+  return AI_OK;
+}
+
+struct Plan {
+  int64_t lo = 0, hi = 0, n_keys = 0;
+  int32_t n_blocks = 0, n_fwd = 0, n_kv = 0;
+};
+
+int plan(const AiPrepList* lists, int32_t n_lists, const int32_t* list_of_row, int32_t batch, int32_t seq_len,
+         int32_t fwd_tile, int32_t kv_tile, Plan* p) {
+  if (!lists || !list_of_row || !p) return AI_ERR_NULL;
+  if (n_lists <= 0 || batch <= 0 || seq_len <= 0 || fwd_tile <= 0 || kv_tile <= 0) return AI_ERR_SHAPE;
+  for (int32_t u = 0; u < n_lists; ++u) {
+    int rc = check_list(lists[u], seq_len);
+    if (rc != AI_OK) return rc;
+  }
+  Plan q;
+  for (int32_t u = 0; u < n_lists; ++u) {
+    const AiPrepList& l = lists[u];
+    for (int64_t i = 0; i < l.n_query; ++i) {
+      q.lo = std::min(q.lo, l.query_pos[i]);
+      q.hi = std::max(q.hi, l.query_pos[i]);
+    }
+    for (int64_t j = 0; j < l.n_keys; ++j)
+      if (l.attn_mask[j]) {
+        q.lo = std::min(q.lo, l.key_pos[j]);
+        q.hi = std::max(q.hi, l.key_pos[j]);
+      }
+    q.n_keys += l.n_keys;
+  }
+  if (q.hi - q.lo + 1 > (int64_t)AI_KEY_ROW_MASK) return AI_ERR_LAYOUT;
+  for (int32_t b = 0; b < batch; ++b) {
+    const int32_t u = list_of_row[b];
+    if (u < 0 || u >= n_lists) return AI_ERR_LAYOUT;
+    const AiPrepList& l = lists[u];
+    q.n_blocks += l.n_blocks;
+    for (int32_t i = 0; i < l.n_blocks; ++i) {
+      const int64_t s = l.boundary[4 * (int64_t)i], e = l.boundary[4 * (int64_t)i + 1];
+      q.n_fwd += (int32_t)((e - s + fwd_tile - 1) / fwd_tile);
+    }
+    q.n_kv += (int32_t)((l.n_query + kv_tile - 1) / kv_tile);
+  }
+  *p = q;
+  return AI_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int ai_attn_positions_from_ops_sizes(const int64_t* ops, int32_t n_ops, int32_t* n_blocks, int64_t* n_query,
+                                     int64_t* n_keys) {
+  if (!ops || !n_blocks || !n_query || !n_keys) return AI_ERR_NULL;
+  return replay_ops(reinterpret_cast<const Op*>(ops), n_ops, nullptr, n_query, n_blocks, n_keys);
+}
+
+int ai_attn_positions_from_ops(const int64_t* ops, int32_t n_ops, int64_t* boundary, int64_t* query_pos,
+                               int64_t* key_pos, uint8_t* attn_mask, uint8_t* abs_mask, int32_t* block_type) {
+  if (!ops || !boundary || !query_pos || !key_pos || !attn_mask || !abs_mask) return AI_ERR_NULL;
+  std::vector<PushedBlock> blocks;
+  int64_t T = 0, nk = 0;
+  int32_t nb = 0;
+  int rc = replay_ops(reinterpret_cast<const Op*>(ops), n_ops, &blocks, &T, &nb, &nk);
+  if (rc != AI_OK) return rc;
+  int64_t kcum = 0, qcum = 0;
+  for (int32_t i = 0; i < nb; ++i) {
+    const PushedBlock& b = blocks[(size_t)i];
+    boundary[4 * (int64_t)i] = b.start;
+    boundary[4 * (int64_t)i + 1] = b.end;
+    boundary[4 * (int64_t)i + 2] = kcum;
+    boundary[4 * (int64_t)i + 3] = kcum + b.end;
+    if (block_type) block_type[i] = b.type;
+    std::memcpy(key_pos + kcum, b.key_pos.data(), sizeof(int64_t) * (size_t)b.end);
+    std::memcpy(attn_mask + kcum, b.attn.data(), (size_t)b.end);
+    std::memcpy(abs_mask + kcum, b.abs.data(), (size_t)b.end);
+    std::memcpy(query_pos + qcum, b.query_pos.data(), sizeof(int64_t) * b.query_pos.size());
+    kcum += b.end;
+    qcum += (int64_t)b.query_pos.size();
+  }
+  return AI_OK;
+}
+
+int ai_attn_prep_sizes(const AiPrepList* lists, int32_t n_lists, const int32_t* list_of_row, int32_t batch,
+                       int32_t seq_len, int32_t fwd_tile, int32_t kv_tile, AiPrepSizes* sizes) {
+  if (!sizes) return AI_ERR_NULL;
+  Plan p;
+  int rc = plan(lists, n_lists, list_of_row, batch, seq_len, fwd_tile, kv_tile, &p);
+  if (rc != AI_OK) return rc;
+  sizes->n_blocks = p.n_blocks;
+  sizes->n_fwd_items = p.n_fwd;
+  sizes->n_kv_items = p.n_kv;
+  sizes->n_keys = p.n_keys;
+  sizes->p_min = p.lo;
+  sizes->p_max = p.hi;
+  return AI_OK;
+}
+
+int ai_attn_prep(const AiPrepList* lists, int32_t n_lists, const int32_t* list_of_row, int32_t batch,
+                 int32_t seq_len, int32_t fwd_tile, int32_t kv_tile, AiPrepTables* out) {
+  if (!out || !out->blocks || !out->row_blocks || !out->row_cov || !out->key_info || !out->q_pos || !out->k_own ||
+      !out->fwd_items || !out->kv_items)
+    return AI_ERR_NULL;
+  Plan p;
+  int rc = plan(lists, n_lists, list_of_row, batch, seq_len, fwd_tile, kv_tile, &p);
+  if (rc != AI_OK) return rc;
+  const int64_t lo = p.lo, n_pos = p.hi - p.lo + 1;
+  auto row_of = [&](int64_t pos) -> uint32_t {
+    int64_t r = pos - lo;
+    r = r < 0 ? 0 : (r >= n_pos ? n_pos - 1 : r);
+    return (uint32_t)r;
+  };
+
+  // Per list: key words, own-block rows, OWNPOS per block, finite pairs.
+  std::vector<ListView> views((size_t)n_lists);
+  int64_t base = 0;
+  for (int32_t u = 0; u < n_lists; ++u) {
+    const AiPrepList& l = lists[u];
+    ListView& v = views[(size_t)u];
+    v.l = &l;
+    v.key_base = base;
+    base += l.n_keys;
+    v.info.resize((size_t)l.n_keys);
+    for (int64_t j = 0; j < l.n_keys; ++j) {
+      const bool at = l.attn_mask[j] != 0, ab = l.abs_mask && l.abs_mask[j] && at;
+      v.info[(size_t)j] = row_of(l.key_pos[j]) | (at ? AI_KEY_ATTN : 0u) | (ab ? AI_KEY_ABS : 0u);
+    }
+    v.own.assign((size_t)seq_len, 0);
+    for (int32_t i = 0; i < l.n_blocks; ++i) {
+      const int64_t* bd = l.boundary + 4 * (int64_t)i;
+      for (int64_t r = bd[0]; r < bd[1]; ++r) v.own[(size_t)r] = (int32_t)(v.info[(size_t)(bd[2] + r)] & AI_KEY_ROW_MASK);
+    }
+    v.own_ok.resize((size_t)l.n_blocks);
+    for (int32_t i = 0; i < l.n_blocks; ++i) {
+      const int64_t* bd = l.boundary + 4 * (int64_t)i;
+      bool ok = true;
+      int64_t cum = 0;
+      for (int64_t j = 0; j < bd[1]; ++j) {
+        const uint32_t w = v.info[(size_t)(bd[2] + j)];
+        if (w & AI_KEY_ATTN) {
+          ++cum;
+          if ((int32_t)(w & AI_KEY_ROW_MASK) != v.own[(size_t)j]) ok = false;
+        }
+        if (j >= bd[0]) v.pairs += cum;  // row j sees the attended keys up to j
+      }
+      v.own_ok[(size_t)i] = ok;
+    }
+    std::memcpy(out->key_info + v.key_base, v.info.data(), sizeof(uint32_t) * (size_t)l.n_keys);
+  }
+
+  // Blocks, row tables, query / own rows.
+  struct FwdItem {
+    int64_t cost;
+    int32_t block, q0, q1, group;
+  };
+  struct KvItem {
+    int64_t cost;
+    int32_t row, j0, j1;
+    bool abs;
+  };
+  std::vector<FwdItem> fwd;
+  std::vector<KvItem> kv;
+  fwd.reserve((size_t)p.n_fwd);
+  kv.reserve((size_t)p.n_kv);
+  int32_t nb = 0;
+  int64_t pairs = 0;
+  bool all_owned = true;
+  out->row_blocks[0] = 0;
+  for (int32_t b = 0; b < batch; ++b) {
+    const ListView& v = views[(size_t)list_of_row[b]];
+    const AiPrepList& l = *v.l;
+    const int32_t first = nb;
+    for (int32_t i = 0; i < l.n_blocks; ++i) {
+      const int64_t* bd = l.boundary + 4 * (int64_t)i;
+      const int64_t s = bd[0], e = bd[1], ks = bd[2];
+      int64_t kv_lo = e, abs_lo = 0, abs_hi = 0, last_att = -1;
+      bool any_abs = false;
+      for (int64_t j = 0; j < e; ++j) {
+        const uint32_t w = v.info[(size_t)(ks + j)];
+        if (w & AI_KEY_ATTN) {
+          if (kv_lo == e) kv_lo = j;
+          last_att = j;
+        }
+        if (w & AI_KEY_ABS) {
+          if (!any_abs) abs_lo = j;
+          abs_hi = j + 1;
+          any_abs = true;
+        }
+      }
+      int32_t flags = 0;
+      if (kv_lo < e) {
+        int64_t attended = 0;
+        for (int64_t j = kv_lo; j < e; ++j) attended += (v.info[(size_t)(ks + j)] & AI_KEY_ATTN) ? 1 : 0;
+        if (attended != e - kv_lo) flags |= AI_BLOCKF_MASKED;
+      }
+      (void)last_att;
+      if (any_abs) flags |= AI_BLOCKF_ABS;
+      if (v.own_ok[(size_t)i]) flags |= AI_BLOCKF_OWNPOS;
+      int32_t* rec = out->blocks + (int64_t)AI_BLOCK_FIELDS * nb;
+      rec[AI_BLOCK_ROW] = b;
+      rec[AI_BLOCK_START] = (int32_t)s;
+      rec[AI_BLOCK_END] = (int32_t)e;
+      rec[AI_BLOCK_KEY_OFF] = (int32_t)(v.key_base + ks);
+      rec[AI_BLOCK_KV_LO] = (int32_t)kv_lo;
+      rec[AI_BLOCK_FLAGS] = flags;
+      rec[AI_BLOCK_ABS_LO] = (int32_t)abs_lo;
+      rec[AI_BLOCK_ABS_HI] = (int32_t)abs_hi;
+      for (int64_t q0 = s; q0 < e; q0 += fwd_tile) {
+        const int64_t q1 = std::min<int64_t>(q0 + fwd_tile, e);
+        const int64_t cost = (q1 - q0) * std::max<int64_t>(0, std::min(e, q1) - kv_lo);
+        const int32_t group = (flags & AI_BLOCKF_ABS) ? 0 : (q1 - q0 <= fwd_tile / 2 ? 1 : 2);
+        fwd.push_back({cost, nb, (int32_t)q0, (int32_t)q1, group});
+      }
+      ++nb;
+    }
+    out->row_blocks[b + 1] = nb;
+    const int64_t cov = l.n_query;
+    out->row_cov[b] = (int32_t)cov;
+    if (cov < seq_len) all_owned = false;
+    int32_t* qp = out->q_pos + (int64_t)b * seq_len;
+    int32_t* ko = out->k_own + (int64_t)b * seq_len;
+    const uint32_t zero_row = row_of(0);
+    for (int64_t r = 0; r < seq_len; ++r) {
+      qp[r] = (int32_t)(r < cov ? row_of(l.query_pos[r]) : zero_row);
+      ko[r] = v.own[(size_t)r];
+    }
+    pairs += v.pairs;
+    // Key tiles of this row: cost = query rows that see them; whether they
+    // hold an abs key of some block.
+    for (int64_t j0 = 0; j0 < cov; j0 += kv_tile) {
+      const int64_t j1 = std::min<int64_t>(j0 + kv_tile, cov);
+      int64_t cost = 0;
+      bool abs = false;
+      for (int32_t bi = first; bi < nb; ++bi) {
+        const int32_t* rec = out->blocks + (int64_t)AI_BLOCK_FIELDS * bi;
+        const int64_t s = rec[AI_BLOCK_START], e = rec[AI_BLOCK_END];
+        if (!(e > j0 && rec[AI_BLOCK_KV_LO] < j1)) continue;
+        cost += std::max<int64_t>(e - std::max<int64_t>(s, j0), 0);
+        if ((rec[AI_BLOCK_FLAGS] & AI_BLOCKF_ABS) && rec[AI_BLOCK_ABS_LO] < j1 && rec[AI_BLOCK_ABS_HI] > j0) abs = true;
+      }
+      kv.push_back({cost, b, (int32_t)j0, (int32_t)j1, abs});
+    }
+  }
+
+  // Forward items: abs blocks' items, then short items, then the rest;
+  // longest first in each group (stable, so ties keep block order).
+  std::stable_sort(fwd.begin(), fwd.end(), [](const FwdItem& x, const FwdItem& y) {
+    if (x.group != y.group) return x.group < y.group;
+    return x.cost > y.cost;
+  });
+  int32_t n_abs = 0, n_short = 0;
+  for (size_t i = 0; i < fwd.size(); ++i) {
+    out->fwd_items[4 * i] = fwd[i].block;
+    out->fwd_items[4 * i + 1] = fwd[i].q0;
+    out->fwd_items[4 * i + 2] = fwd[i].q1;
+    out->fwd_items[4 * i + 3] = 0;
+    n_abs += fwd[i].group == 0;
+    n_short += fwd[i].group == 1;
+  }
+  std::stable_sort(kv.begin(), kv.end(), [](const KvItem& x, const KvItem& y) {
+    if (x.abs != y.abs) return x.abs;
+    return x.cost > y.cost;
+  });
+  int32_t n_kv_abs = 0;
+  for (size_t i = 0; i < kv.size(); ++i) {
+    out->kv_items[4 * i] = kv[i].row;
+    out->kv_items[4 * i + 1] = kv[i].j0;
+    out->kv_items[4 * i + 2] = kv[i].j1;
+    out->kv_items[4 * i + 3] = 0;
+    n_kv_abs += kv[i].abs;
+  }
+  out->n_fwd_abs_items = n_abs;
+  out->n_fwd_short_items = n_short;
+  out->n_kv_abs_items = n_kv_abs;
+  out->all_rows_owned = all_owned ? 1 : 0;
+  out->pairs_per_head = pairs;
+  return AI_OK;
+}
+
+}  // extern "C"

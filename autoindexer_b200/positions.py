@@ -40,6 +40,7 @@ __all__ = [
     "PositionBlockList",
     "document_blocks",
     "blocks_from_concat",
+    "positions_from_operations",
     "cursor_stream",
 ]
 
@@ -176,6 +177,42 @@ def blocks_from_concat(boundary_indices, query_pos_ids, concat_key_pos_ids, conc
                              start_idx=s, end_idx=e, block_type=None))
     out.concat()
     return out
+
+
+def positions_from_operations(operations, device=None, block_cls=None, list_cls=None) -> PositionBlockList:
+    """The position-block list of an edit chain, built natively
+    (``ai_attn_positions_from_ops``): the same list the reference's
+    ``perturb_labels_per_sequence`` + ``get_parsed_positions_from_perturbations``
+    (``perturb_labels.py:236-275, 395-467``) build from these operations, in
+    one pass over host arrays instead of per-operation device ops with a host
+    sync each.  ``operations``: the ``Operation`` objects
+    ``sample_cursor_operations`` returns, or rows of (num_insert, num_delete,
+    start_rel_pos, end_rel_pos, num_extend).  Returns the concat()-ed list."""
+    import ctypes
+
+    from . import _lib
+
+    rows = [(o.num_insert, o.num_delete, o.start_rel_pos, o.end_rel_pos, o.num_extend) if hasattr(o, "num_insert")
+            else tuple(o) for o in operations]
+    ops = np.ascontiguousarray(np.asarray(rows, dtype=np.int64).reshape(-1, 5))
+    lib = _lib.lib()
+    nb, nq, nk = ctypes.c_int32(0), ctypes.c_int64(0), ctypes.c_int64(0)
+    _lib.check(lib.ai_attn_positions_from_ops_sizes(ops.ctypes.data, ops.shape[0], ctypes.byref(nb), ctypes.byref(nq),
+                                                    ctypes.byref(nk)), "ai_attn_positions_from_ops")
+    bounds = np.empty((nb.value, 4), dtype=np.int64)
+    qpos = np.empty(nq.value, dtype=np.int64)
+    kpos = np.empty(nk.value, dtype=np.int64)
+    attn = np.empty(nk.value, dtype=np.uint8)
+    absm = np.empty(nk.value, dtype=np.uint8)
+    types = np.empty(nb.value, dtype=np.int32)
+    _lib.check(lib.ai_attn_positions_from_ops(ops.ctypes.data, ops.shape[0], bounds.ctypes.data, qpos.ctypes.data,
+                                              kpos.ctypes.data, attn.ctypes.data, absm.ctypes.data,
+                                              types.ctypes.data), "ai_attn_positions_from_ops")
+    lay = blocks_from_concat(bounds, qpos, kpos, attn.astype(bool), absm.astype(bool), block_cls=block_cls,
+                             list_cls=list_cls, device=device)
+    for blk, t in zip(lay, types):
+        blk.block_type = BlockType(int(t))
+    return lay
 
 
 def cursor_stream(n: int, rng: np.random.Generator, p_step: float = 0.8) -> np.ndarray:

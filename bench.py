@@ -442,6 +442,19 @@ def run_ours(args):
     e2e_value = job_tflops(job_flops, args.steps, t_e2e)
     assert read_status(dev) == 0
 
+    # Layout compile per new position-block list (a training step builds one):
+    # fresh list objects (no cache), native tables, one copy to the device,
+    # the rotary table from the module on the device; median of three.
+    t_layouts = []
+    for _ in range(3):
+        fresh = build_workload(args.config, seed=0, device=dev).rows
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        compile_layout(fresh, Bw, Tw, D, torch.bfloat16, wl.rope, dev)
+        torch.cuda.synchronize(dev)
+        t_layouts.append((time.perf_counter() - t0) * 1e3)
+    layout_ms = float(np.median(t_layouts))
+
     peak, peak_sus, peak_kind = peaks()
     # Dominant kernel: algorithmic FLOPs per launch (per query head and finite
     # (query, key) pair: forward 4·D, dQ 6·D — S, dP, dQ — and dK/dV 8·D — S,
@@ -487,6 +500,7 @@ def run_ours(args):
         "e2e": {"value": round(e2e_value, 3), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
         "gpu_launches": int(round(launches_per_step * args.steps)),
+        "layout_compile_ms": round(layout_ms, 3),
         "clocks": clocks.summary(),
     }
     if gather_ms is not None:

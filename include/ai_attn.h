@@ -247,6 +247,83 @@ int ai_attn_decode_workspace(const AiAttnDecodeArgs* args, size_t* bytes);
 /* out = softmax(scale * q . R(pos_j) k_j masked) . v, per (row, query head). */
 int ai_attn_decode(const AiAttnDecodeArgs* args, void* stream);
 
+/* ------------------------------------------------------------------------
+ * Host-side layout builders (plain host memory, no GPU, no allocation by the
+ * caller's device).
+ *
+ *   ai_attn_positions_from_ops <- perturb_labels.py:236-275 perturb_labels_per_sequence,
+ *                                 :395-467 get_parsed_positions_from_perturbations and
+ *                                 :341-357 PositionBlockList.concat(): an edit chain (the
+ *                                 operations sample_cursor_operations returns, in order) ->
+ *                                 the concat()-ed arrays of its position-block list.
+ *   ai_attn_prep               <- the device tables the backends build per layout
+ *                                 (triton_rope_attn.py:1012-1055 build_multi_segment_launch_cache,
+ *                                 cutedsl/meta.py:66-98 build_cutedsl_meta): concat()-ed lists ->
+ *                                 the AiAttnLayout tables, written into host buffers for one
+ *                                 host-to-device copy.  The rotary table for positions
+ *                                 [p_min, p_max] is the caller's (it comes from its rotary module).
+ * ------------------------------------------------------------------------ */
+#define AI_BLOCK_TYPE_EXTEND 1
+#define AI_BLOCK_TYPE_EDIT 2
+#define AI_BLOCK_TYPE_COMPLETE 3
+
+/* Sizes of the list an edit chain yields.  ops: n_ops rows of five int64
+ * (num_insert, num_delete, start_rel_pos, end_rel_pos, num_extend); the first
+ * must be a pure extend.  AI_ERR_LAYOUT for a chain the reference rejects. */
+int ai_attn_positions_from_ops_sizes(const int64_t* ops, int32_t n_ops, int32_t* n_blocks, int64_t* n_query,
+                                     int64_t* n_keys);
+/* boundary [n_blocks][4] (start, end, key_start, key_end); query_pos [n_query];
+ * key_pos, attn_mask, abs_mask [n_keys]; block_type [n_blocks] (AI_BLOCK_TYPE_*,
+ * may be NULL). */
+int ai_attn_positions_from_ops(const int64_t* ops, int32_t n_ops, int64_t* boundary, int64_t* query_pos,
+                               int64_t* key_pos, uint8_t* attn_mask, uint8_t* abs_mask, int32_t* block_type);
+
+/* One concat()-ed position-block list (perturb_labels.py:341-357), host memory. */
+typedef struct AiPrepList {
+  int32_t n_blocks;
+  const int64_t* boundary;    /* [n_blocks][4]: start, end, key_start, key_end */
+  int64_t n_query;            /* entries of query_pos: the last block's end */
+  const int64_t* query_pos;
+  int64_t n_keys;             /* entries of the key arrays: the last block's key_end */
+  const int64_t* key_pos;
+  const uint8_t* attn_mask;
+  const uint8_t* abs_mask;    /* NULL: no abs keys */
+} AiPrepList;
+
+typedef struct AiPrepSizes {
+  int32_t n_blocks;           /* block records over the batch */
+  int32_t n_fwd_items;
+  int32_t n_kv_items;
+  int64_t n_keys;             /* key words (sum over the distinct lists) */
+  int64_t p_min, p_max;       /* position ids the rotary table must cover (row r = position p_min + r) */
+} AiPrepSizes;
+
+/* Host buffers for ai_attn_prep, sized from AiPrepSizes; the counts and
+ * flags come back in the last fields.  Copied to the device they are the
+ * AiAttnLayout tables of the same names. */
+typedef struct AiPrepTables {
+  int32_t* blocks;            /* [n_blocks][AI_BLOCK_FIELDS] */
+  int32_t* row_blocks;        /* [batch + 1] */
+  int32_t* row_cov;           /* [batch] */
+  int32_t* key_info;          /* [n_keys] */
+  int32_t* q_pos;             /* [batch][seq_len] */
+  int32_t* k_own;             /* [batch][seq_len] */
+  int32_t* fwd_items;         /* [n_fwd_items][4] */
+  int32_t* kv_items;          /* [n_kv_items][4] */
+  int32_t n_fwd_abs_items;
+  int32_t n_fwd_short_items;
+  int32_t n_kv_abs_items;
+  int32_t all_rows_owned;
+  int64_t pairs_per_head;     /* finite (query, key) logits of one head over the batch */
+} AiPrepTables;
+
+/* lists: n_lists distinct lists; list_of_row[b]: the list batch row b uses.
+ * fwd_tile / kv_tile: ai_attn_fwd_tile_rows / ai_attn_kv_tile_rows. */
+int ai_attn_prep_sizes(const AiPrepList* lists, int32_t n_lists, const int32_t* list_of_row, int32_t batch,
+                       int32_t seq_len, int32_t fwd_tile, int32_t kv_tile, AiPrepSizes* sizes);
+int ai_attn_prep(const AiPrepList* lists, int32_t n_lists, const int32_t* list_of_row, int32_t batch,
+                 int32_t seq_len, int32_t fwd_tile, int32_t kv_tile, AiPrepTables* out);
+
 /* Synchronises the stream, copies the device status word to *host_out and
  * resets it to AI_OK.  For tests and debugging; not needed on the hot path. */
 int ai_attn_read_status(int32_t* dev_status, void* stream, int32_t* host_out);

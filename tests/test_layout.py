@@ -1,6 +1,8 @@
 """Layout compiler (``autoindexer_b200.meta``): the device tables the kernels
 read, built on the CPU from reference-format position-block lists."""
 
+import os
+
 import numpy as np
 import pytest
 import torch
@@ -179,3 +181,58 @@ def test_blocks_from_concat_inverts_concat():
     assert np.array_equal(lay.concat_key_pos_ids.numpy(), g["concat_key_pos_ids"])
     assert np.array_equal(lay.concat_attn_masks.numpy(), g["concat_attn_masks"])
     assert np.array_equal(lay.concat_abs_pos_masks.numpy(), g["concat_abs_pos_masks"])
+
+
+@pytest.mark.parametrize("case", [f"op{i}" for i in range(10)] + ["chain_e"])
+def test_positions_from_operations_match_reference(case):
+    """The native edit-chain builder reproduces the layouts the reference's
+    get_parsed_positions_from_perturbations built from the same operations
+    (the ten operation_tuples.json cases and the +E chain)."""
+    from conftest import GOLDEN
+    from autoindexer_b200 import positions_from_operations
+
+    with np.load(os.path.join(GOLDEN, "ops_cases.npz")) as z:
+        ops = z[case]
+    g = load_golden(case if case == "chain_e" else f"{case}_d32")
+    lay = positions_from_operations(ops)
+    assert np.array_equal(np.asarray(lay.boundary_indices), g["boundary_indices"])
+    assert np.array_equal(lay.query_pos_ids.numpy(), g["query_pos_ids"])
+    assert np.array_equal(lay.concat_key_pos_ids.numpy(), g["concat_key_pos_ids"])
+    assert np.array_equal(lay.concat_attn_masks.numpy(), g["concat_attn_masks"])
+    assert np.array_equal(lay.concat_abs_pos_masks.numpy(), g["concat_abs_pos_masks"])
+
+
+def test_positions_from_operations_rejects_invalid_chains():
+    from autoindexer_b200 import positions_from_operations
+
+    with pytest.raises(RuntimeError):
+        positions_from_operations([(3, 0, 0, 0, 5)])  # an edit cannot open the sequence
+    with pytest.raises(RuntimeError):
+        positions_from_operations([(0, 0, 0, 0, 5), (1, 1, 4, 9, 0)])  # cursor range past the text
+
+
+@pytest.mark.parametrize("which", ["golden", "bench1", "benchE", "bench4"])
+def test_native_tables_match_numpy_restatement(which):
+    """ai_attn_prep (the native builder behind compile_layout) gives the
+    tables of the numpy restatement in tests/layout_numpy.py, on every golden
+    layout (shared by two rows) and on the benchmark layouts."""
+    import layout_numpy as LN
+
+    if which == "golden":
+        cases = []
+        for name in golden_names():
+            g = load_golden(name)
+            cases.append((ArrayLayout.from_golden(g), 2, int(g["T"]) + 5, golden_rope(g)[0], int(g["D"])))
+    else:
+        import bench
+
+        wl = bench.build_workload(which[5:], 0, "cpu")
+        cases = [(wl.rows, wl.batch, wl.seq_len, wl.rope, 128)]
+    for lay, B, T, mod, D in cases:
+        c = compile_layout(lay, B, T, D, torch.bfloat16, mod, "cpu")
+        want = LN.host_tables(lay, B, T, c.fwd_tile, c.kv_tile)
+        for name in ("blocks", "row_blocks", "row_cov", "key_info", "q_pos", "k_own", "fwd_items", "kv_items"):
+            assert np.array_equal(getattr(c, name).numpy(), np.asarray(want[name]).reshape(getattr(c, name).shape)), name
+        for name in ("n_fwd_abs_items", "n_kv_abs_items", "n_fwd_short_items", "pairs_per_head", "all_rows_owned",
+                     "p_min", "n_pos"):
+            assert getattr(c, name) == want[name], name
