@@ -19,6 +19,7 @@ from .meta import CompiledLayout, RowLayouts, compile_layout
 from .positions import (BlockType, PositionBlock, PositionBlockList, blocks_from_concat, cursor_stream,
                         document_blocks, positions_from_operations)
 from .decode import decode_attention
+from .index_head import compute_index_losses_b200
 from .prefill import plain_causal_attn_b200, prefill_attention_interface, prefill_layout
 from .rope import SectionedRope, default_inv_freq
 
@@ -41,6 +42,7 @@ __all__ = [
     "blocks_from_concat",
     "positions_from_operations",
     "decode_attention",
+    "compute_index_losses_b200",
     "plain_causal_attn_b200",
     "prefill_attention_interface",
     "prefill_layout",

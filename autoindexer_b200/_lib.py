@@ -55,6 +55,8 @@ EXPORTED_SYMBOLS = (
     "ai_attn_positions_from_ops",
     "ai_attn_prep_sizes",
     "ai_attn_prep",
+    "ai_index_fwd",
+    "ai_index_bwd",
 )
 
 _i32p = ctypes.POINTER(ctypes.c_int32)
@@ -156,6 +158,40 @@ class AiAttnDecodeArgs(ctypes.Structure):
     ]
 
 
+class AiIndexArgs(ctypes.Structure):
+    _fields_ = [
+        ("batch", ctypes.c_int32),
+        ("seq_len", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
+        ("dtype", ctypes.c_int32),
+        ("scale", ctypes.c_float),
+        ("q", AiTensor4),
+        ("k", AiTensor4),
+        ("n_rows", ctypes.c_int32),
+        ("rows", ctypes.c_void_p),
+        ("targets", ctypes.c_void_p),
+        ("n_keys", ctypes.c_int64),
+        ("key_rows", ctypes.c_void_p),
+        ("key_ok", ctypes.c_void_p),
+        ("rope_cos", ctypes.c_void_p),
+        ("rope_sin", ctypes.c_void_p),
+        ("n_pos", ctypes.c_int32),
+        ("logits", ctypes.c_void_p),
+        ("lse", ctypes.c_void_p),
+        ("loss", ctypes.c_void_p),
+        ("status", ctypes.c_void_p),
+    ]
+
+
+class AiIndexBwdArgs(ctypes.Structure):
+    _fields_ = [
+        ("fwd", AiIndexArgs),
+        ("dloss", ctypes.c_void_p),
+        ("dq", AiTensor4),
+        ("dk", AiTensor4),
+    ]
+
+
 class AiPrepList(ctypes.Structure):
     _fields_ = [
         ("n_blocks", ctypes.c_int32),
@@ -243,6 +279,10 @@ def _bind(handle):
     handle.ai_attn_prep_sizes.argtypes = [P(AiPrepList), i32, vp, i32, i32, i32, i32, P(AiPrepSizes)]
     handle.ai_attn_prep.restype = ctypes.c_int
     handle.ai_attn_prep.argtypes = [P(AiPrepList), i32, vp, i32, i32, i32, i32, P(AiPrepTables)]
+    handle.ai_index_fwd.restype = ctypes.c_int
+    handle.ai_index_fwd.argtypes = [P(AiIndexArgs), vp]
+    handle.ai_index_bwd.restype = ctypes.c_int
+    handle.ai_index_bwd.argtypes = [P(AiIndexBwdArgs), vp]
     return handle
 
 

@@ -16,7 +16,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "_ai_attn.so")
 SOURCES = ["ai_capi.cu", "ai_attn_simt.cu", "ai_attn_fwd_sm100.cu", "ai_attn_bwd_sm100.cu", "ai_prerot.cu",
-           "ai_noalloc.cu", "ai_profile.cu", "ai_decode.cu", "ai_selftest.cu", "ai_prep.cpp"]
+           "ai_noalloc.cu", "ai_profile.cu", "ai_decode.cu", "ai_selftest.cu", "ai_index.cu", "ai_prep.cpp"]
 FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-lineinfo", "-std=c++17",

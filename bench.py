@@ -402,11 +402,14 @@ def run_ours(args):
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(dev)
+    if sharded:
+        bufs.gather_ms()  # forget the warm-up's gathers
     with ClockSampler(local) as clocks:
         for i in range(args.steps):
             flush.fill_(float(i))
             step(ev[i])
         torch.cuda.synchronize(dev)
+    gather_ms = bufs.gather_ms() if sharded else None
     if world > 1:
         dist.barrier()
     t_fwd = sum(a.elapsed_time(b) for a, b, _ in ev) / 1e3
@@ -426,9 +429,6 @@ def run_ours(args):
             flush.fill_(float(i))
             step()
         torch.cuda.synchronize(dev)
-    gather_ms = None
-    if sharded:
-        gather_ms = bufs.gather_ms()
 
     # End to end through the public API.
     if sharded:
@@ -966,10 +966,27 @@ def run_train(args):
     model.train()
     n_params = sum(p.numel() for p in model.parameters())
     n_embed = model.model.embed_tokens.weight.numel() + model.lm_head.weight.numel()
-    net = model
+
+    class LossStep(nn.Module):
+        """The loss of one sequence; the position-block list and the rotary
+        function are held here and passed to the backbone inside forward (as
+        AutoIndexerModelBase.decode passes the lists it builds), so that DDP's
+        input handling never sees them."""
+
+        def __init__(self, m):
+            super().__init__()
+            self.m = m
+            self.layout = None
+            object.__setattr__(self, "rope", None)  # not a submodule: its tables are not DDP buffers
+
+        def forward(self, ids):
+            return self.m(input_ids=ids, labels=ids, parsed_positions=self.layout, rotary_emb=self.rope).loss
+
+    step_mod = LossStep(model)
+    net = step_mod
     if world > 1:
-        net = nn.parallel.DistributedDataParallel(model, device_ids=[local], gradient_as_bucket_view=True,
-                                                  bucket_cap_mb=256)
+        net = nn.parallel.DistributedDataParallel(step_mod, device_ids=[local], gradient_as_bucket_view=True,
+                                                  bucket_cap_mb=256, broadcast_buffers=False)
     opt = torch.optim.AdamW(model.parameters(), lr=1e-4, weight_decay=0.0, fused=True)
 
     rng = np.random.default_rng(100 + rank)
@@ -984,14 +1001,16 @@ def run_train(args):
     layout = ab.RowLayouts([ab.document_blocks([TRAIN_T], position_ids=np.arange(TRAIN_T))])
     loss_host = torch.empty((), dtype=torch.float32).pin_memory()
     stream = torch.cuda.current_stream(dev)
+    step_mod.layout = layout
+    object.__setattr__(step_mod, "rope", rope)
 
     def step():
         ids_dev.copy_(ids_host, non_blocking=True)
-        out = net(input_ids=ids_dev, labels=ids_dev, parsed_positions=layout, rotary_emb=rope)
-        out.loss.backward()
+        loss = net(ids_dev)
+        loss.backward()
         opt.step()
         opt.zero_grad(set_to_none=True)
-        loss_host.copy_(out.loss.detach().float(), non_blocking=True)
+        loss_host.copy_(loss.detach().float(), non_blocking=True)
 
     for _ in range(args.warmup):
         step()

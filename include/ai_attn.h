@@ -248,6 +248,52 @@ int ai_attn_decode_workspace(const AiAttnDecodeArgs* args, size_t* bytes);
 int ai_attn_decode(const AiAttnDecodeArgs* args, void* stream);
 
 /* ------------------------------------------------------------------------
+ * Index-head cursor attention (the edit-cursor losses of the index head).
+ *
+ *   ai_index_fwd / ai_index_bwd <- attn_layers.py:40-110 compute_index_losses (with
+ *                                  :15-27 compute_attn_weights_iter and :30-37
+ *                                  compute_end_index_mask): per edit a start row (head 0) and
+ *                                  an end row (head 1), each q . R(rel_j) k_j over a key prefix,
+ *                                  masked, scaled, -log_softmax at the cursor key.  The
+ *                                  reference runs a Python loop of small torch ops per edit;
+ *                                  here one launch runs every row (forward) and two launches
+ *                                  the backward, without atomics.
+ * ------------------------------------------------------------------------ */
+typedef struct AiIndexArgs {
+  int32_t batch;
+  int32_t seq_len;
+  int32_t head_dim;          /* 32, 64 or 128 */
+  int32_t dtype;             /* AI_DTYPE_BF16 or AI_DTYPE_F32 (q, k, dq, dk) */
+  float scale;
+  AiTensor4 q;               /* (B, 2, T, D) index-head queries, unrotated */
+  AiTensor4 k;               /* (B, 2, T, D) index-head keys, unrotated */
+  int32_t n_rows;            /* index rows (two per edit) */
+  const int32_t* rows;       /* [n_rows][4]: head, query row, n (the row sees keys [0, n)),
+                                offset of its keys in key_rows / key_ok / logits */
+  const int32_t* targets;    /* [n_rows]: the cursor key of the row, in [0, n) */
+  int64_t n_keys;            /* entries of key_rows / key_ok (sum of n over the rows) */
+  const int32_t* key_rows;   /* rotary table row of each key's position relative to the query */
+  const uint8_t* key_ok;     /* 1: the key may be attended */
+  const float* rope_cos;     /* [n_pos][D/2] */
+  const float* rope_sin;
+  int32_t n_pos;
+  float* logits;             /* [B][n_keys] out: scaled logits, -inf where masked (read by the backward) */
+  float* lse;                /* [B][n_rows] out: log-sum-exp of the row */
+  float* loss;               /* [B][n_rows] out: lse - logit at the target (+inf if the target is masked) */
+  int32_t* status;           /* optional device status word */
+} AiIndexArgs;
+
+typedef struct AiIndexBwdArgs {
+  AiIndexArgs fwd;           /* as the forward ran, its outputs included */
+  const float* dloss;        /* [B][n_rows]: dL/dloss */
+  AiTensor4 dq;              /* (B, 2, T, D): the index rows are written, the other rows are left as they are */
+  AiTensor4 dk;              /* (B, 2, T, D): every row is written */
+} AiIndexBwdArgs;
+
+int ai_index_fwd(const AiIndexArgs* args, void* stream);
+int ai_index_bwd(const AiIndexBwdArgs* args, void* stream);
+
+/* ------------------------------------------------------------------------
  * Host-side layout builders (plain host memory, no GPU, no allocation by the
  * caller's device).
  *

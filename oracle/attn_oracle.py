@@ -59,6 +59,8 @@ __all__ = [
     "attn_backward",
     "count_pairs",
     "attn_chunked",
+    "index_rows",
+    "index_losses",
 ]
 
 
@@ -412,6 +414,81 @@ def attn_chunked(q, k, v, dout, layout, rope, scale=None, dtype=np.float64, chun
     if not backward:
         return out, lse, None, None, None
     return out, lse, dq, dk, dv
+
+
+# ---------------------------------------------------------------------------
+# Index head: edit-cursor losses
+# ---------------------------------------------------------------------------
+
+BLOCK_EXTEND = 1
+
+
+def index_rows(layout, block_type, edits, editable_start=0):
+    """The rows of ``compute_index_losses`` (``attn_layers.py:40-110``): for
+    every EXTEND block (an edit; its last row is the edit marker ``ed``) a
+    start row (head 0, query ``ed - 1``, keys ``[0, ed)`` at positions
+    ``key_pos[:-1] - query_pos[-2]``, attended where ``attn_mask[:-1] &
+    key_pos >= editable_start``) and an end row (head 1, query ``ed``, keys
+    ``[0, ed]`` at ``key_pos - query_pos[-1]``, attended where ``attn_mask &
+    key_pos >= editable_start`` and the relative position is > 0,
+    ``compute_end_index_mask`` ``:30-37``).  ``edits``: rows of (edit marker
+    index, start cursor, end cursor).  Returns a list of
+    ``(head, query_row, rel_pos, ok, target, edit)``."""
+    bounds, qpos, kpos, am, _ = _layout_arrays(layout)
+    cursor = {int(e): (int(s), int(t)) for e, s, t in np.asarray(edits).reshape(-1, 3)}
+    rows = []
+    for bi, (s, e, ks, ke) in enumerate(bounds):
+        if int(block_type[bi]) != BLOCK_EXTEND:
+            continue
+        ed = e - 1
+        kp, att, qp = kpos[ks:ke], am[ks:ke], qpos[s:e]
+        tgt_s, tgt_e = cursor[ed]
+        rel = kp[:-1] - qp[-2]
+        rows.append((0, ed - 1, rel, att[:-1] & (kp[:-1] >= editable_start), tgt_s, ed))
+        rel = kp - qp[-1]
+        rows.append((1, ed, rel, att & (kp >= editable_start) & (rel > 0), tgt_e, ed))
+    return rows
+
+
+def index_losses(q, k, layout, block_type, edits, rope, scale=None, editable_start=0, w_start=1.0, w_end=1.0,
+                 dtype=np.float64):
+    """Restates ``compute_index_losses`` (``attn_layers.py:40-110``) with
+    ``compute_attn_weights_iter`` (``:15-27``: the query unrotated, every key
+    rotated by its relative position, masked keys ``-inf``, times ``scale``):
+    ``start_loss`` / ``end_loss`` are the means over the batch of
+    ``-log_softmax`` at the cursor key, averaged over the edits.  Also
+    returns the gradients of ``w_start * start_loss + w_end * end_loss`` with
+    respect to ``q`` and ``k`` (``(B, 2, T, D)``), written out by hand:
+    ``dlogit_j = w * (softmax_j - [j == target]) / (B * n_edits)``,
+    ``dq = scale sum_j dlogit_j R(rel_j) k_j``,
+    ``dk_j = scale dlogit_j R(rel_j)^T q``."""
+    q, k = (_np(t).astype(dtype) for t in (q, k))
+    B, H, T, D = q.shape
+    assert H == 2
+    if scale is None:
+        scale = D ** -0.5
+    rows = index_rows(layout, block_type, edits, editable_start)
+    n_edits = len(rows) // 2
+    dq = np.zeros_like(q)
+    dk = np.zeros_like(k)
+    totals = [0.0, 0.0]
+    for h, qi, rel, ok, tgt, _ in rows:
+        n = rel.shape[0]
+        cos, sin = rope(rel)
+        kr = apply_cos_sin(k[:, h, :n, :], cos, sin)  # (B, n, D)
+        w = np.einsum("bd,bnd->bn", q[:, h, qi, :], kr) * scale
+        w = np.where(ok[None, :], w, -np.inf)
+        p, lse = _softmax(w)
+        totals[h] += float(np.mean(lse - w[:, tgt]))
+        weight = (w_start if h == 0 else w_end) / (B * max(n_edits, 1))
+        g = p.copy()
+        g[:, tgt] -= 1.0
+        g = np.where(ok[None, :], g * weight, 0.0)  # masked logits are constants (masked_fill)
+        dq[:, h, qi, :] += scale * np.einsum("bn,bnd->bd", g, kr)
+        dk[:, h, :n, :] += scale * apply_cos_sin_T(g[:, :, None] * q[:, h, qi, None, :], cos, sin)
+    if n_edits > 0:
+        totals = [t / n_edits for t in totals]
+    return totals[0], totals[1], dq, dk
 
 
 # ---------------------------------------------------------------------------

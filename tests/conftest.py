@@ -28,7 +28,7 @@ def golden_names():
     """The chain-of-edits golden cases (not the known-answer tables or the
     decode-step vectors)."""
     return sorted(f[:-4] for f in os.listdir(GOLDEN)
-                  if f.endswith(".npz") and not f.startswith(("kat_", "decode_", "ops_")))
+                  if f.endswith(".npz") and not f.startswith(("kat_", "decode_", "ops_", "index_")))
 
 
 def load_golden(name):

@@ -17,7 +17,7 @@ HEADER = os.path.join(ROOT, "include", "ai_attn.h")
 def declared_functions():
     text = open(HEADER).read()
     text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
-    return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\s*\*?\s*(ai_attn_\w+)\s*\(", text, flags=re.M)))
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\s*\*?\s*(ai_\w+)\s*\(", text, flags=re.M)))
 
 
 def test_library_exports_every_declared_function():

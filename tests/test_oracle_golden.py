@@ -95,3 +95,23 @@ def test_chunked_oracle_matches_dense_oracle(name):
     for label, a, b in zip(("out", "lse", "dq", "dk", "dv"), got, want):
         np.testing.assert_allclose(a, b, rtol=1e-10, atol=1e-10, err_msg=f"{name}:{label}")
     np.testing.assert_allclose(got[0], g["out"], rtol=2e-5, atol=2e-5)
+
+
+@pytest.mark.parametrize("case", range(10))
+@pytest.mark.parametrize("es", [0, 3])
+def test_index_loss_oracle_matches_reference(case, es):
+    """The index-head oracle reproduces the reference's compute_index_losses
+    (attn_layers.py:40-110) and its autograd gradients on the reference's own
+    operation cases (tests/golden/make_index_golden.py), editable_start 0 and 3."""
+    g = load_golden(f"index_op{case}")
+    lay = ArrayLayout.from_golden(g)
+    rope = O.make_rope(g["inv_freq"])
+    from golden_inputs import make_inputs
+
+    q, k, _, _ = make_inputs(int(g["seed"]), int(g["B"]), 2, 2, int(g["T"]), int(g["D"]))
+    sl, el, dq, dk = O.index_losses(q, k, lay, g["block_type"], g["cursor_edits"], rope, editable_start=es,
+                                    w_start=1.0, w_end=2.0)
+    np.testing.assert_allclose(sl, g[f"start_loss_es{es}"], rtol=1e-6)
+    np.testing.assert_allclose(el, g[f"end_loss_es{es}"], rtol=1e-6)
+    np.testing.assert_allclose(dq, g[f"dq_es{es}"], rtol=2e-5, atol=2e-6)
+    np.testing.assert_allclose(dk, g[f"dk_es{es}"], rtol=2e-5, atol=2e-6)
