@@ -32,7 +32,7 @@ LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_ai_attn.so
 DTYPE_BF16, DTYPE_F16, DTYPE_F32 = 0, 1, 2
 # AiProfKind, in order.
 PROF_KINDS = ("prerot", "fwd", "fwd_fill", "delta", "dq", "dkdv", "bwd_fill", "simt", "decode")
-ABI_VERSION = 7
+ABI_VERSION = 8
 
 # Every function include/ai_attn.h declares.
 EXPORTED_SYMBOLS = (
@@ -96,6 +96,13 @@ class AiAttnLayout(ctypes.Structure):
         ("n_kv_abs_items", ctypes.c_int32),
         ("all_rows_owned", ctypes.c_int32),
         ("n_fwd_short_items", ctypes.c_int32),
+        ("kv_chunks", ctypes.c_void_p),
+        ("n_kv_chunks", ctypes.c_int32),
+        ("n_kv_partials", ctypes.c_int32),
+        ("kv_reduce", ctypes.c_void_p),
+        ("n_kv_reduce", ctypes.c_int32),
+        ("kv_cost_max", ctypes.c_int32),
+        ("kv_cost_total", ctypes.c_int32),
     ]
 
 
@@ -210,6 +217,8 @@ class AiPrepSizes(ctypes.Structure):
         ("n_blocks", ctypes.c_int32),
         ("n_fwd_items", ctypes.c_int32),
         ("n_kv_items", ctypes.c_int32),
+        ("n_kv_chunks", ctypes.c_int32),
+        ("n_kv_reduce", ctypes.c_int32),
         ("n_keys", ctypes.c_int64),
         ("p_min", ctypes.c_int64),
         ("p_max", ctypes.c_int64),
@@ -226,6 +235,11 @@ class AiPrepTables(ctypes.Structure):
         ("k_own", ctypes.c_void_p),
         ("fwd_items", ctypes.c_void_p),
         ("kv_items", ctypes.c_void_p),
+        ("kv_chunks", ctypes.c_void_p),
+        ("kv_reduce", ctypes.c_void_p),
+        ("n_kv_partials", ctypes.c_int32),
+        ("kv_cost_max", ctypes.c_int32),
+        ("kv_cost_total", ctypes.c_int32),
         ("n_fwd_abs_items", ctypes.c_int32),
         ("n_fwd_short_items", ctypes.c_int32),
         ("n_kv_abs_items", ctypes.c_int32),

@@ -1372,12 +1372,16 @@ constexpr long long kWait = 1000000000LL;
 // role); with skip_abs, only the blocks with no abs key among [j0, j1)
 // (the others go to the abs pass, dkdv_kernel with abs_only, which adds its
 // part afterwards).
+//
+// The 64-row query tiles of the blocks it yields are numbered in order; with
+// a chunk [qt0, qt1) only the blocks holding some of those tiles are yielded,
+// and [lq0, lq1) are the block's own tiles of the chunk.
 struct BlockIter {
   const AiAttnLayout* L;
-  int b, j0, j1, bi, end;
+  int b, j0, j1, bi, end, qt0, qt1, qcum = 0, lq0 = 0, lq1 = 0;
   bool skip_abs;
-  __device__ BlockIter(const AiAttnLayout* L_, int b_, int j0_, int j1_, bool skip_abs_)
-      : L(L_), b(b_), j0(j0_), j1(j1_), skip_abs(skip_abs_) {
+  __device__ BlockIter(const AiAttnLayout* L_, int b_, int j0_, int j1_, bool skip_abs_, int qt0_, int qt1_)
+      : L(L_), b(b_), j0(j0_), j1(j1_), qt0(qt0_), qt1(qt1_), skip_abs(skip_abs_) {
     bi = L->row_blocks[b] - 1;
     end = L->row_blocks[b + 1];
   }
@@ -1386,6 +1390,11 @@ struct BlockIter {
       blk = load_block(L->blocks, bi);
       if (blk.e <= j0 || blk.kv_lo >= j1 || max(blk.s, j0) >= blk.e) continue;
       if (skip_abs && blk.abs_in(j0, j1)) continue;
+      const int nq = (blk.e - max(blk.s, j0) + kvw::BQ - 1) / kvw::BQ, c0 = qcum;
+      qcum += nq;
+      lq0 = max(qt0, c0) - c0;
+      lq1 = min(qt1, c0 + nq) - c0;
+      if (lq0 >= lq1) continue;
       return true;
     }
     return false;
@@ -1396,7 +1405,8 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
     dkdv_ws_kernel(const AiAttnBwdArgs a, const float* __restrict__ delta, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_q,
                    const __grid_constant__ CUtensorMap tm_do, const __grid_constant__ CUtensorMap tm_kr,
-                   const int prerot, const int item_base, const int skip_abs) {
+                   const int prerot, const int item_base, const int skip_abs, const int32_t* __restrict__ chunks,
+                   float* __restrict__ partials) {
   using namespace kvw;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = tile::align1024(smem_raw);
@@ -1409,7 +1419,17 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
 
   const AiAttnFwdArgs& f = a.fwd;
   const AiAttnLayout& L = f.layout;
-  const int32_t* item = L.kv_items + 4 * (int64_t)(item_base + blockIdx.x);
+  // A CTA runs one key tile whole, or one chunk of its query tiles when the
+  // tile is split (kv_chunks): then it writes fp32 partial sums to `partials`.
+  int it_idx = item_base + (int)blockIdx.x, qt0 = 0, qt1 = 0x7fffffff, slot = -1;
+  if (chunks) {
+    const int32_t* c = chunks + 4 * (int64_t)blockIdx.x;
+    it_idx = c[0];
+    qt0 = c[1];
+    qt1 = c[2];
+    slot = c[3];
+  }
+  const int32_t* item = L.kv_items + 4 * (int64_t)it_idx;
   const int b = item[0], j0 = item[1], j1 = item[2];
   const int hk = blockIdx.y, G = f.num_q_heads / f.num_kv_heads;
   const __half2* cs16 = static_cast<const __half2*>(L.rope_cs16);
@@ -1445,7 +1465,8 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
     }
     return true;
   };
-  auto n_steps_of = [&](const Block& blk) { return ((blk.e - max(blk.s, j0) + BQ - 1) / BQ) * G; };
+  // Steps of the current block of an iterator: its query tiles in the chunk x the group's heads.
+  auto n_steps_of = [&](const BlockIter& bit) { return (bit.lq1 - bit.lq0) * G; };
 
   if (warp < 4 * kGroups) {
     // ------------------------------------------------------------ score groups
@@ -1453,7 +1474,7 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
     const uint32_t lane_base = (uint32_t)((warp % 4) * 32) << 16;
     const float sl2 = f.scale * kLog2e, scale = f.scale;
     const float2 sl2x2 = make_float2(sl2, sl2), scalex2 = make_float2(scale, scale);
-    BlockIter it(&L, b, j0, j1, skip_abs != 0);
+    BlockIter it(&L, b, j0, j1, skip_abs != 0, qt0, qt1);
     Block blk;
     int s = 0, nb = 0;
     bool any = false;
@@ -1463,9 +1484,9 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
       uint32_t info = 0;
       if (j < kmax) info = (uint32_t)__ldg(L.key_info + blk.key_off + j);
       const bool key_ok = (info & AI_KEY_ATTN) != 0;
-      const int nsteps = n_steps_of(blk);
+      const int nsteps = n_steps_of(it);
       for (int st = 0; st < nsteps; ++st, ++s) {
-        const int x = s & 1, qslot = s % kQS, q0 = qs + (st / G) * BQ, q1 = min(q0 + BQ, blk.e);
+        const int x = s & 1, qslot = s % kQS, q0 = qs + (it.lq0 + st / G) * BQ, q1 = min(q0 + BQ, blk.e);
         if (!wait(Q_READY + qslot, (s / kQS) & 1) || !wait(S_FULL + x, (s >> 1) & 1)) break;
         ptx::tc_fence_after();
         // This group's 16 query columns of the step: c0 + [0, 16).
@@ -1558,13 +1579,20 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
           static_cast<__nv_bfloat16*>(a.dk.ptr) + b * a.dk.stride_b + hk * a.dk.stride_h + (int64_t)j * a.dk.stride_t;
       __nv_bfloat16* dv_row =
           static_cast<__nv_bfloat16*>(a.dv.ptr) + b * a.dv.stride_b + hk * a.dv.stride_h + (int64_t)j * a.dv.stride_t;
+      // A chunk of a split key tile leaves fp32 partial sums instead:
+      // [slot][kv head][dK, dV][key][d].
+      float* part = slot >= 0 ? partials + (((int64_t)slot * f.num_kv_heads + hk) * 2) * (BN * D) + lrow * D : nullptr;
 #pragma unroll
       for (int h2 = 0; h2 < 2; ++h2) {
         const int d0 = kCols * t + 64 * h2;
         float v[kCols];
 #pragma unroll
         for (int x = 0; x < kCols; ++x) v[x] = s_dk[(d0 + x) * BN + lrow];
-        if (j < j1) {
+        if (j < j1 && part) {
+#pragma unroll
+          for (int x = 0; x < kCols; x += 4)
+            *reinterpret_cast<float4*>(part + d0 + x) = make_float4(v[x], v[x + 1], v[x + 2], v[x + 3]);
+        } else if (j < j1) {
           *reinterpret_cast<uint4*>(dk_row + d0) = tile::pack8(*reinterpret_cast<const float(*)[8]>(v));
           *reinterpret_cast<uint4*>(dk_row + d0 + 8) = tile::pack8(*reinterpret_cast<const float(*)[8]>(v + 8));
         }
@@ -1575,7 +1603,11 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
         }
 #pragma unroll
         for (int x = 0; x < kCols; ++x) v[x] = any ? __uint_as_float(rr[x]) : 0.f;
-        if (j < j1) {
+        if (j < j1 && part) {
+#pragma unroll
+          for (int x = 0; x < kCols; x += 4)
+            *reinterpret_cast<float4*>(part + BN * D + d0 + x) = make_float4(v[x], v[x + 1], v[x + 2], v[x + 3]);
+        } else if (j < j1) {
           *reinterpret_cast<uint4*>(dv_row + d0) = tile::pack8(*reinterpret_cast<const float(*)[8]>(v));
           *reinterpret_cast<uint4*>(dv_row + d0 + 8) = tile::pack8(*reinterpret_cast<const float(*)[8]>(v + 8));
         }
@@ -1591,7 +1623,7 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
       ptx::mbar_arrive_expect_tx(bar(V_FULL), 32768);
       ptx::tma_load_4d(sbase + V, &tm_v, bar(V_FULL), 0, j0, hk, b);
       ptx::tma_load_4d(sbase + V + 16384, &tm_v, bar(V_FULL), 64, j0, hk, b);
-      BlockIter it(&L, b, j0, j1, skip_abs != 0);
+      BlockIter it(&L, b, j0, j1, skip_abs != 0, qt0, qt1);
       Block blk;
       int s = 0, nb = 0;
       bool ok = true;
@@ -1601,9 +1633,9 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
         ptx::mbar_arrive_expect_tx(bar(K_FULL), 32768);
         ptx::tma_load_4d(sbase + K, mk, bar(K_FULL), 0, j0, hk, b);
         ptx::tma_load_4d(sbase + K + 16384, mk, bar(K_FULL), 64, j0, hk, b);
-        const int qs = max(blk.s, j0), nsteps = n_steps_of(blk);
+        const int qs = max(blk.s, j0), nsteps = n_steps_of(it);
         for (int st = 0; st < nsteps; ++st, ++s) {
-          const int qslot = s % kQS, q0 = qs + (st / G) * BQ, h = hk * G + st % G;
+          const int qslot = s % kQS, q0 = qs + (it.lq0 + st / G) * BQ, h = hk * G + st % G;
           if (s >= kQS && !wait(Q_EMPTY + qslot, ((s / kQS) - 1) & 1)) {
             ok = false;
             break;
@@ -1660,13 +1692,13 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
       }
     };
     bool ok = wait_u(V_FULL, 0);
-    BlockIter it(&L, b, j0, j1, skip_abs != 0);
+    BlockIter it(&L, b, j0, j1, skip_abs != 0, qt0, qt1);
     Block blk;
     int s = 0, nb = 0, sl = 0;
     uint32_t ph = 0;
     bool dv_started = false;
     while (ok && it.next(blk)) {
-      const int nsteps = n_steps_of(blk);
+      const int nsteps = n_steps_of(it);
       if (!wait_u(K_READY, nb & 1)) break;
       ptx::tc_fence_after();
       const int sb = s;
@@ -1721,7 +1753,7 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
   } else {
     // ------------------------------------------------------------ rotation (warps 18-19)
     const int rt = tid - 32 * (4 * kGroups + 2);  // 0..63: Q row rt, K rows rt and rt + 64
-    BlockIter it(&L, b, j0, j1, skip_abs != 0);
+    BlockIter it(&L, b, j0, j1, skip_abs != 0, qt0, qt1);
     Block blk;
     int s = 0, nb = 0;
     while (!*s_abort && it.next(blk)) {
@@ -1762,10 +1794,10 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
         ptx::fence_proxy_async_smem();
         ptx::mbar_arrive(bar(K_READY));
       }
-      const int qs = max(blk.s, j0), nsteps = n_steps_of(blk);
+      const int qs = max(blk.s, j0), nsteps = n_steps_of(it);
       const int r = rt;
       for (int st = 0; st < nsteps; ++st, ++s) {
-        const int qslot = s % kQS, q0 = qs + (st / G) * BQ, q1 = min(q0 + BQ, blk.e), h = hk * G + st % G;
+        const int qslot = s % kQS, q0 = qs + (it.lq0 + st / G) * BQ, q1 = min(q0 + BQ, blk.e), h = hk * G + st % G;
         const int i = q0 + r;
         // Row position and row statistics are fetched before the TMA wait.
         int p = 0;
@@ -1821,13 +1853,57 @@ bool strides_ok(const AiTensor4& t) {
   return ((uintptr_t)t.ptr % 16 == 0) && (t.stride_b % 8 == 0) && (t.stride_h % 8 == 0) && (t.stride_t % 8 == 0);
 }
 
+// Sums the partial dK / dV of a split key tile in chunk order and writes the
+// bf16 rows: one CTA per (split key tile, KV head), a warp per key, four d a lane.
+__global__ void __launch_bounds__(256) dkdv_reduce_kernel(const AiAttnBwdArgs a, const float* __restrict__ partials) {
+  const AiAttnFwdArgs& f = a.fwd;
+  const AiAttnLayout& L = f.layout;
+  const int32_t* red = L.kv_reduce + 4 * (int64_t)blockIdx.x;
+  const int32_t* item = L.kv_items + 4 * (int64_t)red[0];
+  const int b = item[0], j0 = item[1], j1 = item[2], first = red[1], n = red[2];
+  const int hk = blockIdx.y, warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  constexpr int BN = kvw::BN;
+  for (int kk = warp; kk < BN && j0 + kk < j1; kk += 8) {
+    float4 dk = make_float4(0.f, 0.f, 0.f, 0.f), dv = dk;
+    for (int c = 0; c < n; ++c) {
+      const float* part = partials + (((int64_t)(first + c) * f.num_kv_heads + hk) * 2) * (BN * D) + kk * D + 4 * lane;
+      const float4 x = *reinterpret_cast<const float4*>(part);
+      const float4 y = *reinterpret_cast<const float4*>(part + BN * D);
+      dk.x += x.x; dk.y += x.y; dk.z += x.z; dk.w += x.w;
+      dv.x += y.x; dv.y += y.y; dv.z += y.z; dv.w += y.w;
+    }
+    const int j = j0 + kk;
+    __nv_bfloat16* dk_row =
+        static_cast<__nv_bfloat16*>(a.dk.ptr) + b * a.dk.stride_b + hk * a.dk.stride_h + (int64_t)j * a.dk.stride_t;
+    __nv_bfloat16* dv_row =
+        static_cast<__nv_bfloat16*>(a.dv.ptr) + b * a.dv.stride_b + hk * a.dv.stride_h + (int64_t)j * a.dv.stride_t;
+    __nv_bfloat162 k2[2] = {__floats2bfloat162_rn(dk.x, dk.y), __floats2bfloat162_rn(dk.z, dk.w)};
+    __nv_bfloat162 v2[2] = {__floats2bfloat162_rn(dv.x, dv.y), __floats2bfloat162_rn(dv.z, dv.w)};
+    *reinterpret_cast<uint2*>(dk_row + 4 * lane) = *reinterpret_cast<const uint2*>(k2);
+    *reinterpret_cast<uint2*>(dv_row + 4 * lane) = *reinterpret_cast<const uint2*>(v2);
+  }
+}
+
 }  // namespace sm100bwd
 
 bool sm100_bwd_supported(int dtype, int head_dim) { return dtype == AI_DTYPE_BF16 && head_dim == sm100bwd::D; }
 
 int sm100_kv_tile_rows() { return sm100bwd::kv::BN; }
 
-int sm100_bwd(const AiAttnBwdArgs& a, float* delta, void* rot, bool rot_ready, cudaStream_t st,
+size_t sm100_kv_partial_bytes(const AiAttnFwdArgs& f) {
+  const AiAttnLayout& L = f.layout;
+  if (L.n_kv_chunks <= 0 || L.n_kv_partials <= 0 || !L.kv_chunks || !L.kv_reduce) return 0;
+  // Split the key tiles only when the costliest one outweighs the average
+  // work of an SM (one CTA per key tile and KV head otherwise sets the pace).
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const double avg = (double)L.kv_cost_total * f.num_kv_heads / (sms > 0 ? sms : 148);
+  if ((double)L.kv_cost_max <= 1.25 * avg) return 0;
+  const size_t n = (size_t)L.n_kv_partials * f.num_kv_heads * 2 * sm100bwd::kvw::BN * sm100bwd::D * sizeof(float);
+  return (n + 255) & ~size_t(255);
+}
+
+int sm100_bwd(const AiAttnBwdArgs& a, float* delta, void* rot, bool rot_ready, float* partials, cudaStream_t st,
               cudaError_t* cuda_err) {
   using namespace sm100bwd;
   const AiAttnFwdArgs& f = a.fwd;
@@ -1917,7 +1993,8 @@ int sm100_bwd(const AiAttnBwdArgs& a, float* delta, void* rot, bool rot_ready, c
         // nothing it reads) signals at the start of each CTA, so these CTAs
         // fill the SMs its CTAs leave; everything before that kernel is done.
         cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3(n_plain, f.num_kv_heads);
+        const bool split = partials != nullptr;
+        cfg.gridDim = dim3(split ? f.layout.n_kv_chunks : n_plain, f.num_kv_heads);
         cfg.blockDim = dim3(kvw::kThreads);
         cfg.dynamicSmemBytes = kvw::kSmem;
         cfg.stream = st;
@@ -1927,8 +2004,13 @@ int sm100_bwd(const AiAttnBwdArgs& a, float* delta, void* rot, bool rot_ready, c
         cfg.attrs = attr;
         cfg.numAttrs = 1;
         e = cudaLaunchKernelEx(&cfg, dkdv_ws_kernel, a, (const float*)delta, tk, tv, pre ? tqr : tq, tdo, tkr,
-                               pre ? 1 : 0, 0, n_abs > 0 ? 1 : 0);
+                               pre ? 1 : 0, 0, n_abs > 0 ? 1 : 0, split ? f.layout.kv_chunks : (const int32_t*)nullptr,
+                               partials);
         if (e == cudaSuccess) e = cudaGetLastError();
+        if (e == cudaSuccess && split && f.layout.n_kv_reduce > 0) {
+          dkdv_reduce_kernel<<<dim3(f.layout.n_kv_reduce, f.num_kv_heads), 256, 0, st>>>(a, partials);
+          e = cudaGetLastError();
+        }
       }
     }
     if (e == cudaSuccess && n_abs > 0) {

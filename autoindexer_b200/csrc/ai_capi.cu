@@ -46,6 +46,9 @@ int validate_fwd(const AiAttnFwdArgs* a) {
     return AI_ERR_NULL;
   if (a->workspace && ((uintptr_t)a->workspace % 256)) return AI_ERR_ALIGN;
   if (L.n_blocks < 0 || L.n_keys < 0 || L.n_pos <= 0 || L.n_fwd_items < 0 || L.n_kv_items < 0) return AI_ERR_LAYOUT;
+  if (L.n_kv_chunks < 0 || L.n_kv_partials < 0 || L.n_kv_reduce < 0 || (L.n_kv_chunks > 0 && !L.kv_chunks) ||
+      (L.n_kv_reduce > 0 && !L.kv_reduce) || (L.n_kv_chunks > 0 && L.n_kv_chunks < L.n_kv_items))
+    return AI_ERR_LAYOUT;
   if (L.n_fwd_abs_items < 0 || L.n_fwd_short_items < 0 ||
       (int64_t)L.n_fwd_abs_items + L.n_fwd_short_items > L.n_fwd_items || L.n_kv_abs_items < 0 ||
       L.n_kv_abs_items > L.n_kv_items)
@@ -118,8 +121,10 @@ int ai_attn_bwd_workspace(const AiAttnBwdArgs* a, size_t* bytes) {
   int rc = validate_fwd(&a->fwd);
   if (rc != AI_OK) return rc;
   *bytes = delta_bytes(a->fwd);
-  if (ai::sm100_bwd_supported(a->fwd.dtype, a->fwd.head_dim) && !fwd_copies(*a))
-    *bytes += ai::prerot_bytes(a->fwd, nullptr);
+  if (ai::sm100_bwd_supported(a->fwd.dtype, a->fwd.head_dim)) {
+    *bytes += ai::sm100_kv_partial_bytes(a->fwd);
+    if (!fwd_copies(*a)) *bytes += ai::prerot_bytes(a->fwd, nullptr);
+  }
   return AI_OK;
 }
 
@@ -134,13 +139,21 @@ int ai_attn_bwd(const AiAttnBwdArgs* a, void* stream) {
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   float* delta = static_cast<float*>(a->workspace);
   if (ai::sm100_bwd_supported(a->fwd.dtype, a->fwd.head_dim)) {
-    // Rotated Q and K copies: the forward's (fwd_rotated), else rotated into
-    // the workspace after delta if it fits, else none (in-kernel rotation).
-    if (fwd_copies(*a)) return ai::sm100_bwd(*a, delta, a->fwd.workspace, true, st, nullptr);
-    const size_t db = delta_bytes(a->fwd);
+    // Workspace: delta, then the dK/dV partial sums of split key tiles when
+    // the layout splits some and they fit, then the rotated Q and K copies
+    // when the forward's are not passed (fwd_rotated) and they fit (else
+    // every tile is rotated in shared memory).
+    size_t used = delta_bytes(a->fwd);
+    float* partials = nullptr;
+    const size_t pb = ai::sm100_kv_partial_bytes(a->fwd);
+    if (pb > 0 && a->workspace_bytes >= used + pb) {
+      partials = reinterpret_cast<float*>(static_cast<char*>(a->workspace) + used);
+      used += pb;
+    }
+    if (fwd_copies(*a)) return ai::sm100_bwd(*a, delta, a->fwd.workspace, true, partials, st, nullptr);
     void* rot = nullptr;
-    if (a->workspace_bytes >= db + ai::prerot_bytes(a->fwd, nullptr)) rot = static_cast<char*>(a->workspace) + db;
-    return ai::sm100_bwd(*a, delta, rot, false, st, nullptr);
+    if (a->workspace_bytes >= used + ai::prerot_bytes(a->fwd, nullptr)) rot = static_cast<char*>(a->workspace) + used;
+    return ai::sm100_bwd(*a, delta, rot, false, partials, st, nullptr);
   }
   ai::ProfScope ps(AI_PROF_SIMT, st);
   return launch_status(ai::simt_bwd(*a, delta, st));

@@ -43,7 +43,10 @@ int sm100_kv_tile_rows();
 // `rot`: scratch for the once-rotated Q/K copies (prerot_bytes), or nullptr to
 // rotate every tile in shared memory; `rot_ready`: `rot` already holds them
 // (written by the forward), so they are not rotated again.
-int sm100_bwd(const AiAttnBwdArgs& a, float* delta, void* rot, bool rot_ready, cudaStream_t st,
+// Bytes of fp32 partial sums the dK/dV pass wants for split key tiles (0:
+// the layout splits none, or splitting would not pay on this device).
+size_t sm100_kv_partial_bytes(const AiAttnFwdArgs& f);
+int sm100_bwd(const AiAttnBwdArgs& a, float* delta, void* rot, bool rot_ready, float* partials, cudaStream_t st,
               cudaError_t* cuda_err);
 // TMA map over a (B, H, T, 128) bf16 tensor, box 64 x box_rows, 128-byte swizzle.
 bool sm100_make_map(CUtensorMap* map, const AiTensor4& t, int B, int H, int T, int box_rows);

@@ -218,6 +218,258 @@ int plan(const AiPrepList* lists, int32_t n_lists, const int32_t* list_of_row, i
   return AI_OK;
 }
 
+// Every table of a layout, in host vectors.
+struct Tables {
+  std::vector<int32_t> blocks, row_blocks, row_cov, q_pos, k_own, fwd_items, kv_items, kv_chunks, kv_reduce;
+  std::vector<uint32_t> key_info;
+  int32_t n_fwd_abs = 0, n_fwd_short = 0, n_kv_abs = 0, n_kv_partials = 0, kv_cost_max = 0, kv_cost_total = 0;
+  bool all_owned = true;
+  int64_t pairs = 0, p_min = 0, p_max = 0;
+};
+
+// Query rows per step of the tensor-core dK/dV kernel, and its chunking costs.
+constexpr int64_t kKvStepRows = 64, kSplitCost = 64, kChunkCost = 40;
+
+int build(const AiPrepList* lists, int32_t n_lists, const int32_t* list_of_row, int32_t batch, int32_t seq_len,
+          int32_t fwd_tile, int32_t kv_tile, Tables* t) {
+  Plan p;
+  int rc = plan(lists, n_lists, list_of_row, batch, seq_len, fwd_tile, kv_tile, &p);
+  if (rc != AI_OK) return rc;
+  const int64_t lo = p.lo, n_pos = p.hi - p.lo + 1;
+  auto row_of = [&](int64_t pos) -> uint32_t {
+    int64_t r = pos - lo;
+    r = r < 0 ? 0 : (r >= n_pos ? n_pos - 1 : r);
+    return (uint32_t)r;
+  };
+
+  t->key_info.assign((size_t)p.n_keys, 0);
+  // Per list: key words, own-block rows, OWNPOS per block, finite pairs.
+  std::vector<ListView> views((size_t)n_lists);
+  int64_t base = 0;
+  for (int32_t u = 0; u < n_lists; ++u) {
+    const AiPrepList& l = lists[u];
+    ListView& v = views[(size_t)u];
+    v.l = &l;
+    v.key_base = base;
+    base += l.n_keys;
+    v.info.resize((size_t)l.n_keys);
+    for (int64_t j = 0; j < l.n_keys; ++j) {
+      const bool at = l.attn_mask[j] != 0, ab = l.abs_mask && l.abs_mask[j] && at;
+      v.info[(size_t)j] = row_of(l.key_pos[j]) | (at ? AI_KEY_ATTN : 0u) | (ab ? AI_KEY_ABS : 0u);
+    }
+    v.own.assign((size_t)seq_len, 0);
+    for (int32_t i = 0; i < l.n_blocks; ++i) {
+      const int64_t* bd = l.boundary + 4 * (int64_t)i;
+      for (int64_t r = bd[0]; r < bd[1]; ++r) v.own[(size_t)r] = (int32_t)(v.info[(size_t)(bd[2] + r)] & AI_KEY_ROW_MASK);
+    }
+    v.own_ok.resize((size_t)l.n_blocks);
+    for (int32_t i = 0; i < l.n_blocks; ++i) {
+      const int64_t* bd = l.boundary + 4 * (int64_t)i;
+      bool ok = true;
+      int64_t cum = 0;
+      for (int64_t j = 0; j < bd[1]; ++j) {
+        const uint32_t w = v.info[(size_t)(bd[2] + j)];
+        if (w & AI_KEY_ATTN) {
+          ++cum;
+          if ((int32_t)(w & AI_KEY_ROW_MASK) != v.own[(size_t)j]) ok = false;
+        }
+        if (j >= bd[0]) v.pairs += cum;  // row j sees the attended keys up to j
+      }
+      v.own_ok[(size_t)i] = ok;
+    }
+    std::memcpy(t->key_info.data() + v.key_base, v.info.data(), sizeof(uint32_t) * (size_t)l.n_keys);
+  }
+
+  // Blocks, row tables, query / own rows.
+  struct FwdItem {
+    int64_t cost;
+    int32_t block, q0, q1, group;
+  };
+  struct KvItem {
+    int64_t cost;
+    int32_t row, j0, j1;
+    bool abs;
+  };
+  std::vector<FwdItem> fwd;
+  std::vector<KvItem> kv;
+  fwd.reserve((size_t)p.n_fwd);
+  kv.reserve((size_t)p.n_kv);
+  int32_t nb = 0;
+  int64_t pairs = 0;
+  bool all_owned = true;
+  t->row_blocks.assign((size_t)batch + 1, 0);
+  t->row_cov.assign((size_t)batch, 0);
+  t->q_pos.assign((size_t)batch * seq_len, 0);
+  t->k_own.assign((size_t)batch * seq_len, 0);
+  t->blocks.assign((size_t)AI_BLOCK_FIELDS * p.n_blocks, 0);
+  for (int32_t b = 0; b < batch; ++b) {
+    const ListView& v = views[(size_t)list_of_row[b]];
+    const AiPrepList& l = *v.l;
+    const int32_t first = nb;
+    for (int32_t i = 0; i < l.n_blocks; ++i) {
+      const int64_t* bd = l.boundary + 4 * (int64_t)i;
+      const int64_t s = bd[0], e = bd[1], ks = bd[2];
+      int64_t kv_lo = e, abs_lo = 0, abs_hi = 0, last_att = -1;
+      bool any_abs = false;
+      for (int64_t j = 0; j < e; ++j) {
+        const uint32_t w = v.info[(size_t)(ks + j)];
+        if (w & AI_KEY_ATTN) {
+          if (kv_lo == e) kv_lo = j;
+          last_att = j;
+        }
+        if (w & AI_KEY_ABS) {
+          if (!any_abs) abs_lo = j;
+          abs_hi = j + 1;
+          any_abs = true;
+        }
+      }
+      int32_t flags = 0;
+      if (kv_lo < e) {
+        int64_t attended = 0;
+        for (int64_t j = kv_lo; j < e; ++j) attended += (v.info[(size_t)(ks + j)] & AI_KEY_ATTN) ? 1 : 0;
+        if (attended != e - kv_lo) flags |= AI_BLOCKF_MASKED;
+      }
+      (void)last_att;
+      if (any_abs) flags |= AI_BLOCKF_ABS;
+      if (v.own_ok[(size_t)i]) flags |= AI_BLOCKF_OWNPOS;
+      int32_t* rec = t->blocks.data() + (int64_t)AI_BLOCK_FIELDS * nb;
+      rec[AI_BLOCK_ROW] = b;
+      rec[AI_BLOCK_START] = (int32_t)s;
+      rec[AI_BLOCK_END] = (int32_t)e;
+      rec[AI_BLOCK_KEY_OFF] = (int32_t)(v.key_base + ks);
+      rec[AI_BLOCK_KV_LO] = (int32_t)kv_lo;
+      rec[AI_BLOCK_FLAGS] = flags;
+      rec[AI_BLOCK_ABS_LO] = (int32_t)abs_lo;
+      rec[AI_BLOCK_ABS_HI] = (int32_t)abs_hi;
+      for (int64_t q0 = s; q0 < e; q0 += fwd_tile) {
+        const int64_t q1 = std::min<int64_t>(q0 + fwd_tile, e);
+        const int64_t cost = (q1 - q0) * std::max<int64_t>(0, std::min(e, q1) - kv_lo);
+        const int32_t group = (flags & AI_BLOCKF_ABS) ? 0 : (q1 - q0 <= fwd_tile / 2 ? 1 : 2);
+        fwd.push_back({cost, nb, (int32_t)q0, (int32_t)q1, group});
+      }
+      ++nb;
+    }
+    t->row_blocks[(size_t)b + 1] = nb;
+    const int64_t cov = l.n_query;
+    t->row_cov[(size_t)b] = (int32_t)cov;
+    if (cov < seq_len) all_owned = false;
+    int32_t* qp = t->q_pos.data() + (int64_t)b * seq_len;
+    int32_t* ko = t->k_own.data() + (int64_t)b * seq_len;
+    const uint32_t zero_row = row_of(0);
+    for (int64_t r = 0; r < seq_len; ++r) {
+      qp[r] = (int32_t)(r < cov ? row_of(l.query_pos[r]) : zero_row);
+      ko[r] = v.own[(size_t)r];
+    }
+    pairs += v.pairs;
+    // Key tiles of this row: cost = query rows that see them; whether they
+    // hold an abs key of some block.
+    for (int64_t j0 = 0; j0 < cov; j0 += kv_tile) {
+      const int64_t j1 = std::min<int64_t>(j0 + kv_tile, cov);
+      int64_t cost = 0;
+      bool abs = false;
+      for (int32_t bi = first; bi < nb; ++bi) {
+        const int32_t* rec = t->blocks.data() + (int64_t)AI_BLOCK_FIELDS * bi;
+        const int64_t s = rec[AI_BLOCK_START], e = rec[AI_BLOCK_END];
+        if (!(e > j0 && rec[AI_BLOCK_KV_LO] < j1)) continue;
+        cost += std::max<int64_t>(e - std::max<int64_t>(s, j0), 0);
+        if ((rec[AI_BLOCK_FLAGS] & AI_BLOCKF_ABS) && rec[AI_BLOCK_ABS_LO] < j1 && rec[AI_BLOCK_ABS_HI] > j0) abs = true;
+      }
+      kv.push_back({cost, b, (int32_t)j0, (int32_t)j1, abs});
+    }
+  }
+
+  // Forward items: abs blocks' items, then short items, then the rest;
+  // longest first in each group (stable, so ties keep block order).
+  std::stable_sort(fwd.begin(), fwd.end(), [](const FwdItem& x, const FwdItem& y) {
+    if (x.group != y.group) return x.group < y.group;
+    return x.cost > y.cost;
+  });
+  t->fwd_items.resize(4 * fwd.size());
+  for (size_t i = 0; i < fwd.size(); ++i) {
+    t->fwd_items[4 * i] = fwd[i].block;
+    t->fwd_items[4 * i + 1] = fwd[i].q0;
+    t->fwd_items[4 * i + 2] = fwd[i].q1;
+    t->fwd_items[4 * i + 3] = 0;
+    t->n_fwd_abs += fwd[i].group == 0;
+    t->n_fwd_short += fwd[i].group == 1;
+  }
+  std::stable_sort(kv.begin(), kv.end(), [](const KvItem& x, const KvItem& y) {
+    if (x.abs != y.abs) return x.abs;
+    return x.cost > y.cost;
+  });
+  t->kv_items.resize(4 * kv.size());
+  for (size_t i = 0; i < kv.size(); ++i) {
+    t->kv_items[4 * i] = kv[i].row;
+    t->kv_items[4 * i + 1] = kv[i].j0;
+    t->kv_items[4 * i + 2] = kv[i].j1;
+    t->kv_items[4 * i + 3] = 0;
+    t->n_kv_abs += kv[i].abs;
+  }
+  t->all_owned = all_owned;
+  t->pairs = pairs;
+  t->p_min = p.lo;
+  t->p_max = p.hi;
+
+  // dK/dV chunks: each key tile's 64-row query tiles (blocks without an abs
+  // key among the tile's keys, block order), cost 1 a query tile and 2 a
+  // block start; a tile costing more than kSplitCost is cut into chunks of
+  // about kChunkCost (a chunk that starts inside a block pays its start).
+  struct Chunk {
+    int64_t cost;
+    int32_t item, q0, q1, slot;
+  };
+  std::vector<Chunk> chunks;
+  const bool any_abs_item = t->n_kv_abs > 0;
+  for (size_t k = 0; k < kv.size(); ++k) {
+    const int32_t b = kv[k].row, j0 = kv[k].j0, j1 = kv[k].j1;
+    std::vector<int64_t> tile_cost;  // cost charged to each query tile, in order
+    for (int32_t bi = t->row_blocks[(size_t)b]; bi < t->row_blocks[(size_t)b + 1]; ++bi) {
+      const int32_t* rec = t->blocks.data() + (int64_t)AI_BLOCK_FIELDS * bi;
+      const int64_t s = rec[AI_BLOCK_START], e = rec[AI_BLOCK_END];
+      if (!(e > j0 && rec[AI_BLOCK_KV_LO] < j1 && std::max<int64_t>(s, j0) < e)) continue;
+      if (any_abs_item && (rec[AI_BLOCK_FLAGS] & AI_BLOCKF_ABS)) {
+        const int32_t lo = rec[AI_BLOCK_ABS_LO], hi = rec[AI_BLOCK_ABS_HI];
+        if (hi <= lo || (j0 < hi && lo < j1)) continue;
+      }
+      const int64_t nq = (e - std::max<int64_t>(s, j0) + kKvStepRows - 1) / kKvStepRows;
+      for (int64_t x = 0; x < nq; ++x) tile_cost.push_back(x == 0 ? 3 : 1);
+    }
+    int64_t total = 0;
+    for (int64_t c : tile_cost) total += c;
+    t->kv_cost_max = std::max<int32_t>(t->kv_cost_max, (int32_t)std::min<int64_t>(total, INT32_MAX));
+    t->kv_cost_total = (int32_t)std::min<int64_t>((int64_t)t->kv_cost_total + total, INT32_MAX);
+    const int32_t nqt = (int32_t)tile_cost.size();
+    if (total <= kSplitCost) {
+      chunks.push_back({total, (int32_t)k, 0, nqt, -1});
+      continue;
+    }
+    int32_t first = (int32_t)chunks.size(), start = 0;
+    int64_t acc = 0;
+    for (int32_t x = 0; x < nqt; ++x) {
+      acc += (x == start && tile_cost[(size_t)x] == 1) ? 3 : tile_cost[(size_t)x];
+      if (acc >= kChunkCost && x + 1 < nqt) {
+        chunks.push_back({acc, (int32_t)k, start, x + 1, 0});
+        start = x + 1;
+        acc = 0;
+      }
+    }
+    chunks.push_back({acc, (int32_t)k, start, nqt, 0});
+    const int32_t n = (int32_t)chunks.size() - first;
+    for (int32_t c = 0; c < n; ++c) chunks[(size_t)(first + c)].slot = t->n_kv_partials + c;
+    t->kv_reduce.insert(t->kv_reduce.end(), {(int32_t)k, t->n_kv_partials, n, 0});
+    t->n_kv_partials += n;
+  }
+  std::stable_sort(chunks.begin(), chunks.end(), [](const Chunk& x, const Chunk& y) { return x.cost > y.cost; });
+  t->kv_chunks.resize(4 * chunks.size());
+  for (size_t i = 0; i < chunks.size(); ++i) {
+    t->kv_chunks[4 * i] = chunks[i].item;
+    t->kv_chunks[4 * i + 1] = chunks[i].q0;
+    t->kv_chunks[4 * i + 2] = chunks[i].q1;
+    t->kv_chunks[4 * i + 3] = chunks[i].slot;
+  }
+  return AI_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -257,196 +509,52 @@ int ai_attn_positions_from_ops(const int64_t* ops, int32_t n_ops, int64_t* bound
 int ai_attn_prep_sizes(const AiPrepList* lists, int32_t n_lists, const int32_t* list_of_row, int32_t batch,
                        int32_t seq_len, int32_t fwd_tile, int32_t kv_tile, AiPrepSizes* sizes) {
   if (!sizes) return AI_ERR_NULL;
-  Plan p;
-  int rc = plan(lists, n_lists, list_of_row, batch, seq_len, fwd_tile, kv_tile, &p);
+  Tables t;
+  int rc = build(lists, n_lists, list_of_row, batch, seq_len, fwd_tile, kv_tile, &t);
   if (rc != AI_OK) return rc;
-  sizes->n_blocks = p.n_blocks;
-  sizes->n_fwd_items = p.n_fwd;
-  sizes->n_kv_items = p.n_kv;
-  sizes->n_keys = p.n_keys;
-  sizes->p_min = p.lo;
-  sizes->p_max = p.hi;
+  sizes->n_blocks = (int32_t)(t.blocks.size() / AI_BLOCK_FIELDS);
+  sizes->n_fwd_items = (int32_t)(t.fwd_items.size() / 4);
+  sizes->n_kv_items = (int32_t)(t.kv_items.size() / 4);
+  sizes->n_kv_chunks = (int32_t)(t.kv_chunks.size() / 4);
+  sizes->n_kv_reduce = (int32_t)(t.kv_reduce.size() / 4);
+  sizes->n_keys = (int64_t)t.key_info.size();
+  sizes->p_min = t.p_min;
+  sizes->p_max = t.p_max;
   return AI_OK;
 }
 
 int ai_attn_prep(const AiPrepList* lists, int32_t n_lists, const int32_t* list_of_row, int32_t batch,
                  int32_t seq_len, int32_t fwd_tile, int32_t kv_tile, AiPrepTables* out) {
   if (!out || !out->blocks || !out->row_blocks || !out->row_cov || !out->key_info || !out->q_pos || !out->k_own ||
-      !out->fwd_items || !out->kv_items)
+      !out->fwd_items || !out->kv_items || !out->kv_chunks)
     return AI_ERR_NULL;
-  Plan p;
-  int rc = plan(lists, n_lists, list_of_row, batch, seq_len, fwd_tile, kv_tile, &p);
+  Tables t;
+  int rc = build(lists, n_lists, list_of_row, batch, seq_len, fwd_tile, kv_tile, &t);
   if (rc != AI_OK) return rc;
-  const int64_t lo = p.lo, n_pos = p.hi - p.lo + 1;
-  auto row_of = [&](int64_t pos) -> uint32_t {
-    int64_t r = pos - lo;
-    r = r < 0 ? 0 : (r >= n_pos ? n_pos - 1 : r);
-    return (uint32_t)r;
+  auto put = [](int32_t* dst, const std::vector<int32_t>& v) {
+    if (!v.empty()) std::memcpy(dst, v.data(), sizeof(int32_t) * v.size());
   };
-
-  // Per list: key words, own-block rows, OWNPOS per block, finite pairs.
-  std::vector<ListView> views((size_t)n_lists);
-  int64_t base = 0;
-  for (int32_t u = 0; u < n_lists; ++u) {
-    const AiPrepList& l = lists[u];
-    ListView& v = views[(size_t)u];
-    v.l = &l;
-    v.key_base = base;
-    base += l.n_keys;
-    v.info.resize((size_t)l.n_keys);
-    for (int64_t j = 0; j < l.n_keys; ++j) {
-      const bool at = l.attn_mask[j] != 0, ab = l.abs_mask && l.abs_mask[j] && at;
-      v.info[(size_t)j] = row_of(l.key_pos[j]) | (at ? AI_KEY_ATTN : 0u) | (ab ? AI_KEY_ABS : 0u);
-    }
-    v.own.assign((size_t)seq_len, 0);
-    for (int32_t i = 0; i < l.n_blocks; ++i) {
-      const int64_t* bd = l.boundary + 4 * (int64_t)i;
-      for (int64_t r = bd[0]; r < bd[1]; ++r) v.own[(size_t)r] = (int32_t)(v.info[(size_t)(bd[2] + r)] & AI_KEY_ROW_MASK);
-    }
-    v.own_ok.resize((size_t)l.n_blocks);
-    for (int32_t i = 0; i < l.n_blocks; ++i) {
-      const int64_t* bd = l.boundary + 4 * (int64_t)i;
-      bool ok = true;
-      int64_t cum = 0;
-      for (int64_t j = 0; j < bd[1]; ++j) {
-        const uint32_t w = v.info[(size_t)(bd[2] + j)];
-        if (w & AI_KEY_ATTN) {
-          ++cum;
-          if ((int32_t)(w & AI_KEY_ROW_MASK) != v.own[(size_t)j]) ok = false;
-        }
-        if (j >= bd[0]) v.pairs += cum;  // row j sees the attended keys up to j
-      }
-      v.own_ok[(size_t)i] = ok;
-    }
-    std::memcpy(out->key_info + v.key_base, v.info.data(), sizeof(uint32_t) * (size_t)l.n_keys);
+  put(out->blocks, t.blocks);
+  put(out->row_blocks, t.row_blocks);
+  put(out->row_cov, t.row_cov);
+  if (!t.key_info.empty()) std::memcpy(out->key_info, t.key_info.data(), sizeof(uint32_t) * t.key_info.size());
+  put(out->q_pos, t.q_pos);
+  put(out->k_own, t.k_own);
+  put(out->fwd_items, t.fwd_items);
+  put(out->kv_items, t.kv_items);
+  put(out->kv_chunks, t.kv_chunks);
+  if (!t.kv_reduce.empty()) {
+    if (!out->kv_reduce) return AI_ERR_NULL;
+    put(out->kv_reduce, t.kv_reduce);
   }
-
-  // Blocks, row tables, query / own rows.
-  struct FwdItem {
-    int64_t cost;
-    int32_t block, q0, q1, group;
-  };
-  struct KvItem {
-    int64_t cost;
-    int32_t row, j0, j1;
-    bool abs;
-  };
-  std::vector<FwdItem> fwd;
-  std::vector<KvItem> kv;
-  fwd.reserve((size_t)p.n_fwd);
-  kv.reserve((size_t)p.n_kv);
-  int32_t nb = 0;
-  int64_t pairs = 0;
-  bool all_owned = true;
-  out->row_blocks[0] = 0;
-  for (int32_t b = 0; b < batch; ++b) {
-    const ListView& v = views[(size_t)list_of_row[b]];
-    const AiPrepList& l = *v.l;
-    const int32_t first = nb;
-    for (int32_t i = 0; i < l.n_blocks; ++i) {
-      const int64_t* bd = l.boundary + 4 * (int64_t)i;
-      const int64_t s = bd[0], e = bd[1], ks = bd[2];
-      int64_t kv_lo = e, abs_lo = 0, abs_hi = 0, last_att = -1;
-      bool any_abs = false;
-      for (int64_t j = 0; j < e; ++j) {
-        const uint32_t w = v.info[(size_t)(ks + j)];
-        if (w & AI_KEY_ATTN) {
-          if (kv_lo == e) kv_lo = j;
-          last_att = j;
-        }
-        if (w & AI_KEY_ABS) {
-          if (!any_abs) abs_lo = j;
-          abs_hi = j + 1;
-          any_abs = true;
-        }
-      }
-      int32_t flags = 0;
-      if (kv_lo < e) {
-        int64_t attended = 0;
-        for (int64_t j = kv_lo; j < e; ++j) attended += (v.info[(size_t)(ks + j)] & AI_KEY_ATTN) ? 1 : 0;
-        if (attended != e - kv_lo) flags |= AI_BLOCKF_MASKED;
-      }
-      (void)last_att;
-      if (any_abs) flags |= AI_BLOCKF_ABS;
-      if (v.own_ok[(size_t)i]) flags |= AI_BLOCKF_OWNPOS;
-      int32_t* rec = out->blocks + (int64_t)AI_BLOCK_FIELDS * nb;
-      rec[AI_BLOCK_ROW] = b;
-      rec[AI_BLOCK_START] = (int32_t)s;
-      rec[AI_BLOCK_END] = (int32_t)e;
-      rec[AI_BLOCK_KEY_OFF] = (int32_t)(v.key_base + ks);
-      rec[AI_BLOCK_KV_LO] = (int32_t)kv_lo;
-      rec[AI_BLOCK_FLAGS] = flags;
-      rec[AI_BLOCK_ABS_LO] = (int32_t)abs_lo;
-      rec[AI_BLOCK_ABS_HI] = (int32_t)abs_hi;
-      for (int64_t q0 = s; q0 < e; q0 += fwd_tile) {
-        const int64_t q1 = std::min<int64_t>(q0 + fwd_tile, e);
-        const int64_t cost = (q1 - q0) * std::max<int64_t>(0, std::min(e, q1) - kv_lo);
-        const int32_t group = (flags & AI_BLOCKF_ABS) ? 0 : (q1 - q0 <= fwd_tile / 2 ? 1 : 2);
-        fwd.push_back({cost, nb, (int32_t)q0, (int32_t)q1, group});
-      }
-      ++nb;
-    }
-    out->row_blocks[b + 1] = nb;
-    const int64_t cov = l.n_query;
-    out->row_cov[b] = (int32_t)cov;
-    if (cov < seq_len) all_owned = false;
-    int32_t* qp = out->q_pos + (int64_t)b * seq_len;
-    int32_t* ko = out->k_own + (int64_t)b * seq_len;
-    const uint32_t zero_row = row_of(0);
-    for (int64_t r = 0; r < seq_len; ++r) {
-      qp[r] = (int32_t)(r < cov ? row_of(l.query_pos[r]) : zero_row);
-      ko[r] = v.own[(size_t)r];
-    }
-    pairs += v.pairs;
-    // Key tiles of this row: cost = query rows that see them; whether they
-    // hold an abs key of some block.
-    for (int64_t j0 = 0; j0 < cov; j0 += kv_tile) {
-      const int64_t j1 = std::min<int64_t>(j0 + kv_tile, cov);
-      int64_t cost = 0;
-      bool abs = false;
-      for (int32_t bi = first; bi < nb; ++bi) {
-        const int32_t* rec = out->blocks + (int64_t)AI_BLOCK_FIELDS * bi;
-        const int64_t s = rec[AI_BLOCK_START], e = rec[AI_BLOCK_END];
-        if (!(e > j0 && rec[AI_BLOCK_KV_LO] < j1)) continue;
-        cost += std::max<int64_t>(e - std::max<int64_t>(s, j0), 0);
-        if ((rec[AI_BLOCK_FLAGS] & AI_BLOCKF_ABS) && rec[AI_BLOCK_ABS_LO] < j1 && rec[AI_BLOCK_ABS_HI] > j0) abs = true;
-      }
-      kv.push_back({cost, b, (int32_t)j0, (int32_t)j1, abs});
-    }
-  }
-
-  // Forward items: abs blocks' items, then short items, then the rest;
-  // longest first in each group (stable, so ties keep block order).
-  std::stable_sort(fwd.begin(), fwd.end(), [](const FwdItem& x, const FwdItem& y) {
-    if (x.group != y.group) return x.group < y.group;
-    return x.cost > y.cost;
-  });
-  int32_t n_abs = 0, n_short = 0;
-  for (size_t i = 0; i < fwd.size(); ++i) {
-    out->fwd_items[4 * i] = fwd[i].block;
-    out->fwd_items[4 * i + 1] = fwd[i].q0;
-    out->fwd_items[4 * i + 2] = fwd[i].q1;
-    out->fwd_items[4 * i + 3] = 0;
-    n_abs += fwd[i].group == 0;
-    n_short += fwd[i].group == 1;
-  }
-  std::stable_sort(kv.begin(), kv.end(), [](const KvItem& x, const KvItem& y) {
-    if (x.abs != y.abs) return x.abs;
-    return x.cost > y.cost;
-  });
-  int32_t n_kv_abs = 0;
-  for (size_t i = 0; i < kv.size(); ++i) {
-    out->kv_items[4 * i] = kv[i].row;
-    out->kv_items[4 * i + 1] = kv[i].j0;
-    out->kv_items[4 * i + 2] = kv[i].j1;
-    out->kv_items[4 * i + 3] = 0;
-    n_kv_abs += kv[i].abs;
-  }
-  out->n_fwd_abs_items = n_abs;
-  out->n_fwd_short_items = n_short;
-  out->n_kv_abs_items = n_kv_abs;
-  out->all_rows_owned = all_owned ? 1 : 0;
-  out->pairs_per_head = pairs;
+  out->n_kv_partials = t.n_kv_partials;
+  out->kv_cost_max = t.kv_cost_max;
+  out->kv_cost_total = t.kv_cost_total;
+  out->n_fwd_abs_items = t.n_fwd_abs;
+  out->n_fwd_short_items = t.n_fwd_short;
+  out->n_kv_abs_items = t.n_kv_abs;
+  out->all_rows_owned = t.all_owned ? 1 : 0;
+  out->pairs_per_head = t.pairs;
   return AI_OK;
 }
 

@@ -113,6 +113,11 @@ class CompiledLayout:
     n_fwd_abs_items: int         # leading fwd_items whose block has abs keys
     n_kv_abs_items: int          # leading kv_items that a block with abs keys sees
     n_fwd_short_items: int       # fwd_items after the abs ones with at most fwd_tile / 2 rows
+    kv_chunks: torch.Tensor      # [c, 4]: kv item, first / end query tile, partial slot (-1: whole item)
+    kv_reduce: torch.Tensor      # [r, 4]: kv item, first slot, slots (items split into chunks)
+    n_kv_partials: int           # partial slots of the split items
+    kv_cost_max: int             # cost of the costliest key tile (query tiles + 2 per block)
+    kv_cost_total: int           # cost of all key tiles
     pairs_per_head: int          # finite (query, key) logits of one head summed over the batch
     all_rows_owned: bool = False  # every row of every batch row belongs to a block (no fill launches)
     host_blocks: np.ndarray = field(repr=False, default=None)
@@ -142,6 +147,13 @@ class CompiledLayout:
         L.n_kv_abs_items = int(self.n_kv_abs_items)
         L.all_rows_owned = int(self.all_rows_owned)
         L.n_fwd_short_items = int(self.n_fwd_short_items)
+        L.kv_chunks = self.kv_chunks.data_ptr() if self.kv_chunks.numel() else None
+        L.n_kv_chunks = int(self.kv_chunks.shape[0])
+        L.n_kv_partials = int(self.n_kv_partials)
+        L.kv_reduce = self.kv_reduce.data_ptr() if self.kv_reduce.numel() else None
+        L.n_kv_reduce = int(self.kv_reduce.shape[0])
+        L.kv_cost_max = int(self.kv_cost_max)
+        L.kv_cost_total = int(self.kv_cost_total)
         return L
 
 
@@ -224,7 +236,7 @@ def _compile(parsed_positions, batch, seq_len, head_dim, code, rotary_emb, devic
     # One int32 buffer holds every table (sections 16-byte aligned).
     parts = [("blocks", sz.n_blocks * 8), ("row_blocks", batch + 1), ("row_cov", batch), ("key_info", sz.n_keys),
              ("q_pos", batch * seq_len), ("k_own", batch * seq_len), ("fwd_items", sz.n_fwd_items * 4),
-             ("kv_items", sz.n_kv_items * 4)]
+             ("kv_items", sz.n_kv_items * 4), ("kv_chunks", sz.n_kv_chunks * 4), ("kv_reduce", sz.n_kv_reduce * 4)]
     offs, total = {}, 0
     for name, n in parts:
         offs[name] = (total, int(n))
@@ -255,6 +267,8 @@ def _compile(parsed_positions, batch, seq_len, head_dim, code, rotary_emb, devic
         key_info=view("key_info", (-1,)), q_pos=view("q_pos", (batch, seq_len)), k_own=view("k_own", (batch, seq_len)),
         rope_cos=cos, rope_sin=sin, rope_cs16=torch.stack([cos, sin], dim=-1).to(torch.float16).contiguous(),
         fwd_items=view("fwd_items", (-1, 4)), kv_items=view("kv_items", (-1, 4)),
+        kv_chunks=view("kv_chunks", (-1, 4)), kv_reduce=view("kv_reduce", (-1, 4)), n_kv_partials=int(t.n_kv_partials),
+        kv_cost_max=int(t.kv_cost_max), kv_cost_total=int(t.kv_cost_total),
         n_fwd_abs_items=int(t.n_fwd_abs_items), n_kv_abs_items=int(t.n_kv_abs_items),
         n_fwd_short_items=int(t.n_fwd_short_items), pairs_per_head=int(t.pairs_per_head),
         all_rows_owned=bool(t.all_rows_owned), host_blocks=blocks_host, _host_buffer=host,

@@ -56,7 +56,8 @@ SECTIONS3 = [(0, 24), (24, 48), (48, 64)]
 WORKLOAD = ("cfg1: bf16 B=4 T=4096 Hq=32 Hkv=8 D=128 theta=1e6, docs U[256,2048] packed per row, "
             "2 RoPE sections (32+32 freq slots: arange, cursor stream)")
 METRIC = "multi-seg RoPE attn fwd+bwd TFLOP/s (causal-adjusted, 14*D*pairs*Hq)"
-DOM_KERNEL_NAMES = {"fwd": "fwd_pers_kernel (forward)", "dq": "dq_pers_kernel (dQ)", "dkdv": "dkdv_ws_kernel (dK/dV)"}
+DOM_KERNEL_NAMES = {"fwd": "fwd_pers_kernel (forward)", "dq": "dq_pers_kernel (dQ)", "dkdv": "dkdv_ws_kernel (dK/dV)",
+                    "simt": "simt fp32 kernels (forward + backward)"}
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch on the
 # config-1 workload, from one ncu capture of the three kernels (profiles/).
 TRAFFIC_BYTES = {"fwd": 368016640, "dq": 549332224, "dkdv": 401622016}
@@ -78,14 +79,15 @@ def make_rows(seed: int):
     return rows, streams
 
 
-def _inputs(seed, b, hq, hkv, t):
+def _inputs(seed, b, hq, hkv, t, dtype=None):
     import torch
 
+    dtype = dtype or torch.bfloat16
     g = torch.Generator().manual_seed(seed)
-    q = torch.randn(b, hq, t, D, generator=g).to(torch.bfloat16)
-    k = torch.randn(b, hkv, t, D, generator=g).to(torch.bfloat16)
-    v = torch.randn(b, hkv, t, D, generator=g).to(torch.bfloat16)
-    dout = torch.randn(b, t, hq, D, generator=g).to(torch.bfloat16)
+    q = torch.randn(b, hq, t, D, generator=g).to(dtype)
+    k = torch.randn(b, hkv, t, D, generator=g).to(dtype)
+    v = torch.randn(b, hkv, t, D, generator=g).to(dtype)
+    dout = torch.randn(b, t, hq, D, generator=g).to(dtype)
     return q, k, v, dout
 
 
@@ -111,7 +113,8 @@ class Workload:
     rope: Any          # RotaryEmbeddingFunc (torch module)
     streams: List[np.ndarray]
     sections: List[tuple]
-    host: tuple        # q, k, v, dout (CPU bf16)
+    host: tuple        # q, k, v, dout (CPU tensors of the workload's dtype)
+    full_cpu: bool = False  # the CPU baseline runs the whole workload (else one row x KV group slice)
 
     def row_lists(self):
         """One position-block list per batch row."""
@@ -121,6 +124,8 @@ class Workload:
 
 
 CONFIG_DESC = {
+    "0": ("cfg0: fp32 B=2 T=1024 Hq=32 Hkv=8 D=128 theta=1e6, one causal sequence per row, 2 RoPE sections "
+          "(32+32 freq slots: arange, cursor stream); the fp32 kernels"),
     "1": WORKLOAD,
     "E": ("cfgE: bf16 B=1 T=3072 Hq=32 Hkv=8 D=128 theta=1e6, CPT edit chain from the reference's sampler "
           "(autoindexer_8B.yaml perturbation: 71 blocks, sum E=145958, 12798 abs keys), 1 RoPE section"),
@@ -153,6 +158,14 @@ def build_workload(cfg: str, seed: int, device) -> Workload:
         streams = [np.arange(pmax)]
         rope = ab.SectionedRope(D, THETA, [torch.as_tensor(streams[0])], [(0, D // 2)], device=device)
         return Workload(cfg, CONFIG_DESC[cfg], 1, t, lay, rope, streams, [(0, D // 2)], _inputs(seed, 1, HQ, HKV, t))
+    if cfg == "0":
+        t = 1024
+        rng = np.random.default_rng(0)
+        streams = [np.arange(t), ab.cursor_stream(t, rng)]
+        rows = ab.RowLayouts([ab.document_blocks([t], position_ids=np.arange(t)) for _ in range(2)])
+        rope = ab.SectionedRope(D, THETA, [torch.as_tensor(s) for s in streams], SECTIONS, device=device)
+        return Workload(cfg, CONFIG_DESC[cfg], 2, t, rows, rope, streams, SECTIONS,
+                        _inputs(seed, 2, HQ, HKV, t, torch.float32), full_cpu=True)
     if cfg == "4":
         t = 65536
         rng = np.random.default_rng(4)
@@ -276,7 +289,7 @@ def job_tflops(job_flops_per_step: float, steps: int, t_max: float) -> float:
     return job_flops_per_step * steps / t_max / 1e12
 
 
-def _e2e(args, dev, host, apply, out_shapes, world):
+def _e2e(args, dev, host, apply, out_shapes, world, dtype):
     """End to end through a public function: every step copies its inputs in
     from pinned host memory (copy-in stream, two device buffer sets), runs
     ``apply(q, k, v) -> out`` and its autograd backward (compute stream), and
@@ -288,7 +301,7 @@ def _e2e(args, dev, host, apply, out_shapes, world):
     import torch.distributed as dist
 
     pinned = [x.pin_memory() for x in host]
-    outs_host = [torch.empty(s, dtype=torch.bfloat16).pin_memory() for s in out_shapes]
+    outs_host = [torch.empty(s, dtype=dtype).pin_memory() for s in out_shapes]
     h2d = sum(x.numel() * x.element_size() for x in pinned)
     d2h = sum(x.numel() * x.element_size() for x in outs_host)
     s_in, s_comp, s_out = (torch.cuda.Stream(dev) for _ in range(3))
@@ -360,7 +373,8 @@ def run_ours(args):
     Bw, Tw = wl.batch, wl.seq_len
     q, k, v, dout = (x.to(dev) for x in wl.host)
     scale = D ** -0.5
-    layout = compile_layout(wl.rows, Bw, Tw, D, torch.bfloat16, wl.rope, dev)
+    wdtype = wl.host[0].dtype
+    layout = compile_layout(wl.rows, Bw, Tw, D, wdtype, wl.rope, dev)
     flops = 14.0 * D * HQ * layout.pairs_per_head
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
     stream = torch.cuda.current_stream(dev)
@@ -438,7 +452,7 @@ def run_ours(args):
         def apply(xq, xk, xv):
             return fused_chain_of_edits_attn_b200(wl.rope, xq, xk, xv, wl.rows)[0]
     out_shapes = [(Bw, Tw, HQ, D), (Bw, HQ, Tw, D), (Bw, HKV, Tw, D), (Bw, HKV, Tw, D)]
-    t_e2e, h2d, d2h = _e2e(args, dev, wl.host, apply, out_shapes, world)
+    t_e2e, h2d, d2h = _e2e(args, dev, wl.host, apply, out_shapes, world, wdtype)
     e2e_value = job_tflops(job_flops, args.steps, t_e2e)
     assert read_status(dev) == 0
 
@@ -450,7 +464,7 @@ def run_ours(args):
         fresh = build_workload(args.config, seed=0, device=dev).rows
         torch.cuda.synchronize(dev)
         t0 = time.perf_counter()
-        compile_layout(fresh, Bw, Tw, D, torch.bfloat16, wl.rope, dev)
+        compile_layout(fresh, Bw, Tw, D, wdtype, wl.rope, dev)
         torch.cuda.synchronize(dev)
         t_layouts.append((time.perf_counter() - t0) * 1e3)
     layout_ms = float(np.median(t_layouts))
@@ -461,6 +475,8 @@ def run_ours(args):
     # dP, dV, dK) over its event-timed duration.
     hq_local = (HQ // world) if sharded else HQ
     kflops = {kk: c * D * hq_local * layout.pairs_per_head for kk, c in (("fwd", 4.0), ("dq", 6.0), ("dkdv", 8.0))}
+    if wdtype == torch.float32:  # one fp32 (SIMT) kernel family does forward and backward
+        kflops = {"simt": 14.0 * D * hq_local * layout.pairs_per_head}
     dom = max(kflops, key=lambda kk: kt.ms[kk])
     dom_ms = kt.ms[dom] / max(1, kt.launches[dom])  # per launch
     achieved = kflops[dom] * args.steps / (kt.ms[dom] * 1e-3) / 1e12
@@ -478,7 +494,7 @@ def run_ours(args):
         "higher_is_better": True,
         "scaling": "strong" if sharded else "weak",
         "vs_baseline": None,
-        "dtype": "bf16",
+        "dtype": "f32" if wdtype == torch.float32 else "bf16",
         "data": "synthetic (seeded randn q/k/v/dO; seeded layouts and cursor streams)",
         "config": {"workload": wl.desc, "global_batch": Bw * n_ranks_work, "seq_len": Tw,
                    "parallelism": (f"kv-head shards over {world} ranks + NCCL all-gather" if sharded
@@ -491,7 +507,7 @@ def run_ours(args):
         "pct_bf16_peak": round(100 * value / n_ranks_work / peak, 2) if not sharded else
         round(100 * value / world / peak, 2),
         "pct_bf16_spec_2250": round(100 * value / (world if sharded else n_ranks_work) / 2250.0, 2),
-        "roofline": {"bound": "tensor", "kernel": DOM_KERNEL_NAMES[dom],
+        "roofline": {"bound": "tensor" if dom != "simt" else "fp32 fma", "kernel": DOM_KERNEL_NAMES[dom],
                      "achieved": round(achieved, 3), "peak": peak, "unit": "TFLOP/s",
                      "frac": round(achieved / peak, 4), "peak_kind": f"{peak_kind} burst bf16",
                      "launch_ms": round(dom_ms, 4),
@@ -505,7 +521,7 @@ def run_ours(args):
     }
     if gather_ms is not None:
         line["allgather_ms_per_step"] = round(max_over_ranks(gather_ms / args.steps, world, dev), 4)
-    if world == 1 and args.config == "1" and not args.no_cpu_baseline:  # the CPU baseline is an N=1 figure
+    if world == 1 and args.config in ("0", "1") and not args.no_cpu_baseline:  # the CPU baseline is an N=1 figure
         line["cpu_baseline"] = cpu_baseline(wl, seed=0)
     if rank == 0:
         print(json.dumps(line), flush=True)
@@ -546,6 +562,8 @@ def cpu_baseline(wl: Workload, seed=0, reps=1):
     pairs = sum(int(np.cumsum(np.asarray(lay.concat_attn_masks[ks:ke], dtype=np.int64))[s:e].sum())
                 for s, e, ks, ke in lay.boundary_indices)
     flops = 14.0 * D * G * pairs
+    if wl.full_cpu:  # the whole workload: every row (same list here) and every head
+        flops *= wl.batch * (HQ // G)
     mods = _reference_modules()
     from threadpoolctl import threadpool_limits
 
@@ -564,6 +582,13 @@ def cpu_baseline(wl: Workload, seed=0, reps=1):
             t0 = time.perf_counter()
             for _ in range(reps):
                 rlay._query_rotary_pos_emb = rlay._keys_rotary_pos_emb = None
+                if wl.full_cpu:
+                    from transformers.models.llama.modeling_llama import repeat_kv
+
+                    qs, ks, vs = (x.float().requires_grad_(True) for x in (q, k, v))
+                    out, _ = ref.chain_of_edits_attn_ref(rope, qs, repeat_kv(ks, G), repeat_kv(vs, G), rlay)
+                    out.backward(dout.float())
+                    continue
                 qs = q[:1, :G].float().requires_grad_(True)
                 ks = k[:1, :1].float().requires_grad_(True)
                 vs = v[:1, :1].float().requires_grad_(True)
@@ -577,8 +602,12 @@ def cpu_baseline(wl: Workload, seed=0, reps=1):
         from oracle import attn_oracle as O
 
         rope = O.make_sectioned_rope(wl.rope.inv_freq.cpu().numpy(), wl.streams, wl.sections)
-        qs, ks, vs = (x[:1, :n].float().numpy() for x, n in ((q, G), (k, 1), (v, 1)))
-        dos = dout[:1, :, :G].float().numpy()
+        if wl.full_cpu:
+            lay = wl.row_lists()
+            qs, ks, vs, dos = (x.float().numpy() for x in (q, k, v, dout))
+        else:
+            qs, ks, vs = (x[:1, :n].float().numpy() for x, n in ((q, G), (k, 1), (v, 1)))
+            dos = dout[:1, :, :G].float().numpy()
         with threadpool_limits(limits=cores):
             t0 = time.perf_counter()
             for _ in range(reps):
@@ -586,8 +615,10 @@ def cpu_baseline(wl: Workload, seed=0, reps=1):
                 O.attn_backward(qs, ks, vs, dos, lay, rope, dtype=np.float32)
             dt = (time.perf_counter() - t0) / reps
         kind, what = "port", "oracle (numpy restatement of the reference's eager path), fp32"
+    sample = (f"the whole workload (B={wl.batch}, {HQ} query heads), T={Tw}" if wl.full_cpu
+              else f"batch row 0, kv group 0 ({G} query heads), T={Tw}")
     return {"value": round(flops / dt / 1e12, 6), "unit": "TFLOP/s", "cores": cores, "kind": kind,
-            "sample": f"batch row 0, kv group 0 ({G} query heads), T={Tw}: fwd+bwd, {what}, {dt:.2f} s"}
+            "sample": f"{sample}: fwd+bwd, {what}, {dt:.2f} s"}
 
 
 def run_reference(args):

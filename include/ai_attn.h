@@ -43,7 +43,7 @@
 extern "C" {
 #endif
 
-#define AI_ATTN_ABI_VERSION 7
+#define AI_ATTN_ABI_VERSION 8
 
 typedef enum AiDtype {
   AI_DTYPE_BF16 = 0,
@@ -119,13 +119,28 @@ typedef struct AiAttnLayout {
   int32_t kv_tile;            /* keys per dK/dV work item (ai_attn_kv_tile_rows) */
   const int32_t* kv_items;    /* [n_kv_items][4]: row, j0, j1, 0 */
   int32_t n_kv_items;
-  int32_t n_kv_abs_items;     /* the first n_kv_abs_items items see a block with AI_BLOCKF_ABS */
+  int32_t n_kv_abs_items;     /* the first n_kv_abs_items items hold an abs key of some block */
   int32_t all_rows_owned;     /* 1: row_cov[b] == seq_len for every b (no diagonal-only rows), so the
                                  fill launches are skipped; 0: not known (they run) */
   int32_t n_fwd_short_items;  /* the n_fwd_short_items items right after the abs items have at most
                                  fwd_tile / 2 query rows (ABI 7): with four or more query heads per KV
                                  head the tensor-core kernels pack two heads' rows of such an item into
                                  one 128-row tile; 0: no item is treated as short */
+  /* dK/dV work split (ABI 8; all optional: n_kv_chunks = 0 runs one CTA per key tile).  The 64-row
+     query tiles a key tile's blocks give it (blocks with an abs key among its keys left out) are
+     numbered in block order; a chunk is a range of them.  A key tile with one chunk is written
+     directly; the chunks of a longer one write fp32 partial sums (ai_attn_bwd_workspace counts
+     them) that one more launch adds up in chunk order (deterministic). */
+  const int32_t* kv_chunks;   /* [n_kv_chunks][4]: kv item, first query tile, end query tile, partial
+                                 slot (-1: the item's only chunk) */
+  int32_t n_kv_chunks;
+  int32_t n_kv_partials;      /* partial slots */
+  const int32_t* kv_reduce;   /* [n_kv_reduce][4]: kv item, first slot, slots, 0 */
+  int32_t n_kv_reduce;
+  int32_t kv_cost_max;        /* work of the costliest key tile and of all key tiles (query tiles
+                                 plus two per block a key tile walks): the chunks run only when the
+                                 costliest tile outweighs the average work of an SM */
+  int32_t kv_cost_total;
 } AiAttnLayout;
 
 typedef struct AiAttnFwdArgs {
@@ -340,6 +355,8 @@ typedef struct AiPrepSizes {
   int32_t n_blocks;           /* block records over the batch */
   int32_t n_fwd_items;
   int32_t n_kv_items;
+  int32_t n_kv_chunks;        /* entries of kv_chunks (at least n_kv_items) */
+  int32_t n_kv_reduce;        /* entries of kv_reduce */
   int64_t n_keys;             /* key words (sum over the distinct lists) */
   int64_t p_min, p_max;       /* position ids the rotary table must cover (row r = position p_min + r) */
 } AiPrepSizes;
@@ -356,6 +373,11 @@ typedef struct AiPrepTables {
   int32_t* k_own;             /* [batch][seq_len] */
   int32_t* fwd_items;         /* [n_fwd_items][4] */
   int32_t* kv_items;          /* [n_kv_items][4] */
+  int32_t* kv_chunks;         /* [n_kv_chunks][4] */
+  int32_t* kv_reduce;         /* [n_kv_reduce][4] */
+  int32_t n_kv_partials;
+  int32_t kv_cost_max;
+  int32_t kv_cost_total;
   int32_t n_fwd_abs_items;
   int32_t n_fwd_short_items;
   int32_t n_kv_abs_items;

@@ -74,8 +74,8 @@ def test_fp32_index_losses_match_reference(case, es, cuda_device):
     tq, tk = (torch.as_tensor(x).to(cuda_device).requires_grad_(True) for x in (q, k))
     (sl, el), _ = compute_index_losses_b200(rope, tq, tk, blocks, cursor, editable_start=es)
     (sl + 2 * el).backward()
-    np.testing.assert_allclose(float(sl), g[f"start_loss_es{es}"], rtol=1e-4, atol=1e-4)
-    np.testing.assert_allclose(float(el), g[f"end_loss_es{es}"], rtol=1e-4, atol=1e-4)
+    np.testing.assert_allclose(sl.item(), g[f"start_loss_es{es}"], rtol=1e-4, atol=1e-4)
+    np.testing.assert_allclose(el.item(), g[f"end_loss_es{es}"], rtol=1e-4, atol=1e-4)
     np.testing.assert_allclose(tq.grad.cpu().numpy(), g[f"dq_es{es}"], rtol=1e-4, atol=1e-4)
     np.testing.assert_allclose(tk.grad.cpu().numpy(), g[f"dk_es{es}"], rtol=1e-4, atol=1e-4)
 
@@ -116,8 +116,8 @@ def test_bf16_index_losses_on_the_training_chain(cuda_device):
     edits = np.asarray([(e, s, t) for e, (s, t) in sorted(cursor.items())])
     osl, oel, odq, odk = O.index_losses(q.double().numpy(), k.double().numpy(), lay, types, edits,
                                         O.make_rope(inv), w_start=1.0, w_end=2.0)
-    assert abs(float(sl) - osl) <= 1e-2 * abs(osl) + 1e-2
-    assert abs(float(el) - oel) <= 1e-2 * abs(oel) + 1e-2
+    assert abs(sl.item() - osl) <= 1e-2 * abs(osl) + 1e-2
+    assert abs(el.item() - oel) <= 1e-2 * abs(oel) + 1e-2
     assert rel_l2(tq.grad.double().cpu().numpy(), odq) <= 1e-2
     assert rel_l2(tk.grad.double().cpu().numpy(), odk) <= 1e-2
     # returned weights: the masked, scaled logits of the first edit's rows

@@ -236,3 +236,46 @@ def test_native_tables_match_numpy_restatement(which):
         for name in ("n_fwd_abs_items", "n_kv_abs_items", "n_fwd_short_items", "pairs_per_head", "all_rows_owned",
                      "p_min", "n_pos"):
             assert getattr(c, name) == want[name], name
+
+
+@pytest.mark.parametrize("which", ["bench1", "benchE", "bench2a"])
+def test_kv_chunks_partition_each_key_tile(which):
+    """dK/dV chunks: the query tiles of every key tile (64-row tiles of the
+    blocks that see it, blocks with an abs key among its keys left out) are
+    covered once, in order; split tiles own consecutive partial slots listed
+    in kv_reduce; the costs are query tiles plus two per block."""
+    import bench
+
+    wl = bench.build_workload(which[5:], 0, "cpu")
+    c = compile_layout(wl.rows, wl.batch, wl.seq_len, 128, torch.bfloat16, wl.rope, "cpu")
+    blocks, kv, ch, red = (x.numpy() for x in (c.blocks, c.kv_items, c.kv_chunks, c.kv_reduce))
+    row_blocks = c.row_blocks.numpy()
+    any_abs = c.n_kv_abs_items > 0
+    cost_max = cost_total = 0
+    by_item = {}
+    for item, q0, q1, slot in ch:
+        by_item.setdefault(int(item), []).append((int(q0), int(q1), int(slot)))
+    assert sorted(by_item) == list(range(kv.shape[0]))
+    reduce_of = {int(r[0]): (int(r[1]), int(r[2])) for r in red}
+    for k, (row, j0, j1, _) in enumerate(kv):
+        nq, cost = 0, 0
+        for bi in range(row_blocks[row], row_blocks[row + 1]):
+            _, s, e, _, kv_lo, flags, alo, ahi = blocks[bi]
+            if not (e > j0 and kv_lo < j1 and max(s, j0) < e):
+                continue
+            if any_abs and flags & 2 and (ahi <= alo or (j0 < ahi and alo < j1)):
+                continue
+            n = (e - max(s, j0) + 63) // 64
+            nq += n
+            cost += n + 2
+        cost_max, cost_total = max(cost_max, cost), cost_total + cost
+        parts = sorted(by_item[k])
+        assert parts[0][0] == 0 and parts[-1][1] == nq
+        assert all(a[1] == b[0] for a, b in zip(parts, parts[1:]))
+        if len(parts) == 1:
+            assert parts[0][2] == -1 and k not in reduce_of
+        else:
+            first, n = reduce_of[k]
+            assert n == len(parts) and [p[2] for p in parts] == list(range(first, first + n))
+    assert c.kv_cost_max == cost_max and c.kv_cost_total == cost_total
+    assert c.n_kv_partials == sum(n for _, n in reduce_of.values())

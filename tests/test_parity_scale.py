@@ -185,3 +185,44 @@ def test_bf16_bench_layout_documents(cuda_device):
                 _check_bf16(sl, want, f"bench row {b} doc {di} group {grp}")
                 checked += 1
     assert checked >= 2 * (len(rows[0].boundary_indices) + 3)
+
+
+def test_bf16_split_key_tiles_match_whole_key_tiles(cuda_device):
+    """The +E chain's long key tiles are split into chunks of query tiles
+    whose fp32 partial sums a second launch adds up (when the workspace holds
+    them); without room for the partials every key tile runs whole.  Both
+    give the same gradients up to the order of the fp32 sums."""
+    import ctypes
+
+    from autoindexer_b200 import _lib
+    from autoindexer_b200.attention import _fwd_args, _t4
+
+    lay, q, k, v, dout, mod, _ = _chain_e(8, 2, 128, 22)
+    tq, tk, tv, tdo = (torch.as_tensor(x).to(cuda_device, torch.bfloat16) for x in (q, k, v, dout))
+    B, Hq, T, D = tq.shape
+    layout = compile_layout(lay, B, T, D, torch.bfloat16, mod.to(cuda_device), cuda_device)
+    assert layout.n_kv_partials > 0
+    out, lse, fws = attn_fwd(tq, tk, tv, layout, D ** -0.5, keep_workspace=True)
+    lib = _lib.lib()
+    stream = ctypes.c_void_p(torch.cuda.current_stream(cuda_device).cuda_stream)
+    res = []
+    for split in (True, False):
+        grads = [torch.empty_like(x) for x in (tq, tk, tv)]
+        a = _lib.AiAttnBwdArgs()
+        a.fwd = _fwd_args(tq, tk, tv, out.permute(0, 2, 1, 3), lse, layout, D ** -0.5)
+        a.dout = _t4(tdo.permute(0, 2, 1, 3))
+        a.dq, a.dk, a.dv = (_t4(x) for x in grads)
+        a.fwd.workspace, a.fwd.workspace_bytes, a.fwd_rotated = fws.data_ptr(), fws.numel(), 1
+        nbytes = ctypes.c_size_t(0)
+        assert lib.ai_attn_bwd_workspace(ctypes.byref(a), ctypes.byref(nbytes)) == 0
+        delta_only = (B * Hq * T * 4 + 255) // 256 * 256
+        assert nbytes.value > delta_only  # the partials are asked for
+        ws = torch.empty(nbytes.value if split else delta_only, dtype=torch.uint8, device=cuda_device)
+        a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
+        assert lib.ai_attn_bwd(ctypes.byref(a), stream) == 0
+        torch.cuda.synchronize(cuda_device)
+        assert read_status(cuda_device) == 0
+        res.append([x.double().cpu().numpy() for x in grads])
+    for name, a_, b_ in zip(("dq", "dk", "dv"), *res):
+        assert rel_l2(a_, b_) <= 2e-3, (name, rel_l2(a_, b_))
+    assert np.array_equal(res[0][0], res[1][0])  # dQ does not take part in the split
