@@ -32,7 +32,7 @@ LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_ai_attn.so
 DTYPE_BF16, DTYPE_F16, DTYPE_F32 = 0, 1, 2
 # AiProfKind, in order.
 PROF_KINDS = ("prerot", "fwd", "fwd_fill", "delta", "dq", "dkdv", "bwd_fill", "simt", "decode")
-ABI_VERSION = 8
+ABI_VERSION = 9
 
 # Every function include/ai_attn.h declares.
 EXPORTED_SYMBOLS = (
@@ -103,6 +103,11 @@ class AiAttnLayout(ctypes.Structure):
         ("n_kv_reduce", ctypes.c_int32),
         ("kv_cost_max", ctypes.c_int32),
         ("kv_cost_total", ctypes.c_int32),
+        ("blk_cls", ctypes.c_void_p),
+        ("chunk_cls", ctypes.c_void_p),
+        ("n_chunk_cls", ctypes.c_int32),
+        ("rot_classes", ctypes.c_void_p),
+        ("n_rot_classes", ctypes.c_int32),
     ]
 
 
@@ -219,6 +224,8 @@ class AiPrepSizes(ctypes.Structure):
         ("n_kv_items", ctypes.c_int32),
         ("n_kv_chunks", ctypes.c_int32),
         ("n_kv_reduce", ctypes.c_int32),
+        ("n_chunk_cls", ctypes.c_int32),
+        ("n_rot_classes", ctypes.c_int32),
         ("n_keys", ctypes.c_int64),
         ("p_min", ctypes.c_int64),
         ("p_max", ctypes.c_int64),
@@ -237,6 +244,9 @@ class AiPrepTables(ctypes.Structure):
         ("kv_items", ctypes.c_void_p),
         ("kv_chunks", ctypes.c_void_p),
         ("kv_reduce", ctypes.c_void_p),
+        ("blk_cls", ctypes.c_void_p),
+        ("chunk_cls", ctypes.c_void_p),
+        ("rot_classes", ctypes.c_void_p),
         ("n_kv_partials", ctypes.c_int32),
         ("kv_cost_max", ctypes.c_int32),
         ("kv_cost_total", ctypes.c_int32),

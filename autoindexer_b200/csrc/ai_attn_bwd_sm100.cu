@@ -115,7 +115,7 @@ constexpr uint32_t C_S = 0, C_DP = 64, C_DQR = 128, C_DQA = 256, C_SA = 384;
 
 __global__ void __launch_bounds__(kThreads, 1)
     dq_kernel(const AiAttnBwdArgs a, const float* __restrict__ delta, const __grid_constant__ CUtensorMap tm_k,
-              const __grid_constant__ CUtensorMap tm_v) {
+              const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_kc, const int prerot) {
   using namespace dq;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = tile::align1024(smem_raw);
@@ -137,6 +137,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const bool has_abs = (blk.flags & AI_BLOCKF_ABS) != 0;
   const int kv_hi = min(blk.e, q1);
   const int i = q0 + tid % slot;
+  // The block's rotation classes: a 64-key tile with one comes rotated.
+  const int cls = block_classes(L, item[0], prerot != 0);
 
   if (tid == 0) {
     ptx::mbar_init(bar_tma, 1);
@@ -202,14 +204,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   int n_tiles = 0;
   bool aborted = false, dqa_started = false;
 
-  for (int k0 = blk.kv_lo; k0 < kv_hi; k0 += BN) {
+  for (int k0 = blk.kv_lo, jt = 0; k0 < kv_hi; k0 += BN, ++jt) {
     // Only a tile that holds one of the block's abs keys needs S_abs and dQabs.
     const bool tabs = blk.abs_in(k0, min(k0 + BN, kv_hi));
+    const int kc = cls >= 0 ? chunk_class(L, cls, jt, f.status) : -1;
     if (tid == 0) {
       ptx::fence_proxy_async_smem();
       ptx::mbar_arrive_expect_tx(bar_tma, 2 * 16384);
-      ptx::tma_load_4d(sbase + KR, &tm_k, bar_tma, 0, k0, hk, b);
-      ptx::tma_load_4d(sbase + KR + 8192, &tm_k, bar_tma, 64, k0, hk, b);
+      if (kc >= 0) {
+        ptx::tma_load_4d(sbase + KR, &tm_kc, bar_tma, 0, 0, hk, kc);
+        ptx::tma_load_4d(sbase + KR + 8192, &tm_kc, bar_tma, 64, 0, hk, kc);
+      } else {
+        ptx::tma_load_4d(sbase + KR, &tm_k, bar_tma, 0, k0, hk, b);
+        ptx::tma_load_4d(sbase + KR + 8192, &tm_k, bar_tma, 64, k0, hk, b);
+      }
       ptx::tma_load_4d(sbase + VV, &tm_v, bar_tma, 0, k0, hk, b);
       ptx::tma_load_4d(sbase + VV + 8192, &tm_v, bar_tma, 64, k0, hk, b);
     }
@@ -217,24 +225,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     if (*s_abort) { aborted = true; break; }
 
-    // Rotate key rows in place: thread -> (row tid % 64, chunk pairs 4*(tid/64) .. +3).
+    // Rotate key rows in place (fp16 (cos, sin) table, as the rotated copies
+    // are made): thread -> (row tid % 64, chunk pairs 4*(tid/64) .. +3).
     {
       const int r = tid & 63, cg = tid >> 6, j = k0 + r;
       uint32_t info = 0;
       if (j < kv_hi) {
         info = (uint32_t)L.key_info[blk.key_off + j];
-        const int p = key_row(info, L.n_pos, f.status);
-        const float* cs = L.rope_cos + (int64_t)p * (D / 2);
-        const float* sn = L.rope_sin + (int64_t)p * (D / 2);
+        if (kc < 0) {
+          const int p = key_row(info, L.n_pos, f.status);
+          const uint4* tp = static_cast<const uint4*>(L.rope_cs16) + (int64_t)p * (D / 8);
 #pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
-          const int c = 4 * cg + cc;
-          uint4* pa = reinterpret_cast<uint4*>(sm + KR + chunk_off<BN>(r, c));
-          uint4* pb = reinterpret_cast<uint4*>(sm + KR + chunk_off<BN>(r, c + 8));
-          uint4 y1, y2;
-          rotate8(*pa, *pb, cs + 8 * c, sn + 8 * c, y1, y2);
-          *pa = y1;
-          *pb = y2;
+          for (int cc = 0; cc < 4; ++cc) {
+            const int c = 4 * cg + cc;
+            uint4* pa = reinterpret_cast<uint4*>(sm + KR + chunk_off<BN>(r, c));
+            uint4* pb = reinterpret_cast<uint4*>(sm + KR + chunk_off<BN>(r, c + 8));
+            uint4 y1, y2;
+            tile::rotate8h(*pa, *pb, __ldg(tp + 2 * c), __ldg(tp + 2 * c + 1), y1, y2);
+            *pa = y1;
+            *pb = y2;
+          }
         }
       }
       if (cg == 0) s_info[r] = info;
@@ -405,7 +415,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     dkdv_kernel(const AiAttnBwdArgs a, const float* __restrict__ delta, const __grid_constant__ CUtensorMap tm_k,
                 const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_q,
                 const __grid_constant__ CUtensorMap tm_do, const __grid_constant__ CUtensorMap tm_qp,
-                const __grid_constant__ CUtensorMap tm_dop, const int abs_only) {
+                const __grid_constant__ CUtensorMap tm_dop, const __grid_constant__ CUtensorMap tm_kc,
+                const int prerot, const int abs_only) {
   using namespace kv;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = tile::align1024(smem_raw);
@@ -469,13 +480,33 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool has_abs = (blk.flags & AI_BLOCKF_ABS) != 0;
     if (abs_only && !blk.abs_in(j0, j1)) continue;
     const int kmax = min(j1, blk.e);
+    // The tile's two 64-key chunks in this block's rotation classes, if any.
+    int c0 = -1, c1 = -1;
+    {
+      const int base = block_classes(L, bi, prerot != 0);
+      if (base >= 0 && j0 >= blk.kv_lo && !(blk.flags & AI_BLOCKF_OWNPOS)) {
+        const int ci = (j0 - blk.kv_lo) / AI_ROT_CLASS_KEYS;
+        const int n = 2 * ((blk.e - blk.kv_lo + 2 * AI_ROT_CLASS_KEYS - 1) / (2 * AI_ROT_CLASS_KEYS));
+        c0 = chunk_class(L, base, ci, f.status);
+        c1 = ci + 1 < n ? chunk_class(L, base, ci + 1, f.status) : c0;
+      }
+    }
+    const bool ctile = c0 >= 0 && c1 >= 0;
 
-    // Raw K tile, rotated in place by this block's key positions.
+    // K tile: the rotated class copies, or raw and rotated in place by this
+    // block's key positions.
     if (tid == 0) {
       ptx::fence_proxy_async_smem();
       ptx::mbar_arrive_expect_tx(bar_k, 32768);
-      ptx::tma_load_4d(sbase + KR, &tm_k, bar_k, 0, j0, hk, b);
-      ptx::tma_load_4d(sbase + KR + 16384, &tm_k, bar_k, 64, j0, hk, b);
+      if (ctile) {
+        ptx::tma_load_4d(sbase + KR, &tm_kc, bar_k, 0, 0, hk, c0);
+        ptx::tma_load_4d(sbase + KR + 8192, &tm_kc, bar_k, 0, 0, hk, c1);
+        ptx::tma_load_4d(sbase + KR + 16384, &tm_kc, bar_k, 64, 0, hk, c0);
+        ptx::tma_load_4d(sbase + KR + 16384 + 8192, &tm_kc, bar_k, 64, 0, hk, c1);
+      } else {
+        ptx::tma_load_4d(sbase + KR, &tm_k, bar_k, 0, j0, hk, b);
+        ptx::tma_load_4d(sbase + KR + 16384, &tm_k, bar_k, 64, j0, hk, b);
+      }
     }
     wait_or_flag(bar_k, ph_k, s_abort, f.status);
     __syncthreads();
@@ -485,16 +516,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (j < kmax) {
       my_info = (uint32_t)L.key_info[blk.key_off + j];
       my_row = key_row(my_info, L.n_pos, f.status);
-      const float* cs = L.rope_cos + (int64_t)my_row * (D / 2);
-      const float* sn = L.rope_sin + (int64_t)my_row * (D / 2);
+      if (!ctile) {
+        const uint4* tp = static_cast<const uint4*>(L.rope_cs16) + (int64_t)my_row * (D / 8);
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        uint4* pa = reinterpret_cast<uint4*>(sm + KR + chunk_off<BN>(tid, c));
-        uint4* pb = reinterpret_cast<uint4*>(sm + KR + chunk_off<BN>(tid, c + 8));
-        uint4 y1, y2;
-        rotate8(*pa, *pb, cs + 8 * c, sn + 8 * c, y1, y2);
-        *pa = y1;
-        *pb = y2;
+        for (int c = 0; c < 8; ++c) {
+          uint4* pa = reinterpret_cast<uint4*>(sm + KR + chunk_off<BN>(tid, c));
+          uint4* pb = reinterpret_cast<uint4*>(sm + KR + chunk_off<BN>(tid, c + 8));
+          uint4 y1, y2;
+          tile::rotate8h(*pa, *pb, __ldg(tp + 2 * c), __ldg(tp + 2 * c + 1), y1, y2);
+          *pa = y1;
+          *pb = y2;
+        }
       }
     }
     const bool key_ok = (my_info & AI_KEY_ATTN) != 0;
@@ -824,8 +856,15 @@ constexpr long long kWait = 1000000000LL;
 struct Unit {
   Block blk;
   int q0, q1, h0, pk, hk, kv_lo, kv_hi, n;
+  int cls;  // the block's first rotation-class entry (chunk_cls), -1: none
   bool masked, k_pre;
 };
+
+// Rotation class of K tile j (64 keys: one class chunk) of a unit, -1: the
+// tile is rotated in shared memory (or comes from k_rot when k_pre).
+__device__ __forceinline__ int tile_class(const AiAttnLayout& L, const Unit& w, int j, int32_t* status) {
+  return w.cls < 0 ? -1 : chunk_class(L, w.cls, j, status);
+}
 
 __device__ __forceinline__ int unit_head(const Unit& w, int t, int r) {
   return w.pk == 2 ? w.h0 + 2 * t + (r >> 6) : w.h0 + t;
@@ -857,6 +896,7 @@ __device__ __forceinline__ Unit load_unit(const AiAttnFwdArgs& f, int u, int pre
   w.n = w.kv_hi > w.kv_lo ? (w.kv_hi - w.kv_lo + BN - 1) / BN : 0;
   w.masked = (w.blk.flags & AI_BLOCKF_MASKED) != 0;
   w.k_pre = prerot && (w.blk.flags & AI_BLOCKF_OWNPOS);
+  w.cls = w.k_pre ? -1 : block_classes(L, item[0], prerot != 0);
   return w;
 }
 }  // namespace dqw
@@ -886,7 +926,8 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_qr,
                    const __grid_constant__ CUtensorMap tm_do, const __grid_constant__ CUtensorMap tm_kr,
                    const __grid_constant__ CUtensorMap tm_qr64, const __grid_constant__ CUtensorMap tm_do64,
-                   const int prerot, const int n_units, const int n_pack_units) {
+                   const __grid_constant__ CUtensorMap tm_kc, const int prerot, const int n_units,
+                   const int n_pack_units) {
   using namespace dqw;
   // The dK/dV kernel launched after this one reads nothing it writes: let it
   // start as soon as every CTA here has started, so its CTAs take each SM as
@@ -1166,8 +1207,14 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
           }
           const uint32_t kb = sbase + KB + 16384u * (uint32_t)slot, vb = sbase + VB + 16384u * (uint32_t)slot;
           ptx::mbar_arrive_expect_tx(bar(KV_FULL + slot), 32768);
-          ptx::tma_load_4d(kb, mk, bar(KV_FULL + slot), 0, k0, w.hk, b);
-          ptx::tma_load_4d(kb + 8192, mk, bar(KV_FULL + slot), 64, k0, w.hk, b);
+          const int kc = tile_class(L, w, j, f.status);
+          if (kc >= 0) {
+            ptx::tma_load_4d(kb, &tm_kc, bar(KV_FULL + slot), 0, 0, w.hk, kc);
+            ptx::tma_load_4d(kb + 8192, &tm_kc, bar(KV_FULL + slot), 64, 0, w.hk, kc);
+          } else {
+            ptx::tma_load_4d(kb, mk, bar(KV_FULL + slot), 0, k0, w.hk, b);
+            ptx::tma_load_4d(kb + 8192, mk, bar(KV_FULL + slot), 64, k0, w.hk, b);
+          }
           ptx::tma_load_4d(vb, &tm_v, bar(KV_FULL + slot), 0, k0, w.hk, b);
           ptx::tma_load_4d(vb + 8192, &tm_v, bar(KV_FULL + slot), 64, k0, w.hk, b);
         }
@@ -1278,9 +1325,10 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
           info = (uint32_t)__ldg(L.key_info + w.blk.key_off + key);
           p = key_row(info, L.n_pos, f.status);
         }
+        const bool pre_tile = w.k_pre || tile_class(L, w, j, f.status) >= 0;
         if (!wait(KV_FULL + slot, (g / kKS) & 1)) break;
         const uint32_t kt = KB + 16384u * (uint32_t)slot;
-        if (!w.k_pre && key < w.kv_hi) {
+        if (!pre_tile && key < w.kv_hi) {
           const uint4* tp = reinterpret_cast<const uint4*>(cs16 + (int64_t)p * (D / 2));
 #pragma unroll
           for (int cg = 0; cg < 2; ++cg) {
@@ -1401,12 +1449,59 @@ struct BlockIter {
   }
 };
 
+// BlockIter with one block of lookahead, grouping consecutive blocks into
+// segments that give the key tile the same rotation: both 64-key chunks of
+// [j0, j0 + 128) in the same rotation classes (the keys every block of the
+// segment attends sit at the same positions).  Within a segment the rotated
+// K tile is loaded once and dKrot accumulates in TMEM; it is folded into dK
+// at the segment's end.  A block without classes for the tile is a segment
+// of its own.
+struct SegIter {
+  BlockIter it, ahead;
+  Block nxt;
+  int2 sig = make_int2(-1, -1), sig_nxt = make_int2(-1, -1);
+  bool has_nxt = false, started = false, seg_first = true, seg_last = true;
+  bool prerot;
+  int32_t* status;
+  __device__ SegIter(const AiAttnLayout* L_, int b_, int j0_, int j1_, bool skip_abs_, int qt0_, int qt1_,
+                     bool prerot_, int32_t* status_)
+      : it(L_, b_, j0_, j1_, skip_abs_, qt0_, qt1_), ahead(it), prerot(prerot_), status(status_) {}
+  // Rotation classes of the tile's two chunks in block bi, (-1, -1): none.
+  __device__ int2 sig_of(int bi, const Block& blk) const {
+    const AiAttnLayout& L = *it.L;
+    const int base = block_classes(L, bi, prerot);
+    if (base < 0 || it.j0 < blk.kv_lo || (blk.flags & AI_BLOCKF_OWNPOS)) return make_int2(-1, -1);
+    const int i = (it.j0 - blk.kv_lo) / AI_ROT_CLASS_KEYS;
+    const int n = 2 * ((blk.e - blk.kv_lo + 2 * AI_ROT_CLASS_KEYS - 1) / (2 * AI_ROT_CLASS_KEYS));
+    const int c0 = chunk_class(L, base, i, status);
+    const int c1 = i + 1 < n ? chunk_class(L, base, i + 1, status) : c0;  // past the block's keys
+    return (c0 >= 0 && c1 >= 0) ? make_int2(c0, c1) : make_int2(-1, -1);
+  }
+  __device__ bool next(Block& blk) {
+    if (!started) {
+      started = true;
+      has_nxt = ahead.next(nxt);
+      if (has_nxt) sig_nxt = sig_of(ahead.bi, nxt);
+    }
+    if (!has_nxt) return false;
+    const int2 prev = sig;
+    it = ahead;
+    blk = nxt;
+    sig = sig_nxt;
+    seg_first = !(sig.x >= 0 && sig.x == prev.x && sig.y == prev.y);
+    has_nxt = ahead.next(nxt);
+    sig_nxt = has_nxt ? sig_of(ahead.bi, nxt) : make_int2(-1, -1);
+    seg_last = !(has_nxt && sig_nxt.x >= 0 && sig_nxt.x == sig.x && sig_nxt.y == sig.y);
+    return true;
+  }
+};
+
 __global__ void __launch_bounds__(kvw::kThreads, 1)
     dkdv_ws_kernel(const AiAttnBwdArgs a, const float* __restrict__ delta, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_q,
                    const __grid_constant__ CUtensorMap tm_do, const __grid_constant__ CUtensorMap tm_kr,
-                   const int prerot, const int item_base, const int skip_abs, const int32_t* __restrict__ chunks,
-                   float* __restrict__ partials) {
+                   const __grid_constant__ CUtensorMap tm_kc, const int prerot, const int item_base,
+                   const int skip_abs, const int32_t* __restrict__ chunks, float* __restrict__ partials) {
   using namespace kvw;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = tile::align1024(smem_raw);
@@ -1474,12 +1569,14 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
     const uint32_t lane_base = (uint32_t)((warp % 4) * 32) << 16;
     const float sl2 = f.scale * kLog2e, scale = f.scale;
     const float2 sl2x2 = make_float2(sl2, sl2), scalex2 = make_float2(scale, scale);
-    BlockIter it(&L, b, j0, j1, skip_abs != 0, qt0, qt1);
+    SegIter sit(&L, b, j0, j1, skip_abs != 0, qt0, qt1, prerot != 0, f.status);
+    const BlockIter& it = sit.it;
     Block blk;
-    int s = 0, nb = 0;
+    int s = 0, seg = -1;
     bool any = false;
-    while (!*s_abort && it.next(blk)) {
+    while (!*s_abort && sit.next(blk)) {
       any = true;
+      seg += sit.seg_first ? 1 : 0;
       const int kmax = min(j1, blk.e), qs = max(blk.s, j0);
       uint32_t info = 0;
       if (j < kmax) info = (uint32_t)__ldg(L.key_info + blk.key_off + j);
@@ -1539,10 +1636,10 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
         ptx::mbar_arrive(bar(P_READY + x));
       }
       if (*s_abort) break;
-      {
-        // Fold this block's dKrot into dK: dK += R(key position)^T dKrot;
+      if (sit.seg_last) {
+        // Fold the segment's dKrot into dK: dK += R(key position)^T dKrot;
         // group t takes the rotation pairs (d, d + 64) with d in [16t, 16t + 16).
-        if (!wait(BLK_DONE, nb & 1)) break;
+        if (!wait(BLK_DONE, seg & 1)) break;
         ptx::tc_fence_after();
         const int p = key_row(info, L.n_pos, f.status);
         const uint4* tp = reinterpret_cast<const uint4*>(cs16 + (int64_t)p * (D / 2));
@@ -1568,7 +1665,6 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
         ptx::tc_fence_before();
         ptx::mbar_arrive(bar(FOLD_DONE));
       }
-      ++nb;
     }
     // Epilogue: group t writes the columns it folded, d in [16t, 16t + 16)
     // and [64 + 16t, 80 + 16t), of dK (smem) and dV (TMEM; the last block's
@@ -1623,16 +1719,28 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
       ptx::mbar_arrive_expect_tx(bar(V_FULL), 32768);
       ptx::tma_load_4d(sbase + V, &tm_v, bar(V_FULL), 0, j0, hk, b);
       ptx::tma_load_4d(sbase + V + 16384, &tm_v, bar(V_FULL), 64, j0, hk, b);
-      BlockIter it(&L, b, j0, j1, skip_abs != 0, qt0, qt1);
+      SegIter sit(&L, b, j0, j1, skip_abs != 0, qt0, qt1, prerot != 0, f.status);
+      const BlockIter& it = sit.it;
       Block blk;
-      int s = 0, nb = 0;
+      int s = 0, seg = -1;
       bool ok = true;
-      while (ok && it.next(blk)) {
-        if (nb > 0 && !wait(BLK_DONE, (nb - 1) & 1)) break;
-        const CUtensorMap* mk = (prerot && (blk.flags & AI_BLOCKF_OWNPOS)) ? &tm_kr : &tm_k;
-        ptx::mbar_arrive_expect_tx(bar(K_FULL), 32768);
-        ptx::tma_load_4d(sbase + K, mk, bar(K_FULL), 0, j0, hk, b);
-        ptx::tma_load_4d(sbase + K + 16384, mk, bar(K_FULL), 64, j0, hk, b);
+      while (ok && sit.next(blk)) {
+        if (sit.seg_first) {
+          // A new segment's K tile, once the previous segment's MMAs are done.
+          if (++seg > 0 && !wait(BLK_DONE, (seg - 1) & 1)) break;
+          ptx::mbar_arrive_expect_tx(bar(K_FULL), 32768);
+          if (sit.sig.x >= 0) {
+            // rows 0-63 and 64-127 from the two chunks' rotated copies
+            ptx::tma_load_4d(sbase + K, &tm_kc, bar(K_FULL), 0, 0, hk, sit.sig.x);
+            ptx::tma_load_4d(sbase + K + 8192, &tm_kc, bar(K_FULL), 0, 0, hk, sit.sig.y);
+            ptx::tma_load_4d(sbase + K + 16384, &tm_kc, bar(K_FULL), 64, 0, hk, sit.sig.x);
+            ptx::tma_load_4d(sbase + K + 16384 + 8192, &tm_kc, bar(K_FULL), 64, 0, hk, sit.sig.y);
+          } else {
+            const CUtensorMap* mk = (prerot && (blk.flags & AI_BLOCKF_OWNPOS)) ? &tm_kr : &tm_k;
+            ptx::tma_load_4d(sbase + K, mk, bar(K_FULL), 0, j0, hk, b);
+            ptx::tma_load_4d(sbase + K + 16384, mk, bar(K_FULL), 64, j0, hk, b);
+          }
+        }
         const int qs = max(blk.s, j0), nsteps = n_steps_of(it);
         for (int st = 0; st < nsteps; ++st, ++s) {
           const int qslot = s % kQS, q0 = qs + (it.lq0 + st / G) * BQ, h = hk * G + st % G;
@@ -1647,7 +1755,6 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
           ptx::tma_load_4d(ob, &tm_do, bar(Q_FULL + qslot), 0, q0, h, b);
           ptx::tma_load_4d(ob + 8192, &tm_do, bar(Q_FULL + qslot), 64, q0, h, b);
         }
-        ++nb;
       }
     }
   } else if (warp == 4 * kGroups + 1) {
@@ -1692,14 +1799,19 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
       }
     };
     bool ok = wait_u(V_FULL, 0);
-    BlockIter it(&L, b, j0, j1, skip_abs != 0, qt0, qt1);
+    SegIter sit(&L, b, j0, j1, skip_abs != 0, qt0, qt1, prerot != 0, f.status);
+    const BlockIter& it = sit.it;
     Block blk;
-    int s = 0, nb = 0, sl = 0;
+    int s = 0, seg = -1, sl = 0;
     uint32_t ph = 0;
     bool dv_started = false;
-    while (ok && it.next(blk)) {
+    while (ok && sit.next(blk)) {
       const int nsteps = n_steps_of(it);
-      if (!wait_u(K_READY, nb & 1)) break;
+      const bool seg_first = sit.seg_first;
+      if (seg_first) {
+        ++seg;
+        if (!wait_u(K_READY, seg & 1)) break;
+      }
       ptx::tc_fence_after();
       const int sb = s;
       // scores of the block's first step
@@ -1723,7 +1835,7 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
           ok = false;
           break;
         }
-        if (s == sb && nb > 0 && !wait_u(FOLD_DONE, (nb - 1) & 1)) {
+        if (s == sb && seg_first && seg > 0 && !wait_u(FOLD_DONE, (seg - 1) & 1)) {
           ok = false;
           break;
         }
@@ -1736,7 +1848,7 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
           const uint32_t ca = cb + (uint32_t)(kCols * kk);
           const uint64_t ko = (uint64_t)(2048 * kk) >> 4;
           ptx::mma_ts_w(tmem + C_DV, ca, dqa + kDo + ko, idesc_acc, (dv_started || kk > 0) ? 1u : 0u);
-          ptx::mma_ts_w(tmem + C_DKR, ca + 64u, dqa + ko, idesc_acc, (s > sb || kk > 0) ? 1u : 0u);
+          ptx::mma_ts_w(tmem + C_DKR, ca + 64u, dqa + ko, idesc_acc, (s > sb || kk > 0 || !seg_first) ? 1u : 0u);
         }
         ptx::mma_commit_w(bar(Q_EMPTY + sl));
         dv_started = true;
@@ -1745,22 +1857,23 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
         advance(sl1, ph1);
       }
       if (!ok) break;
-      ptx::mma_commit_w(bar(BLK_DONE));
-      ++nb;
+      if (sit.seg_last) ptx::mma_commit_w(bar(BLK_DONE));
     }
     ptx::mma_commit_w(bar(FINAL));
     ptx::mbar_wait(bar(FINAL), 0, kWait);
   } else {
     // ------------------------------------------------------------ rotation (warps 18-19)
     const int rt = tid - 32 * (4 * kGroups + 2);  // 0..63: Q row rt, K rows rt and rt + 64
-    BlockIter it(&L, b, j0, j1, skip_abs != 0, qt0, qt1);
+    SegIter sit(&L, b, j0, j1, skip_abs != 0, qt0, qt1, prerot != 0, f.status);
+    const BlockIter& it = sit.it;
     Block blk;
-    int s = 0, nb = 0;
-    while (!*s_abort && it.next(blk)) {
-      // K rows by this block's key position (already rotated when the block
-      // reads the once-rotated copy).
-      {
-        const bool k_pre = prerot && (blk.flags & AI_BLOCKF_OWNPOS);
+    int s = 0, seg = -1;
+    while (!*s_abort && sit.next(blk)) {
+      // K rows of a new segment by its key positions (already rotated when
+      // they come from k_rot or the rotation-class copies).
+      if (sit.seg_first) {
+        ++seg;
+        const bool k_pre = (prerot && (blk.flags & AI_BLOCKF_OWNPOS)) || sit.sig.x >= 0;
         const int kend = min(j1, blk.e);
         int p[2] = {0, 0};
 #pragma unroll
@@ -1768,7 +1881,7 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
           const int key = j0 + rt + kRot * u;
           if (key < kend) p[u] = key_row((uint32_t)__ldg(L.key_info + blk.key_off + key), L.n_pos, f.status);
         }
-        if (!wait(K_FULL, nb & 1)) break;
+        if (!wait(K_FULL, seg & 1)) break;
 #pragma unroll 1
         for (int u = 0; u < 2; ++u) {
           const int kr = rt + kRot * u;
@@ -1833,7 +1946,6 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
         ptx::fence_proxy_async_smem();
         ptx::mbar_arrive(bar(Q_READY + qslot));
       }
-      ++nb;
     }
   }
 
@@ -1912,9 +2024,9 @@ int sm100_bwd(const AiAttnBwdArgs& a, float* delta, void* rot, bool rot_ready, f
     return AI_ERR_STRIDE;
   // With `rot` scratch, Q and K are rotated once (HBM-bound) and the
   // warp-specialised kernels read the rotated copies.
-  AiTensor4 qr{}, kr{};
+  AiTensor4 qr{}, kr{}, kc{};
   const bool pre = rot != nullptr;
-  if (pre && !sm100_rotated_views(f, rot, &qr, &kr)) return AI_ERR_ALIGN;
+  if (pre && !sm100_rotated_views(f, rot, &qr, &kr, &kc)) return AI_ERR_ALIGN;
   cudaError_t e;
   {
     ProfScope ps(AI_PROF_DELTA, st);
@@ -1937,11 +2049,15 @@ int sm100_bwd(const AiAttnBwdArgs& a, float* delta, void* rot, bool rot_ready, f
     const int G = f.num_q_heads / f.num_kv_heads;
     const int n_single = (G % 2 == 0) ? f.layout.n_fwd_abs_items : f.layout.n_fwd_items;
     const int n_pair = f.layout.n_fwd_items - n_single;
+    CUtensorMap tkc = tk;
+    if (pre && f.layout.n_rot_classes > 0 &&
+        !sm100_make_map(&tkc, kc, f.layout.n_rot_classes, f.num_kv_heads, AI_ROT_CLASS_KEYS, AI_ROT_CLASS_KEYS))
+      return AI_ERR_TMA;
     if (n_single > 0) {
       e = cudaFuncSetAttribute(dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dq::kSmem);
       if (e == cudaSuccess) {
         ProfScope ps(AI_PROF_DQ, st);
-        dq_kernel<<<dim3(n_single, f.num_q_heads), kThreads, dq::kSmem, st>>>(a, delta, tk, tv);
+        dq_kernel<<<dim3(n_single, f.num_q_heads), kThreads, dq::kSmem, st>>>(a, delta, tk, tv, tkc, pre ? 1 : 0);
         e = cudaGetLastError();
       }
     }
@@ -1962,7 +2078,7 @@ int sm100_bwd(const AiAttnBwdArgs& a, float* delta, void* rot, bool rot_ready, f
       if (e == cudaSuccess) {
         ProfScope ps(AI_PROF_DQ, st);
         dq_pers_kernel<<<grid, dqw::kThreads, dqw::kSmem, st>>>(a, delta, tk, tv, tqr, tdo, tkr, tqr64, tdo64,
-                                                                pre ? 1 : 0, n_units, n_pack_units);
+                                                                tkc, pre ? 1 : 0, n_units, n_pack_units);
         e = cudaGetLastError();
       }
     }
@@ -1978,6 +2094,10 @@ int sm100_bwd(const AiAttnBwdArgs& a, float* delta, void* rot, bool rot_ready, f
     tkr = tk;
     if (pre && (!sm100_make_map(&tqr, qr, f.batch, f.num_q_heads, f.seq_len, kv::BQ) ||
                 !sm100_make_map(&tkr, kr, f.batch, f.num_kv_heads, f.seq_len, kv::BN)))
+      return AI_ERR_TMA;
+    CUtensorMap tkc = tk;
+    if (pre && f.layout.n_rot_classes > 0 &&
+        !sm100_make_map(&tkc, kc, f.layout.n_rot_classes, f.num_kv_heads, AI_ROT_CLASS_KEYS, AI_ROT_CLASS_KEYS))
       return AI_ERR_TMA;
     // Every key tile runs on the warp-specialised kernel for the blocks
     // without abs keys; then the key tiles that blocks with abs keys see
@@ -2003,7 +2123,7 @@ int sm100_bwd(const AiAttnBwdArgs& a, float* delta, void* rot, bool rot_ready, f
         attr[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        e = cudaLaunchKernelEx(&cfg, dkdv_ws_kernel, a, (const float*)delta, tk, tv, pre ? tqr : tq, tdo, tkr,
+        e = cudaLaunchKernelEx(&cfg, dkdv_ws_kernel, a, (const float*)delta, tk, tv, pre ? tqr : tq, tdo, tkr, tkc,
                                pre ? 1 : 0, 0, n_abs > 0 ? 1 : 0, split ? f.layout.kv_chunks : (const int32_t*)nullptr,
                                partials);
         if (e == cudaSuccess) e = cudaGetLastError();
@@ -2025,7 +2145,7 @@ int sm100_bwd(const AiAttnBwdArgs& a, float* delta, void* rot, bool rot_ready, f
       if (e == cudaSuccess) {
         ProfScope ps(AI_PROF_DKDV, st);
         dkdv_kernel<<<dim3(n_abs, f.num_kv_heads), kThreads, kv::kSmem, st>>>(a, delta, tk, tv, tq, tdo, tqp, tdop,
-                                                                               1);
+                                                                               tkc, pre ? 1 : 0, 1);
         e = cudaGetLastError();
       }
     }

@@ -74,7 +74,8 @@ using tile::rotate8;
 __device__ __forceinline__ uint32_t chunk_off(int r, int c) { return tile::chunk_off<BM>(r, c); }
 
 __global__ void __launch_bounds__(kThreads, 1)
-    fwd_kernel(const AiAttnFwdArgs a, const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v) {
+    fwd_kernel(const AiAttnFwdArgs a, const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+               const __grid_constant__ CUtensorMap tm_kc, const int prerot) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = tile::align1024(smem_raw);
   const uint32_t sbase = ptx::smem_u32(sm);
@@ -95,6 +96,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int h = (int)blockIdx.y * P + tid / slot, hk = ((int)blockIdx.y * P) / G, b = blk.row;
   const bool has_abs = (blk.flags & AI_BLOCKF_ABS) != 0;
   const int kv_hi = min(blk.e, q1);
+  // The block's rotation classes: K tiles whose two chunks have one come rotated.
+  const int cls = block_classes(L, item[0], prerot != 0);
 
   if (tid == 0) {
     ptx::mbar_init(bar_tma, 1);
@@ -150,15 +153,25 @@ __global__ void __launch_bounds__(kThreads, 1)
   int n_tiles = 0;
   bool aborted = false;
 
-  for (int k0 = blk.kv_lo; k0 < kv_hi; k0 += BN) {
+  for (int k0 = blk.kv_lo, jt = 0; k0 < kv_hi; k0 += BN, ++jt) {
     // Only a tile that holds one of the block's abs keys needs S_abs.
     const bool tabs = blk.abs_in(k0, min(k0 + BN, kv_hi));
-    // 1. K and V tiles by TMA.
+    const int c0 = cls >= 0 ? chunk_class(L, cls, 2 * jt, a.status) : -1;
+    const int c1 = c0 >= 0 ? chunk_class(L, cls, 2 * jt + 1, a.status) : -1;
+    const bool ctile = c0 >= 0 && c1 >= 0;
+    // 1. K and V tiles by TMA (K from its chunks' rotated copies when it has them).
     if (tid == 0) {
       ptx::fence_proxy_async_smem();
       ptx::mbar_arrive_expect_tx(bar_tma, 2 * kTile);
-      ptx::tma_load_4d(sbase + Smem::K, &tm_k, bar_tma, 0, k0, hk, b);
-      ptx::tma_load_4d(sbase + Smem::K + kHalf, &tm_k, bar_tma, 64, k0, hk, b);
+      if (ctile) {
+        ptx::tma_load_4d(sbase + Smem::K, &tm_kc, bar_tma, 0, 0, hk, c0);
+        ptx::tma_load_4d(sbase + Smem::K + kHalf / 2, &tm_kc, bar_tma, 0, 0, hk, c1);
+        ptx::tma_load_4d(sbase + Smem::K + kHalf, &tm_kc, bar_tma, 64, 0, hk, c0);
+        ptx::tma_load_4d(sbase + Smem::K + kHalf + kHalf / 2, &tm_kc, bar_tma, 64, 0, hk, c1);
+      } else {
+        ptx::tma_load_4d(sbase + Smem::K, &tm_k, bar_tma, 0, k0, hk, b);
+        ptx::tma_load_4d(sbase + Smem::K + kHalf, &tm_k, bar_tma, 64, k0, hk, b);
+      }
       ptx::tma_load_4d(sbase + Smem::V, &tm_v, bar_tma, 0, k0, hk, b);
       ptx::tma_load_4d(sbase + Smem::V + kHalf, &tm_v, bar_tma, 64, k0, hk, b);
     }
@@ -173,23 +186,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       break;
     }
 
-    // 2. Rotate key row `tid` in place by its position in this block.
+    // 2. Rotate key row `tid` in place by its position in this block (the
+    // fp16 (cos, sin) table, as the rotated copies are made).
     {
       const int j = k0 + tid;
       uint32_t info = 0;
       if (j < kv_hi) {
         info = (uint32_t)L.key_info[blk.key_off + j];
-        const int p = key_row(info, L.n_pos, a.status);
-        const float* cs = L.rope_cos + (int64_t)p * (D / 2);
-        const float* sn = L.rope_sin + (int64_t)p * (D / 2);
+        if (!ctile) {
+          const int p = key_row(info, L.n_pos, a.status);
+          const uint4* tp = static_cast<const uint4*>(L.rope_cs16) + (int64_t)p * (D / 8);
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          uint4* pa = reinterpret_cast<uint4*>(sm + Smem::K + chunk_off(tid, c));
-          uint4* pb = reinterpret_cast<uint4*>(sm + Smem::K + chunk_off(tid, c + 8));
-          uint4 y1, y2;
-          rotate8(*pa, *pb, cs + 8 * c, sn + 8 * c, y1, y2);
-          *pa = y1;
-          *pb = y2;
+          for (int c = 0; c < 8; ++c) {
+            uint4* pa = reinterpret_cast<uint4*>(sm + Smem::K + chunk_off(tid, c));
+            uint4* pb = reinterpret_cast<uint4*>(sm + Smem::K + chunk_off(tid, c + 8));
+            uint4 y1, y2;
+            tile::rotate8h(*pa, *pb, __ldg(tp + 2 * c), __ldg(tp + 2 * c + 1), y1, y2);
+            *pa = y1;
+            *pb = y2;
+          }
         }
       }
       s_info[tid] = info;
@@ -452,8 +467,19 @@ static_assert(kSmem <= 227 * 1024, "shared memory budget");
 struct Unit {
   Block blk;
   int q0, q1, h0, pk, hk, kv_lo, kv_hi, n;
+  int cls;  // the block's first rotation-class entry (chunk_cls), -1: none
   bool masked, k_pre;
 };
+
+// Rotation classes of the two 64-key chunks of K tile j of a unit: a tile
+// whose chunks both have a class is read rotated from the class copies.
+__device__ __forceinline__ bool class_tile(const AiAttnLayout& L, const Unit& w, int j, int32_t* status, int& c0,
+                                           int& c1) {
+  if (w.cls < 0) return false;
+  c0 = chunk_class(L, w.cls, 2 * j, status);
+  c1 = chunk_class(L, w.cls, 2 * j + 1, status);
+  return c0 >= 0 && c1 >= 0;
+}
 
 // Head and query row of TMEM lane r of tile t.
 __device__ __forceinline__ int unit_head(const Unit& w, int t, int r) {
@@ -486,6 +512,7 @@ __device__ __forceinline__ Unit load_unit(const AiAttnFwdArgs& a, int u, int pre
   w.n = w.kv_hi > w.kv_lo ? (w.kv_hi - w.kv_lo + BN - 1) / BN : 0;
   w.masked = (w.blk.flags & AI_BLOCKF_MASKED) != 0;
   w.k_pre = prerot && (w.blk.flags & AI_BLOCKF_OWNPOS);
+  w.cls = w.k_pre ? -1 : block_classes(L, item[0], prerot != 0);
   return w;
 }
 }  // namespace pf
@@ -494,8 +521,8 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
     fwd_pers_kernel(const AiAttnFwdArgs a, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_qr,
                     const __grid_constant__ CUtensorMap tm_kr, const __grid_constant__ CUtensorMap tm_o,
-                    const __grid_constant__ CUtensorMap tm_qr64, const int prerot, const int n_units,
-                    const int n_pack_units) {
+                    const __grid_constant__ CUtensorMap tm_qr64, const __grid_constant__ CUtensorMap tm_kc,
+                    const int prerot, const int n_units, const int n_pack_units) {
   using namespace pf;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = tile::align1024(smem_raw);
@@ -826,8 +853,18 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
             break;
           }
           ptx::mbar_arrive_expect_tx(bar(K_FULL + slot), kTile);
-          ptx::tma_load_4d(kb, mk, bar(K_FULL + slot), 0, k0, w.hk, b);
-          ptx::tma_load_4d(kb + kHalf, mk, bar(K_FULL + slot), 64, k0, w.hk, b);
+          int c0, c1;
+          if (class_tile(L, w, j, a.status, c0, c1)) {
+            // Rows 0-63 from chunk c0's copy, rows 64-127 from c1's (64-row
+            // boxes land in the same 128-byte-swizzled layout as one 128-row box).
+            ptx::tma_load_4d(kb, &tm_kc, bar(K_FULL + slot), 0, 0, w.hk, c0);
+            ptx::tma_load_4d(kb + kHalf / 2, &tm_kc, bar(K_FULL + slot), 0, 0, w.hk, c1);
+            ptx::tma_load_4d(kb + kHalf, &tm_kc, bar(K_FULL + slot), 64, 0, w.hk, c0);
+            ptx::tma_load_4d(kb + kHalf + kHalf / 2, &tm_kc, bar(K_FULL + slot), 64, 0, w.hk, c1);
+          } else {
+            ptx::tma_load_4d(kb, mk, bar(K_FULL + slot), 0, k0, w.hk, b);
+            ptx::tma_load_4d(kb + kHalf, mk, bar(K_FULL + slot), 64, k0, w.hk, b);
+          }
           if (g >= 2 && !wait(V_EMPTY + slot, ((g >> 1) - 1) & 1)) {
             ok = false;
             break;
@@ -945,6 +982,8 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
       const Unit w = load_unit(a, u, prerot, n_pack_units);
       for (int j = 0; j < w.n; ++j, ++g) {
         const int slot = g & 1;
+        int c0, c1;
+        const bool pre_tile = w.k_pre || class_tile(L, w, j, a.status, c0, c1);
         if (!wait(K_FULL + slot, (g >> 1) & 1)) break;
         const uint32_t kt = KB + (uint32_t)slot * kTile;
 #pragma unroll
@@ -953,7 +992,7 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
           uint32_t info = 0;
           if (key < w.kv_hi) {
             info = (uint32_t)__ldg(L.key_info + w.blk.key_off + key);
-            if (!w.k_pre) {
+            if (!pre_tile) {
               const int p = key_row(info, L.n_pos, a.status);
               const uint4* tp = reinterpret_cast<const uint4*>(cs16 + (int64_t)p * (D / 2));
 #pragma unroll
@@ -1038,9 +1077,9 @@ int sm100_fwd(const AiAttnFwdArgs& a, cudaStream_t st, cudaError_t* cuda_err) {
   // warp-specialised kernel reads the rotated copies.  They are written
   // whenever the workspace holds them, so that the backward can reuse them.
   const bool pre = a.workspace && a.workspace_bytes >= prerot_bytes(a, nullptr);
-  AiTensor4 qr{}, kr{};
+  AiTensor4 qr{}, kr{}, kc{};
   if (pre) {
-    if (!sm100_rotated_views(a, a.workspace, &qr, &kr)) return AI_ERR_ALIGN;
+    if (!sm100_rotated_views(a, a.workspace, &qr, &kr, &kc)) return AI_ERR_ALIGN;
     e = prerot(a, a.workspace, st);
   }
   if (e == cudaSuccess && a.layout.n_fwd_items > 0) {
@@ -1053,11 +1092,15 @@ int sm100_fwd(const AiAttnFwdArgs& a, cudaStream_t st, cudaError_t* cuda_err) {
     const int G = a.num_q_heads / a.num_kv_heads;
     const int n_single = (G % 2 == 0) ? a.layout.n_fwd_abs_items : a.layout.n_fwd_items;
     const int n_pair = a.layout.n_fwd_items - n_single;
+    CUtensorMap tm_kc = tm_k;
+    if (pre && a.layout.n_rot_classes > 0 &&
+        !sm100_make_map(&tm_kc, kc, a.layout.n_rot_classes, a.num_kv_heads, AI_ROT_CLASS_KEYS, AI_ROT_CLASS_KEYS))
+      return AI_ERR_TMA;
     if (n_single > 0) {
       e = cudaFuncSetAttribute(fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
       if (e == cudaSuccess) {
         ProfScope ps(AI_PROF_FWD, st);
-        fwd_kernel<<<dim3(n_single, a.num_q_heads), kThreads, kSmemBytes, st>>>(a, tm_k, tm_v);
+        fwd_kernel<<<dim3(n_single, a.num_q_heads), kThreads, kSmemBytes, st>>>(a, tm_k, tm_v, tm_kc, pre ? 1 : 0);
         e = cudaGetLastError();
       }
     }
@@ -1081,7 +1124,7 @@ int sm100_fwd(const AiAttnFwdArgs& a, cudaStream_t st, cudaError_t* cuda_err) {
       e = cudaFuncSetAttribute(fwd_pers_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pf::kSmem);
       if (e == cudaSuccess) {
         ProfScope ps(AI_PROF_FWD, st);
-        fwd_pers_kernel<<<grid, pf::kThreads, pf::kSmem, st>>>(a, tm_k, tm_v, tm_qr, tm_kr, tm_o, tm_qr64,
+        fwd_pers_kernel<<<grid, pf::kThreads, pf::kSmem, st>>>(a, tm_k, tm_v, tm_qr, tm_kr, tm_o, tm_qr64, tm_kc,
                                                                 pre ? 1 : 0, n_units, n_pack_units);
         e = cudaGetLastError();
       }
@@ -1091,10 +1134,10 @@ int sm100_fwd(const AiAttnFwdArgs& a, cudaStream_t st, cudaError_t* cuda_err) {
   return e == cudaSuccess ? AI_OK : AI_ERR_LAUNCH;
 }
 
-bool sm100_rotated_views(const AiAttnFwdArgs& a, void* buf, AiTensor4* qr, AiTensor4* kr) {
+bool sm100_rotated_views(const AiAttnFwdArgs& a, void* buf, AiTensor4* qr, AiTensor4* kr, AiTensor4* kc) {
   if (!buf || ((uintptr_t)buf % 256)) return false;
-  size_t qb = 0;
-  prerot_bytes(a, &qb);
+  size_t qb = 0, qkb = 0;
+  prerot_bytes(a, &qb, &qkb);
   const int64_t T = a.seq_len, Dm = sm100::D;
   qr->ptr = buf;
   qr->stride_t = Dm;
@@ -1104,6 +1147,12 @@ bool sm100_rotated_views(const AiAttnFwdArgs& a, void* buf, AiTensor4* qr, AiTen
   kr->stride_t = Dm;
   kr->stride_h = T * Dm;
   kr->stride_b = (int64_t)a.num_kv_heads * T * Dm;
+  if (kc) {
+    kc->ptr = static_cast<char*>(buf) + qkb;
+    kc->stride_t = Dm;
+    kc->stride_h = (int64_t)AI_ROT_CLASS_KEYS * Dm;
+    kc->stride_b = (int64_t)a.num_kv_heads * AI_ROT_CLASS_KEYS * Dm;
+  }
   return true;
 }
 

@@ -49,6 +49,9 @@ int validate_fwd(const AiAttnFwdArgs* a) {
   if (L.n_kv_chunks < 0 || L.n_kv_partials < 0 || L.n_kv_reduce < 0 || (L.n_kv_chunks > 0 && !L.kv_chunks) ||
       (L.n_kv_reduce > 0 && !L.kv_reduce) || (L.n_kv_chunks > 0 && L.n_kv_chunks < L.n_kv_items))
     return AI_ERR_LAYOUT;
+  if (L.n_rot_classes < 0 || L.n_chunk_cls < 0 ||
+      (L.n_rot_classes > 0 && (!L.blk_cls || !L.chunk_cls || !L.rot_classes || L.n_chunk_cls <= 0)))
+    return AI_ERR_LAYOUT;
   if (L.n_fwd_abs_items < 0 || L.n_fwd_short_items < 0 ||
       (int64_t)L.n_fwd_abs_items + L.n_fwd_short_items > L.n_fwd_items || L.n_kv_abs_items < 0 ||
       L.n_kv_abs_items > L.n_kv_items)

@@ -79,6 +79,30 @@ __device__ __forceinline__ int pack_heads(int rows, int G) {
   return 1;
 }
 
+// First chunk_cls entry of a block's rotation classes, or -1 when the block
+// has none or the rotated copies are not in the workspace (`prerot` false).
+__device__ __forceinline__ int block_classes(const AiAttnLayout& L, int block, bool prerot) {
+  if (!prerot || L.n_rot_classes <= 0 || !L.blk_cls) return -1;
+  return __ldg(L.blk_cls + block);
+}
+
+// Rotation class of chunk i of a block whose entries start at `base`; an
+// index or class outside the tables is reported (AI_ERR_DEV_BOUNDS) and
+// gives -1, which sends the chunk down the rotate-in-shared-memory path.
+__device__ __forceinline__ int chunk_class(const AiAttnLayout& L, int base, int i, int32_t* status) {
+  const int idx = base + i;
+  if (base < 0 || idx >= L.n_chunk_cls) {
+    if (base >= 0) report(status, AI_ERR_DEV_BOUNDS);
+    return -1;
+  }
+  const int c = __ldg(L.chunk_cls + idx);
+  if (c < 0 || c >= L.n_rot_classes) {
+    report(status, AI_ERR_DEV_BOUNDS);
+    return -1;
+  }
+  return c;
+}
+
 __device__ __forceinline__ int clamp_row(int r, int n_pos, int32_t* status) {
   if (r < 0 || r >= n_pos) {
     report(status, AI_ERR_DEV_BOUNDS);

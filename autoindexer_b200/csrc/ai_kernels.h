@@ -54,9 +54,11 @@ bool sm100_make_map(CUtensorMap* map, const AiTensor4& t, int B, int H, int T, i
 // Once-rotated Q and K copies (bf16, head_dim 128) for the tensor-core kernels:
 // bytes of scratch they need (q_bytes: offset of the K copy), and the launch
 // writing q_rot = R(q_pos) q at buf and k_rot = R(k_own) k at buf + q_bytes.
-size_t prerot_bytes(const AiAttnFwdArgs& a, size_t* q_bytes);
+// The rotation-class chunks follow at buf + qk_bytes.
+size_t prerot_bytes(const AiAttnFwdArgs& a, size_t* q_bytes, size_t* qk_bytes = nullptr);
 cudaError_t prerot(const AiAttnFwdArgs& a, void* buf, cudaStream_t st);
-// (B, H, T, 128) views of the two copies inside buf (false if buf is misaligned).
-bool sm100_rotated_views(const AiAttnFwdArgs& a, void* buf, AiTensor4* qr, AiTensor4* kr);
+// (B, H, T, 128) views of the two copies inside buf, and (n_rot_classes, Hkv,
+// 64, 128) of the class chunks (false if buf is misaligned).
+bool sm100_rotated_views(const AiAttnFwdArgs& a, void* buf, AiTensor4* qr, AiTensor4* kr, AiTensor4* kc = nullptr);
 
 }  // namespace ai

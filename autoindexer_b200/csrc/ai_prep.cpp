@@ -19,6 +19,7 @@
 #include <algorithm>
 #include <cstdint>
 #include <cstring>
+#include <unordered_map>
 #include <vector>
 
 #include "../../include/ai_attn.h"
@@ -221,6 +222,7 @@ int plan(const AiPrepList* lists, int32_t n_lists, const int32_t* list_of_row, i
 // Every table of a layout, in host vectors.
 struct Tables {
   std::vector<int32_t> blocks, row_blocks, row_cov, q_pos, k_own, fwd_items, kv_items, kv_chunks, kv_reduce;
+  std::vector<int32_t> blk_cls, chunk_cls, rot_classes;
   std::vector<uint32_t> key_info;
   int32_t n_fwd_abs = 0, n_fwd_short = 0, n_kv_abs = 0, n_kv_partials = 0, kv_cost_max = 0, kv_cost_total = 0;
   bool all_owned = true;
@@ -229,6 +231,90 @@ struct Tables {
 
 // Query rows per step of the tensor-core dK/dV kernel, and its chunking costs.
 constexpr int64_t kKvStepRows = 64, kSplitCost = 64, kChunkCost = 40;
+// Keys per rotation-class chunk, and the most classes one layout gets
+// (8192 classes x 8 KV heads x 16 KB = 1 GiB of rotated chunks); blocks
+// past the cap rotate their keys in shared memory.
+constexpr int64_t kClsKeys = 64;
+constexpr int32_t kMaxRotClasses = 8192;
+
+// Rotation classes: every 64-key chunk of a block without own positions
+// (and with kv_lo on a chunk boundary) is described by its batch row, first
+// key and, per key, the rotary table row (attended), kUnattended or kPast
+// (at or past the block's end); equal descriptions share a class.
+constexpr uint32_t kUnattended = 0xFFFFFFFEu, kPast = 0xFFFFFFFFu;
+
+// FNV-1a over a chunk description's words.
+inline uint64_t hash_words(const uint32_t* w, int n) {
+  uint64_t h = 1469598103934665603ull;
+  for (int i = 0; i < n; ++i) {
+    h ^= w[i];
+    h *= 1099511628211ull;
+  }
+  return h;
+}
+
+void build_rot_classes(Tables* t) {
+  constexpr int kWords = 2 + (int)kClsKeys;  // batch row, first key, one word per key
+  const int32_t nb = (int32_t)(t->blocks.size() / AI_BLOCK_FIELDS);
+  t->blk_cls.assign((size_t)nb, -1);
+  t->chunk_cls.clear();
+  t->rot_classes.clear();
+  std::vector<uint32_t> descs;                      // [class][kWords]
+  std::unordered_multimap<uint64_t, int32_t> by_hash;
+  std::vector<uint32_t> cur;                        // this block's chunk descriptions
+  std::vector<int32_t> found;
+  auto lookup = [&](const uint32_t* w, uint64_t h) -> int32_t {
+    auto range = by_hash.equal_range(h);
+    for (auto it = range.first; it != range.second; ++it)
+      if (std::memcmp(descs.data() + (size_t)it->second * kWords, w, sizeof(uint32_t) * kWords) == 0)
+        return it->second;
+    return -1;
+  };
+  for (int32_t bi = 0; bi < nb; ++bi) {
+    const int32_t* rec = t->blocks.data() + (int64_t)AI_BLOCK_FIELDS * bi;
+    const int64_t e = rec[AI_BLOCK_END], kv_lo = rec[AI_BLOCK_KV_LO], off = rec[AI_BLOCK_KEY_OFF];
+    if ((rec[AI_BLOCK_FLAGS] & AI_BLOCKF_OWNPOS) || kv_lo >= e || kv_lo % kClsKeys) continue;
+    const int64_t n_chunks = 2 * ((e - kv_lo + 2 * kClsKeys - 1) / (2 * kClsKeys));
+    const int64_t n_real = (e - kv_lo + kClsKeys - 1) / kClsKeys;
+    cur.assign((size_t)(n_real * kWords), 0);
+    found.assign((size_t)n_real, -1);
+    std::vector<uint64_t> hashes((size_t)n_real);
+    int32_t fresh = 0;
+    for (int64_t i = 0; i < n_real; ++i) {
+      const int64_t k0 = kv_lo + kClsKeys * i;
+      uint32_t* w = cur.data() + (size_t)(i * kWords);
+      w[0] = (uint32_t)rec[AI_BLOCK_ROW];
+      w[1] = (uint32_t)k0;
+      for (int64_t j = k0; j < k0 + kClsKeys; ++j) {
+        uint32_t x = kPast;
+        if (j < e) {
+          const uint32_t kw = t->key_info[(size_t)(off + j)];
+          x = (kw & AI_KEY_ATTN) ? (kw & AI_KEY_ROW_MASK) : kUnattended;
+        }
+        w[2 + (j - k0)] = x;
+      }
+      hashes[(size_t)i] = hash_words(w, kWords);
+      found[(size_t)i] = lookup(w, hashes[(size_t)i]);
+      fresh += found[(size_t)i] < 0;  // a block's own chunks differ in their first key
+    }
+    if ((int64_t)(descs.size() / kWords) + fresh > kMaxRotClasses) continue;
+    t->blk_cls[(size_t)bi] = (int32_t)t->chunk_cls.size();
+    int32_t last = -1;
+    for (int64_t i = 0; i < n_real; ++i) {
+      int32_t id = found[(size_t)i];
+      if (id < 0) {
+        id = (int32_t)(descs.size() / kWords);
+        descs.insert(descs.end(), cur.begin() + i * kWords, cur.begin() + (i + 1) * kWords);
+        by_hash.emplace(hashes[(size_t)i], id);
+        t->rot_classes.push_back(bi);
+        t->rot_classes.push_back((int32_t)(kv_lo + kClsKeys * i));
+      }
+      last = id;
+      t->chunk_cls.push_back(id);
+    }
+    for (int64_t i = n_real; i < n_chunks; ++i) t->chunk_cls.push_back(last);  // padding of the last 128-key tile
+  }
+}
 
 int build(const AiPrepList* lists, int32_t n_lists, const int32_t* list_of_row, int32_t batch, int32_t seq_len,
           int32_t fwd_tile, int32_t kv_tile, Tables* t) {
@@ -467,6 +553,7 @@ int build(const AiPrepList* lists, int32_t n_lists, const int32_t* list_of_row, 
     t->kv_chunks[4 * i + 2] = chunks[i].q1;
     t->kv_chunks[4 * i + 3] = chunks[i].slot;
   }
+  build_rot_classes(t);
   return AI_OK;
 }
 
@@ -517,6 +604,8 @@ int ai_attn_prep_sizes(const AiPrepList* lists, int32_t n_lists, const int32_t* 
   sizes->n_kv_items = (int32_t)(t.kv_items.size() / 4);
   sizes->n_kv_chunks = (int32_t)(t.kv_chunks.size() / 4);
   sizes->n_kv_reduce = (int32_t)(t.kv_reduce.size() / 4);
+  sizes->n_chunk_cls = (int32_t)t.chunk_cls.size();
+  sizes->n_rot_classes = (int32_t)(t.rot_classes.size() / 2);
   sizes->n_keys = (int64_t)t.key_info.size();
   sizes->p_min = t.p_min;
   sizes->p_max = t.p_max;
@@ -546,6 +635,13 @@ int ai_attn_prep(const AiPrepList* lists, int32_t n_lists, const int32_t* list_o
   if (!t.kv_reduce.empty()) {
     if (!out->kv_reduce) return AI_ERR_NULL;
     put(out->kv_reduce, t.kv_reduce);
+  }
+  if (!out->blk_cls) return AI_ERR_NULL;
+  put(out->blk_cls, t.blk_cls);
+  if (!t.chunk_cls.empty()) {
+    if (!out->chunk_cls || !out->rot_classes) return AI_ERR_NULL;
+    put(out->chunk_cls, t.chunk_cls);
+    put(out->rot_classes, t.rot_classes);
   }
   out->n_kv_partials = t.n_kv_partials;
   out->kv_cost_max = t.kv_cost_max;

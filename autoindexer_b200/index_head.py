@@ -93,7 +93,9 @@ def _t4(x: Tensor) -> "_lib.AiTensor4":
 
 
 class _Prepared:
-    """Device copies of the rows and the rotary table for one call."""
+    """Device copies of the rows and the rotary table for one call: the
+    row table, targets, key table rows and key flags go over in one copy
+    from one pinned host buffer."""
 
     def __init__(self, ir: IndexRows, rotary_emb, head_dim: int, device):
         ok_rel = ir.rel[ir.ok.astype(bool)]
@@ -101,13 +103,26 @@ class _Prepared:
         hi = int(max(0, ok_rel.max())) if ok_rel.size else 0
         self.cos, self.sin = rope_table(rotary_emb, lo, hi, head_dim, device)
         self.n_pos = hi - lo + 1
-        key_rows = np.clip(ir.rel - lo, 0, self.n_pos - 1).astype(np.int32)
-        self.rows = torch.from_numpy(np.ascontiguousarray(ir.rows)).to(device)
-        self.targets = torch.from_numpy(np.ascontiguousarray(ir.targets)).to(device)
-        self.key_rows = torch.from_numpy(key_rows).to(device)
-        self.key_ok = torch.from_numpy(np.ascontiguousarray(ir.ok)).to(device)
         self.n_rows = int(ir.rows.shape[0])
-        self.n_keys = int(key_rows.shape[0])
+        self.n_keys = int(ir.rel.shape[0])
+        # int32 sections (16-byte aligned): rows [n_rows][4], targets, key rows; then the uint8 key flags
+        n_rows4, n_keys4 = 4 * self.n_rows, (self.n_keys + 3) // 4 * 4
+        o_tg = n_rows4
+        o_kr = o_tg + (self.n_rows + 3) // 4 * 4
+        o_ok = o_kr + n_keys4
+        host = torch.empty(4 * o_ok + n_keys4, dtype=torch.uint8, pin_memory=True)
+        h32 = host[:4 * o_ok].view(torch.int32).numpy()
+        h32[:n_rows4] = ir.rows.reshape(-1)
+        h32[o_tg:o_tg + self.n_rows] = ir.targets
+        h32[o_kr:o_kr + self.n_keys] = np.clip(ir.rel - lo, 0, self.n_pos - 1)
+        host[4 * o_ok:4 * o_ok + self.n_keys].numpy()[:] = ir.ok
+        dev = host.to(device, non_blocking=True)
+        d32 = dev[:4 * o_ok].view(torch.int32)
+        self.rows = d32[:n_rows4]
+        self.targets = d32[o_tg:o_tg + self.n_rows]
+        self.key_rows = d32[o_kr:o_kr + self.n_keys]
+        self.key_ok = dev[4 * o_ok:4 * o_ok + self.n_keys]
+        self._host = host  # the copy reads it asynchronously
 
 
 def _args(q, k, prep: _Prepared, scale, logits, lse, loss):
@@ -202,10 +217,9 @@ def compute_index_losses_b200(
     q = query if query.stride(-1) == 1 else query.contiguous()
     k = keys if keys.stride(-1) == 1 else keys.contiguous()
     loss, logits = IndexLossFn.apply(q, k, prep, scale)
-    heads = torch.as_tensor(ir.rows[:, 0], device=query.device)
-    per_row = loss.mean(dim=0)  # mean over the batch, as .mean() in the reference
-    start_loss = per_row[heads == 0].sum() / n_edits
-    end_loss = per_row[heads == 1].sum() / n_edits
+    # rows come in (start, end) pairs per edit; mean over the batch as .mean() in the reference
+    per_edit = loss.mean(dim=0).view(n_edits, 2).sum(dim=0) / n_edits
+    start_loss, end_loss = per_edit[0], per_edit[1]
     weights = {}
     if return_weights:
         for r in range(ir.rows.shape[0]):

@@ -118,6 +118,9 @@ class CompiledLayout:
     n_kv_partials: int           # partial slots of the split items
     kv_cost_max: int             # cost of the costliest key tile (query tiles + 2 per block)
     kv_cost_total: int           # cost of all key tiles
+    blk_cls: torch.Tensor        # [n_blocks]: first rotation-class entry of the block in chunk_cls, -1: none
+    chunk_cls: torch.Tensor      # [n]: rotation class of each 64-key chunk of the blocks that have classes
+    rot_classes: torch.Tensor    # [c, 2]: block and first key whose chunk defines the class
     pairs_per_head: int          # finite (query, key) logits of one head summed over the batch
     all_rows_owned: bool = False  # every row of every batch row belongs to a block (no fill launches)
     host_blocks: np.ndarray = field(repr=False, default=None)
@@ -154,6 +157,11 @@ class CompiledLayout:
         L.n_kv_reduce = int(self.kv_reduce.shape[0])
         L.kv_cost_max = int(self.kv_cost_max)
         L.kv_cost_total = int(self.kv_cost_total)
+        L.blk_cls = self.blk_cls.data_ptr() if self.blk_cls.numel() else None
+        L.chunk_cls = self.chunk_cls.data_ptr() if self.chunk_cls.numel() else None
+        L.n_chunk_cls = int(self.chunk_cls.shape[0])
+        L.rot_classes = self.rot_classes.data_ptr() if self.rot_classes.numel() else None
+        L.n_rot_classes = int(self.rot_classes.shape[0])
         return L
 
 
@@ -236,7 +244,8 @@ def _compile(parsed_positions, batch, seq_len, head_dim, code, rotary_emb, devic
     # One int32 buffer holds every table (sections 16-byte aligned).
     parts = [("blocks", sz.n_blocks * 8), ("row_blocks", batch + 1), ("row_cov", batch), ("key_info", sz.n_keys),
              ("q_pos", batch * seq_len), ("k_own", batch * seq_len), ("fwd_items", sz.n_fwd_items * 4),
-             ("kv_items", sz.n_kv_items * 4), ("kv_chunks", sz.n_kv_chunks * 4), ("kv_reduce", sz.n_kv_reduce * 4)]
+             ("kv_items", sz.n_kv_items * 4), ("kv_chunks", sz.n_kv_chunks * 4), ("kv_reduce", sz.n_kv_reduce * 4),
+             ("blk_cls", sz.n_blocks), ("chunk_cls", sz.n_chunk_cls), ("rot_classes", sz.n_rot_classes * 2)]
     offs, total = {}, 0
     for name, n in parts:
         offs[name] = (total, int(n))
@@ -268,6 +277,7 @@ def _compile(parsed_positions, batch, seq_len, head_dim, code, rotary_emb, devic
         rope_cos=cos, rope_sin=sin, rope_cs16=torch.stack([cos, sin], dim=-1).to(torch.float16).contiguous(),
         fwd_items=view("fwd_items", (-1, 4)), kv_items=view("kv_items", (-1, 4)),
         kv_chunks=view("kv_chunks", (-1, 4)), kv_reduce=view("kv_reduce", (-1, 4)), n_kv_partials=int(t.n_kv_partials),
+        blk_cls=view("blk_cls", (-1,)), chunk_cls=view("chunk_cls", (-1,)), rot_classes=view("rot_classes", (-1, 2)),
         kv_cost_max=int(t.kv_cost_max), kv_cost_total=int(t.kv_cost_total),
         n_fwd_abs_items=int(t.n_fwd_abs_items), n_kv_abs_items=int(t.n_kv_abs_items),
         n_fwd_short_items=int(t.n_fwd_short_items), pairs_per_head=int(t.pairs_per_head),

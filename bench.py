@@ -934,6 +934,127 @@ def run_decode(args):
 
 
 
+INDEX_B = 4
+INDEX_WORKLOAD = ("index head: bf16 B=4, 2 heads (start / end cursor), D=128, theta=1e6, the +E edit chain "
+                  "(46 edits, T=3072), cursor targets drawn among each row's attendable keys")
+
+
+def run_index(args):
+    """Index-head cursor losses (``compute_index_losses_b200``) against the
+    reference's ``compute_index_losses`` (``attn_layers.py:40-110``, from
+    ``baseline/_ref``) on the same GPU and inputs: losses of every edit
+    forward, backward of ``start + 2 * end``, L2 flushed between steps.  The
+    per-call host work (the rows of every edit, the rotary table) is inside
+    both steps, as it is in training.  One JSON line, not the headline
+    metric."""
+    import torch
+
+    import autoindexer_b200 as ab
+    from autoindexer_b200.index_head import index_rows
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    with np.load(os.path.join(ROOT, "tests", "golden", "ops_cases.npz")) as z:
+        ops = z["chain_e"]
+    lay = ab.positions_from_operations(ops)
+    rng = np.random.default_rng(7)
+    cursor = {}
+    for blk, (s_, e_, _, _) in zip(lay, lay.boundary_indices):
+        if int(blk.block_type) == 1:
+            cursor[int(e_) - 1] = (0, 0)
+    probe = index_rows(lay, cursor)
+    for r in range(0, probe.rows.shape[0], 2):
+        picks = []
+        for rr in (r, r + 1):
+            _, _, n, off = probe.rows[rr]
+            cand = np.flatnonzero(probe.ok[off:off + n])
+            picks.append(int(rng.choice(cand)) if cand.size else 0)
+        cursor[int(probe.edits[r])] = tuple(picks)
+    T = int(lay.boundary_indices[-1][1])
+    inv = 1.0 / (THETA ** (np.arange(0, D, 2, dtype=np.float64) / D))
+
+    class PlainRope(torch.nn.Module):  # transformers' default rotary: cos/sin of pos * inv_freq, in x.dtype
+        def __init__(self):
+            super().__init__()
+            self.register_buffer("inv_freq", torch.as_tensor(inv, dtype=torch.float32), persistent=False)
+
+        @torch.no_grad()
+        def forward(self, x, position_ids):
+            f = position_ids.to(self.inv_freq.device).float()[..., None] * self.inv_freq
+            emb = torch.cat((f, f), dim=-1)
+            return emb.cos().to(x.dtype), emb.sin().to(x.dtype)
+
+    rope = PlainRope().to(dev)
+    g = torch.Generator().manual_seed(11)
+    q0 = torch.randn(INDEX_B, 2, T, D, generator=g).to(torch.bfloat16).to(dev)
+    k0 = torch.randn(INDEX_B, 2, T, D, generator=g).to(torch.bfloat16).to(dev)
+    q, k = q0.clone().requires_grad_(True), k0.clone().requires_grad_(True)
+    flush = torch.empty(64 * 1024 * 1024, device=dev)
+    mods = _reference_modules()
+    ref_lay = None
+    if mods is not None:
+        from autoindexer.models.autoindexer import attn_layers as ref_al
+
+        _, pl, tu = mods
+        ref_lay = ab.positions_from_operations(ops, device=dev, block_cls=tu.PositionBlock,
+                                               list_cls=pl.PositionBlockList)
+
+    def ours():
+        q.grad = k.grad = None
+        (sl, el), _ = ab.compute_index_losses_b200(rope, q, k, lay, cursor)
+        (sl + 2 * el).backward()
+        return sl, el
+
+    def reference():
+        q.grad = k.grad = None
+        (sl, el), _ = ref_al.compute_index_losses(rope, q, k, ref_lay, cursor)
+        (sl + 2 * el).backward()
+        return sl, el
+
+    def timed(fn):
+        for _ in range(max(3, args.warmup)):
+            fn()
+        torch.cuda.synchronize(dev)
+        tot = 0.0
+        for i in range(args.steps):
+            flush.fill_(float(i))
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize(dev)
+            tot += e0.elapsed_time(e1) / 1e3
+        return tot / args.steps
+
+    t_ours = timed(ours)
+    sl, el = ours()
+    got = (float(sl), float(el), q.grad.float().clone(), k.grad.float().clone())
+    n_rows = probe.rows.shape[0]
+    # algorithmic bytes: every (row, key) reads the key's K row once forward and once per backward pass
+    key_bytes = int(probe.rows[:, 2].astype(np.int64).sum()) * D * 2 * INDEX_B
+    line = {
+        "metric": "index-head cursor losses fwd+bwd ms per step", "value": round(t_ours * 1e3, 4), "unit": "ms",
+        "steps": args.steps, "warmup": args.warmup, "higher_is_better": False, "dtype": "bf16",
+        "data": "synthetic (seeded randn q/k, seeded cursor targets)",
+        "config": {"workload": INDEX_WORKLOAD, "edits": n_rows // 2, "l2": "flushed between timed steps"},
+        "key_bytes_per_pass": key_bytes,
+    }
+    if mods is not None:
+        t_ref = timed(reference)
+        rl, re_ = reference()
+        line["reference"] = {"ms_per_step": round(t_ref * 1e3, 4),
+                             "what": "reference compute_index_losses + autograd (Python loop over edits), same GPU"}
+        line["speedup_vs_reference"] = round(t_ref / t_ours, 2)
+        line["diff_vs_reference"] = {
+            "start_loss": round(abs(got[0] - float(rl)), 5), "end_loss": round(abs(got[1] - float(re_)), 5),
+            "dq_rel_l2": round(float((got[2] - q.grad.float()).norm() / q.grad.float().norm()), 5),
+            "dk_rel_l2": round(float((got[3] - k.grad.float()).norm() / k.grad.float().norm()), 5)}
+    else:
+        line["reference"] = "unavailable: the reference is not installed under baseline/_ref"
+    print(json.dumps(line), flush=True)
+
+
+
 TRAIN_T = 8192
 TRAIN_WORKLOAD = ("cfg2: Qwen3-8B-architecture decoder (36 layers, hidden 4096, Hq=32, Hkv=8, D=128, SwiGLU 12288, "
                   "RMSNorm, vocab 151936), random-init bf16 weights, T=8192, micro-batch 1 per GPU, tokens U[vocab] "
@@ -1112,8 +1233,12 @@ def main():
                     help="time the reference's Triton backend against this library (one extra JSON line)")
     ap.add_argument("--prefill", action="store_true", help="time the prefill path instead (one extra JSON line)")
     ap.add_argument("--decode", action="store_true", help="time one decode step instead (one extra JSON line)")
+    ap.add_argument("--index", action="store_true",
+                    help="time the index-head cursor losses instead (one extra JSON line)")
     args = ap.parse_args()
-    if args.prefill:
+    if args.index:
+        run_index(args)
+    elif args.prefill:
         run_prefill(args)
     elif args.decode:
         run_decode(args)

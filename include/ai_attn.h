@@ -43,7 +43,7 @@
 extern "C" {
 #endif
 
-#define AI_ATTN_ABI_VERSION 8
+#define AI_ATTN_ABI_VERSION 9
 
 typedef enum AiDtype {
   AI_DTYPE_BF16 = 0,
@@ -88,6 +88,7 @@ typedef struct AiTensor4 {
 #define AI_BLOCK_ABS_HI 7  /* ... one past the last such key; ABS_HI <= ABS_LO means "any key of the block"
                               (ABI 7: key tiles outside [ABS_LO, ABS_HI) take the fast kernels) */
 #define AI_BLOCK_FIELDS 8
+#define AI_ROT_CLASS_KEYS 64 /* keys per rotation-class chunk (AiAttnLayout.chunk_cls) */
 #define AI_BLOCKF_MASKED 1 /* some key in [kv_lo, e) has attn_mask false */
 #define AI_BLOCKF_ABS 2    /* some key has abs_pos_mask set */
 #define AI_BLOCKF_OWNPOS 4 /* every attended key has the position k_own gives it (so a K copy
@@ -141,6 +142,19 @@ typedef struct AiAttnLayout {
                                  plus two per block a key tile walks): the chunks run only when the
                                  costliest tile outweighs the average work of an SM */
   int32_t kv_cost_total;
+  /* Rotation classes (ABI 9; optional: n_rot_classes = 0 turns them off).  The keys of a block
+     without AI_BLOCKF_OWNPOS whose kv_lo is a multiple of 64 are taken in 64-key chunks
+     [kv_lo + 64 i, kv_lo + 64 i + 64), 2 * ceil((e - kv_lo) / 128) of them (chunks past e pad the
+     last 128-key tile).  Chunks of one batch row that give every attended key the same rotary
+     table row, and leave the same keys unattended or past their block's end, share a class.
+     When the forward workspace holds the rotated copies (ai_attn_fwd_workspace counts the
+     classes) each class's chunk is rotated once per KV head, and the tensor-core kernels read it
+     instead of rotating the chunk's keys in shared memory for every block that sees them. */
+  const int32_t* blk_cls;     /* [n_blocks]: index in chunk_cls of the block's chunk 0, -1: no classes */
+  const int32_t* chunk_cls;   /* [n_chunk_cls]: class of each chunk */
+  int32_t n_chunk_cls;
+  const int32_t* rot_classes; /* [n_rot_classes][2]: block and first key of a chunk with the class's rows */
+  int32_t n_rot_classes;
 } AiAttnLayout;
 
 typedef struct AiAttnFwdArgs {
@@ -357,6 +371,8 @@ typedef struct AiPrepSizes {
   int32_t n_kv_items;
   int32_t n_kv_chunks;        /* entries of kv_chunks (at least n_kv_items) */
   int32_t n_kv_reduce;        /* entries of kv_reduce */
+  int32_t n_chunk_cls;        /* entries of chunk_cls */
+  int32_t n_rot_classes;      /* entries of rot_classes */
   int64_t n_keys;             /* key words (sum over the distinct lists) */
   int64_t p_min, p_max;       /* position ids the rotary table must cover (row r = position p_min + r) */
 } AiPrepSizes;
@@ -375,6 +391,9 @@ typedef struct AiPrepTables {
   int32_t* kv_items;          /* [n_kv_items][4] */
   int32_t* kv_chunks;         /* [n_kv_chunks][4] */
   int32_t* kv_reduce;         /* [n_kv_reduce][4] */
+  int32_t* blk_cls;           /* [n_blocks] */
+  int32_t* chunk_cls;         /* [n_chunk_cls] */
+  int32_t* rot_classes;       /* [n_rot_classes][2] */
   int32_t n_kv_partials;
   int32_t kv_cost_max;
   int32_t kv_cost_total;

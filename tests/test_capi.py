@@ -31,7 +31,7 @@ def test_library_exports_every_declared_function():
 
 def test_abi_version_and_tiles():
     L = _lib.lib()
-    assert L.ai_attn_abi_version() == 8 == _lib.ABI_VERSION
+    assert L.ai_attn_abi_version() == 9 == _lib.ABI_VERSION
     assert L.ai_attn_fwd_tile_rows(_lib.DTYPE_BF16, 128) == 128
     assert L.ai_attn_fwd_tile_rows(_lib.DTYPE_F32, 64) == 32
     assert L.ai_attn_kv_tile_rows(_lib.DTYPE_F32, 64) > 0

@@ -279,3 +279,64 @@ def test_kv_chunks_partition_each_key_tile(which):
             assert n == len(parts) and [p[2] for p in parts] == list(range(first, first + n))
     assert c.kv_cost_max == cost_max and c.kv_cost_total == cost_total
     assert c.n_kv_partials == sum(n for _, n in reduce_of.values())
+
+
+def _class_cases():
+    import bench
+
+    out = []
+    for which in ("E", "1"):
+        wl = bench.build_workload(which, 0, "cpu")
+        out.append((wl.rows, wl.batch, wl.seq_len, wl.rope, 128))
+    # the golden edit chains shared by two batch rows: classes are per row
+    for name in golden_names()[:4]:
+        g = load_golden(name)
+        out.append((ArrayLayout.from_golden(g), 2, int(g["T"]) + 5, golden_rope(g)[0], int(g["D"])))
+    return out
+
+
+@pytest.mark.parametrize("case", range(6))
+def test_rotation_classes_describe_each_chunk(case):
+    """Rotation classes: every 64-key chunk of a block without own positions
+    (kv_lo on a chunk boundary) has a class whose defining chunk (same batch
+    row, same first key) gives each key the same attended / past-the-end
+    state and every attended key the same rotary table row; padding chunks of
+    the last 128-key tile repeat the last real chunk's class; no two classes
+    describe the same chunk; own-position blocks have none."""
+    lay, B, T, rope, D = _class_cases()[case]
+    c = compile_layout(lay, B, T, D, torch.bfloat16, rope, "cpu")
+    blocks, info = c.blocks.numpy(), c.key_info.numpy().view(np.uint32)
+    blk_cls, chunk_cls, rc = c.blk_cls.numpy(), c.chunk_cls.numpy(), c.rot_classes.numpy()
+    assert blk_cls.shape == (blocks.shape[0],)
+
+    def describe(bi, k0):
+        row, s, e, off, kv_lo = (int(x) for x in blocks[bi][:5])
+        d = [row, k0]
+        for j in range(k0, k0 + 64):
+            if j >= e:
+                d.append(-1)
+            elif info[off + j] & 0x40000000:
+                d.append(int(info[off + j] & 0x3FFFFFFF))
+            else:
+                d.append(-2)
+        return tuple(d)
+
+    descs = [describe(int(bi), int(k0)) for bi, k0 in rc]
+    assert len(set(descs)) == len(descs)
+    for bi, (row, s, e, off, kv_lo, flags, _, _) in enumerate(blocks):
+        if (flags & 4) or kv_lo >= e or kv_lo % 64:
+            assert blk_cls[bi] == -1
+            continue
+        if blk_cls[bi] < 0:
+            continue  # over the class cap (not reached here)
+        n = 2 * ((e - kv_lo + 127) // 128)
+        ent = chunk_cls[blk_cls[bi]:blk_cls[bi] + n]
+        assert ent.shape[0] == n
+        for i in range(n):
+            k0 = kv_lo + 64 * i
+            if k0 >= e:
+                assert ent[i] == ent[i - 1]
+                continue
+            assert descs[ent[i]] == describe(bi, k0)
+    if c.rot_classes.shape[0]:
+        assert chunk_cls.max() == c.rot_classes.shape[0] - 1

@@ -226,3 +226,31 @@ def test_bf16_split_key_tiles_match_whole_key_tiles(cuda_device):
     for name, a_, b_ in zip(("dq", "dk", "dv"), *res):
         assert rel_l2(a_, b_) <= 2e-3, (name, rel_l2(a_, b_))
     assert np.array_equal(res[0][0], res[1][0])  # dQ does not take part in the split
+
+
+def test_bf16_rotation_classes_match_shared_memory_rotation(cuda_device):
+    """The +E chain's blocks read their keys from the rotation-class copies
+    (each distinct 64-key chunk rotated once); with the classes removed from
+    the layout the same kernels rotate every K tile in shared memory.  The
+    rotation arithmetic is the same, so out, lse, dQ and dV are equal bit for
+    bit; dK differs by the order of its fp32 sums (with classes, consecutive
+    blocks that rotate a key tile alike accumulate in TMEM and are folded
+    once)."""
+    import dataclasses
+
+    lay, q, k, v, dout, mod, _ = _chain_e(8, 2, 128, 23)
+    tq, tk, tv, tdo = (torch.as_tensor(x).to(cuda_device, torch.bfloat16) for x in (q, k, v, dout))
+    B, Hq, T, D = tq.shape
+    layout = compile_layout(lay, B, T, D, torch.bfloat16, mod.to(cuda_device), cuda_device)
+    assert layout.rot_classes.shape[0] > 0
+    none = dataclasses.replace(layout, chunk_cls=layout.chunk_cls[:0], rot_classes=layout.rot_classes[:0])
+    res = []
+    for lo in (layout, none):
+        out, lse, fws = attn_fwd(tq, tk, tv, lo, D ** -0.5, keep_workspace=True)
+        dq, dk, dv = attn_bwd(tq, tk, tv, out, lse, tdo, lo, D ** -0.5, fwd_workspace=fws)
+        torch.cuda.synchronize(cuda_device)
+        assert read_status(cuda_device) == 0
+        res.append((out, lse, dq, dk, dv))
+    for name, a_, b_ in zip(("out", "lse", "dq", "dv"), *(r[:3] + r[4:] for r in res)):
+        assert torch.equal(a_, b_), name
+    assert rel_l2(res[0][3].double().cpu().numpy(), res[1][3].double().cpu().numpy()) <= 2e-3
