@@ -57,6 +57,8 @@ EXPORTED_SYMBOLS = (
     "ai_attn_prep",
     "ai_index_fwd",
     "ai_index_bwd",
+    "ai_index_rows_sizes",
+    "ai_index_rows",
 )
 
 _i32p = ctypes.POINTER(ctypes.c_int32)
@@ -108,6 +110,7 @@ class AiAttnLayout(ctypes.Structure):
         ("n_chunk_cls", ctypes.c_int32),
         ("rot_classes", ctypes.c_void_p),
         ("n_rot_classes", ctypes.c_int32),
+        ("n_fwd_abs_short_items", ctypes.c_int32),
     ]
 
 
@@ -217,6 +220,16 @@ class AiPrepList(ctypes.Structure):
     ]
 
 
+class AiIndexRowsOut(ctypes.Structure):
+    _fields_ = [
+        ("rows", ctypes.c_void_p),
+        ("key_rows", ctypes.c_void_p),
+        ("key_ok", ctypes.c_void_p),
+        ("rel_lo", ctypes.c_int64),
+        ("rel_hi", ctypes.c_int64),
+    ]
+
+
 class AiPrepSizes(ctypes.Structure):
     _fields_ = [
         ("n_blocks", ctypes.c_int32),
@@ -252,6 +265,7 @@ class AiPrepTables(ctypes.Structure):
         ("kv_cost_total", ctypes.c_int32),
         ("n_fwd_abs_items", ctypes.c_int32),
         ("n_fwd_short_items", ctypes.c_int32),
+        ("n_fwd_abs_short_items", ctypes.c_int32),
         ("n_kv_abs_items", ctypes.c_int32),
         ("all_rows_owned", ctypes.c_int32),
         ("pairs_per_head", ctypes.c_int64),
@@ -307,6 +321,10 @@ def _bind(handle):
     handle.ai_index_fwd.argtypes = [P(AiIndexArgs), vp]
     handle.ai_index_bwd.restype = ctypes.c_int
     handle.ai_index_bwd.argtypes = [P(AiIndexBwdArgs), vp]
+    handle.ai_index_rows_sizes.restype = ctypes.c_int
+    handle.ai_index_rows_sizes.argtypes = [P(AiPrepList), vp, P(i32), P(i64), vp]
+    handle.ai_index_rows.restype = ctypes.c_int
+    handle.ai_index_rows.argtypes = [P(AiPrepList), vp, i64, P(AiIndexRowsOut)]
     return handle
 
 

@@ -115,7 +115,8 @@ constexpr uint32_t C_S = 0, C_DP = 64, C_DQR = 128, C_DQA = 256, C_SA = 384;
 
 __global__ void __launch_bounds__(kThreads, 1)
     dq_kernel(const AiAttnBwdArgs a, const float* __restrict__ delta, const __grid_constant__ CUtensorMap tm_k,
-              const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_kc, const int prerot) {
+              const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_kc, const int prerot,
+              const float* __restrict__ part_dq) {
   using namespace dq;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = tile::align1024(smem_raw);
@@ -204,7 +205,35 @@ __global__ void __launch_bounds__(kThreads, 1)
   int n_tiles = 0;
   bool aborted = false, dqa_started = false;
 
-  for (int k0 = blk.kv_lo, jt = 0; k0 < kv_hi; k0 += BN, ++jt) {
+  // With the abs split the persistent kernel has run this item's key tiles
+  // without abs keys and left each row's dQrot (fp32): start the rotated
+  // accumulator from it and run the tiles that hold abs keys only.
+  const bool o_init = part_dq != nullptr;
+  int j_begin = 0, j_end = kv_hi > blk.kv_lo ? (kv_hi - blk.kv_lo + BN - 1) / BN : 0;
+  if (o_init) {
+    abs_tiles(blk, blk.kv_lo, kv_hi, BN, j_begin, j_end);
+    const bool have = i < q1;
+    const float* prow = part_dq + (((int64_t)blockIdx.x * f.num_q_heads + h) * BM + (i - q0)) * D;
+#pragma unroll
+    for (int cc = 0; cc < D / 32; ++cc) {
+      uint32_t r[32];
+#pragma unroll
+      for (int x = 0; x < 32; x += 4) {
+        const float4 v = have ? *reinterpret_cast<const float4*>(prow + 32 * cc + x) : make_float4(0.f, 0.f, 0.f, 0.f);
+        r[x] = __float_as_uint(v.x);
+        r[x + 1] = __float_as_uint(v.y);
+        r[x + 2] = __float_as_uint(v.z);
+        r[x + 3] = __float_as_uint(v.w);
+      }
+      ptx::tmem_st32(tmem + lane_base + C_DQR + 32 * cc, r);
+    }
+    ptx::tmem_wait_st();
+    ptx::tc_fence_before();
+    __syncthreads();
+    ptx::tc_fence_after();
+  }
+
+  for (int jt = j_begin, k0 = blk.kv_lo + j_begin * BN; jt < j_end; ++jt, k0 += BN) {
     // Only a tile that holds one of the block's abs keys needs S_abs and dQabs.
     const bool tabs = blk.abs_in(k0, min(k0 + BN, kv_hi));
     const int kc = cls >= 0 ? chunk_class(L, cls, jt, f.status) : -1;
@@ -317,7 +346,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int kk = 0; kk < BN / 16; ++kk) {
         const uint32_t ao = (uint32_t)kk * 32u;
         const uint32_t bo = (uint32_t)kk * 2048u;  // 16 key rows of 128 bytes
-        const uint32_t acc = (n_tiles > 0 || kk > 0) ? 1u : 0u;
+        const uint32_t acc = (n_tiles > 0 || o_init || kk > 0) ? 1u : 0u;
         ptx::mma_ss(tmem + C_DQR, ptx::sdesc_sw128(sbase + DS + ao, 16, 1024),
                     ptx::sdesc_sw128(sbase + KR + bo, 8192, 1024), idesc_dq, acc);
         if (tabs)
@@ -343,7 +372,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
       uint32_t g1[32], g2[32], a1[32], a2[32];
-      if (n_tiles > 0) {
+      const bool have_r = n_tiles > 0 || o_init;
+      if (have_r) {
         ptx::tmem_ld32(tmem + lane_base + C_DQR + 32 * half, g1);
         ptx::tmem_ld32(tmem + lane_base + C_DQR + 64 + 32 * half, g2);
         if (dqa_started) {
@@ -357,7 +387,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int x = 0; x < 32; ++x) {
         const int d = 32 * half + x;
         float y1 = 0.f, y2 = 0.f;
-        if (n_tiles > 0) {
+        if (have_r) {
           const float c = cs[d], s = sn[d];
           const float v1 = __uint_as_float(g1[x]), v2 = __uint_as_float(g2[x]);
           y1 = v1 * c + v2 * s;
@@ -855,15 +885,20 @@ constexpr long long kWait = 1000000000LL;
 // h0, h0 + 1 (pk = 1: tile t holds head h0 + t), as in the persistent forward.
 struct Unit {
   Block blk;
+  int it;   // work item
   int q0, q1, h0, pk, hk, kv_lo, kv_hi, n;
+  int ja, jb;  // an abs-block unit skips key tiles [ja, jb) (they hold abs keys); n counts the others
   int cls;  // the block's first rotation-class entry (chunk_cls), -1: none
-  bool masked, k_pre;
+  bool masked, k_pre, abs;
 };
 
-// Rotation class of K tile j (64 keys: one class chunk) of a unit, -1: the
-// tile is rotated in shared memory (or comes from k_rot when k_pre).
+// Key tile of the unit's j-th tile (abs-block units skip [ja, jb)).
+__device__ __forceinline__ int unit_tile(const Unit& w, int j) { return j < w.ja ? j : j + (w.jb - w.ja); }
+
+// Rotation class of the unit's j-th K tile (64 keys: one class chunk), -1:
+// the tile is rotated in shared memory (or comes from k_rot when k_pre).
 __device__ __forceinline__ int tile_class(const AiAttnLayout& L, const Unit& w, int j, int32_t* status) {
-  return w.cls < 0 ? -1 : chunk_class(L, w.cls, j, status);
+  return w.cls < 0 ? -1 : chunk_class(L, w.cls, unit_tile(w, j), status);
 }
 
 __device__ __forceinline__ int unit_head(const Unit& w, int t, int r) {
@@ -871,21 +906,35 @@ __device__ __forceinline__ int unit_head(const Unit& w, int t, int r) {
 }
 __device__ __forceinline__ int unit_row(const Unit& w, int r) { return w.q0 + (w.pk == 2 ? (r & 63) : r); }
 
-__device__ __forceinline__ Unit load_unit(const AiAttnFwdArgs& f, int u, int prerot, int n_pack_units) {
+__device__ __forceinline__ Unit load_unit(const AiAttnFwdArgs& f, int u, int prerot, const UnitPlan& up) {
   const AiAttnLayout& L = f.layout;
   const int hpairs = f.num_q_heads / 2, hquads = f.num_q_heads / 4, G = f.num_q_heads / f.num_kv_heads;
   int it;
   Unit w;
-  if (u < n_pack_units) {
-    it = L.n_fwd_abs_items + u / hquads;
-    w.h0 = 4 * (u % hquads);
+  w.abs = u < up.n_abs_units;
+  if (w.abs) {
+    if (u < up.n_abs_pack_units) {
+      it = u / hquads;
+      w.h0 = 4 * (u % hquads);
+      w.pk = 2;
+    } else {
+      const int v = u - up.n_abs_pack_units;
+      it = up.n_abs_pack_units / hquads + v / hpairs;
+      w.h0 = 2 * (v % hpairs);
+      w.pk = 1;
+    }
+  } else if (u - up.n_abs_units < up.n_pack_units) {
+    const int v = u - up.n_abs_units;
+    it = L.n_fwd_abs_items + v / hquads;
+    w.h0 = 4 * (v % hquads);
     w.pk = 2;
   } else {
-    const int v = u - n_pack_units;
-    it = L.n_fwd_abs_items + (n_pack_units > 0 ? L.n_fwd_short_items : 0) + v / hpairs;
+    const int v = u - up.n_abs_units - up.n_pack_units;
+    it = L.n_fwd_abs_items + (up.n_pack_units > 0 ? L.n_fwd_short_items : 0) + v / hpairs;
     w.h0 = 2 * (v % hpairs);
     w.pk = 1;
   }
+  w.it = it;
   const int32_t* item = L.fwd_items + 4 * (int64_t)it;
   w.blk = load_block(L.blocks, item[0]);
   w.q0 = item[1];
@@ -894,6 +943,11 @@ __device__ __forceinline__ Unit load_unit(const AiAttnFwdArgs& f, int u, int pre
   w.kv_lo = w.blk.kv_lo;
   w.kv_hi = min(w.blk.e, w.q1);
   w.n = w.kv_hi > w.kv_lo ? (w.kv_hi - w.kv_lo + BN - 1) / BN : 0;
+  w.ja = w.jb = 0;
+  if (w.abs) {
+    abs_tiles(w.blk, w.kv_lo, w.kv_hi, BN, w.ja, w.jb);
+    w.n -= w.jb - w.ja;
+  }
   w.masked = (w.blk.flags & AI_BLOCKF_MASKED) != 0;
   w.k_pre = prerot && (w.blk.flags & AI_BLOCKF_OWNPOS);
   w.cls = w.k_pre ? -1 : block_classes(L, item[0], prerot != 0);
@@ -926,9 +980,10 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_qr,
                    const __grid_constant__ CUtensorMap tm_do, const __grid_constant__ CUtensorMap tm_kr,
                    const __grid_constant__ CUtensorMap tm_qr64, const __grid_constant__ CUtensorMap tm_do64,
-                   const __grid_constant__ CUtensorMap tm_kc, const int prerot, const int n_units,
-                   const int n_pack_units) {
+                   const __grid_constant__ CUtensorMap tm_kc, const int prerot, const UnitPlan up,
+                   float* __restrict__ part_dq) {
   using namespace dqw;
+  const int n_units = up.n_units;
   // The dK/dV kernel launched after this one reads nothing it writes: let it
   // start as soon as every CTA here has started, so its CTAs take each SM as
   // this kernel's CTA there finishes.
@@ -989,7 +1044,7 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
     const float2 sl2x2 = make_float2(sl2, sl2), scalex2 = make_float2(scale, scale);
     int g = 0, k = 0, ko = 0;  // ko: units with key tiles so far (DQ_DONE phases)
     for (int u = snake_unit(k); u < n_units && !*s_abort; u = snake_unit(++k)) {
-      const Unit w = load_unit(f, u, prerot, n_pack_units);
+      const Unit w = load_unit(f, u, prerot, up);
       const int i = unit_row(w, r), h = unit_head(w, t, r), b = w.blk.row, q1 = w.q1;
       int qrow = 0;
       float lse2 = 0.f, dl = 0.f;
@@ -1043,7 +1098,7 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
       const float2 nlse2 = make_float2(-lse2r, -lse2r), ndls = make_float2(-dls, -dls);
       int done = 0;
       for (int j = 0; j < w.n; ++j) {
-        const int gj = g + j, slot = gj % kKS, k0 = w.kv_lo + j * BN;
+        const int gj = g + j, slot = gj % kKS, k0 = w.kv_lo + unit_tile(w, j) * BN;
         if (!wait(S_FULL + t, gj & 1)) break;
         ptx::tc_fence_after();
         // Tiles wholly below the diagonal of a block without masked keys take
@@ -1128,6 +1183,23 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
           ptx::tc_fence_before();
           ptx::mbar_arrive(bar(DQ_FREE + t));
         }
+        if (w.abs) {
+          // An abs-block unit leaves its rows' dQrot (fp32, not rotated back)
+          // for the abs pass, which adds the tiles holding abs keys.
+          if (i < q1) {
+            float* po = part_dq + (((int64_t)w.it * f.num_q_heads + h) * BM + (i - w.q0)) * D;
+#pragma unroll
+            for (int x = 0; x < 32; x += 4) {
+              *reinterpret_cast<float4*>(po + 32 * hf + x) =
+                  make_float4(__uint_as_float(g1[x]), __uint_as_float(g1[x + 1]), __uint_as_float(g1[x + 2]),
+                              __uint_as_float(g1[x + 3]));
+              *reinterpret_cast<float4*>(po + 64 + 32 * hf + x) =
+                  make_float4(__uint_as_float(g2[x]), __uint_as_float(g2[x + 1]), __uint_as_float(g2[x + 2]),
+                              __uint_as_float(g2[x + 3]));
+            }
+          }
+          continue;
+        }
         float o1[32], o2[32];
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
@@ -1171,7 +1243,7 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
       int g = 0, k = 0;
       bool ok = true;
       for (int u = snake_unit(k); ok && u < n_units; u = snake_unit(++k)) {
-        const Unit w = load_unit(f, u, prerot, n_pack_units);
+        const Unit w = load_unit(f, u, prerot, up);
         const int b = w.blk.row;
         if (prerot) {
           if (k > 0 && !wait(Q_EMPTY, (k - 1) & 1)) break;
@@ -1200,7 +1272,7 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
         }
         const CUtensorMap* mk = w.k_pre ? &tm_kr : &tm_k;
         for (int j = 0; j < w.n; ++j, ++g) {
-          const int slot = g % kKS, k0 = w.kv_lo + j * BN;
+          const int slot = g % kKS, k0 = w.kv_lo + unit_tile(w, j) * BN;
           if (g >= kKS && !wait(KV_EMPTY + slot, ((g / kKS) - 1) & 1)) {
             ok = false;
             break;
@@ -1267,7 +1339,7 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
     int g = 0, k = 0;
     bool ok = true;
     for (int u = snake_unit(k); ok && u < n_units; u = snake_unit(++k)) {
-      const Unit w = load_unit(f, u, prerot, n_pack_units);
+      const Unit w = load_unit(f, u, prerot, up);
       if (!wait_u(Q_READY, k & 1)) break;
       if (w.n == 0) {
         ptx::mma_commit_w(bar(Q_EMPTY));
@@ -1316,9 +1388,9 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
     const int row = tid - 320;  // 0..63: key row of the tile
     int g = 0;
     for (int kr = 0, u = snake_unit(0); u < n_units && !*s_abort; u = snake_unit(++kr)) {
-      const Unit w = load_unit(f, u, prerot, n_pack_units);
+      const Unit w = load_unit(f, u, prerot, up);
       for (int j = 0; j < w.n; ++j, ++g) {
-        const int slot = g % kKS, key = w.kv_lo + j * BN + row;
+        const int slot = g % kKS, key = w.kv_lo + unit_tile(w, j) * BN + row;
         uint32_t info = 0;
         int p = 0;
         if (key < w.kv_hi) {
@@ -2015,8 +2087,15 @@ size_t sm100_kv_partial_bytes(const AiAttnFwdArgs& f) {
   return (n + 255) & ~size_t(255);
 }
 
-int sm100_bwd(const AiAttnBwdArgs& a, float* delta, void* rot, bool rot_ready, float* partials, cudaStream_t st,
-              cudaError_t* cuda_err) {
+size_t sm100_dq_abs_part_bytes(const AiAttnFwdArgs& f) {
+  const int G = f.num_kv_heads > 0 ? f.num_q_heads / f.num_kv_heads : 0;
+  if (!sm100_bwd_supported(f.dtype, f.head_dim) || G % 2 != 0 || f.layout.n_fwd_abs_items <= 0) return 0;
+  const size_t n = (size_t)f.layout.n_fwd_abs_items * f.num_q_heads * sm100bwd::dq::BM * sm100bwd::D * sizeof(float);
+  return (n + 255) & ~size_t(255);
+}
+
+int sm100_bwd(const AiAttnBwdArgs& a, float* delta, void* rot, bool rot_ready, float* partials, float* dq_part,
+              cudaStream_t st, cudaError_t* cuda_err) {
   using namespace sm100bwd;
   const AiAttnFwdArgs& f = a.fwd;
   if (!strides_ok(f.q) || !strides_ok(f.k) || !strides_ok(f.v) || !strides_ok(a.dout) || !strides_ok(a.dq) ||
@@ -2033,6 +2112,14 @@ int sm100_bwd(const AiAttnBwdArgs& a, float* delta, void* rot, bool rot_ready, f
     e = bwd_delta(a, delta, st);
   }
   if (e == cudaSuccess && pre && !rot_ready) e = prerot(f, rot, st);
+  // The abs split (with the rotated copies and room for dq_part): the
+  // persistent dQ kernel also runs the abs-block items' key tiles that hold
+  // no abs key and leaves their dQrot in dq_part; the one-head kernel, later
+  // in the stream, adds the tiles with abs keys and writes those rows.
+  const int Gq = f.num_q_heads / f.num_kv_heads;
+  const bool dq_split = pre && dq_part && Gq % 2 == 0 && f.layout.n_fwd_abs_items > 0;
+  CUtensorMap dq_tk, dq_tv, dq_tkc;  // maps of the deferred one-head dQ launch
+  bool dq_deferred = false;
   if (e == cudaSuccess && f.layout.n_fwd_items > 0) {
     CUtensorMap tk, tv, tqr, tdo, tkr;
     if (!sm100_make_map(&tk, f.k, f.batch, f.num_kv_heads, f.seq_len, dq::BN) ||
@@ -2053,36 +2140,64 @@ int sm100_bwd(const AiAttnBwdArgs& a, float* delta, void* rot, bool rot_ready, f
     if (pre && f.layout.n_rot_classes > 0 &&
         !sm100_make_map(&tkc, kc, f.layout.n_rot_classes, f.num_kv_heads, AI_ROT_CLASS_KEYS, AI_ROT_CLASS_KEYS))
       return AI_ERR_TMA;
-    if (n_single > 0) {
+    if (n_single > 0 && dq_split) {
+      dq_tk = tk;
+      dq_tv = tv;
+      dq_tkc = tkc;
+      dq_deferred = true;
+    } else if (n_single > 0) {
       e = cudaFuncSetAttribute(dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dq::kSmem);
       if (e == cudaSuccess) {
         ProfScope ps(AI_PROF_DQ, st);
-        dq_kernel<<<dim3(n_single, f.num_q_heads), kThreads, dq::kSmem, st>>>(a, delta, tk, tv, tkc, pre ? 1 : 0);
+        dq_kernel<<<dim3(n_single, f.num_q_heads), kThreads, dq::kSmem, st>>>(a, delta, tk, tv, tkc, pre ? 1 : 0,
+                                                                              nullptr);
         e = cudaGetLastError();
       }
     }
     CUtensorMap tqr64 = tk, tdo64 = tk;
     if (!sm100_make_map(&tdo64, a.dout, f.batch, f.num_q_heads, f.seq_len, dq::BM / 2)) return AI_ERR_TMA;
     if (pre && !sm100_make_map(&tqr64, qr, f.batch, f.num_q_heads, f.seq_len, dq::BM / 2)) return AI_ERR_TMA;
-    if (e == cudaSuccess && n_pair > 0) {
-      // Persistent: one CTA per SM walks the units: four-head units of the
-      // short items when a GQA group has a multiple of four query heads, then
-      // two-head units of the other items (the forward's order).
+    // Persistent: one CTA per SM walks the units (the forward's order): with
+    // the split, the abs-block items' units first, then four-head units of
+    // the short items when a GQA group has a multiple of four query heads,
+    // then two-head units of the other items.
+    UnitPlan up{0, 0, 0, 0};
+    if (G % 2 == 0) {
       const int n_short = (G % 4 == 0) ? f.layout.n_fwd_short_items : 0;
-      const int n_pack_units = n_short * (f.num_q_heads / 4);
-      const int n_units = n_pack_units + (n_pair - n_short) * (f.num_q_heads / 2);
+      up.n_pack_units = n_short * (f.num_q_heads / 4);
+      if (dq_split) {
+        const int n_abs_short = (G % 4 == 0) ? f.layout.n_fwd_abs_short_items : 0;
+        up.n_abs_pack_units = n_abs_short * (f.num_q_heads / 4);
+        up.n_abs_units = up.n_abs_pack_units + (f.layout.n_fwd_abs_items - n_abs_short) * (f.num_q_heads / 2);
+      }
+      up.n_units = up.n_abs_units + up.n_pack_units + (n_pair - n_short) * (f.num_q_heads / 2);
+    }
+    if (e == cudaSuccess && up.n_units > 0) {
       int dev = 0, sms = 148;
       if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-      const int grid = n_units < sms ? n_units : sms;
+      const int grid = up.n_units < sms ? up.n_units : sms;
       e = cudaFuncSetAttribute(dq_pers_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dqw::kSmem);
       if (e == cudaSuccess) {
         ProfScope ps(AI_PROF_DQ, st);
         dq_pers_kernel<<<grid, dqw::kThreads, dqw::kSmem, st>>>(a, delta, tk, tv, tqr, tdo, tkr, tqr64, tdo64,
-                                                                tkc, pre ? 1 : 0, n_units, n_pack_units);
+                                                                tkc, pre ? 1 : 0, up, dq_split ? dq_part : nullptr);
         e = cudaGetLastError();
       }
     }
   }
+  // The deferred one-head dQ launch (after the dK/dV pass below, so that the
+  // dK/dV CTAs start under the persistent dQ as before).
+  auto launch_dq_deferred = [&]() {
+    if (!dq_deferred || e != cudaSuccess) return;
+    dq_deferred = false;
+    e = cudaFuncSetAttribute(dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dq::kSmem);
+    if (e == cudaSuccess) {
+      ProfScope ps(AI_PROF_DQ, st);
+      dq_kernel<<<dim3(f.layout.n_fwd_abs_items, f.num_q_heads), kThreads, dq::kSmem, st>>>(
+          a, delta, dq_tk, dq_tv, dq_tkc, 1, dq_part);
+      e = cudaGetLastError();
+    }
+  };
   if (e == cudaSuccess && f.layout.n_kv_items > 0) {
     CUtensorMap tk, tv, tq, tdo, tqr, tkr;
     if (!sm100_make_map(&tk, f.k, f.batch, f.num_kv_heads, f.seq_len, kv::BN) ||
@@ -2133,6 +2248,7 @@ int sm100_bwd(const AiAttnBwdArgs& a, float* delta, void* rot, bool rot_ready, f
         }
       }
     }
+    launch_dq_deferred();
     if (e == cudaSuccess && n_abs > 0) {
       // Boxes of 64 / G rows for the steps that pack a group's heads.
       const int Gk = f.num_q_heads / f.num_kv_heads;
@@ -2150,6 +2266,7 @@ int sm100_bwd(const AiAttnBwdArgs& a, float* delta, void* rot, bool rot_ready, f
       }
     }
   }
+  launch_dq_deferred();  // (no key tiles at all: not launched above)
   if (e == cudaSuccess && !f.layout.all_rows_owned) {
     ProfScope ps(AI_PROF_BWD_FILL, st);
     e = bwd_fill(a, st);

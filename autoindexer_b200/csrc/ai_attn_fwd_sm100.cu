@@ -75,7 +75,8 @@ __device__ __forceinline__ uint32_t chunk_off(int r, int c) { return tile::chunk
 
 __global__ void __launch_bounds__(kThreads, 1)
     fwd_kernel(const AiAttnFwdArgs a, const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
-               const __grid_constant__ CUtensorMap tm_kc, const int prerot) {
+               const __grid_constant__ CUtensorMap tm_kc, const int prerot, const float* __restrict__ part_o,
+               const float* __restrict__ part_lse) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = tile::align1024(smem_raw);
   const uint32_t sbase = ptx::smem_u32(sm);
@@ -153,7 +154,40 @@ __global__ void __launch_bounds__(kThreads, 1)
   int n_tiles = 0;
   bool aborted = false;
 
-  for (int k0 = blk.kv_lo, jt = 0; k0 < kv_hi; k0 += BN, ++jt) {
+  // With the abs split the persistent kernel has run this item's key tiles
+  // without abs keys and left each row's (O / l, log2-sum) partial: start
+  // the online softmax from it (m = that sum, l = 1, O = the partial) and
+  // run the tiles that hold abs keys only.
+  const bool o_init = part_o != nullptr;
+  int j_begin = 0, j_end = kv_hi > blk.kv_lo ? (kv_hi - blk.kv_lo + BN - 1) / BN : 0;
+  if (o_init) {
+    abs_tiles(blk, blk.kv_lo, kv_hi, BN, j_begin, j_end);
+    const int64_t prow = ((int64_t)blockIdx.x * a.num_q_heads + h) * BM + (i - q0);
+    const bool have = i < q1;
+    const float lp = have ? part_lse[prow] : -CUDART_INF_F;
+    m_use = lp;
+    l = lp > -CUDART_INF_F ? 1.f : 0.f;
+#pragma unroll
+    for (int cc = 0; cc < D / 32; ++cc) {
+      uint32_t r[32];
+#pragma unroll
+      for (int x = 0; x < 32; x += 4) {
+        const float4 v = (have && l > 0.f) ? *reinterpret_cast<const float4*>(part_o + prow * D + 32 * cc + x)
+                                           : make_float4(0.f, 0.f, 0.f, 0.f);
+        r[x] = __float_as_uint(v.x);
+        r[x + 1] = __float_as_uint(v.y);
+        r[x + 2] = __float_as_uint(v.z);
+        r[x + 3] = __float_as_uint(v.w);
+      }
+      ptx::tmem_st32(tmem + lane_base + kColO + 32 * cc, r);
+    }
+    ptx::tmem_wait_st();
+    ptx::tc_fence_before();
+    __syncthreads();
+    ptx::tc_fence_after();
+  }
+
+  for (int jt = j_begin, k0 = blk.kv_lo + j_begin * BN; jt < j_end; ++jt, k0 += BN) {
     // Only a tile that holds one of the block's abs keys needs S_abs.
     const bool tabs = blk.abs_in(k0, min(k0 + BN, kv_hi));
     const int c0 = cls >= 0 ? chunk_class(L, cls, 2 * jt, a.status) : -1;
@@ -272,7 +306,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     float alpha = 1.f;
     bool rescale = false;
     if (m_new > m_use + 8.f) {
-      if (n_tiles > 0 && l > 0.f) {
+      if ((n_tiles > 0 || o_init) && l > 0.f) {
         alpha = exp2f(m_use - m_new);
         rescale = true;
       }
@@ -317,7 +351,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t aoff = (uint32_t)(kk >> 2) * kHalf + (uint32_t)(kk & 3) * 32u;
         const uint32_t boff = (uint32_t)kk * 2048u;  // 16 key rows of 128 bytes
         ptx::mma_ss(tmem + kColO, ptx::sdesc_sw128(sbase + Smem::P + aoff, 16, 1024),
-                    ptx::sdesc_sw128(sbase + Smem::V + boff, kHalf, 1024), idesc_pv, (n_tiles > 0 || kk > 0) ? 1u : 0u);
+                    ptx::sdesc_sw128(sbase + Smem::V + boff, kHalf, 1024), idesc_pv,
+                    (n_tiles > 0 || o_init || kk > 0) ? 1u : 0u);
       }
       ptx::mma_commit(bar_mma);
     }
@@ -343,7 +378,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
     for (int cc = 0; cc < D / 32; ++cc) {
       uint32_t r[32];
-      if (n_tiles > 0) {
+      if (n_tiles > 0 || o_init) {
         ptx::tmem_ld32(tmem + lane_base + kColO + 32 * cc, r);
         ptx::tmem_wait_ld();
       } else {
@@ -466,18 +501,24 @@ static_assert(kSmem <= 227 * 1024, "shared memory budget");
 // in the work list), then the two-head units of the remaining items.
 struct Unit {
   Block blk;
+  int it;   // work item
   int q0, q1, h0, pk, hk, kv_lo, kv_hi, n;
+  int ja, jb;  // an abs-block unit skips key tiles [ja, jb) (they hold abs keys); n counts the others
   int cls;  // the block's first rotation-class entry (chunk_cls), -1: none
-  bool masked, k_pre;
+  bool masked, k_pre, abs;
 };
+
+// Key tile of the unit's j-th tile (abs-block units skip [ja, jb)).
+__device__ __forceinline__ int unit_tile(const Unit& w, int j) { return j < w.ja ? j : j + (w.jb - w.ja); }
 
 // Rotation classes of the two 64-key chunks of K tile j of a unit: a tile
 // whose chunks both have a class is read rotated from the class copies.
 __device__ __forceinline__ bool class_tile(const AiAttnLayout& L, const Unit& w, int j, int32_t* status, int& c0,
                                            int& c1) {
   if (w.cls < 0) return false;
-  c0 = chunk_class(L, w.cls, 2 * j, status);
-  c1 = chunk_class(L, w.cls, 2 * j + 1, status);
+  const int jt = unit_tile(w, j);
+  c0 = chunk_class(L, w.cls, 2 * jt, status);
+  c1 = chunk_class(L, w.cls, 2 * jt + 1, status);
   return c0 >= 0 && c1 >= 0;
 }
 
@@ -487,21 +528,35 @@ __device__ __forceinline__ int unit_head(const Unit& w, int t, int r) {
 }
 __device__ __forceinline__ int unit_row(const Unit& w, int r) { return w.q0 + (w.pk == 2 ? (r & 63) : r); }
 
-__device__ __forceinline__ Unit load_unit(const AiAttnFwdArgs& a, int u, int prerot, int n_pack_units) {
+__device__ __forceinline__ Unit load_unit(const AiAttnFwdArgs& a, int u, int prerot, const UnitPlan& up) {
   const AiAttnLayout& L = a.layout;
   const int hpairs = a.num_q_heads / 2, hquads = a.num_q_heads / 4, G = a.num_q_heads / a.num_kv_heads;
   int it;
   Unit w;
-  if (u < n_pack_units) {
-    it = L.n_fwd_abs_items + u / hquads;
-    w.h0 = 4 * (u % hquads);
+  w.abs = u < up.n_abs_units;
+  if (w.abs) {
+    if (u < up.n_abs_pack_units) {
+      it = u / hquads;
+      w.h0 = 4 * (u % hquads);
+      w.pk = 2;
+    } else {
+      const int v = u - up.n_abs_pack_units;
+      it = up.n_abs_pack_units / hquads + v / hpairs;
+      w.h0 = 2 * (v % hpairs);
+      w.pk = 1;
+    }
+  } else if (u - up.n_abs_units < up.n_pack_units) {
+    const int v = u - up.n_abs_units;
+    it = L.n_fwd_abs_items + v / hquads;
+    w.h0 = 4 * (v % hquads);
     w.pk = 2;
   } else {
-    const int v = u - n_pack_units;
-    it = L.n_fwd_abs_items + (n_pack_units > 0 ? L.n_fwd_short_items : 0) + v / hpairs;
+    const int v = u - up.n_abs_units - up.n_pack_units;
+    it = L.n_fwd_abs_items + (up.n_pack_units > 0 ? L.n_fwd_short_items : 0) + v / hpairs;
     w.h0 = 2 * (v % hpairs);
     w.pk = 1;
   }
+  w.it = it;
   const int32_t* item = L.fwd_items + 4 * (int64_t)it;
   w.blk = load_block(L.blocks, item[0]);
   w.q0 = item[1];
@@ -510,6 +565,11 @@ __device__ __forceinline__ Unit load_unit(const AiAttnFwdArgs& a, int u, int pre
   w.kv_lo = w.blk.kv_lo;
   w.kv_hi = min(w.blk.e, w.q1);
   w.n = w.kv_hi > w.kv_lo ? (w.kv_hi - w.kv_lo + BN - 1) / BN : 0;
+  w.ja = w.jb = 0;
+  if (w.abs) {
+    abs_tiles(w.blk, w.kv_lo, w.kv_hi, BN, w.ja, w.jb);
+    w.n -= w.jb - w.ja;
+  }
   w.masked = (w.blk.flags & AI_BLOCKF_MASKED) != 0;
   w.k_pre = prerot && (w.blk.flags & AI_BLOCKF_OWNPOS);
   w.cls = w.k_pre ? -1 : block_classes(L, item[0], prerot != 0);
@@ -522,8 +582,9 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_qr,
                     const __grid_constant__ CUtensorMap tm_kr, const __grid_constant__ CUtensorMap tm_o,
                     const __grid_constant__ CUtensorMap tm_qr64, const __grid_constant__ CUtensorMap tm_kc,
-                    const int prerot, const int n_units, const int n_pack_units) {
+                    const int prerot, const UnitPlan up, float* __restrict__ part_o, float* __restrict__ part_lse) {
   using namespace pf;
+  const int n_units = up.n_units;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = tile::align1024(smem_raw);
   const uint32_t sbase = ptx::smem_u32(sm);
@@ -581,7 +642,7 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
     // The next unit's description is read from global memory while this
     // unit's last PV MMAs run (before the epilogue's O_DONE wait).
     Unit w_next{};
-    if (snake_unit(0) < n_units) w_next = load_unit(a, snake_unit(0), prerot, n_pack_units);
+    if (snake_unit(0) < n_units) w_next = load_unit(a, snake_unit(0), prerot, up);
     bool store_pending = false;  // thread 0: the last TMA store's smem read not yet waited for
     for (int u = snake_unit(k); u < n_units && !*s_abort; u = snake_unit(++k)) {
       const Unit w = w_next;
@@ -623,7 +684,7 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
       float m_use = -CUDART_INF_F, l = 0.f;
       int done = 0;
       for (int j = 0; j < w.n; ++j) {
-        const int gj = g + j, k0 = w.kv_lo + j * BN;
+        const int gj = g + j, k0 = w.kv_lo + unit_tile(w, j) * BN;
         if (!wait(S_FULL + t, gj & 1)) break;
         ptx::tc_fence_after();
         const bool fast = !w.masked && (k0 + BN <= w.kv_hi) && (k0 + BN - 1 <= w.q0);
@@ -713,7 +774,7 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
         done = j + 1;
       }
       if (done != w.n) break;
-      if (snake_unit(k + 1) < n_units) w_next = load_unit(a, snake_unit(k + 1), prerot, n_pack_units);
+      if (snake_unit(k + 1) < n_units) w_next = load_unit(a, snake_unit(k + 1), prerot, up);
       // Epilogue: O_t / l.  O_t is read into registers, then released to the
       // next unit's first PV before the global stores.
       bool have_o = false;
@@ -726,6 +787,10 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
       __nv_bfloat16* Orow = static_cast<__nv_bfloat16*>(a.out.ptr) + b * a.out.stride_b + h * a.out.stride_h +
                             (int64_t)i * a.out.stride_t;
       const float inv = l > 0.f ? 1.f / l : 0.f;
+      // An abs-block unit leaves its rows' partial (O / l in fp32, log2-sum)
+      // for the abs pass, which adds the tiles holding abs keys.
+      const int64_t prow = ((int64_t)w.it * a.num_q_heads + h) * BM + (i - w.q0);
+      float* po = (w.abs && i < w.q1) ? part_o + prow * D : nullptr;
       uint4 packed[D / 8];
 #pragma unroll
       for (int cc = 0; cc < D / 32; ++cc) {
@@ -736,6 +801,13 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
         } else {
 #pragma unroll
           for (int x = 0; x < 32; ++x) rr[x] = 0u;
+        }
+        if (po) {
+#pragma unroll
+          for (int x = 0; x < 32; x += 4)
+            *reinterpret_cast<float4*>(po + 32 * cc + x) =
+                make_float4(__uint_as_float(rr[x]) * inv, __uint_as_float(rr[x + 1]) * inv,
+                            __uint_as_float(rr[x + 2]) * inv, __uint_as_float(rr[x + 3]) * inv);
         }
 #pragma unroll
         for (int c8 = 0; c8 < 4; ++c8) {
@@ -756,7 +828,7 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
       // (the TMA box would spill into the next block's rows).  A unit without
       // key tiles stores its zero rows directly: its thread 0 has not waited
       // for the group's other threads in O_DONE.
-      const bool full = w.pk == 1 && w.q1 == w.q0 + BM && w.n > 0;
+      const bool full = !w.abs && w.pk == 1 && w.q1 == w.q0 + BM && w.n > 0;
       const uint32_t buf = OSTAGE + (uint32_t)t * kHalf;
       bool ok_st = true;
       if (full) {
@@ -793,12 +865,14 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
           }
           ++nst;
         }
-      } else if (i < w.q1) {
+      } else if (i < w.q1 && !w.abs) {
 #pragma unroll
         for (int c = 0; c < D / 8; ++c) *reinterpret_cast<uint4*>(Orow + 8 * c) = packed[c];
       }
       if (!ok_st) break;
-      if (i < w.q1)
+      if (i < w.q1 && w.abs)
+        part_lse[prow] = l > 0.f ? m_use + log2f(l) : -CUDART_INF_F;
+      else if (i < w.q1)
         a.lse[((int64_t)b * a.num_q_heads + h) * a.seq_len + i] = l > 0.f ? (m_use + log2f(l)) * kLn2 : -CUDART_INF_F;
       g += w.n;
     }
@@ -819,7 +893,7 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
       int g = 0, k = 0;
       bool ok = true;
       for (int u = snake_unit(k); ok && u < n_units; u = snake_unit(++k)) {
-        const Unit w = load_unit(a, u, prerot, n_pack_units);
+        const Unit w = load_unit(a, u, prerot, up);
         const int b = w.blk.row;
         const CUtensorMap* mk = w.k_pre ? &tm_kr : &tm_k;
         for (int j = 0; j <= w.n && ok; ++j) {
@@ -846,7 +920,7 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
             }
           }
           if (j == w.n) break;
-          const int slot = g & 1, k0 = w.kv_lo + j * BN;
+          const int slot = g & 1, k0 = w.kv_lo + unit_tile(w, j) * BN;
           const uint32_t kb = sbase + KB + (uint32_t)slot * kTile, vb = sbase + VB + (uint32_t)slot * kTile;
           if (g >= 2 && !wait(K_EMPTY + slot, ((g >> 1) - 1) & 1)) {
             ok = false;
@@ -922,7 +996,7 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
     int g = 0, k = 0;
     bool ok = true;
     for (int u = snake_unit(k); ok && u < n_units; u = snake_unit(++k)) {
-      const Unit w = load_unit(a, u, prerot, n_pack_units);
+      const Unit w = load_unit(a, u, prerot, up);
       if (!wait_u(Q_READY, k & 1)) break;
       if (w.n == 0) {
         ptx::mma_commit_w(bar(Q_EMPTY));
@@ -979,7 +1053,7 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
     const __half2* cs16 = static_cast<const __half2*>(L.rope_cs16);
     int g = 0;
     for (int kr = 0, u = snake_unit(0); u < n_units && !*s_abort; u = snake_unit(++kr)) {
-      const Unit w = load_unit(a, u, prerot, n_pack_units);
+      const Unit w = load_unit(a, u, prerot, up);
       for (int j = 0; j < w.n; ++j, ++g) {
         const int slot = g & 1;
         int c0, c1;
@@ -988,7 +1062,7 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
         const uint32_t kt = KB + (uint32_t)slot * kTile;
 #pragma unroll
         for (int hr = 0; hr < 2; ++hr) {
-          const int row = rt + 64 * hr, key = w.kv_lo + j * BN + row;
+          const int row = rt + 64 * hr, key = w.kv_lo + unit_tile(w, j) * BN + row;
           uint32_t info = 0;
           if (key < w.kv_hi) {
             info = (uint32_t)__ldg(L.key_info + w.blk.key_off + key);
@@ -1069,6 +1143,13 @@ bool sm100_fwd_supported(int dtype, int head_dim) { return dtype == AI_DTYPE_BF1
 
 int sm100_fwd_tile_rows() { return sm100::BM; }
 
+size_t sm100_fwd_abs_part_bytes(const AiAttnFwdArgs& a) {
+  const int G = a.num_kv_heads > 0 ? a.num_q_heads / a.num_kv_heads : 0;
+  if (!sm100_fwd_supported(a.dtype, a.head_dim) || G % 2 != 0 || a.layout.n_fwd_abs_items <= 0) return 0;
+  const size_t rows = (size_t)a.layout.n_fwd_abs_items * a.num_q_heads * sm100::BM;
+  return (rows * (sm100::D + 1) * sizeof(float) + 255) & ~size_t(255);
+}
+
 int sm100_fwd(const AiAttnFwdArgs& a, cudaStream_t st, cudaError_t* cuda_err) {
   using namespace sm100;
   if (!strides_ok(a.q) || !strides_ok(a.k) || !strides_ok(a.v) || !strides_ok(a.out)) return AI_ERR_STRIDE;
@@ -1076,7 +1157,8 @@ int sm100_fwd(const AiAttnFwdArgs& a, cudaStream_t st, cudaError_t* cuda_err) {
   // With enough workspace, Q and K are rotated once (HBM-bound) and the
   // warp-specialised kernel reads the rotated copies.  They are written
   // whenever the workspace holds them, so that the backward can reuse them.
-  const bool pre = a.workspace && a.workspace_bytes >= prerot_bytes(a, nullptr);
+  const size_t pb = prerot_bytes(a, nullptr);
+  const bool pre = a.workspace && a.workspace_bytes >= pb;
   AiTensor4 qr{}, kr{}, kc{};
   if (pre) {
     if (!sm100_rotated_views(a, a.workspace, &qr, &kr, &kc)) return AI_ERR_ALIGN;
@@ -1088,47 +1170,69 @@ int sm100_fwd(const AiAttnFwdArgs& a, cudaStream_t st, cudaError_t* cuda_err) {
     if (!sm100_make_map(&tm_v, a.v, a.batch, a.num_kv_heads, a.seq_len, BN)) return AI_ERR_TMA;
     // Items of blocks with abs keys (and every item when a GQA group has an
     // odd number of query heads) run on the one-head kernel; the rest run two
-    // heads per CTA on the warp-specialised kernel.
+    // or four heads per unit on the warp-specialised persistent kernel.  With
+    // room in the workspace for the abs split, the persistent kernel also
+    // runs the abs-block items' key tiles that hold no abs key, leaving
+    // partial rows that the one-head kernel finishes with the other tiles.
     const int G = a.num_q_heads / a.num_kv_heads;
     const int n_single = (G % 2 == 0) ? a.layout.n_fwd_abs_items : a.layout.n_fwd_items;
     const int n_pair = a.layout.n_fwd_items - n_single;
+    const size_t part_bytes = sm100_fwd_abs_part_bytes(a);
+    const bool split = pre && part_bytes > 0 && a.workspace_bytes >= pb + part_bytes;
+    float* part_o = split ? reinterpret_cast<float*>(static_cast<char*>(a.workspace) + pb) : nullptr;
+    float* part_lse = split ? part_o + (size_t)a.layout.n_fwd_abs_items * a.num_q_heads * BM * D : nullptr;
+    UnitPlan up{0, 0, 0, 0};
+    if (G % 2 == 0) {
+      const int n_short = (G % 4 == 0) ? a.layout.n_fwd_short_items : 0;
+      up.n_pack_units = n_short * (a.num_q_heads / 4);
+      if (split) {
+        const int n_abs_short = (G % 4 == 0) ? a.layout.n_fwd_abs_short_items : 0;
+        up.n_abs_pack_units = n_abs_short * (a.num_q_heads / 4);
+        up.n_abs_units = up.n_abs_pack_units + (a.layout.n_fwd_abs_items - n_abs_short) * (a.num_q_heads / 2);
+      }
+      up.n_units = up.n_abs_units + up.n_pack_units + (n_pair - n_short) * (a.num_q_heads / 2);
+    }
     CUtensorMap tm_kc = tm_k;
     if (pre && a.layout.n_rot_classes > 0 &&
         !sm100_make_map(&tm_kc, kc, a.layout.n_rot_classes, a.num_kv_heads, AI_ROT_CLASS_KEYS, AI_ROT_CLASS_KEYS))
       return AI_ERR_TMA;
-    if (n_single > 0) {
+    auto launch_single = [&]() -> int {
+      if (n_single <= 0) return AI_OK;
       e = cudaFuncSetAttribute(fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
       if (e == cudaSuccess) {
         ProfScope ps(AI_PROF_FWD, st);
-        fwd_kernel<<<dim3(n_single, a.num_q_heads), kThreads, kSmemBytes, st>>>(a, tm_k, tm_v, tm_kc, pre ? 1 : 0);
+        fwd_kernel<<<dim3(n_single, a.num_q_heads), kThreads, kSmemBytes, st>>>(a, tm_k, tm_v, tm_kc, pre ? 1 : 0,
+                                                                                part_o, part_lse);
         e = cudaGetLastError();
       }
-    }
-    if (e == cudaSuccess && n_pair > 0) {
+      return AI_OK;
+    };
+    auto launch_pers = [&]() -> int {
+      if (up.n_units <= 0) return AI_OK;
       CUtensorMap tm_qr = tm_k, tm_kr = tm_k, tm_qr64 = tm_k;
       if (pre && (!sm100_make_map(&tm_qr, qr, a.batch, a.num_q_heads, a.seq_len, BM) ||
                   !sm100_make_map(&tm_qr64, qr, a.batch, a.num_q_heads, a.seq_len, BM / 2) ||
                   !sm100_make_map(&tm_kr, kr, a.batch, a.num_kv_heads, a.seq_len, BN)))
         return AI_ERR_TMA;
-      // Persistent: one CTA per SM walks the units: four-head units of the
-      // short items when a GQA group has a multiple of four query heads, then
-      // two-head units of the other items.
-      const int n_short = (G % 4 == 0) ? a.layout.n_fwd_short_items : 0;
-      const int n_pack_units = n_short * (a.num_q_heads / 4);
-      const int n_units = n_pack_units + (n_pair - n_short) * (a.num_q_heads / 2);
       int dev = 0, sms = 148;
       if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-      const int grid = n_units < sms ? n_units : sms;
+      const int grid = up.n_units < sms ? up.n_units : sms;
       CUtensorMap tm_o;
       if (!sm100_make_map(&tm_o, a.out, a.batch, a.num_q_heads, a.seq_len, BM)) return AI_ERR_TMA;
       e = cudaFuncSetAttribute(fwd_pers_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pf::kSmem);
       if (e == cudaSuccess) {
         ProfScope ps(AI_PROF_FWD, st);
         fwd_pers_kernel<<<grid, pf::kThreads, pf::kSmem, st>>>(a, tm_k, tm_v, tm_qr, tm_kr, tm_o, tm_qr64, tm_kc,
-                                                                pre ? 1 : 0, n_units, n_pack_units);
+                                                                pre ? 1 : 0, up, part_o, part_lse);
         e = cudaGetLastError();
       }
-    }
+      return AI_OK;
+    };
+    // The split's partial rows come from the persistent kernel: it runs first.
+    int rc = split ? launch_pers() : launch_single();
+    if (rc != AI_OK) return rc;
+    if (e == cudaSuccess) rc = split ? launch_single() : launch_pers();
+    if (rc != AI_OK) return rc;
   }
   if (cuda_err) *cuda_err = e;
   return e == cudaSuccess ? AI_OK : AI_ERR_LAUNCH;

@@ -52,6 +52,7 @@ int validate_fwd(const AiAttnFwdArgs* a) {
   if (L.n_rot_classes < 0 || L.n_chunk_cls < 0 ||
       (L.n_rot_classes > 0 && (!L.blk_cls || !L.chunk_cls || !L.rot_classes || L.n_chunk_cls <= 0)))
     return AI_ERR_LAYOUT;
+  if (L.n_fwd_abs_short_items < 0 || L.n_fwd_abs_short_items > L.n_fwd_abs_items) return AI_ERR_LAYOUT;
   if (L.n_fwd_abs_items < 0 || L.n_fwd_short_items < 0 ||
       (int64_t)L.n_fwd_abs_items + L.n_fwd_short_items > L.n_fwd_items || L.n_kv_abs_items < 0 ||
       L.n_kv_abs_items > L.n_kv_items)
@@ -115,7 +116,9 @@ int ai_attn_fwd_workspace(const AiAttnFwdArgs* a, size_t* bytes) {
   if (!a || !bytes) return AI_ERR_NULL;
   int rc = validate_fwd(a);
   if (rc != AI_OK) return rc;
-  *bytes = ai::sm100_fwd_supported(a->dtype, a->head_dim) ? ai::prerot_bytes(*a, nullptr) : 0;
+  *bytes = ai::sm100_fwd_supported(a->dtype, a->head_dim)
+               ? ai::prerot_bytes(*a, nullptr) + ai::sm100_fwd_abs_part_bytes(*a)
+               : 0;
   return AI_OK;
 }
 
@@ -125,7 +128,7 @@ int ai_attn_bwd_workspace(const AiAttnBwdArgs* a, size_t* bytes) {
   if (rc != AI_OK) return rc;
   *bytes = delta_bytes(a->fwd);
   if (ai::sm100_bwd_supported(a->fwd.dtype, a->fwd.head_dim)) {
-    *bytes += ai::sm100_kv_partial_bytes(a->fwd);
+    *bytes += ai::sm100_kv_partial_bytes(a->fwd) + ai::sm100_dq_abs_part_bytes(a->fwd);
     if (!fwd_copies(*a)) *bytes += ai::prerot_bytes(a->fwd, nullptr);
   }
   return AI_OK;
@@ -143,20 +146,22 @@ int ai_attn_bwd(const AiAttnBwdArgs* a, void* stream) {
   float* delta = static_cast<float*>(a->workspace);
   if (ai::sm100_bwd_supported(a->fwd.dtype, a->fwd.head_dim)) {
     // Workspace: delta, then the dK/dV partial sums of split key tiles when
-    // the layout splits some and they fit, then the rotated Q and K copies
-    // when the forward's are not passed (fwd_rotated) and they fit (else
-    // every tile is rotated in shared memory).
+    // the layout splits some and they fit, then the dQ partials of the abs
+    // split when they fit, then the rotated Q and K copies when the
+    // forward's are not passed (fwd_rotated) and they fit (else every tile is
+    // rotated in shared memory and the abs split is off).
     size_t used = delta_bytes(a->fwd);
-    float* partials = nullptr;
-    const size_t pb = ai::sm100_kv_partial_bytes(a->fwd);
-    if (pb > 0 && a->workspace_bytes >= used + pb) {
-      partials = reinterpret_cast<float*>(static_cast<char*>(a->workspace) + used);
-      used += pb;
-    }
-    if (fwd_copies(*a)) return ai::sm100_bwd(*a, delta, a->fwd.workspace, true, partials, st, nullptr);
-    void* rot = nullptr;
-    if (a->workspace_bytes >= used + ai::prerot_bytes(a->fwd, nullptr)) rot = static_cast<char*>(a->workspace) + used;
-    return ai::sm100_bwd(*a, delta, rot, false, partials, st, nullptr);
+    auto take = [&](size_t n) -> float* {
+      if (n == 0 || a->workspace_bytes < used + n) return nullptr;
+      float* p = reinterpret_cast<float*>(static_cast<char*>(a->workspace) + used);
+      used += n;
+      return p;
+    };
+    float* partials = take(ai::sm100_kv_partial_bytes(a->fwd));
+    float* dq_part = take(ai::sm100_dq_abs_part_bytes(a->fwd));
+    if (fwd_copies(*a)) return ai::sm100_bwd(*a, delta, a->fwd.workspace, true, partials, dq_part, st, nullptr);
+    void* rot = take(ai::prerot_bytes(a->fwd, nullptr));
+    return ai::sm100_bwd(*a, delta, rot, false, partials, dq_part, st, nullptr);
   }
   ai::ProfScope ps(AI_PROF_SIMT, st);
   return launch_status(ai::simt_bwd(*a, delta, st));

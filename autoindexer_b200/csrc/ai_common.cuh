@@ -79,6 +79,36 @@ __device__ __forceinline__ int pack_heads(int rows, int G) {
   return 1;
 }
 
+// Work units of the persistent forward / dQ kernels: with the abs split on,
+// the items of blocks with abs keys come first (their key tiles without abs
+// keys: n_abs_pack_units four-head units of the short ones, then two-head
+// units of the others), then n_pack_units four-head units of the other short
+// items, then two-head units of the rest; n_units in all.
+struct UnitPlan {
+  int n_abs_pack_units, n_abs_units, n_pack_units, n_units;
+};
+
+// Key tiles [ja, jb) (tiles of bn keys from kv_lo, the last one ending at
+// kv_hi) that hold one of the block's abs keys: exactly the tiles for which
+// Block::abs_in(k0, min(k0 + bn, kv_hi)) holds (a contiguous range, since the
+// abs keys lie in [abs_lo, abs_hi)); ja = jb = 0 when there are none.
+__device__ __forceinline__ void abs_tiles(const Block& blk, int kv_lo, int kv_hi, int bn, int& ja, int& jb) {
+  ja = jb = 0;
+  const int n = kv_hi > kv_lo ? (kv_hi - kv_lo + bn - 1) / bn : 0;
+  if (!(blk.flags & AI_BLOCKF_ABS) || n == 0) return;
+  if (blk.abs_hi <= blk.abs_lo) {
+    jb = n;
+    return;
+  }
+  if (blk.abs_lo >= kv_hi || blk.abs_hi <= kv_lo) return;
+  const int a0 = blk.abs_lo < kv_lo ? 0 : (blk.abs_lo - kv_lo) / bn;
+  const int a1 = min(n, (blk.abs_hi - kv_lo + bn - 1) / bn);
+  if (a0 < a1) {
+    ja = a0;
+    jb = a1;
+  }
+}
+
 // First chunk_cls entry of a block's rotation classes, or -1 when the block
 // has none or the rotated copies are not in the workspace (`prerot` false).
 __device__ __forceinline__ int block_classes(const AiAttnLayout& L, int block, bool prerot) {

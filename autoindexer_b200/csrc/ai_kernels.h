@@ -38,6 +38,9 @@ struct ProfScope {
 
 // Returns AI_OK or an AiStatus > 0; `cuda_err` receives the CUDA error of a failed launch.
 int sm100_fwd(const AiAttnFwdArgs& a, cudaStream_t st, cudaError_t* cuda_err);
+// Forward workspace after the rotated copies for the abs split: partial rows
+// (fp32 O / l and log2-sum) of the abs-block items (0: no split possible).
+size_t sm100_fwd_abs_part_bytes(const AiAttnFwdArgs& a);
 bool sm100_bwd_supported(int dtype, int head_dim);
 int sm100_kv_tile_rows();
 // `rot`: scratch for the once-rotated Q/K copies (prerot_bytes), or nullptr to
@@ -46,8 +49,11 @@ int sm100_kv_tile_rows();
 // Bytes of fp32 partial sums the dK/dV pass wants for split key tiles (0:
 // the layout splits none, or splitting would not pay on this device).
 size_t sm100_kv_partial_bytes(const AiAttnFwdArgs& f);
-int sm100_bwd(const AiAttnBwdArgs& a, float* delta, void* rot, bool rot_ready, float* partials, cudaStream_t st,
-              cudaError_t* cuda_err);
+// `dq_part`: scratch of sm100_dq_abs_part_bytes for the abs split of dQ, or
+// nullptr (the one-head kernel then runs the abs-block items whole).
+size_t sm100_dq_abs_part_bytes(const AiAttnFwdArgs& f);
+int sm100_bwd(const AiAttnBwdArgs& a, float* delta, void* rot, bool rot_ready, float* partials, float* dq_part,
+              cudaStream_t st, cudaError_t* cuda_err);
 // TMA map over a (B, H, T, 128) bf16 tensor, box 64 x box_rows, 128-byte swizzle.
 bool sm100_make_map(CUtensorMap* map, const AiTensor4& t, int B, int H, int T, int box_rows);
 

@@ -224,7 +224,7 @@ struct Tables {
   std::vector<int32_t> blocks, row_blocks, row_cov, q_pos, k_own, fwd_items, kv_items, kv_chunks, kv_reduce;
   std::vector<int32_t> blk_cls, chunk_cls, rot_classes;
   std::vector<uint32_t> key_info;
-  int32_t n_fwd_abs = 0, n_fwd_short = 0, n_kv_abs = 0, n_kv_partials = 0, kv_cost_max = 0, kv_cost_total = 0;
+  int32_t n_fwd_abs = 0, n_fwd_abs_short = 0, n_fwd_short = 0, n_kv_abs = 0, n_kv_partials = 0, kv_cost_max = 0, kv_cost_total = 0;
   bool all_owned = true;
   int64_t pairs = 0, p_min = 0, p_max = 0;
 };
@@ -430,7 +430,8 @@ int build(const AiPrepList* lists, int32_t n_lists, const int32_t* list_of_row, 
       for (int64_t q0 = s; q0 < e; q0 += fwd_tile) {
         const int64_t q1 = std::min<int64_t>(q0 + fwd_tile, e);
         const int64_t cost = (q1 - q0) * std::max<int64_t>(0, std::min(e, q1) - kv_lo);
-        const int32_t group = (flags & AI_BLOCKF_ABS) ? 0 : (q1 - q0 <= fwd_tile / 2 ? 1 : 2);
+        const bool short_item = q1 - q0 <= fwd_tile / 2;
+        const int32_t group = (flags & AI_BLOCKF_ABS) ? (short_item ? 0 : 1) : (short_item ? 2 : 3);
         fwd.push_back({cost, nb, (int32_t)q0, (int32_t)q1, group});
       }
       ++nb;
@@ -464,8 +465,9 @@ int build(const AiPrepList* lists, int32_t n_lists, const int32_t* list_of_row, 
     }
   }
 
-  // Forward items: abs blocks' items, then short items, then the rest;
-  // longest first in each group (stable, so ties keep block order).
+  // Forward items: abs blocks' short items (at most fwd_tile / 2 rows), their
+  // other items, then the other blocks' short items, then the rest; longest
+  // first in each group (stable, so ties keep block order).
   std::stable_sort(fwd.begin(), fwd.end(), [](const FwdItem& x, const FwdItem& y) {
     if (x.group != y.group) return x.group < y.group;
     return x.cost > y.cost;
@@ -476,8 +478,9 @@ int build(const AiPrepList* lists, int32_t n_lists, const int32_t* list_of_row, 
     t->fwd_items[4 * i + 1] = fwd[i].q0;
     t->fwd_items[4 * i + 2] = fwd[i].q1;
     t->fwd_items[4 * i + 3] = 0;
-    t->n_fwd_abs += fwd[i].group == 0;
-    t->n_fwd_short += fwd[i].group == 1;
+    t->n_fwd_abs += fwd[i].group <= 1;
+    t->n_fwd_abs_short += fwd[i].group == 0;
+    t->n_fwd_short += fwd[i].group == 2;
   }
   std::stable_sort(kv.begin(), kv.end(), [](const KvItem& x, const KvItem& y) {
     if (x.abs != y.abs) return x.abs;
@@ -554,6 +557,63 @@ int build(const AiPrepList* lists, int32_t n_lists, const int32_t* list_of_row, 
     t->kv_chunks[4 * i + 3] = chunks[i].slot;
   }
   build_rot_classes(t);
+  return AI_OK;
+}
+
+// Index-head rows: one pass over the EXTEND blocks (compute_index_losses,
+// attn_layers.py:56-104); `fill` false only counts.
+int index_rows(const AiPrepList* l, const int32_t* type, int64_t editable_start, bool fill, int32_t* n_rows_out,
+               int64_t* n_keys_out, int64_t* edits, AiIndexRowsOut* out) {
+  if (!l || !type) return AI_ERR_NULL;
+  if (l->n_blocks < 0 || (l->n_blocks > 0 && (!l->boundary || !l->query_pos || !l->key_pos || !l->attn_mask)))
+    return AI_ERR_NULL;
+  int32_t nr = 0;
+  int64_t nk = 0, lo = 0, hi = 0;
+  for (int pass = 0; pass < (fill ? 2 : 1); ++pass) {
+    nr = 0;
+    nk = 0;
+    for (int32_t i = 0; i < l->n_blocks; ++i) {
+      if (type[i] != AI_BLOCK_TYPE_EXTEND) continue;
+      const int64_t* bd = l->boundary + 4 * (int64_t)i;
+      const int64_t s = bd[0], e = bd[1], ks = bd[2], ke = bd[3];
+      if (e - s < 2 || ke - ks != e || e > l->n_query || ke > l->n_keys) return AI_ERR_LAYOUT;
+      const int64_t ed = e - 1;
+      if (!fill && edits) edits[nr / 2] = ed;
+      for (int head = 0; head < 2; ++head) {
+        const int64_t qi = ed - 1 + head, n = ed + head, qpos = l->query_pos[qi];
+        if (fill) {
+          int32_t* row = out->rows + 4 * (int64_t)nr;
+          row[0] = head;
+          row[1] = (int32_t)qi;
+          row[2] = (int32_t)n;
+          row[3] = (int32_t)nk;
+          for (int64_t j = 0; j < n; ++j) {
+            const int64_t kp = l->key_pos[ks + j], rel = kp - qpos;
+            const bool ok = l->attn_mask[ks + j] && kp >= editable_start && (head == 0 || rel > 0);
+            if (pass == 0) {
+              if (ok) {
+                lo = std::min(lo, rel);
+                hi = std::max(hi, rel);
+              }
+            } else {
+              const int64_t r = std::min(std::max(rel - lo, (int64_t)0), hi - lo);
+              out->key_rows[nk + j] = (int32_t)r;
+              out->key_ok[nk + j] = ok ? 1 : 0;
+            }
+          }
+        }
+        ++nr;
+        nk += n;
+        if (nk > INT32_MAX) return AI_ERR_LAYOUT;
+      }
+    }
+  }
+  if (n_rows_out) *n_rows_out = nr;
+  if (n_keys_out) *n_keys_out = nk;
+  if (fill) {
+    out->rel_lo = lo;
+    out->rel_hi = hi;
+  }
   return AI_OK;
 }
 
@@ -648,10 +708,22 @@ int ai_attn_prep(const AiPrepList* lists, int32_t n_lists, const int32_t* list_o
   out->kv_cost_total = t.kv_cost_total;
   out->n_fwd_abs_items = t.n_fwd_abs;
   out->n_fwd_short_items = t.n_fwd_short;
+  out->n_fwd_abs_short_items = t.n_fwd_abs_short;
   out->n_kv_abs_items = t.n_kv_abs;
   out->all_rows_owned = t.all_owned ? 1 : 0;
   out->pairs_per_head = t.pairs;
   return AI_OK;
+}
+
+int ai_index_rows_sizes(const AiPrepList* list, const int32_t* block_type, int32_t* n_rows, int64_t* n_keys,
+                        int64_t* edits) {
+  if (!n_rows || !n_keys) return AI_ERR_NULL;
+  return index_rows(list, block_type, 0, false, n_rows, n_keys, edits, nullptr);
+}
+
+int ai_index_rows(const AiPrepList* list, const int32_t* block_type, int64_t editable_start, AiIndexRowsOut* out) {
+  if (!out || !out->rows || !out->key_rows || !out->key_ok) return AI_ERR_NULL;
+  return index_rows(list, block_type, editable_start, true, nullptr, nullptr, nullptr, out);
 }
 
 }  // extern "C"

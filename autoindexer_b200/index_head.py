@@ -95,16 +95,46 @@ def _t4(x: Tensor) -> "_lib.AiTensor4":
 class _Prepared:
     """Device copies of the rows and the rotary table for one call: the
     row table, targets, key table rows and key flags go over in one copy
-    from one pinned host buffer."""
+    from one pinned host buffer (filled by the native builder,
+    ``ai_index_rows``, in ``native``)."""
 
-    def __init__(self, ir: IndexRows, rotary_emb, head_dim: int, device):
-        ok_rel = ir.rel[ir.ok.astype(bool)]
-        lo = int(min(0, ok_rel.min())) if ok_rel.size else 0
-        hi = int(max(0, ok_rel.max())) if ok_rel.size else 0
-        self.cos, self.sin = rope_table(rotary_emb, lo, hi, head_dim, device)
-        self.n_pos = hi - lo + 1
-        self.n_rows = int(ir.rows.shape[0])
-        self.n_keys = int(ir.rel.shape[0])
+    @classmethod
+    def native(cls, parsed_positions, cursor_indices, editable_start: int, rotary_emb, head_dim: int, device):
+        """The rows of every edit built by ``ai_index_rows`` straight into the
+        pinned buffer; ``None`` when the list has no edit."""
+        from .meta import _prep_list
+
+        pl, keep = _prep_list(parsed_positions, 0)
+        types = np.ascontiguousarray(np.asarray([int(b.block_type or 0) for b in parsed_positions], dtype=np.int32))
+        if types.shape[0] != pl.n_blocks:
+            raise ValueError("block_type count does not match boundary_indices")
+        lib = _lib.lib()
+        n_rows, n_keys = ctypes.c_int32(0), ctypes.c_int64(0)
+        edits = np.zeros(max(1, pl.n_blocks), dtype=np.int64)
+        _lib.check(lib.ai_index_rows_sizes(ctypes.byref(pl), types.ctypes.data, ctypes.byref(n_rows),
+                                           ctypes.byref(n_keys), edits.ctypes.data), "ai_index_rows_sizes")
+        self = cls.__new__(cls)
+        self.n_rows, self.n_keys = int(n_rows.value), int(n_keys.value)
+        if self.n_rows == 0:
+            return None
+        self.edits = np.repeat(edits[:self.n_rows // 2], 2)
+        tg = np.asarray([cursor_indices[int(e)] for e in edits[:self.n_rows // 2]], dtype=np.int32).reshape(-1)
+        self._fill(tg, device, lambda rows, key_rows, key_ok: cls._native_fill(pl, types, editable_start, rows,
+                                                                                key_rows, key_ok))
+        self.cos, self.sin = rope_table(rotary_emb, self.lo, self.hi, head_dim, device)
+        self.n_pos = self.hi - self.lo + 1
+        del keep
+        return self
+
+    @staticmethod
+    def _native_fill(pl, types, editable_start, rows, key_rows, key_ok):
+        out = _lib.AiIndexRowsOut()
+        out.rows, out.key_rows, out.key_ok = rows.ctypes.data, key_rows.ctypes.data, key_ok.ctypes.data
+        _lib.check(_lib.lib().ai_index_rows(ctypes.byref(pl), types.ctypes.data, int(editable_start),
+                                            ctypes.byref(out)), "ai_index_rows")
+        return int(out.rel_lo), int(out.rel_hi)
+
+    def _fill(self, targets, device, writer):
         # int32 sections (16-byte aligned): rows [n_rows][4], targets, key rows; then the uint8 key flags
         n_rows4, n_keys4 = 4 * self.n_rows, (self.n_keys + 3) // 4 * 4
         o_tg = n_rows4
@@ -112,10 +142,10 @@ class _Prepared:
         o_ok = o_kr + n_keys4
         host = torch.empty(4 * o_ok + n_keys4, dtype=torch.uint8, pin_memory=True)
         h32 = host[:4 * o_ok].view(torch.int32).numpy()
-        h32[:n_rows4] = ir.rows.reshape(-1)
-        h32[o_tg:o_tg + self.n_rows] = ir.targets
-        h32[o_kr:o_kr + self.n_keys] = np.clip(ir.rel - lo, 0, self.n_pos - 1)
-        host[4 * o_ok:4 * o_ok + self.n_keys].numpy()[:] = ir.ok
+        h32[o_tg:o_tg + self.n_rows] = targets
+        rows = h32[:n_rows4].reshape(-1, 4)
+        self.lo, self.hi = writer(rows, h32[o_kr:o_kr + self.n_keys], host[4 * o_ok:4 * o_ok + self.n_keys].numpy())
+        self.host_rows = rows
         dev = host.to(device, non_blocking=True)
         d32 = dev[:4 * o_ok].view(torch.int32)
         self.rows = d32[:n_rows4]
@@ -207,13 +237,12 @@ def compute_index_losses_b200(
     if query.dtype not in (torch.bfloat16, torch.float32):
         raise TypeError(f"unsupported dtype {query.dtype}")
     scale = float(scaling) if scaling is not None else D ** -0.5
-    ir = index_rows(parsed_positions, cursor_indices, editable_start)
-    n_edits = ir.rows.shape[0] // 2
-    zero = (query.sum() + keys.sum()) * 0.0
-    if n_edits == 0:
+    prep = _Prepared.native(parsed_positions, cursor_indices, editable_start, rotary_emb, D, query.device)
+    if prep is None:
         # as the reference: keep q/k in the graph with a zero contribution
+        zero = (query.sum() + keys.sum()) * 0.0
         return (zero.to(query.dtype), zero.to(query.dtype)), {}
-    prep = _Prepared(ir, rotary_emb, D, query.device)
+    n_edits = prep.n_rows // 2
     q = query if query.stride(-1) == 1 else query.contiguous()
     k = keys if keys.stride(-1) == 1 else keys.contiguous()
     loss, logits = IndexLossFn.apply(q, k, prep, scale)
@@ -222,10 +251,10 @@ def compute_index_losses_b200(
     start_loss, end_loss = per_edit[0], per_edit[1]
     weights = {}
     if return_weights:
-        for r in range(ir.rows.shape[0]):
-            h, _, n, off = (int(x) for x in ir.rows[r])
+        for r in range(prep.n_rows):
+            h, _, n, off = (int(x) for x in prep.host_rows[r])
             w = logits[:, off:off + n].to(query.dtype).view(B, 1, 1, n)
-            ed = int(ir.edits[r])
+            ed = int(prep.edits[r])
             s_w, e_w = weights.get(ed, (None, None))
             weights[ed] = (w, e_w) if h == 0 else (s_w, w)
     return (start_loss.to(query.dtype), end_loss.to(query.dtype)), weights

@@ -113,6 +113,7 @@ class CompiledLayout:
     n_fwd_abs_items: int         # leading fwd_items whose block has abs keys
     n_kv_abs_items: int          # leading kv_items that a block with abs keys sees
     n_fwd_short_items: int       # fwd_items after the abs ones with at most fwd_tile / 2 rows
+    n_fwd_abs_short_items: int   # the first abs items, with at most fwd_tile / 2 rows
     kv_chunks: torch.Tensor      # [c, 4]: kv item, first / end query tile, partial slot (-1: whole item)
     kv_reduce: torch.Tensor      # [r, 4]: kv item, first slot, slots (items split into chunks)
     n_kv_partials: int           # partial slots of the split items
@@ -162,6 +163,7 @@ class CompiledLayout:
         L.n_chunk_cls = int(self.chunk_cls.shape[0])
         L.rot_classes = self.rot_classes.data_ptr() if self.rot_classes.numel() else None
         L.n_rot_classes = int(self.rot_classes.shape[0])
+        L.n_fwd_abs_short_items = int(self.n_fwd_abs_short_items)
         return L
 
 
@@ -280,6 +282,7 @@ def _compile(parsed_positions, batch, seq_len, head_dim, code, rotary_emb, devic
         blk_cls=view("blk_cls", (-1,)), chunk_cls=view("chunk_cls", (-1,)), rot_classes=view("rot_classes", (-1, 2)),
         kv_cost_max=int(t.kv_cost_max), kv_cost_total=int(t.kv_cost_total),
         n_fwd_abs_items=int(t.n_fwd_abs_items), n_kv_abs_items=int(t.n_kv_abs_items),
-        n_fwd_short_items=int(t.n_fwd_short_items), pairs_per_head=int(t.pairs_per_head),
+        n_fwd_short_items=int(t.n_fwd_short_items), n_fwd_abs_short_items=int(t.n_fwd_abs_short_items),
+        pairs_per_head=int(t.pairs_per_head),
         all_rows_owned=bool(t.all_rows_owned), host_blocks=blocks_host, _host_buffer=host,
     )

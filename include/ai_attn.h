@@ -155,6 +155,9 @@ typedef struct AiAttnLayout {
   int32_t n_chunk_cls;
   const int32_t* rot_classes; /* [n_rot_classes][2]: block and first key of a chunk with the class's rows */
   int32_t n_rot_classes;
+  int32_t n_fwd_abs_short_items; /* the first n_fwd_abs_short_items of the abs items have at most
+                                    fwd_tile / 2 rows (ABI 9); with the split below they pack four heads
+                                    of a GQA group per unit on the persistent kernels */
 } AiAttnLayout;
 
 typedef struct AiAttnFwdArgs {
@@ -322,6 +325,7 @@ typedef struct AiIndexBwdArgs {
 int ai_index_fwd(const AiIndexArgs* args, void* stream);
 int ai_index_bwd(const AiIndexBwdArgs* args, void* stream);
 
+
 /* ------------------------------------------------------------------------
  * Host-side layout builders (plain host memory, no GPU, no allocation by the
  * caller's device).
@@ -399,6 +403,7 @@ typedef struct AiPrepTables {
   int32_t kv_cost_total;
   int32_t n_fwd_abs_items;
   int32_t n_fwd_short_items;
+  int32_t n_fwd_abs_short_items;
   int32_t n_kv_abs_items;
   int32_t all_rows_owned;
   int64_t pairs_per_head;     /* finite (query, key) logits of one head over the batch */
@@ -410,6 +415,28 @@ int ai_attn_prep_sizes(const AiPrepList* lists, int32_t n_lists, const int32_t* 
                        int32_t seq_len, int32_t fwd_tile, int32_t kv_tile, AiPrepSizes* sizes);
 int ai_attn_prep(const AiPrepList* lists, int32_t n_lists, const int32_t* list_of_row, int32_t batch,
                  int32_t seq_len, int32_t fwd_tile, int32_t kv_tile, AiPrepTables* out);
+
+/* Host side of the index head (no GPU): the rows of compute_index_losses
+ * (attn_layers.py:56-104) for one concat()-ed list whose blocks carry
+ * block_type (AI_BLOCK_TYPE_*).  Per EXTEND block, in block order, edit
+ * marker ed = end - 1: the start row (head 0, query ed - 1, keys [0, ed),
+ * rel = key_pos - query_pos[ed - 1]) and the end row (head 1, query ed, keys
+ * [0, ed + 1), rel = key_pos - query_pos[ed]); a key may be attended when its
+ * attn_mask is set and key_pos >= editable_start, for the end row also when
+ * rel > 0.  ai_index_rows_sizes gives the counts and the edit markers (edits:
+ * NULL or [n_rows / 2]); ai_index_rows writes the AiIndexArgs tables: rows,
+ * key_rows (rel - rel_lo, clamped into the table) and key_ok, and the
+ * relative positions [rel_lo, rel_hi] (0 included) the rotary table must
+ * cover.  An EXTEND block of fewer than two rows is AI_ERR_LAYOUT. */
+typedef struct AiIndexRowsOut {
+  int32_t* rows;             /* [n_rows][4] */
+  int32_t* key_rows;         /* [n_keys] */
+  uint8_t* key_ok;           /* [n_keys] */
+  int64_t rel_lo, rel_hi;    /* out */
+} AiIndexRowsOut;
+int ai_index_rows_sizes(const AiPrepList* list, const int32_t* block_type, int32_t* n_rows, int64_t* n_keys,
+                        int64_t* edits);
+int ai_index_rows(const AiPrepList* list, const int32_t* block_type, int64_t editable_start, AiIndexRowsOut* out);
 
 /* Synchronises the stream, copies the device status word to *host_out and
  * resets it to AI_OK.  For tests and debugging; not needed on the hot path. */

@@ -79,17 +79,19 @@ def _tiles(fwd_tile: int, kv_tile: int, blocks: np.ndarray, row_cov: np.ndarray)
             q1 = min(q0 + fwd_tile, e)
             cost = (q1 - q0) * max(0, min(e, q1) - kv_lo)
             fwd.append((cost, bi, q0, q1))
-    # Items of blocks with abs keys first (they run on their own kernel), then
-    # the short items (at most half a tile of rows: the tensor-core kernels
-    # pack two heads of such an item into one tile), then the rest; longest
-    # first within each group.
+    # Items of blocks with abs keys first (short ones, then the others), then
+    # the other short items (at most half a tile of rows: the tensor-core
+    # kernels pack several heads of such an item into one tile), then the
+    # rest; longest first within each group.
     def group(t):
+        short = t[3] - t[2] <= fwd_tile // 2
         if int(blocks[t[1], 5]) & BLOCKF_ABS:
-            return 0
-        return 1 if t[3] - t[2] <= fwd_tile // 2 else 2
+            return 0 if short else 1
+        return 2 if short else 3
     fwd.sort(key=lambda t: (group(t), -t[0]))
-    n_abs = sum(1 for t in fwd if group(t) == 0)
-    n_short = sum(1 for t in fwd if group(t) == 1)
+    n_abs = sum(1 for t in fwd if group(t) <= 1)
+    n_abs_short = sum(1 for t in fwd if group(t) == 0)
+    n_short = sum(1 for t in fwd if group(t) == 2)
     # Key tiles: cost = query rows that see them; tiles that hold an abs key
     # of some block first (the abs pass adds those blocks' part), then
     # longest first.
@@ -107,7 +109,7 @@ def _tiles(fwd_tile: int, kv_tile: int, blocks: np.ndarray, row_cov: np.ndarray)
     n_kv_abs = sum(1 for t in kv if t[0])
     fwd_arr = np.asarray([(bi, q0, q1, 0) for _, bi, q0, q1 in fwd], dtype=np.int32).reshape(-1, 4)
     kv_arr = np.asarray([(row, j0, j1, 0) for _, _, row, j0, j1 in kv], dtype=np.int32).reshape(-1, 4)
-    return fwd_arr, kv_arr, n_abs, n_kv_abs, n_short
+    return fwd_arr, kv_arr, n_abs, n_kv_abs, n_short, n_abs_short
 
 
 def host_tables(parsed_positions, batch, seq_len, fwd_tile, kv_tile):
@@ -186,9 +188,10 @@ def host_tables(parsed_positions, batch, seq_len, fwd_tile, kv_tile):
 
     blocks_np = np.asarray(blocks, dtype=np.int32).reshape(-1, 8)
     row_cov_np = np.asarray(row_cov, dtype=np.int32)
-    fwd_items, kv_items, n_abs, n_kv_abs, n_short = _tiles(fwd_tile, kv_tile, blocks_np, row_cov_np)
+    fwd_items, kv_items, n_abs, n_kv_abs, n_short, n_abs_short = _tiles(fwd_tile, kv_tile, blocks_np, row_cov_np)
 
     return dict(blocks=blocks_np, row_blocks=np.asarray(row_blocks, dtype=np.int32), row_cov=row_cov_np,
                 key_info=key_info, q_pos=q_pos, k_own=k_own, fwd_items=fwd_items, kv_items=kv_items,
-                n_fwd_abs_items=n_abs, n_kv_abs_items=n_kv_abs, n_fwd_short_items=n_short, pairs_per_head=pairs,
+                n_fwd_abs_items=n_abs, n_kv_abs_items=n_kv_abs, n_fwd_short_items=n_short,
+                n_fwd_abs_short_items=n_abs_short, pairs_per_head=pairs,
                 all_rows_owned=bool(np.all(row_cov_np >= seq_len)), p_min=lo, n_pos=n_pos)

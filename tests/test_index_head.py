@@ -133,3 +133,45 @@ def test_bf16_index_losses_on_the_training_chain(cuda_device):
     fin = ok[None, :].repeat(B, 0)
     assert np.all(np.isneginf(got[~fin]))
     assert np.max(np.abs(got[fin] - want[fin])) <= 0.1
+
+
+@pytest.mark.parametrize("case", [0, 3, 9, "chain_e"])
+@pytest.mark.parametrize("es", [0, 3])
+def test_native_index_rows_match_python_rows(case, es):
+    """ai_index_rows (the rows compute_index_losses_b200 uploads) equals
+    index_rows, the Python statement of the reference's per-edit loop: row
+    table, edit markers, key flags and the keys' table rows (relative
+    position minus the lowest attended one)."""
+    import ctypes
+
+    from autoindexer_b200 import _lib
+    from autoindexer_b200.index_head import _Prepared, index_rows
+    from autoindexer_b200.meta import _prep_list
+
+    if case == "chain_e":
+        from autoindexer_b200 import positions_from_operations
+
+        with np.load(os.path.join(GOLDEN, "ops_cases.npz")) as z:
+            blocks = positions_from_operations(z["chain_e"])
+    else:
+        _, blocks, _, _, _ = _golden_case(case)
+    types = np.asarray([int(b.block_type or 0) for b in blocks], dtype=np.int32)
+    pl, keep = _prep_list(blocks, 0)
+    n_rows, n_keys = ctypes.c_int32(0), ctypes.c_int64(0)
+    edits = np.zeros(len(types), dtype=np.int64)
+    lib = _lib.lib()
+    assert lib.ai_index_rows_sizes(ctypes.byref(pl), types.ctypes.data, ctypes.byref(n_rows), ctypes.byref(n_keys),
+                                   edits.ctypes.data) == 0
+    cursor = {int(e): (0, 1) for e in edits[:n_rows.value // 2]}
+    want = index_rows(blocks, cursor, editable_start=es)
+    assert n_rows.value == want.rows.shape[0] and n_keys.value == want.rel.shape[0]
+    rows = np.zeros((n_rows.value, 4), dtype=np.int32)
+    key_rows = np.zeros(n_keys.value, dtype=np.int32)
+    key_ok = np.zeros(n_keys.value, dtype=np.uint8)
+    lo, hi = _Prepared._native_fill(pl, types, es, rows, key_rows, key_ok)
+    assert np.array_equal(rows, want.rows)
+    assert np.array_equal(np.repeat(edits[:n_rows.value // 2], 2), want.edits)
+    assert np.array_equal(key_ok, want.ok)
+    ok = want.ok.astype(bool)
+    assert lo == min(0, int(want.rel[ok].min())) and hi == max(0, int(want.rel[ok].max()))
+    assert np.array_equal(key_rows[ok], (want.rel[ok] - lo).astype(np.int32))

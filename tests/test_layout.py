@@ -233,7 +233,8 @@ def test_native_tables_match_numpy_restatement(which):
         want = LN.host_tables(lay, B, T, c.fwd_tile, c.kv_tile)
         for name in ("blocks", "row_blocks", "row_cov", "key_info", "q_pos", "k_own", "fwd_items", "kv_items"):
             assert np.array_equal(getattr(c, name).numpy(), np.asarray(want[name]).reshape(getattr(c, name).shape)), name
-        for name in ("n_fwd_abs_items", "n_kv_abs_items", "n_fwd_short_items", "pairs_per_head", "all_rows_owned",
+        for name in ("n_fwd_abs_items", "n_kv_abs_items", "n_fwd_short_items", "n_fwd_abs_short_items",
+                     "pairs_per_head", "all_rows_owned",
                      "p_min", "n_pos"):
             assert getattr(c, name) == want[name], name
 

@@ -254,3 +254,55 @@ def test_bf16_rotation_classes_match_shared_memory_rotation(cuda_device):
     for name, a_, b_ in zip(("out", "lse", "dq", "dv"), *(r[:3] + r[4:] for r in res)):
         assert torch.equal(a_, b_), name
     assert rel_l2(res[0][3].double().cpu().numpy(), res[1][3].double().cpu().numpy()) <= 2e-3
+
+
+def test_bf16_abs_split_matches_whole_abs_items(cuda_device):
+    """The abs split: the persistent kernels run the abs blocks' key tiles
+    without abs keys and leave partial rows (forward: O / l and the log-sum;
+    dQ: the rotated accumulator) that the one-head kernels finish with the
+    tiles holding abs keys.  Without room for the partials in the
+    workspaces the one-head kernels run those items whole.  Both agree to
+    the rounding of the merge; the split one is also checked against the
+    oracle by the +E parity tests."""
+    import ctypes
+
+    from autoindexer_b200 import _lib
+    from autoindexer_b200.attention import _fwd_args, _t4
+
+    lay, q, k, v, dout, mod, _ = _chain_e(8, 2, 128, 24)
+    tq, tk, tv, tdo = (torch.as_tensor(x).to(cuda_device, torch.bfloat16) for x in (q, k, v, dout))
+    B, Hq, T, D = tq.shape
+    layout = compile_layout(lay, B, T, D, torch.bfloat16, mod.to(cuda_device), cuda_device)
+    n_abs = layout.n_fwd_abs_items
+    assert n_abs > 0
+    fwd_part = (n_abs * Hq * 128 * (D + 1) * 4 + 255) // 256 * 256
+    dq_part = (n_abs * Hq * 128 * D * 4 + 255) // 256 * 256
+    lib = _lib.lib()
+    stream = ctypes.c_void_p(torch.cuda.current_stream(cuda_device).cuda_stream)
+    res = []
+    for split in (True, False):
+        out = torch.empty((B, T, Hq, D), dtype=torch.bfloat16, device=cuda_device)
+        lse = torch.empty((B, Hq, T), dtype=torch.float32, device=cuda_device)
+        a = _fwd_args(tq, tk, tv, out.permute(0, 2, 1, 3), lse, layout, D ** -0.5)
+        nbytes = ctypes.c_size_t(0)
+        assert lib.ai_attn_fwd_workspace(ctypes.byref(a), ctypes.byref(nbytes)) == 0
+        fws = torch.empty(nbytes.value, dtype=torch.uint8, device=cuda_device)
+        a.workspace, a.workspace_bytes = fws.data_ptr(), nbytes.value - (0 if split else fwd_part)
+        assert lib.ai_attn_fwd(ctypes.byref(a), stream) == 0
+        grads = [torch.empty_like(x) for x in (tq, tk, tv)]
+        b = _lib.AiAttnBwdArgs()
+        b.fwd = a
+        b.fwd_rotated = 1
+        b.dout = _t4(tdo.permute(0, 2, 1, 3))
+        b.dq, b.dk, b.dv = (_t4(x) for x in grads)
+        assert lib.ai_attn_bwd_workspace(ctypes.byref(b), ctypes.byref(nbytes)) == 0
+        ws = torch.empty(nbytes.value, dtype=torch.uint8, device=cuda_device)
+        b.workspace, b.workspace_bytes = ws.data_ptr(), nbytes.value - (0 if split else dq_part)
+        assert lib.ai_attn_bwd(ctypes.byref(b), stream) == 0
+        torch.cuda.synchronize(cuda_device)
+        assert read_status(cuda_device) == 0
+        res.append([x.double().cpu().numpy() for x in (out, lse, *grads)])
+    for name, a_, b_ in zip(("out", "lse", "dq", "dk", "dv"), *res):
+        fin = np.isfinite(a_) & np.isfinite(b_)
+        assert np.array_equal(np.isfinite(a_), np.isfinite(b_)), name
+        assert rel_l2(a_[fin], b_[fin]) <= 5e-3, (name, rel_l2(a_[fin], b_[fin]))
