@@ -33,6 +33,7 @@ DTYPE_BF16, DTYPE_F16, DTYPE_F32 = 0, 1, 2
 # AiProfKind, in order.
 PROF_KINDS = ("prerot", "fwd", "fwd_fill", "delta", "dq", "dkdv", "bwd_fill", "simt", "decode")
 ABI_VERSION = 9
+BWD_DQ, BWD_DKDV = 1, 2
 
 # Every function include/ai_attn.h declares.
 EXPORTED_SYMBOLS = (
@@ -145,6 +146,7 @@ class AiAttnBwdArgs(ctypes.Structure):
         ("workspace", ctypes.c_void_p),
         ("workspace_bytes", ctypes.c_size_t),
         ("fwd_rotated", ctypes.c_int32),
+        ("parts", ctypes.c_int32),
     ]
 
 

@@ -131,14 +131,17 @@ def attn_fwd(q: Tensor, k: Tensor, v: Tensor, layout: CompiledLayout, scale: flo
 
 
 def attn_bwd(q, k, v, out, lse, dout, layout: CompiledLayout, scale: float, rotated_copies: bool = True,
-             fwd_workspace: Optional[Tensor] = None, grads: Optional[Tuple[Tensor, Tensor, Tensor]] = None):
+             fwd_workspace: Optional[Tensor] = None, grads: Optional[Tuple[Tensor, Tensor, Tensor]] = None,
+             after_dq=None):
     """Launches ``ai_attn_bwd``: returns ``dq, dk, dv`` shaped like ``q, k, v``
     (``rotated_copies`` as for ``attn_fwd``; without it the workspace holds
     only the row sums of dO.O).  ``fwd_workspace``: the scratch that
     ``attn_fwd(..., keep_workspace=True)`` returned for these q, k and layout;
     its rotated Q/K copies are reused (``fwd_rotated`` in the C ABI).
     ``grads``: ``(dq, dk, dv)`` views (shaped like q, k, v, d contiguous) the
-    kernels write into instead of new tensors."""
+    kernels write into instead of new tensors.  ``after_dq``: called between
+    the dQ launches and the dK/dV launches (two ``ai_attn_bwd`` calls,
+    ``parts`` = dQ then dK/dV), when dQ is complete in stream order."""
     if grads is not None:
         dq, dk, dv = grads
         for g, x in ((dq, q), (dk, k), (dv, v)):
@@ -172,7 +175,15 @@ def attn_bwd(q, k, v, out, lse, dout, layout: CompiledLayout, scale: float, rota
     a.workspace = ws.data_ptr()
     a.workspace_bytes = ws.numel()
     stream = torch.cuda.current_stream(q.device).cuda_stream
-    _lib.check(lib.ai_attn_bwd(ctypes.byref(a), ctypes.c_void_p(stream)), "ai_attn_bwd")
+    if after_dq is None:
+        _lib.check(lib.ai_attn_bwd(ctypes.byref(a), ctypes.c_void_p(stream)), "ai_attn_bwd")
+    else:
+        a.parts = _lib.BWD_DQ
+        _lib.check(lib.ai_attn_bwd(ctypes.byref(a), ctypes.c_void_p(stream)), "ai_attn_bwd")
+        after_dq()
+        a.parts = _lib.BWD_DKDV
+        _lib.check(lib.ai_attn_bwd(ctypes.byref(a), ctypes.c_void_p(torch.cuda.current_stream(q.device).cuda_stream)),
+                   "ai_attn_bwd")
     del dout_keep, ws
     return dq, dk, dv
 

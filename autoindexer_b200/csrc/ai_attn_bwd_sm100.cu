@@ -2095,9 +2095,10 @@ size_t sm100_dq_abs_part_bytes(const AiAttnFwdArgs& f) {
 }
 
 int sm100_bwd(const AiAttnBwdArgs& a, float* delta, void* rot, bool rot_ready, float* partials, float* dq_part,
-              cudaStream_t st, cudaError_t* cuda_err) {
+              int parts, cudaStream_t st, cudaError_t* cuda_err) {
   using namespace sm100bwd;
   const AiAttnFwdArgs& f = a.fwd;
+  const bool do_dq = (parts & AI_BWD_DQ) != 0, do_kv = (parts & AI_BWD_DKDV) != 0;
   if (!strides_ok(f.q) || !strides_ok(f.k) || !strides_ok(f.v) || !strides_ok(a.dout) || !strides_ok(a.dq) ||
       !strides_ok(a.dk) || !strides_ok(a.dv))
     return AI_ERR_STRIDE;
@@ -2106,12 +2107,14 @@ int sm100_bwd(const AiAttnBwdArgs& a, float* delta, void* rot, bool rot_ready, f
   AiTensor4 qr{}, kr{}, kc{};
   const bool pre = rot != nullptr;
   if (pre && !sm100_rotated_views(f, rot, &qr, &kr, &kc)) return AI_ERR_ALIGN;
-  cudaError_t e;
-  {
-    ProfScope ps(AI_PROF_DELTA, st);
-    e = bwd_delta(a, delta, st);
+  cudaError_t e = cudaSuccess;
+  if (do_dq) {  // (a dK/dV-only call reads what the dQ call left in the workspace)
+    {
+      ProfScope ps(AI_PROF_DELTA, st);
+      e = bwd_delta(a, delta, st);
+    }
+    if (e == cudaSuccess && pre && !rot_ready) e = prerot(f, rot, st);
   }
-  if (e == cudaSuccess && pre && !rot_ready) e = prerot(f, rot, st);
   // The abs split (with the rotated copies and room for dq_part): the
   // persistent dQ kernel also runs the abs-block items' key tiles that hold
   // no abs key and leaves their dQrot in dq_part; the one-head kernel, later
@@ -2120,7 +2123,7 @@ int sm100_bwd(const AiAttnBwdArgs& a, float* delta, void* rot, bool rot_ready, f
   const bool dq_split = pre && dq_part && Gq % 2 == 0 && f.layout.n_fwd_abs_items > 0;
   CUtensorMap dq_tk, dq_tv, dq_tkc;  // maps of the deferred one-head dQ launch
   bool dq_deferred = false;
-  if (e == cudaSuccess && f.layout.n_fwd_items > 0) {
+  if (e == cudaSuccess && do_dq && f.layout.n_fwd_items > 0) {
     CUtensorMap tk, tv, tqr, tdo, tkr;
     if (!sm100_make_map(&tk, f.k, f.batch, f.num_kv_heads, f.seq_len, dq::BN) ||
         !sm100_make_map(&tv, f.v, f.batch, f.num_kv_heads, f.seq_len, dq::BN) ||
@@ -2198,7 +2201,7 @@ int sm100_bwd(const AiAttnBwdArgs& a, float* delta, void* rot, bool rot_ready, f
       e = cudaGetLastError();
     }
   };
-  if (e == cudaSuccess && f.layout.n_kv_items > 0) {
+  if (e == cudaSuccess && do_kv && f.layout.n_kv_items > 0) {
     CUtensorMap tk, tv, tq, tdo, tqr, tkr;
     if (!sm100_make_map(&tk, f.k, f.batch, f.num_kv_heads, f.seq_len, kv::BN) ||
         !sm100_make_map(&tv, f.v, f.batch, f.num_kv_heads, f.seq_len, kv::BN) ||
@@ -2266,8 +2269,8 @@ int sm100_bwd(const AiAttnBwdArgs& a, float* delta, void* rot, bool rot_ready, f
       }
     }
   }
-  launch_dq_deferred();  // (no key tiles at all: not launched above)
-  if (e == cudaSuccess && !f.layout.all_rows_owned) {
+  launch_dq_deferred();  // (a dQ-only call, or no key tiles: not launched above)
+  if (e == cudaSuccess && do_dq && !f.layout.all_rows_owned) {
     ProfScope ps(AI_PROF_BWD_FILL, st);
     e = bwd_fill(a, st);
   }

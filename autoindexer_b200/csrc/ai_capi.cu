@@ -141,7 +141,9 @@ int ai_attn_bwd(const AiAttnBwdArgs* a, void* stream) {
   if (!tensor_ok(a->dout) || !tensor_ok(a->dq) || !tensor_ok(a->dk) || !tensor_ok(a->dv)) return AI_ERR_NULL;
   if (!a->workspace || a->workspace_bytes < delta_bytes(a->fwd)) return AI_ERR_WORKSPACE;
   if ((uintptr_t)a->workspace % 256) return AI_ERR_ALIGN;
+  if (a->parts < 0 || a->parts > (AI_BWD_DQ | AI_BWD_DKDV)) return AI_ERR_LAYOUT;
   if (!device_is_sm100()) return AI_ERR_NO_DEVICE;
+  const int parts = a->parts ? a->parts : (AI_BWD_DQ | AI_BWD_DKDV);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   float* delta = static_cast<float*>(a->workspace);
   if (ai::sm100_bwd_supported(a->fwd.dtype, a->fwd.head_dim)) {
@@ -159,10 +161,13 @@ int ai_attn_bwd(const AiAttnBwdArgs* a, void* stream) {
     };
     float* partials = take(ai::sm100_kv_partial_bytes(a->fwd));
     float* dq_part = take(ai::sm100_dq_abs_part_bytes(a->fwd));
-    if (fwd_copies(*a)) return ai::sm100_bwd(*a, delta, a->fwd.workspace, true, partials, dq_part, st, nullptr);
+    if (fwd_copies(*a))
+      return ai::sm100_bwd(*a, delta, a->fwd.workspace, true, partials, dq_part, parts, st, nullptr);
+    // (a dK/dV-only call finds the copies its dQ call rotated)
     void* rot = take(ai::prerot_bytes(a->fwd, nullptr));
-    return ai::sm100_bwd(*a, delta, rot, false, partials, dq_part, st, nullptr);
+    return ai::sm100_bwd(*a, delta, rot, !(parts & AI_BWD_DQ), partials, dq_part, parts, st, nullptr);
   }
+  if (!(parts & AI_BWD_DQ)) return AI_OK;  // the fp32 / fp16 path did everything in the dQ call
   ai::ProfScope ps(AI_PROF_SIMT, st);
   return launch_status(ai::simt_bwd(*a, delta, st));
 }

@@ -52,8 +52,9 @@ size_t sm100_kv_partial_bytes(const AiAttnFwdArgs& f);
 // `dq_part`: scratch of sm100_dq_abs_part_bytes for the abs split of dQ, or
 // nullptr (the one-head kernel then runs the abs-block items whole).
 size_t sm100_dq_abs_part_bytes(const AiAttnFwdArgs& f);
+// `parts`: AI_BWD_DQ and / or AI_BWD_DKDV (see AiAttnBwdArgs.parts).
 int sm100_bwd(const AiAttnBwdArgs& a, float* delta, void* rot, bool rot_ready, float* partials, float* dq_part,
-              cudaStream_t st, cudaError_t* cuda_err);
+              int parts, cudaStream_t st, cudaError_t* cuda_err);
 // TMA map over a (B, H, T, 128) bf16 tensor, box 64 x box_rows, 128-byte swizzle.
 bool sm100_make_map(CUtensorMap* map, const AiTensor4& t, int B, int H, int T, int box_rows);
 

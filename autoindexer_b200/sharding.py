@@ -34,7 +34,9 @@ from .meta import CompiledLayout
 
 # local_fwd(q, k, v, layout, scale, out_bhtd) -> (out (B, T, h, D), state); out_bhtd, when not None, is
 #   the (B, h, T, D) view the result must be written into
-# local_bwd(state, dout (B, T, h, D), grads) -> (dq, dk, dv); grads, when not None, are the views to fill
+# local_bwd(state, dout (B, T, h, D), grads, after_dq=None) -> (dq, dk, dv); grads, when not None, are the
+#   views to fill; after_dq, when not None, is called once dQ is complete in stream order (before dK / dV
+#   are: a local backward that computes all three at once calls it at the end)
 LocalFwd = Callable[..., Tuple[Tensor, object]]
 LocalBwd = Callable[..., Tuple[Tensor, Tensor, Tensor]]
 
@@ -50,12 +52,14 @@ def kernel_fwd(q: Tensor, k: Tensor, v: Tensor, layout: CompiledLayout, scale: f
     return out, (q, k, v, out, lse, ws, layout, scale)
 
 
-def kernel_bwd(state, dout: Tensor, grads=None):
-    """The library's backward for one rank's heads (``ai_attn_bwd``)."""
+def kernel_bwd(state, dout: Tensor, grads=None, after_dq=None):
+    """The library's backward for one rank's heads (``ai_attn_bwd``; with
+    ``after_dq`` as two calls, dQ then dK / dV)."""
     from .attention import attn_bwd
 
     q, k, v, out, lse, ws, layout, scale = state
-    return attn_bwd(q, k, v, out, lse, dout.contiguous(), layout, scale, fwd_workspace=ws, grads=grads)
+    return attn_bwd(q, k, v, out, lse, dout.contiguous(), layout, scale, fwd_workspace=ws, grads=grads,
+                    after_dq=after_dq)
 
 
 def head_range(num_heads: int, rank: int, world: int) -> Tuple[int, int]:
@@ -72,24 +76,25 @@ def _world(group) -> Tuple[int, int]:
     return dist.get_world_size(group), dist.get_rank(group)
 
 
-def gather_heads_inplace(full: Tensor, group: Optional[dist.ProcessGroup]) -> None:
+def gather_heads_inplace(full: Tensor, group: Optional[dist.ProcessGroup], async_op: bool = False):
     """All-gather along dim 1 of the head-major buffer ``full`` ``(B, H, T,
     D)``, whose own head slice this rank has written: afterwards every slice
     holds its rank's heads.  With ``B == 1`` the slices are contiguous and
-    NCCL gathers in place; otherwise through a staging buffer."""
+    NCCL gathers in place (with ``async_op`` the work handle is returned and
+    the caller waits on it); otherwise through a staging buffer, at once."""
     world, rank = _world(group)
     if world == 1:
-        return
+        return None
     Bf, H = full.shape[0], full.shape[1]
     h0, h1 = head_range(H, rank, world)
     if Bf == 1 and full.is_contiguous():
         flat = full.view(-1)
         n = flat.numel() // world
-        dist.all_gather_into_tensor(flat, flat[rank * n:(rank + 1) * n], group=group)
-        return
+        return dist.all_gather_into_tensor(flat, flat[rank * n:(rank + 1) * n], group=group, async_op=async_op)
     stage = torch.empty((world,) + tuple(full[:, h0:h1].shape), dtype=full.dtype, device=full.device)
     dist.all_gather_into_tensor(stage, full[:, h0:h1].contiguous(), group=group)
     full.copy_(stage.permute(1, 0, 2, 3, 4).reshape(full.shape))
+    return None
 
 
 def gather_heads(x: Tensor, axis: int, group: Optional[dist.ProcessGroup]) -> Tensor:
@@ -138,6 +143,29 @@ class GatherBuffers:
             e1.record(stream)
             self.events.append((e0, e1))
 
+    def gather_async(self, full: Tensor):
+        """Starts the gather of ``full`` (returns what ``finish`` takes): in
+        place on NCCL's stream when the layout allows it, at once otherwise."""
+        work = gather_heads_inplace(full, self.group, async_op=True)
+        if work is None:
+            return None
+        return work
+
+    def finish(self, work) -> None:
+        """Makes the current stream wait for a gather started by
+        ``gather_async``; the time it waits counts as gather time."""
+        if work is None:
+            return
+        stream = torch.cuda.current_stream() if torch.cuda.is_available() and self.out.is_cuda else None
+        if self.timing and stream is not None:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            work.wait()
+            e1.record(stream)
+            self.events.append((e0, e1))
+        else:
+            work.wait()
+
     def gather_ms(self) -> float:
         """Milliseconds spent in the gathers recorded so far (synchronises),
         then forgets them."""
@@ -159,12 +187,23 @@ def sharded_forward(q_l: Tensor, k_l: Tensor, v_l: Tensor, layout: CompiledLayou
 
 def sharded_backward(dout_l: Tensor, bufs: GatherBuffers, local_bwd: LocalBwd = kernel_bwd):
     """This rank's dQ, dK, dV written into its slices of the buffers, then
-    gathered: returns the full ``(dq, dk, dv)`` on every rank."""
+    gathered: returns the full ``(dq, dk, dv)`` on every rank.  The dQ
+    gather is issued as soon as dQ is complete (``after_dq``) and runs on
+    NCCL's stream while the dK / dV kernels run; the caller's stream waits
+    for it before returning."""
     q0, q1 = bufs.q_heads
     k0, k1 = bufs.kv_heads
-    local_bwd(bufs.state, dout_l, (bufs.dq[:, q0:q1], bufs.dk[:, k0:k1], bufs.dv[:, k0:k1]))
+    pending = []
+
+    def after_dq():
+        if bufs.world > 1:
+            pending.append(bufs.gather_async(bufs.dq))
+
+    local_bwd(bufs.state, dout_l, (bufs.dq[:, q0:q1], bufs.dk[:, k0:k1], bufs.dv[:, k0:k1]), after_dq=after_dq)
     bufs.state = None
-    bufs.gather(bufs.dq, bufs.dk, bufs.dv)
+    bufs.gather(bufs.dk, bufs.dv)
+    for w in pending:
+        bufs.finish(w)
     return bufs.dq, bufs.dk, bufs.dv
 
 

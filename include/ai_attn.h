@@ -195,7 +195,17 @@ typedef struct AiAttnBwdArgs {
                              ai_attn_fwd_workspace); the backward reads them instead of rotating
                              again, and its own workspace needs only the B*Hq*T floats.
                              0: fwd.workspace is ignored. */
+  int32_t parts;          /* ABI 9: 0 (or AI_BWD_DQ | AI_BWD_DKDV) runs the whole backward.
+                             AI_BWD_DQ: the row sums of dO.O, the rotated copies when needed, dQ and
+                             the rows no block owns; AI_BWD_DKDV: dK and dV only, reading what a
+                             preceding AI_BWD_DQ call with the same arguments and workspace left
+                             there (stream order).  The two calls let a caller start using dQ (an
+                             all-gather, say) while dK and dV are computed.  The fp32 / fp16 path
+                             computes every gradient in the AI_BWD_DQ call. */
 } AiAttnBwdArgs;
+
+#define AI_BWD_DQ 1
+#define AI_BWD_DKDV 2
 
 /* ABI version this library was built with (AI_ATTN_ABI_VERSION). */
 int ai_attn_abi_version(void);

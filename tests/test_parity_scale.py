@@ -216,8 +216,10 @@ def test_bf16_split_key_tiles_match_whole_key_tiles(cuda_device):
         nbytes = ctypes.c_size_t(0)
         assert lib.ai_attn_bwd_workspace(ctypes.byref(a), ctypes.byref(nbytes)) == 0
         delta_only = (B * Hq * T * 4 + 255) // 256 * 256
-        assert nbytes.value > delta_only  # the partials are asked for
-        ws = torch.empty(nbytes.value if split else delta_only, dtype=torch.uint8, device=cuda_device)
+        # the dQ partials of the abs split come after the dK/dV partials: left out of both runs
+        dq_part = (layout.n_fwd_abs_items * Hq * 128 * D * 4 + 255) // 256 * 256
+        assert nbytes.value > delta_only + dq_part  # the dK/dV partials are asked for
+        ws = torch.empty(nbytes.value - dq_part if split else delta_only, dtype=torch.uint8, device=cuda_device)
         a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
         assert lib.ai_attn_bwd(ctypes.byref(a), stream) == 0
         torch.cuda.synchronize(cuda_device)
@@ -306,3 +308,22 @@ def test_bf16_abs_split_matches_whole_abs_items(cuda_device):
         fin = np.isfinite(a_) & np.isfinite(b_)
         assert np.array_equal(np.isfinite(a_), np.isfinite(b_)), name
         assert rel_l2(a_[fin], b_[fin]) <= 5e-3, (name, rel_l2(a_[fin], b_[fin]))
+
+
+def test_bf16_backward_in_two_parts_equals_one_call(cuda_device):
+    """ai_attn_bwd with parts = dQ, then parts = dK/dV on the same
+    arguments and workspace (what the sharded backward does to start the dQ
+    all-gather early) gives the one-call gradients bit for bit, on the +E
+    chain (abs split, split key tiles, rotation classes)."""
+    lay, q, k, v, dout, mod, _ = _chain_e(8, 2, 128, 25)
+    tq, tk, tv, tdo = (torch.as_tensor(x).to(cuda_device, torch.bfloat16) for x in (q, k, v, dout))
+    B, Hq, T, D = tq.shape
+    layout = compile_layout(lay, B, T, D, torch.bfloat16, mod.to(cuda_device), cuda_device)
+    out, lse, fws = attn_fwd(tq, tk, tv, layout, D ** -0.5, keep_workspace=True)
+    one = attn_bwd(tq, tk, tv, out, lse, tdo, layout, D ** -0.5, fwd_workspace=fws)
+    seen = []
+    two = attn_bwd(tq, tk, tv, out, lse, tdo, layout, D ** -0.5, fwd_workspace=fws, after_dq=lambda: seen.append(1))
+    torch.cuda.synchronize(cuda_device)
+    assert seen == [1] and read_status(cuda_device) == 0
+    for name, a_, b_ in zip(("dq", "dk", "dv"), one, two):
+        assert torch.equal(a_, b_), name

@@ -57,14 +57,20 @@ def _oracle_local(rope):
             out_bhtd.copy_(out.permute(0, 2, 1, 3))
         return out, (q, k, v, rows, scale)
 
-    def bwd(state, dout, grads=None):
+    def bwd(state, dout, grads=None, after_dq=None):
+        # dQ is written first and handed over (its gather starts) before dK and dV
         q, k, v, rows, scale = state
         res = O.attn_backward(q.detach().numpy(), k.detach().numpy(), v.detach().numpy(), dout.numpy(), rows,
                               rope, scale)
         res = tuple(torch.from_numpy(x) for x in res)
         if grads is not None:
-            for g, x in zip(grads, res):
+            grads[0].copy_(res[0])
+            if after_dq is not None:
+                after_dq()
+            for g, x in zip(grads[1:], res[1:]):
                 g.copy_(x)
+        elif after_dq is not None:
+            after_dq()
         return res
 
     return fwd, bwd
