@@ -446,6 +446,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_q,
                 const __grid_constant__ CUtensorMap tm_do, const __grid_constant__ CUtensorMap tm_qp,
                 const __grid_constant__ CUtensorMap tm_dop, const __grid_constant__ CUtensorMap tm_kc,
+                const __grid_constant__ CUtensorMap tm_qr, const __grid_constant__ CUtensorMap tm_qrp,
                 const int prerot, const int abs_only) {
   using namespace kv;
   extern __shared__ uint8_t smem_raw[];
@@ -573,20 +574,34 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int q1 = min(q0 + BQ, blk.e);
       for (int g = 0; g < G; g += P) {
         const int h = hk * G + g;
+        // Raw query rows go to QA (abs blocks) or straight to QR to be rotated
+        // there; with the rotated copies the rotated rows come by TMA as well.
         const uint32_t qdst = has_abs ? QA : QR;
         if (tid == 0) {
           ptx::fence_proxy_async_smem();
-          ptx::mbar_arrive_expect_tx(bar_q, 4 * 8192);
+          ptx::mbar_arrive_expect_tx(bar_q, (prerot && has_abs ? 6u : 4u) * 8192u);
           if (P == 1) {
-            ptx::tma_load_4d(sbase + qdst, &tm_q, bar_q, 0, q0, h, b);
-            ptx::tma_load_4d(sbase + qdst + 8192, &tm_q, bar_q, 64, q0, h, b);
+            if (!prerot || has_abs) {
+              ptx::tma_load_4d(sbase + qdst, &tm_q, bar_q, 0, q0, h, b);
+              ptx::tma_load_4d(sbase + qdst + 8192, &tm_q, bar_q, 64, q0, h, b);
+            }
+            if (prerot) {
+              ptx::tma_load_4d(sbase + QR, &tm_qr, bar_q, 0, q0, h, b);
+              ptx::tma_load_4d(sbase + QR + 8192, &tm_qr, bar_q, 64, q0, h, b);
+            }
             ptx::tma_load_4d(sbase + DO, &tm_do, bar_q, 0, q0, h, b);
             ptx::tma_load_4d(sbase + DO + 8192, &tm_do, bar_q, 64, q0, h, b);
           } else {
             for (int x = 0; x < P; ++x) {
               const uint32_t ro = (uint32_t)(x * sr) * 128u;
-              ptx::tma_load_4d(sbase + qdst + ro, &tm_qp, bar_q, 0, q0, hk * G + x, b);
-              ptx::tma_load_4d(sbase + qdst + 8192 + ro, &tm_qp, bar_q, 64, q0, hk * G + x, b);
+              if (!prerot || has_abs) {
+                ptx::tma_load_4d(sbase + qdst + ro, &tm_qp, bar_q, 0, q0, hk * G + x, b);
+                ptx::tma_load_4d(sbase + qdst + 8192 + ro, &tm_qp, bar_q, 64, q0, hk * G + x, b);
+              }
+              if (prerot) {
+                ptx::tma_load_4d(sbase + QR + ro, &tm_qrp, bar_q, 0, q0, hk * G + x, b);
+                ptx::tma_load_4d(sbase + QR + 8192 + ro, &tm_qrp, bar_q, 64, q0, hk * G + x, b);
+              }
               ptx::tma_load_4d(sbase + DO + ro, &tm_dop, bar_q, 0, q0, hk * G + x, b);
               ptx::tma_load_4d(sbase + DO + 8192 + ro, &tm_dop, bar_q, 64, q0, hk * G + x, b);
             }
@@ -611,7 +626,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (*s_abort) { aborted = true; break; }
 
         // Rotate the query rows: thread -> (row tid % 64, chunk pairs 4*(tid/64) .. +3).
-        {
+        if (!prerot) {
           const int r = tid & 63, cg = tid >> 6;
           const int p = s_qpos[r];
           const float* cs = L.rope_cos + (int64_t)p * (D / 2);
@@ -906,31 +921,20 @@ __device__ __forceinline__ int unit_head(const Unit& w, int t, int r) {
 }
 __device__ __forceinline__ int unit_row(const Unit& w, int r) { return w.q0 + (w.pk == 2 ? (r & 63) : r); }
 
+template <bool kAbs>
 __device__ __forceinline__ Unit load_unit(const AiAttnFwdArgs& f, int u, int prerot, const UnitPlan& up) {
   const AiAttnLayout& L = f.layout;
   const int hpairs = f.num_q_heads / 2, hquads = f.num_q_heads / 4, G = f.num_q_heads / f.num_kv_heads;
   int it;
   Unit w;
-  w.abs = u < up.n_abs_units;
-  if (w.abs) {
-    if (u < up.n_abs_pack_units) {
-      it = u / hquads;
-      w.h0 = 4 * (u % hquads);
-      w.pk = 2;
-    } else {
-      const int v = u - up.n_abs_pack_units;
-      it = up.n_abs_pack_units / hquads + v / hpairs;
-      w.h0 = 2 * (v % hpairs);
-      w.pk = 1;
-    }
-  } else if (u - up.n_abs_units < up.n_pack_units) {
-    const int v = u - up.n_abs_units;
-    it = L.n_fwd_abs_items + v / hquads;
-    w.h0 = 4 * (v % hquads);
+  w.abs = kAbs;
+  if (u < up.n_pack_units) {
+    it = up.item_base + u / hquads;
+    w.h0 = 4 * (u % hquads);
     w.pk = 2;
   } else {
-    const int v = u - up.n_abs_units - up.n_pack_units;
-    it = L.n_fwd_abs_items + (up.n_pack_units > 0 ? L.n_fwd_short_items : 0) + v / hpairs;
+    const int v = u - up.n_pack_units;
+    it = up.item_base + up.n_pack_items + v / hpairs;
     w.h0 = 2 * (v % hpairs);
     w.pk = 1;
   }
@@ -944,7 +948,7 @@ __device__ __forceinline__ Unit load_unit(const AiAttnFwdArgs& f, int u, int pre
   w.kv_hi = min(w.blk.e, w.q1);
   w.n = w.kv_hi > w.kv_lo ? (w.kv_hi - w.kv_lo + BN - 1) / BN : 0;
   w.ja = w.jb = 0;
-  if (w.abs) {
+  if (kAbs) {
     abs_tiles(w.blk, w.kv_lo, w.kv_hi, BN, w.ja, w.jb);
     w.n -= w.jb - w.ja;
   }
@@ -975,6 +979,9 @@ __device__ __forceinline__ Unit load_unit(const AiAttnFwdArgs& f, int u, int pre
 // (Q_EMPTY); a unit's first dQ MMA waits until the previous unit's dQ_t has
 // been read (DQ_FREE).
 // ===========================================================================
+// kAbs: the units are the abs-block items' key tiles without abs keys
+// (their dQrot into part_dq); otherwise the other items, whole.
+template <bool kAbs>
 __global__ void __launch_bounds__(dqw::kThreads, 1)
     dq_pers_kernel(const AiAttnBwdArgs a, const float* __restrict__ delta, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_qr,
@@ -1044,7 +1051,7 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
     const float2 sl2x2 = make_float2(sl2, sl2), scalex2 = make_float2(scale, scale);
     int g = 0, k = 0, ko = 0;  // ko: units with key tiles so far (DQ_DONE phases)
     for (int u = snake_unit(k); u < n_units && !*s_abort; u = snake_unit(++k)) {
-      const Unit w = load_unit(f, u, prerot, up);
+      const Unit w = load_unit<kAbs>(f, u, prerot, up);
       const int i = unit_row(w, r), h = unit_head(w, t, r), b = w.blk.row, q1 = w.q1;
       int qrow = 0;
       float lse2 = 0.f, dl = 0.f;
@@ -1243,7 +1250,7 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
       int g = 0, k = 0;
       bool ok = true;
       for (int u = snake_unit(k); ok && u < n_units; u = snake_unit(++k)) {
-        const Unit w = load_unit(f, u, prerot, up);
+        const Unit w = load_unit<kAbs>(f, u, prerot, up);
         const int b = w.blk.row;
         if (prerot) {
           if (k > 0 && !wait(Q_EMPTY, (k - 1) & 1)) break;
@@ -1339,7 +1346,7 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
     int g = 0, k = 0;
     bool ok = true;
     for (int u = snake_unit(k); ok && u < n_units; u = snake_unit(++k)) {
-      const Unit w = load_unit(f, u, prerot, up);
+      const Unit w = load_unit<kAbs>(f, u, prerot, up);
       if (!wait_u(Q_READY, k & 1)) break;
       if (w.n == 0) {
         ptx::mma_commit_w(bar(Q_EMPTY));
@@ -1388,7 +1395,7 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
     const int row = tid - 320;  // 0..63: key row of the tile
     int g = 0;
     for (int kr = 0, u = snake_unit(0); u < n_units && !*s_abort; u = snake_unit(++kr)) {
-      const Unit w = load_unit(f, u, prerot, up);
+      const Unit w = load_unit<kAbs>(f, u, prerot, up);
       for (int j = 0; j < w.n; ++j, ++g) {
         const int slot = g % kKS, key = w.kv_lo + unit_tile(w, j) * BN + row;
         uint32_t info = 0;
@@ -2164,29 +2171,48 @@ int sm100_bwd(const AiAttnBwdArgs& a, float* delta, void* rot, bool rot_ready, f
     // the split, the abs-block items' units first, then four-head units of
     // the short items when a GQA group has a multiple of four query heads,
     // then two-head units of the other items.
-    UnitPlan up{0, 0, 0, 0};
+    UnitPlan up{f.layout.n_fwd_abs_items, 0, 0, 0}, up_abs{0, 0, 0, 0};
     if (G % 2 == 0) {
-      const int n_short = (G % 4 == 0) ? f.layout.n_fwd_short_items : 0;
-      up.n_pack_units = n_short * (f.num_q_heads / 4);
+      up.n_pack_items = (G % 4 == 0) ? f.layout.n_fwd_short_items : 0;
+      up.n_pack_units = up.n_pack_items * (f.num_q_heads / 4);
+      up.n_units = up.n_pack_units + (n_pair - up.n_pack_items) * (f.num_q_heads / 2);
       if (dq_split) {
-        const int n_abs_short = (G % 4 == 0) ? f.layout.n_fwd_abs_short_items : 0;
-        up.n_abs_pack_units = n_abs_short * (f.num_q_heads / 4);
-        up.n_abs_units = up.n_abs_pack_units + (f.layout.n_fwd_abs_items - n_abs_short) * (f.num_q_heads / 2);
+        up_abs.n_pack_items = (G % 4 == 0) ? f.layout.n_fwd_abs_short_items : 0;
+        up_abs.n_pack_units = up_abs.n_pack_items * (f.num_q_heads / 4);
+        up_abs.n_units =
+            up_abs.n_pack_units + (f.layout.n_fwd_abs_items - up_abs.n_pack_items) * (f.num_q_heads / 2);
       }
-      up.n_units = up.n_abs_units + up.n_pack_units + (n_pair - n_short) * (f.num_q_heads / 2);
     }
-    if (e == cudaSuccess && up.n_units > 0) {
-      int dev = 0, sms = 148;
-      if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-      const int grid = up.n_units < sms ? up.n_units : sms;
-      e = cudaFuncSetAttribute(dq_pers_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dqw::kSmem);
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    auto launch_pers = [&](auto kernel, const UnitPlan& p, bool after_pers) {
+      if (p.n_units <= 0 || e != cudaSuccess) return;
+      const int grid = p.n_units < sms ? p.n_units : sms;
+      e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dqw::kSmem);
       if (e == cudaSuccess) {
         ProfScope ps(AI_PROF_DQ, st);
-        dq_pers_kernel<<<grid, dqw::kThreads, dqw::kSmem, st>>>(a, delta, tk, tv, tqr, tdo, tkr, tqr64, tdo64,
-                                                                tkc, pre ? 1 : 0, up, dq_split ? dq_part : nullptr);
-        e = cudaGetLastError();
+        // Right after the other persistent launch (which shares no data with
+        // this one) it starts by programmatic dependent launch.
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(grid);
+        cfg.blockDim = dim3(dqw::kThreads);
+        cfg.dynamicSmemBytes = dqw::kSmem;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = after_pers ? 1 : 0;
+        e = cudaLaunchKernelEx(&cfg, kernel, a, delta, tk, tv, tqr, tdo, tkr, tqr64, tdo64, tkc, pre ? 1 : 0, p,
+                               dq_split ? dq_part : (float*)nullptr);
+        if (e == cudaSuccess) e = cudaGetLastError();
       }
-    }
+    };
+    // The abs launch first: the other launch, then the dK/dV pass below,
+    // start their CTAs under the tail of the launch right before them
+    // (programmatic dependent launch).
+    if (dq_split) launch_pers(dq_pers_kernel<true>, up_abs, false);
+    launch_pers(dq_pers_kernel<false>, up, dq_split && up_abs.n_units > 0);
   }
   // The deferred one-head dQ launch (after the dK/dV pass below, so that the
   // dK/dV CTAs start under the persistent dQ as before).
@@ -2255,16 +2281,17 @@ int sm100_bwd(const AiAttnBwdArgs& a, float* delta, void* rot, bool rot_ready, f
     if (e == cudaSuccess && n_abs > 0) {
       // Boxes of 64 / G rows for the steps that pack a group's heads.
       const int Gk = f.num_q_heads / f.num_kv_heads;
-      CUtensorMap tqp = tq, tdop = tdo;
+      CUtensorMap tqp = tq, tdop = tdo, tqrp = tqr;
       if ((Gk == 2 || Gk == 4 || Gk == 8) &&
           (!sm100_make_map(&tqp, f.q, f.batch, f.num_q_heads, f.seq_len, kv::BQ / Gk) ||
-           !sm100_make_map(&tdop, a.dout, f.batch, f.num_q_heads, f.seq_len, kv::BQ / Gk)))
+           !sm100_make_map(&tdop, a.dout, f.batch, f.num_q_heads, f.seq_len, kv::BQ / Gk) ||
+           (pre && !sm100_make_map(&tqrp, qr, f.batch, f.num_q_heads, f.seq_len, kv::BQ / Gk))))
         return AI_ERR_TMA;
       e = cudaFuncSetAttribute(dkdv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kv::kSmem);
       if (e == cudaSuccess) {
         ProfScope ps(AI_PROF_DKDV, st);
         dkdv_kernel<<<dim3(n_abs, f.num_kv_heads), kThreads, kv::kSmem, st>>>(a, delta, tk, tv, tq, tdo, tqp, tdop,
-                                                                               tkc, pre ? 1 : 0, 1);
+                                                                               tkc, tqr, tqrp, pre ? 1 : 0, 1);
         e = cudaGetLastError();
       }
     }

@@ -528,31 +528,20 @@ __device__ __forceinline__ int unit_head(const Unit& w, int t, int r) {
 }
 __device__ __forceinline__ int unit_row(const Unit& w, int r) { return w.q0 + (w.pk == 2 ? (r & 63) : r); }
 
+template <bool kAbs>
 __device__ __forceinline__ Unit load_unit(const AiAttnFwdArgs& a, int u, int prerot, const UnitPlan& up) {
   const AiAttnLayout& L = a.layout;
   const int hpairs = a.num_q_heads / 2, hquads = a.num_q_heads / 4, G = a.num_q_heads / a.num_kv_heads;
   int it;
   Unit w;
-  w.abs = u < up.n_abs_units;
-  if (w.abs) {
-    if (u < up.n_abs_pack_units) {
-      it = u / hquads;
-      w.h0 = 4 * (u % hquads);
-      w.pk = 2;
-    } else {
-      const int v = u - up.n_abs_pack_units;
-      it = up.n_abs_pack_units / hquads + v / hpairs;
-      w.h0 = 2 * (v % hpairs);
-      w.pk = 1;
-    }
-  } else if (u - up.n_abs_units < up.n_pack_units) {
-    const int v = u - up.n_abs_units;
-    it = L.n_fwd_abs_items + v / hquads;
-    w.h0 = 4 * (v % hquads);
+  w.abs = kAbs;
+  if (u < up.n_pack_units) {
+    it = up.item_base + u / hquads;
+    w.h0 = 4 * (u % hquads);
     w.pk = 2;
   } else {
-    const int v = u - up.n_abs_units - up.n_pack_units;
-    it = L.n_fwd_abs_items + (up.n_pack_units > 0 ? L.n_fwd_short_items : 0) + v / hpairs;
+    const int v = u - up.n_pack_units;
+    it = up.item_base + up.n_pack_items + v / hpairs;
     w.h0 = 2 * (v % hpairs);
     w.pk = 1;
   }
@@ -566,7 +555,7 @@ __device__ __forceinline__ Unit load_unit(const AiAttnFwdArgs& a, int u, int pre
   w.kv_hi = min(w.blk.e, w.q1);
   w.n = w.kv_hi > w.kv_lo ? (w.kv_hi - w.kv_lo + BN - 1) / BN : 0;
   w.ja = w.jb = 0;
-  if (w.abs) {
+  if (kAbs) {
     abs_tiles(w.blk, w.kv_lo, w.kv_hi, BN, w.ja, w.jb);
     w.n -= w.jb - w.ja;
   }
@@ -577,6 +566,9 @@ __device__ __forceinline__ Unit load_unit(const AiAttnFwdArgs& a, int u, int pre
 }
 }  // namespace pf
 
+// kAbs: the units are the abs-block items' key tiles without abs keys
+// (partial rows into part_o / part_lse); otherwise the other items, whole.
+template <bool kAbs>
 __global__ void __launch_bounds__(pf::kThreads, 1)
     fwd_pers_kernel(const AiAttnFwdArgs a, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_qr,
@@ -584,6 +576,9 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
                     const __grid_constant__ CUtensorMap tm_qr64, const __grid_constant__ CUtensorMap tm_kc,
                     const int prerot, const UnitPlan up, float* __restrict__ part_o, float* __restrict__ part_lse) {
   using namespace pf;
+  // The launch after this one (the other persistent launch of the split)
+  // reads nothing this one writes: let its CTAs take the SMs these leave.
+  if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int n_units = up.n_units;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = tile::align1024(smem_raw);
@@ -642,7 +637,7 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
     // The next unit's description is read from global memory while this
     // unit's last PV MMAs run (before the epilogue's O_DONE wait).
     Unit w_next{};
-    if (snake_unit(0) < n_units) w_next = load_unit(a, snake_unit(0), prerot, up);
+    if (snake_unit(0) < n_units) w_next = load_unit<kAbs>(a, snake_unit(0), prerot, up);
     bool store_pending = false;  // thread 0: the last TMA store's smem read not yet waited for
     for (int u = snake_unit(k); u < n_units && !*s_abort; u = snake_unit(++k)) {
       const Unit w = w_next;
@@ -774,7 +769,7 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
         done = j + 1;
       }
       if (done != w.n) break;
-      if (snake_unit(k + 1) < n_units) w_next = load_unit(a, snake_unit(k + 1), prerot, up);
+      if (snake_unit(k + 1) < n_units) w_next = load_unit<kAbs>(a, snake_unit(k + 1), prerot, up);
       // Epilogue: O_t / l.  O_t is read into registers, then released to the
       // next unit's first PV before the global stores.
       bool have_o = false;
@@ -893,7 +888,7 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
       int g = 0, k = 0;
       bool ok = true;
       for (int u = snake_unit(k); ok && u < n_units; u = snake_unit(++k)) {
-        const Unit w = load_unit(a, u, prerot, up);
+        const Unit w = load_unit<kAbs>(a, u, prerot, up);
         const int b = w.blk.row;
         const CUtensorMap* mk = w.k_pre ? &tm_kr : &tm_k;
         for (int j = 0; j <= w.n && ok; ++j) {
@@ -996,7 +991,7 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
     int g = 0, k = 0;
     bool ok = true;
     for (int u = snake_unit(k); ok && u < n_units; u = snake_unit(++k)) {
-      const Unit w = load_unit(a, u, prerot, up);
+      const Unit w = load_unit<kAbs>(a, u, prerot, up);
       if (!wait_u(Q_READY, k & 1)) break;
       if (w.n == 0) {
         ptx::mma_commit_w(bar(Q_EMPTY));
@@ -1053,7 +1048,7 @@ __global__ void __launch_bounds__(pf::kThreads, 1)
     const __half2* cs16 = static_cast<const __half2*>(L.rope_cs16);
     int g = 0;
     for (int kr = 0, u = snake_unit(0); u < n_units && !*s_abort; u = snake_unit(++kr)) {
-      const Unit w = load_unit(a, u, prerot, up);
+      const Unit w = load_unit<kAbs>(a, u, prerot, up);
       for (int j = 0; j < w.n; ++j, ++g) {
         const int slot = g & 1;
         int c0, c1;
@@ -1181,16 +1176,18 @@ int sm100_fwd(const AiAttnFwdArgs& a, cudaStream_t st, cudaError_t* cuda_err) {
     const bool split = pre && part_bytes > 0 && a.workspace_bytes >= pb + part_bytes;
     float* part_o = split ? reinterpret_cast<float*>(static_cast<char*>(a.workspace) + pb) : nullptr;
     float* part_lse = split ? part_o + (size_t)a.layout.n_fwd_abs_items * a.num_q_heads * BM * D : nullptr;
-    UnitPlan up{0, 0, 0, 0};
+    // Units of the persistent launches: the items after the abs ones, and
+    // (split) the abs items' key tiles without abs keys.
+    UnitPlan up{a.layout.n_fwd_abs_items, 0, 0, 0}, up_abs{0, 0, 0, 0};
     if (G % 2 == 0) {
-      const int n_short = (G % 4 == 0) ? a.layout.n_fwd_short_items : 0;
-      up.n_pack_units = n_short * (a.num_q_heads / 4);
+      up.n_pack_items = (G % 4 == 0) ? a.layout.n_fwd_short_items : 0;
+      up.n_pack_units = up.n_pack_items * (a.num_q_heads / 4);
+      up.n_units = up.n_pack_units + (n_pair - up.n_pack_items) * (a.num_q_heads / 2);
       if (split) {
-        const int n_abs_short = (G % 4 == 0) ? a.layout.n_fwd_abs_short_items : 0;
-        up.n_abs_pack_units = n_abs_short * (a.num_q_heads / 4);
-        up.n_abs_units = up.n_abs_pack_units + (a.layout.n_fwd_abs_items - n_abs_short) * (a.num_q_heads / 2);
+        up_abs.n_pack_items = (G % 4 == 0) ? a.layout.n_fwd_abs_short_items : 0;
+        up_abs.n_pack_units = up_abs.n_pack_items * (a.num_q_heads / 4);
+        up_abs.n_units = up_abs.n_pack_units + (a.layout.n_fwd_abs_items - up_abs.n_pack_items) * (a.num_q_heads / 2);
       }
-      up.n_units = up.n_abs_units + up.n_pack_units + (n_pair - n_short) * (a.num_q_heads / 2);
     }
     CUtensorMap tm_kc = tm_k;
     if (pre && a.layout.n_rot_classes > 0 &&
@@ -1207,32 +1204,44 @@ int sm100_fwd(const AiAttnFwdArgs& a, cudaStream_t st, cudaError_t* cuda_err) {
       }
       return AI_OK;
     };
-    auto launch_pers = [&]() -> int {
-      if (up.n_units <= 0) return AI_OK;
-      CUtensorMap tm_qr = tm_k, tm_kr = tm_k, tm_qr64 = tm_k;
-      if (pre && (!sm100_make_map(&tm_qr, qr, a.batch, a.num_q_heads, a.seq_len, BM) ||
-                  !sm100_make_map(&tm_qr64, qr, a.batch, a.num_q_heads, a.seq_len, BM / 2) ||
-                  !sm100_make_map(&tm_kr, kr, a.batch, a.num_kv_heads, a.seq_len, BN)))
-        return AI_ERR_TMA;
-      int dev = 0, sms = 148;
-      if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-      const int grid = up.n_units < sms ? up.n_units : sms;
-      CUtensorMap tm_o;
-      if (!sm100_make_map(&tm_o, a.out, a.batch, a.num_q_heads, a.seq_len, BM)) return AI_ERR_TMA;
-      e = cudaFuncSetAttribute(fwd_pers_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pf::kSmem);
+    CUtensorMap tm_qr = tm_k, tm_kr = tm_k, tm_qr64 = tm_k, tm_o;
+    if (pre && (!sm100_make_map(&tm_qr, qr, a.batch, a.num_q_heads, a.seq_len, BM) ||
+                !sm100_make_map(&tm_qr64, qr, a.batch, a.num_q_heads, a.seq_len, BM / 2) ||
+                !sm100_make_map(&tm_kr, kr, a.batch, a.num_kv_heads, a.seq_len, BN)))
+      return AI_ERR_TMA;
+    if (!sm100_make_map(&tm_o, a.out, a.batch, a.num_q_heads, a.seq_len, BM)) return AI_ERR_TMA;
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    auto launch_pers = [&](auto kernel, const UnitPlan& p, bool after_pers) {
+      if (p.n_units <= 0 || e != cudaSuccess) return;
+      const int grid = p.n_units < sms ? p.n_units : sms;
+      e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pf::kSmem);
       if (e == cudaSuccess) {
         ProfScope ps(AI_PROF_FWD, st);
-        fwd_pers_kernel<<<grid, pf::kThreads, pf::kSmem, st>>>(a, tm_k, tm_v, tm_qr, tm_kr, tm_o, tm_qr64, tm_kc,
-                                                                pre ? 1 : 0, up, part_o, part_lse);
-        e = cudaGetLastError();
+        // Right after the other persistent launch (which reads and writes
+        // nothing this one touches) it starts by programmatic dependent
+        // launch on the SMs that one leaves.
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(grid);
+        cfg.blockDim = dim3(pf::kThreads);
+        cfg.dynamicSmemBytes = pf::kSmem;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = after_pers ? 1 : 0;
+        e = cudaLaunchKernelEx(&cfg, kernel, a, tm_k, tm_v, tm_qr, tm_kr, tm_o, tm_qr64, tm_kc, pre ? 1 : 0, p, part_o,
+                               part_lse);
+        if (e == cudaSuccess) e = cudaGetLastError();
       }
-      return AI_OK;
     };
-    // The split's partial rows come from the persistent kernel: it runs first.
-    int rc = split ? launch_pers() : launch_single();
-    if (rc != AI_OK) return rc;
-    if (e == cudaSuccess) rc = split ? launch_single() : launch_pers();
-    if (rc != AI_OK) return rc;
+    // The split's partial rows come from the abs launch of the persistent
+    // kernel (first: its units are short, the other launch fills in behind
+    // it); the one-head kernel runs after both.
+    if (split) launch_pers(fwd_pers_kernel<true>, up_abs, false);
+    launch_pers(fwd_pers_kernel<false>, up, split && up_abs.n_units > 0);
+    if (e == cudaSuccess) launch_single();
   }
   if (cuda_err) *cuda_err = e;
   return e == cudaSuccess ? AI_OK : AI_ERR_LAUNCH;

@@ -79,13 +79,13 @@ __device__ __forceinline__ int pack_heads(int rows, int G) {
   return 1;
 }
 
-// Work units of the persistent forward / dQ kernels: with the abs split on,
-// the items of blocks with abs keys come first (their key tiles without abs
-// keys: n_abs_pack_units four-head units of the short ones, then two-head
-// units of the others), then n_pack_units four-head units of the other short
-// items, then two-head units of the rest; n_units in all.
+// Work units of one launch of the persistent forward / dQ kernels: the work
+// items from item_base on, the first n_pack_items of them (items of at most
+// 64 rows) as n_pack_units four-head units, the others as two-head units;
+// n_units in all.  The abs split launches them once for the abs-block items
+// (item_base 0; their key tiles without abs keys) and once for the rest.
 struct UnitPlan {
-  int n_abs_pack_units, n_abs_units, n_pack_units, n_units;
+  int item_base, n_pack_items, n_pack_units, n_units;
 };
 
 // Key tiles [ja, jb) (tiles of bn keys from kv_lo, the last one ending at

@@ -187,6 +187,12 @@ def test_bf16_bench_layout_documents(cuda_device):
     assert checked >= 2 * (len(rows[0].boundary_indices) + 3)
 
 
+def _dq_scratch_bytes(layout, Hq, D=128):
+    """Backward workspace bytes of the abs split's dQ partials (they follow
+    the split key tiles' partials)."""
+    return (layout.n_fwd_abs_items * Hq * 128 * D * 4 + 255) // 256 * 256 if layout.n_fwd_abs_items else 0
+
+
 def test_bf16_split_key_tiles_match_whole_key_tiles(cuda_device):
     """The +E chain's long key tiles are split into chunks of query tiles
     whose fp32 partial sums a second launch adds up (when the workspace holds
@@ -216,8 +222,8 @@ def test_bf16_split_key_tiles_match_whole_key_tiles(cuda_device):
         nbytes = ctypes.c_size_t(0)
         assert lib.ai_attn_bwd_workspace(ctypes.byref(a), ctypes.byref(nbytes)) == 0
         delta_only = (B * Hq * T * 4 + 255) // 256 * 256
-        # the dQ partials of the abs split come after the dK/dV partials: left out of both runs
-        dq_part = (layout.n_fwd_abs_items * Hq * 128 * D * 4 + 255) // 256 * 256
+        # the abs splits' partials come after the split key tiles' ones: left out of both runs
+        dq_part = _dq_scratch_bytes(layout, Hq, D)
         assert nbytes.value > delta_only + dq_part  # the dK/dV partials are asked for
         ws = torch.empty(nbytes.value - dq_part if split else delta_only, dtype=torch.uint8, device=cuda_device)
         a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
@@ -278,7 +284,7 @@ def test_bf16_abs_split_matches_whole_abs_items(cuda_device):
     n_abs = layout.n_fwd_abs_items
     assert n_abs > 0
     fwd_part = (n_abs * Hq * 128 * (D + 1) * 4 + 255) // 256 * 256
-    dq_part = (n_abs * Hq * 128 * D * 4 + 255) // 256 * 256
+    dq_part = _dq_scratch_bytes(layout, Hq, D)
     lib = _lib.lib()
     stream = ctypes.c_void_p(torch.cuda.current_stream(cuda_device).cuda_stream)
     res = []
