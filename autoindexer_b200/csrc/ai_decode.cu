@@ -8,7 +8,9 @@
 // chunks' partial softmax results.
 //
 // HBM-bound: per key 2 x 256 B of K and V (bf16, D = 128) plus a 256 B rotary
-// row that stays in L2.  Split CTA (256 threads), per 256-key sub-tile:
+// row that stays in L2.  The default split kernel streams K and V by TMA
+// (decode_tma_kernel, below); without 16-byte aligned K / V it falls back to
+// the register-streaming split kernel (256 threads), per 256-key sub-tile:
 //   phase 1  thread t = key: rotated K row . q_g for each query head g
 //            (q in shared memory, broadcast reads), logits to shared memory;
 //   softmax  warp g = query head g: sub-tile max, running max / sum, the
@@ -27,6 +29,8 @@
 #include "../../include/ai_attn.h"
 #include "ai_common.cuh"
 #include "ai_kernels.h"
+#include "sm100_ptx.cuh"
+#include "sm100_tile.cuh"
 
 namespace ai {
 namespace dec {
@@ -222,6 +226,240 @@ __global__ void __launch_bounds__(kThreads, kG <= 4 ? 4 : 3)
   }
 }
 
+// TMA-pipelined variant (the default when K and V allow tensor maps): the
+// K and V rows of 64-key sub-tiles stream into shared memory by TMA through
+// a 3-stage ring, so every CTA keeps up to three sub-tiles (96 KB) in
+// flight and the cache is read at full line width; two CTAs per SM.
+//   phase 1  four threads per key (two rotation pairs of 8 dims each): the
+//            key's dims rotated with the fp16 table row, dotted with the
+//            group's queries, summed over the four lanes;
+//   softmax  warp g = query head g, as in the split kernel;
+//   phase 2  warp w = keys 8 w .. 8 w + 7, lane = dims 4 l .. 4 l + 3 of the
+//            V rows in shared memory: o_g += p_g,j v_j.
+// A bounded wait that expires records AI_ERR_DEV_TIMEOUT, waits (bounded)
+// for the loads still in flight and ends the CTA.
+namespace tma {
+constexpr int kKeys = 64;                   // keys per sub-tile (TMA box rows)
+constexpr int kStages = 3;
+constexpr uint32_t kHalf = kKeys * 128;     // one 64-dim column block of a sub-tile (128-byte rows)
+constexpr uint32_t kTile = 2 * kHalf;       // 16 KB
+constexpr uint32_t K0 = 0;                  // K ring
+constexpr uint32_t V0 = K0 + kStages * kTile;
+constexpr uint32_t Q = V0 + kStages * kTile;  // float [kMaxG][D]
+constexpr uint32_t P = Q + kMaxG * D * 4;     // float [kMaxG][kKeys]
+constexpr uint32_t ALPHA = P + kMaxG * kKeys * 4;
+constexpr uint32_t OSUM = ALPHA + kMaxG * 4;  // float [8 warps][D]
+constexpr uint32_t BARS = OSUM + (kThreads / 32) * D * 4;
+constexpr uint32_t TOTAL = BARS + 8 * kStages;
+constexpr size_t kSmem = TOTAL + 1024;
+static_assert(2 * kSmem <= 227 * 1024, "two CTAs per SM");
+constexpr long long kWait = 1000000000LL;
+}  // namespace tma
+
+template <int kG>
+__global__ void __launch_bounds__(kThreads, 2)
+    decode_tma_kernel(const AiAttnDecodeArgs a, const __grid_constant__ CUtensorMap tm_k,
+                      const __grid_constant__ CUtensorMap tm_v, float* __restrict__ part, int n_split, int chunk) {
+  using namespace tma;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = tile::align1024(smem_raw);
+  const uint32_t sbase = ptx::smem_u32(sm);
+  float* s_q = reinterpret_cast<float*>(sm + Q);
+  float* s_p = reinterpret_cast<float*>(sm + P);
+  float* s_alpha = reinterpret_cast<float*>(sm + ALPHA);
+  float* s_o = reinterpret_cast<float*>(sm + OSUM);
+  auto bar = [&](int i) { return sbase + BARS + 8u * (uint32_t)i; };
+
+  const int split = blockIdx.x, bh = blockIdx.y;
+  const int b = bh / a.num_kv_heads, hk = bh % a.num_kv_heads;
+  const int G = a.num_q_heads / a.num_kv_heads;
+  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+  const int c0 = split * chunk, c1 = min(a.kv_len, c0 + chunk);
+  const int n_tiles = c1 > c0 ? (c1 - c0 + kKeys - 1) / kKeys : 0;
+
+  auto issue = [&](int i) {  // sub-tile i into stage i % kStages (thread 0)
+    const int st = i % kStages, k0 = c0 + i * kKeys;
+    ptx::mbar_arrive_expect_tx(bar(st), 2 * kTile);
+    ptx::tma_load_4d(sbase + K0 + st * kTile, &tm_k, bar(st), 0, k0, hk, b);
+    ptx::tma_load_4d(sbase + K0 + st * kTile + kHalf, &tm_k, bar(st), 64, k0, hk, b);
+    ptx::tma_load_4d(sbase + V0 + st * kTile, &tm_v, bar(st), 0, k0, hk, b);
+    ptx::tma_load_4d(sbase + V0 + st * kTile + kHalf, &tm_v, bar(st), 64, k0, hk, b);
+  };
+  if (tid == 0) {
+    for (int i = 0; i < kStages; ++i) ptx::mbar_init(bar(i), 1);
+    ptx::fence_mbar_init();
+    ptx::prefetch_tmap(&tm_k);
+    ptx::prefetch_tmap(&tm_v);
+    for (int i = 0; i < kStages && i < n_tiles; ++i) issue(i);
+  }
+  for (int i = tid; i < G * D; i += kThreads) {
+    const int g = i / D, d = i % D;
+    const __nv_bfloat16* qr = static_cast<const __nv_bfloat16*>(a.q.ptr) + b * a.q.stride_b +
+                              (int64_t)(hk * G + g) * a.q.stride_h;
+    s_q[g * D + d] = __bfloat162float(qr[d]);
+  }
+  __syncthreads();
+
+  const int32_t* krow = a.key_rows + b * a.key_rows_stride_b;
+  const uint8_t* kok = a.key_ok ? a.key_ok + b * a.key_ok_stride_b : nullptr;
+  const uint4* cs = static_cast<const uint4*>(a.rope_cs16);  // 16 uint4 per table row
+  const float sl2 = a.scale * kLog2e;
+  float m_run = -CUDART_INF_F, l_run = 0.f;
+  float o[kG][4];
+#pragma unroll
+  for (int g = 0; g < kG; ++g) o[g][0] = o[g][1] = o[g][2] = o[g][3] = 0.f;
+
+  int done = 0;  // sub-tiles consumed
+  bool ok_all = true;
+  for (int i = 0; i < n_tiles; ++i) {
+    const int st = i % kStages;
+    // The key's table row and flag are fetched before the wait for its tile.
+    const int kk = tid / 4, pp = tid % 4, j = c0 + i * kKeys + kk;
+    const bool inb = j < c1;
+    int r = inb ? __ldg(krow + j) : 0;
+    const bool ok = inb && (kok == nullptr || __ldg(kok + j) != 0);
+    if (ok && (r < 0 || r >= a.n_pos)) {
+      report(a.status, AI_ERR_DEV_BOUNDS);
+      r = 0;
+    }
+    if (!ptx::mbar_wait(bar(st), (uint32_t)(i / kStages) & 1u, kWait)) {
+      report(a.status, AI_ERR_DEV_TIMEOUT);
+      ok_all = false;
+    }
+    if (__syncthreads_or(!ok_all)) break;
+    // ---- phase 1: key kk, rotation pairs 2 pp and 2 pp + 1
+    {
+      float acc[kG];
+#pragma unroll
+      for (int g = 0; g < kG; ++g) acc[g] = 0.f;
+      if (ok) {
+        const uint4* tr = cs + (int64_t)r * (D / 8);
+        const uint8_t* kt = sm + K0 + st * kTile;
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc) {
+          const int c = 2 * pp + cc;
+          float x1[8], x2[8];
+          unpack8(*reinterpret_cast<const uint4*>(kt + tile::chunk_off<kKeys>(kk, c)), x1);
+          unpack8(*reinterpret_cast<const uint4*>(kt + tile::chunk_off<kKeys>(kk, c + 8)), x2);
+          const uint4 t0 = __ldg(tr + 2 * c), t1 = __ldg(tr + 2 * c + 1);
+          const __half2* h0 = reinterpret_cast<const __half2*>(&t0);
+          const __half2* h1 = reinterpret_cast<const __half2*>(&t1);
+          float y1[8], y2[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const float2 csn = __half22float2(e < 4 ? h0[e] : h1[e - 4]);
+            y1[e] = x1[e] * csn.x - x2[e] * csn.y;
+            y2[e] = x2[e] * csn.x + x1[e] * csn.y;
+          }
+#pragma unroll
+          for (int g = 0; g < kG; ++g) {
+            if (g < G) {
+              const float* qg = s_q + g * D;
+#pragma unroll
+              for (int e = 0; e < 8; ++e) acc[g] = fmaf(y1[e], qg[8 * c + e], fmaf(y2[e], qg[64 + 8 * c + e], acc[g]));
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int g = 0; g < kG; ++g) {
+        acc[g] += __shfl_xor_sync(0xffffffffu, acc[g], 1);
+        acc[g] += __shfl_xor_sync(0xffffffffu, acc[g], 2);
+        if (g < G && pp == 0) s_p[g * kKeys + kk] = ok ? acc[g] * sl2 : -CUDART_INF_F;
+      }
+    }
+    __syncthreads();
+    // ---- softmax bookkeeping: warp g handles head g
+    if (warp < G) {
+      const float v0 = s_p[warp * kKeys + lane], v1 = s_p[warp * kKeys + 32 + lane];
+      float mx = fmaxf(v0, v1);
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      const float m_new = fmaxf(m_run, mx);
+      const float msub = m_new == -CUDART_INF_F ? 0.f : m_new;
+      const float p0 = exp2f(v0 - msub), p1 = exp2f(v1 - msub);
+      s_p[warp * kKeys + lane] = p0;
+      s_p[warp * kKeys + 32 + lane] = p1;
+      float sum = p0 + p1;
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+      const float alpha = exp2f(m_run - msub);  // 0 while m_run is -inf
+      l_run = l_run * alpha + sum;
+      m_run = m_new;
+      if (lane == 0) s_alpha[warp] = alpha;
+    }
+    __syncthreads();
+    // ---- phase 2: o_g += p_g,j v_j over this warp's 8 keys
+    {
+#pragma unroll
+      for (int g = 0; g < kG; ++g) {
+        if (g < G) {
+          const float al = s_alpha[g];
+          o[g][0] *= al;
+          o[g][1] *= al;
+          o[g][2] *= al;
+          o[g][3] *= al;
+        }
+      }
+      const uint8_t* vt = sm + V0 + st * kTile;
+      const int hf = lane / 16, cidx = (lane % 16) / 2, sub = (lane % 2) * 8;
+#pragma unroll
+      for (int x = 0; x < kKeys / (kThreads / 32); ++x) {
+        const int key = warp * (kKeys / (kThreads / 32)) + x;
+        const uint2 raw = *reinterpret_cast<const uint2*>(vt + tile::chunk_off<kKeys>(key, 8 * hf + cidx) + sub);
+        const float2 v01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
+        const float2 v23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
+#pragma unroll
+        for (int g = 0; g < kG; ++g) {
+          if (g < G) {
+            const float pv = s_p[g * kKeys + key];
+            o[g][0] = fmaf(pv, v01.x, o[g][0]);
+            o[g][1] = fmaf(pv, v01.y, o[g][1]);
+            o[g][2] = fmaf(pv, v23.x, o[g][2]);
+            o[g][3] = fmaf(pv, v23.y, o[g][3]);
+          }
+        }
+      }
+    }
+    __syncthreads();  // stage st and the probabilities are free again
+    done = i + 1;
+    if (tid == 0 && i + kStages < n_tiles) issue(i + kStages);
+  }
+  if (!ok_all) {
+    // Loads still in flight land before the CTA ends (bounded).
+    if (tid == 0)
+      for (int i = done; i < n_tiles && i < done + kStages; ++i)
+        ptx::mbar_wait(bar(i % kStages), (uint32_t)(i / kStages) & 1u, kWait);
+    __syncthreads();
+    return;
+  }
+
+  // ---- partials: per head, (m, l, o[128]) with o summed over the warps; lane
+  // l holds dims 4 l .. 4 l + 3 of its warp's keys
+  float* base = part + ((int64_t)(b * a.num_q_heads + hk * G) * n_split + split) * (2 + D);
+#pragma unroll
+  for (int g = 0; g < kG; ++g) {
+    if (g >= G) break;  // (G is uniform: every thread leaves together)
+    s_o[warp * D + 4 * lane] = o[g][0];
+    s_o[warp * D + 4 * lane + 1] = o[g][1];
+    s_o[warp * D + 4 * lane + 2] = o[g][2];
+    s_o[warp * D + 4 * lane + 3] = o[g][3];
+    __syncthreads();
+    float* dst = base + (int64_t)g * n_split * (2 + D);
+    if (tid < D) {
+      float acc = 0.f;
+#pragma unroll
+      for (int w = 0; w < kThreads / 32; ++w) acc += s_o[w * D + tid];
+      dst[2 + tid] = acc;
+    }
+    if (warp == g && lane == 0) {
+      dst[0] = m_run;
+      dst[1] = l_run;
+    }
+    __syncthreads();
+  }
+}
+
 // One CTA per (row, query head), thread = dim: merges the chunks' partials.
 __global__ void __launch_bounds__(D) decode_combine_kernel(const AiAttnDecodeArgs a, const float* __restrict__ part,
                                                            int n_split) {
@@ -243,14 +481,23 @@ __global__ void __launch_bounds__(D) decode_combine_kernel(const AiAttnDecodeArg
 
 }  // namespace dec
 
-// Splits: enough CTAs to fill every SM at the split kernel's register bound,
-// chunks of whole 256-key sub-tiles.
+// Whether the TMA kernel can read K and V: 16-byte aligned bases and strides
+// (what a tensor map needs).
+static bool decode_tma_ok(const AiAttnDecodeArgs& a) {
+  const uintptr_t m = reinterpret_cast<uintptr_t>(a.k.ptr) | reinterpret_cast<uintptr_t>(a.v.ptr);
+  const int64_t st = a.k.stride_t | a.k.stride_h | a.k.stride_b | a.v.stride_t | a.v.stride_h | a.v.stride_b;
+  return (m & 15) == 0 && (st & 7) == 0;
+}
+
+// Splits: enough CTAs to fill every SM once at the kernel's CTAs per SM,
+// chunks of whole sub-tiles (256 keys; the TMA kernel's 64-key sub-tiles
+// divide them).
 static void decode_plan(const AiAttnDecodeArgs& a, int* n_split, int* chunk) {
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int pairs = a.batch * a.num_kv_heads;
   const int subtiles = (a.kv_len + dec::kSub - 1) / dec::kSub;
-  const int per_sm = a.num_q_heads / a.num_kv_heads <= 4 ? 4 : 3;  // the split kernel's CTAs per SM
+  const int per_sm = decode_tma_ok(a) ? 2 : (a.num_q_heads / a.num_kv_heads <= 4 ? 4 : 3);
   int want = (per_sm * sms) / pairs;  // at most one wave: a partial second wave doubles the tail
   if (want > subtiles) want = subtiles;
   if (want < 1) want = 1;
@@ -296,7 +543,26 @@ int decode_launch(const AiAttnDecodeArgs& a, cudaStream_t st) {
   ProfScope ps(AI_PROF_DECODE, st);
   const dim3 grid(n_split, a.batch * a.num_kv_heads);
   const int G = a.num_q_heads / a.num_kv_heads;
-  if (G <= 1)
+  CUtensorMap tk, tv;
+  AiTensor4 k4 = a.k, v4 = a.v;
+  if (decode_tma_ok(a) && sm100_make_map(&tk, k4, a.batch, a.num_kv_heads, a.kv_len, dec::tma::kKeys) &&
+      sm100_make_map(&tv, v4, a.batch, a.num_kv_heads, a.kv_len, dec::tma::kKeys)) {
+    auto run = [&](auto kernel) -> cudaError_t {
+      cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dec::tma::kSmem);
+      if (e == cudaSuccess) kernel<<<grid, dec::kThreads, dec::tma::kSmem, st>>>(a, tk, tv, part, n_split, chunk);
+      return e;
+    };
+    cudaError_t e;
+    if (G <= 1)
+      e = run(dec::decode_tma_kernel<1>);
+    else if (G <= 2)
+      e = run(dec::decode_tma_kernel<2>);
+    else if (G <= 4)
+      e = run(dec::decode_tma_kernel<4>);
+    else
+      e = run(dec::decode_tma_kernel<8>);
+    if (e != cudaSuccess) return AI_ERR_LAUNCH;
+  } else if (G <= 1)
     dec::decode_split_kernel<1><<<grid, dec::kThreads, 0, st>>>(a, part, n_split, chunk);
   else if (G <= 2)
     dec::decode_split_kernel<2><<<grid, dec::kThreads, 0, st>>>(a, part, n_split, chunk);

@@ -185,21 +185,30 @@ def sharded_forward(q_l: Tensor, k_l: Tensor, v_l: Tensor, layout: CompiledLayou
     return bufs.out.permute(0, 2, 1, 3)
 
 
-def sharded_backward(dout_l: Tensor, bufs: GatherBuffers, local_bwd: LocalBwd = kernel_bwd):
+def sharded_backward(dout_l: Tensor, bufs: GatherBuffers, local_bwd: LocalBwd = kernel_bwd, overlap: bool = False):
     """This rank's dQ, dK, dV written into its slices of the buffers, then
-    gathered: returns the full ``(dq, dk, dv)`` on every rank.  The dQ
-    gather is issued as soon as dQ is complete (``after_dq``) and runs on
-    NCCL's stream while the dK / dV kernels run; the caller's stream waits
-    for it before returning."""
+    gathered: returns the full ``(dq, dk, dv)`` on every rank.  With
+    ``overlap`` the backward runs in two parts and the dQ gather is issued
+    as soon as dQ is complete (``after_dq``), on NCCL's stream while the
+    dK / dV kernels run; the caller's stream waits for it before returning.
+    (Off by default: on two B200s the NCCL kernels then share the SMs with
+    dK / dV and the dK / dV launch no longer starts under the tail of the dQ
+    kernel, which cost more than the 0.4 ms of dQ gather it hid.)"""
     q0, q1 = bufs.q_heads
     k0, k1 = bufs.kv_heads
+    grads = (bufs.dq[:, q0:q1], bufs.dk[:, k0:k1], bufs.dv[:, k0:k1])
+    if not overlap:
+        local_bwd(bufs.state, dout_l, grads)
+        bufs.state = None
+        bufs.gather(bufs.dq, bufs.dk, bufs.dv)
+        return bufs.dq, bufs.dk, bufs.dv
     pending = []
 
     def after_dq():
         if bufs.world > 1:
             pending.append(bufs.gather_async(bufs.dq))
 
-    local_bwd(bufs.state, dout_l, (bufs.dq[:, q0:q1], bufs.dk[:, k0:k1], bufs.dv[:, k0:k1]), after_dq=after_dq)
+    local_bwd(bufs.state, dout_l, grads, after_dq=after_dq)
     bufs.state = None
     bufs.gather(bufs.dk, bufs.dv)
     for w in pending:
@@ -214,7 +223,7 @@ class KVShardedAttention(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, q, k, v, layout: CompiledLayout, scale: float, group, local_fwd: LocalFwd,
-                local_bwd: LocalBwd):
+                local_bwd: LocalBwd, overlap: bool = False):
         Hq, Hkv = q.shape[1], k.shape[1]
         if Hq % Hkv:
             raise ValueError(f"num_q_heads {Hq} is not a multiple of num_kv_heads {Hkv}")
@@ -222,21 +231,23 @@ class KVShardedAttention(torch.autograd.Function):
         k0, k1 = bufs.kv_heads
         q0, q1 = bufs.q_heads
         out = sharded_forward(q[:, q0:q1], k[:, k0:k1], v[:, k0:k1], layout, scale, bufs, local_fwd)
-        ctx.bufs, ctx.local_bwd = bufs, local_bwd
+        ctx.bufs, ctx.local_bwd, ctx.overlap = bufs, local_bwd, overlap
         return out
 
     @staticmethod
     def backward(ctx, dout):
         bufs = ctx.bufs
         q0, q1 = bufs.q_heads
-        dq, dk, dv = sharded_backward(dout[:, :, q0:q1], bufs, ctx.local_bwd)
+        dq, dk, dv = sharded_backward(dout[:, :, q0:q1], bufs, ctx.local_bwd, ctx.overlap)
         ctx.bufs = None
-        return dq, dk, dv, None, None, None, None, None
+        return dq, dk, dv, None, None, None, None, None, None
 
 
 def kv_sharded_attention(q: Tensor, k: Tensor, v: Tensor, layout: CompiledLayout, scale: float,
                          group: Optional[dist.ProcessGroup] = None, local_fwd: LocalFwd = kernel_fwd,
-                         local_bwd: LocalBwd = kernel_bwd) -> Tensor:
+                         local_bwd: LocalBwd = kernel_bwd, overlap: bool = False) -> Tensor:
     """Differentiable KV-head-sharded attention (see the module docstring);
-    with one rank, or no process group, it is the single-GPU attention."""
-    return KVShardedAttention.apply(q, k, v, layout, scale, group, local_fwd, local_bwd)
+    with one rank, or no process group, it is the single-GPU attention.
+    ``overlap``: start the dQ all-gather while dK / dV are computed (see
+    ``sharded_backward``)."""
+    return KVShardedAttention.apply(q, k, v, layout, scale, group, local_fwd, local_bwd, overlap)

@@ -79,6 +79,29 @@ def test_decode_matches_oracle(B, Hq, Hkv, L, per_row, masked, cuda_device):
 
 
 @pytest.mark.gpu
+def test_decode_unaligned_cache_matches_oracle(cuda_device):
+    """A V cache that is 8- but not 16-byte aligned cannot be read by TMA:
+    the register-streaming split kernel runs it; both kernels match the
+    oracle (the aligned case takes the TMA kernel)."""
+    from autoindexer_b200 import decode_attention, read_status
+
+    B, Hq, Hkv, L = 2, 8, 2, 777
+    q, k, v, kp, am, pp, mod, rope = _case(B, Hq, Hkv, L, True, True, 11, cuda_device)
+    want = O.decode_forward(q.double().numpy(), k.double().numpy(), v.double().numpy(), kp, am, rope)
+    wide = torch.zeros(B, Hkv, L, 136, dtype=torch.bfloat16)
+    wide[..., 4:132] = v
+    v_odd = wide.to(cuda_device)[..., 4:132]  # base 8 bytes past a 16-byte boundary
+    assert v_odd.data_ptr() % 16 == 8
+    outs = [decode_attention(q.to(cuda_device), k.to(cuda_device), vv, pp, mod) for vv in (v.to(cuda_device), v_odd)]
+    torch.cuda.synchronize(cuda_device)
+    assert read_status(cuda_device) == 0
+    for out in outs:
+        got = out.double().cpu().numpy()
+        assert np.max(np.abs(got - want)) <= 2e-2
+        assert rel_l2(got, want) <= 1e-2
+
+
+@pytest.mark.gpu
 def test_decode_all_masked_row_is_zero(cuda_device):
     from autoindexer_b200 import decode_attention
 

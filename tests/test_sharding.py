@@ -89,7 +89,7 @@ def _gloo_rank(rank: int, world: int, port: int, out):
         fwd, bwd = _oracle_local(rope)
         tq, tk, tv = (torch.from_numpy(x).requires_grad_(True) for x in (q, k, v))
         scale = q.shape[-1] ** -0.5
-        o = kv_sharded_attention(tq, tk, tv, list(rows), scale, None, fwd, bwd)
+        o = kv_sharded_attention(tq, tk, tv, list(rows), scale, None, fwd, bwd, overlap=True)
         o.backward(torch.from_numpy(dout))
         out.put((rank, o.detach().numpy(), tq.grad.numpy(), tk.grad.numpy(), tv.grad.numpy()))
         dist.barrier()
@@ -179,8 +179,9 @@ def _nccl_rank(rank: int, world: int, port: int, out):
         sc = 128 ** -0.5
         a = _run(lambda x, y, z: kv_sharded_attention(x, y, z, lay, sc), q, k, v, dout)
         b = _run(lambda x, y, z: AttentionFn.apply(x, y, z, lay, sc), q, k, v, dout)
+        c = _run(lambda x, y, z: kv_sharded_attention(x, y, z, lay, sc, overlap=True), q, k, v, dout)
         torch.cuda.synchronize(dev)
-        out.put((rank, all(torch.equal(x, y) for x, y in zip(a, b))))
+        out.put((rank, all(torch.equal(x, y) and torch.equal(x, w) for x, y, w in zip(a, b, c))))
         dist.barrier()
     finally:
         dist.destroy_process_group()
