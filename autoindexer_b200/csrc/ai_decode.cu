@@ -230,9 +230,10 @@ __global__ void __launch_bounds__(kThreads, kG <= 4 ? 4 : 3)
 // K and V rows of 64-key sub-tiles stream into shared memory by TMA through
 // a 3-stage ring, so every CTA keeps up to three sub-tiles (96 KB) in
 // flight and the cache is read at full line width; two CTAs per SM.
-//   phase 1  four threads per key (two rotation pairs of 8 dims each): the
-//            key's dims rotated with the fp16 table row, dotted with the
-//            group's queries, summed over the four lanes;
+//   phase 1  eight threads per key (one rotation pair of 8 + 8 dims each,
+//            the group's query dims of that pair in registers): the key's
+//            dims rotated with the fp16 table row, dotted with the queries,
+//            summed over the eight lanes;
 //   softmax  warp g = query head g, as in the split kernel;
 //   phase 2  warp w = keys 8 w .. 8 w + 7, lane = dims 4 l .. 4 l + 3 of the
 //            V rows in shared memory: o_g += p_g,j v_j.
@@ -309,54 +310,77 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
   for (int g = 0; g < kG; ++g) o[g][0] = o[g][1] = o[g][2] = o[g][3] = 0.f;
 
+  // Thread t owns rotation pair c = t % 8 (dims 8c .. 8c+7 and 64+8c ..
+  // 64+8c+7) of keys t / 8 and t / 8 + 32 of every sub-tile; with at most
+  // four heads per group their query dims stay in registers (shared-memory
+  // reads of the queries would bound the loop otherwise).
+  const int c = tid % 8;
+  constexpr bool kQReg = kG <= 4;
+  float qa[kQReg ? kG : 1][8], qb[kQReg ? kG : 1][8];
+  if (kQReg) {
+#pragma unroll
+    for (int g = 0; g < (kQReg ? kG : 1); ++g)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        qa[g][e] = g < G ? s_q[g * D + 8 * c + e] : 0.f;
+        qb[g][e] = g < G ? s_q[g * D + 64 + 8 * c + e] : 0.f;
+      }
+  }
+
   int done = 0;  // sub-tiles consumed
   bool ok_all = true;
   for (int i = 0; i < n_tiles; ++i) {
     const int st = i % kStages;
-    // The key's table row and flag are fetched before the wait for its tile.
-    const int kk = tid / 4, pp = tid % 4, j = c0 + i * kKeys + kk;
-    const bool inb = j < c1;
-    int r = inb ? __ldg(krow + j) : 0;
-    const bool ok = inb && (kok == nullptr || __ldg(kok + j) != 0);
-    if (ok && (r < 0 || r >= a.n_pos)) {
-      report(a.status, AI_ERR_DEV_BOUNDS);
-      r = 0;
+    // The keys' table rows and flags are fetched before the wait for their tile.
+    int rr[2];
+    bool okk[2];
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const int j = c0 + i * kKeys + tid / 8 + 32 * hh;
+      const bool inb = j < c1;
+      rr[hh] = inb ? __ldg(krow + j) : 0;
+      okk[hh] = inb && (kok == nullptr || __ldg(kok + j) != 0);
+      if (okk[hh] && (rr[hh] < 0 || rr[hh] >= a.n_pos)) {
+        report(a.status, AI_ERR_DEV_BOUNDS);
+        rr[hh] = 0;
+      }
     }
     if (!ptx::mbar_wait(bar(st), (uint32_t)(i / kStages) & 1u, kWait)) {
       report(a.status, AI_ERR_DEV_TIMEOUT);
       ok_all = false;
     }
     if (__syncthreads_or(!ok_all)) break;
-    // ---- phase 1: key kk, rotation pairs 2 pp and 2 pp + 1
-    {
+    // ---- phase 1: keys tid / 8 and tid / 8 + 32, rotation pair c
+    const uint8_t* kt = sm + K0 + st * kTile;
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      const int kk = tid / 8 + 32 * hh;
       float acc[kG];
 #pragma unroll
       for (int g = 0; g < kG; ++g) acc[g] = 0.f;
-      if (ok) {
-        const uint4* tr = cs + (int64_t)r * (D / 8);
-        const uint8_t* kt = sm + K0 + st * kTile;
+      if (okk[hh]) {
+        float x1[8], x2[8];
+        unpack8(*reinterpret_cast<const uint4*>(kt + tile::chunk_off<kKeys>(kk, c)), x1);
+        unpack8(*reinterpret_cast<const uint4*>(kt + tile::chunk_off<kKeys>(kk, c + 8)), x2);
+        const uint4* tr = cs + (int64_t)rr[hh] * (D / 8);
+        const uint4 t0 = __ldg(tr + 2 * c), t1 = __ldg(tr + 2 * c + 1);
+        const __half2* h0 = reinterpret_cast<const __half2*>(&t0);
+        const __half2* h1 = reinterpret_cast<const __half2*>(&t1);
+        float y1[8], y2[8];
 #pragma unroll
-        for (int cc = 0; cc < 2; ++cc) {
-          const int c = 2 * pp + cc;
-          float x1[8], x2[8];
-          unpack8(*reinterpret_cast<const uint4*>(kt + tile::chunk_off<kKeys>(kk, c)), x1);
-          unpack8(*reinterpret_cast<const uint4*>(kt + tile::chunk_off<kKeys>(kk, c + 8)), x2);
-          const uint4 t0 = __ldg(tr + 2 * c), t1 = __ldg(tr + 2 * c + 1);
-          const __half2* h0 = reinterpret_cast<const __half2*>(&t0);
-          const __half2* h1 = reinterpret_cast<const __half2*>(&t1);
-          float y1[8], y2[8];
+        for (int e = 0; e < 8; ++e) {
+          const float2 csn = __half22float2(e < 4 ? h0[e] : h1[e - 4]);
+          y1[e] = x1[e] * csn.x - x2[e] * csn.y;
+          y2[e] = x2[e] * csn.x + x1[e] * csn.y;
+        }
 #pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const float2 csn = __half22float2(e < 4 ? h0[e] : h1[e - 4]);
-            y1[e] = x1[e] * csn.x - x2[e] * csn.y;
-            y2[e] = x2[e] * csn.x + x1[e] * csn.y;
-          }
+        for (int g = 0; g < kG; ++g) {
+          if (g < G) {
 #pragma unroll
-          for (int g = 0; g < kG; ++g) {
-            if (g < G) {
-              const float* qg = s_q + g * D;
-#pragma unroll
-              for (int e = 0; e < 8; ++e) acc[g] = fmaf(y1[e], qg[8 * c + e], fmaf(y2[e], qg[64 + 8 * c + e], acc[g]));
+            for (int e = 0; e < 8; ++e) {
+              const float q1 = kQReg ? qa[kQReg ? g : 0][e] : s_q[g * D + 8 * c + e];
+              const float q2 = kQReg ? qb[kQReg ? g : 0][e] : s_q[g * D + 64 + 8 * c + e];
+              acc[g] = fmaf(y1[e], q1, fmaf(y2[e], q2, acc[g]));
             }
           }
         }
@@ -365,7 +389,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       for (int g = 0; g < kG; ++g) {
         acc[g] += __shfl_xor_sync(0xffffffffu, acc[g], 1);
         acc[g] += __shfl_xor_sync(0xffffffffu, acc[g], 2);
-        if (g < G && pp == 0) s_p[g * kKeys + kk] = ok ? acc[g] * sl2 : -CUDART_INF_F;
+        acc[g] += __shfl_xor_sync(0xffffffffu, acc[g], 4);
+        if (g < G && c == 0) s_p[g * kKeys + kk] = okk[hh] ? acc[g] * sl2 : -CUDART_INF_F;
       }
     }
     __syncthreads();
