@@ -331,19 +331,23 @@ __global__ void __launch_bounds__(kThreads, 2)
   bool ok_all = true;
   for (int i = 0; i < n_tiles; ++i) {
     const int st = i % kStages;
-    // The keys' table rows and flags are fetched before the wait for their tile.
-    int rr[2];
+    // The keys' table rows, flags and rotary values are fetched before the
+    // wait for their tile (the table reads hide under it).
     bool okk[2];
+    uint4 tt[2][2];
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
       const int j = c0 + i * kKeys + tid / 8 + 32 * hh;
       const bool inb = j < c1;
-      rr[hh] = inb ? __ldg(krow + j) : 0;
+      int r = inb ? __ldg(krow + j) : 0;
       okk[hh] = inb && (kok == nullptr || __ldg(kok + j) != 0);
-      if (okk[hh] && (rr[hh] < 0 || rr[hh] >= a.n_pos)) {
+      if (okk[hh] && (r < 0 || r >= a.n_pos)) {
         report(a.status, AI_ERR_DEV_BOUNDS);
-        rr[hh] = 0;
+        r = 0;
       }
+      const uint4* tr = cs + (int64_t)r * (D / 8);
+      tt[hh][0] = okk[hh] ? __ldg(tr + 2 * c) : make_uint4(0, 0, 0, 0);
+      tt[hh][1] = okk[hh] ? __ldg(tr + 2 * c + 1) : make_uint4(0, 0, 0, 0);
     }
     if (!ptx::mbar_wait(bar(st), (uint32_t)(i / kStages) & 1u, kWait)) {
       report(a.status, AI_ERR_DEV_TIMEOUT);
@@ -362,10 +366,8 @@ __global__ void __launch_bounds__(kThreads, 2)
         float x1[8], x2[8];
         unpack8(*reinterpret_cast<const uint4*>(kt + tile::chunk_off<kKeys>(kk, c)), x1);
         unpack8(*reinterpret_cast<const uint4*>(kt + tile::chunk_off<kKeys>(kk, c + 8)), x2);
-        const uint4* tr = cs + (int64_t)rr[hh] * (D / 8);
-        const uint4 t0 = __ldg(tr + 2 * c), t1 = __ldg(tr + 2 * c + 1);
-        const __half2* h0 = reinterpret_cast<const __half2*>(&t0);
-        const __half2* h1 = reinterpret_cast<const __half2*>(&t1);
+        const __half2* h0 = reinterpret_cast<const __half2*>(&tt[hh][0]);
+        const __half2* h1 = reinterpret_cast<const __half2*>(&tt[hh][1]);
         float y1[8], y2[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
@@ -514,20 +516,32 @@ static bool decode_tma_ok(const AiAttnDecodeArgs& a) {
   return (m & 15) == 0 && (st & 7) == 0;
 }
 
-// Splits: enough CTAs to fill every SM once at the kernel's CTAs per SM,
-// chunks of whole sub-tiles (256 keys; the TMA kernel's 64-key sub-tiles
-// divide them).
+// Splits of each (row, KV head) pair's keys into chunks of whole 64-key
+// sub-tiles: the count that minimises (waves of CTAs) x (sub-tiles per CTA
+// + one for a CTA's first loads), at the kernel's CTAs per SM.
 static void decode_plan(const AiAttnDecodeArgs& a, int* n_split, int* chunk) {
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int pairs = a.batch * a.num_kv_heads;
-  const int subtiles = (a.kv_len + dec::kSub - 1) / dec::kSub;
+  constexpr int kUnit = dec::tma::kKeys;
+  const int units = (a.kv_len + kUnit - 1) / kUnit;
   const int per_sm = decode_tma_ok(a) ? 2 : (a.num_q_heads / a.num_kv_heads <= 4 ? 4 : 3);
-  int want = (per_sm * sms) / pairs;  // at most one wave: a partial second wave doubles the tail
-  if (want > subtiles) want = subtiles;
-  if (want < 1) want = 1;
-  const int per = (subtiles + want - 1) / want;  // sub-tiles per chunk
-  *chunk = per * dec::kSub;
+  const int64_t slots = (int64_t)per_sm * sms;
+  int best = 1;
+  int64_t best_cost = -1;
+  for (int n = 1; n <= units && n <= 1024; ++n) {
+    const int per = (units + n - 1) / n;
+    const int used = (units + per - 1) / per;  // chunks actually needed
+    if (used != n) continue;
+    const int64_t waves = ((int64_t)pairs * n + slots - 1) / slots;
+    const int64_t cost = waves * (per + 1);
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best = n;
+    }
+  }
+  const int per = (units + best - 1) / best;
+  *chunk = per * kUnit;
   *n_split = (a.kv_len + *chunk - 1) / *chunk;
   if (*n_split < 1) *n_split = 1;
 }
