@@ -306,9 +306,9 @@ __global__ void __launch_bounds__(kThreads, 2)
   const uint4* cs = static_cast<const uint4*>(a.rope_cs16);  // 16 uint4 per table row
   const float sl2 = a.scale * kLog2e;
   float m_run = -CUDART_INF_F, l_run = 0.f;
-  float o[kG][4];
+  float2 o[kG][2];
 #pragma unroll
-  for (int g = 0; g < kG; ++g) o[g][0] = o[g][1] = o[g][2] = o[g][3] = 0.f;
+  for (int g = 0; g < kG; ++g) o[g][0] = o[g][1] = make_float2(0.f, 0.f);
 
   // Thread t owns rotation pair c = t % 8 (dims 8c .. 8c+7 and 64+8c ..
   // 64+8c+7) of keys t / 8 and t / 8 + 32 of every sub-tile; with at most
@@ -316,14 +316,18 @@ __global__ void __launch_bounds__(kThreads, 2)
   // reads of the queries would bound the loop otherwise).
   const int c = tid % 8;
   constexpr bool kQReg = kG <= 4;
-  float qa[kQReg ? kG : 1][8], qb[kQReg ? kG : 1][8];
+  // (pairs of dims in float2: the rotation, the dot products and the P.V
+  // accumulation run as packed fp32 FMAs, two dims an instruction)
+  float2 qa[kQReg ? kG : 1][4], qb[kQReg ? kG : 1][4];
   if (kQReg) {
 #pragma unroll
     for (int g = 0; g < (kQReg ? kG : 1); ++g)
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        qa[g][e] = g < G ? s_q[g * D + 8 * c + e] : 0.f;
-        qb[g][e] = g < G ? s_q[g * D + 64 + 8 * c + e] : 0.f;
+      for (int e = 0; e < 4; ++e) {
+        qa[g][e] = g < G ? make_float2(s_q[g * D + 8 * c + 2 * e], s_q[g * D + 8 * c + 2 * e + 1])
+                         : make_float2(0.f, 0.f);
+        qb[g][e] = g < G ? make_float2(s_q[g * D + 64 + 8 * c + 2 * e], s_q[g * D + 64 + 8 * c + 2 * e + 1])
+                         : make_float2(0.f, 0.f);
       }
   }
 
@@ -363,27 +367,36 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
       for (int g = 0; g < kG; ++g) acc[g] = 0.f;
       if (okk[hh]) {
-        float x1[8], x2[8];
-        unpack8(*reinterpret_cast<const uint4*>(kt + tile::chunk_off<kKeys>(kk, c)), x1);
-        unpack8(*reinterpret_cast<const uint4*>(kt + tile::chunk_off<kKeys>(kk, c + 8)), x2);
+        const uint4 ra = *reinterpret_cast<const uint4*>(kt + tile::chunk_off<kKeys>(kk, c));
+        const uint4 rb = *reinterpret_cast<const uint4*>(kt + tile::chunk_off<kKeys>(kk, c + 8));
+        const __nv_bfloat162* ka = reinterpret_cast<const __nv_bfloat162*>(&ra);
+        const __nv_bfloat162* kb = reinterpret_cast<const __nv_bfloat162*>(&rb);
         const __half2* h0 = reinterpret_cast<const __half2*>(&tt[hh][0]);
         const __half2* h1 = reinterpret_cast<const __half2*>(&tt[hh][1]);
-        float y1[8], y2[8];
+        float2 y1[4], y2[4];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float2 csn = __half22float2(e < 4 ? h0[e] : h1[e - 4]);
-          y1[e] = x1[e] * csn.x - x2[e] * csn.y;
-          y2[e] = x2[e] * csn.x + x1[e] * csn.y;
+        for (int e = 0; e < 4; ++e) {
+          const float2 x1 = __bfloat1622float2(ka[e]), x2 = __bfloat1622float2(kb[e]);
+          const float2 cs0 = __half22float2(e < 2 ? h0[2 * e] : h1[2 * e - 4]);      // (cos, sin) of dim 2e
+          const float2 cs1 = __half22float2(e < 2 ? h0[2 * e + 1] : h1[2 * e - 3]);  // of dim 2e + 1
+          const float2 cv = make_float2(cs0.x, cs1.x), sv = make_float2(cs0.y, cs1.y);
+          const float2 nsv = make_float2(-sv.x, -sv.y);
+          y1[e] = __ffma2_rn(x1, cv, __fmul2_rn(x2, nsv));
+          y2[e] = __ffma2_rn(x2, cv, __fmul2_rn(x1, sv));
         }
 #pragma unroll
         for (int g = 0; g < kG; ++g) {
           if (g < G) {
+            float2 a2 = make_float2(0.f, 0.f);
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const float q1 = kQReg ? qa[kQReg ? g : 0][e] : s_q[g * D + 8 * c + e];
-              const float q2 = kQReg ? qb[kQReg ? g : 0][e] : s_q[g * D + 64 + 8 * c + e];
-              acc[g] = fmaf(y1[e], q1, fmaf(y2[e], q2, acc[g]));
+            for (int e = 0; e < 4; ++e) {
+              const float2 q1 = kQReg ? qa[kQReg ? g : 0][e]
+                                      : make_float2(s_q[g * D + 8 * c + 2 * e], s_q[g * D + 8 * c + 2 * e + 1]);
+              const float2 q2 = kQReg ? qb[kQReg ? g : 0][e]
+                                      : make_float2(s_q[g * D + 64 + 8 * c + 2 * e], s_q[g * D + 64 + 8 * c + 2 * e + 1]);
+              a2 = __ffma2_rn(y1[e], q1, __ffma2_rn(y2[e], q2, a2));
             }
+            acc[g] = a2.x + a2.y;
           }
         }
       }
@@ -421,11 +434,9 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
       for (int g = 0; g < kG; ++g) {
         if (g < G) {
-          const float al = s_alpha[g];
-          o[g][0] *= al;
-          o[g][1] *= al;
-          o[g][2] *= al;
-          o[g][3] *= al;
+          const float2 al = make_float2(s_alpha[g], s_alpha[g]);
+          o[g][0] = __fmul2_rn(o[g][0], al);
+          o[g][1] = __fmul2_rn(o[g][1], al);
         }
       }
       const uint8_t* vt = sm + V0 + st * kTile;
@@ -440,10 +451,9 @@ __global__ void __launch_bounds__(kThreads, 2)
         for (int g = 0; g < kG; ++g) {
           if (g < G) {
             const float pv = s_p[g * kKeys + key];
-            o[g][0] = fmaf(pv, v01.x, o[g][0]);
-            o[g][1] = fmaf(pv, v01.y, o[g][1]);
-            o[g][2] = fmaf(pv, v23.x, o[g][2]);
-            o[g][3] = fmaf(pv, v23.y, o[g][3]);
+            const float2 p2 = make_float2(pv, pv);
+            o[g][0] = __ffma2_rn(p2, v01, o[g][0]);
+            o[g][1] = __ffma2_rn(p2, v23, o[g][1]);
           }
         }
       }
@@ -467,10 +477,10 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
   for (int g = 0; g < kG; ++g) {
     if (g >= G) break;  // (G is uniform: every thread leaves together)
-    s_o[warp * D + 4 * lane] = o[g][0];
-    s_o[warp * D + 4 * lane + 1] = o[g][1];
-    s_o[warp * D + 4 * lane + 2] = o[g][2];
-    s_o[warp * D + 4 * lane + 3] = o[g][3];
+    s_o[warp * D + 4 * lane] = o[g][0].x;
+    s_o[warp * D + 4 * lane + 1] = o[g][0].y;
+    s_o[warp * D + 4 * lane + 2] = o[g][1].x;
+    s_o[warp * D + 4 * lane + 3] = o[g][1].y;
     __syncthreads();
     float* dst = base + (int64_t)g * n_split * (2 + D);
     if (tid < D) {
