@@ -1164,7 +1164,17 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
       }
       if (done != w.n) break;
       // Epilogue: dQ = R(qpos)^T dQrot; dQ_t is released to the next unit's
-      // first dQ MMA once it has been read.
+      // first dQ MMA once it has been read.  The row's rotary entries are
+      // requested before the wait for the last dQ MMAs: each of these loads
+      // touches 32 table rows, and their latency (thousands of cycles with
+      // every warp of the CTA loading at once) would otherwise hold up the
+      // next unit's first tile.
+      uint4 tv_row[16];
+      if (!kAbs) {
+        const uint4* tab = reinterpret_cast<const uint4*>(cs16 + (int64_t)qrow * (D / 2));
+#pragma unroll
+        for (int q = 0; q < 16; ++q) tv_row[q] = __ldg(tab + q);
+      }
       bool have = false;
       if (w.n > 0) {
         have = wait(DQ_DONE + t, (uint32_t)ko & 1u);
@@ -1174,7 +1184,6 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
       ptx::tc_fence_after();
       __nv_bfloat16* dQrow = static_cast<__nv_bfloat16*>(a.dq.ptr) + b * a.dq.stride_b + h * a.dq.stride_h +
                              (int64_t)i * a.dq.stride_t;
-      const uint4* tab = reinterpret_cast<const uint4*>(cs16 + (int64_t)qrow * (D / 2));
 #pragma unroll
       for (int hf = 0; hf < 2; ++hf) {
         uint32_t g1[32], g2[32];
@@ -1210,7 +1219,7 @@ __global__ void __launch_bounds__(dqw::kThreads, 1)
         float o1[32], o2[32];
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
-          const uint4 tv = __ldg(tab + 8 * hf + q);
+          const uint4 tv = tv_row[8 * hf + q];
           const __half2* h2 = reinterpret_cast<const __half2*>(&tv);
 #pragma unroll
           for (int uu = 0; uu < 4; ++uu) {
