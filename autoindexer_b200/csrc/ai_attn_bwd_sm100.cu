@@ -461,9 +461,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const AiAttnFwdArgs& f = a.fwd;
   const AiAttnLayout& L = f.layout;
-  const int32_t* item = L.kv_items + 4 * (int64_t)blockIdx.x;
+  // One-dimensional grid, KV head fastest (entries costliest first).
+  const int32_t* item = L.kv_items + 4 * (int64_t)(blockIdx.x / (unsigned)f.num_kv_heads);
   const int b = item[0], j0 = item[1], j1 = item[2];
-  const int hk = blockIdx.y, G = f.num_q_heads / f.num_kv_heads;
+  const int hk = (int)(blockIdx.x % (unsigned)f.num_kv_heads), G = f.num_q_heads / f.num_kv_heads;
   const int j = j0 + tid;  // this thread's key
 
   if (tid == 0) {
@@ -1589,7 +1590,8 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_q,
                    const __grid_constant__ CUtensorMap tm_do, const __grid_constant__ CUtensorMap tm_kr,
                    const __grid_constant__ CUtensorMap tm_kc, const int prerot, const int item_base,
-                   const int skip_abs, const int32_t* __restrict__ chunks, float* __restrict__ partials) {
+                   const int skip_abs, const int32_t* __restrict__ chunks, float* __restrict__ partials,
+                   const int hg) {
   using namespace kvw;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = tile::align1024(smem_raw);
@@ -1604,9 +1606,17 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
   const AiAttnLayout& L = f.layout;
   // A CTA runs one key tile whole, or one chunk of its query tiles when the
   // tile is split (kv_chunks): then it writes fp32 partial sums to `partials`.
-  int it_idx = item_base + (int)blockIdx.x, qt0 = 0, qt1 = 0x7fffffff, slot = -1;
+  // CTA order (one-dimensional grid): the KV heads in groups of hg, one
+  // group after the other; within a group the entries in their order
+  // (costliest first) with the group's heads varying fastest.  A group's
+  // CTAs read the query / dO rows of its heads only, which then stay in L2,
+  // and its costliest entries start first, so its last wave holds short CTAs.
+  const unsigned per_grp = (gridDim.x / (unsigned)a.fwd.num_kv_heads) * (unsigned)hg;
+  const unsigned grp = blockIdx.x / per_grp, rem = blockIdx.x % per_grp;
+  const int ent = (int)(rem / (unsigned)hg);
+  int it_idx = item_base + ent, qt0 = 0, qt1 = 0x7fffffff, slot = -1;
   if (chunks) {
-    const int32_t* c = chunks + 4 * (int64_t)blockIdx.x;
+    const int32_t* c = chunks + 4 * (int64_t)ent;
     it_idx = c[0];
     qt0 = c[1];
     qt1 = c[2];
@@ -1614,7 +1624,7 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
   }
   const int32_t* item = L.kv_items + 4 * (int64_t)it_idx;
   const int b = item[0], j0 = item[1], j1 = item[2];
-  const int hk = blockIdx.y, G = f.num_q_heads / f.num_kv_heads;
+  const int hk = (int)(grp * (unsigned)hg + rem % (unsigned)hg), G = f.num_q_heads / f.num_kv_heads;
   const __half2* cs16 = static_cast<const __half2*>(L.rope_cs16);
 
   if (tid == 0) {
@@ -2267,7 +2277,13 @@ int sm100_bwd(const AiAttnBwdArgs& a, float* delta, void* rot, bool rot_ready, f
         // fill the SMs its CTAs leave; everything before that kernel is done.
         cudaLaunchConfig_t cfg = {};
         const bool split = partials != nullptr;
-        cfg.gridDim = dim3(split ? f.layout.n_kv_chunks : n_plain, f.num_kv_heads);
+        const unsigned n_ent = (unsigned)(split ? f.layout.n_kv_chunks : n_plain);
+        // Head groups as small as keep three waves of CTAs in a group.
+        int hg = 1, dev = 0, sms = 148;
+        if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        while (hg < f.num_kv_heads && f.num_kv_heads % (2 * hg) == 0 && (int64_t)n_ent * hg < 3 * (int64_t)sms)
+          hg *= 2;
+        cfg.gridDim = dim3(n_ent * (unsigned)f.num_kv_heads);
         cfg.blockDim = dim3(kvw::kThreads);
         cfg.dynamicSmemBytes = kvw::kSmem;
         cfg.stream = st;
@@ -2278,7 +2294,7 @@ int sm100_bwd(const AiAttnBwdArgs& a, float* delta, void* rot, bool rot_ready, f
         cfg.numAttrs = 1;
         e = cudaLaunchKernelEx(&cfg, dkdv_ws_kernel, a, (const float*)delta, tk, tv, pre ? tqr : tq, tdo, tkr, tkc,
                                pre ? 1 : 0, 0, n_abs > 0 ? 1 : 0, split ? f.layout.kv_chunks : (const int32_t*)nullptr,
-                               partials);
+                               partials, hg);
         if (e == cudaSuccess) e = cudaGetLastError();
         if (e == cudaSuccess && split && f.layout.n_kv_reduce > 0) {
           dkdv_reduce_kernel<<<dim3(f.layout.n_kv_reduce, f.num_kv_heads), 256, 0, st>>>(a, partials);
@@ -2299,7 +2315,7 @@ int sm100_bwd(const AiAttnBwdArgs& a, float* delta, void* rot, bool rot_ready, f
       e = cudaFuncSetAttribute(dkdv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kv::kSmem);
       if (e == cudaSuccess) {
         ProfScope ps(AI_PROF_DKDV, st);
-        dkdv_kernel<<<dim3(n_abs, f.num_kv_heads), kThreads, kv::kSmem, st>>>(a, delta, tk, tv, tq, tdo, tqp, tdop,
+        dkdv_kernel<<<dim3((unsigned)n_abs * (unsigned)f.num_kv_heads), kThreads, kv::kSmem, st>>>(a, delta, tk, tv, tq, tdo, tqp, tdop,
                                                                                tkc, tqr, tqrp, pre ? 1 : 0, 1);
         e = cudaGetLastError();
       }
