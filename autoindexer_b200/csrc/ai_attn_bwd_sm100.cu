@@ -116,7 +116,7 @@ constexpr uint32_t C_S = 0, C_DP = 64, C_DQR = 128, C_DQA = 256, C_SA = 384;
 __global__ void __launch_bounds__(kThreads, 1)
     dq_kernel(const AiAttnBwdArgs a, const float* __restrict__ delta, const __grid_constant__ CUtensorMap tm_k,
               const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_kc, const int prerot,
-              const float* __restrict__ part_dq) {
+              float* __restrict__ part_dq) {
   using namespace dq;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = tile::align1024(smem_raw);
@@ -132,9 +132,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   const Block blk = load_block(L.blocks, item[0]);
   const int q0 = item[1], q1 = item[2];
   // A short item packs P heads of the group into the tile (as the forward).
+  // With the abs split (part_dq given) the P CTAs y, y + Hq / P, ... of a
+  // head group each take one of P consecutive chunks of the item's abs tiles
+  // and leave their rows' dQ (fp32, rotated back) at row chunk * (128 / P) +
+  // r of the (item, head) slab, which dq_abs_combine_kernel sums.
   const int G = f.num_q_heads / f.num_kv_heads, P = pack_heads(q1 - q0, G), slot = BM / P;
-  if ((int)blockIdx.y * P >= f.num_q_heads) return;
-  const int h = (int)blockIdx.y * P + tid / slot, hk = ((int)blockIdx.y * P) / G, b = blk.row;
+  const bool chunked = part_dq != nullptr && P > 1;
+  int y = (int)blockIdx.y, chunk = 0;
+  if (chunked) {
+    chunk = y / (f.num_q_heads / P);
+    y %= f.num_q_heads / P;
+  } else if (y * P >= f.num_q_heads) {
+    return;
+  }
+  const int h = y * P + tid / slot, hk = (y * P) / G, b = blk.row;
   const bool has_abs = (blk.flags & AI_BLOCKF_ABS) != 0;
   const int kv_hi = min(blk.e, q1);
   const int i = q0 + tid % slot;
@@ -207,11 +218,19 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // With the abs split the persistent kernel has run this item's key tiles
   // without abs keys and left each row's dQrot (fp32): start the rotated
-  // accumulator from it and run the tiles that hold abs keys only.
-  const bool o_init = part_dq != nullptr;
+  // accumulator from it and run the tiles that hold abs keys only (chunk 0
+  // of a chunked item starts from the partial, the other chunks from zero).
+  const bool o_init = part_dq != nullptr && chunk == 0;
   int j_begin = 0, j_end = kv_hi > blk.kv_lo ? (kv_hi - blk.kv_lo + BN - 1) / BN : 0;
-  if (o_init) {
+  if (part_dq != nullptr) {
     abs_tiles(blk, blk.kv_lo, kv_hi, BN, j_begin, j_end);
+    if (chunked) {
+      const int n = j_end - j_begin, jb = j_begin;
+      j_begin = jb + n * chunk / P;
+      j_end = jb + n * (chunk + 1) / P;
+    }
+  }
+  if (o_init) {
     const bool have = i < q1;
     const float* prow = part_dq + (((int64_t)blockIdx.x * f.num_q_heads + h) * BM + (i - q0)) * D;
 #pragma unroll
@@ -400,7 +419,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         o1[x] = y1;
         o2[x] = y2;
       }
-      if (i < q1) {
+      if (i < q1 && chunked) {
+        float* prow = part_dq + (((int64_t)blockIdx.x * f.num_q_heads + h) * BM + chunk * slot + (i - q0)) * D;
+#pragma unroll
+        for (int x = 0; x < 32; x += 4) {
+          *reinterpret_cast<float4*>(prow + 32 * half + x) = make_float4(o1[x], o1[x + 1], o1[x + 2], o1[x + 3]);
+          *reinterpret_cast<float4*>(prow + 64 + 32 * half + x) = make_float4(o2[x], o2[x + 1], o2[x + 2], o2[x + 3]);
+        }
+      } else if (i < q1) {
         store_bf16_row32(dQrow + 32 * half, o1);
         store_bf16_row32(dQrow + 64 + 32 * half, o2);
       }
@@ -411,6 +437,27 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// Sums the P chunk rows dq_kernel left for the abs items it ran chunked
+// (P = heads packed per tile > 1), in chunk order, into the bf16 dQ rows.
+// Grid (abs items, query heads); thread d owns dimension d of every row.
+__global__ void __launch_bounds__(D) dq_abs_combine_kernel(const AiAttnBwdArgs a, const float* __restrict__ part_dq) {
+  const AiAttnFwdArgs& f = a.fwd;
+  const AiAttnLayout& L = f.layout;
+  const int it = (int)blockIdx.x, h = (int)blockIdx.y, d = (int)threadIdx.x;
+  const int32_t* item = L.fwd_items + 4 * (int64_t)it;
+  const int b = load_block(L.blocks, item[0]).row, q0 = item[1], q1 = item[2];
+  const int G = f.num_q_heads / f.num_kv_heads, P = pack_heads(q1 - q0, G), slot = dq::BM / P;
+  if (P == 1) return;  // written whole by dq_kernel
+  const int64_t base = ((int64_t)it * f.num_q_heads + h) * dq::BM;
+  for (int r = 0; r < q1 - q0; ++r) {
+    float g = 0.f;
+    for (int c = 0; c < P; ++c) g += part_dq[(base + c * slot + r) * D + d];
+    __nv_bfloat16* dQrow = static_cast<__nv_bfloat16*>(a.dq.ptr) + b * a.dq.stride_b + h * a.dq.stride_h +
+                           (int64_t)(q0 + r) * a.dq.stride_t;
+    dQrow[d] = __float2bfloat16_rn(g);
   }
 }
 
@@ -2244,6 +2291,11 @@ int sm100_bwd(const AiAttnBwdArgs& a, float* delta, void* rot, bool rot_ready, f
       dq_kernel<<<dim3(f.layout.n_fwd_abs_items, f.num_q_heads), kThreads, dq::kSmem, st>>>(
           a, delta, dq_tk, dq_tv, dq_tkc, 1, dq_part);
       e = cudaGetLastError();
+      // The short abs items ran chunked: sum their chunks' rows.
+      if (e == cudaSuccess) {
+        dq_abs_combine_kernel<<<dim3(f.layout.n_fwd_abs_items, f.num_q_heads), D, 0, st>>>(a, dq_part);
+        e = cudaGetLastError();
+      }
     }
   };
   if (e == cudaSuccess && do_kv && f.layout.n_kv_items > 0) {

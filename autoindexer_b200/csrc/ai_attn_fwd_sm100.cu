@@ -75,8 +75,8 @@ __device__ __forceinline__ uint32_t chunk_off(int r, int c) { return tile::chunk
 
 __global__ void __launch_bounds__(kThreads, 1)
     fwd_kernel(const AiAttnFwdArgs a, const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
-               const __grid_constant__ CUtensorMap tm_kc, const int prerot, const float* __restrict__ part_o,
-               const float* __restrict__ part_lse) {
+               const __grid_constant__ CUtensorMap tm_kc, const int prerot, float* __restrict__ part_o,
+               float* __restrict__ part_lse) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = tile::align1024(smem_raw);
   const uint32_t sbase = ptx::smem_u32(sm);
@@ -90,11 +90,23 @@ __global__ void __launch_bounds__(kThreads, 1)
   const Block blk = load_block(L.blocks, item[0]);
   const int q0 = item[1], q1 = item[2];
   // A short item packs P heads of the group into the tile: thread tid is row
-  // tid % (128 / P) of head blockIdx.y * P + tid / (128 / P); the CTAs of
-  // the heads that others took return at once.
+  // tid % (128 / P) of head y * P + tid / (128 / P).  Without the abs split
+  // the CTAs y >= Hq / P return at once.  With it (part_o given), the P CTAs
+  // y, y + Hq / P, ... of a head group each take one of P consecutive chunks
+  // of the item's abs tiles and leave a partial row in the workspace at row
+  // chunk * (128 / P) + r of the (item, head) slab, which
+  // fwd_abs_combine_kernel merges: the longest abs ranges (up to a whole
+  // edit chain's keys) no longer run serially on one SM.
   const int G = a.num_q_heads / a.num_kv_heads, P = pack_heads(q1 - q0, G), slot = BM / P;
-  if ((int)blockIdx.y * P >= a.num_q_heads) return;
-  const int h = (int)blockIdx.y * P + tid / slot, hk = ((int)blockIdx.y * P) / G, b = blk.row;
+  const bool chunked = part_o != nullptr && P > 1;
+  int y = (int)blockIdx.y, chunk = 0;
+  if (chunked) {
+    chunk = y / (a.num_q_heads / P);
+    y %= a.num_q_heads / P;
+  } else if (y * P >= a.num_q_heads) {
+    return;
+  }
+  const int h = y * P + tid / slot, hk = (y * P) / G, b = blk.row;
   const bool has_abs = (blk.flags & AI_BLOCKF_ABS) != 0;
   const int kv_hi = min(blk.e, q1);
   // The block's rotation classes: K tiles whose two chunks have one come rotated.
@@ -157,11 +169,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   // With the abs split the persistent kernel has run this item's key tiles
   // without abs keys and left each row's (O / l, log2-sum) partial: start
   // the online softmax from it (m = that sum, l = 1, O = the partial) and
-  // run the tiles that hold abs keys only.
-  const bool o_init = part_o != nullptr;
+  // run the tiles that hold abs keys only (chunk 0 of a chunked item starts
+  // from the partial, the other chunks from nothing).
+  const bool o_init = part_o != nullptr && chunk == 0;
   int j_begin = 0, j_end = kv_hi > blk.kv_lo ? (kv_hi - blk.kv_lo + BN - 1) / BN : 0;
-  if (o_init) {
+  if (part_o != nullptr) {
     abs_tiles(blk, blk.kv_lo, kv_hi, BN, j_begin, j_end);
+    if (chunked) {
+      const int n = j_end - j_begin, jb = j_begin;
+      j_begin = jb + n * chunk / P;
+      j_end = jb + n * (chunk + 1) / P;
+    }
+  }
+  if (o_init) {
     const int64_t prow = ((int64_t)blockIdx.x * a.num_q_heads + h) * BM + (i - q0);
     const bool have = i < q1;
     const float lp = have ? part_lse[prow] : -CUDART_INF_F;
@@ -370,8 +390,31 @@ __global__ void __launch_bounds__(kThreads, 1)
     ++n_tiles;
   }
 
-  // Epilogue: O / l -> bf16 row, lse.
-  if (!aborted) {
+  // Epilogue: O / l -> bf16 row, lse; a chunk leaves its partial row
+  // (O / l in fp32, log2-sum) for fwd_abs_combine_kernel instead.
+  if (!aborted && chunked) {
+    const float inv = l > 0.f ? 1.f / l : 0.f;
+    const int64_t prow = ((int64_t)blockIdx.x * a.num_q_heads + h) * BM + chunk * slot + (i - q0);
+#pragma unroll
+    for (int cc = 0; cc < D / 32; ++cc) {
+      uint32_t r[32];
+      if (n_tiles > 0 || o_init) {
+        ptx::tmem_ld32(tmem + lane_base + kColO + 32 * cc, r);
+        ptx::tmem_wait_ld();
+      } else {
+#pragma unroll
+        for (int x = 0; x < 32; ++x) r[x] = 0u;
+      }
+      if (i < q1) {
+#pragma unroll
+        for (int x = 0; x < 32; x += 4)
+          *reinterpret_cast<float4*>(part_o + prow * D + 32 * cc + x) =
+              make_float4(__uint_as_float(r[x]) * inv, __uint_as_float(r[x + 1]) * inv,
+                          __uint_as_float(r[x + 2]) * inv, __uint_as_float(r[x + 3]) * inv);
+      }
+    }
+    if (i < q1) part_lse[prow] = l > 0.f ? m_use + log2f(l) : -CUDART_INF_F;
+  } else if (!aborted) {
     __nv_bfloat16* Orow =
         static_cast<__nv_bfloat16*>(a.out.ptr) + b * a.out.stride_b + h * a.out.stride_h + (int64_t)i * a.out.stride_t;
     const float inv = l > 0.f ? 1.f / l : 0.f;
@@ -404,6 +447,49 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// Merges the P chunk partials fwd_kernel left for the abs items it ran
+// chunked (P = heads packed per tile > 1): per row, in chunk order (so the
+// result does not depend on the launch order of the chunks),
+//   lse2 = log2 sum_c 2^lse2_c,  O = sum_c 2^(lse2_c - lse2) (O / l)_c,
+// then the bf16 output row and lse.  Grid (abs items, query heads); thread d
+// owns dimension d of every row of the item.
+__global__ void __launch_bounds__(D) fwd_abs_combine_kernel(const AiAttnFwdArgs a, const float* __restrict__ part_o,
+                                                             const float* __restrict__ part_lse) {
+  const AiAttnLayout& L = a.layout;
+  const int it = (int)blockIdx.x, h = (int)blockIdx.y, d = (int)threadIdx.x;
+  const int32_t* item = L.fwd_items + 4 * (int64_t)it;
+  const int b = load_block(L.blocks, item[0]).row, q0 = item[1], q1 = item[2];
+  const int G = a.num_q_heads / a.num_kv_heads, P = pack_heads(q1 - q0, G), slot = BM / P;
+  if (P == 1) return;  // run whole by fwd_kernel
+  const int64_t base = ((int64_t)it * a.num_q_heads + h) * BM;
+  for (int r = 0; r < q1 - q0; ++r) {
+    float l2[4], m = -CUDART_INF_F;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      l2[c] = c < P ? part_lse[base + c * slot + r] : -CUDART_INF_F;
+      m = fmaxf(m, l2[c]);
+    }
+    float o = 0.f, w_sum = 0.f;
+    if (m > -CUDART_INF_F) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        if (c < P && l2[c] > -CUDART_INF_F) {
+          const float w = exp2f(l2[c] - m);
+          w_sum += w;
+          o += w * part_o[(base + c * slot + r) * D + d];
+        }
+      }
+    }
+    const int i = q0 + r;
+    __nv_bfloat16* Orow =
+        static_cast<__nv_bfloat16*>(a.out.ptr) + b * a.out.stride_b + h * a.out.stride_h + (int64_t)i * a.out.stride_t;
+    Orow[d] = __float2bfloat16_rn(w_sum > 0.f ? o / w_sum : 0.f);
+    if (d == 0)
+      a.lse[((int64_t)b * a.num_q_heads + h) * a.seq_len + i] =
+          w_sum > 0.f ? (m + log2f(w_sum)) * kLn2 : -CUDART_INF_F;
   }
 }
 
@@ -1242,6 +1328,12 @@ int sm100_fwd(const AiAttnFwdArgs& a, cudaStream_t st, cudaError_t* cuda_err) {
     if (split) launch_pers(fwd_pers_kernel<true>, up_abs, false);
     launch_pers(fwd_pers_kernel<false>, up, split && up_abs.n_units > 0);
     if (e == cudaSuccess) launch_single();
+    // With the split, short abs items ran chunked: merge their partial rows.
+    if (e == cudaSuccess && split && n_single > 0) {
+      ProfScope ps(AI_PROF_FWD, st);
+      fwd_abs_combine_kernel<<<dim3(n_single, a.num_q_heads), D, 0, st>>>(a, part_o, part_lse);
+      e = cudaGetLastError();
+    }
   }
   if (cuda_err) *cuda_err = e;
   return e == cudaSuccess ? AI_OK : AI_ERR_LAUNCH;
