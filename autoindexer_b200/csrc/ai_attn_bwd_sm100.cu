@@ -48,6 +48,8 @@ constexpr int D = 128;
 constexpr int kThreads = 128;
 constexpr uint32_t kTmemCols = 512;
 constexpr long long kWaitCycles = 4000000000LL;
+// Fewest 64-key abs tiles a chunk of a short abs item takes in dq_kernel.
+constexpr int kDqChunkTiles = 4;
 
 using tile::chunk_off;
 using tile::pack8;
@@ -133,21 +135,28 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int q0 = item[1], q1 = item[2];
   // A short item packs P heads of the group into the tile (as the forward).
   // With the abs split (part_dq given) the P CTAs y, y + Hq / P, ... of a
-  // head group each take one of P consecutive chunks of the item's abs tiles
-  // and leave their rows' dQ (fp32, rotated back) at row chunk * (128 / P) +
-  // r of the (item, head) slab, which dq_abs_combine_kernel sums.
+  // head group each take one of up to P consecutive chunks of the item's abs
+  // tiles (abs_chunks) and leave their rows' dQ (fp32, rotated back) at row
+  // chunk * (128 / P) + r of the (item, head) slab, which
+  // dq_abs_combine_kernel sums.
+  // An abs range shorter than two chunks of kDqChunkTiles stays whole on
+  // chunk 0's CTA (the others return at once).
   const int G = f.num_q_heads / f.num_kv_heads, P = pack_heads(q1 - q0, G), slot = BM / P;
-  const bool chunked = part_dq != nullptr && P > 1;
-  int y = (int)blockIdx.y, chunk = 0;
-  if (chunked) {
+  const int kv_hi = min(blk.e, q1);
+  int y = (int)blockIdx.y, chunk = 0, n_chunks = 1;
+  if (part_dq != nullptr && P > 1) {
     chunk = y / (f.num_q_heads / P);
     y %= f.num_q_heads / P;
+    int ja, jb;
+    abs_tiles(blk, blk.kv_lo, kv_hi, BN, ja, jb);
+    n_chunks = abs_chunks(jb - ja, P, kDqChunkTiles);
+    if (chunk >= n_chunks) return;
   } else if (y * P >= f.num_q_heads) {
     return;
   }
+  const bool chunked = n_chunks > 1;
   const int h = y * P + tid / slot, hk = (y * P) / G, b = blk.row;
   const bool has_abs = (blk.flags & AI_BLOCKF_ABS) != 0;
-  const int kv_hi = min(blk.e, q1);
   const int i = q0 + tid % slot;
   // The block's rotation classes: a 64-key tile with one comes rotated.
   const int cls = block_classes(L, item[0], prerot != 0);
@@ -226,8 +235,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     abs_tiles(blk, blk.kv_lo, kv_hi, BN, j_begin, j_end);
     if (chunked) {
       const int n = j_end - j_begin, jb = j_begin;
-      j_begin = jb + n * chunk / P;
-      j_end = jb + n * (chunk + 1) / P;
+      j_begin = jb + n * chunk / n_chunks;
+      j_end = jb + n * (chunk + 1) / n_chunks;
     }
   }
   if (o_init) {
@@ -440,21 +449,27 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// Sums the P chunk rows dq_kernel left for the abs items it ran chunked
-// (P = heads packed per tile > 1), in chunk order, into the bf16 dQ rows.
+// Sums the chunk rows dq_kernel left for the abs items it ran chunked
+// (P = heads packed per tile > 1, more than one chunk), in chunk order, into
+// the bf16 dQ rows.
 // Grid (abs items, query heads); thread d owns dimension d of every row.
 __global__ void __launch_bounds__(D) dq_abs_combine_kernel(const AiAttnBwdArgs a, const float* __restrict__ part_dq) {
   const AiAttnFwdArgs& f = a.fwd;
   const AiAttnLayout& L = f.layout;
   const int it = (int)blockIdx.x, h = (int)blockIdx.y, d = (int)threadIdx.x;
   const int32_t* item = L.fwd_items + 4 * (int64_t)it;
-  const int b = load_block(L.blocks, item[0]).row, q0 = item[1], q1 = item[2];
+  const Block blk = load_block(L.blocks, item[0]);
+  const int b = blk.row, q0 = item[1], q1 = item[2];
   const int G = f.num_q_heads / f.num_kv_heads, P = pack_heads(q1 - q0, G), slot = dq::BM / P;
   if (P == 1) return;  // written whole by dq_kernel
+  int ja, jb;
+  abs_tiles(blk, blk.kv_lo, min(blk.e, q1), dq::BN, ja, jb);
+  const int nc = abs_chunks(jb - ja, P, kDqChunkTiles);
+  if (nc == 1) return;  // finished by its one CTA
   const int64_t base = ((int64_t)it * f.num_q_heads + h) * dq::BM;
   for (int r = 0; r < q1 - q0; ++r) {
     float g = 0.f;
-    for (int c = 0; c < P; ++c) g += part_dq[(base + c * slot + r) * D + d];
+    for (int c = 0; c < nc; ++c) g += part_dq[(base + c * slot + r) * D + d];
     __nv_bfloat16* dQrow = static_cast<__nv_bfloat16*>(a.dq.ptr) + b * a.dq.stride_b + h * a.dq.stride_h +
                            (int64_t)(q0 + r) * a.dq.stride_t;
     dQrow[d] = __float2bfloat16_rn(g);
@@ -2330,10 +2345,15 @@ int sm100_bwd(const AiAttnBwdArgs& a, float* delta, void* rot, bool rot_ready, f
         cudaLaunchConfig_t cfg = {};
         const bool split = partials != nullptr;
         const unsigned n_ent = (unsigned)(split ? f.layout.n_kv_chunks : n_plain);
-        // Head groups as small as keep three waves of CTAs in a group.
+        // Head groups as small as keep one and a half waves of CTAs in a
+        // group: smaller groups keep a group's query / dO rows in L2, larger
+        // ones shorten the tail of each group's last wave (measured on B200:
+        // config 1 takes groups of two KV heads, 0.424 ms against 0.435 ms
+        // with four; config 4 one head, 2.10 ms against 2.16 ms with two;
+        // configs 2a and 3 run alike with groups of 4 or 8, 1 or 2).
         int hg = 1, dev = 0, sms = 148;
         if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        while (hg < f.num_kv_heads && f.num_kv_heads % (2 * hg) == 0 && (int64_t)n_ent * hg < 3 * (int64_t)sms)
+        while (hg < f.num_kv_heads && f.num_kv_heads % (2 * hg) == 0 && (int64_t)n_ent * hg * 2 < 3 * (int64_t)sms)
           hg *= 2;
         cfg.gridDim = dim3(n_ent * (unsigned)f.num_kv_heads);
         cfg.blockDim = dim3(kvw::kThreads);

@@ -52,6 +52,9 @@ constexpr uint32_t kTile = 2 * kHalf;  // 128 rows x 128 bf16
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0, kColSabs = 128, kColO = 256;
 constexpr long long kWaitCycles = 4000000000LL;
+// Fewest 128-key abs tiles a chunk of a short abs item takes (a chunk costs
+// its CTA's set-up and a partial row on top of its tiles).
+constexpr int kFwdChunkTiles = 2;
 
 struct Smem {
   static constexpr uint32_t Q = 0;
@@ -92,23 +95,29 @@ __global__ void __launch_bounds__(kThreads, 1)
   // A short item packs P heads of the group into the tile: thread tid is row
   // tid % (128 / P) of head y * P + tid / (128 / P).  Without the abs split
   // the CTAs y >= Hq / P return at once.  With it (part_o given), the P CTAs
-  // y, y + Hq / P, ... of a head group each take one of P consecutive chunks
-  // of the item's abs tiles and leave a partial row in the workspace at row
-  // chunk * (128 / P) + r of the (item, head) slab, which
-  // fwd_abs_combine_kernel merges: the longest abs ranges (up to a whole
-  // edit chain's keys) no longer run serially on one SM.
+  // y, y + Hq / P, ... of a head group each take one of up to P consecutive
+  // chunks of the item's abs tiles (abs_chunks) and leave a partial row in
+  // the workspace at row chunk * (128 / P) + r of the (item, head) slab,
+  // which fwd_abs_combine_kernel merges: the longest abs ranges (up to a
+  // whole edit chain's keys) no longer run serially on one SM.
+  // An abs range shorter than two chunks of kFwdChunkTiles stays whole on
+  // chunk 0's CTA (the others return at once).
   const int G = a.num_q_heads / a.num_kv_heads, P = pack_heads(q1 - q0, G), slot = BM / P;
-  const bool chunked = part_o != nullptr && P > 1;
-  int y = (int)blockIdx.y, chunk = 0;
-  if (chunked) {
+  const int kv_hi = min(blk.e, q1);
+  int y = (int)blockIdx.y, chunk = 0, n_chunks = 1;
+  if (part_o != nullptr && P > 1) {
     chunk = y / (a.num_q_heads / P);
     y %= a.num_q_heads / P;
+    int ja, jb;
+    abs_tiles(blk, blk.kv_lo, kv_hi, BN, ja, jb);
+    n_chunks = abs_chunks(jb - ja, P, kFwdChunkTiles);
+    if (chunk >= n_chunks) return;
   } else if (y * P >= a.num_q_heads) {
     return;
   }
+  const bool chunked = n_chunks > 1;
   const int h = y * P + tid / slot, hk = (y * P) / G, b = blk.row;
   const bool has_abs = (blk.flags & AI_BLOCKF_ABS) != 0;
-  const int kv_hi = min(blk.e, q1);
   // The block's rotation classes: K tiles whose two chunks have one come rotated.
   const int cls = block_classes(L, item[0], prerot != 0);
 
@@ -177,8 +186,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     abs_tiles(blk, blk.kv_lo, kv_hi, BN, j_begin, j_end);
     if (chunked) {
       const int n = j_end - j_begin, jb = j_begin;
-      j_begin = jb + n * chunk / P;
-      j_end = jb + n * (chunk + 1) / P;
+      j_begin = jb + n * chunk / n_chunks;
+      j_end = jb + n * (chunk + 1) / n_chunks;
     }
   }
   if (o_init) {
@@ -450,9 +459,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// Merges the P chunk partials fwd_kernel left for the abs items it ran
-// chunked (P = heads packed per tile > 1): per row, in chunk order (so the
-// result does not depend on the launch order of the chunks),
+// Merges the chunk partials fwd_kernel left for the abs items it ran
+// chunked (P = heads packed per tile > 1, more than one chunk): per row, in
+// chunk order (so the result does not depend on the launch order of the
+// chunks),
 //   lse2 = log2 sum_c 2^lse2_c,  O = sum_c 2^(lse2_c - lse2) (O / l)_c,
 // then the bf16 output row and lse.  Grid (abs items, query heads); thread d
 // owns dimension d of every row of the item.
@@ -461,22 +471,27 @@ __global__ void __launch_bounds__(D) fwd_abs_combine_kernel(const AiAttnFwdArgs 
   const AiAttnLayout& L = a.layout;
   const int it = (int)blockIdx.x, h = (int)blockIdx.y, d = (int)threadIdx.x;
   const int32_t* item = L.fwd_items + 4 * (int64_t)it;
-  const int b = load_block(L.blocks, item[0]).row, q0 = item[1], q1 = item[2];
+  const Block blk = load_block(L.blocks, item[0]);
+  const int b = blk.row, q0 = item[1], q1 = item[2];
   const int G = a.num_q_heads / a.num_kv_heads, P = pack_heads(q1 - q0, G), slot = BM / P;
   if (P == 1) return;  // run whole by fwd_kernel
+  int ja, jb;
+  abs_tiles(blk, blk.kv_lo, min(blk.e, q1), BN, ja, jb);
+  const int nc = abs_chunks(jb - ja, P, kFwdChunkTiles);
+  if (nc == 1) return;  // finished by its one CTA
   const int64_t base = ((int64_t)it * a.num_q_heads + h) * BM;
   for (int r = 0; r < q1 - q0; ++r) {
     float l2[4], m = -CUDART_INF_F;
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
-      l2[c] = c < P ? part_lse[base + c * slot + r] : -CUDART_INF_F;
+      l2[c] = c < nc ? part_lse[base + c * slot + r] : -CUDART_INF_F;
       m = fmaxf(m, l2[c]);
     }
     float o = 0.f, w_sum = 0.f;
     if (m > -CUDART_INF_F) {
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
-        if (c < P && l2[c] > -CUDART_INF_F) {
+        if (c < nc && l2[c] > -CUDART_INF_F) {
           const float w = exp2f(l2[c] - m);
           w_sum += w;
           o += w * part_o[(base + c * slot + r) * D + d];

@@ -109,6 +109,15 @@ __device__ __forceinline__ void abs_tiles(const Block& blk, int kv_lo, int kv_hi
   }
 }
 
+// Number of CTAs that share the n abs tiles of a short abs item whose tile
+// packs P heads (P CTAs per head group are launched): up to P chunks of at
+// least min_tiles tiles each, 1 when the range is shorter (that CTA writes
+// the final rows itself).  Chunk c takes tiles [n c / k, n (c + 1) / k).
+__device__ __forceinline__ int abs_chunks(int n, int P, int min_tiles) {
+  const int k = n / min_tiles;
+  return k < 1 ? 1 : (k < P ? k : P);
+}
+
 // First chunk_cls entry of a block's rotation classes, or -1 when the block
 // has none or the rotated copies are not in the workspace (`prerot` false).
 __device__ __forceinline__ int block_classes(const AiAttnLayout& L, int block, bool prerot) {
