@@ -58,9 +58,10 @@ WORKLOAD = ("cfg1: bf16 B=4 T=4096 Hq=32 Hkv=8 D=128 theta=1e6, docs U[256,2048]
 METRIC = "multi-seg RoPE attn fwd+bwd TFLOP/s (causal-adjusted, 14*D*pairs*Hq)"
 DOM_KERNEL_NAMES = {"fwd": "fwd_pers_kernel (forward)", "dq": "dq_pers_kernel (dQ)", "dkdv": "dkdv_ws_kernel (dK/dV)",
                     "simt": "simt fp32 kernels (forward + backward)"}
-# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch on the
-# config-1 workload, from one ncu capture of the three kernels (profiles/).
-TRAFFIC_BYTES = {"fwd": 368016640, "dq": 549332224, "dkdv": 401622016}
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the
+# dominant kernel on the config-1 workload, from one ncu capture of it
+# (profiles/cfg1_dkdv_ws_kernel_full.md).
+TRAFFIC_BYTES = {"dkdv": 408681728}
 REF_PATH = os.path.join(ROOT, "baseline", "_ref")
 
 
