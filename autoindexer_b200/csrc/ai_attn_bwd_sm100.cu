@@ -105,9 +105,11 @@ constexpr uint32_t KR = DO + 32768;   // 64 keys x 128, rotated in place
 constexpr uint32_t VV = KR + 16384;   // 64 keys x 128
 constexpr uint32_t DS = VV + 16384;   // 128 rows x 64 keys: dS on non-abs keys
 constexpr uint32_t DSA = DS + 16384;  // dS on abs keys
-constexpr uint32_t INFO = DSA + 16384;
-constexpr uint32_t BAR_TMA = INFO + 4 * BN;
-constexpr uint32_t BAR_MMA = BAR_TMA + 8;
+constexpr uint32_t KR1 = DSA + 16384;  // second K / V buffer: tile j + 1 loads while tile j runs
+constexpr uint32_t VV1 = KR1 + 16384;
+constexpr uint32_t INFO = VV1 + 16384;
+constexpr uint32_t BAR_TMA = INFO + 4 * BN;  // two barriers, one per K / V buffer
+constexpr uint32_t BAR_MMA = BAR_TMA + 16;
 constexpr uint32_t TMEM_SLOT = BAR_MMA + 8;
 constexpr uint32_t ABORT = TMEM_SLOT + 4;
 constexpr uint32_t TOTAL = ABORT + 4;
@@ -161,13 +163,51 @@ __global__ void __launch_bounds__(kThreads, 1)
   // The block's rotation classes: a 64-key tile with one comes rotated.
   const int cls = block_classes(L, item[0], prerot != 0);
 
+  // Key tiles of this CTA: the block's, or with the abs split only those
+  // holding abs keys (chunk 0 of a chunked item starts from the persistent
+  // kernel's partial, the other chunks from zero).
+  const bool o_init = part_dq != nullptr && chunk == 0;
+  int j_begin = 0, j_end = kv_hi > blk.kv_lo ? (kv_hi - blk.kv_lo + BN - 1) / BN : 0;
+  if (part_dq != nullptr) {
+    abs_tiles(blk, blk.kv_lo, kv_hi, BN, j_begin, j_end);
+    if (chunked) {
+      const int n = j_end - j_begin, jb = j_begin;
+      j_begin = jb + n * chunk / n_chunks;
+      j_end = jb + n * (chunk + 1) / n_chunks;
+    }
+  }
+
+  // K and V of tile jt into buffer `buf` by TMA (K from its class copy when
+  // it has one).  Tile jt + 1 loads while tile jt runs; its buffer was last
+  // read by tile jt - 1's MMAs, complete by then.
+  auto issue_tile = [&](int jt, int buf) {
+    const int k0 = blk.kv_lo + jt * BN;
+    const int kc = cls >= 0 ? chunk_class(L, cls, jt, f.status) : -1;
+    const uint32_t kb = sbase + (buf ? KR1 : KR), vb = sbase + (buf ? VV1 : VV);
+    const uint32_t bt = bar_tma + 8u * (uint32_t)buf;
+    ptx::fence_proxy_async_smem();
+    ptx::mbar_arrive_expect_tx(bt, 2 * 16384);
+    if (kc >= 0) {
+      ptx::tma_load_4d(kb, &tm_kc, bt, 0, 0, hk, kc);
+      ptx::tma_load_4d(kb + 8192, &tm_kc, bt, 64, 0, hk, kc);
+    } else {
+      ptx::tma_load_4d(kb, &tm_k, bt, 0, k0, hk, b);
+      ptx::tma_load_4d(kb + 8192, &tm_k, bt, 64, k0, hk, b);
+    }
+    ptx::tma_load_4d(vb, &tm_v, bt, 0, k0, hk, b);
+    ptx::tma_load_4d(vb + 8192, &tm_v, bt, 64, k0, hk, b);
+  };
+
   if (tid == 0) {
     ptx::mbar_init(bar_tma, 1);
+    ptx::mbar_init(bar_tma + 8, 1);
     ptx::mbar_init(bar_mma, 1);
     *s_abort = 0;
     ptx::fence_mbar_init();
     ptx::prefetch_tmap(&tm_k);
     ptx::prefetch_tmap(&tm_v);
+    // The first tile loads while the query rows are set up.
+    if (j_begin < j_end) issue_tile(j_begin, 0);
   }
   if (warp == 0) {
     ptx::tmem_alloc(sbase + TMEM_SLOT, kTmemCols);
@@ -221,24 +261,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr uint32_t idesc_s = ptx::idesc_bf16_f32(BM, BN, false, false);
   constexpr uint32_t idesc_dq = ptx::idesc_bf16_f32(BM, D, false, true);
   const float sl2 = f.scale * kLog2e;
-  uint32_t ph_tma = 0, ph_mma = 0;
+  uint32_t ph_tma = 0, ph_mma = 0;  // ph_tma: bit b = phase of K / V buffer b
   int n_tiles = 0;
   bool aborted = false, dqa_started = false;
 
   // With the abs split the persistent kernel has run this item's key tiles
   // without abs keys and left each row's dQrot (fp32): start the rotated
-  // accumulator from it and run the tiles that hold abs keys only (chunk 0
-  // of a chunked item starts from the partial, the other chunks from zero).
-  const bool o_init = part_dq != nullptr && chunk == 0;
-  int j_begin = 0, j_end = kv_hi > blk.kv_lo ? (kv_hi - blk.kv_lo + BN - 1) / BN : 0;
-  if (part_dq != nullptr) {
-    abs_tiles(blk, blk.kv_lo, kv_hi, BN, j_begin, j_end);
-    if (chunked) {
-      const int n = j_end - j_begin, jb = j_begin;
-      j_begin = jb + n * chunk / n_chunks;
-      j_end = jb + n * (chunk + 1) / n_chunks;
-    }
-  }
+  // accumulator from it and run the tiles that hold abs keys only.
   if (o_init) {
     const bool have = i < q1;
     const float* prow = part_dq + (((int64_t)blockIdx.x * f.num_q_heads + h) * BM + (i - q0)) * D;
@@ -265,38 +294,31 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Only a tile that holds one of the block's abs keys needs S_abs and dQabs.
     const bool tabs = blk.abs_in(k0, min(k0 + BN, kv_hi));
     const int kc = cls >= 0 ? chunk_class(L, cls, jt, f.status) : -1;
-    if (tid == 0) {
-      ptx::fence_proxy_async_smem();
-      ptx::mbar_arrive_expect_tx(bar_tma, 2 * 16384);
-      if (kc >= 0) {
-        ptx::tma_load_4d(sbase + KR, &tm_kc, bar_tma, 0, 0, hk, kc);
-        ptx::tma_load_4d(sbase + KR + 8192, &tm_kc, bar_tma, 64, 0, hk, kc);
-      } else {
-        ptx::tma_load_4d(sbase + KR, &tm_k, bar_tma, 0, k0, hk, b);
-        ptx::tma_load_4d(sbase + KR + 8192, &tm_k, bar_tma, 64, k0, hk, b);
-      }
-      ptx::tma_load_4d(sbase + VV, &tm_v, bar_tma, 0, k0, hk, b);
-      ptx::tma_load_4d(sbase + VV + 8192, &tm_v, bar_tma, 64, k0, hk, b);
-    }
-    wait_or_flag(bar_tma, ph_tma, s_abort, f.status);
+    const int buf = (jt - j_begin) & 1;
+    const uint32_t KC = buf ? KR1 : KR, VC = buf ? VV1 : VV;
+    // The next tile's K and V start loading (this tile's were requested one
+    // tile ago); key row r's flags are read meanwhile.
+    if (tid == 0 && jt + 1 < j_end) issue_tile(jt + 1, buf ^ 1);
+    const int r = tid & 63, cg = tid >> 6, j = k0 + r;
+    const uint32_t info = j < kv_hi ? (uint32_t)L.key_info[blk.key_off + j] : 0u;
+    uint32_t ph = (ph_tma >> buf) & 1u;
+    wait_or_flag(bar_tma + 8u * (uint32_t)buf, ph, s_abort, f.status);
+    ph_tma ^= 1u << buf;
     __syncthreads();
     if (*s_abort) { aborted = true; break; }
 
     // Rotate key rows in place (fp16 (cos, sin) table, as the rotated copies
     // are made): thread -> (row tid % 64, chunk pairs 4*(tid/64) .. +3).
     {
-      const int r = tid & 63, cg = tid >> 6, j = k0 + r;
-      uint32_t info = 0;
       if (j < kv_hi) {
-        info = (uint32_t)L.key_info[blk.key_off + j];
         if (kc < 0) {
           const int p = key_row(info, L.n_pos, f.status);
           const uint4* tp = static_cast<const uint4*>(L.rope_cs16) + (int64_t)p * (D / 8);
 #pragma unroll
           for (int cc = 0; cc < 4; ++cc) {
             const int c = 4 * cg + cc;
-            uint4* pa = reinterpret_cast<uint4*>(sm + KR + chunk_off<BN>(r, c));
-            uint4* pb = reinterpret_cast<uint4*>(sm + KR + chunk_off<BN>(r, c + 8));
+            uint4* pa = reinterpret_cast<uint4*>(sm + KC + chunk_off<BN>(r, c));
+            uint4* pb = reinterpret_cast<uint4*>(sm + KC + chunk_off<BN>(r, c + 8));
             uint4 y1, y2;
             tile::rotate8h(*pa, *pb, __ldg(tp + 2 * c), __ldg(tp + 2 * c + 1), y1, y2);
             *pa = y1;
@@ -315,13 +337,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int kk = 0; kk < D / 16; ++kk) {
         const uint32_t ao = (uint32_t)(kk >> 2) * 16384u + (uint32_t)(kk & 3) * 32u;
         const uint32_t bo = (uint32_t)(kk >> 2) * 8192u + (uint32_t)(kk & 3) * 32u;
-        ptx::mma_ss(tmem + C_S, ptx::sdesc_sw128(sbase + QR + ao, 16, 1024), ptx::sdesc_sw128(sbase + KR + bo, 16, 1024),
+        ptx::mma_ss(tmem + C_S, ptx::sdesc_sw128(sbase + QR + ao, 16, 1024), ptx::sdesc_sw128(sbase + KC + bo, 16, 1024),
                     idesc_s, kk > 0);
         ptx::mma_ss(tmem + C_DP, ptx::sdesc_sw128(sbase + DO + ao, 16, 1024),
-                    ptx::sdesc_sw128(sbase + VV + bo, 16, 1024), idesc_s, kk > 0);
+                    ptx::sdesc_sw128(sbase + VC + bo, 16, 1024), idesc_s, kk > 0);
         if (tabs)
           ptx::mma_ss(tmem + C_SA, ptx::sdesc_sw128(sbase + QA + ao, 16, 1024),
-                      ptx::sdesc_sw128(sbase + KR + bo, 16, 1024), idesc_s, kk > 0);
+                      ptx::sdesc_sw128(sbase + KC + bo, 16, 1024), idesc_s, kk > 0);
       }
       ptx::mma_commit(bar_mma);
     }
@@ -346,7 +368,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool is_abs = tabs && (info & AI_KEY_ABS);
         const float s = is_abs ? __uint_as_float(ra[x]) : __uint_as_float(rs[x]);
         const bool valid = (info & AI_KEY_ATTN) && (k0 + c <= i) && (i < q1);
-        const float p = valid ? exp2f(s * sl2 - lse2) : 0.f;
+        const float p = valid ? ptx::ex2(s * sl2 - lse2) : 0.f;
         const float ds = p * (__uint_as_float(rp[x]) - dl) * f.scale;
         dsr[x] = is_abs ? 0.f : ds;
         dsa[x] = is_abs ? ds : 0.f;
@@ -376,10 +398,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t bo = (uint32_t)kk * 2048u;  // 16 key rows of 128 bytes
         const uint32_t acc = (n_tiles > 0 || o_init || kk > 0) ? 1u : 0u;
         ptx::mma_ss(tmem + C_DQR, ptx::sdesc_sw128(sbase + DS + ao, 16, 1024),
-                    ptx::sdesc_sw128(sbase + KR + bo, 8192, 1024), idesc_dq, acc);
+                    ptx::sdesc_sw128(sbase + KC + bo, 8192, 1024), idesc_dq, acc);
         if (tabs)
           ptx::mma_ss(tmem + C_DQA, ptx::sdesc_sw128(sbase + DSA + ao, 16, 1024),
-                      ptx::sdesc_sw128(sbase + KR + bo, 8192, 1024), idesc_dq, (dqa_started || kk > 0) ? 1u : 0u);
+                      ptx::sdesc_sw128(sbase + KC + bo, 8192, 1024), idesc_dq, (dqa_started || kk > 0) ? 1u : 0u);
       }
       ptx::mma_commit(bar_mma);
     }
@@ -773,7 +795,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int x = 0; x < 32; ++x) {
             const int c = 32 * cc + x, r = q0 + c % sr;
             const bool valid = key_ok && (j <= r) && (r < q1) && (j < kmax);
-            const float p = valid ? exp2f(s[c] * sl2 - s_lse[c]) : 0.f;
+            const float p = valid ? ptx::ex2(s[c] * sl2 - s_lse[c]) : 0.f;
             pv[x] = p;
             dsv[x] = p * (__uint_as_float(rp[x]) - s_del[c]) * f.scale;
           }

@@ -59,12 +59,14 @@ constexpr int kFwdChunkTiles = 2;
 struct Smem {
   static constexpr uint32_t Q = 0;
   static constexpr uint32_t QA = Q + kTile;
-  static constexpr uint32_t K = QA + kTile;
+  static constexpr uint32_t K = QA + kTile;  // K / V buffer 0
   static constexpr uint32_t V = K + kTile;
   static constexpr uint32_t P = V + kTile;
-  static constexpr uint32_t INFO = P + kTile;
-  static constexpr uint32_t BAR_TMA = INFO + 4 * BN;
-  static constexpr uint32_t BAR_MMA = BAR_TMA + 8;
+  static constexpr uint32_t K1 = P + kTile;  // K / V buffer 1: tile j + 1 loads while tile j runs
+  static constexpr uint32_t V1 = K1 + kTile;
+  static constexpr uint32_t INFO = V1 + kTile;
+  static constexpr uint32_t BAR_TMA = INFO + 4 * BN;  // two barriers, one per K / V buffer
+  static constexpr uint32_t BAR_MMA = BAR_TMA + 16;
   static constexpr uint32_t TMEM_SLOT = BAR_MMA + 8;
   static constexpr uint32_t ABORT = TMEM_SLOT + 4;
   static constexpr uint32_t TOTAL = ABORT + 4;
@@ -121,13 +123,54 @@ __global__ void __launch_bounds__(kThreads, 1)
   // The block's rotation classes: K tiles whose two chunks have one come rotated.
   const int cls = block_classes(L, item[0], prerot != 0);
 
+  // Key tiles of this CTA: the block's, or with the abs split only those
+  // holding abs keys (chunk 0 of a chunked item starts from the persistent
+  // kernel's partial, the other chunks from nothing).
+  const bool o_init = part_o != nullptr && chunk == 0;
+  int j_begin = 0, j_end = kv_hi > blk.kv_lo ? (kv_hi - blk.kv_lo + BN - 1) / BN : 0;
+  if (part_o != nullptr) {
+    abs_tiles(blk, blk.kv_lo, kv_hi, BN, j_begin, j_end);
+    if (chunked) {
+      const int n = j_end - j_begin, jb = j_begin;
+      j_begin = jb + n * chunk / n_chunks;
+      j_end = jb + n * (chunk + 1) / n_chunks;
+    }
+  }
+
+  // K and V of tile jt into buffer `buf` by TMA (K from its chunks' rotated
+  // copies when it has them).  Tile jt + 1 loads while tile jt runs; its
+  // buffer was last read by tile jt - 1's MMAs, complete by then.
+  auto issue_tile = [&](int jt, int buf) {
+    const int k0 = blk.kv_lo + jt * BN;
+    const int c0 = cls >= 0 ? chunk_class(L, cls, 2 * jt, a.status) : -1;
+    const int c1 = c0 >= 0 ? chunk_class(L, cls, 2 * jt + 1, a.status) : -1;
+    const uint32_t kb = sbase + (buf ? Smem::K1 : Smem::K), vb = sbase + (buf ? Smem::V1 : Smem::V);
+    const uint32_t bt = bar_tma + 8u * (uint32_t)buf;
+    ptx::fence_proxy_async_smem();
+    ptx::mbar_arrive_expect_tx(bt, 2 * kTile);
+    if (c0 >= 0 && c1 >= 0) {
+      ptx::tma_load_4d(kb, &tm_kc, bt, 0, 0, hk, c0);
+      ptx::tma_load_4d(kb + kHalf / 2, &tm_kc, bt, 0, 0, hk, c1);
+      ptx::tma_load_4d(kb + kHalf, &tm_kc, bt, 64, 0, hk, c0);
+      ptx::tma_load_4d(kb + kHalf + kHalf / 2, &tm_kc, bt, 64, 0, hk, c1);
+    } else {
+      ptx::tma_load_4d(kb, &tm_k, bt, 0, k0, hk, b);
+      ptx::tma_load_4d(kb + kHalf, &tm_k, bt, 64, k0, hk, b);
+    }
+    ptx::tma_load_4d(vb, &tm_v, bt, 0, k0, hk, b);
+    ptx::tma_load_4d(vb + kHalf, &tm_v, bt, 64, k0, hk, b);
+  };
+
   if (tid == 0) {
     ptx::mbar_init(bar_tma, 1);
+    ptx::mbar_init(bar_tma + 8, 1);
     ptx::mbar_init(bar_mma, 1);
     *s_abort = 0;
     ptx::fence_mbar_init();
     ptx::prefetch_tmap(&tm_k);
     ptx::prefetch_tmap(&tm_v);
+    // The first tile loads while the query rows are set up.
+    if (j_begin < j_end) issue_tile(j_begin, 0);
   }
   if (warp == 0) {
     ptx::tmem_alloc(sbase + Smem::TMEM_SLOT, kTmemCols);
@@ -171,25 +214,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr uint32_t idesc_pv = ptx::idesc_bf16_f32(BM, D, false, true);
   const int i = q0 + tid % slot;
   float m_use = -CUDART_INF_F, l = 0.f;
-  uint32_t ph_tma = 0, ph_mma = 0;
+  uint32_t ph_tma = 0, ph_mma = 0;  // ph_tma: bit b = phase of K / V buffer b
   int n_tiles = 0;
   bool aborted = false;
 
   // With the abs split the persistent kernel has run this item's key tiles
   // without abs keys and left each row's (O / l, log2-sum) partial: start
   // the online softmax from it (m = that sum, l = 1, O = the partial) and
-  // run the tiles that hold abs keys only (chunk 0 of a chunked item starts
-  // from the partial, the other chunks from nothing).
-  const bool o_init = part_o != nullptr && chunk == 0;
-  int j_begin = 0, j_end = kv_hi > blk.kv_lo ? (kv_hi - blk.kv_lo + BN - 1) / BN : 0;
-  if (part_o != nullptr) {
-    abs_tiles(blk, blk.kv_lo, kv_hi, BN, j_begin, j_end);
-    if (chunked) {
-      const int n = j_end - j_begin, jb = j_begin;
-      j_begin = jb + n * chunk / n_chunks;
-      j_end = jb + n * (chunk + 1) / n_chunks;
-    }
-  }
+  // run the tiles that hold abs keys only.
   if (o_init) {
     const int64_t prow = ((int64_t)blockIdx.x * a.num_q_heads + h) * BM + (i - q0);
     const bool have = i < q1;
@@ -217,32 +249,23 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   for (int jt = j_begin, k0 = blk.kv_lo + j_begin * BN; jt < j_end; ++jt, k0 += BN) {
+    const int buf = (jt - j_begin) & 1;
+    const uint32_t kcur = buf ? Smem::K1 : Smem::K, vcur = buf ? Smem::V1 : Smem::V;
     // Only a tile that holds one of the block's abs keys needs S_abs.
     const bool tabs = blk.abs_in(k0, min(k0 + BN, kv_hi));
     const int c0 = cls >= 0 ? chunk_class(L, cls, 2 * jt, a.status) : -1;
     const int c1 = c0 >= 0 ? chunk_class(L, cls, 2 * jt + 1, a.status) : -1;
     const bool ctile = c0 >= 0 && c1 >= 0;
-    // 1. K and V tiles by TMA (K from its chunks' rotated copies when it has them).
-    if (tid == 0) {
-      ptx::fence_proxy_async_smem();
-      ptx::mbar_arrive_expect_tx(bar_tma, 2 * kTile);
-      if (ctile) {
-        ptx::tma_load_4d(sbase + Smem::K, &tm_kc, bar_tma, 0, 0, hk, c0);
-        ptx::tma_load_4d(sbase + Smem::K + kHalf / 2, &tm_kc, bar_tma, 0, 0, hk, c1);
-        ptx::tma_load_4d(sbase + Smem::K + kHalf, &tm_kc, bar_tma, 64, 0, hk, c0);
-        ptx::tma_load_4d(sbase + Smem::K + kHalf + kHalf / 2, &tm_kc, bar_tma, 64, 0, hk, c1);
-      } else {
-        ptx::tma_load_4d(sbase + Smem::K, &tm_k, bar_tma, 0, k0, hk, b);
-        ptx::tma_load_4d(sbase + Smem::K + kHalf, &tm_k, bar_tma, 64, k0, hk, b);
-      }
-      ptx::tma_load_4d(sbase + Smem::V, &tm_v, bar_tma, 0, k0, hk, b);
-      ptx::tma_load_4d(sbase + Smem::V + kHalf, &tm_v, bar_tma, 64, k0, hk, b);
-    }
-    if (!ptx::mbar_wait(bar_tma, ph_tma, kWaitCycles)) {
+    // 1. The next tile's K and V start loading; this tile's have been
+    // requested one tile ago.  Key row `tid`'s flags are read meanwhile.
+    if (tid == 0 && jt + 1 < j_end) issue_tile(jt + 1, buf ^ 1);
+    const int j = k0 + tid;
+    const uint32_t info = j < kv_hi ? (uint32_t)L.key_info[blk.key_off + j] : 0u;
+    if (!ptx::mbar_wait(bar_tma + 8u * (uint32_t)buf, (ph_tma >> buf) & 1u, kWaitCycles)) {
       report(a.status, AI_ERR_DEV_TIMEOUT);
       *s_abort = 1;
     }
-    ph_tma ^= 1;
+    ph_tma ^= 1u << buf;
     __syncthreads();
     if (*s_abort) {
       aborted = true;
@@ -252,17 +275,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     // 2. Rotate key row `tid` in place by its position in this block (the
     // fp16 (cos, sin) table, as the rotated copies are made).
     {
-      const int j = k0 + tid;
-      uint32_t info = 0;
       if (j < kv_hi) {
-        info = (uint32_t)L.key_info[blk.key_off + j];
         if (!ctile) {
           const int p = key_row(info, L.n_pos, a.status);
           const uint4* tp = static_cast<const uint4*>(L.rope_cs16) + (int64_t)p * (D / 8);
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
-            uint4* pa = reinterpret_cast<uint4*>(sm + Smem::K + chunk_off(tid, c));
-            uint4* pb = reinterpret_cast<uint4*>(sm + Smem::K + chunk_off(tid, c + 8));
+            uint4* pa = reinterpret_cast<uint4*>(sm + kcur + chunk_off(tid, c));
+            uint4* pb = reinterpret_cast<uint4*>(sm + kcur + chunk_off(tid, c + 8));
             uint4 y1, y2;
             tile::rotate8h(*pa, *pb, __ldg(tp + 2 * c), __ldg(tp + 2 * c + 1), y1, y2);
             *pa = y1;
@@ -282,14 +302,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int kk = 0; kk < D / 16; ++kk) {
         const uint32_t off = (uint32_t)(kk >> 2) * kHalf + (uint32_t)(kk & 3) * 32u;
         ptx::mma_ss(tmem + kColS, ptx::sdesc_sw128(sbase + Smem::Q + off, 16, 1024),
-                    ptx::sdesc_sw128(sbase + Smem::K + off, 16, 1024), idesc_qk, kk > 0);
+                    ptx::sdesc_sw128(sbase + kcur + off, 16, 1024), idesc_qk, kk > 0);
       }
       if (tabs) {
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (uint32_t)(kk >> 2) * kHalf + (uint32_t)(kk & 3) * 32u;
           ptx::mma_ss(tmem + kColSabs, ptx::sdesc_sw128(sbase + Smem::QA + off, 16, 1024),
-                      ptx::sdesc_sw128(sbase + Smem::K + off, 16, 1024), idesc_qk, kk > 0);
+                      ptx::sdesc_sw128(sbase + kcur + off, 16, 1024), idesc_qk, kk > 0);
         }
       }
       ptx::mma_commit(bar_mma);
@@ -336,7 +356,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool rescale = false;
     if (m_new > m_use + 8.f) {
       if ((n_tiles > 0 || o_init) && l > 0.f) {
-        alpha = exp2f(m_use - m_new);
+        alpha = ptx::ex2(m_use - m_new);
         rescale = true;
       }
       m_use = m_new;
@@ -362,7 +382,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int x = 0; x < 8; ++x) {
         const float v = s[8 * c8 + x];
-        pv[x] = (v == -CUDART_INF_F) ? 0.f : exp2f(v - m_use);
+        pv[x] = (v == -CUDART_INF_F) ? 0.f : ptx::ex2(v - m_use);
         sum += pv[x];
       }
       *reinterpret_cast<uint4*>(sm + Smem::P + chunk_off(tid, c8)) = pack8(pv);
@@ -380,7 +400,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t aoff = (uint32_t)(kk >> 2) * kHalf + (uint32_t)(kk & 3) * 32u;
         const uint32_t boff = (uint32_t)kk * 2048u;  // 16 key rows of 128 bytes
         ptx::mma_ss(tmem + kColO, ptx::sdesc_sw128(sbase + Smem::P + aoff, 16, 1024),
-                    ptx::sdesc_sw128(sbase + Smem::V + boff, kHalf, 1024), idesc_pv,
+                    ptx::sdesc_sw128(sbase + vcur + boff, kHalf, 1024), idesc_pv,
                     (n_tiles > 0 || o_init || kk > 0) ? 1u : 0u);
       }
       ptx::mma_commit(bar_mma);
