@@ -588,6 +588,40 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (*s_abort) aborted = true;
 
+  // Query / dO rows of one step by TMA: the 64 rows from q0 of head h, or
+  // (P > 1) 64 / P rows of each of the P heads of the group from hk * G.
+  auto issue_q = [&](bool has_abs, int P, int sr, int q0, int h) {
+    const uint32_t qdst = has_abs ? QA : QR;
+    ptx::fence_proxy_async_smem();
+    ptx::mbar_arrive_expect_tx(bar_q, (prerot && has_abs ? 6u : 4u) * 8192u);
+    if (P == 1) {
+      if (!prerot || has_abs) {
+        ptx::tma_load_4d(sbase + qdst, &tm_q, bar_q, 0, q0, h, b);
+        ptx::tma_load_4d(sbase + qdst + 8192, &tm_q, bar_q, 64, q0, h, b);
+      }
+      if (prerot) {
+        ptx::tma_load_4d(sbase + QR, &tm_qr, bar_q, 0, q0, h, b);
+        ptx::tma_load_4d(sbase + QR + 8192, &tm_qr, bar_q, 64, q0, h, b);
+      }
+      ptx::tma_load_4d(sbase + DO, &tm_do, bar_q, 0, q0, h, b);
+      ptx::tma_load_4d(sbase + DO + 8192, &tm_do, bar_q, 64, q0, h, b);
+    } else {
+      for (int x = 0; x < P; ++x) {
+        const uint32_t ro = (uint32_t)(x * sr) * 128u;
+        if (!prerot || has_abs) {
+          ptx::tma_load_4d(sbase + qdst + ro, &tm_qp, bar_q, 0, q0, hk * G + x, b);
+          ptx::tma_load_4d(sbase + qdst + 8192 + ro, &tm_qp, bar_q, 64, q0, hk * G + x, b);
+        }
+        if (prerot) {
+          ptx::tma_load_4d(sbase + QR + ro, &tm_qrp, bar_q, 0, q0, hk * G + x, b);
+          ptx::tma_load_4d(sbase + QR + 8192 + ro, &tm_qrp, bar_q, 64, q0, hk * G + x, b);
+        }
+        ptx::tma_load_4d(sbase + DO + ro, &tm_dop, bar_q, 0, q0, hk * G + x, b);
+        ptx::tma_load_4d(sbase + DO + 8192 + ro, &tm_dop, bar_q, 64, q0, hk * G + x, b);
+      }
+    }
+  };
+
   for (int bi = L.row_blocks[b]; bi < L.row_blocks[b + 1] && !aborted; ++bi) {
     const Block blk = load_block(L.blocks, bi);
     if (blk.e <= j0 || blk.kv_lo >= j1) continue;
@@ -595,6 +629,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (qs >= blk.e) continue;
     const bool has_abs = (blk.flags & AI_BLOCKF_ABS) != 0;
     if (abs_only && !blk.abs_in(j0, j1)) continue;
+    // A block of at most 64 / G rows packs the rows of all G heads of the
+    // group into one step: column c is row q0 + c % (64 / G) of head
+    // hk * G + c / (64 / G) (tm_qp / tm_dop have boxes of 64 / G rows).
+    const int P = ((G == 2 || G == 4 || G == 8) && blk.e - qs <= BQ / G) ? G : 1, sr = BQ / P;
     const int kmax = min(j1, blk.e);
     // The tile's two 64-key chunks in this block's rotation classes, if any.
     int c0 = -1, c1 = -1;
@@ -623,14 +661,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         ptx::tma_load_4d(sbase + KR, &tm_k, bar_k, 0, j0, hk, b);
         ptx::tma_load_4d(sbase + KR + 16384, &tm_k, bar_k, 64, j0, hk, b);
       }
+      // The block's first step's query / dO rows load alongside (the previous
+      // block's MMAs, the last readers of those buffers, are complete).
+      issue_q(has_abs, P, sr, qs, hk * G);
     }
+    const uint32_t my_info = j < kmax ? (uint32_t)L.key_info[blk.key_off + j] : 0u;
     wait_or_flag(bar_k, ph_k, s_abort, f.status);
     __syncthreads();
     if (*s_abort) { aborted = true; break; }
-    uint32_t my_info = 0;
     int my_row = 0;
     if (j < kmax) {
-      my_info = (uint32_t)L.key_info[blk.key_off + j];
       my_row = key_row(my_info, L.n_pos, f.status);
       if (!ctile) {
         const uint4* tp = static_cast<const uint4*>(L.rope_cs16) + (int64_t)my_row * (D / 8);
@@ -651,47 +691,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
 
     bool dkr_started = false;
-    // A block of at most 64 / G rows packs the rows of all G heads of the
-    // group into one step: column c is row q0 + c % (64 / G) of head
-    // hk * G + c / (64 / G) (tm_qp / tm_dop have boxes of 64 / G rows).
-    const int P = ((G == 2 || G == 4 || G == 8) && blk.e - qs <= BQ / G) ? G : 1, sr = BQ / P;
+    bool first_step = true;
     for (int q0 = qs; q0 < blk.e && !aborted; q0 += BQ) {
       const int q1 = min(q0 + BQ, blk.e);
       for (int g = 0; g < G; g += P) {
         const int h = hk * G + g;
         // Raw query rows go to QA (abs blocks) or straight to QR to be rotated
         // there; with the rotated copies the rotated rows come by TMA as well.
+        // The block's first step was requested with its K tile.
         const uint32_t qdst = has_abs ? QA : QR;
-        if (tid == 0) {
-          ptx::fence_proxy_async_smem();
-          ptx::mbar_arrive_expect_tx(bar_q, (prerot && has_abs ? 6u : 4u) * 8192u);
-          if (P == 1) {
-            if (!prerot || has_abs) {
-              ptx::tma_load_4d(sbase + qdst, &tm_q, bar_q, 0, q0, h, b);
-              ptx::tma_load_4d(sbase + qdst + 8192, &tm_q, bar_q, 64, q0, h, b);
-            }
-            if (prerot) {
-              ptx::tma_load_4d(sbase + QR, &tm_qr, bar_q, 0, q0, h, b);
-              ptx::tma_load_4d(sbase + QR + 8192, &tm_qr, bar_q, 64, q0, h, b);
-            }
-            ptx::tma_load_4d(sbase + DO, &tm_do, bar_q, 0, q0, h, b);
-            ptx::tma_load_4d(sbase + DO + 8192, &tm_do, bar_q, 64, q0, h, b);
-          } else {
-            for (int x = 0; x < P; ++x) {
-              const uint32_t ro = (uint32_t)(x * sr) * 128u;
-              if (!prerot || has_abs) {
-                ptx::tma_load_4d(sbase + qdst + ro, &tm_qp, bar_q, 0, q0, hk * G + x, b);
-                ptx::tma_load_4d(sbase + qdst + 8192 + ro, &tm_qp, bar_q, 64, q0, hk * G + x, b);
-              }
-              if (prerot) {
-                ptx::tma_load_4d(sbase + QR + ro, &tm_qrp, bar_q, 0, q0, hk * G + x, b);
-                ptx::tma_load_4d(sbase + QR + 8192 + ro, &tm_qrp, bar_q, 64, q0, hk * G + x, b);
-              }
-              ptx::tma_load_4d(sbase + DO + ro, &tm_dop, bar_q, 0, q0, hk * G + x, b);
-              ptx::tma_load_4d(sbase + DO + 8192 + ro, &tm_dop, bar_q, 64, q0, hk * G + x, b);
-            }
-          }
-        }
+        if (tid == 0 && !first_step) issue_q(has_abs, P, sr, q0, h);
+        first_step = false;
         if (tid < BQ) {
           const int r = q0 + tid % sr, hc = P == 1 ? h : hk * G + tid / sr;
           float l2 = CUDART_INF_F, dlt = 0.f;
