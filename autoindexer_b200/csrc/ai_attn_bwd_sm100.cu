@@ -1735,9 +1735,6 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
     ptx::tmem_alloc(sbase + TMEM_SLOT, kTmemCols);
     ptx::tmem_relinquish();
   }
-  if (warp < 4) {
-    for (int d = 0; d < D; ++d) s_dk[d * BN + tid] = 0.f;
-  }
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
@@ -1758,6 +1755,14 @@ __global__ void __launch_bounds__(kvw::kThreads, 1)
   if (warp < 4 * kGroups) {
     // ------------------------------------------------------------ score groups
     const int t = warp / 4, lrow = tid % 128, j = j0 + lrow;
+    // The fp32 dK accumulator entries this thread folds into and writes out
+    // (key lrow, d in [16t, 16t + 16) and [64 + 16t, 80 + 16t)) are its own:
+    // it clears them here, while the first tiles load.
+#pragma unroll
+    for (int x = 0; x < kCols; ++x) {
+      s_dk[(kCols * t + x) * BN + lrow] = 0.f;
+      s_dk[(64 + kCols * t + x) * BN + lrow] = 0.f;
+    }
     const uint32_t lane_base = (uint32_t)((warp % 4) * 32) << 16;
     const float sl2 = f.scale * kLog2e, scale = f.scale;
     const float2 sl2x2 = make_float2(sl2, sl2), scalex2 = make_float2(scale, scale);
