@@ -49,7 +49,7 @@ constexpr int kThreads = 128;
 constexpr uint32_t kTmemCols = 512;
 constexpr long long kWaitCycles = 4000000000LL;
 // Fewest 64-key abs tiles a chunk of a short abs item takes in dq_kernel.
-constexpr int kDqChunkTiles = 4;
+constexpr int kDqChunkTiles = 6;
 
 using tile::chunk_off;
 using tile::pack8;

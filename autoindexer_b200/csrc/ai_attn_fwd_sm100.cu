@@ -54,7 +54,7 @@ constexpr uint32_t kColS = 0, kColSabs = 128, kColO = 256;
 constexpr long long kWaitCycles = 4000000000LL;
 // Fewest 128-key abs tiles a chunk of a short abs item takes (a chunk costs
 // its CTA's set-up and a partial row on top of its tiles).
-constexpr int kFwdChunkTiles = 2;
+constexpr int kFwdChunkTiles = 3;
 
 struct Smem {
   static constexpr uint32_t Q = 0;
