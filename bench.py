@@ -283,6 +283,16 @@ def sum_over_ranks(x: float, world: int, device) -> float:
     return float(tt.item())
 
 
+def workload_config(wl, world: int, sharded: bool) -> dict:
+    """The ``config`` of a bench line for workload ``wl`` at ``world`` ranks:
+    this library's arm and the reference arm report the same dict (the
+    reference arm's bounded CPU sample is described in its ``cpu_baseline``)."""
+    return {"workload": wl.desc, "global_batch": wl.batch * (1 if sharded else world), "seq_len": wl.seq_len,
+            "parallelism": (f"kv-head shards over {world} ranks + NCCL all-gather" if sharded
+                            else f"dp{world} (independent rows)"),
+            "l2": "flushed between timed steps (256 MB write, untimed)"}
+
+
 def job_tflops(job_flops_per_step: float, steps: int, t_max: float) -> float:
     """Whole-job throughput: job FLOPs per step (summed over ranks for weak
     scaling, the one problem's FLOPs for strong scaling) over the slowest
@@ -497,10 +507,7 @@ def run_ours(args):
         "vs_baseline": None,
         "dtype": "f32" if wdtype == torch.float32 else "bf16",
         "data": "synthetic (seeded randn q/k/v/dO; seeded layouts and cursor streams)",
-        "config": {"workload": wl.desc, "global_batch": Bw * n_ranks_work, "seq_len": Tw,
-                   "parallelism": (f"kv-head shards over {world} ranks + NCCL all-gather" if sharded
-                                   else f"dp{world} (independent rows)"),
-                   "l2": "flushed between timed steps (256 MB write, untimed)"},
+        "config": workload_config(wl, world, sharded),
         "fwd_ms": round(max_over_ranks(t_fwd, world, dev) / args.steps * 1e3, 4),
         "bwd_ms": round(max_over_ranks(t_bwd, world, dev) / args.steps * 1e3, 4),
         "tokens_per_s": round(tokens, 1),
@@ -638,7 +645,7 @@ def run_reference(args):
         "metric": METRIC, "value": round(value, 6), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (same generator as the GPU arm)", "impl": "reference",
-        "config": {"workload": wl.desc, "global_batch": wl.batch, "seq_len": wl.seq_len, "parallelism": "cpu"},
+        "config": workload_config(wl, world, args.config == "3" and world > 1),
         "cpu_baseline": cb,
         "e2e": {"value": round(value, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
