@@ -530,7 +530,7 @@ def run_ours(args):
     if gather_ms is not None:
         line["allgather_ms_per_step"] = round(max_over_ranks(gather_ms / args.steps, world, dev), 4)
     if world == 1 and args.config in ("0", "1") and not args.no_cpu_baseline:  # the CPU baseline is an N=1 figure
-        line["cpu_baseline"] = cpu_baseline(wl, seed=0)
+        line["cpu_baseline"] = cpu_baseline(wl, seed=0, min_seconds=10.0)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -554,14 +554,25 @@ def _reference_modules():
     return ref, pl, tu
 
 
-def cpu_baseline(wl: Workload, seed=0, reps=1):
+def cpu_baseline(wl: Workload, seed=0, reps=1, min_seconds=0.0):
     """The reference's eager attention (``chain_of_edits_attn_ref``,
     ``attention/reference.py:116-141``, from ``baseline/_ref``) forward +
     autograd backward in fp32 on all host cores, on one (batch row, KV group)
     slice of the workload: 4 query heads of batch row 0, K/V expanded as the
     reference's interface does.  Without the install, the oracle (numpy
-    restatement of the same code) on the same slice."""
+    restatement of the same code) on the same slice.  The slice runs ``reps``
+    times, and again until ``min_seconds`` have passed (at most 64 times);
+    the figure is the mean per run."""
     import torch
+
+    def timed(run_once):
+        t0, n = time.perf_counter(), 0
+        while True:
+            run_once()
+            n += 1
+            el = time.perf_counter() - t0
+            if n >= reps and (el >= min_seconds or n >= 64):
+                return el / n, n
 
     q, k, v, dout = wl.host
     G = HQ // HKV
@@ -586,23 +597,23 @@ def cpu_baseline(wl: Workload, seed=0, reps=1):
         rope = ab.SectionedRope(D, THETA, [torch.as_tensor(s) for s in wl.streams], wl.sections)
         prev = torch.get_num_threads()
         torch.set_num_threads(cores)
-        try:
-            t0 = time.perf_counter()
-            for _ in range(reps):
-                rlay._query_rotary_pos_emb = rlay._keys_rotary_pos_emb = None
-                if wl.full_cpu:
-                    from transformers.models.llama.modeling_llama import repeat_kv
+        def run_once():
+            rlay._query_rotary_pos_emb = rlay._keys_rotary_pos_emb = None
+            if wl.full_cpu:
+                from transformers.models.llama.modeling_llama import repeat_kv
 
-                    qs, ks, vs = (x.float().requires_grad_(True) for x in (q, k, v))
-                    out, _ = ref.chain_of_edits_attn_ref(rope, qs, repeat_kv(ks, G), repeat_kv(vs, G), rlay)
-                    out.backward(dout.float())
-                    continue
-                qs = q[:1, :G].float().requires_grad_(True)
-                ks = k[:1, :1].float().requires_grad_(True)
-                vs = v[:1, :1].float().requires_grad_(True)
-                out, _ = ref.chain_of_edits_attn_ref(rope, qs, ks.expand(1, G, Tw, D), vs.expand(1, G, Tw, D), rlay)
-                out.backward(dout[:1, :, :G].float())
-            dt = (time.perf_counter() - t0) / reps
+                qs, ks, vs = (x.float().requires_grad_(True) for x in (q, k, v))
+                out, _ = ref.chain_of_edits_attn_ref(rope, qs, repeat_kv(ks, G), repeat_kv(vs, G), rlay)
+                out.backward(dout.float())
+                return
+            qs = q[:1, :G].float().requires_grad_(True)
+            ks = k[:1, :1].float().requires_grad_(True)
+            vs = v[:1, :1].float().requires_grad_(True)
+            out, _ = ref.chain_of_edits_attn_ref(rope, qs, ks.expand(1, G, Tw, D), vs.expand(1, G, Tw, D), rlay)
+            out.backward(dout[:1, :, :G].float())
+
+        try:
+            dt, n_runs = timed(run_once)
         finally:
             torch.set_num_threads(prev)
         kind, what = "reference", "reference eager chain_of_edits_attn_ref + autograd, torch fp32"
@@ -616,17 +627,18 @@ def cpu_baseline(wl: Workload, seed=0, reps=1):
         else:
             qs, ks, vs = (x[:1, :n].float().numpy() for x, n in ((q, G), (k, 1), (v, 1)))
             dos = dout[:1, :, :G].float().numpy()
+        def run_once():
+            O.attn_forward(qs, ks, vs, lay, rope, dtype=np.float32)
+            O.attn_backward(qs, ks, vs, dos, lay, rope, dtype=np.float32)
+
         with threadpool_limits(limits=cores):
-            t0 = time.perf_counter()
-            for _ in range(reps):
-                O.attn_forward(qs, ks, vs, lay, rope, dtype=np.float32)
-                O.attn_backward(qs, ks, vs, dos, lay, rope, dtype=np.float32)
-            dt = (time.perf_counter() - t0) / reps
+            dt, n_runs = timed(run_once)
         kind, what = "port", "oracle (numpy restatement of the reference's eager path), fp32"
     sample = (f"the whole workload (B={wl.batch}, {HQ} query heads), T={Tw}" if wl.full_cpu
               else f"batch row 0, kv group 0 ({G} query heads), T={Tw}")
     return {"value": round(flops / dt / 1e12, 6), "unit": "TFLOP/s", "cores": cores, "kind": kind,
-            "sample": f"{sample}: fwd+bwd, {what}, {dt:.2f} s"}
+            "sample": f"{sample}: fwd+bwd, {what}, {dt:.2f} s a run, "
+                      f"{n_runs} run{'s' if n_runs != 1 else ''} ({dt * n_runs:.1f} s)"}
 
 
 def run_reference(args):
