@@ -59,8 +59,8 @@ METRIC = "multi-seg RoPE attn fwd+bwd TFLOP/s (causal-adjusted, 14*D*pairs*Hq)"
 DOM_KERNEL_NAMES = {"fwd": "fwd_pers_kernel (forward)", "dq": "dq_pers_kernel (dQ)", "dkdv": "dkdv_ws_kernel (dK/dV)",
                     "simt": "simt fp32 kernels (forward + backward)"}
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the
-# dominant kernel on the config-1 workload, from one ncu capture of it
-# (profiles/cfg1_dkdv_ws_kernel_full.md).
+# dominant kernel on the config-1 workload, from one `ncu --set full` capture
+# of it on the current build (the summary sits with the other profiles).
 TRAFFIC_BYTES = {"dkdv": 408681728}
 REF_PATH = os.path.join(ROOT, "baseline", "_ref")
 
